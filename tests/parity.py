@@ -1,0 +1,57 @@
+"""Shared parity helpers: golden fixtures, ulp distances and the index-list comparison rule."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def golden(name: str) -> dict[str, np.ndarray]:
+    with np.load(GOLDEN / f"{name}.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+def f32_ulp_diff(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in float32 units in the last place (monotone integer map of the bit patterns)."""
+
+    def key(x: np.ndarray) -> np.ndarray:
+        i = np.ascontiguousarray(x, dtype=np.float32).view(np.int32).astype(np.int64)
+        return np.where(i < 0, -(i & 0x7FFFFFFF), i)
+
+    return np.abs(key(a) - key(b))
+
+
+def bf16_ulp_diff(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in bf16 units in the last place between two arrays of bf16 values (as float32)."""
+    return f32_ulp_diff(a, b) >> 16
+
+
+def index_parity(ours: np.ndarray, ref: np.ndarray, bound: np.ndarray, tie_tol: float = 0.0) -> dict[str, int]:
+    """Compare two top-K index lists [h, K] (candidate ids) under the tie rule.
+
+    Lists must agree position by position, except that a position may differ where both entries'
+    bounds are within `tie_tol` of the K-th bound of that head (an exact tie when `tie_tol` is 0).
+    Returns counts; `bad` must be 0.
+    """
+    h, k = ours.shape
+    exact = 0
+    tie = 0
+    bad = 0
+    for j in range(h):
+        kth = np.sort(bound[j])[::-1][k - 1]
+        near = lambda b: abs(float(bound[j][b]) - float(kth)) <= tie_tol  # noqa: E731
+        so, sr = set(ours[j].tolist()), set(ref[j].tolist())
+        for b in so ^ sr:
+            if not near(b):
+                bad += 1
+        for p in range(k):
+            if ours[j, p] == ref[j, p]:
+                exact += 1
+            elif near(ours[j, p]) or near(ref[j, p]) or bound[j][ours[j, p]] == bound[j][ref[j, p]]:
+                tie += 1
+            else:
+                bad += 1
+    return {"exact": exact, "tie": tie, "bad": bad}
