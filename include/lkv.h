@@ -1,0 +1,142 @@
+/*
+ * lkv.h — C ABI of liblkv_sm100.so, the sm_100a kernels behind LazyKV's tiered decode path.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers, sizes and a CUDA stream (as void*),
+ * never synchronises, and returns an lkv_status. On a non-zero status, lkv_last_error() gives
+ * the message of the calling thread's last failure. Device pointers may also be device views of
+ * pinned, mapped host memory (the cold tier read through zero-copy loads).
+ *
+ * Reference interfaces are cited as file:line within PS12007/LazyKV; each entry point replaces
+ * the torch calls made there.
+ */
+#ifndef LKV_H
+#define LKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  LKV_OK = 0,
+  LKV_ERR_ARG = 1,      /* a size, shape or dtype the kernels do not support */
+  LKV_ERR_PTR = 2,      /* a null or misaligned pointer where one is required */
+  LKV_ERR_CUDA = 3,     /* a CUDA launch or runtime error */
+  LKV_ERR_WORKSPACE = 4 /* the workspace passed is smaller than the query function says */
+} lkv_status;
+
+/* Element types of KV, metadata and queries. */
+typedef enum { LKV_F32 = 0, LKV_BF16 = 1 } lkv_dtype;
+
+/* Cold-tier storage: int8 records (lazykv/quant.py:73-87) or whole pairs in the model dtype. */
+typedef enum { LKV_COLD_INT8 = 0, LKV_COLD_PAIRS = 1 } lkv_cold_kind;
+
+/* Library version string and the calling thread's last error message (copied into buf). */
+const char* lkv_version(void);
+size_t lkv_last_error(char* buf, size_t len);
+
+/* Bytes of one packed (block, head) record. Replaces lazykv/quant.py:46-49 packed_pair_bytes. */
+int64_t lkv_packed_pair_bytes(int bs, int d);
+
+/*
+ * Channel-wise min/max of each block's keys. Replaces the amin/amax of
+ * lazykv/selection.py:142-144, lazykv/tiered.py:173-175 and :369-370.
+ * Key element (head j, block b, token t, channel c) is keys[j*s_head + b*s_block + t*s_tok + c];
+ * kmin/kmax [h, cap, d] (same dtype as keys) are written at [j, first_block + b, :] with
+ * m_head = cap * d.
+ */
+int lkv_block_minmax(const void* keys, int dtype, int h, int n_blocks, int bs, int d,
+                     int64_t s_head, int64_t s_block, int64_t s_tok, void* kmin, void* kmax,
+                     int64_t m_head, int first_block, void* stream);
+
+/*
+ * int8 quantise-on-write. Replaces lazykv/quant.py:73-87 pack (and, fused, the dequantise and
+ * metadata of lazykv/tiered.py:187-197 and :365-370). pairs [n_blocks, h, 2, bs, d] in `dtype`
+ * -> records [n_blocks, h, W] (W = lkv_packed_pair_bytes), bit-exact with the reference.
+ * Optional outputs (NULL to skip): kmin/kmax over the dequantised keys in `dtype`, written like
+ * lkv_block_minmax; deq [n_blocks, h, 2, bs, d] the dequantised pairs in `dtype`.
+ */
+int lkv_pack_int8(const void* pairs, int dtype, int n_blocks, int h, int bs, int d,
+                  uint8_t* records, void* kmin, void* kmax, int64_t m_head, int first_block,
+                  void* deq, void* stream);
+
+/* int8 dequantise-on-read. Replaces lazykv/quant.py:90-105 unpack: records [n, W] -> out
+ * [n, 2, bs, d] in out_dtype, bit-exact. */
+int lkv_unpack_int8(const uint8_t* records, int64_t n, int bs, int d, void* out, int out_dtype,
+                    void* stream);
+
+/*
+ * Gather-scatter fetch of (block, head) pairs from the host store into the slot pool. Replaces
+ * the staged gather of lazykv/tiered.py:429-447 (index_select, H2D, unpack, index_copy_).
+ * src: int8 records [rows, W] (LKV_COLD_INT8, dequantised into `dtype`) or pairs
+ * [rows, 2, bs, d] in `dtype` (LKV_COLD_PAIRS). dst: pairs [rows, 2, bs, d] in `dtype`.
+ * Row i of the fetch copies src row src_rows[i] to dst row dst_rows[i].
+ */
+int lkv_fetch_pairs(const void* src, int src_kind, const int64_t* src_rows, void* dst,
+                    const int64_t* dst_rows, int64_t n, int bs, int d, int dtype, void* stream);
+
+/*
+ * Quest bound and device-side top-k. Replaces lazykv/selection.py:38-62 quest_bound/top_blocks
+ * and the host round trip of lazykv/tiered.py:383-387 rank.
+ * q [hq, d] (q_dtype); kmin/kmax [h, cap, d] (meta_dtype, row stride m_head per head);
+ * candidates are blocks [first_block, first_block + n_cand). bound_mode LKV_BF16 rounds as the
+ * reference's bf16 matmuls do, LKV_F32 keeps float32. Output: out_blocks [h, k] (row stride
+ * out_ld >= k) block ids in descending bound order, ties by ascending block id. Optional: out_bound [h, n_cand] float32;
+ * bitmap [h, bitmap_words] set exactly at the selected block ids (the words are cleared first).
+ * Workspace: lkv_quest_topk_workspace(h, n_cand) bytes.
+ */
+size_t lkv_quest_topk_workspace(int h, int n_cand);
+int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
+                   const void* kmax, int meta_dtype, int64_t m_head, int first_block, int n_cand,
+                   int k, int bound_mode, int32_t* out_blocks, int out_ld, float* out_bound,
+                   uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/*
+ * Split decode attention over listed blocks, emitting (normalised out, lse). Replaces the gather
+ * + SDPA + GPU log-sum-exp of lazykv/tiered.py:465-487, lazykv/attention.py:97-136 and
+ * lazykv/exact.py:380-393.
+ * Per KV head j the key sequence is the n_list blocks blocks[j*n_list + i] in order; the last one
+ * holds `last_fill` live tokens (the current block, lazykv/selection.py:65-69), the others bs.
+ * A listed id b maps to storage row r = slot_of ? slot_of[j*slot_stride + b] : b, and key element
+ * (t, c) of that row is k_base[r*s_row + j*s_head + t*s_tok + c] (values at v_base, same strides).
+ * q [hq, d] in `dtype`; out [hq, d] float32 (divided by its normaliser) and lse [hq] float32.
+ * Workspace: lkv_attention_workspace(h, hq, d, n_list) bytes.
+ */
+size_t lkv_attention_workspace(int h, int hq, int d, int n_items);
+int lkv_hot_attention(const void* q, int hq, int h, int d, int bs, const void* k_base,
+                      const void* v_base, int dtype, int64_t s_row, int64_t s_head, int64_t s_tok,
+                      const int32_t* blocks, int n_list, const int32_t* slot_of,
+                      int64_t slot_stride, int last_fill, float scale, float* out, float* lse,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Exact pass over the cold blocks. Replaces lazykv/exact.py:88-127 cpu_partial_attention (and
+ * the float32 mirror it reads, lazykv/exact.py:130-152) with a GPU pass over the complement only.
+ * Attends blocks [first_block, first_block + n_blocks) of every KV head j, skipping those whose
+ * bit is set in excluded[j*bitmap_words + b/32]; the store is cold [blocks, h, W] int8 records
+ * (dequantised in float32, fused) or cold [blocks, h, 2, bs, d] pairs in `dtype`
+ * (LKV_COLD_PAIRS). A head with no block left returns lse = -inf and out = 0.
+ * Workspace: lkv_attention_workspace(h, hq, d, n_blocks) bytes.
+ */
+int lkv_cold_attention(const void* q, int hq, int h, int d, int bs, const void* cold,
+                       int cold_kind, int dtype, int first_block, int n_blocks,
+                       const uint32_t* excluded, int bitmap_words, float scale, float* out,
+                       float* lse, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Log-sum-exp merge of n_parts partials. Replaces lazykv/exact.py:69-85 merge_lse (n_parts = 2)
+ * and is the cross-GPU merge of all-gathered shard partials. outs [n_parts, rows, d] and lses
+ * [n_parts, rows] float32 -> out [rows, d] in out_dtype, lse_out [rows] float32 (optional).
+ * Parts with lse = -inf contribute nothing; all parts empty gives out = 0, lse = -inf.
+ */
+int lkv_lse_merge(const float* outs, const float* lses, int n_parts, int64_t rows, int d,
+                  void* out, int out_dtype, float* lse_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LKV_H */

@@ -1,0 +1,95 @@
+"""ctypes binding of liblkv_sm100.so (the C ABI declared in include/lkv.h).
+
+The library is loaded from this package directory and must have been built for sm_100a
+(`python -m lazykv_b200.build`). There is no fallback: if it is missing or a call fails, the
+caller gets an exception carrying the library's own message.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "liblkv_sm100.so"
+
+LKV_F32, LKV_BF16 = 0, 1
+LKV_COLD_INT8, LKV_COLD_PAIRS = 0, 1
+
+_lib: ctypes.CDLL | None = None
+
+# name -> (restype, argtypes); every entry point of include/lkv.h.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "lkv_version": (c_char_p, []),
+    "lkv_last_error": (c_size_t, [c_char_p, c_size_t]),
+    "lkv_packed_pair_bytes": (c_int64, [c_int, c_int]),
+    "lkv_block_minmax": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "lkv_pack_int8": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "lkv_unpack_int8": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]),
+    "lkv_fetch_pairs": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),
+    "lkv_quest_topk_workspace": (c_size_t, [c_int, c_int]),
+    "lkv_quest_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "lkv_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "lkv_hot_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "lkv_cold_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "lkv_lse_merge": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_int, c_void_p, c_void_p]),
+}
+
+
+class LkvError(RuntimeError):
+    """A non-zero status from liblkv_sm100.so, with the library's message."""
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH.name} is not built; run `python -m lazykv_b200.build` (needs nvcc, targets sm_100a)")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(512)
+    lib().lkv_last_error(buf, 512)
+    return buf.value.decode()
+
+
+def call(name: str, *args: object) -> None:
+    """Call an lkv_* entry point returning a status; raise LkvError on failure."""
+    rc = getattr(lib(), name)(*args)
+    if rc != 0:
+        raise LkvError(f"{name} failed ({rc}): {last_error()}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    """Raw address of a tensor's first element (None for None)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return LKV_BF16
+    if dt == torch.float32:
+        return LKV_F32
+    raise ValueError(f"unsupported dtype {dt}; the kernels take bfloat16 or float32")
+
+
+def require_cuda(*tensors: torch.Tensor) -> torch.device:
+    """The kernels run on CUDA tensors only: there is no CPU path."""
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("lazykv_b200 computes on CUDA tensors; got a CPU tensor (there is no CPU fallback)")
+    return next(t.device for t in tensors if t is not None)

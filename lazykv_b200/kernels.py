@@ -1,0 +1,180 @@
+"""torch-facing wrappers of the C ABI: shape checks, output allocation and a per-device workspace.
+
+Each function launches on the current CUDA stream and never synchronises. Inputs must be CUDA
+tensors (or device views of pinned host memory); there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from lazykv_b200 import _lib as L
+from lazykv_b200._lib import call, dtype_code, ptr, require_cuda, stream_handle
+
+_WS: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def workspace(device: torch.device, nbytes: int, slot: int = 0) -> torch.Tensor:
+    """A reusable device buffer of at least `nbytes` (grown on demand), one per (device, slot).
+
+    Calls on one stream run in order, so reusing the buffer between them is safe; work on another
+    stream must use another slot.
+    """
+    key = (device.index if device.index is not None else torch.cuda.current_device(), slot)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def packed_pair_bytes(block_size: int, head_dim: int) -> int:
+    return int(L.lib().lkv_packed_pair_bytes(block_size, head_dim))
+
+
+def block_minmax(keys: torch.Tensor, block_size: int, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int = 0) -> None:
+    """kmin/kmax[j, first_block + b] = channel min/max of block b of `keys` [h, n*bs, d] (any strides)."""
+    require_cuda(keys, kmin, kmax)
+    h, t, d = keys.shape
+    n = t // block_size
+    if kmin.shape[-1] != d or kmin.dtype != keys.dtype or kmax.dtype != keys.dtype or kmin.stride(-1) != 1 or keys.stride(-1) != 1:
+        raise ValueError("block_minmax: metadata must be [h, cap, d] in the keys' dtype, contiguous in d")
+    s_head, s_tok = keys.stride(0), keys.stride(1)
+    call("lkv_block_minmax", ptr(keys), dtype_code(keys.dtype), h, n, block_size, d, s_head, block_size * s_tok, s_tok,
+         ptr(kmin), ptr(kmax), kmin.stride(-3) if kmin.dim() >= 3 else kmin.shape[-2] * d, first_block, stream_handle(keys.device))
+
+
+def pack_int8(pairs: torch.Tensor, records: torch.Tensor | None = None, kmin: torch.Tensor | None = None, kmax: torch.Tensor | None = None,
+              first_block: int = 0, deq: torch.Tensor | None = None) -> torch.Tensor:
+    """Records [n, h, W] for pairs [n, h, 2, bs, d]; optionally metadata and dequantised pairs.
+
+    kmin/kmax, when given, are [h, cap, d] in the pairs' dtype (written at first_block + b).
+    """
+    require_cuda(pairs)
+    n, h, two, bs, d = pairs.shape
+    if two != 2:
+        raise ValueError(f"expected a [..., 2, block_size, head_dim] KV pair, got {tuple(pairs.shape)}")
+    pairs = pairs.contiguous()
+    w = packed_pair_bytes(bs, d)
+    if records is None:
+        records = torch.empty((n, h, w), dtype=torch.uint8, device=pairs.device)
+    m_head = 0 if kmin is None else kmin.stride(-3)
+    call("lkv_pack_int8", ptr(pairs), dtype_code(pairs.dtype), n, h, bs, d, ptr(records), ptr(kmin), ptr(kmax), m_head, first_block,
+         ptr(deq), stream_handle(pairs.device))
+    return records
+
+
+def unpack_int8(records: torch.Tensor, block_size: int, head_dim: int, dtype: torch.dtype) -> torch.Tensor:
+    """[m, W] uint8 records -> [m, 2, bs, d] in `dtype`, bit-exact with the reference's unpack."""
+    require_cuda(records)
+    out = torch.empty((records.shape[0], 2, block_size, head_dim), dtype=dtype, device=records.device)
+    if records.shape[0]:
+        call("lkv_unpack_int8", ptr(records.contiguous()), records.shape[0], block_size, head_dim, ptr(out), dtype_code(dtype),
+             stream_handle(records.device))
+    return out
+
+
+def fetch_pairs(src: torch.Tensor, src_rows: torch.Tensor, dst: torch.Tensor, dst_rows: torch.Tensor, block_size: int, head_dim: int) -> None:
+    """dst row dst_rows[i] <- src row src_rows[i]; int8 records are dequantised into dst's dtype."""
+    kind = L.LKV_COLD_INT8 if src.dtype == torch.uint8 else L.LKV_COLD_PAIRS
+    n = src_rows.numel()
+    if n == 0:
+        return
+    call("lkv_fetch_pairs", ptr(src), kind, ptr(src_rows), ptr(dst), ptr(dst_rows), n, block_size, head_dim, dtype_code(dst.dtype),
+         stream_handle(dst.device))
+
+
+def quest_topk(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int, n_cand: int, k: int,
+               bound_dtype: torch.dtype | None = None, out_blocks: torch.Tensor | None = None, want_bound: bool = False,
+               bitmap: torch.Tensor | None = None, ws_slot: int = 0) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Top-k block ids [h, k] (int32, descending bound, ties by lower id) over candidates
+    [first_block, first_block + n_cand) of metadata [h, cap, d]; optionally the bounds [h, n_cand]."""
+    dev = require_cuda(query, kmin, kmax)
+    hq, d = query.shape[-3] if query.dim() == 4 else query.shape[0], query.shape[-1]
+    q = query.reshape(hq, d).contiguous()
+    h = kmin.shape[-3]
+    bound_dtype = bound_dtype or q.dtype
+    if out_blocks is None:
+        out_blocks = torch.empty((h, k), dtype=torch.int32, device=dev)
+    if out_blocks.stride(-1) != 1 or out_blocks.shape[-1] < k:
+        raise ValueError("quest_topk: out_blocks must be [h, >=k] int32 with unit column stride")
+    bound = torch.empty((h, n_cand), dtype=torch.float32, device=dev) if want_bound else None
+    nbytes = int(L.lib().lkv_quest_topk_workspace(h, n_cand))
+    ws = workspace(dev, nbytes, ws_slot)
+    words = 0 if bitmap is None else bitmap.shape[-1]
+    call("lkv_quest_topk", ptr(q), dtype_code(q.dtype), hq, h, d, ptr(kmin), ptr(kmax), dtype_code(kmin.dtype), kmin.stride(-3),
+         first_block, n_cand, k, dtype_code(bound_dtype), ptr(out_blocks), out_blocks.stride(0), ptr(bound), ptr(bitmap), words, ptr(ws), ws.numel(),
+         stream_handle(dev))
+    return out_blocks, bound
+
+
+def attention_workspace_bytes(h: int, hq: int, d: int, n_items: int) -> int:
+    return int(L.lib().lkv_attention_workspace(h, hq, d, n_items))
+
+
+def hot_attention(query: torch.Tensor, k_base: torch.Tensor, v_base: torch.Tensor, strides: tuple[int, int, int], blocks: torch.Tensor,
+                  last_fill: int, scale: float, block_size: int, slot_of: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                  lse: torch.Tensor | None = None, ws_slot: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Attention of query [hq, d] over, per KV head j, the blocks listed in blocks[j] (int32 [h, n]).
+
+    Block b of head j is storage row slot_of[j, b] (or b), its key (t, c) at
+    k_base[row*s_row + j*s_head + t*s_tok + c]; the last listed block has `last_fill` live tokens.
+    Returns float32 (out [hq, d], lse [hq]).
+    """
+    dev = require_cuda(query, k_base, v_base, blocks)
+    hq, d = query.shape[-3] if query.dim() == 4 else query.shape[0], query.shape[-1]
+    q = query.reshape(hq, d).contiguous()
+    h, n = blocks.shape
+    out = torch.empty((hq, d), dtype=torch.float32, device=dev) if out is None else out
+    lse = torch.empty((hq,), dtype=torch.float32, device=dev) if lse is None else lse
+    ws = workspace(dev, attention_workspace_bytes(h, hq, d, n), ws_slot)
+    s_row, s_head, s_tok = strides
+    call("lkv_hot_attention", ptr(q), hq, h, d, block_size, ptr(k_base), ptr(v_base), dtype_code(k_base.dtype), s_row, s_head, s_tok,
+         ptr(blocks), n, ptr(slot_of), 0 if slot_of is None else slot_of.stride(0), last_fill, scale, ptr(out), ptr(lse), ptr(ws), ws.numel(),
+         stream_handle(dev))
+    return out, lse
+
+
+def cold_attention(query: torch.Tensor, cold: torch.Tensor, block_size: int, first_block: int, n_blocks: int, scale: float,
+                   excluded: torch.Tensor | None = None, dtype: torch.dtype | None = None, out: torch.Tensor | None = None,
+                   lse: torch.Tensor | None = None, ws_slot: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Exact attention of query [hq, d] over blocks [first_block, first_block + n_blocks) of the
+    cold store, minus the blocks set in excluded [h, words] (uint32 bitmap, viewed as int32).
+
+    cold: int8 records [blocks, h, W] (uint8) or pairs [blocks, h, 2, bs, d]. Returns float32
+    (out [hq, d], lse [hq]); a head with nothing left gets lse = -inf and out = 0.
+    """
+    dev = require_cuda(query, cold)
+    hq, d = query.shape[-3] if query.dim() == 4 else query.shape[0], query.shape[-1]
+    q = query.reshape(hq, d).contiguous()
+    h = cold.shape[1]
+    kind = L.LKV_COLD_INT8 if cold.dtype == torch.uint8 else L.LKV_COLD_PAIRS
+    dt = q.dtype if dtype is None else dtype
+    if kind == L.LKV_COLD_PAIRS and cold.dtype != dt:
+        raise ValueError(f"cold pairs are {cold.dtype} but the query is {dt}")
+    out = torch.empty((hq, d), dtype=torch.float32, device=dev) if out is None else out
+    lse = torch.empty((hq,), dtype=torch.float32, device=dev) if lse is None else lse
+    ws = workspace(dev, attention_workspace_bytes(h, hq, d, n_blocks), ws_slot)
+    words = 0 if excluded is None else excluded.shape[-1]
+    call("lkv_cold_attention", ptr(q), hq, h, d, block_size, ptr(cold), kind, dtype_code(dt), first_block, n_blocks, ptr(excluded), words,
+         scale, ptr(out), ptr(lse), ptr(ws), ws.numel(), stream_handle(dev))
+    return out, lse
+
+
+def lse_merge(outs: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None,
+              lse_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Merge partials outs [p, rows, d] / lses [p, rows] (float32) into (out [rows, d], lse [rows])."""
+    dev = require_cuda(outs, lses)
+    p, rows, d = outs.shape
+    out = torch.empty((rows, d), dtype=out_dtype, device=dev) if out is None else out
+    lse_out = torch.empty((rows,), dtype=torch.float32, device=dev) if lse_out is None else lse_out
+    call("lkv_lse_merge", ptr(outs.contiguous()), ptr(lses.contiguous()), p, rows, d, ptr(out), dtype_code(out.dtype), ptr(lse_out),
+         stream_handle(dev))
+    return out, lse_out
+
+
+def bitmap_words(n_blocks: int) -> int:
+    """uint32 words of a per-head block bitmap covering block ids [0, n_blocks)."""
+    return max(1, math.ceil(n_blocks / 32))
