@@ -29,6 +29,14 @@ def bf16_ulp_diff(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return f32_ulp_diff(a, b) >> 16
 
 
+def bf16_close(got: np.ndarray, want: np.ndarray, tol: float = 2e-5) -> bool:
+    """A bf16 result is the bf16 rounding of a value within `tol` (relative to max|want|) of `want`:
+    |got - want| <= 2^-8 |want| (half a bf16 unit) + tol * max|want|, elementwise."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return bool(np.all(np.abs(got - want) <= 2.0**-8 * np.abs(want) + tol * np.abs(want).max()))
+
+
 def index_parity(ours: np.ndarray, ref: np.ndarray, bound: np.ndarray, tie_tol: float = 0.0) -> dict[str, int]:
     """Compare two top-K index lists [h, K] (candidate ids) under the tie rule.
 

@@ -13,7 +13,7 @@ import torch
 
 import oracle as O
 from tests.golden import inputs as I
-from tests.parity import bf16_ulp_diff, golden, index_parity
+from tests.parity import bf16_close, golden, index_parity
 
 pytestmark = pytest.mark.gpu
 
@@ -245,7 +245,7 @@ def test_int8_exact_step_matches_the_oracle_composition(fill: int) -> None:
     live = min(fill, 9)
     cur[:, :, :live] = tail[:, :, :live]
     if fill > 9:
-        cur[:, :, 9:fill] = torch.randn(8, 2, fill - 9, 64, device=DEV).bfloat16()
+        cur[:, :, 9:fill] = torch.randn(8, 2, fill - 9, 64, generator=torch.Generator().manual_seed(fill)).bfloat16().to(DEV)
     kmin = torch.empty((8, n, 64), dtype=torch.bfloat16, device=DEV)
     kmax = torch.empty_like(kmin)
     deq = torch.empty_like(pairs)
@@ -269,9 +269,9 @@ def test_int8_exact_step_matches_the_oracle_composition(fill: int) -> None:
     assert _rel(cold.view(8, 4, 64).cpu().numpy(), r["cold_out"]) < 1e-5
     assert _rel(lse.view(8, 4).cpu().numpy(), r["lse"]) < 1e-5
     # The merged output before its cast is within 1e-5 of the float64 composition; the bf16 output
-    # is that value rounded, so it is within one bf16 unit of the composition rounded to bf16
-    # (bf16 rounding alone is up to 2^-8 relative, so a relative bar on it would test the format).
+    # is that value rounded, so it is within half a bf16 unit plus that tolerance of the composition
+    # (bf16 rounding alone is up to 2^-8 relative, so a plain relative bar on it would test the format).
     assert _rel(out32.view(8, 4, 64).cpu().numpy(), r["out"]) < 1e-5
-    assert bf16_ulp_diff(out.float().view(8, 4, 64).cpu().numpy(), O.bf16_round(r["out"].astype(np.float32))).max() <= 1
+    assert bf16_close(out.float().view(8, 4, 64).cpu().numpy(), r["out"])
     if fill == 9:
         assert _rel(out32.view(8, 4, 64).cpu().numpy(), E["int8_out"]) < 2e-3
