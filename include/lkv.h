@@ -95,6 +95,21 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
                    void* stream);
 
 /*
+ * lkv_quest_topk without a workspace argument, for callers that cannot allocate device memory
+ * when they select (an allocator-free runtime, an allocator callback, a process that reserved all
+ * device memory up front). No counterpart in the reference. Same arguments, results and errors
+ * as lkv_quest_topk; its scratch is a fixed 4 MiB device array inside the library, so it takes
+ * h * n_cand <= 524,288 and returns LKV_ERR_ARG above that. It allocates nothing. The first call
+ * on a device looks up that array's device address (make it before any stream capture); calls
+ * must run with the stream's device current. All calls share the array: calls that overlap on
+ * the GPU race, so serialise them (one stream, or events).
+ */
+int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
+                           const void* kmax, int meta_dtype, int64_t m_head, int first_block,
+                           int n_cand, int k, int bound_mode, int32_t* out_blocks, int out_ld,
+                           float* out_bound, uint32_t* bitmap, int bitmap_words, void* stream);
+
+/*
  * Split decode attention over listed blocks, emitting (normalised out, lse). Replaces the gather
  * + SDPA + GPU log-sum-exp of lazykv/tiered.py:465-487, lazykv/attention.py:97-136 and
  * lazykv/exact.py:380-393.

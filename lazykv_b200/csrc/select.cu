@@ -12,6 +12,8 @@
 // workspace, L2-resident) finds the k-th largest key exactly (keys are unique); the keys at or
 // above it are compacted into shared memory, bitonic-sorted descending and written out as block
 // ids. The optional bitmap marks the selected block ids for the exact pass's complement.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace lkv {
@@ -259,3 +261,61 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
 }
 
 }  // extern "C"
+
+// ---- allocation-free top-k -------------------------------------------------------------------
+//
+// Some callers cannot allocate device memory at the point where they select blocks: an
+// allocator-free serving runtime, code running inside an allocator callback or under a
+// framework's memory guard, or a host that has reserved all device memory up front. For them,
+// lkv_quest_topk_noalloc keeps its scratch (the 64-bit (bound, block) keys the score kernel writes
+// and the select kernel reads) in the fixed array below instead of a caller workspace.
+
+namespace lkv {
+namespace {
+
+// 4 MiB of keys: h * n_cand <= 524,288 (e.g. 8 KV heads x 65,536 candidate blocks, a 1M-token
+// context in 16-token blocks). Every device that loads the library holds it until exit.
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+static __device__ __align__(256) uint64_t g_topk_scratch[kNoAllocScratchBytes / sizeof(uint64_t)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_topk_scratch on the current device, looked up once per device. In host
+// code the array's name is only a stand-in for the symbol, never an address to pass to a kernel.
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LKV_ERR_ARG, "lkv_quest_topk_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_topk_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(LKV_ERR_CUDA, "lkv_quest_topk_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return LKV_OK;
+}
+
+}  // namespace
+}  // namespace lkv
+
+extern "C" int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
+                                      const void* kmax, int meta_dtype, int64_t m_head, int first_block, int n_cand,
+                                      int k, int bound_mode, int32_t* out_blocks, int out_ld, float* out_bound,
+                                      uint32_t* bitmap, int bitmap_words, void* stream) {
+  const size_t need = lkv_quest_topk_workspace(h, n_cand);
+  if (need > kNoAllocScratchBytes)
+    return fail(LKV_ERR_ARG, "lkv_quest_topk_noalloc: %d heads x %d candidates need %zu bytes of scratch, above its fixed %zu (h * n_cand <= %zu)",
+                h, n_cand, need, kNoAllocScratchBytes, kNoAllocScratchBytes / sizeof(uint64_t));
+  void* scratch = nullptr;
+  if (int rc = scratch_address(&scratch)) return rc;
+  // Nothing in the scratch has to start at zero: the score kernel writes every key the select
+  // kernel reads. Calls whose kernels overlap on the GPU share the array and race.
+  return lkv_quest_topk(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode,
+                        out_blocks, out_ld, out_bound, bitmap, bitmap_words, scratch, kNoAllocScratchBytes, stream);
+}
