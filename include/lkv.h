@@ -142,6 +142,52 @@ int lkv_cold_attention(const void* q, int hq, int h, int d, int bs, const void* 
                        float* lse, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The hot set of lkv_exact_attention: the arguments of lkv_hot_attention, as a struct.
+ */
+typedef struct {
+  const void* k_base;
+  const void* v_base;
+  int dtype;
+  int64_t s_row, s_head, s_tok;
+  const int32_t* blocks;
+  int n_list;
+  const int32_t* slot_of;
+  int64_t slot_stride;
+  int last_fill;
+} lkv_hot_set;
+
+/* The cold set of lkv_exact_attention: the arguments of lkv_cold_attention, as a struct. */
+typedef struct {
+  const void* store;
+  int kind;
+  int first_block;
+  int n_blocks;
+  const uint32_t* excluded;
+  int bitmap_words;
+} lkv_cold_set;
+
+/*
+ * Both passes and their merge in one launch (plus one small combine): replaces the GPU attention,
+ * the CPU pass and the blend of lazykv/exact.py:225-264 (ExactTieredCache.merge). The hot and cold
+ * partials are computed by one grid whose CTAs take chunks of either set; the combine writes the
+ * merged out [hq, d] in out_dtype and lse [hq] (both optional), and optionally the per-set
+ * partials part_out [2, hq, d] / part_lse [2, hq] (hot first), float32. q is in hot->dtype.
+ * Workspace: lkv_exact_attention_workspace(h, hq, d, n_list, n_blocks) bytes.
+ */
+size_t lkv_exact_attention_workspace(int h, int hq, int d, int n_list, int n_blocks);
+int lkv_exact_attention(const void* q, int hq, int h, int d, int bs, const lkv_hot_set* hot,
+                        const lkv_cold_set* cold, float scale, void* out, int out_dtype,
+                        float* lse, float* part_out, float* part_lse, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/*
+ * Status word of the kernels that wait on shared-memory barriers (bounded waits): 0 when no wait
+ * ran out, else the first code recorded (1 = a wait timed out). Synchronous; clears it if asked.
+ * No reference counterpart (the reference has no device-side waits).
+ */
+int lkv_device_status(int* status, int clear);
+
+/*
  * Log-sum-exp merge of n_parts partials. Replaces lazykv/exact.py:69-85 merge_lse (n_parts = 2)
  * and is the cross-GPU merge of all-gathered shard partials. outs [n_parts, rows, d] and lses
  * [n_parts, rows] float32 -> out [rows, d] in out_dtype, lse_out [rows] float32 (optional).

@@ -36,7 +36,23 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_hot_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_cold_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_lse_merge": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_int, c_void_p, c_void_p]),
+    "lkv_exact_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "lkv_exact_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "lkv_device_status": (c_int, [c_void_p, c_int]),
 }
+
+
+class HotSet(ctypes.Structure):
+    """lkv_hot_set of include/lkv.h."""
+
+    _fields_ = [("k_base", c_void_p), ("v_base", c_void_p), ("dtype", c_int), ("s_row", c_int64), ("s_head", c_int64), ("s_tok", c_int64),
+                ("blocks", c_void_p), ("n_list", c_int), ("slot_of", c_void_p), ("slot_stride", c_int64), ("last_fill", c_int)]
+
+
+class ColdSet(ctypes.Structure):
+    """lkv_cold_set of include/lkv.h."""
+
+    _fields_ = [("store", c_void_p), ("kind", c_int), ("first_block", c_int), ("n_blocks", c_int), ("excluded", c_void_p), ("bitmap_words", c_int)]
 
 
 class LkvError(RuntimeError):

@@ -1,0 +1,53 @@
+// TMA bulk copies and bounded mbarrier waits (sm_90+ PTX, used on sm_100a by attention.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace lkv {
+
+// Status word of the kernels that wait on mbarriers: 0, or the first LKV_DEV_* code a kernel
+// recorded; read by lkv_device_status. Defined here because attention.cu, which holds those kernels
+// and that entry point, is the only translation unit that includes this header.
+__device__ int g_device_status = 0;
+constexpr int LKV_DEV_WAIT_TIMEOUT = 1;       // an mbarrier wait ran out of iterations
+constexpr uint32_t kMaxWaitIters = 1u << 22;  // each try_wait also suspends for a bounded time
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Makes initialised mbarriers visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// One bulk copy global -> this CTA's shared memory (16-byte aligned addresses, size a multiple of
+// 16), completing `bytes` of transaction count on `bar`. No multicast.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Waits for the phase of `bar` with the given parity. Gives up after kMaxWaitIters tries, records
+// LKV_DEV_WAIT_TIMEOUT in g_device_status and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  atomicCAS(&g_device_status, 0, LKV_DEV_WAIT_TIMEOUT);
+  return false;
+}
+
+}  // namespace lkv

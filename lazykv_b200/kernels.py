@@ -6,6 +6,7 @@ tensors (or device views of pinned host memory); there is no CPU path.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -178,3 +179,40 @@ def lse_merge(outs: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtype = t
 def bitmap_words(n_blocks: int) -> int:
     """uint32 words of a per-head block bitmap covering block ids [0, n_blocks)."""
     return max(1, math.ceil(n_blocks / 32))
+
+
+def exact_attention(query: torch.Tensor, k_base: torch.Tensor, v_base: torch.Tensor, strides: tuple[int, int, int], blocks: torch.Tensor,
+                    last_fill: int, cold: torch.Tensor, first_block: int, n_blocks: int, scale: float, block_size: int,
+                    excluded: torch.Tensor | None = None, slot_of: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+                    out: torch.Tensor | None = None, lse: torch.Tensor | None = None, parts: tuple[torch.Tensor, torch.Tensor] | None = None,
+                    ws_slot: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Hot pass, cold pass and their merge in one launch (plus the combine).
+
+    The hot set is as in `hot_attention`, the cold set as in `cold_attention`; returns the merged
+    (out [hq, d] in `out_dtype`, lse [hq] float32). `parts`, when given, receives the per-set float32
+    partials (out [2, hq, d], lse [2, hq]), hot first.
+    """
+    dev = require_cuda(query, k_base, v_base, blocks, cold)
+    hq, d = query.shape[-3] if query.dim() == 4 else query.shape[0], query.shape[-1]
+    q = query.reshape(hq, d).contiguous()
+    h, n = blocks.shape
+    out_dtype = out_dtype or q.dtype
+    out = torch.empty((hq, d), dtype=out_dtype, device=dev) if out is None else out
+    lse = torch.empty((hq,), dtype=torch.float32, device=dev) if lse is None else lse
+    ws = workspace(dev, int(L.lib().lkv_exact_attention_workspace(h, hq, d, n, n_blocks)), ws_slot)
+    s_row, s_head, s_tok = strides
+    hot = L.HotSet(ptr(k_base), ptr(v_base), dtype_code(k_base.dtype), s_row, s_head, s_tok, ptr(blocks), n, ptr(slot_of),
+                   0 if slot_of is None else slot_of.stride(0), last_fill)
+    kind = L.LKV_COLD_INT8 if cold.dtype == torch.uint8 else L.LKV_COLD_PAIRS
+    cs = L.ColdSet(ptr(cold), kind, first_block, n_blocks, ptr(excluded), 0 if excluded is None else excluded.shape[-1])
+    po, pl = (None, None) if parts is None else parts
+    call("lkv_exact_attention", ptr(q), hq, h, d, block_size, ctypes.byref(hot), ctypes.byref(cs), scale, ptr(out), dtype_code(out.dtype),
+         ptr(lse), ptr(po), ptr(pl), ptr(ws), ws.numel(), stream_handle(dev))
+    return out, lse
+
+
+def device_status(clear: bool = True) -> int:
+    """Status word of the kernels with bounded waits (0 = no wait ran out). Synchronises."""
+    st = ctypes.c_int(0)
+    call("lkv_device_status", ctypes.byref(st), int(clear))
+    return st.value
