@@ -168,7 +168,8 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev) -> tuple[
         sel_off = int(has_sink)
         if has_cur:
             L.list[:, -1] = nblk  # local id of the current block
-        K.quest_topk(L.q, L.kmin, L.kmax, cand_lo - lo, n_cand, k_local, out_blocks=L.list[:, sel_off : sel_off + k_local], bitmap=L.bitmap)
+        K.quest_topk(L.q, L.kmin, L.kmax, cand_lo - lo, n_cand, k_local, out_blocks=L.list[:, sel_off : sel_off + k_local], bitmap=L.bitmap,
+                     by_block=True)
         # Steady-state residency: slot s holds the s-th listed block of each head.
         L.pool = torch.zeros((n_slots, HKV, 2, BS, D), dtype=torch.bfloat16, device=dev)
         L.slot_of = torch.zeros((HKV, nblk + 1), dtype=torch.int32, device=dev)
@@ -208,7 +209,7 @@ def layer_step(L, geo: dict, cold_store=None, events: list | None = None) -> Non
 
     mark()
     K.quest_topk(L.q, L.kmin, L.kmax, geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["k_local"],
-                 out_blocks=L.list[:, geo["sel_off"] : geo["sel_off"] + geo["k_local"]], bitmap=L.bitmap)
+                 out_blocks=L.list[:, geo["sel_off"] : geo["sel_off"] + geo["k_local"]], bitmap=L.bitmap, by_block=True)
     mark()
     K.exact_attention(L.q, L.pool, L.pool[:, :, 1], (HKV * 2 * BS * D, 2 * BS * D, D), L.list, BS, L.records if cold_store is None else cold_store,
                       geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["scale"], BS, excluded=L.bitmap, slot_of=L.slot_of, out=L.out, lse=L.lse)

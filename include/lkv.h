@@ -30,6 +30,9 @@ typedef enum {
 /* Element types of KV, metadata and queries. */
 typedef enum { LKV_F32 = 0, LKV_BF16 = 1 } lkv_dtype;
 
+/* Order of a top-k list: descending bound then ascending id (top_blocks' order), or ascending id. */
+typedef enum { LKV_ORDER_BOUND = 0, LKV_ORDER_BLOCK = 1 } lkv_order;
+
 /* Cold-tier storage: int8 records (lazykv/quant.py:73-87) or whole pairs in the model dtype. */
 typedef enum { LKV_COLD_INT8 = 0, LKV_COLD_PAIRS = 1 } lkv_cold_kind;
 
@@ -83,16 +86,18 @@ int lkv_fetch_pairs(const void* src, int src_kind, const int64_t* src_rows, void
  * q [hq, d] (q_dtype); kmin/kmax [h, cap, d] (meta_dtype, row stride m_head per head);
  * candidates are blocks [first_block, first_block + n_cand). bound_mode LKV_BF16 rounds as the
  * reference's bf16 matmuls do, LKV_F32 keeps float32. Output: out_blocks [h, k] (row stride
- * out_ld >= k) block ids in descending bound order, ties by ascending block id. Optional: out_bound [h, n_cand] float32;
+ * out_ld >= k) block ids; with LKV_ORDER_BOUND in descending bound order, ties by ascending block
+ * id (the selected set is the same either way; ties at the k-th bound go to the lower ids), with
+ * LKV_ORDER_BLOCK in ascending block id (no sort). Optional: out_bound [h, n_cand] float32;
  * bitmap [h, bitmap_words] set exactly at the selected block ids (the words are cleared first).
  * Workspace: lkv_quest_topk_workspace(h, n_cand) bytes.
  */
 size_t lkv_quest_topk_workspace(int h, int n_cand);
 int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
                    const void* kmax, int meta_dtype, int64_t m_head, int first_block, int n_cand,
-                   int k, int bound_mode, int32_t* out_blocks, int out_ld, float* out_bound,
-                   uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes,
-                   void* stream);
+                   int k, int bound_mode, int order, int32_t* out_blocks, int out_ld,
+                   float* out_bound, uint32_t* bitmap, int bitmap_words, void* workspace,
+                   size_t workspace_bytes, void* stream);
 
 /*
  * lkv_quest_topk without a workspace argument, for callers that cannot allocate device memory
@@ -106,8 +111,9 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
  */
 int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
                            const void* kmax, int meta_dtype, int64_t m_head, int first_block,
-                           int n_cand, int k, int bound_mode, int32_t* out_blocks, int out_ld,
-                           float* out_bound, uint32_t* bitmap, int bitmap_words, void* stream);
+                           int n_cand, int k, int bound_mode, int order, int32_t* out_blocks,
+                           int out_ld, float* out_bound, uint32_t* bitmap, int bitmap_words,
+                           void* stream);
 
 /*
  * Split decode attention over listed blocks, emitting (normalised out, lse). Replaces the gather

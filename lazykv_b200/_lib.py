@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "liblkv_sm100.so"
 
 LKV_F32, LKV_BF16 = 0, 1
 LKV_COLD_INT8, LKV_COLD_PAIRS = 0, 1
+LKV_ORDER_BOUND, LKV_ORDER_BLOCK = 0, 1
 
 _lib: ctypes.CDLL | None = None
 
@@ -30,8 +31,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_unpack_int8": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_int, c_void_p]),
     "lkv_fetch_pairs": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),
     "lkv_quest_topk_workspace": (c_size_t, [c_int, c_int]),
-    "lkv_quest_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
-    "lkv_quest_topk_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p]),
+    "lkv_quest_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "lkv_quest_topk_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p]),
     "lkv_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
     "lkv_hot_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_cold_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

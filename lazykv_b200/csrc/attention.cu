@@ -35,6 +35,7 @@ constexpr int kMinChunk = 16;             // blocks per CTA at least (4 per warp
 constexpr int kTargetCtas = 2 * kNumSMs;  // two resident CTAs per SM
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kLazy = 8.0f;  // log2-domain headroom of the lazy rescaling (weights <= 256)
 
 enum SegKind { SEG_LIST = 0, SEG_RANGE_REC = 1, SEG_RANGE_PAIRS = 2 };
 
@@ -564,29 +565,43 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
         sc[r][i] = acc.x + acc.y;
       }
     }
-    // ---- softmax update ----
-    float pr[G][TPL];
+    // ---- softmax update (lazy rescaling) ----
+    // m is a reference maximum, not the running one: weights exp2(s - m) may reach 2^kLazy before
+    // the accumulators are rescaled, so a block needs the warp-wide maximum only when one of its
+    // scores passes m + kLazy (one vote instead of a max reduction per row and block).
+    bool need = false;
 #pragma unroll
     for (int r = 0; r < G; ++r) {
-      float mb = -INFINITY;
 #pragma unroll
       for (int i = 0; i < TPL; ++i) {
 #pragma unroll
         for (int off = 1; off < CG; off <<= 1) sc[r][i] += __shfl_xor_sync(0xffffffffu, sc[r][i], off);
         if (tl + TL * i >= live) sc[r][i] = -INFINITY;
-        mb = fmaxf(mb, sc[r][i]);
+        need |= sc[r][i] > m[r] + kLazy;
       }
+    }
+    if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
-      for (int off = CG; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-      if (mb > m[r]) {
-        const float alpha = exp2f(m[r] - mb);  // 0 when m was -inf
-        l[r] *= alpha;
-        zs[r] *= alpha;
-        const float2 a2 = f2(alpha, alpha);
+      for (int r = 0; r < G; ++r) {
+        float mb = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) o2[r][w] = __fmul2_rn(o2[r][w], a2);
-        m[r] = mb;
+        for (int i = 0; i < TPL; ++i) mb = fmaxf(mb, sc[r][i]);
+#pragma unroll
+        for (int off = CG; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        if (mb > m[r] + kLazy) {
+          const float alpha = exp2f(m[r] - mb);  // 0 when m was -inf
+          l[r] *= alpha;
+          zs[r] *= alpha;
+          const float2 a2 = f2(alpha, alpha);
+#pragma unroll
+          for (int w = 0; w < 8; ++w) o2[r][w] = __fmul2_rn(o2[r][w], a2);
+          m[r] = mb;
+        }
       }
+    }
+    float pr[G][TPL];
+#pragma unroll
+    for (int r = 0; r < G; ++r) {
 #pragma unroll
       for (int i = 0; i < TPL; ++i) {
         pr[r][i] = m[r] == -INFINITY ? 0.0f : exp2f(sc[r][i] - m[r]);
@@ -709,60 +724,91 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
 // ============================================================================================
 
 // Fold the splits of each segment (segment 0: [0, n0), segment 1: [n0, n0 + n1)) of each (head,
-// query row) into per-segment (out, lse) and their merge. Outputs may be null.
+// query row) into per-segment (out, lse) and their merge. One CTA per (head, row): the threads split
+// the channels x the splits so the partials are read with independent loads. Outputs may be null.
+constexpr int kCombineThreads = 256;
+
 template <typename TO, int G, int D>
-__global__ void attn_combine_kernel(const float* __restrict__ part, int n0, int n1, TO* __restrict__ out, float* __restrict__ lse,
-                                    float* __restrict__ seg_out, float* __restrict__ seg_lse, int hq) {
-  const int j = blockIdx.x;
+__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const float* __restrict__ part, int n0, int n1, TO* __restrict__ out,
+                                                                       float* __restrict__ lse, float* __restrict__ seg_out,
+                                                                       float* __restrict__ seg_lse, int hq) {
+  constexpr int KS = kCombineThreads / D;  // split lanes per channel
+  __shared__ float red_m[kCombineThreads / 32];
+  __shared__ float acc_o[KS][D];
+  __shared__ float acc_l[KS];
+  __shared__ float seg_M[2], seg_L[2];
+  __shared__ float seg_O[2][D];
+  const int j = blockIdx.x, r = blockIdx.y;
   const int nt = n0 + n1;
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    const int r = e / D, c = e % D;
-    float Ms[2], Ls[2], Os[2];
+  const int c = threadIdx.x % D, k = threadIdx.x / D;
+  const int64_t stride = G * (D + 2);
+  const float* base = part + (int64_t)j * nt * stride;
+#pragma unroll
+  for (int sgi = 0; sgi < 2; ++sgi) {
+    const int a = sgi == 0 ? 0 : n0, b = sgi == 0 ? n0 : nt;
+    float mloc = -INFINITY;
+    for (int sp = a + threadIdx.x; sp < b; sp += kCombineThreads) mloc = fmaxf(mloc, base[sp * stride + r]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
+    if ((threadIdx.x & 31) == 0) red_m[threadIdx.x >> 5] = mloc;
+    __syncthreads();
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kCombineThreads / 32; ++w) M = fmaxf(M, red_m[w]);
+    float O = 0.0f, L = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll 4
+      for (int sp = a + k; sp < b; sp += KS) {
+        const float* ps = base + sp * stride;
+        const float ms = ps[r];
+        const float f = ms == -INFINITY ? 0.0f : exp2f(ms - M);
+        O = fmaf(ps[2 * G + r * D + c], f, O);
+        L = fmaf(ps[G + r], f, L);
+      }
+    }
+    acc_o[k][c] = O;
+    if (c == 0) acc_l[k] = L;
+    __syncthreads();
+    if (k == 0) {
+      float Os = 0.0f, Ls = 0.0f;
+#pragma unroll
+      for (int q = 0; q < KS; ++q) {
+        Os += acc_o[q][c];
+        Ls += acc_l[q];
+      }
+      seg_O[sgi][c] = Os;
+      if (c == 0) {
+        seg_M[sgi] = M;
+        seg_L[sgi] = Ls;
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x >= D) return;
+  const int64_t row = (int64_t)j * G + r;
+  if (seg_out != nullptr) {
 #pragma unroll
     for (int sgi = 0; sgi < 2; ++sgi) {
-      const int a = sgi == 0 ? 0 : n0, b = sgi == 0 ? n0 : nt;
-      float M = -INFINITY;
-      for (int sp = a; sp < b; ++sp) M = fmaxf(M, part[((int64_t)j * nt + sp) * G * (D + 2) + r]);
-      float O = 0.0f, L = 0.0f;
-      if (M != -INFINITY) {
-        for (int sp = a; sp < b; ++sp) {
-          const float* ps = part + ((int64_t)j * nt + sp) * G * (D + 2);
-          const float ms = ps[r];
-          if (ms == -INFINITY) continue;
-          const float f = exp2f(ms - M);
-          L = fmaf(ps[G + r], f, L);
-          O = fmaf(ps[2 * G + r * D + c], f, O);
-        }
-      }
-      Ms[sgi] = M;
-      Ls[sgi] = L;
-      Os[sgi] = O;
+      const bool empty = !(seg_L[sgi] > 0.0f);
+      seg_out[(int64_t)sgi * hq * D + row * D + c] = empty ? 0.0f : seg_O[sgi][c] / seg_L[sgi];
+      if (c == 0 && seg_lse != nullptr) seg_lse[(int64_t)sgi * hq + row] = empty ? -INFINITY : (seg_M[sgi] + log2f(seg_L[sgi])) * kLn2;
     }
-    const int64_t row = (int64_t)j * G + r;
-    if (seg_out != nullptr) {
+  }
+  if (out != nullptr) {
+    const float M = fmaxf(seg_M[0], seg_M[1]);
+    float O = 0.0f, L = 0.0f;
+    if (M != -INFINITY) {
 #pragma unroll
       for (int sgi = 0; sgi < 2; ++sgi) {
-        const bool empty = !(Ls[sgi] > 0.0f);
-        seg_out[(int64_t)sgi * hq * D + row * D + c] = empty ? 0.0f : Os[sgi] / Ls[sgi];
-        if (c == 0 && seg_lse != nullptr) seg_lse[(int64_t)sgi * hq + row] = empty ? -INFINITY : (Ms[sgi] + log2f(Ls[sgi])) * kLn2;
+        if (seg_M[sgi] == -INFINITY) continue;
+        const float f = exp2f(seg_M[sgi] - M);
+        O = fmaf(seg_O[sgi][c], f, O);
+        L = fmaf(seg_L[sgi], f, L);
       }
     }
-    if (out != nullptr) {
-      const float M = fmaxf(Ms[0], Ms[1]);
-      float O = 0.0f, L = 0.0f;
-      if (M != -INFINITY) {
-#pragma unroll
-        for (int sgi = 0; sgi < 2; ++sgi) {
-          if (Ms[sgi] == -INFINITY) continue;
-          const float f = exp2f(Ms[sgi] - M);
-          O = fmaf(Os[sgi], f, O);
-          L = fmaf(Ls[sgi], f, L);
-        }
-      }
-      const bool empty = !(L > 0.0f);
-      out[row * D + c] = from_f32<TO>(empty ? 0.0f : O / L);
-      if (c == 0 && lse != nullptr) lse[row] = empty ? -INFINITY : (M + log2f(L)) * kLn2;
-    }
+    const bool empty = !(L > 0.0f);
+    out[row * D + c] = from_f32<TO>(empty ? 0.0f : O / L);
+    if (c == 0 && lse != nullptr) lse[row] = empty ? -INFINITY : (M + log2f(L)) * kLn2;
   }
 }
 
@@ -847,9 +893,8 @@ int launch_all(AttnParams& p, bool use_tma, TO* out, float* lse, float* seg_out,
       attn_ldg_kernel<T, G, D><<<grid, kThreads, 0, st>>>(p);
     }
   }
-  const int threads = G * D < 1024 ? G * D : 1024;
   const int n0 = p.seg[0].n_splits, n1 = p.n_segs > 1 ? p.seg[1].n_splits : 0;
-  attn_combine_kernel<TO, G, D><<<p.h, threads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq);
+  attn_combine_kernel<TO, G, D><<<dim3(p.h, G), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq);
   return launched("lkv attention");
 }
 

@@ -19,38 +19,77 @@
 namespace lkv {
 namespace {
 
-constexpr int kScoreThreads = 128;
 constexpr int kSelectThreads = 1024;
-constexpr int kMaxK = 16384;  // shared-memory sort capacity (128 KiB of keys)
+constexpr int kMaxK = 16384;             // shared-memory sort capacity (128 KiB of keys)
+constexpr int kScoreTileBytes = 32768;   // one metadata array's tile per CTA
 
+// Rows (candidates) per scoring CTA: a 32 KiB tile of each of kmin and kmax, at most 256 rows.
+inline int score_rows(int d, size_t es) {
+  const int r = kScoreTileBytes / (int)(d * es);
+  return r < 256 ? r : 256;
+}
+
+// One thread per candidate row of a tile. The CTA first copies the tile's kmin and kmax rows
+// (contiguous in memory) into shared memory with coalesced 16-byte loads, storing 16-byte chunk c
+// of row t at chunk position c ^ (t & 7): a quarter-warp reading chunk c of 8 consecutive rows then
+// touches 8 distinct bank groups, while each thread still walks its row's channels in order.
 template <typename TQ, typename TM, int G>
-__global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(
-    const TQ* __restrict__ q, int d, const TM* __restrict__ kmin, const TM* __restrict__ kmax,
-    int64_t m_head, int first_block, int n_cand, int bound_mode, uint64_t* __restrict__ keys,
-    float* __restrict__ out_bound) {
-  extern __shared__ float qs[];  // qp [G][d] then qn [G][d]
+__global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin, const TM* __restrict__ kmax,
+                                   int64_t m_head, int first_block, int n_cand, int bound_mode, uint64_t* __restrict__ keys,
+                                   float* __restrict__ out_bound) {
+  extern __shared__ __align__(16) float qs[];  // qp [G][d], qn [G][d], then the two tiles
+  const int rows = blockDim.x;
+  const int row_bytes = d * (int)sizeof(TM);
+  const int chunks = row_bytes / 16;
+  unsigned char* tile_max = reinterpret_cast<unsigned char*>(qs + 2 * G * d);
+  unsigned char* tile_min = tile_max + (size_t)rows * row_bytes;
   const int j = blockIdx.y;
+  const int c_first = blockIdx.x * rows;
+  const int n_rows = min(rows, n_cand - c_first);
   for (int e = threadIdx.x; e < G * d; e += blockDim.x) {
     const float v = to_f32<TQ>(q[(int64_t)j * G * d + e]);
-    const float vp = fmaxf(v, 0.0f);      // q.clamp_min(0)
+    const float vp = fmaxf(v, 0.0f);   // q.clamp_min(0)
     qs[e] = vp;
-    qs[G * d + e] = __fsub_rn(v, vp);     // q - qp
+    qs[G * d + e] = __fsub_rn(v, vp);  // q - qp
   }
+  const unsigned char* gmax = reinterpret_cast<const unsigned char*>(kmax + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
+  const unsigned char* gmin = reinterpret_cast<const unsigned char*>(kmin + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
+  for (int u = threadIdx.x; u < n_rows * chunks; u += blockDim.x) {
+    const int t = u / chunks, c = u % chunks;
+    const int pos = t * row_bytes + ((c ^ (t & 7)) * 16);
+    cp_async16(tile_max + pos, reinterpret_cast<const uint4*>(gmax) + u);
+    cp_async16(tile_min + pos, reinterpret_cast<const uint4*>(gmin) + u);
+  }
+  cp_async_wait_all();
   __syncthreads();
-  const int ci = blockIdx.x * blockDim.x + threadIdx.x;
-  if (ci >= n_cand) return;
-  const int64_t row = (int64_t)j * m_head + (int64_t)(first_block + ci) * d;
-  const TM* pmax = kmax + row;
-  const TM* pmin = kmin + row;
+  const int t = threadIdx.x;
+  if (t >= n_rows) return;
   float a[G], b[G];
 #pragma unroll
   for (int r = 0; r < G; ++r) a[r] = b[r] = 0.0f;
-  for (int c0 = 0; c0 < d; c0 += 8) {
+  constexpr int PER = 16 / (int)sizeof(TM);  // elements per 16-byte chunk
+  for (int c = 0; c < chunks; ++c) {
+    const int pos = t * row_bytes + ((c ^ (t & 7)) * 16);
     float mx[8], mn[8];
-    Vec8<TM>::load(pmax + c0, mx);
-    Vec8<TM>::load(pmin + c0, mn);
+    if constexpr (PER == 8) {
+      // Plain shared-memory loads (the read-only global path cannot address shared memory).
+      const uint4 x = *reinterpret_cast<const uint4*>(tile_max + pos), y = *reinterpret_cast<const uint4*>(tile_min + pos);
+      const uint32_t wx[4] = {x.x, x.y, x.z, x.w}, wy[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 4; ++i) {
+        mx[2 * i] = __uint_as_float(wx[i] << 16);
+        mx[2 * i + 1] = __uint_as_float(wx[i] & 0xffff0000u);
+        mn[2 * i] = __uint_as_float(wy[i] << 16);
+        mn[2 * i + 1] = __uint_as_float(wy[i] & 0xffff0000u);
+      }
+    } else {
+      const float4 x = *reinterpret_cast<const float4*>(tile_max + pos), y = *reinterpret_cast<const float4*>(tile_min + pos);
+      mx[0] = x.x; mx[1] = x.y; mx[2] = x.z; mx[3] = x.w;
+      mn[0] = y.x; mn[1] = y.y; mn[2] = y.z; mn[3] = y.w;
+    }
+    const int c0 = c * PER;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
 #pragma unroll
       for (int r = 0; r < G; ++r) {
         a[r] = __fadd_rn(a[r], __fmul_rn(qs[r * d + c0 + i], mx[i]));
@@ -61,21 +100,20 @@ __global__ void __launch_bounds__(kScoreThreads) quest_score_kernel(
   float best = -INFINITY;
 #pragma unroll
   for (int r = 0; r < G; ++r) {
-    float s = bound_mode == LKV_BF16 ? bf16_round(__fadd_rn(bf16_round(a[r]), bf16_round(b[r]))) : __fadd_rn(a[r], b[r]);
-    best = fmaxf(best, s);
+    float sc = bound_mode == LKV_BF16 ? bf16_round(__fadd_rn(bf16_round(a[r]), bf16_round(b[r]))) : __fadd_rn(a[r], b[r]);
+    best = fmaxf(best, sc);
   }
+  const int ci = c_first + t;
   const uint64_t key = ((uint64_t)orderable(best) << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
   keys[(int64_t)j * n_cand + ci] = key;
   if (out_bound != nullptr) out_bound[(int64_t)j * n_cand + ci] = best == 0.0f ? 0.0f : best;
 }
 
-// Finds, among keys matching `prefix` under `mask`, the digit at `shift` holding the `remaining`-th
-// largest; called by all threads after `hist` is complete. Warp 0 scans the 256 bins from the top.
-__device__ void pick_digit(const uint32_t* hist, uint32_t* sh_digit, uint32_t* sh_remaining,
-                           uint32_t* sh_bincount) {
+// Finds the digit (8 bits at `shift` of the 32-bit bound) holding the `remaining`-th largest among
+// the keys counted in `hist`; warp 0 scans the 256 bins from the top.
+__device__ void pick_digit(const uint32_t* hist, uint32_t* sh_digit, uint32_t* sh_remaining, uint32_t* sh_bincount) {
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
-    // Lane l owns bins 255-8l .. 248-8l (highest first).
     uint32_t cnt[8];
     uint32_t sum = 0;
 #pragma unroll
@@ -107,68 +145,138 @@ __device__ void pick_digit(const uint32_t* hist, uint32_t* sh_digit, uint32_t* s
   }
 }
 
-__global__ void __launch_bounds__(kSelectThreads) topk_kernel(
-    const uint64_t* __restrict__ keys_all, int n_cand, int k, int first_block,
-    int32_t* __restrict__ out_blocks, int out_ld, uint32_t* __restrict__ bitmap, int bitmap_words) {
-  extern __shared__ uint64_t sel[];  // [P]
+// Exclusive block-wide scan of one value per thread (1024 threads); returns the prefix and writes
+// the total to *total.
+__device__ uint32_t block_scan(uint32_t v, uint32_t* warp_sums, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0u;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += x;
+    }
+    warp_sums[lane] = wi - w;
+    if (lane == 31) *total = wi;
+  }
+  __syncthreads();
+  const uint32_t r = warp_sums[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
+// One CTA per KV head. Keys (orderable bound << 32 | ~candidate) are staged in shared memory when
+// they fit. An MSB-first radix select over the 32-bit bound (4 passes; 2 for bf16 bounds, whose low
+// 16 bits carry no order) finds the k-th largest bound T and
+// how many keys at T are needed; those are the lowest candidate ids at T (the tie rule), picked by a
+// block-wide scan in candidate order. The k selected keys, in ascending candidate order after the
+// scan, are written out as block ids either in that order (by_block) or bitonic-sorted descending
+// (descending bound, ascending id: the order of top_blocks); the bitmap marks them.
+__global__ void __launch_bounds__(kSelectThreads) topk_kernel(const uint64_t* __restrict__ keys_all, int n_cand, int k, int first_block,
+                                                             int32_t* __restrict__ out_blocks, int out_ld, uint32_t* __restrict__ bitmap,
+                                                             int bitmap_words, int stage_keys, int by_block, int n_passes) {
+  extern __shared__ uint64_t smem64[];  // sel [P], then (when staged) keys [n_cand]
   __shared__ uint32_t hist[256];
-  __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_count;
-  __shared__ uint64_t sh_thr;
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total;
   const int j = blockIdx.x;
+  int P = 1;
+  const int kk = k < n_cand ? k : n_cand;
+  while (P < kk) P <<= 1;
+  uint64_t* sel = smem64;
   const uint64_t* keys = keys_all + (int64_t)j * n_cand;
+  if (stage_keys) {
+    uint64_t* ks = smem64 + (P < 2 ? 2 : P);  // 16-byte aligned
+    if ((reinterpret_cast<uintptr_t>(keys) & 15) == 0) {
+      // 16-byte async copies for the even-sized body, a plain load for an odd last key.
+      const int pairs = n_cand / 2;
+      for (int i = threadIdx.x; i < pairs; i += blockDim.x) cp_async16(ks + 2 * i, keys + 2 * i);
+      if ((n_cand & 1) && threadIdx.x == 0) ks[n_cand - 1] = keys[n_cand - 1];
+      cp_async_wait_all();
+    } else {
+      for (int i = threadIdx.x; i < n_cand; i += blockDim.x) ks[i] = keys[i];
+    }
+    keys = ks;
+  }
   if (bitmap != nullptr)
     for (int w = threadIdx.x; w < bitmap_words; w += blockDim.x) bitmap[(int64_t)j * bitmap_words + w] = 0u;
-
-  uint64_t prefix = 0, mask = 0;
   if (threadIdx.x == 0) {
-    sh_remaining = (uint32_t)k;
-    sh_count = 0;
+    sh_remaining = (uint32_t)kk;
+    sh_bincount = 0;
   }
-  bool done = (k >= n_cand);
-  for (int pass = 0; pass < 8 && !done; ++pass) {
-    const int shift = 56 - 8 * pass;
+  __syncthreads();
+
+  uint32_t prefix = 0, mask = 0;
+  bool take_all_equal = (kk >= n_cand);
+  for (int pass = 0; pass < n_passes && !take_all_equal; ++pass) {
+    const int shift = 24 - 8 * pass;
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < n_cand; i += blockDim.x) {
-      const uint64_t key = keys[i];
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    // Keys share their top bits (sign and exponent) heavily, so lanes holding the same digit add
+    // their count once per warp instead of contending on one shared-memory word.
+    for (int i0 = 0; i0 < n_cand; i0 += blockDim.x) {
+      const int i = i0 + threadIdx.x;
+      const uint32_t hi = i < n_cand ? (uint32_t)(keys[i] >> 32) : 0u;
+      const bool counted = i < n_cand && (hi & mask) == prefix;
+      const uint32_t digit = counted ? ((hi >> shift) & 255u) : 256u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+      if (counted && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
     }
     __syncthreads();
     pick_digit(hist, &sh_digit, &sh_remaining, &sh_bincount);
     __syncthreads();
-    prefix |= (uint64_t)sh_digit << shift;
-    mask |= (uint64_t)255u << shift;
-    // Every key matching the prefix is taken: the threshold is the prefix itself.
-    done = (sh_bincount == sh_remaining);
+    prefix |= sh_digit << shift;
+    mask |= 255u << shift;
+    take_all_equal = (sh_bincount == sh_remaining);
     __syncthreads();
   }
-  if (threadIdx.x == 0) sh_thr = (k >= n_cand) ? 0ull : prefix;
-  __syncthreads();
-  const uint64_t thr = sh_thr;
-  int P = 1;
-  const int kk = k < n_cand ? k : n_cand;
-  while (P < kk) P <<= 1;
-  for (int i = threadIdx.x; i < n_cand; i += blockDim.x) {
+  const uint32_t need_equal = take_all_equal ? 0xffffffffu : sh_remaining;
+
+  // Compaction in candidate order: thread t owns the contiguous range [t*seg, (t+1)*seg).
+  const int seg = (n_cand + blockDim.x - 1) / blockDim.x;
+  const int lo = threadIdx.x * seg, hi_end = min(n_cand, lo + seg);
+  uint32_t n_gt = 0, n_eq = 0;
+  for (int i = lo; i < hi_end; ++i) {
+    const uint32_t h = (uint32_t)(keys[i] >> 32) & mask;
+    n_gt += (kk >= n_cand) || h > prefix;
+    n_eq += (kk < n_cand) && h == prefix;
+  }
+  const uint32_t eq_before = block_scan(n_eq, warp_sums, &sh_total);
+  // Equal keys taken by this thread: those whose rank among equals is below need_equal.
+  uint32_t take_eq = 0;
+  if (eq_before < need_equal) take_eq = min(n_eq, need_equal - eq_before);
+  const uint32_t pos0 = block_scan(n_gt + take_eq, warp_sums, &sh_total);
+  uint32_t pos = pos0, eq_seen = 0;
+  for (int i = lo; i < hi_end; ++i) {
     const uint64_t key = keys[i];
-    if (key >= thr) {
-      const uint32_t pos = atomicAdd(&sh_count, 1u);
-      if (pos < (uint32_t)P) sel[pos] = key;
-    }
+    const uint32_t h = (uint32_t)(key >> 32) & mask;
+    bool take = (kk >= n_cand) || h > prefix;
+    if (!take && h == prefix) take = eq_seen++ < take_eq;
+    if (take && pos < (uint32_t)P) sel[pos++] = key;
   }
   __syncthreads();
   for (int i = kk + threadIdx.x; i < P; i += blockDim.x) sel[i] = 0ull;
   __syncthreads();
-  // Bitonic sort, descending.
-  for (int size = 2; size <= P; size <<= 1) {
+  // Bitonic sort, descending (skipped for ascending block-id order: the scan wrote that order).
+  for (int size = 2; size <= (by_block ? 1 : P); size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       for (int i = threadIdx.x; i < P / 2; i += blockDim.x) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool desc = (lo & size) == 0;
-        const uint64_t a = sel[lo], b = sel[hi];
+        const int lo2 = 2 * i - (i & (stride - 1));
+        const int hi2 = lo2 + stride;
+        const bool desc = (lo2 & size) == 0;
+        const uint64_t a = sel[lo2], b = sel[hi2];
         if ((a < b) == desc) {
-          sel[lo] = b;
-          sel[hi] = a;
+          sel[lo2] = b;
+          sel[hi2] = a;
         }
       }
       __syncthreads();
@@ -178,21 +286,24 @@ __global__ void __launch_bounds__(kSelectThreads) topk_kernel(
     const uint32_t ci = 0xffffffffu - (uint32_t)(sel[i] & 0xffffffffull);
     const int blk = first_block + (int)ci;
     out_blocks[(int64_t)j * out_ld + i] = blk;
-    if (bitmap != nullptr && blk / 32 < bitmap_words)
-      atomicOr(&bitmap[(int64_t)j * bitmap_words + blk / 32], 1u << (blk % 32));
+    if (bitmap != nullptr && blk / 32 < bitmap_words) atomicOr(&bitmap[(int64_t)j * bitmap_words + blk / 32], 1u << (blk % 32));
   }
 }
 
 template <typename TQ, typename TM>
-int launch_score(int g, dim3 grid, size_t smem, cudaStream_t st, const void* q, int d, const void* kmin,
-                 const void* kmax, int64_t m_head, int first_block, int n_cand, int bound_mode,
-                 uint64_t* keys, float* out_bound) {
-#define LKV_SCORE(G)                                                                            \
-  case G:                                                                                       \
-    quest_score_kernel<TQ, TM, G><<<grid, kScoreThreads, smem, st>>>(                           \
-        static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin), static_cast<const TM*>(kmax), \
-        m_head, first_block, n_cand, bound_mode, keys, out_bound);                              \
-    break;
+int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
+                 int n_cand, int bound_mode, uint64_t* keys, float* out_bound) {
+  const int rows = score_rows(d, sizeof(TM));
+  dim3 grid((n_cand + rows - 1) / rows, h);
+  const size_t smem = 2 * (size_t)g * d * sizeof(float) + 2 * (size_t)rows * d * sizeof(TM);
+#define LKV_SCORE(G)                                                                                                   \
+  case G: {                                                                                                            \
+    auto kern = quest_score_kernel<TQ, TM, G>;                                                                         \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);          \
+    kern<<<grid, rows, smem, st>>>(static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin), static_cast<const TM*>(kmax), \
+                                   m_head, first_block, n_cand, bound_mode, keys, out_bound);                          \
+    break;                                                                                                             \
+  }
   switch (g) {
     LKV_SCORE(1)
     LKV_SCORE(2)
@@ -217,7 +328,7 @@ size_t lkv_quest_topk_workspace(int h, int n_cand) {
 }
 
 int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax,
-                   int meta_dtype, int64_t m_head, int first_block, int n_cand, int k, int bound_mode,
+                   int meta_dtype, int64_t m_head, int first_block, int n_cand, int k, int bound_mode, int order,
                    int32_t* out_blocks, int out_ld, float* out_bound, uint32_t* bitmap, int bitmap_words,
                    void* workspace, size_t workspace_bytes, void* stream) {
   if (!dtype_ok(q_dtype) || !dtype_ok(meta_dtype) || !dtype_ok(bound_mode))
@@ -228,6 +339,7 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   if (k > kMaxK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
   if (first_block < 0) return fail(LKV_ERR_ARG, "lkv_quest_topk: negative first block");
   if (out_ld < k) return fail(LKV_ERR_ARG, "lkv_quest_topk: output row stride %d < k=%d", out_ld, k);
+  if (order != LKV_ORDER_BOUND && order != LKV_ORDER_BLOCK) return fail(LKV_ERR_ARG, "lkv_quest_topk: bad order %d", order);
   if (q == nullptr || kmin == nullptr || kmax == nullptr || out_blocks == nullptr || workspace == nullptr)
     return fail(LKV_ERR_PTR, "lkv_quest_topk: null pointer");
   if (!aligned(kmin, 16) || !aligned(kmax, 16) || (m_head * (int64_t)dtype_size(meta_dtype)) % 16 != 0)
@@ -239,24 +351,28 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   const int g = hq / h;
   cudaStream_t st = as_stream(stream);
   uint64_t* keys = static_cast<uint64_t*>(workspace);
-  dim3 grid((n_cand + kScoreThreads - 1) / kScoreThreads, h);
-  const size_t smem = 2 * (size_t)g * d * sizeof(float);
   int rc;
   if (q_dtype == LKV_BF16 && meta_dtype == LKV_BF16)
-    rc = launch_score<__nv_bfloat16, __nv_bfloat16>(g, grid, smem, st, q, d, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
+    rc = launch_score<__nv_bfloat16, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
   else if (q_dtype == LKV_F32 && meta_dtype == LKV_F32)
-    rc = launch_score<float, float>(g, grid, smem, st, q, d, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
+    rc = launch_score<float, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
   else if (q_dtype == LKV_BF16 && meta_dtype == LKV_F32)
-    rc = launch_score<__nv_bfloat16, float>(g, grid, smem, st, q, d, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
+    rc = launch_score<__nv_bfloat16, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
   else
-    rc = launch_score<float, __nv_bfloat16>(g, grid, smem, st, q, d, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
+    rc = launch_score<float, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
   if (rc) return rc;
   if ((rc = launched("lkv_quest_topk(score)"))) return rc;
   int P = 1;
   while (P < k) P <<= 1;
-  const size_t sel_smem = (size_t)P * sizeof(uint64_t);
-  if (sel_smem > 48 * 1024) cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sel_smem);
-  topk_kernel<<<h, kSelectThreads, sel_smem, st>>>(keys, n_cand, k, first_block, out_blocks, out_ld, bitmap, bitmap_words);
+  const size_t sel_smem = (size_t)(P < 2 ? 2 : P) * sizeof(uint64_t);
+  const int stage_keys = sel_smem + (size_t)n_cand * sizeof(uint64_t) <= 200 * 1024;
+  const size_t smem = sel_smem + (stage_keys ? (size_t)n_cand * sizeof(uint64_t) : 0);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // A bf16 bound's orderable 32-bit form has constant low 16 bits for a given sign, so its top 16
+  // bits order the keys: two 8-bit passes reach the k-th bound; ties go to the scan.
+  const int n_passes = bound_mode == LKV_BF16 ? 2 : 4;
+  topk_kernel<<<h, kSelectThreads, smem, st>>>(keys, n_cand, k, first_block, out_blocks, out_ld, bitmap, bitmap_words, stage_keys,
+                                                order == LKV_ORDER_BLOCK, n_passes);
   return launched("lkv_quest_topk(select)");
 }
 
@@ -306,7 +422,7 @@ int scratch_address(void** out) {
 
 extern "C" int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
                                       const void* kmax, int meta_dtype, int64_t m_head, int first_block, int n_cand,
-                                      int k, int bound_mode, int32_t* out_blocks, int out_ld, float* out_bound,
+                                      int k, int bound_mode, int order, int32_t* out_blocks, int out_ld, float* out_bound,
                                       uint32_t* bitmap, int bitmap_words, void* stream) {
   const size_t need = lkv_quest_topk_workspace(h, n_cand);
   if (need > kNoAllocScratchBytes)
@@ -316,6 +432,6 @@ extern "C" int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h,
   if (int rc = scratch_address(&scratch)) return rc;
   // Nothing in the scratch has to start at zero: the score kernel writes every key the select
   // kernel reads. Calls whose kernels overlap on the GPU share the array and race.
-  return lkv_quest_topk(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode,
+  return lkv_quest_topk(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode, order,
                         out_blocks, out_ld, out_bound, bitmap, bitmap_words, scratch, kNoAllocScratchBytes, stream);
 }

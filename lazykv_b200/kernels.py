@@ -89,9 +89,10 @@ def fetch_pairs(src: torch.Tensor, src_rows: torch.Tensor, dst: torch.Tensor, ds
 
 def quest_topk(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int, n_cand: int, k: int,
                bound_dtype: torch.dtype | None = None, out_blocks: torch.Tensor | None = None, want_bound: bool = False,
-               bitmap: torch.Tensor | None = None, ws_slot: int = 0) -> tuple[torch.Tensor, torch.Tensor | None]:
-    """Top-k block ids [h, k] (int32, descending bound, ties by lower id) over candidates
-    [first_block, first_block + n_cand) of metadata [h, cap, d]; optionally the bounds [h, n_cand]."""
+               bitmap: torch.Tensor | None = None, ws_slot: int = 0, by_block: bool = False) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Top-k block ids [h, k] (int32) over candidates [first_block, first_block + n_cand) of
+    metadata [h, cap, d]: descending bound with ties to the lower id, or ascending id when
+    `by_block` (the same set, no sort); optionally the bounds [h, n_cand]."""
     dev = require_cuda(query, kmin, kmax)
     hq, d = query.shape[-3] if query.dim() == 4 else query.shape[0], query.shape[-1]
     q = query.reshape(hq, d).contiguous()
@@ -106,7 +107,8 @@ def quest_topk(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, firs
     ws = workspace(dev, nbytes, ws_slot)
     words = 0 if bitmap is None else bitmap.shape[-1]
     call("lkv_quest_topk", ptr(q), dtype_code(q.dtype), hq, h, d, ptr(kmin), ptr(kmax), dtype_code(kmin.dtype), kmin.stride(-3),
-         first_block, n_cand, k, dtype_code(bound_dtype), ptr(out_blocks), out_blocks.stride(0), ptr(bound), ptr(bitmap), words, ptr(ws), ws.numel(),
+         first_block, n_cand, k, dtype_code(bound_dtype), L.LKV_ORDER_BLOCK if by_block else L.LKV_ORDER_BOUND, ptr(out_blocks),
+         out_blocks.stride(0), ptr(bound), ptr(bitmap), words, ptr(ws), ws.numel(),
          stream_handle(dev))
     return out_blocks, bound
 

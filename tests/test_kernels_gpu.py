@@ -158,6 +158,9 @@ def test_bf16_selection_is_bit_exact_with_the_oracle(case: str, seed: int, t: in
     ref_bound = I.from_bf16_np(S[f"{case}_bound"])
     par = index_parity(idx.cpu().numpy() - 1, S[f"{case}_idx"] - 1, ref_bound, tie_tol=np.abs(ref_bound).max() * 2.0**-7)
     assert par["bad"] == 0, par
+    # Ascending block-id order: the same set, no sort.
+    by_id, _ = k.quest_topk(lay["q"].to(DEV), kmin, kmax, 1, nb - 2, kk, by_block=True)
+    assert np.array_equal(by_id.cpu().numpy(), np.sort(want, axis=1))
 
 
 def test_selection_edge_cases_k_equals_candidates_and_all_ties() -> None:

@@ -49,9 +49,9 @@ def test_invalid_arguments_return_a_status_and_a_message(lib) -> None:  # noqa: 
     from lazykv_b200 import _lib
 
     # k larger than the candidates: rejected before any launch.
-    rc = lib.lkv_quest_topk(None, 1, 32, 8, 64, None, None, 1, 0, 1, 10, 11, 1, None, 11, None, None, 0, None, 0, None)
+    rc = lib.lkv_quest_topk(None, 1, 32, 8, 64, None, None, 1, 0, 1, 10, 11, 1, 0, None, 11, None, None, 0, None, 0, None)
     assert rc == 1 and "k <= n_cand" in _lib.last_error()
-    rc = lib.lkv_quest_topk(None, 1, 30, 8, 64, None, None, 1, 0, 1, 10, 5, 1, None, 5, None, None, 0, None, 0, None)
+    rc = lib.lkv_quest_topk(None, 1, 30, 8, 64, None, None, 1, 0, 1, 10, 5, 1, 0, None, 5, None, None, 0, None, 0, None)
     assert rc == 1 and "do not group" in _lib.last_error()
     rc = lib.lkv_pack_int8(None, 1, 1, 8, 12, 64, None, None, None, 0, 0, None, None)
     assert rc == 1 and "geometry" in _lib.last_error()

@@ -35,7 +35,7 @@ def _run(entry: str, q, kmin, kmax, first: int, n_cand: int, k: int, mode: int):
     words = (kmin.shape[1] + 31) // 32
     bitmap = torch.full((h, words), -1, dtype=torch.int32, device=DEV)
     common = (q.data_ptr(), _lib.dtype_code(q.dtype), q.shape[0], h, d, kmin.data_ptr(), kmax.data_ptr(), _lib.dtype_code(kmin.dtype),
-              kmin.stride(0), first, n_cand, k, mode, out.data_ptr(), k, bound.data_ptr(), bitmap.data_ptr(), words)
+              kmin.stride(0), first, n_cand, k, mode, _lib.LKV_ORDER_BOUND, out.data_ptr(), k, bound.data_ptr(), bitmap.data_ptr(), words)
     stream = torch.cuda.current_stream().cuda_stream
     if entry == "noalloc":
         before = torch.cuda.memory_stats().get("allocation.all.allocated", 0)
@@ -72,6 +72,6 @@ def test_noalloc_rejects_inputs_beyond_its_fixed_scratch() -> None:
 
     lib = _lib.lib()
     # 8 heads x 65,537 candidates need 524,296 keys; the array holds 524,288.
-    rc = lib.lkv_quest_topk_noalloc(None, 1, 32, 8, 64, None, None, 1, 0, 1, 65537, 16, 1, None, 16, None, None, 0, None)
+    rc = lib.lkv_quest_topk_noalloc(None, 1, 32, 8, 64, None, None, 1, 0, 1, 65537, 16, 1, 0, None, 16, None, None, 0, None)
     assert rc == 1  # LKV_ERR_ARG
     assert "fixed" in _lib.last_error() and "524288" in _lib.last_error()
