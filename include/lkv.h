@@ -187,6 +187,26 @@ int lkv_exact_attention(const void* q, int hq, int h, int d, int bs, const lkv_h
                         size_t workspace_bytes, void* stream);
 
 /*
+ * Residency admit on the device, fused with the fetch of the misses. Replaces the host side of
+ * lazykv/tiered.py:383-487 (rank's device-to-host copy, the numpy LRU of admit, the staged H2D and
+ * index_copy_, and the gather's last_used update), with the same LRU rule: for KV head j, chosen
+ * [h, k] (row stride chosen_ld) block ids; a chosen block with block_slot -1 misses; victims are the
+ * slots not holding a chosen block, least recently used first (ties by slot), given to the misses
+ * in chosen order; evicted blocks get block_slot -1 and evicted_at = step (evicted_at optional);
+ * every chosen slot gets last_used = step. Tables: block_slot [h, cap] int32 (pool index
+ * 1..n_slots or -1), slot_block [h, n_slots] int32, last_used [h, n_slots] int64, evicted_at [h, cap]
+ * int64. Each miss is then copied from the store (rows block*h + head: int8 records dequantised as
+ * lazykv/quant.py:unpack, or pairs in `dtype`) into pool [n_slots + 2, h, 2, bs, d] row slot*h + head.
+ * miss_blk / miss_slot [h, k] receive the misses in chosen order and n_miss [h] their count;
+ * slots_out [h, k] (row stride slots_ld, optional) the pool index of every chosen block afterwards.
+ */
+int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32_t* block_slot,
+                   int cap, int32_t* slot_block, int64_t* last_used, int n_slots,
+                   int64_t* evicted_at, int64_t step, const void* store, int store_kind, void* pool,
+                   int bs, int d, int dtype, int32_t* miss_blk, int32_t* miss_slot, int32_t* n_miss,
+                   int32_t* slots_out, int64_t slots_ld, void* stream);
+
+/*
  * Status word of the kernels that wait on shared-memory barriers (bounded waits): 0 when no wait
  * ran out, else the first code recorded (1 = a wait timed out). Synchronous; clears it if asked.
  * No reference counterpart (the reference has no device-side waits).

@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_exact_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "lkv_exact_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_device_status": (c_int, [c_void_p, c_int]),
+    "lkv_tier_admit": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int,
+                               c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
 }
 
 

@@ -1,0 +1,239 @@
+// Device-side residency of the tier: admit (lazykv/tiered.py:389-487) and the fetch of the misses.
+//
+// The reference keeps its residency tables in numpy and brings the selection to the host to update
+// them; here they live on the device and the update is one kernel per decode step and layer (one
+// CTA per KV head), with the reference's rule unchanged:
+//  * a chosen block whose block_slot is -1 misses;
+//  * victims are the slots not holding a chosen block, least recently used first, ties by slot
+//    index (np.argsort(last_used[free], kind="stable")), assigned to the misses in chosen order;
+//  * an evicted block gets block_slot = -1 and evicted_at = step; a filled slot gets its block and
+//    last_used = step; every chosen slot gets last_used = step (the gather's put_along_axis).
+// Table conventions are the reference's: slot_block [h, n_slots] (block or -1), block_slot
+// [h, cap] (pool index 1..n_slots or -1), last_used [h, n_slots] and evicted_at [h, cap] int64.
+// The fetch kernel then copies each miss from the host store (pairs in the model dtype, or int8
+// records dequantised exactly as lazykv/quant.py:unpack) into its slot of the pool
+// [n_slots + 2, h, 2, bs, d].
+#include "common.cuh"
+
+namespace lkv {
+namespace {
+
+constexpr int kAdmitThreads = 1024;
+
+__device__ uint32_t admit_scan(uint32_t v, uint32_t* warp_sums) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t w = warp_sums[lane];
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += x;
+    }
+    warp_sums[lane] = wi - w;
+  }
+  __syncthreads();
+  const uint32_t r = warp_sums[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
+// One CTA per KV head. Shared memory: per slot a 64-bit LRU key (last_used + 4 << 24 | slot), and a
+// kept flag; the free slots are bitonic-sorted by key.
+__global__ void __launch_bounds__(kAdmitThreads) admit_kernel(const int32_t* __restrict__ chosen, int k, int64_t chosen_ld,
+                                                               int32_t* __restrict__ block_slot, int cap, int32_t* __restrict__ slot_block,
+                                                               int64_t* __restrict__ last_used, int n_slots, int64_t* __restrict__ evicted_at,
+                                                               int64_t step, int32_t* __restrict__ miss_blk, int32_t* __restrict__ miss_slot,
+                                                               int32_t* __restrict__ n_miss, int32_t* __restrict__ slots_out, int64_t slots_ld) {
+  extern __shared__ uint64_t keys[];  // [P]
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sh_nfree, sh_nmiss;
+  unsigned char* kept = reinterpret_cast<unsigned char*>(keys + 0);  // reused below, see layout
+  const int j = blockIdx.x;
+  int P = 1;
+  while (P < n_slots) P <<= 1;
+  kept = reinterpret_cast<unsigned char*>(keys + P);
+  const int32_t* ch = chosen + (int64_t)j * chosen_ld;
+  int32_t* bslot = block_slot + (int64_t)j * cap;
+  int32_t* sblock = slot_block + (int64_t)j * n_slots;
+  int64_t* lu = last_used + (int64_t)j * n_slots;
+
+  for (int s = threadIdx.x; s < n_slots; s += blockDim.x) kept[s] = 0;
+  __syncthreads();
+  // Hits mark their slot kept.
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const int b = ch[i];
+    const int s = (b >= 0 && b < cap) ? bslot[b] : -1;
+    if (s >= 1 && s <= n_slots) kept[s - 1] = 1;
+  }
+  __syncthreads();
+  // Free slots, compacted in slot order, then sorted by (last_used, slot).
+  const int seg = (n_slots + blockDim.x - 1) / blockDim.x;
+  const int lo = threadIdx.x * seg, hi = min(n_slots, lo + seg);
+  uint32_t nf = 0;
+  for (int s = lo; s < hi; ++s) nf += !kept[s];
+  uint32_t pos = admit_scan(nf, warp_sums);
+  for (int s = lo; s < hi; ++s)
+    if (!kept[s]) keys[pos++] = ((uint64_t)(lu[s] + 4) << 24) | (uint64_t)s;
+  if (threadIdx.x == blockDim.x - 1) sh_nfree = pos;
+  __syncthreads();
+  const int n_free = (int)sh_nfree;
+  for (int i = n_free + threadIdx.x; i < P; i += blockDim.x) keys[i] = ~0ull;
+  __syncthreads();
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < P / 2; i += blockDim.x) {
+        const int a = 2 * i - (i & (stride - 1)), b = a + stride;
+        const bool asc = (a & size) == 0;
+        const uint64_t x = keys[a], y = keys[b];
+        if ((x > y) == asc) {
+          keys[a] = y;
+          keys[b] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // Misses, ranked in chosen order.
+  const int segk = (k + blockDim.x - 1) / blockDim.x;
+  const int klo = threadIdx.x * segk, khi = min(k, klo + segk);
+  uint32_t nm = 0;
+  for (int i = klo; i < khi; ++i) {
+    const int b = ch[i];
+    nm += (b >= 0 && b < cap && bslot[b] < 1);
+  }
+  uint32_t rank = admit_scan(nm, warp_sums);
+  if (threadIdx.x == blockDim.x - 1) sh_nmiss = rank + nm;
+  // Evict every victim's old block first (old blocks are never chosen), then assign.
+  for (int i = klo; i < khi; ++i) {
+    const int b = ch[i];
+    if (!(b >= 0 && b < cap && bslot[b] < 1)) continue;
+    const int v = rank < (uint32_t)n_free ? (int)(keys[rank] & 0xffffffull) : -1;
+    if (v >= 0) {
+      const int old = sblock[v];
+      if (old >= 0) {
+        bslot[old] = -1;
+        if (evicted_at != nullptr) evicted_at[(int64_t)j * cap + old] = step;
+      }
+    }
+    ++rank;
+  }
+  __syncthreads();
+  rank -= nm;
+  for (int i = klo; i < khi; ++i) {
+    const int b = ch[i];
+    if (!(b >= 0 && b < cap && bslot[b] < 1)) continue;
+    const int v = rank < (uint32_t)n_free ? (int)(keys[rank] & 0xffffffull) : -1;
+    if (v >= 0) {
+      sblock[v] = b;
+      bslot[b] = v + 1;
+      lu[v] = step;
+      miss_blk[(int64_t)j * k + rank] = b;
+      miss_slot[(int64_t)j * k + rank] = v + 1;
+    }
+    ++rank;
+  }
+  __syncthreads();
+  // Every chosen slot was used at this step.
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const int b = ch[i];
+    const int s = (b >= 0 && b < cap) ? bslot[b] : -1;
+    if (s >= 1 && s <= n_slots) lu[s - 1] = step;
+    if (slots_out != nullptr) slots_out[(int64_t)j * slots_ld + i] = s;
+  }
+  if (threadIdx.x == 0) n_miss[j] = (int)min(sh_nmiss, (uint32_t)n_free);
+}
+
+// Copy (or dequantise) the misses of every head into their slots; warps stride over the misses.
+// An int8 record is first staged whole in the warp's shared memory (16-byte loads, once over the
+// link when the store is host memory), then dequantised from there.
+constexpr int kFetchWarps = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kFetchWarps) fetch_misses_kernel(const void* __restrict__ store, int store_kind, int64_t width,
+                                                                        T* __restrict__ pool, int h, int bs, int d, int k,
+                                                                        const int32_t* __restrict__ miss_blk,
+                                                                        const int32_t* __restrict__ miss_slot,
+                                                                        const int32_t* __restrict__ n_miss) {
+  extern __shared__ __align__(16) unsigned char stage_all[];
+  const int j = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* stage = stage_all + (size_t)warp * ((width + 15) / 16 * 16);
+  const int n = n_miss[j];
+  const int n1 = bs * d, n2 = 2 * n1;
+  for (int m = blockIdx.x * kFetchWarps + warp; m < n; m += gridDim.x * kFetchWarps) {
+    const int b = miss_blk[(int64_t)j * k + m], slot = miss_slot[(int64_t)j * k + m];
+    T* dst = pool + ((int64_t)slot * h + j) * n2;
+    if (store_kind == LKV_COLD_INT8) {
+      const uint4* rec = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(store) + ((int64_t)b * h + j) * width);
+      for (int e = lane; e < (int)(width / 16); e += 32) reinterpret_cast<uint4*>(stage)[e] = rec[e];
+      __syncwarp();
+      const __half* ks = reinterpret_cast<const __half*>(stage + 2 * n1);
+      const __half* kz = ks + d;
+      const __half* vs = ks + 2 * d;
+      const __half* vz = vs + bs;
+      for (int e = lane; e < n2; e += 32) {
+        const int kv = e / n1, rem = e % n1, t = rem / d, c = rem % d;
+        const float q = (float)reinterpret_cast<const int8_t*>(stage)[e];
+        const float sc = __half2float(kv ? vs[t] : ks[c]), z = __half2float(kv ? vz[t] : kz[c]);
+        dst[e] = from_f32<T>(__fadd_rn(__fmul_rn(__fadd_rn(q, 128.0f), sc), z));  // quant.py:103-104
+      }
+      __syncwarp();
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(store) + ((int64_t)b * h + j) * n2);
+      uint4* o = reinterpret_cast<uint4*>(dst);
+      for (int e = lane; e < n2 * (int)sizeof(T) / 16; e += 32) o[e] = src[e];
+    }
+  }
+}
+
+}  // namespace
+}  // namespace lkv
+
+using namespace lkv;
+
+extern "C" int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32_t* block_slot, int cap, int32_t* slot_block,
+                              int64_t* last_used, int n_slots, int64_t* evicted_at, int64_t step, const void* store, int store_kind,
+                              void* pool, int bs, int d, int dtype, int32_t* miss_blk, int32_t* miss_slot, int32_t* n_miss,
+                              int32_t* slots_out, int64_t slots_ld, void* stream) {
+  if (!dtype_ok(dtype)) return fail(LKV_ERR_ARG, "lkv_tier_admit: bad dtype %d", dtype);
+  if (store_kind != LKV_COLD_INT8 && store_kind != LKV_COLD_PAIRS) return fail(LKV_ERR_ARG, "lkv_tier_admit: bad store kind %d", store_kind);
+  if (h <= 0 || k <= 0 || cap <= 0 || n_slots < k) return fail(LKV_ERR_ARG, "lkv_tier_admit: need h, k, cap > 0 and n_slots >= k (%d < %d)", n_slots, k);
+  if (n_slots > (1 << 16)) return fail(LKV_ERR_ARG, "lkv_tier_admit: %d slots above 65536", n_slots);
+  if (chosen == nullptr || block_slot == nullptr || slot_block == nullptr || last_used == nullptr || store == nullptr || pool == nullptr ||
+      miss_blk == nullptr || miss_slot == nullptr || n_miss == nullptr)
+    return fail(LKV_ERR_PTR, "lkv_tier_admit: null pointer");
+  if (!aligned(store, 16) || !aligned(pool, 16)) return fail(LKV_ERR_PTR, "lkv_tier_admit: store and pool must be 16-byte aligned");
+  if (bs % 8 || d % 8 || bs > 128 || d > 256) return fail(LKV_ERR_ARG, "lkv_tier_admit: bs and d must be multiples of 8 (bs <= 128, d <= 256)");
+  int P = 1;
+  while (P < n_slots) P <<= 1;
+  const size_t smem = (size_t)P * 8 + (size_t)((n_slots + 15) / 16 * 16);
+  cudaStream_t st = as_stream(stream);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(admit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  admit_kernel<<<h, kAdmitThreads, smem, st>>>(chosen, k, chosen_ld, block_slot, cap, slot_block, last_used, n_slots, evicted_at, step,
+                                                miss_blk, miss_slot, n_miss, slots_out, slots_ld);
+  if (int rc = launched("lkv_tier_admit(admit)")) return rc;
+  const int64_t width = lkv_packed_pair_bytes(bs, d);
+  const int fetch_ctas = (k + kFetchWarps - 1) / kFetchWarps < 32 ? (k + kFetchWarps - 1) / kFetchWarps : 32;
+  dim3 grid(fetch_ctas, h);
+  const size_t fsmem = store_kind == LKV_COLD_INT8 ? (size_t)kFetchWarps * ((width + 15) / 16 * 16) : 0;
+  if (fsmem > 200 * 1024) return fail(LKV_ERR_ARG, "lkv_tier_admit: records of %lld bytes are too wide to stage", (long long)width);
+  if (dtype == LKV_BF16) {
+    auto kern = fetch_misses_kernel<__nv_bfloat16>;
+    if (fsmem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
+    kern<<<grid, 32 * kFetchWarps, fsmem, st>>>(store, store_kind, width, static_cast<__nv_bfloat16*>(pool), h, bs, d, k, miss_blk, miss_slot, n_miss);
+  } else {
+    auto kern = fetch_misses_kernel<float>;
+    if (fsmem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
+    kern<<<grid, 32 * kFetchWarps, fsmem, st>>>(store, store_kind, width, static_cast<float*>(pool), h, bs, d, k, miss_blk, miss_slot, n_miss);
+  }
+  return launched("lkv_tier_admit(fetch)");
+}

@@ -218,3 +218,17 @@ def device_status(clear: bool = True) -> int:
     st = ctypes.c_int(0)
     call("lkv_device_status", ctypes.byref(st), int(clear))
     return st.value
+
+
+def tier_admit(chosen: torch.Tensor, block_slot: torch.Tensor, slot_block: torch.Tensor, last_used: torch.Tensor, evicted_at: torch.Tensor | None,
+               step: int, store: torch.Tensor, pool: torch.Tensor, miss_blk: torch.Tensor, miss_slot: torch.Tensor, n_miss: torch.Tensor,
+               slots_out: torch.Tensor | None = None) -> None:
+    """Device-side residency admit of `chosen` [h, k] plus the fetch of the misses (see lkv_tier_admit)."""
+    dev = require_cuda(chosen, block_slot, slot_block, last_used, store, pool)
+    h, k = chosen.shape
+    n_slots = slot_block.shape[1]
+    bs, d = pool.shape[-2], pool.shape[-1]
+    kind = L.LKV_COLD_INT8 if store.dtype == torch.uint8 else L.LKV_COLD_PAIRS
+    call("lkv_tier_admit", ptr(chosen), h, k, chosen.stride(0), ptr(block_slot), block_slot.shape[1], ptr(slot_block), ptr(last_used), n_slots,
+         ptr(evicted_at), step, ptr(store), kind, ptr(pool), bs, d, dtype_code(pool.dtype), ptr(miss_blk), ptr(miss_slot), ptr(n_miss),
+         ptr(slots_out), 0 if slots_out is None else slots_out.stride(0), stream_handle(dev))

@@ -1,0 +1,537 @@
+"""The tier: HBM slot pool, pinned host store, and a decode step that never returns to the host.
+
+API of lazykv/tiered.py (TieredLayer :150-535, TieredCache :538-860, allocate_host_pools :874-882)
+with the same layouts: the pool [n_slots + 2, h, 2, bs, d] in the model dtype (slot 0 the sink,
+the last slot the block being filled), the host store [cap, h, 2, bs, d] in the model dtype or
+[cap, h, packed_pair_bytes] int8 records, metadata [1, h, cap, d], and the reference's residency
+tables (slot_block, block_slot, last_used, evicted_at).
+
+What changes is where the work runs. Per selecting layer and decode step:
+  1. selection: Quest bound + top-K on the device (lkv_quest_topk); indices stay there;
+  2. residency: the reference's LRU admit as a device kernel, which also fetches the misses from
+     the host store (zero-copy loads; int8 records dequantised exactly as unpack) into their slots
+     (lkv_tier_admit), so the tables live on the device;
+  3. attention over [sink, selected, current] read in place from the pool (lkv_hot_attention), or,
+     in the exact tier, that and the cold pass over every other sealed block with the merge, in one
+     launch (lkv_exact_attention).
+Sealing a block packs or copies it into the host store with a kernel and updates its metadata on
+the device, asynchronously. The host only tracks lengths.
+
+Cold placement: the store the exact pass and the fetches read is the pinned host store through its
+device view (`cold_placement="host"`, zero-copy over the link), or a device copy kept alongside it
+(`"device"`).
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import asdict, dataclass, field
+from typing import Any
+
+import numpy as np
+import torch
+from transformers import PreTrainedModel
+from transformers.cache_utils import Cache
+
+from lazykv_b200 import kernels as K
+from lazykv_b200.cache import CacheStats, FullGPUCache
+from lazykv_b200.pinned import device_view, pinned_empty
+from lazykv_b200.quant import packed_pair_bytes
+from lazykv_b200.selection import QUEST_DENSE_LAYERS, current_block_mask
+
+NEVER = -(2**40)  # "evicted at" of pairs never evicted (tiered.py:69)
+BOUNDARY_CHUNK = 128  # blocks packed at once at the boundary (tiered.py:70)
+
+
+@dataclass
+class TierCounters:
+    """What the tier did (the reference's tiered.py:76-109, less its host-time split)."""
+
+    host_select_s: float = 0.0
+    selections: int = 0
+    selected_pairs: int = 0
+    hit_pairs: int = 0
+    fetched_pairs: int = 0
+    fetch_transfers: int = 0
+    fetch_bytes: int = 0
+    seals: int = 0
+    seal_bytes: int = 0
+    boundary_d2h_s: float = 0.0
+    boundary_d2h_bytes: int = 0
+    zerocopy_bytes: int = 0
+    ingest_forwards: int = 0
+    ingest_tokens: int = 0
+    ingest_h2d_bytes: int = 0
+    fetched_pairs_per_step: list[int] = field(default_factory=list)
+
+
+class TieredLayer:
+    """One selecting layer: GPU slot pool, pinned host store, metadata and device residency tables."""
+
+    def __init__(self, keys: torch.Tensor, values: torch.Tensor, k_blocks: int, block_size: int, capacity_tokens: int,
+                 host: torch.Tensor | None = None, n_slots: int | None = None, quant: str | None = None, cold_placement: str = "host") -> None:
+        _, h, length, d = keys.shape
+        bs = block_size
+        n_blocks, tail = divmod(length, bs)
+        dev, dt = keys.device, keys.dtype
+        self._allocate(h, d, n_blocks, k_blocks, bs, capacity_tokens, dev, dt, host, n_slots, quant, cold_placement)
+        seed = min(self.n_slots, n_blocks - 1)
+        lo_seed = n_blocks - seed
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for c0 in range(0, n_blocks, BOUNDARY_CHUNK):
+            c1 = min(n_blocks, c0 + BOUNDARY_CHUNK)
+            chunk = torch.stack([keys[0, :, c0 * bs : c1 * bs], values[0, :, c0 * bs : c1 * bs]], dim=1)  # [h, 2, n*bs, d]
+            chunk = chunk.unflatten(2, (c1 - c0, bs)).permute(2, 0, 1, 3, 4).contiguous()  # [n, h, 2, bs, d]
+            if quant is None:
+                self.host[c0:c1].copy_(chunk, non_blocking=True)
+                if self.dev_store is not None:
+                    self.dev_store[c0:c1].copy_(chunk)
+                K.block_minmax(keys[0, :, c0 * bs : c1 * bs], bs, self.kmin[0], self.kmax[0], first_block=c0)
+                seeded = chunk
+            else:
+                # Records are written straight into the pinned store through its device view; the
+                # metadata and the seeded slots come from the dequantised keys (tiered.py:182-197).
+                seeded = torch.empty_like(chunk)
+                K.pack_int8(chunk, records=self.host_dev[c0:c1], kmin=self.kmin[0], kmax=self.kmax[0], first_block=c0, deq=seeded)
+                if self.dev_store is not None:
+                    self.dev_store[c0:c1].copy_(self.host_dev[c0:c1])
+            lo, hi = max(c0, lo_seed), c1
+            if lo < hi and seed > 0:
+                self.pool[1 + lo - lo_seed : 1 + hi - lo_seed] = seeded[lo - c0 : hi - c0]
+        # The sink never leaves VRAM and stays exact, even under int8 (tiered.py:200-202).
+        self.pool[0] = torch.stack([keys[0, :, :bs], values[0, :, :bs]], dim=1)
+        if tail:
+            self.pool[self.tail_slot, :, 0, :tail] = keys[0, :, n_blocks * bs : length]
+            self.pool[self.tail_slot, :, 1, :tail] = values[0, :, n_blocks * bs : length]
+        torch.cuda.synchronize(dev)
+        self.boundary_d2h_s = time.perf_counter() - t0
+        self.boundary_d2h_bytes = n_blocks * h * self.pair_bytes
+        self._finish(n_blocks, tail, seed)
+
+    # -- set-up ----------------------------------------------------------------------------------
+
+    def _allocate(self, h: int, d: int, n_blocks: int, k_blocks: int, bs: int, capacity_tokens: int, dev: torch.device, dt: torch.dtype,
+                  host: torch.Tensor | None, n_slots: int | None, quant: str | None, cold_placement: str) -> None:
+        if n_blocks - 1 <= k_blocks:
+            raise ValueError(f"budget of {k_blocks} blocks covers all {n_blocks - 1} candidate blocks; the tier needs selection")
+        n_slots = k_blocks if n_slots is None else n_slots
+        if 0 < n_slots < k_blocks:
+            raise ValueError(f"{n_slots} slots cannot hold a selection of {k_blocks} blocks")
+        if quant not in (None, "int8"):
+            raise ValueError(f"unknown tier precision {quant!r}")
+        if cold_placement not in ("host", "device"):
+            raise ValueError(f"unknown cold placement {cold_placement!r}")
+        self.h, self.d, self.bs, self.k, self.n_slots = h, d, bs, k_blocks, n_slots
+        self.quant, self.cold_placement = quant, cold_placement
+        self.cap_blocks = -(-capacity_tokens // bs)
+        self.tail_slot = n_slots + 1
+        self.pool = torch.zeros((n_slots + 2, h, 2, bs, d), dtype=dt, device=dev)
+        self.kmin = torch.empty((1, h, self.cap_blocks, d), dtype=dt, device=dev)
+        self.kmax = torch.empty_like(self.kmin)
+        self.logical_pair_bytes = 2 * bs * d * self.pool.element_size()
+        shape = (self.cap_blocks, h, 2, bs, d) if quant is None else (self.cap_blocks, h, packed_pair_bytes(bs, d))
+        want = dt if quant is None else torch.uint8
+        if host is None:
+            host = pinned_empty(shape, want)
+        elif tuple(host.shape) != shape or host.dtype != want or not host.is_pinned():
+            raise ValueError(f"host pool must be pinned {want} with shape {shape}, got {host.dtype} {tuple(host.shape)}")
+        self.host = host
+        self.host_dev = device_view(host)  # the pinned store as kernels see it (zero-copy)
+        # The store the exact pass and the fetches read: the pinned store itself (zero-copy), or a
+        # device copy written alongside it.
+        self.dev_store = torch.empty(shape, dtype=want, device=dev) if cold_placement == "device" else None
+        self.store = self.dev_store if self.dev_store is not None else self.host_dev
+        self.pair_bytes = self.logical_pair_bytes if quant is None else packed_pair_bytes(bs, d)
+
+    def _finish(self, n_blocks: int, fill: int, seed: int) -> None:
+        h, dev = self.h, self.pool.device
+        self.n_sealed, self.fill, self.length = n_blocks, fill, n_blocks * self.bs + fill
+        recent = torch.arange(n_blocks - seed, n_blocks, device=dev, dtype=torch.int32)
+        ns = max(self.n_slots, 1)
+        self._slot_block = torch.full((h, ns), -1, dtype=torch.int32, device=dev)
+        self._block_slot = torch.full((h, self.cap_blocks), -1, dtype=torch.int32, device=dev)
+        self._last_used = torch.full((h, ns), -2, dtype=torch.int64, device=dev)
+        self._evicted_at = torch.full((h, self.cap_blocks), NEVER, dtype=torch.int64, device=dev)
+        if seed > 0:
+            self._slot_block[:, :seed] = recent
+            self._block_slot[:, n_blocks - seed : n_blocks] = torch.arange(1, seed + 1, device=dev, dtype=torch.int32)
+            self._last_used[:, :seed] = -1
+        k2 = self.k + 2
+        self.hot_list = torch.zeros((h, k2), dtype=torch.int32, device=dev)  # pool slots: sink, selected, current
+        self.hot_list[:, -1] = self.tail_slot
+        self.chosen = torch.zeros((h, self.k), dtype=torch.int32, device=dev)
+        self.words = K.bitmap_words(self.cap_blocks + 1)
+        self.bitmap = torch.zeros((h, self.words), dtype=torch.int32, device=dev)
+        self.miss_blk = torch.zeros((h, self.k), dtype=torch.int32, device=dev)
+        self.miss_slot = torch.zeros((h, self.k), dtype=torch.int32, device=dev)
+        self.n_miss = torch.zeros((h,), dtype=torch.int32, device=dev)
+        self.fetched_total = torch.zeros((), dtype=torch.int64, device=dev)
+        self.ends = torch.tensor([0, self.tail_slot], dtype=torch.int32, device=dev).repeat(h, 1).contiguous()  # sink, current
+        self.out: torch.Tensor | None = None  # [hq, d] float32, allocated on first use
+        self.lse: torch.Tensor | None = None
+
+    # -- residency tables, as numpy copies (synchronising) -----------------------------------------
+
+    def _get(self, t: torch.Tensor) -> np.ndarray:
+        return t.cpu().numpy()
+
+    @property
+    def slot_block(self) -> np.ndarray:
+        return self._get(self._slot_block)[:, : self.n_slots]
+
+    @property
+    def block_slot(self) -> np.ndarray:
+        return self._get(self._block_slot)
+
+    @property
+    def last_used(self) -> np.ndarray:
+        return self._get(self._last_used)[:, : self.n_slots]
+
+    @property
+    def evicted_at(self) -> np.ndarray:
+        return self._get(self._evicted_at)
+
+    def set_tables(self, slot_block: np.ndarray | None = None, block_slot: np.ndarray | None = None, last_used: np.ndarray | None = None) -> None:
+        """Overwrite residency tables from host arrays (tests and tooling)."""
+        for src, dst in ((slot_block, self._slot_block), (block_slot, self._block_slot), (last_used, self._last_used)):
+            if src is not None:
+                dst[:, : src.shape[1]].copy_(torch.from_numpy(np.ascontiguousarray(src)).to(dst.dtype))
+
+    # -- writes (tiered.py:306-375) ---------------------------------------------------------------
+
+    def append(self, key: torch.Tensor, value: torch.Tensor, counters: TierCounters) -> None:
+        """Write one decode token; seal the current block first if it is full (lazily)."""
+        if self.fill == self.bs:
+            self._seal(counters)
+        t = self.pool[self.tail_slot]
+        t[:, 0, self.fill].copy_(key[0, :, 0])
+        t[:, 1, self.fill].copy_(value[0, :, 0])
+        self.fill += 1
+        self.length += 1
+
+    def extend(self, keys: torch.Tensor, values: torch.Tensor, counters: TierCounters) -> None:
+        """Write a multi-token forward's KV [1, h, T, d] as T appends would."""
+        n, i = keys.shape[2], 0
+        while i < n:
+            if self.fill == self.bs:
+                self._seal(counters)
+            m = min(self.bs - self.fill, n - i)
+            t = self.pool[self.tail_slot]
+            t[:, 0, self.fill : self.fill + m].copy_(keys[0, :, i : i + m])
+            t[:, 1, self.fill : self.fill + m].copy_(values[0, :, i : i + m])
+            self.fill += m
+            self.length += m
+            i += m
+
+    def dense_kv(self, keys: torch.Tensor, values: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, int]:
+        """The layer's whole KV from the host store, then the tail and `keys`/`values` (bf16 tier)."""
+        if self.quant is not None:
+            raise NotImplementedError("dense ingestion is implemented for the bf16 tier only")
+        n = self.n_sealed
+        g = self.host[:n].to(keys.device, non_blocking=True).permute(1, 2, 0, 3, 4).reshape(self.h, 2, n * self.bs, self.d)
+        tail = self.pool[self.tail_slot, :, :, : self.fill]
+        k = torch.cat([g[:, 0], tail[:, 0], keys[0]], dim=1).unsqueeze(0)
+        v = torch.cat([g[:, 1], tail[:, 1], values[0]], dim=1).unsqueeze(0)
+        return k, v, n * self.h * self.pair_bytes
+
+    def _seal(self, counters: TierCounters) -> None:
+        b = self.n_sealed
+        if b >= self.cap_blocks:
+            raise RuntimeError(f"host pool full: {self.cap_blocks} blocks")
+        tail = self.pool[self.tail_slot : self.tail_slot + 1]  # [1, h, 2, bs, d]
+        if self.quant is None:
+            self.host[b].copy_(tail[0], non_blocking=True)
+            if self.dev_store is not None:
+                self.dev_store[b].copy_(tail[0])
+            K.block_minmax(tail[0, :, 0], self.bs, self.kmin[0], self.kmax[0], first_block=b)
+        else:
+            K.pack_int8(tail, records=self.host_dev[b : b + 1], kmin=self.kmin[0], kmax=self.kmax[0], first_block=b)
+            if self.dev_store is not None:
+                self.dev_store[b].copy_(self.host_dev[b])
+        self.n_sealed += 1
+        self.fill = 0
+        counters.seals += 1
+        counters.seal_bytes += self.h * self.pair_bytes
+
+    # -- the device decode step ------------------------------------------------------------------------
+
+    def candidates(self) -> tuple[int, int]:
+        """(n_full, fill): blocks 1..n_full-1 are selectable, block n_full is the current one."""
+        return self.n_sealed, self.fill
+
+    def choose(self, query: torch.Tensor, bitmap: bool = False) -> torch.Tensor:
+        """Top-K block ids [h, K] on the device (ascending id), optionally marking the bitmap."""
+        n_full, _ = self.candidates()
+        K.quest_topk(query, self.kmin[0], self.kmax[0], 1, n_full - 1, self.k, out_blocks=self.chosen, bitmap=self.bitmap if bitmap else None,
+                     by_block=True)
+        return self.chosen
+
+    def admit_device(self, step: int) -> None:
+        """Device-side admit of self.chosen and the fetch of its misses; fills the hot list."""
+        K.tier_admit(self.chosen, self._block_slot, self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool,
+                     self.miss_blk, self.miss_slot, self.n_miss, slots_out=self.hot_list[:, 1 : self.k + 1])
+        self.fetched_total += self.n_miss.sum()
+
+    def attend(self, query: torch.Tensor, scale: float, step: int, exact: bool, zerocopy: bool = False) -> torch.Tensor:
+        """One decode step of this layer on the device; returns out [hq, d] float32."""
+        hq, d = query.shape[1], self.d
+        if self.out is None or self.out.shape != (hq, d):
+            self.out = torch.empty((hq, d), dtype=torch.float32, device=query.device)
+            self.lse = torch.empty((hq,), dtype=torch.float32, device=query.device)
+        self.choose(query, bitmap=exact)
+        pool_strides = (self.h * 2 * self.bs * d, 2 * self.bs * d, d)
+        if zerocopy:
+            return self._attend_zerocopy(query, scale, exact, pool_strides)
+        self.admit_device(step)
+        if exact:
+            K.exact_attention(query, self.pool, self.pool[:, :, 1], pool_strides, self.hot_list, self.fill, self.store, 1, self.n_sealed - 1,
+                              scale, self.bs, excluded=self.bitmap, out_dtype=torch.float32, out=self.out, lse=self.lse)
+        else:
+            K.hot_attention(query, self.pool, self.pool[:, :, 1], pool_strides, self.hot_list, self.fill, scale, self.bs, out=self.out, lse=self.lse)
+        return self.out
+
+    def _attend_zerocopy(self, query: torch.Tensor, scale: float, exact: bool, pool_strides: tuple[int, int, int]) -> torch.Tensor:
+        """No slots: the selected blocks are read in place from the host store, the sink and the
+        current block from the pool; the partials are merged."""
+        d = self.d
+        o1, l1 = K.hot_attention(query, self.pool, self.pool[:, :, 1], pool_strides, self.ends, self.fill, scale, self.bs)
+        if self.quant is None:
+            st = self.host_dev
+            o2, l2 = K.hot_attention(query, st, st[:, :, 1], (self.h * 2 * self.bs * d, 2 * self.bs * d, d), self.chosen, self.bs, scale, self.bs)
+        else:
+            raise ValueError("the zero-copy fetch reads bf16 blocks in place; the int8 tier needs fetch='gather'")
+        parts_o, parts_l = [o1, o2], [l1, l2]
+        if exact:
+            o3, l3 = K.cold_attention(query, self.store, self.bs, 1, self.n_sealed - 1, scale, excluded=self.bitmap)
+            parts_o.append(o3)
+            parts_l.append(l3)
+        K.lse_merge(torch.stack(parts_o), torch.stack(parts_l), torch.float32, out=self.out, lse_out=self.lse)
+        return self.out
+
+    # -- the reference's host-facing calls (synchronising) ------------------------------------------
+
+    def rank(self, query: torch.Tensor, bitmap: bool = False) -> np.ndarray:
+        """Top-K block ids [h, K] for a query, descending bound (tiered.py:383-387), optionally
+        marking them in the bitmap the cold pass skips. Syncs."""
+        n_full, _ = self.candidates()
+        top, _ = K.quest_topk(query, self.kmin[0], self.kmax[0], 1, n_full - 1, self.k, bitmap=self.bitmap if bitmap else None)
+        return top.cpu().numpy().astype(np.int64)
+
+    def admit(self, chosen: np.ndarray, step: int, counters: TierCounters, stream: Any = None, stage: Any = None) -> tuple[np.ndarray, np.ndarray, int]:
+        """Make every (head, block) in `chosen` [h, K] resident (tiered.py:389-463), on the device.
+
+        Returns the fetched pairs (heads, blocks) in the reference's order and the number of fetch
+        launches. Synchronises to read the misses back.
+        """
+        ch = torch.from_numpy(np.ascontiguousarray(chosen)).to(device=self.pool.device, dtype=torch.int32)
+        K.tier_admit(ch, self._block_slot, self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool,
+                     self.miss_blk, self.miss_slot, self.n_miss)
+        self.fetched_total += self.n_miss.sum()
+        n = self.n_miss.cpu().numpy()
+        blk = self.miss_blk.cpu().numpy()
+        # Head-major, chosen order within a head: the order of np.nonzero(miss) in the reference.
+        mh = np.concatenate([np.full(n[j], j, dtype=np.int64) for j in range(self.h)])
+        mb = np.concatenate([blk[j, : n[j]].astype(np.int64) for j in range(self.h)])
+        return mh, mb, int(n.sum() > 0)
+
+    def gather(self, chosen: np.ndarray, step: int, query: torch.Tensor, mask_cache: dict[str, Any]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Attention inputs for `chosen` after admit: sink, chosen blocks in the given order, current block."""
+        slots = self.hot_list[:, 1 : self.k + 1].long()  # written by the admit
+        idx = torch.cat([torch.zeros((self.h, 1), dtype=torch.long, device=slots.device), slots,
+                         torch.full((self.h, 1), self.tail_slot, dtype=torch.long, device=slots.device)], dim=1)
+        flat = idx * self.h + torch.arange(self.h, device=slots.device)[:, None]
+        pool_flat = self.pool.view(-1, 2, self.bs, self.d)
+        k2 = self.k + 2
+        shape = (1, self.h, k2 * self.bs, self.d)
+        k_sel = pool_flat[flat.reshape(-1), 0].view(shape)
+        v_sel = pool_flat[flat.reshape(-1), 1].view(shape)
+        fill = self.fill
+        if mask_cache.get("fill") != fill or mask_cache.get("total") != k2 * self.bs:
+            mask_cache["mask"] = current_block_mask(k2 * self.bs, self.bs, fill, query.dtype, query.device)
+            mask_cache["fill"], mask_cache["total"] = fill, k2 * self.bs
+        return k_sel, v_sel, mask_cache["mask"]
+
+    # -- accounting -------------------------------------------------------------------------------------
+
+    def gpu_bytes(self) -> int:
+        return self.pool.numel() * self.pool.element_size()
+
+    def metadata_bytes(self) -> int:
+        return 2 * self.kmin.numel() * self.kmin.element_size()
+
+    def host_bytes(self) -> int:
+        return self.n_sealed * self.h * self.pair_bytes
+
+    def not_resident_pairs(self) -> int:
+        return (self.n_sealed - 1) * self.h - int((self._slot_block[:, : self.n_slots] >= 0).sum().item())
+
+    def not_resident_bytes(self) -> int:
+        return self.not_resident_pairs() * self.pair_bytes
+
+    def not_resident_logical_bytes(self) -> int:
+        return self.not_resident_pairs() * self.logical_pair_bytes
+
+
+class TieredCache(Cache):
+    """Decode-time cache: dense layers share the prefilled FullGPUCache, selecting layers are tiered.
+
+    Constructor of lazykv/tiered.py:546-565 (plus `cold_placement`). The residency decision runs on
+    the device, which the reference's layer-ahead prefetch (rung 7) and its record/replay ablation
+    existed to work around; both are refused with a message rather than silently ignored.
+    """
+
+    def __init__(self, full: FullGPUCache, k_blocks: int, block_size: int, capacity_tokens: int, model: PreTrainedModel | None = None,
+                 prefetch: bool = False, dense_layers: int = QUEST_DENSE_LAYERS, host_pools: list[torch.Tensor] | None = None,
+                 thrash_window: int = 16, instrument: bool = False, n_slots: int | None = None, fetch: str = "runs", stages: Any = None,
+                 quant: str | None = None, record_selection: bool = False, replay_selection: Any = None,
+                 tiers: dict[int, TieredLayer] | None = None, cold_placement: str = "host") -> None:
+        super().__init__(layers=full.layers)
+        if prefetch and model is None:
+            raise ValueError("prefetch needs the model, to speculate the next layer's query")
+        if fetch not in ("runs", "gather", "zerocopy"):
+            raise ValueError(f"unknown fetch mode {fetch!r}")
+        if quant is not None and fetch != "gather":
+            raise ValueError(f"the int8 tier needs fetch='gather', got {fetch!r}")
+        if fetch == "zerocopy":
+            if prefetch or record_selection or replay_selection is not None:
+                raise ValueError("the zero-copy fetch has no residency to prefetch, record or replay")
+            n_slots = 0 if n_slots is None else n_slots
+        if prefetch:
+            raise ValueError("the layer-ahead prefetch is not built: residency is decided on the device, with no host round trip to hide")
+        if record_selection or replay_selection is not None:
+            raise ValueError("record/replay of selections is not built: the selection never reaches the host")
+        self.full, self.k_blocks, self.block_size, self.dense_layers = full, k_blocks, block_size, dense_layers
+        self.thrash_window, self.instrument, self.quant, self.fetch = thrash_window, instrument, quant, fetch
+        self.prefetch = False
+        self.policy_name = "tiered_int8" if quant else ("tiered_zerocopy" if fetch == "zerocopy" else "tiered_sync")
+        self.counters = TierCounters()
+        if tiers is None:
+            tiers = {}
+            for i in range(dense_layers, len(full.layers)):
+                src = full.layers[i]
+                n = src.get_seq_length()
+                host = None if host_pools is None else host_pools[i - dense_layers]
+                tiers[i] = TieredLayer(src.keys[:, :, :n], src.values[:, :, :n], k_blocks, block_size, capacity_tokens, host, n_slots, quant=quant,
+                                       cold_placement=cold_placement)
+        elif sorted(tiers) != list(range(dense_layers, len(full.layers))):
+            raise ValueError(f"prebuilt tiers must cover layers {dense_layers}..{len(full.layers) - 1}, got {sorted(tiers)}")
+        self.tiers: dict[int, TieredLayer] = tiers
+        for layer in tiers.values():
+            self.counters.boundary_d2h_s += layer.boundary_d2h_s
+            self.counters.boundary_d2h_bytes += layer.boundary_d2h_bytes
+        self.n_slots = next(iter(self.tiers.values())).n_slots
+        self._mask_cache: dict[str, Any] = {}
+        self._step = 0
+        self._step_marks: list[torch.Tensor] = []  # device totals of fetched pairs at each step's end
+        self._last_chosen: torch.Tensor | None = None
+
+    # -- transformers plumbing ------------------------------------------------------------------------
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int, *args: object, **kwargs: object) -> tuple[torch.Tensor, torch.Tensor]:
+        if layer_idx == 0:
+            self._begin_step()
+        tier = self.tiers.get(layer_idx)
+        if tier is None:
+            return self.full.layers[layer_idx].update(key_states, value_states)
+        if key_states.shape[-2] != 1:
+            # A multi-token forward attends to the layer's whole KV (tiered.py:649-663).
+            k, v, moved = tier.dense_kv(key_states, value_states)
+            tier.extend(key_states, value_states, self.counters)
+            c = self.counters
+            c.ingest_forwards += 1
+            c.ingest_tokens += key_states.shape[-2]
+            c.ingest_h2d_bytes += moved
+            return k, v
+        tier.append(key_states, value_states, self.counters)
+        return tier.pool[tier.tail_slot : tier.tail_slot + 1, :, 0], tier.pool[tier.tail_slot : tier.tail_slot + 1, :, 1]
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        tier = self.tiers.get(layer_idx)
+        return tier.length if tier is not None else self.full.layers[layer_idx].get_seq_length()
+
+    def model_kwargs(self) -> dict[str, object]:
+        return {"lazykv_selector": self}
+
+    def close(self) -> None:
+        if self._step > 0:
+            self._flush_step()
+            self._step = 0
+
+    def _begin_step(self) -> None:
+        if self._step > 0:
+            self._flush_step()
+        self._step += 1
+
+    def _flush_step(self) -> None:
+        # The step's fetch total stays on the device until the counters are read: no host sync here.
+        if self.fetch != "zerocopy":
+            self._step_marks.append(sum(t.fetched_total for t in self.tiers.values()).clone())
+
+    # -- decode ---------------------------------------------------------------------------------------------
+
+    exact_pass = False  # True in the exact tier: the cold blocks are attended and merged too
+
+    def decode(self, layer_idx: int, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, scaling: float | None) -> torch.Tensor | None:
+        """The whole decode step of a selecting layer on the device; out [1, Hq, 1, d] in the model dtype."""
+        tier = self.tiers.get(layer_idx)
+        if tier is None or query.shape[-2] != 1:
+            return None
+        t0 = time.perf_counter()
+        scale = scaling if scaling is not None else tier.d**-0.5
+        out = tier.attend(query, scale, self._step, self.exact_pass, zerocopy=self.fetch == "zerocopy")
+        c = self.counters
+        c.selections += 1
+        c.selected_pairs += tier.h * tier.k
+        if self.fetch == "zerocopy":
+            c.zerocopy_bytes += tier.h * tier.k * tier.pair_bytes
+        c.host_select_s += time.perf_counter() - t0
+        return out.to(query.dtype).view(1, query.shape[1], 1, tier.d)
+
+    def select(self, layer_idx: int, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None:
+        """The reference's protocol (tiered.py:694-747): gathered (key, value, mask) after the admit."""
+        tier = self.tiers.get(layer_idx)
+        if tier is None or query.shape[-2] != 1:
+            return None
+        if self.fetch == "zerocopy":
+            raise ValueError("the zero-copy tier attends in place; use decode()")
+        chosen = tier.rank(query, bitmap=self.exact_pass)
+        tier.chosen.copy_(torch.from_numpy(chosen).to(torch.int32))
+        tier.admit_device(self._step)
+        self._last_chosen = tier.chosen.clone()
+        self.counters.selections += 1
+        self.counters.selected_pairs += chosen.size
+        return tier.gather(chosen, self._step, query, self._mask_cache)
+
+    # -- accounting --------------------------------------------------------------------------------------
+
+    def counters_dict(self) -> dict[str, Any]:
+        if self.fetch != "zerocopy":
+            marks = [int(m.item()) for m in self._step_marks]
+            self.counters.fetched_pairs_per_step = [b - a for a, b in zip([0] + marks[:-1], marks)]
+            total = int(sum(t.fetched_total for t in self.tiers.values()).item())
+            self.counters.fetched_pairs = total
+            self.counters.hit_pairs = self.counters.selected_pairs - total
+            self.counters.fetch_bytes = total * next(iter(self.tiers.values())).pair_bytes
+        return asdict(self.counters)
+
+    def stats(self) -> CacheStats:
+        dense = sum(self.full.layers[i].resident_bytes() for i in range(self.dense_layers))
+        gpu = dense + sum(t.gpu_bytes() + t.metadata_bytes() for t in self.tiers.values())
+        not_resident = sum(t.not_resident_bytes() for t in self.tiers.values())
+        return CacheStats(seq_len=self.get_seq_length(self.dense_layers), gpu_resident_kv_bytes=gpu, host_kv_bytes=not_resident, gpu_allocated_kv_bytes=gpu)
+
+    def host_logical_bytes(self) -> int:
+        return sum(t.not_resident_logical_bytes() for t in self.tiers.values())
+
+    def host_pinned_bytes(self) -> int:
+        return sum(t.host.numel() * t.host.element_size() for t in self.tiers.values())
+
+
+def allocate_host_pools(n_layers: int, heads: int, head_dim: int, block_size: int, capacity_tokens: int, dtype: torch.dtype = torch.bfloat16,
+                        quant: str | None = None) -> list[torch.Tensor]:
+    """Exact-size pinned host stores, one per selecting layer (tiered.py:874-882)."""
+    blocks = -(-capacity_tokens // block_size)
+    shape, dt = ((blocks, heads, 2, block_size, head_dim), dtype) if quant is None else ((blocks, heads, packed_pair_bytes(block_size, head_dim)), torch.uint8)
+    return [pinned_empty(shape, dt) for _ in range(n_layers)]
+
