@@ -123,13 +123,16 @@ int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h, int d, con
  * holds `last_fill` live tokens (the current block, lazykv/selection.py:65-69), the others bs.
  * A listed id b maps to storage row r = slot_of ? slot_of[j*slot_stride + b] : b, and key element
  * (t, c) of that row is k_base[r*s_row + j*s_head + t*s_tok + c] (values at v_base, same strides).
+ * n_rows: how many storage rows those strides address (rows 0..n_rows-1 of every head lie inside
+ * the buffers); it bounds the tensor-map loads of the bf16 d-64 path, and 0 ("unknown") keeps the
+ * call on the CUDA-core kernels.
  * q [hq, d] in `dtype`; out [hq, d] float32 (divided by its normaliser) and lse [hq] float32.
  * Workspace: lkv_attention_workspace(h, hq, d, n_list) bytes.
  */
 size_t lkv_attention_workspace(int h, int hq, int d, int n_items);
 int lkv_hot_attention(const void* q, int hq, int h, int d, int bs, const void* k_base,
                       const void* v_base, int dtype, int64_t s_row, int64_t s_head, int64_t s_tok,
-                      const int32_t* blocks, int n_list, const int32_t* slot_of,
+                      int64_t n_rows, const int32_t* blocks, int n_list, const int32_t* slot_of,
                       int64_t slot_stride, int last_fill, float scale, float* out, float* lse,
                       void* workspace, size_t workspace_bytes, void* stream);
 
@@ -138,8 +141,9 @@ int lkv_hot_attention(const void* q, int hq, int h, int d, int bs, const void* k
  * the float32 mirror it reads, lazykv/exact.py:130-152) with a GPU pass over the complement only.
  * Attends blocks [first_block, first_block + n_blocks) of every KV head j, skipping those whose
  * bit is set in excluded[j*bitmap_words + b/32]; the store is cold [blocks, h, W] int8 records
- * (dequantised in float32, fused) or cold [blocks, h, 2, bs, d] pairs in `dtype`
- * (LKV_COLD_PAIRS). A head with no block left returns lse = -inf and out = 0.
+ * (dequantised as lazykv/quant.py:unpack to `dtype`, fused: each block is attended as a fetch
+ * would put it in a slot) or cold [blocks, h, 2, bs, d] pairs in `dtype` (LKV_COLD_PAIRS). A head
+ * with no block left returns lse = -inf and out = 0.
  * Workspace: lkv_attention_workspace(h, hq, d, n_blocks) bytes.
  */
 int lkv_cold_attention(const void* q, int hq, int h, int d, int bs, const void* cold,
@@ -160,6 +164,7 @@ typedef struct {
   const int32_t* slot_of;
   int64_t slot_stride;
   int last_fill;
+  int64_t n_rows;
 } lkv_hot_set;
 
 /* The cold set of lkv_exact_attention: the arguments of lkv_cold_attention, as a struct. */

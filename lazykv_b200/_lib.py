@@ -34,7 +34,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_quest_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "lkv_quest_topk_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p]),
     "lkv_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
-    "lkv_hot_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "lkv_hot_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_cold_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_lse_merge": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "lkv_exact_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
@@ -49,7 +49,8 @@ class HotSet(ctypes.Structure):
     """lkv_hot_set of include/lkv.h."""
 
     _fields_ = [("k_base", c_void_p), ("v_base", c_void_p), ("dtype", c_int), ("s_row", c_int64), ("s_head", c_int64), ("s_tok", c_int64),
-                ("blocks", c_void_p), ("n_list", c_int), ("slot_of", c_void_p), ("slot_stride", c_int64), ("last_fill", c_int)]
+                ("blocks", c_void_p), ("n_list", c_int), ("slot_of", c_void_p), ("slot_stride", c_int64), ("last_fill", c_int),
+                ("n_rows", c_int64)]
 
 
 class ColdSet(ctypes.Structure):

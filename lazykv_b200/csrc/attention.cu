@@ -6,8 +6,9 @@
 //    gather copy); the last listed block is the current block with `last_fill` live tokens
 //    (selection.py:65-69);
 //  * cold segment (lazykv/exact.py:88-127): blocks [first, first + n) minus a per-head exclusion
-//    bitmap, read from int8 records with the dequantisation fused (quant.py:103-104, float32
-//    affine), or from pairs in the model dtype.
+//    bitmap, read from int8 records with the dequantisation fused (quant.py:103-104: float32
+//    affine, then rounded to the model dtype, i.e. what a fetch puts in a slot), or from pairs in
+//    the model dtype.
 // Each CTA takes a chunk of one segment's items for one KV head and emits an online-softmax partial
 // (running max m in the log2 domain, sum l, unnormalised o) for the head's G query rows. A combine
 // kernel folds the chunks into per-segment (out = o / l, lse) and into their merge. A partial over
@@ -24,6 +25,9 @@
 //    the same arithmetic with vectorised loads straight from global memory.
 // Lane layout in a warp: CG = d/16 channel groups x TL = 32/CG token lanes; a lane holds 16
 // channels of the G query rows and of its accumulators and takes tokens tl, tl + TL, ... of a block.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "tma.cuh"
 
 namespace lkv {
@@ -53,6 +57,7 @@ struct Seg {
   int n_list, last_fill;
   const int32_t* slot_of;
   int64_t slot_stride;
+  int64_t n_rows;  // storage rows addressable from k_base / v_base (0 = unknown)
   // range items
   int first_block;
   const uint32_t* excluded;
@@ -85,6 +90,23 @@ void set_split(Seg& S, int target) {
 }
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+// A dequantised cold value as the model dtype holds it: the exact pass attends to what a fetch
+// would put in a slot (unpack in the model dtype), so under bf16 each value is rounded once more.
+template <typename T>
+__device__ __forceinline__ float as_model(float x) {
+  if constexpr (sizeof(T) == 2) return __bfloat162float(__float2bfloat16_rn(x));
+  return x;
+}
+template <typename T>
+__device__ __forceinline__ float2 as_model2(float2 x) {
+  if constexpr (sizeof(T) == 2) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(x.x, x.y);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(&b);
+    return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+  return x;
+}
 
 __device__ __forceinline__ bool range_excluded(const Seg& S, int j, int blk) {
   return S.excluded != nullptr && blk / 32 < S.bitmap_words &&
@@ -226,7 +248,7 @@ __global__ void __launch_bounds__(kThreads) attn_ldg_kernel(const AttnParams p) 
       if (int8) {
         load_codes<CPL>(rec + (int64_t)t * D + c0, kv);
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) kv[c] = fmaf(kv[c], ks[c], kz[c]);
+        for (int c = 0; c < CPL; ++c) kv[c] = as_model<T>(fmaf(kv[c], ks[c], kz[c]));
       } else {
         load_chunk<T, CPL>(kp + t * S.s_tok + c0, kv);
       }
@@ -265,7 +287,7 @@ __global__ void __launch_bounds__(kThreads) attn_ldg_kernel(const AttnParams p) 
         const float vs = ldh(sc + 2 * t), vz = ldh(sc + 2 * p.bs + 2 * t);
         load_codes<CPL>(rec + (int64_t)p.bs * D + (int64_t)t * D + c0, kv);
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) kv[c] = fmaf(kv[c], vs, vz);
+        for (int c = 0; c < CPL; ++c) kv[c] = as_model<T>(fmaf(kv[c], vs, vz));
       } else {
         load_chunk<T, CPL>(vp + t * S.s_tok + c0, kv);
       }
@@ -414,13 +436,12 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
       }
     }
   }
-  float m[G], l[G], zs[G];
+  float m[G], l[G];
   float2 o2[G][8];
 #pragma unroll
   for (int r = 0; r < G; ++r) {
     m[r] = -INFINITY;
     l[r] = 0.0f;
-    zs[r] = 0.0f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) o2[r][w] = f2(0.0f, 0.0f);
   }
@@ -553,7 +574,7 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
         float2 u[8];
         codes16(st + t * D + c0, u);
 #pragma unroll
-        for (int w = 0; w < 8; ++w) k2[w] = __ffma2_rn(u[w], ks2[w], kz2[w]);
+        for (int w = 0; w < 8; ++w) k2[w] = as_model2<T>(__ffma2_rn(u[w], ks2[w], kz2[w]));
       } else {
         lds_row16<T>(reinterpret_cast<const T*>(st) + t * D + c0, swap, k2);
       }
@@ -591,7 +612,6 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
         if (mb > m[r] + kLazy) {
           const float alpha = exp2f(m[r] - mb);  // 0 when m was -inf
           l[r] *= alpha;
-          zs[r] *= alpha;
           const float2 a2 = f2(alpha, alpha);
 #pragma unroll
           for (int w = 0; w < 8; ++w) o2[r][w] = __fmul2_rn(o2[r][w], a2);
@@ -614,25 +634,19 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
       const int t = tl + TL * i;
       float2 v2[8];
       if (rec) {
-        // o += p * (u * vs + vz) = (p * vs) * u + p * vz; the second term is channel-independent.
         codes16(st + BS * D + t * D + c0, v2);
         const float vs = scl[2 * C::SCL_K + 2 * t], vz = scl[2 * C::SCL_K + 2 * t + 1];
+        const float2 vs2 = f2(vs, vs), vz2 = f2(vz, vz);
 #pragma unroll
-        for (int r = 0; r < G; ++r) {
-          const float w = pr[r][i] * vs;
-          zs[r] = fmaf(pr[r][i], vz, zs[r]);
-          const float2 ww = f2(w, w);
-#pragma unroll
-          for (int x = 0; x < 8; ++x) o2[r][x] = __ffma2_rn(ww, v2[x], o2[r][x]);
-        }
+        for (int x = 0; x < 8; ++x) v2[x] = as_model2<T>(__ffma2_rn(v2[x], vs2, vz2));
       } else {
         lds_row16<T>(reinterpret_cast<const T*>(st) + BS * D + t * D + c0, swap, v2);
+      }
 #pragma unroll
-        for (int r = 0; r < G; ++r) {
-          const float2 pp = f2(pr[r][i], pr[r][i]);
+      for (int r = 0; r < G; ++r) {
+        const float2 pp = f2(pr[r][i], pr[r][i]);
 #pragma unroll
-          for (int x = 0; x < 8; ++x) o2[r][x] = __ffma2_rn(pp, v2[x], o2[r][x]);
-        }
+        for (int x = 0; x < 8; ++x) o2[r][x] = __ffma2_rn(pp, v2[x], o2[r][x]);
       }
     }
     __syncwarp();  // every lane is done with stage s (and the scale scratch) before it is refilled
@@ -666,9 +680,6 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
   }
 #pragma unroll
   for (int r = 0; r < G; ++r) {
-    const float2 z2 = f2(zs[r], zs[r]);
-#pragma unroll
-    for (int w = 0; w < 8; ++w) o2[r][w] = __fadd2_rn(o2[r][w], z2);
 #pragma unroll
     for (int off = CG; off < 32; off <<= 1) {
       l[r] += __shfl_xor_sync(0xffffffffu, l[r], off);
@@ -705,6 +716,457 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
+        const float mw = sh_ml[w * 2 * G + r];
+        const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+        O = fmaf(sh_o[(w * G + r) * D + c], f, O);
+        Lr = fmaf(sh_ml[w * 2 * G + G + r], f, Lr);
+      }
+    }
+    out[2 * G + r * D + c] = O;
+    if (c == 0) {
+      out[r] = M;
+      out[G + r] = Lr;
+    }
+  }
+}
+
+// ============================================================================================
+// attn_mma_kernel: tensor-core split decode (bf16, d = 64, bs = 16, G <= 8), stores in device memory
+// ============================================================================================
+//
+// Per item (one block of one KV head) a warp runs two small contractions on the tensor cores with
+// mma.sync.m16n8k16 (bf16 operands, float32 accumulators):
+//   S^T [16 tokens x 8 rows]   = K [16 x 64] . Q^T [64 x 8]      (4 k-steps; rows >= G are zero)
+//   O^T [64 channels x 8 rows] += V^T [64 x 16] . P^T [16 x 8]   (4 m-tiles)
+// K and V reach shared memory as bf16 tiles of 16 rows x 128 bytes in the 128-byte swizzle
+// (16-byte chunk c of row r stored at chunk c ^ (r & 7)), so ldmatrix reads them without bank
+// conflicts: hot blocks and cold pairs by tensor-map TMA loads (cp.async.bulk.tensor, SWIZZLE_128B),
+// int8 cold records by a bulk copy of the raw record that the warp dequantises into its own tile
+// (float32 affine of quant.py:103-104, rounded to bf16: what a fetch puts in a slot). The products
+// of bf16 operands are exact in float32; P (float32) enters the second contraction as the sum of
+// three bf16 terms (hi + mid + lo, 24 significant bits), each a separate MMA, so the result keeps
+// float32 accuracy. The score fragment becomes the P^T operand with movmatrix (an 8x8 transpose in
+// registers). Softmax bookkeeping follows the CUDA-core kernels: log2 domain, lazy rescaling.
+
+constexpr int kMmaWarps = 4;
+constexpr int kMmaThreads = 32 * kMmaWarps;
+constexpr int kMmaStages = 3;
+constexpr int kMmaTile = 2048;                  // 16 x 64 bf16, swizzled
+constexpr int kMmaHotStage = 2 * kMmaTile;      // K tile + V tile
+constexpr int kMmaRec = 2368;                   // int8 record at bs 16, d 64
+constexpr int kMmaRecStage = 2432;              // record stage stride (a multiple of 128 bytes)
+constexpr int kMmaCtasPerSm = 4;
+constexpr int kMmaTargetCtas = kMmaCtasPerSm * kNumSMs;
+constexpr int kMmaBody = kMmaWarps * kMmaStages * kMmaHotStage;  // 48 KiB: hot stages, or cold tiles + raw stages
+static_assert(kMmaWarps * 2 * kMmaTile + kMmaWarps * kMmaStages * kMmaRecStage <= kMmaBody, "cold layout exceeds the body");
+constexpr size_t kMmaSmem = 1024 + kMmaBody + kMmaWarps * kMmaStages * 8;
+
+struct MmaParams {
+  AttnParams p;
+  CUtensorMap tk[2], tv[2];  // per segment: K and V maps of a list or pairs segment
+  int head_major[2];         // map coordinate order: (0, 0, head, row) instead of (0, 0, row, head)
+};
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t movtrans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// (lo, hi) -> bf16x2 with lo in the low half; and back to float2 (exact).
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+__device__ __forceinline__ float2 unpack_bf2(uint32_t w) { return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)); }
+
+// Splits (a, b) into three bf16x2 terms whose sum is (a, b) to 24 significant bits.
+__device__ __forceinline__ void split3(float a, float b, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+  hi = pack_bf2(a, b);
+  const float2 r = __fadd2_rn(f2(a, b), f2(-unpack_bf2(hi).x, -unpack_bf2(hi).y));
+  mid = pack_bf2(r.x, r.y);
+  const float2 r2 = __fadd2_rn(r, f2(-unpack_bf2(mid).x, -unpack_bf2(mid).y));
+  lo = pack_bf2(r2.x, r2.y);
+}
+
+// 8 int8 codes -> 4 float2 of (code + 128), exactly (2^23 magic, as codes16).
+__device__ __forceinline__ void codes8(uint2 w, float2 (&u)[4]) {
+  const uint32_t a = w.x ^ 0x80808080u, b = w.y ^ 0x80808080u;
+  const float2 mm = f2(-8388608.0f, -8388608.0f);
+  u[0] = __fadd2_rn(f2(__uint_as_float(__byte_perm(a, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(a, 0x4b000000u, 0x7651))), mm);
+  u[1] = __fadd2_rn(f2(__uint_as_float(__byte_perm(a, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(a, 0x4b000000u, 0x7653))), mm);
+  u[2] = __fadd2_rn(f2(__uint_as_float(__byte_perm(b, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(b, 0x4b000000u, 0x7651))), mm);
+  u[3] = __fadd2_rn(f2(__uint_as_float(__byte_perm(b, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(b, 0x4b000000u, 0x7653))), mm);
+}
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+
+// Dequantises the int8 record at `raw` (kq | vq | k_scale | k_zero | v_scale | v_zero, bs 16, d 64)
+// into bf16 K and V tiles in the swizzled layout. Lane: channel group lane & 7 (8 channels), tokens
+// (lane >> 3) + 4i.
+__device__ __forceinline__ void dequant_record(const unsigned char* raw, unsigned char* kt, unsigned char* vt, int lane) {
+  const int gq = lane & 7, tb = lane >> 3;
+  float2 ks2[4], kz2[4];
+  {
+    const uint4 a = *reinterpret_cast<const uint4*>(raw + 2048 + 16 * gq);
+    const uint4 b = *reinterpret_cast<const uint4*>(raw + 2048 + 128 + 16 * gq);
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      ks2[x] = __half22float2(*reinterpret_cast<const __half2*>(&wa[x]));
+      kz2[x] = __half22float2(*reinterpret_cast<const __half2*>(&wb[x]));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = tb + 4 * i;
+    float2 u[4];
+    codes8(*reinterpret_cast<const uint2*>(raw + t * 64 + 8 * gq), u);
+    float2 k[4];
+#pragma unroll
+    for (int x = 0; x < 4; ++x) k[x] = __ffma2_rn(u[x], ks2[x], kz2[x]);
+    uint4 o;
+    o.x = pack_bf2(k[0].x, k[0].y);
+    o.y = pack_bf2(k[1].x, k[1].y);
+    o.z = pack_bf2(k[2].x, k[2].y);
+    o.w = pack_bf2(k[3].x, k[3].y);
+    *reinterpret_cast<uint4*>(kt + swz(t, gq)) = o;
+  }
+  const __half* vsc = reinterpret_cast<const __half*>(raw + 2304);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = tb + 4 * i;
+    const float vs = __half2float(vsc[t]), vz = __half2float(vsc[16 + t]);
+    const float2 vs2 = f2(vs, vs), vz2 = f2(vz, vz);
+    float2 u[4];
+    codes8(*reinterpret_cast<const uint2*>(raw + 1024 + t * 64 + 8 * gq), u);
+    float2 v[4];
+#pragma unroll
+    for (int x = 0; x < 4; ++x) v[x] = __ffma2_rn(u[x], vs2, vz2);
+    uint4 o;
+    o.x = pack_bf2(v[0].x, v[0].y);
+    o.y = pack_bf2(v[1].x, v[1].y);
+    o.z = pack_bf2(v[2].x, v[2].y);
+    o.w = pack_bf2(v[3].x, v[3].y);
+    *reinterpret_cast<uint4*>(vt + swz(t, gq)) = o;
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kMmaThreads, kMmaCtasPerSm) attn_mma_kernel(const __grid_constant__ MmaParams mp) {
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query group");
+  constexpr int D = 64, BS = 16;
+  const AttnParams& p = mp.p;
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ int sh_bad;
+  unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int j = blockIdx.y;
+  int split = blockIdx.x, si = 0;
+  if (p.n_segs > 1 && split >= p.seg[0].n_splits) {
+    si = 1;
+    split -= p.seg[0].n_splits;
+  }
+  const Seg& S = p.seg[si];
+  const bool list = S.kind == SEG_LIST;
+  const bool rec = S.kind == SEG_RANGE_REC;
+  const CUtensorMap* tk = &mp.tk[si];
+  const CUtensorMap* tv = &mp.tv[si];
+  const bool head_major = mp.head_major[si] != 0;
+
+  // Shared memory: hot/pairs segments use kMmaStages stages of (K tile, V tile) per warp; record
+  // segments a (K tile, V tile) pair per warp followed by kMmaStages raw record stages per warp.
+  unsigned char* tiles = smem + warp * 2 * kMmaTile;  // record segments only
+  unsigned char* stage0 = rec ? smem + kMmaWarps * 2 * kMmaTile + warp * kMmaStages * kMmaRecStage : smem + warp * kMmaStages * kMmaHotStage;
+  const int stage_stride = rec ? kMmaRecStage : kMmaHotStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kMmaBody) + warp * kMmaStages;
+  if (threadIdx.x == 0) sh_bad = 0;
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kMmaStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // Q^T fragments (bf16, exact): b0 = q[g][16ks + 2t .. +1], b1 = q[g][16ks + 2t + 8 .. +9].
+  uint32_t bq[4][2];
+  {
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(static_cast<const __nv_bfloat16*>(p.q) + ((int64_t)j * G + (g < G ? g : 0)) * D);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      bq[ks][0] = g < G ? q[(16 * ks + 2 * t) / 2] : 0u;
+      bq[ks][1] = g < G ? q[(16 * ks + 2 * t + 8) / 2] : 0u;
+    }
+  }
+  // ldmatrix lane offsets within a tile: K (non-transposed, k-step ks) and V (transposed, m-tile mt).
+  uint32_t koff[4], voff[4];
+  {
+    const int i = lane >> 3, r7 = lane & 7;
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      koff[x] = swz(r7 + 8 * (i & 1), 2 * x + (i >> 1));
+      voff[x] = swz(r7 + 8 * (i >> 1), 2 * x + (i & 1));
+    }
+  }
+
+  float o[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) o[a][b] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+
+  const int begin = split * S.chunk;
+  const int end = min(S.n_items, begin + S.chunk);
+  uint32_t excl_word = 0;
+  const int w0 = (S.first_block + begin) / 32;
+  if (!list) {
+    const int w = w0 + lane;
+    excl_word = (S.excluded != nullptr && w < S.bitmap_words && w * 32 < S.first_block + end)
+                    ? __ldg(S.excluded + (int64_t)j * S.bitmap_words + w) : 0u;
+  }
+  auto next_item = [&](int it) -> int {
+    if (list) return it < end ? it : end;
+    while (it < end) {
+      const int blk = S.first_block + it;
+      const int wi = blk / 32 - w0;
+      uint32_t word;
+      if (wi < 32) {
+        word = __shfl_sync(0xffffffffu, excl_word, wi);
+      } else {
+        word = (S.excluded != nullptr && blk / 32 < S.bitmap_words) ? __ldg(S.excluded + (int64_t)j * S.bitmap_words + blk / 32) : 0u;
+      }
+      if (!((word >> (blk % 32)) & 1u)) return it;
+      it += kMmaWarps;
+    }
+    return end;
+  };
+  int row_cache = 0, cache_batch = -1;
+  auto list_row = [&](int n) -> int {
+    const int batch = n >> 5;
+    if (batch != cache_batch) {
+      const int my_it = begin + warp + (batch * 32 + lane) * kMmaWarps;
+      int r = 0;
+      if (my_it < end) {
+        const int blk = __ldg(S.blocks + (int64_t)j * S.n_list + my_it);
+        r = S.slot_of != nullptr ? __ldg(S.slot_of + (int64_t)j * S.slot_stride + blk) : blk;
+      }
+      row_cache = r;
+      cache_batch = batch;
+    }
+    return __shfl_sync(0xffffffffu, row_cache, n & 31);
+  };
+  auto issue = [&](int it, int n, int s) {
+    unsigned char* dst = stage0 + s * stage_stride;
+    const int row = list ? list_row(n) : S.first_block + it;
+    if (lane == 0) {
+      if (rec) {
+        mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaRec);
+        tma_load_1d(dst, S.records + ((int64_t)row * p.h + j) * S.width, (uint32_t)kMmaRec, &bars[s]);
+      } else {
+        mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaHotStage);
+        const int c2 = head_major ? j : row, c3 = head_major ? row : j;
+        tma_load_4d(smem_u32(dst), tk, 0, 0, c2, c3, &bars[s]);
+        tma_load_4d(smem_u32(dst + kMmaTile), tv, 0, 0, c2, c3, &bars[s]);
+      }
+    }
+  };
+
+  int issue_it = next_item(begin + warp), n_issued = 0;
+#pragma unroll 1
+  for (int s = 0; s < kMmaStages; ++s) {
+    if (issue_it < end) {
+      issue(issue_it, n_issued, s);
+      ++n_issued;
+      issue_it = next_item(issue_it + kMmaWarps);
+    }
+  }
+
+  uint32_t phase = 0;
+  int s = 0, n_done = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int it = next_item(begin + warp); it < end; it = next_item(it + kMmaWarps)) {
+    ok = __all_sync(0xffffffffu, mbar_wait(&bars[s], (phase >> s) & 1u));
+    if (!ok) break;
+    phase ^= 1u << s;
+    ++n_done;
+    unsigned char* st = stage0 + s * stage_stride;
+    uint32_t kt, vt;
+    if (rec) {
+      dequant_record(st, tiles, tiles + kMmaTile, lane);
+      __syncwarp();
+      // The raw stage is free again: refill it before the contractions.
+      if (issue_it < end) {
+        issue(issue_it, n_issued, s);
+        ++n_issued;
+        issue_it = next_item(issue_it + kMmaWarps);
+      }
+      kt = smem_u32(tiles);
+      vt = kt + kMmaTile;
+    } else {
+      kt = smem_u32(st);
+      vt = kt + kMmaTile;
+    }
+
+    // ---- S^T = K . Q^T ----
+    float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int ks = 0; ks < 4; ks += 2) {
+      uint32_t a[4], b[4];
+      ldsm_x4(kt + koff[ks], a);
+      ldsm_x4(kt + koff[ks + 1], b);
+      mma_bf16(sa, a, bq[ks][0], bq[ks][1]);
+      mma_bf16(sb, b, bq[ks + 1][0], bq[ks + 1][1]);
+    }
+    // Lane scores: x0 (token g, row 2t), x1 (token g, row 2t+1), x2 / x3 (token g + 8).
+    float x0 = (sa[0] + sb[0]) * p.scale_log2, x1 = (sa[1] + sb[1]) * p.scale_log2;
+    float x2 = (sa[2] + sb[2]) * p.scale_log2, x3 = (sa[3] + sb[3]) * p.scale_log2;
+    if (list && it == S.n_list - 1) {
+      if (g >= S.last_fill) x0 = x1 = -INFINITY;
+      if (g + 8 >= S.last_fill) x2 = x3 = -INFINITY;
+    }
+    // ---- softmax update (lazy rescaling, as the CUDA-core kernels) ----
+    const bool need = x0 > m0 + kLazy || x2 > m0 + kLazy || x1 > m1 + kLazy || x3 > m1 + kLazy;
+    if (__any_sync(0xffffffffu, need)) {
+      float mb0 = fmaxf(x0, x2), mb1 = fmaxf(x1, x3);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
+        mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
+      }
+      if (mb0 > m0 + kLazy) {
+        const float alpha = exp2f(m0 - mb0);  // 0 when m0 was -inf
+        l0 *= alpha;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          o[mt][0] *= alpha;
+          o[mt][2] *= alpha;
+        }
+        m0 = mb0;
+      }
+      if (mb1 > m1 + kLazy) {
+        const float alpha = exp2f(m1 - mb1);
+        l1 *= alpha;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          o[mt][1] *= alpha;
+          o[mt][3] *= alpha;
+        }
+        m1 = mb1;
+      }
+    }
+    const float p0 = m0 == -INFINITY ? 0.0f : exp2f(x0 - m0);
+    const float p2 = m0 == -INFINITY ? 0.0f : exp2f(x2 - m0);
+    const float p1 = m1 == -INFINITY ? 0.0f : exp2f(x1 - m1);
+    const float p3 = m1 == -INFINITY ? 0.0f : exp2f(x3 - m1);
+    l0 += p0 + p2;
+    l1 += p1 + p3;
+    // ---- P^T operand: three bf16 terms, transposed into the B layout ----
+    uint32_t h01, m01, s01, h23, m23, s23;
+    split3(p0, p1, h01, m01, s01);
+    split3(p2, p3, h23, m23, s23);
+    const uint32_t bh0 = movtrans(h01), bh1 = movtrans(h23);
+    const uint32_t bm0 = movtrans(m01), bm1 = movtrans(m23);
+    const uint32_t bl0 = movtrans(s01), bl1 = movtrans(s23);
+    // ---- O^T += V^T . P^T ----
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      uint32_t a[4];
+      ldsm_x4_t(vt + voff[mt], a);
+      mma_bf16(o[mt], a, bl0, bl1);
+      mma_bf16(o[mt], a, bm0, bm1);
+      mma_bf16(o[mt], a, bh0, bh1);
+    }
+    __syncwarp();  // every lane is done with the stage (and the tiles) before they are refilled
+    if (!rec && issue_it < end) {
+      issue(issue_it, n_issued, s);
+      ++n_issued;
+      issue_it = next_item(issue_it + kMmaWarps);
+    }
+    s = (s + 1 == kMmaStages) ? 0 : s + 1;
+  }
+  // After a timed-out wait, wait (bounded) for the copies still in flight.
+  for (int k = n_done; !ok && k < n_issued; ++k) {
+    if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (phase >> s) & 1u))) break;
+    phase ^= 1u << s;
+    s = (s + 1 == kMmaStages) ? 0 : s + 1;
+  }
+  if (!ok && lane == 0) atomicExch(&sh_bad, 1);
+
+  // ---- epilogue: per-warp partials through shared memory (the stages are idle now) ----
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  __syncthreads();
+  float* out = p.part + ((int64_t)j * p.n_splits_total + blockIdx.x) * G * (D + 2);
+  if (sh_bad) {
+    for (int e = threadIdx.x; e < G * (D + 2); e += blockDim.x) out[e] = e < G ? -INFINITY : 0.0f;
+    return;
+  }
+  float* sh_o = reinterpret_cast<float*>(smem);           // [warp][G][D]
+  float* sh_ml = sh_o + kMmaWarps * G * D;                // [warp][m(G) | l(G)]
+  const int r0 = 2 * t, r1 = 2 * t + 1;
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    if (r0 < G) {
+      sh_o[(warp * G + r0) * D + 16 * mt + g] = o[mt][0];
+      sh_o[(warp * G + r0) * D + 16 * mt + g + 8] = o[mt][2];
+    }
+    if (r1 < G) {
+      sh_o[(warp * G + r1) * D + 16 * mt + g] = o[mt][1];
+      sh_o[(warp * G + r1) * D + 16 * mt + g + 8] = o[mt][3];
+    }
+  }
+  if (g == 0) {
+    if (r0 < G) {
+      sh_ml[warp * 2 * G + r0] = m0;
+      sh_ml[warp * 2 * G + G + r0] = l0;
+    }
+    if (r1 < G) {
+      sh_ml[warp * 2 * G + r1] = m1;
+      sh_ml[warp * 2 * G + G + r1] = l1;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int r = e / D, c = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kMmaWarps; ++w) M = fmaxf(M, sh_ml[w * 2 * G + r]);
+    float O = 0.0f, Lr = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kMmaWarps; ++w) {
         const float mw = sh_ml[w * 2 * G + r];
         const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
         O = fmaf(sh_o[(w * G + r) * D + c], f, O);
@@ -938,6 +1400,7 @@ int fill_hot(const char* who, Seg& S, int h, int d, int bs, const lkv_hot_set* h
   S.kind = SEG_LIST;
   S.k_base = hs->k_base; S.v_base = hs->v_base; S.s_row = hs->s_row; S.s_head = hs->s_head; S.s_tok = hs->s_tok;
   S.blocks = hs->blocks; S.n_list = hs->n_list; S.last_fill = hs->last_fill; S.slot_of = hs->slot_of; S.slot_stride = hs->slot_stride;
+  S.n_rows = hs->n_rows > 0 ? hs->n_rows : 0;
   S.n_items = hs->n_list;
   (void)h; (void)d;
   return LKV_OK;
@@ -959,6 +1422,7 @@ int fill_cold(const char* who, Seg& S, int h, int d, int bs, int dtype, const lk
     S.k_base = cs->store;
     S.v_base = static_cast<const char*>(cs->store) + (size_t)bs * d * dtype_size(dtype);
     S.s_row = (int64_t)h * 2 * bs * d; S.s_head = 2ll * bs * d; S.s_tok = d;
+    S.n_rows = (int64_t)cs->first_block + cs->n_blocks;
   }
   S.first_block = cs->first_block; S.excluded = cs->excluded; S.bitmap_words = cs->bitmap_words;
   S.n_items = cs->n_blocks;
@@ -966,8 +1430,8 @@ int fill_cold(const char* who, Seg& S, int h, int d, int bs, int dtype, const lk
 }
 
 // Split the target CTA count between two segments in proportion to their bytes.
-void split_two(Seg& hot, Seg& cold, int h, int hot_item_bytes, int cold_item_bytes) {
-  const int target = (kTargetCtas + h - 1) / h;
+void split_two(Seg& hot, Seg& cold, int h, int hot_item_bytes, int cold_item_bytes, int total_ctas) {
+  const int target = (total_ctas + h - 1) / h;
   const double wh = (double)hot.n_items * hot_item_bytes, wc = (double)cold.n_items * cold_item_bytes;
   int th = wh + wc > 0 ? (int)(target * wh / (wh + wc) + 0.5) : 0;
   if (hot.n_items > 0 && th < 1) th = 1;
@@ -975,6 +1439,119 @@ void split_two(Seg& hot, Seg& cold, int h, int hot_item_bytes, int cold_item_byt
   if (cold.n_items > 0 && tc < 1) tc = 1;
   set_split(hot, th);
   set_split(cold, tc);
+}
+
+// ---- the tensor-core path -----------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// K and V maps of a list or pairs segment: 4-D bf16 tensors (channel, token, row, head) with a box of
+// one 16 x 64 block, 128-byte swizzle. The row and head dimensions are ordered by stride.
+bool make_kv_maps(const Seg& S, int h, CUtensorMap* tk, CUtensorMap* tv, int* head_major) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr || S.n_rows <= 0) return false;
+  const int64_t es = 2;
+  const int64_t st = S.s_tok * es, sr = S.s_row * es, sh = S.s_head * es;
+  const bool hm = sh < sr;
+  const cuuint64_t dims[4] = {64, 16, (cuuint64_t)(hm ? h : S.n_rows), (cuuint64_t)(hm ? S.n_rows : h)};
+  const cuuint64_t strides[3] = {(cuuint64_t)st, (cuuint64_t)(hm ? sh : sr), (cuuint64_t)(hm ? sr : sh)};
+  const cuuint32_t box[4] = {64, 16, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  for (int i = 0; i < 2; ++i) {
+    CUresult r = enc(i == 0 ? tk : tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(i == 0 ? S.k_base : S.v_base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+  }
+  *head_major = hm ? 1 : 0;
+  return true;
+}
+
+// Whether the tensor-core kernel takes this launch (bf16, d 64, bs 16, G <= 8, stores in device
+// memory, 64-channel token rows); fills the tensor maps of its list / pairs segments.
+bool mma_plan(const AttnParams& p, int g, int d, bool bf16, MmaParams& mp) {
+  if (!bf16 || d != 64 || p.bs != 16 || (g != 1 && g != 2 && g != 4 && g != 8)) return false;
+  for (int i = 0; i < p.n_segs; ++i) {
+    const Seg& S = p.seg[i];
+    if (S.n_items == 0) continue;
+    if (S.kind == SEG_RANGE_REC) {
+      if (S.width != kMmaRec || is_host_mapped(S.records)) return false;
+    } else {
+      if (S.s_tok != d || is_host_mapped(S.k_base) || is_host_mapped(S.v_base)) return false;
+      if (!make_kv_maps(S, p.h, &mp.tk[i], &mp.tv[i], &mp.head_major[i])) return false;
+    }
+  }
+  return true;
+}
+
+template <int G>
+int launch_mma(const MmaParams& mp, cudaStream_t st) {
+  static uint64_t attr_set = 0;  // one bit per device
+  auto k = attn_mma_kernel<G>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMmaSmem);
+    if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
+    attr_set |= bit;
+  }
+  k<<<dim3(mp.p.n_splits_total, mp.p.h), kMmaThreads, kMmaSmem, st>>>(mp);
+  return LKV_OK;
+}
+
+// Splits, workspace check and launch of one attention call (partials + combine).
+template <typename T, typename TO>
+int run_attention(const char* who, AttnParams& p, int g, int d, TO* out, float* lse, float* seg_out, float* seg_lse, size_t workspace_bytes,
+                  cudaStream_t st) {
+  MmaParams mp{};
+  const bool mma = mma_plan(p, g, d, sizeof(T) == 2, mp);
+  const int total = mma ? kMmaTargetCtas : kTargetCtas;
+  if (p.n_segs == 1) {
+    set_split(p.seg[0], (total + p.h - 1) / p.h);
+    p.n_splits_total = p.seg[0].n_splits;
+  } else {
+    split_two(p.seg[0], p.seg[1], p.h, 4096, 2368, total);
+    p.n_splits_total = p.seg[0].n_splits + p.seg[1].n_splits;
+  }
+  const size_t need = partial_bytes(p.h, g, d, p.n_splits_total);
+  if (workspace_bytes < need) return fail(LKV_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, need);
+  if (!mma) return dispatch<T, TO>(g, d, p, out, lse, seg_out, seg_lse, st);
+  if constexpr (sizeof(T) == 2) {
+    mp.p = p;
+    int rc = LKV_OK;
+    if (p.n_splits_total > 0) {
+      switch (g) {
+        case 1: rc = launch_mma<1>(mp, st); break;
+        case 2: rc = launch_mma<2>(mp, st); break;
+        case 4: rc = launch_mma<4>(mp, st); break;
+        default: rc = launch_mma<8>(mp, st); break;
+      }
+    }
+    if (rc) return rc;
+    const int n0 = p.seg[0].n_splits, n1 = p.n_segs > 1 ? p.seg[1].n_splits : 0;
+    switch (g) {
+      case 1: attn_combine_kernel<TO, 1, 64><<<dim3(p.h, 1), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq); break;
+      case 2: attn_combine_kernel<TO, 2, 64><<<dim3(p.h, 2), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq); break;
+      case 4: attn_combine_kernel<TO, 4, 64><<<dim3(p.h, 4), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq); break;
+      default: attn_combine_kernel<TO, 8, 64><<<dim3(p.h, 8), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq); break;
+    }
+    return launched("lkv attention");
+  }
+  return fail(LKV_ERR_ARG, "%s: unreachable", who);
 }
 
 }  // namespace
@@ -997,7 +1574,7 @@ int lkv_device_status(int* status, int clear) {
 
 size_t lkv_attention_workspace(int h, int hq, int d, int n_items) {
   if (h <= 0 || hq <= 0) return 0;
-  const int s = splits_for(n_items, (kTargetCtas + h - 1) / h);
+  const int s = splits_for(n_items, (kMmaTargetCtas + h - 1) / h);
   const size_t b = partial_bytes(h, hq / h, d, s);
   return b > 0 ? b : 16;
 }
@@ -1007,29 +1584,26 @@ size_t lkv_exact_attention_workspace(int h, int hq, int d, int n_list, int n_blo
   Seg a{}, b{};
   a.n_items = n_list;
   b.n_items = n_blocks;
-  split_two(a, b, h, 4096, 2368);
+  split_two(a, b, h, 4096, 2368, kMmaTargetCtas);
   const size_t s = partial_bytes(h, hq / h, d, a.n_splits + b.n_splits);
   return s > 0 ? s : 16;
 }
 
 int lkv_hot_attention(const void* q, int hq, int h, int d, int bs, const void* k_base, const void* v_base, int dtype, int64_t s_row,
-                      int64_t s_head, int64_t s_tok, const int32_t* blocks, int n_list, const int32_t* slot_of, int64_t slot_stride,
-                      int last_fill, float scale, float* out, float* lse, void* workspace, size_t workspace_bytes, void* stream) {
+                      int64_t s_head, int64_t s_tok, int64_t n_rows, const int32_t* blocks, int n_list, const int32_t* slot_of,
+                      int64_t slot_stride, int last_fill, float scale, float* out, float* lse, void* workspace, size_t workspace_bytes,
+                      void* stream) {
   if (int rc = common_checks("lkv_hot_attention", q, hq, h, d, bs, dtype, workspace)) return rc;
   if (out == nullptr || lse == nullptr) return fail(LKV_ERR_PTR, "lkv_hot_attention: null pointer");
-  lkv_hot_set hs{k_base, v_base, dtype, s_row, s_head, s_tok, blocks, n_list, slot_of, slot_stride, last_fill};
+  lkv_hot_set hs{k_base, v_base, dtype, s_row, s_head, s_tok, blocks, n_list, slot_of, slot_stride, last_fill, n_rows};
   AttnParams p{};
   p.q = q; p.hq = hq; p.h = h; p.bs = bs; p.scale_log2 = scale * kLog2e;
   if (int rc = fill_hot("lkv_hot_attention", p.seg[0], h, d, bs, &hs)) return rc;
   p.n_segs = 1;
-  set_split(p.seg[0], (kTargetCtas + h - 1) / h);
-  p.n_splits_total = p.seg[0].n_splits;
   p.part = static_cast<float*>(workspace);
-  if (workspace_bytes < partial_bytes(h, hq / h, d, p.n_splits_total))
-    return fail(LKV_ERR_WORKSPACE, "lkv_hot_attention: workspace %zu < %zu bytes", workspace_bytes, partial_bytes(h, hq / h, d, p.n_splits_total));
   cudaStream_t st = as_stream(stream);
-  return dtype == LKV_BF16 ? dispatch<__nv_bfloat16, float>(hq / h, d, p, out, lse, nullptr, nullptr, st)
-                           : dispatch<float, float>(hq / h, d, p, out, lse, nullptr, nullptr, st);
+  return dtype == LKV_BF16 ? run_attention<__nv_bfloat16, float>("lkv_hot_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace_bytes, st)
+                           : run_attention<float, float>("lkv_hot_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace_bytes, st);
 }
 
 int lkv_cold_attention(const void* q, int hq, int h, int d, int bs, const void* cold, int cold_kind, int dtype, int first_block,
@@ -1042,14 +1616,10 @@ int lkv_cold_attention(const void* q, int hq, int h, int d, int bs, const void* 
   p.q = q; p.hq = hq; p.h = h; p.bs = bs; p.scale_log2 = scale * kLog2e;
   if (int rc = fill_cold("lkv_cold_attention", p.seg[0], h, d, bs, dtype, &cs)) return rc;
   p.n_segs = 1;
-  set_split(p.seg[0], (kTargetCtas + h - 1) / h);
-  p.n_splits_total = p.seg[0].n_splits;
   p.part = static_cast<float*>(workspace);
-  if (workspace_bytes < partial_bytes(h, hq / h, d, p.n_splits_total))
-    return fail(LKV_ERR_WORKSPACE, "lkv_cold_attention: workspace %zu < %zu bytes", workspace_bytes, partial_bytes(h, hq / h, d, p.n_splits_total));
   cudaStream_t st = as_stream(stream);
-  return dtype == LKV_BF16 ? dispatch<__nv_bfloat16, float>(hq / h, d, p, out, lse, nullptr, nullptr, st)
-                           : dispatch<float, float>(hq / h, d, p, out, lse, nullptr, nullptr, st);
+  return dtype == LKV_BF16 ? run_attention<__nv_bfloat16, float>("lkv_cold_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace_bytes, st)
+                           : run_attention<float, float>("lkv_cold_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace_bytes, st);
 }
 
 int lkv_exact_attention(const void* q, int hq, int h, int d, int bs, const lkv_hot_set* hot, const lkv_cold_set* cold, float scale,
@@ -1064,19 +1634,16 @@ int lkv_exact_attention(const void* q, int hq, int h, int d, int bs, const lkv_h
   if (int rc = fill_hot("lkv_exact_attention", p.seg[0], h, d, bs, hot)) return rc;
   if (int rc = fill_cold("lkv_exact_attention", p.seg[1], h, d, bs, hot->dtype, cold)) return rc;
   p.n_segs = 2;
-  split_two(p.seg[0], p.seg[1], h, 4096, 2368);
-  p.n_splits_total = p.seg[0].n_splits + p.seg[1].n_splits;
   p.part = static_cast<float*>(workspace);
-  if (workspace_bytes < partial_bytes(h, hq / h, d, p.n_splits_total))
-    return fail(LKV_ERR_WORKSPACE, "lkv_exact_attention: workspace %zu < %zu bytes", workspace_bytes, partial_bytes(h, hq / h, d, p.n_splits_total));
   cudaStream_t st = as_stream(stream);
   const int g = hq / h;
   const bool bf = hot->dtype == LKV_BF16;
+  const char* who = "lkv_exact_attention";
   if (out_dtype == LKV_BF16)
-    return bf ? dispatch<__nv_bfloat16, __nv_bfloat16>(g, d, p, static_cast<__nv_bfloat16*>(out), lse, part_out, part_lse, st)
-              : dispatch<float, __nv_bfloat16>(g, d, p, static_cast<__nv_bfloat16*>(out), lse, part_out, part_lse, st);
-  return bf ? dispatch<__nv_bfloat16, float>(g, d, p, static_cast<float*>(out), lse, part_out, part_lse, st)
-            : dispatch<float, float>(g, d, p, static_cast<float*>(out), lse, part_out, part_lse, st);
+    return bf ? run_attention<__nv_bfloat16, __nv_bfloat16>(who, p, g, d, static_cast<__nv_bfloat16*>(out), lse, part_out, part_lse, workspace_bytes, st)
+              : run_attention<float, __nv_bfloat16>(who, p, g, d, static_cast<__nv_bfloat16*>(out), lse, part_out, part_lse, workspace_bytes, st);
+  return bf ? run_attention<__nv_bfloat16, float>(who, p, g, d, static_cast<float*>(out), lse, part_out, part_lse, workspace_bytes, st)
+            : run_attention<float, float>(who, p, g, d, static_cast<float*>(out), lse, part_out, part_lse, workspace_bytes, st);
 }
 
 int lkv_lse_merge(const float* outs, const float* lses, int n_parts, int64_t rows, int d, void* out, int out_dtype, float* lse_out,

@@ -12,9 +12,13 @@
 // workspace, L2-resident) finds the k-th largest key exactly (keys are unique); the keys at or
 // above it are compacted into shared memory, bitonic-sorted descending and written out as block
 // ids. The optional bitmap marks the selected block ids for the exact pass's complement.
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace lkv {
 namespace {
@@ -31,8 +35,16 @@ inline int score_rows(int d, size_t es) {
 
 // One thread per candidate row of a tile. The CTA first copies the tile's kmin and kmax rows
 // (contiguous in memory) into shared memory with coalesced 16-byte loads, storing 16-byte chunk c
-// of row t at chunk position c ^ (t & 7): a quarter-warp reading chunk c of 8 consecutive rows then
+// of row t at chunk position (c + t % 8) mod chunks (a rotation within the row, so rows of fewer
+// than 8 chunks stay in place): a quarter-warp reading chunk c of 8 consecutive rows then
 // touches 8 distinct bank groups, while each thread still walks its row's channels in order.
+// Position of 16-byte chunk c of tile row t (row_bytes = chunks * 16).
+__device__ __forceinline__ int tile_pos(int t, int c, int chunks, int row_bytes) {
+  int cc = c + (t & 7) % chunks;
+  if (cc >= chunks) cc -= chunks;
+  return t * row_bytes + cc * 16;
+}
+
 template <typename TQ, typename TM, int G>
 __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin, const TM* __restrict__ kmax,
                                    int64_t m_head, int first_block, int n_cand, int bound_mode, uint64_t* __restrict__ keys,
@@ -56,7 +68,7 @@ __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __
   const unsigned char* gmin = reinterpret_cast<const unsigned char*>(kmin + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
   for (int u = threadIdx.x; u < n_rows * chunks; u += blockDim.x) {
     const int t = u / chunks, c = u % chunks;
-    const int pos = t * row_bytes + ((c ^ (t & 7)) * 16);
+    const int pos = tile_pos(t, c, chunks, row_bytes);
     cp_async16(tile_max + pos, reinterpret_cast<const uint4*>(gmax) + u);
     cp_async16(tile_min + pos, reinterpret_cast<const uint4*>(gmin) + u);
   }
@@ -69,7 +81,7 @@ __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __
   for (int r = 0; r < G; ++r) a[r] = b[r] = 0.0f;
   constexpr int PER = 16 / (int)sizeof(TM);  // elements per 16-byte chunk
   for (int c = 0; c < chunks; ++c) {
-    const int pos = t * row_bytes + ((c ^ (t & 7)) * 16);
+    const int pos = tile_pos(t, c, chunks, row_bytes);
     float mx[8], mn[8];
     if constexpr (PER == 8) {
       // Plain shared-memory loads (the read-only global path cannot address shared memory).
@@ -290,6 +302,328 @@ __global__ void __launch_bounds__(kSelectThreads) topk_kernel(const uint64_t* __
   }
 }
 
+// ---- the fused, cluster-wide select (ascending block-id output) -------------------------------
+//
+// One thread-block cluster of C CTAs per KV head (C <= 16): CTA c scores a contiguous slice of the
+// candidates (metadata tiles double-buffered through cp.async, the same per-row arithmetic as
+// quest_score_kernel) and keeps its keys in shared memory. The radix passes of topk_kernel then run
+// cluster-wide: each CTA adds its digit histogram into rank 0's shared memory (distributed shared
+// memory atomics), a cluster barrier, and every CTA reads the totals and picks the same digit.
+// Compaction: each CTA publishes its counts of keys above the k-th bound and equal to it; the
+// exclusive sums over lower ranks give each CTA its output offset and its share of the tied keys
+// (lowest ids first), so the selected ids come out in ascending block-id order with no sort.
+// Every CTA reaches every cluster barrier (no early exit).
+
+constexpr int kClusterThreads = 256;
+constexpr int kClusterMax = 16;
+constexpr int kClusterMaxPer = 4096;  // candidates per CTA (their keys stay in shared memory)
+
+template <typename TM, int G>
+__device__ __forceinline__ float row_bound(const unsigned char* tile_max, const unsigned char* tile_min, int t, int d, const float* qs,
+                                           int bound_mode) {
+  const int row_bytes = d * (int)sizeof(TM);
+  const int chunks = row_bytes / 16;
+  float a[G], b[G];
+#pragma unroll
+  for (int r = 0; r < G; ++r) a[r] = b[r] = 0.0f;
+  constexpr int PER = 16 / (int)sizeof(TM);
+  for (int c = 0; c < chunks; ++c) {
+    const int pos = tile_pos(t, c, chunks, row_bytes);
+    float mx[8], mn[8];
+    if constexpr (PER == 8) {
+      const uint4 x = *reinterpret_cast<const uint4*>(tile_max + pos), y = *reinterpret_cast<const uint4*>(tile_min + pos);
+      const uint32_t wx[4] = {x.x, x.y, x.z, x.w}, wy[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        mx[2 * i] = __uint_as_float(wx[i] << 16);
+        mx[2 * i + 1] = __uint_as_float(wx[i] & 0xffff0000u);
+        mn[2 * i] = __uint_as_float(wy[i] << 16);
+        mn[2 * i + 1] = __uint_as_float(wy[i] & 0xffff0000u);
+      }
+    } else {
+      const float4 x = *reinterpret_cast<const float4*>(tile_max + pos), y = *reinterpret_cast<const float4*>(tile_min + pos);
+      mx[0] = x.x; mx[1] = x.y; mx[2] = x.z; mx[3] = x.w;
+      mn[0] = y.x; mn[1] = y.y; mn[2] = y.z; mn[3] = y.w;
+    }
+    const int c0 = c * PER;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+#pragma unroll
+      for (int r = 0; r < G; ++r) {
+        a[r] = __fadd_rn(a[r], __fmul_rn(qs[r * d + c0 + i], mx[i]));
+        b[r] = __fadd_rn(b[r], __fmul_rn(qs[G * d + r * d + c0 + i], mn[i]));
+      }
+    }
+  }
+  float best = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < G; ++r) {
+    const float sc = bound_mode == LKV_BF16 ? bf16_round(__fadd_rn(bf16_round(a[r]), bf16_round(b[r]))) : __fadd_rn(a[r], b[r]);
+    best = fmaxf(best, sc);
+  }
+  return best;
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename TQ, typename TM, int G>
+__global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin,
+                                                                                const TM* __restrict__ kmax, int64_t m_head, int first_block,
+                                                                                int n_cand, int k, int bound_mode, int n_passes, int per, int rows,
+                                                                                int32_t* __restrict__ out_blocks, int out_ld,
+                                                                                float* __restrict__ out_bound, uint32_t* __restrict__ bitmap,
+                                                                                int bitmap_words) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int c = (int)cluster.block_rank();
+  const int j = blockIdx.y;
+  const int tid = threadIdx.x;
+  extern __shared__ __align__(16) unsigned char sm[];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t ghist[4][256];         // rank 0: cluster totals, one array per pass
+  __shared__ uint32_t table[kClusterMax][2];  // rank 0: per-CTA (above, equal) counts
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total, sh_pos0, sh_eq0;
+  float* qs = reinterpret_cast<float*>(sm);
+  const int row_bytes = d * (int)sizeof(TM);
+  const int chunks = row_bytes / 16;
+  const size_t buf_bytes = (size_t)rows * row_bytes * 2;
+  unsigned char* bufs = sm + (size_t)2 * G * d * sizeof(float);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(bufs + 2 * buf_bytes);
+
+  const int lo = min(n_cand, c * per);
+  const int hi = min(n_cand, lo + per);
+  const int cnt = hi - lo;
+  if (c == 0) {
+    for (int i = tid; i < 4 * 256; i += blockDim.x) (&ghist[0][0])[i] = 0u;
+    if (bitmap != nullptr)
+      for (int w = tid; w < bitmap_words; w += blockDim.x) bitmap[(int64_t)j * bitmap_words + w] = 0u;
+  }
+  for (int e = tid; e < G * d; e += blockDim.x) {
+    const float v = to_f32<TQ>(q[(int64_t)j * G * d + e]);
+    const float vp = fmaxf(v, 0.0f);
+    qs[e] = vp;
+    qs[G * d + e] = __fsub_rn(v, vp);
+  }
+
+  // ---- scores of the slice, in sub-tiles of `rows` candidates, double-buffered ----
+  const int n_sub = (cnt + rows - 1) / rows;
+  auto load = [&](int sub) {
+    unsigned char* tmax = bufs + (size_t)(sub & 1) * buf_bytes;
+    unsigned char* tmin = tmax + (size_t)rows * row_bytes;
+    const int base = lo + sub * rows;
+    const int nr = min(rows, hi - base);
+    const uint4* gmax = reinterpret_cast<const uint4*>(kmax + (int64_t)j * m_head + (int64_t)(first_block + base) * d);
+    const uint4* gmin = reinterpret_cast<const uint4*>(kmin + (int64_t)j * m_head + (int64_t)(first_block + base) * d);
+    for (int u = tid; u < nr * chunks; u += blockDim.x) {
+      const int t = u / chunks, cc = u % chunks;
+      const int pos = tile_pos(t, cc, chunks, row_bytes);
+      cp_async16(tmax + pos, gmax + u);
+      cp_async16(tmin + pos, gmin + u);
+    }
+    cp_async_commit();
+  };
+  if (n_sub > 0) load(0);
+  __syncthreads();  // q split visible
+  for (int sub = 0; sub < n_sub; ++sub) {
+    if (sub + 1 < n_sub) {
+      load(sub + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int base = lo + sub * rows;
+    const int nr = min(rows, hi - base);
+    if (tid < nr) {
+      const unsigned char* tmax = bufs + (size_t)(sub & 1) * buf_bytes;
+      const float best = row_bound<TM, G>(tmax, tmax + (size_t)rows * row_bytes, tid, d, qs, bound_mode);
+      const int ci = base + tid;
+      keys[ci - lo] = ((uint64_t)orderable(best) << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
+      if (out_bound != nullptr) out_bound[(int64_t)j * n_cand + ci] = best == 0.0f ? 0.0f : best;
+    }
+    __syncthreads();  // the buffer is read before it is refilled
+  }
+  cluster.sync();  // every slice scored; rank 0's totals and the bitmap row are zero
+
+  // ---- cluster-wide radix select of the k-th key ----
+  uint32_t* g0 = cluster.map_shared_rank(&ghist[0][0], 0);
+  const int kk = k < n_cand ? k : n_cand;
+  if (tid == 0) {
+    sh_remaining = (uint32_t)kk;
+    sh_bincount = 0;
+  }
+  uint32_t prefix = 0, mask = 0;
+  bool take_all = kk >= n_cand;
+  for (int pass = 0; pass < n_passes && !take_all; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i0 = 0; i0 < cnt; i0 += blockDim.x) {
+      const int i = i0 + tid;
+      const uint32_t h32 = i < cnt ? (uint32_t)(keys[i] >> 32) : 0u;
+      const bool counted = i < cnt && (h32 & mask) == prefix;
+      const uint32_t digit = counted ? ((h32 >> shift) & 255u) : 256u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+      if (counted && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+    }
+    __syncthreads();
+    for (int b = tid; b < 256; b += blockDim.x)
+      if (hist[b]) atomicAdd(&g0[pass * 256 + b], hist[b]);
+    cluster.sync();
+    for (int b = tid; b < 256; b += blockDim.x) hist[b] = g0[pass * 256 + b];
+    __syncthreads();
+    pick_digit(hist, &sh_digit, &sh_remaining, &sh_bincount);
+    __syncthreads();
+    prefix |= sh_digit << shift;
+    mask |= 255u << shift;
+    take_all = (sh_bincount == sh_remaining);
+    __syncthreads();
+  }
+  const uint32_t need_equal = take_all ? 0xffffffffu : sh_remaining;
+  const bool all = kk >= n_cand;
+
+  // ---- compaction in candidate order across the cluster ----
+  const int seg = (cnt + blockDim.x - 1) / blockDim.x;
+  const int tlo = min(cnt, tid * seg), thi = min(cnt, tlo + seg);
+  uint32_t n_gt = 0, n_eq = 0;
+  for (int i = tlo; i < thi; ++i) {
+    const uint32_t h32 = (uint32_t)(keys[i] >> 32) & mask;
+    n_gt += all || h32 > prefix;
+    n_eq += !all && h32 == prefix;
+  }
+  const uint32_t eq_before_t = block_scan(n_eq, warp_sums, &sh_total);
+  const uint32_t cta_eq = sh_total;
+  __syncthreads();
+  const uint32_t gt_before_t = block_scan(n_gt, warp_sums, &sh_total);
+  (void)gt_before_t;
+  const uint32_t cta_gt = sh_total;
+  if (tid == 0) {
+    uint32_t* t0 = cluster.map_shared_rank(&table[0][0], 0);
+    t0[2 * c] = cta_gt;
+    t0[2 * c + 1] = cta_eq;
+  }
+  cluster.sync();
+  if (tid == 0) {
+    const uint32_t* t0 = cluster.map_shared_rank(&table[0][0], 0);
+    uint32_t eqb = 0, posb = 0;
+    for (int r = 0; r < c; ++r) {
+      const uint32_t gt = t0[2 * r], eq = t0[2 * r + 1];
+      const uint32_t take = eqb < need_equal ? min(eq, need_equal - eqb) : 0u;
+      posb += gt + take;
+      eqb += eq;
+    }
+    sh_pos0 = posb;
+    sh_eq0 = eqb;
+  }
+  __syncthreads();
+  const uint32_t eq_before = sh_eq0 + eq_before_t;
+  const uint32_t take_eq = eq_before < need_equal ? min(n_eq, need_equal - eq_before) : 0u;
+  uint32_t pos = sh_pos0 + block_scan(n_gt + take_eq, warp_sums, &sh_total);
+  uint32_t eq_seen = 0;
+  for (int i = tlo; i < thi; ++i) {
+    const uint32_t h32 = (uint32_t)(keys[i] >> 32) & mask;
+    bool take = all || h32 > prefix;
+    if (!take && h32 == prefix) take = eq_seen++ < take_eq;
+    if (take && pos < (uint32_t)kk) {
+      const int blk = first_block + lo + i;
+      out_blocks[(int64_t)j * out_ld + pos] = blk;
+      if (bitmap != nullptr && blk / 32 < bitmap_words) atomicOr(&bitmap[(int64_t)j * bitmap_words + blk / 32], 1u << (blk % 32));
+      ++pos;
+    }
+  }
+  cluster.sync();  // rank 0's shared memory stays alive until every CTA has read it
+}
+
+// Cluster size for n candidates: enough CTAs for ~512 candidates each, at most 16, or 0 when a CTA
+// would need more than kClusterMaxPer keys.
+inline int cluster_size_for(int n_cand, int max_c) {
+  int c = (n_cand + 511) / 512;
+  if (c < 1) c = 1;
+  if (c > max_c) c = max_c;
+  if ((n_cand + c - 1) / c > kClusterMaxPer) return 0;
+  return c;
+}
+
+template <typename TQ, typename TM, int G>
+int launch_select_cluster(int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
+                          int n_cand, int k, int bound_mode, int n_passes, int32_t* out_blocks, int out_ld, float* out_bound, uint32_t* bitmap,
+                          int bitmap_words, bool* handled) {
+  *handled = false;
+  auto kern = quest_select_cluster_kernel<TQ, TM, G>;
+  static int max_c[64];  // per device: the largest schedulable cluster (0 = not yet known, -1 = none)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int di = dev & 63;
+  const int rows = score_rows(d, sizeof(TM));
+  // The attribute is set once per device for every head_dim (up to 256): q split, two buffers of
+  // the two metadata tiles (each at most kScoreTileBytes), the slice's keys.
+  const size_t worst = (size_t)2 * G * 256 * sizeof(float) + (size_t)2 * 2 * kScoreTileBytes + (size_t)kClusterMaxPer * sizeof(uint64_t);
+  if (max_c[di] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)worst);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    int best = -1;
+    for (int cs = kClusterMax; e == cudaSuccess && cs >= 1 && best < 0; cs >>= 1) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = cs;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(cs, 1);
+      cfg.blockDim = dim3(kClusterThreads);
+      cfg.dynamicSmemBytes = worst;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= 1) best = cs;
+    }
+    cudaGetLastError();
+    max_c[di] = best;
+  }
+  if (max_c[di] < 0) return LKV_OK;
+  const int C = cluster_size_for(n_cand, max_c[di]);
+  if (C == 0) return LKV_OK;
+  const int per = (n_cand + C - 1) / C;
+  const int rows_eff = per < rows ? per : rows;
+  const size_t smem = (size_t)2 * G * d * sizeof(float) + (size_t)2 * rows_eff * d * sizeof(TM) * 2 + (size_t)per * sizeof(uint64_t);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(C, h);
+  cfg.blockDim = dim3(kClusterThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin), static_cast<const TM*>(kmax), m_head,
+                                     first_block, n_cand, k, bound_mode, n_passes, per, rows_eff, out_blocks, out_ld, out_bound, bitmap,
+                                     bitmap_words);
+  if (e != cudaSuccess)
+    return fail(LKV_ERR_CUDA, "lkv_quest_topk(cluster select, %d CTAs x %d heads, %zu B shared): %s", C, h, smem, cudaGetErrorString(e));
+  *handled = true;
+  return LKV_OK;
+}
+
+template <typename TQ, typename TM>
+int select_cluster(int g, int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
+                   int n_cand, int k, int bound_mode, int n_passes, int32_t* out_blocks, int out_ld, float* out_bound, uint32_t* bitmap,
+                   int bitmap_words, bool* handled) {
+  switch (g) {
+    case 1: return launch_select_cluster<TQ, TM, 1>(h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, handled);
+    case 2: return launch_select_cluster<TQ, TM, 2>(h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, handled);
+    case 4: return launch_select_cluster<TQ, TM, 4>(h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, handled);
+    case 8: return launch_select_cluster<TQ, TM, 8>(h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, handled);
+    default: *handled = false; return LKV_OK;
+  }
+}
+
 template <typename TQ, typename TM>
 int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
                  int n_cand, int bound_mode, uint64_t* keys, float* out_bound) {
@@ -336,7 +670,7 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   if (h <= 0 || hq <= 0 || hq % h != 0) return fail(LKV_ERR_ARG, "lkv_quest_topk: %d query heads do not group over %d KV heads", hq, h);
   if (d <= 0 || d % 8 != 0 || d > 256) return fail(LKV_ERR_ARG, "lkv_quest_topk: head_dim %d unsupported", d);
   if (n_cand <= 0 || k <= 0 || k > n_cand) return fail(LKV_ERR_ARG, "lkv_quest_topk: need 0 < k <= n_cand (k=%d, n_cand=%d)", k, n_cand);
-  if (k > kMaxK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
+  if (k > kMaxK && order != LKV_ORDER_BLOCK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
   if (first_block < 0) return fail(LKV_ERR_ARG, "lkv_quest_topk: negative first block");
   if (out_ld < k) return fail(LKV_ERR_ARG, "lkv_quest_topk: output row stride %d < k=%d", out_ld, k);
   if (order != LKV_ORDER_BOUND && order != LKV_ORDER_BLOCK) return fail(LKV_ERR_ARG, "lkv_quest_topk: bad order %d", order);
@@ -350,6 +684,24 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
     return fail(LKV_ERR_ARG, "lkv_quest_topk: bitmap of %d words cannot hold block %d", bitmap_words, first_block + n_cand - 1);
   const int g = hq / h;
   cudaStream_t st = as_stream(stream);
+  // A bf16 bound's orderable 32-bit form has constant low 16 bits for a given sign, so its top 16
+  // bits order the keys: two 8-bit passes reach the k-th bound; ties go to the scan.
+  const int n_passes = bound_mode == LKV_BF16 ? 2 : 4;
+  if (order == LKV_ORDER_BLOCK) {
+    bool handled = false;
+    int rc2;
+    if (q_dtype == LKV_BF16 && meta_dtype == LKV_BF16)
+      rc2 = select_cluster<__nv_bfloat16, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, &handled);
+    else if (q_dtype == LKV_F32 && meta_dtype == LKV_F32)
+      rc2 = select_cluster<float, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, &handled);
+    else if (q_dtype == LKV_BF16 && meta_dtype == LKV_F32)
+      rc2 = select_cluster<__nv_bfloat16, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, &handled);
+    else
+      rc2 = select_cluster<float, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, &handled);
+    if (rc2) return rc2;
+    if (handled) return launched("lkv_quest_topk(cluster select)");
+    if (k > kMaxK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
+  }
   uint64_t* keys = static_cast<uint64_t*>(workspace);
   int rc;
   if (q_dtype == LKV_BF16 && meta_dtype == LKV_BF16)
@@ -368,9 +720,6 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   const int stage_keys = sel_smem + (size_t)n_cand * sizeof(uint64_t) <= 200 * 1024;
   const size_t smem = sel_smem + (stage_keys ? (size_t)n_cand * sizeof(uint64_t) : 0);
   if (smem > 48 * 1024) cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  // A bf16 bound's orderable 32-bit form has constant low 16 bits for a given sign, so its top 16
-  // bits order the keys: two 8-bit passes reach the k-th bound; ties go to the scan.
-  const int n_passes = bound_mode == LKV_BF16 ? 2 : 4;
   topk_kernel<<<h, kSelectThreads, smem, st>>>(keys, n_cand, k, first_block, out_blocks, out_ld, bitmap, bitmap_words, stage_keys,
                                                 order == LKV_ORDER_BLOCK, n_passes);
   return launched("lkv_quest_topk(select)");

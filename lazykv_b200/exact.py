@@ -8,10 +8,11 @@ int8 records dequantised in the kernel, and the hot pass, the cold pass and the 
 current block; cold = every other sealed block (exact.py:116-123).
 
 Unlike the reference, an int8 cold tier is allowed (the reference refuses it, exact.py:165-168):
-every sealed block except the sink is then attended as unpack(record) in the model dtype (the
-selected ones, which a fetch put in a slot) or in float32 (the cold ones), so the result does not
-depend on which blocks were selected beyond float32 rounding. The zero-copy fetch is allowed too:
-the selection never has to reach the host.
+every sealed block except the sink is then attended as unpack(record) in the model dtype, whether a
+fetch put it in a slot or the cold pass dequantises it from the record, which is the reference's
+rule for its mirror ("attends to what a fetch would have produced", exact.py:189-192); the result
+does not depend on which blocks were selected beyond float32 rounding. The zero-copy fetch is
+allowed too: the selection never has to reach the host.
 """
 
 from __future__ import annotations

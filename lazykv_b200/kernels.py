@@ -117,6 +117,18 @@ def attention_workspace_bytes(h: int, hq: int, d: int, n_items: int) -> int:
     return int(L.lib().lkv_attention_workspace(h, hq, d, n_items))
 
 
+def storage_rows(k_base: torch.Tensor, v_base: torch.Tensor, strides: tuple[int, int, int], h: int, block_size: int, d: int) -> int:
+    """Storage rows addressable through (s_row, s_head, s_tok) for KV heads 0..h-1 inside both
+    tensors' storage: the bound of the tensor-map loads (0 when not even one row fits)."""
+    s_row, s_head, s_tok = strides
+    reach = (h - 1) * s_head + (block_size - 1) * s_tok + d  # elements one row spans past its start
+    rows = []
+    for t in (k_base, v_base):
+        avail = t.untyped_storage().nbytes() // t.element_size() - t.storage_offset()
+        rows.append(0 if avail < reach else (avail - reach) // s_row + 1)
+    return max(0, min(rows))
+
+
 def hot_attention(query: torch.Tensor, k_base: torch.Tensor, v_base: torch.Tensor, strides: tuple[int, int, int], blocks: torch.Tensor,
                   last_fill: int, scale: float, block_size: int, slot_of: torch.Tensor | None = None, out: torch.Tensor | None = None,
                   lse: torch.Tensor | None = None, ws_slot: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
@@ -134,7 +146,8 @@ def hot_attention(query: torch.Tensor, k_base: torch.Tensor, v_base: torch.Tenso
     lse = torch.empty((hq,), dtype=torch.float32, device=dev) if lse is None else lse
     ws = workspace(dev, attention_workspace_bytes(h, hq, d, n), ws_slot)
     s_row, s_head, s_tok = strides
-    call("lkv_hot_attention", ptr(q), hq, h, d, block_size, ptr(k_base), ptr(v_base), dtype_code(k_base.dtype), s_row, s_head, s_tok,
+    n_rows = storage_rows(k_base, v_base, strides, h, block_size, d)
+    call("lkv_hot_attention", ptr(q), hq, h, d, block_size, ptr(k_base), ptr(v_base), dtype_code(k_base.dtype), s_row, s_head, s_tok, n_rows,
          ptr(blocks), n, ptr(slot_of), 0 if slot_of is None else slot_of.stride(0), last_fill, scale, ptr(out), ptr(lse), ptr(ws), ws.numel(),
          stream_handle(dev))
     return out, lse
@@ -204,7 +217,7 @@ def exact_attention(query: torch.Tensor, k_base: torch.Tensor, v_base: torch.Ten
     ws = workspace(dev, int(L.lib().lkv_exact_attention_workspace(h, hq, d, n, n_blocks)), ws_slot)
     s_row, s_head, s_tok = strides
     hot = L.HotSet(ptr(k_base), ptr(v_base), dtype_code(k_base.dtype), s_row, s_head, s_tok, ptr(blocks), n, ptr(slot_of),
-                   0 if slot_of is None else slot_of.stride(0), last_fill)
+                   0 if slot_of is None else slot_of.stride(0), last_fill, storage_rows(k_base, v_base, strides, h, block_size, d))
     kind = L.LKV_COLD_INT8 if cold.dtype == torch.uint8 else L.LKV_COLD_PAIRS
     cs = L.ColdSet(ptr(cold), kind, first_block, n_blocks, ptr(excluded), 0 if excluded is None else excluded.shape[-1])
     po, pl = (None, None) if parts is None else parts

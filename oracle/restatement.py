@@ -277,8 +277,10 @@ def tiered_decode(
     `query` [Hq, d]; `sealed` [n_sealed, h, 2, bs, d] (the host pool's layout, lazykv/tiered.py:265);
     `current` [h, 2, bs, d] with `fill` live tokens. Block 0 (the sink) is always exact
     (lazykv/tiered.py:200-202); sealed blocks 1..n-1 hold `unpack(pack(block))` under int8
-    (lazykv/tiered.py:187-197), in the model dtype where a fetch puts them in a slot and in
-    float32 where the exact pass reads the record; metadata is taken over the dequantised keys.
+    (lazykv/tiered.py:187-197) in the model dtype, in the hot set and in the cold set alike: the
+    exact pass attends to "what a fetch would have produced" (lazykv/exact.py:189-192, the rule its
+    float32 mirror follows for the bf16 tier), so the output does not depend on which blocks were
+    selected beyond float rounding; metadata is taken over the dequantised keys.
     Selected ids are `top_blocks(...) + 1` (lazykv/tiered.py:383-387). The hot set is
     [sink, selected in rank order, current] (lazykv/tiered.py:465-487); the cold set is every
     other sealed block (lazykv/exact.py:371-378). Returns hot/cold partials, the merged output
@@ -293,9 +295,8 @@ def tiered_decode(
         rec = pack(sealed)  # [n, h, W]
         flat = rec.reshape(n * h, -1)
         hot_blocks = unpack(flat, bs, d, model_dtype).reshape(n, h, 2, bs, d)
-        cold_blocks = unpack(flat, bs, d, "float32").reshape(n, h, 2, bs, d)
         hot_blocks[0] = sealed[0]
-        cold_blocks[0] = sealed[0]
+        cold_blocks = hot_blocks
     elif quant is None:
         rec = None
         hot_blocks = cold_blocks = np.asarray(sealed, dtype=F32)

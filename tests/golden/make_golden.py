@@ -161,9 +161,7 @@ def main(ref_root: str) -> None:
     pairs = I.pairs_from_kv(lay["k"], lay["v"], bs)  # [256, 8, 2, 16, 64]
     rec = pack(pairs)  # [256, 8, W]
     deq_bf = unpack(rec.flatten(0, 1), bs, I.D, torch.bfloat16).view(n_sealed, I.HKV, 2, bs, I.D)
-    deq_32 = unpack(rec.flatten(0, 1), bs, I.D, torch.float32).view(n_sealed, I.HKV, 2, bs, I.D)
     deq_bf[0] = pairs[0]  # the sink never leaves VRAM: exact (tiered.py:200-202)
-    deq_32[0] = pairs[0].float()
     keys_meta = deq_bf[:, :, 0].permute(1, 0, 2, 3)  # [h, n, bs, d]
     kmin, kmax = keys_meta.amin(2)[None], keys_meta.amax(2)[None]
     kk = blocks_for_budget(0.25, 4096 + fill, bs)
@@ -177,9 +175,11 @@ def main(ref_root: str) -> None:
     cur[:, 0, :fill] = lay["k"][:, n_sealed * bs :].float()
     cur[:, 1, :fill] = lay["v"][:, n_sealed * bs :].float()
     # Hot: sink + selected (slot contents = bf16 dequantised) + current; laid out as one sequence
-    # and attended with everything else excluded.
+    # and attended with everything else excluded. Cold: the other sealed blocks as a fetch would
+    # produce them (bf16 dequantised), in float32, as the exact pass attends to its mirror
+    # (exact.py:189-192).
     full_hot = torch.cat([deq_bf.float(), cur[None]], dim=0)  # [n+1, h, 2, bs, d]
-    full_cold = torch.cat([deq_32, cur[None]], dim=0)
+    full_cold = full_hot
     kh = full_hot[:, :, 0].permute(1, 0, 2, 3).reshape(I.HKV, -1, I.D)
     vh = full_hot[:, :, 1].permute(1, 0, 2, 3).reshape(I.HKV, -1, I.D)
     kc = full_cold[:, :, 0].permute(1, 0, 2, 3).reshape(I.HKV, -1, I.D)

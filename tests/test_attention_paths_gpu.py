@@ -1,9 +1,11 @@
-"""Both attention kernels (TMA-pipelined and plain-load) and the fused exact call, against the oracle.
+"""The attention kernels (tensor-core, TMA-pipelined and plain-load) and the fused exact call,
+against the oracle.
 
-The TMA kernel serves stores in device memory at G = 4, bs = 16, d in {64, 128}; the plain-load
-kernel serves every other geometry and cold stores in mapped host memory. Every case is compared
-with float64 attention over the same values (1e-5 of the max), and the fused call with the
-separate calls and their merge.
+The tensor-core kernel serves bf16 stores in device memory at d 64, bs 16, G <= 8; the TMA kernel
+the other device-memory cases at G = 4, bs = 16, d in {64, 128}; the plain-load kernel every other
+geometry and cold stores in mapped host memory. Every case is compared with float64 attention over
+the same values (1e-5 of the max; int8 cold blocks as unpack in the model dtype), and the fused call
+with the separate calls and their merge.
 """
 
 from __future__ import annotations
@@ -80,7 +82,7 @@ def test_hot_cold_and_fused_match_float64(d: int, bs: int, dtype: torch.dtype, i
     kvd, qd = kv.to(DEV), q.to(DEV)
     if int8:
         cold = K.pack_int8(kvd)
-        cold_vals = K.unpack_int8(cold.view(-1, cold.shape[-1]), bs, d, torch.float32).view(n, h, 2, bs, d).cpu().numpy()
+        cold_vals = K.unpack_int8(cold.view(-1, cold.shape[-1]), bs, d, dtype).float().view(n, h, 2, bs, d).cpu().numpy()
     else:
         cold = kvd
         cold_vals = kv.float().numpy()
@@ -114,14 +116,16 @@ def test_host_mapped_cold_store_reads_over_the_link() -> None:
     host.copy_(rec.cpu())
     mapped = device_view(host)
     bitmap = _bitmap(sel, n)
+    # Device records go to the tensor-core kernel, mapped ones to the plain-load kernel: the same
+    # values, two summation orders.
     a, al = K.cold_attention(qd, rec, bs, 1, n - 2, d**-0.5, excluded=bitmap)
     b, bl = K.cold_attention(qd, mapped, bs, 1, n - 2, d**-0.5, excluded=bitmap)
-    assert _rel(b.cpu(), a.cpu().numpy()) < 1e-6 and _rel(bl.cpu(), al.cpu().numpy()) < 1e-6
+    assert _rel(b.cpu(), a.cpu().numpy()) < 1e-5 and _rel(bl.cpu(), al.cpu().numpy()) < 1e-6
     blocks = torch.cat([torch.zeros((h, 1), dtype=torch.int32), sel.int(), torch.full((h, 1), n - 1, dtype=torch.int32)], 1).to(DEV)
     strides = (h * 2 * bs * d, 2 * bs * d, d)
     o1, l1 = K.exact_attention(qd, kvd, kvd[:, :, 1], strides, blocks, fill, rec, 1, n - 2, d**-0.5, bs, excluded=bitmap, out_dtype=torch.float32)
     o2, l2 = K.exact_attention(qd, kvd, kvd[:, :, 1], strides, blocks, fill, mapped, 1, n - 2, d**-0.5, bs, excluded=bitmap, out_dtype=torch.float32)
-    assert _rel(o2.cpu(), o1.cpu().numpy()) < 1e-6 and _rel(l2.cpu(), l1.cpu().numpy()) < 1e-6
+    assert _rel(o2.cpu(), o1.cpu().numpy()) < 1e-5 and _rel(l2.cpu(), l1.cpu().numpy()) < 1e-6
 
 
 def test_slot_map_indirection_and_all_excluded_heads() -> None:
@@ -146,3 +150,74 @@ def test_slot_map_indirection_and_all_excluded_heads() -> None:
     assert (c == 0).all() and torch.isneginf(cl).all()
     out, lse = K.exact_attention(qd, kvd, kvd[:, :, 1], strides, blocks, 7, rec, 1, n - 2, d**-0.5, bs, excluded=everything, out_dtype=torch.float32)
     assert torch.allclose(out, a, rtol=1e-6, atol=1e-7) and torch.allclose(lse, al, rtol=1e-6)
+
+
+@pytest.mark.parametrize("g", [1, 2, 4, 8])
+@pytest.mark.parametrize("layout", ["pool", "cache"])
+def test_tensor_core_path_every_group_and_layout(g: int, layout: str) -> None:
+    """bf16, d 64, bs 16: hot blocks through tensor maps over a slot pool [S, h, 2, bs, d] (rows
+    outer) or a full cache [1, h, T, d] (heads outer), int8 and bf16-pairs cold stores, against
+    float64 over the same values; and the same hot call with the row bound withheld (CUDA-core
+    kernels) within float32 rounding of it."""
+    K = _k()
+    h, d, bs, n, k, fill = 8, 64, 16, 160, 24, 11
+    kv, q, sel = _setup(h, g, d, bs, n, k, torch.bfloat16, seed=100 + g)
+    kvd, qd = kv.to(DEV), q.to(DEV)
+    blocks = torch.cat([torch.zeros((h, 1), dtype=torch.int32), sel.int(), torch.full((h, 1), n - 1, dtype=torch.int32)], 1).to(DEV)
+    scale = d**-0.5
+    if layout == "pool":
+        kb, vb = kvd, kvd[:, :, 1]
+        strides = (h * 2 * bs * d, 2 * bs * d, d)
+    else:
+        kb = kvd[:, :, 0].permute(1, 0, 2, 3).reshape(1, h, n * bs, d).contiguous()  # [1, h, T, d]
+        vb = kvd[:, :, 1].permute(1, 0, 2, 3).reshape(1, h, n * bs, d).contiguous()
+        strides = (bs * d, n * bs * d, d)
+    rec = K.pack_int8(kvd)
+    cold_vals = K.unpack_int8(rec.view(-1, rec.shape[-1]), bs, d, torch.bfloat16).float().view(n, h, 2, bs, d).cpu().numpy()
+    want = _oracle_sets(kv, q, sel, fill, cold_vals, scale)
+    hot, hlse = K.hot_attention(qd, kb, vb, strides, blocks, fill, scale, bs)
+    assert _rel(hot.view(h, g, d).cpu(), want[0]) < 1e-5 and _rel(hlse.view(h, g).cpu(), want[1]) < 1e-5
+    bitmap = _bitmap(sel, n)
+    cld, clse = K.cold_attention(qd, rec, bs, 1, n - 2, scale, excluded=bitmap)
+    assert _rel(cld.view(h, g, d).cpu(), want[2]) < 1e-5 and _rel(clse.view(h, g).cpu(), want[3]) < 1e-5
+    out, lse = K.exact_attention(qd, kb, vb, strides, blocks, fill, rec, 1, n - 2, scale, bs, excluded=bitmap, out_dtype=torch.float32)
+    assert _rel(out.view(h, g, d).cpu(), want[4]) < 1e-5 and _rel(lse.view(h, g).cpu(), want[5]) < 1e-5
+    # bf16 pairs as the cold store (the bf16 exact tier)
+    want_p = _oracle_sets(kv, q, sel, fill, kv.float().numpy(), scale)
+    out_p, lse_p = K.exact_attention(qd, kb, vb, strides, blocks, fill, kvd, 1, n - 2, scale, bs, excluded=bitmap, out_dtype=torch.float32)
+    assert _rel(out_p.view(h, g, d).cpu(), want_p[4]) < 1e-5 and _rel(lse_p.view(h, g).cpu(), want_p[5]) < 1e-5
+    # The CUDA-core kernels (row bound withheld) agree to float32 rounding.
+    from lazykv_b200 import _lib as L
+
+    ref_o = torch.empty_like(hot)
+    ref_l = torch.empty_like(hlse)
+    ws = K.workspace(qd.device, K.attention_workspace_bytes(h, h * g, d, blocks.shape[1]))
+    L.call("lkv_hot_attention", L.ptr(qd), h * g, h, d, bs, L.ptr(kb), L.ptr(vb), L.dtype_code(torch.bfloat16), *strides, 0, L.ptr(blocks),
+           blocks.shape[1], None, 0, fill, scale, L.ptr(ref_o), L.ptr(ref_l), L.ptr(ws), ws.numel(), L.stream_handle(qd.device))
+    assert _rel(ref_o.cpu(), hot.cpu().numpy()) < 1e-5 and _rel(ref_l.cpu(), hlse.cpu().numpy()) < 1e-6
+    assert K.device_status() == 0
+
+
+def test_selection_does_not_change_the_exact_int8_result() -> None:
+    """Every sealed block is attended as unpack(record) in bf16 whether it is hot or cold, so two
+    different selections give the same exact output up to float32 rounding."""
+    K = _k()
+    h, g, d, bs, n, k, fill = 8, 4, 64, 16, 200, 30, 9
+    kv, q, _ = _setup(h, g, d, bs, n, k, torch.bfloat16, seed=9)
+    kvd, qd = kv.to(DEV), q.to(DEV)
+    rec = K.pack_int8(kvd)
+    deq = K.unpack_int8(rec.view(-1, rec.shape[-1]), bs, d, torch.bfloat16).view(n, h, 2, bs, d)
+    deq[0] = kvd[0]  # the sink stays exact
+    strides = (h * 2 * bs * d, 2 * bs * d, d)
+    outs = []
+    for seed in (1, 2):
+        gen = torch.Generator().manual_seed(seed)
+        sel = torch.stack([torch.sort(torch.randperm(n - 2, generator=gen)[:k] + 1).values for _ in range(h)])
+        blocks = torch.cat([torch.zeros((h, 1), dtype=torch.int32), sel.int(), torch.full((h, 1), n - 1, dtype=torch.int32)], 1).to(DEV)
+        # The pool holds what a fetch produces: the dequantised blocks (and the exact sink / current).
+        pool = deq.clone()
+        pool[n - 1] = kvd[n - 1]
+        out, lse = K.exact_attention(qd, pool, pool[:, :, 1], strides, blocks, fill, rec, 1, n - 2, d**-0.5, bs, excluded=_bitmap(sel, n),
+                                     out_dtype=torch.float32)
+        outs.append((out.cpu(), lse.cpu()))
+    assert _rel(outs[0][0], outs[1][0].numpy()) < 2e-6 and _rel(outs[0][1], outs[1][1].numpy()) < 1e-6

@@ -171,8 +171,8 @@ def test_exact_tier_refuses_a_prefetch(tiny) -> None:  # noqa: ANN001
 @pytest.mark.parametrize("placement", ["host", "device"])
 def test_int8_exact_step_matches_the_oracle(tiny, placement: str) -> None:  # noqa: ANN001
     """One exact int8 decode step of a tiered layer against the CPU restatement of the composition:
-    sink and current block exact, selected blocks as unpack(record) in bf16, the other sealed
-    blocks dequantised in float32, merged. Float32 output within 1e-5 of the float64 oracle."""
+    sink and current block exact, every other sealed block as unpack(record) in bf16 (selected or
+    not), merged. Float32 output within 1e-5 of the float64 oracle."""
     import oracle
     from lazykv_b200.exact import ExactTieredCache
     from tests.golden.inputs import to_np

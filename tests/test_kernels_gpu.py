@@ -278,3 +278,59 @@ def test_int8_exact_step_matches_the_oracle_composition(fill: int) -> None:
     assert bf16_close(out.float().view(8, 4, 64).cpu().numpy(), r["out"])
     if fill == 9:
         assert _rel(out32.view(8, 4, 64).cpu().numpy(), E["int8_out"]) < 2e-3
+
+
+@pytest.mark.parametrize("n_cand", [1, 7, 100, 511, 513, 2000, 8190, 20000, 65536])
+@pytest.mark.parametrize("bound", ["bf16", "f32"])
+def test_cluster_select_matches_the_sorting_select(n_cand: int, bound: str) -> None:
+    """Ascending-id selection (one thread-block cluster per KV head, scores and radix passes fused)
+    against the single-CTA select with its descending sort: the same set for every k, including
+    ties (coarsely quantised metadata makes many bounds equal) and a first-block offset; and the
+    bitmap marks exactly that set."""
+    k = _k()
+    h, g, d, first = 8, 4, 64, 3
+    gen = torch.Generator(device=DEV).manual_seed(n_cand)
+    dt = torch.bfloat16 if bound == "bf16" else torch.float32
+    base = torch.randn((h, first + n_cand, d), generator=gen, device=DEV)
+    base = (base * 2).round() / 2  # coarse values: many exactly tied bounds
+    kmin = (base - 0.5).to(dt)
+    kmax = (base + 0.5).to(dt)
+    q = torch.randn((h * g, d), generator=gen, device=DEV).to(dt)
+    words = k.bitmap_words(first + n_cand + 1)
+    if n_cand > 16384:  # beyond the sorting select's capacity: k = n_cand must return every id
+        got, _ = k.quest_topk(q, kmin, kmax, first, n_cand, n_cand, by_block=True)
+        assert np.array_equal(got.cpu().numpy(), np.tile(np.arange(first, first + n_cand), (h, 1)))
+    for kk in sorted({1, max(1, n_cand // 4), max(1, n_cand - 1), n_cand} & set(range(1, 16385))):
+        ref, _ = k.quest_topk(q, kmin, kmax, first, n_cand, kk)
+        bm = torch.full((h, words), -1, dtype=torch.int32, device=DEV)
+        got, _ = k.quest_topk(q, kmin, kmax, first, n_cand, kk, bitmap=bm, by_block=True)
+        want = np.sort(ref.cpu().numpy(), axis=1)
+        assert np.array_equal(got.cpu().numpy(), want), (kk, n_cand)
+        bits = np.unpackbits(bm.cpu().numpy().view(np.uint8), bitorder="little").reshape(h, -1)
+        for j in range(h):
+            assert np.array_equal(np.nonzero(bits[j])[0], want[j])
+    assert k.device_status() == 0
+
+
+@pytest.mark.parametrize("d", [16, 32, 64, 128])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("order", ["bound", "block"])
+def test_bounds_and_selection_every_head_dim(d: int, dt: torch.dtype, order: str) -> None:
+    """The scoring kernels stage metadata rows of d channels in shared memory (rotated 16-byte
+    chunks); every head_dim the ABI takes, bounds bit-exact with the oracle and the selected set the
+    oracle's, through both selects."""
+    k = _k()
+    h, g, n, kk = 4, 4, 300, 37
+    gen = torch.Generator(device=DEV).manual_seed(d)
+    kmin = torch.randn((h, n + 1, d), generator=gen, device=DEV).to(dt)
+    kmax = (kmin.float() + torch.rand((h, n + 1, d), generator=gen, device=DEV)).to(dt)
+    q = torch.randn((h * g, d), generator=gen, device=DEV).to(dt)
+    mode = "bfloat16" if dt == torch.bfloat16 else "float32"
+    want_bound = O.quest_bound(I.to_np(q), I.to_np(kmin[:, 1:]), I.to_np(kmax[:, 1:]), mode)
+    idx, bound = k.quest_topk(q, kmin, kmax, 1, n, kk, want_bound=True, by_block=order == "block")
+    assert np.array_equal(bound.cpu().numpy(), want_bound.astype(np.float32))  # exact (+0 and -0 compare equal)
+    want = O.top_blocks(want_bound, kk) + 1
+    got = idx.cpu().numpy()
+    assert np.array_equal(np.sort(got, 1), np.sort(want, 1))
+    if order == "bound":
+        assert np.array_equal(got, want)

@@ -55,7 +55,7 @@ def test_invalid_arguments_return_a_status_and_a_message(lib) -> None:  # noqa: 
     assert rc == 1 and "do not group" in _lib.last_error()
     rc = lib.lkv_pack_int8(None, 1, 1, 8, 12, 64, None, None, None, 0, 0, None, None)
     assert rc == 1 and "geometry" in _lib.last_error()
-    rc = lib.lkv_hot_attention(None, 32, 8, 64, 16, None, None, 1, 0, 0, 0, None, 4, None, 0, 0, 0.125, None, None, None, 0, None)
+    rc = lib.lkv_hot_attention(None, 32, 8, 64, 16, None, None, 1, 0, 0, 0, 0, None, 4, None, 0, 0, 0.125, None, None, None, 0, None)
     assert rc == 2 and "null" in _lib.last_error()
     rc = lib.lkv_lse_merge(None, None, 0, 4, 64, None, 0, None, None)
     assert rc == 1
