@@ -54,6 +54,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--cold", choices=["device", "host"], default="device")
     p.add_argument("--no-host-leg", action="store_true", help="skip the zero-copy (host cold tier) measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--layers", type=int, default=N_LAYERS - DENSE, help="selecting layers (the metric runs all 14; fewer for profiling)")
     return p.parse_args()
 
 
@@ -149,7 +150,7 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev) -> tuple[
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     layers = []
     torch.cuda.synchronize(dev)
-    for li in range(N_LAYERS - DENSE):
+    for li in range(args.layers):
         L = Layer()
         nblk = hi - lo
         off = torch.randn(HKV, 1, D, device=dev, generator=g) * 0.5**0.5
@@ -216,7 +217,7 @@ def layer_step(L, geo: dict, cold_store=None, events: list | None = None) -> Non
     mark()
 
 
-LAUNCHES_PER_LAYER_STEP = 4  # score + select, attention partial (hot and cold chunks) + combine
+LAUNCHES_PER_LAYER_STEP = 3  # fused score + top-K (one cluster launch), attention partials (hot and cold) + combine
 
 
 def run_ours(args: argparse.Namespace) -> None:
@@ -293,7 +294,7 @@ def run_ours(args: argparse.Namespace) -> None:
     with Clocks(local) as clocks:
         ms = timed(graph.replay if graph is not None else step, n_steps)
     ms_step = ms / n_steps
-    n_sel = N_LAYERS - DENSE
+    n_sel = args.layers
     us_layer = ms_step * 1e3 / n_sel
     tokens_per_s = 1e3 / ms_step
 
@@ -463,7 +464,7 @@ def cpu_baseline(args: argparse.Namespace, budget_s: float = 12.0) -> dict:
         cpu_layer_step(x, k)
         times.append(time.perf_counter() - t0)
     per_layer = statistics.median(times)
-    n_sel = N_LAYERS - DENSE
+    n_sel = args.layers
     return {"value": round(1.0 / (per_layer * n_sel), 4), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
             "sample": f"{len(times)} layer-steps of one selecting layer at {args.ctx} tokens (numpy port of the reference's CPU path: bf16 bound + top-K, two float32 partial attentions over the full mirror, LSE merge); tokens/s = 1 / (14 x median layer-step); BLAS multithreaded, elementwise single-threaded",
             "us_per_layer_step": round(per_layer * 1e6, 1)}
@@ -488,7 +489,7 @@ def run_reference(args: argparse.Namespace) -> None:
         cpu_layer_step(x, k)
         times.append(time.perf_counter() - t0)
     per_layer = statistics.median(times)
-    n_sel = N_LAYERS - DENSE
+    n_sel = args.layers
     value = 1.0 / (per_layer * n_sel)
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tokens/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),

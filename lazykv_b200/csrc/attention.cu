@@ -750,15 +750,17 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
 
 constexpr int kMmaWarps = 4;
 constexpr int kMmaThreads = 32 * kMmaWarps;
-constexpr int kMmaStages = 3;
+constexpr int kMmaStages = 2;
 constexpr int kMmaTile = 2048;                  // 16 x 64 bf16, swizzled
 constexpr int kMmaHotStage = 2 * kMmaTile;      // K tile + V tile
 constexpr int kMmaRec = 2368;                   // int8 record at bs 16, d 64
 constexpr int kMmaRecStage = 2432;              // record stage stride (a multiple of 128 bytes)
-constexpr int kMmaCtasPerSm = 4;
+constexpr int kMmaCtasPerSm = 6;
 constexpr int kMmaTargetCtas = kMmaCtasPerSm * kNumSMs;
-constexpr int kMmaBody = kMmaWarps * kMmaStages * kMmaHotStage;  // 48 KiB: hot stages, or cold tiles + raw stages
-static_assert(kMmaWarps * 2 * kMmaTile + kMmaWarps * kMmaStages * kMmaRecStage <= kMmaBody, "cold layout exceeds the body");
+constexpr int kMmaHotBody = kMmaWarps * kMmaStages * kMmaHotStage;                            // hot / pairs stages
+constexpr int kMmaColdBody = kMmaWarps * 2 * kMmaTile + kMmaWarps * kMmaStages * kMmaRecStage;  // tiles + record stages
+constexpr int kMmaBody = kMmaHotBody > kMmaColdBody ? kMmaHotBody : kMmaColdBody;
+static_assert(kMmaBody >= kMmaWarps * 8 * 64 * 4 + kMmaWarps * 2 * 8 * 4, "epilogue scratch exceeds the body");
 constexpr size_t kMmaSmem = 1024 + kMmaBody + kMmaWarps * kMmaStages * 8;
 
 struct MmaParams {
@@ -791,6 +793,14 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
   asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
                : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 2^x by the hardware approximation (PTX ex2.approx.ftz.f32: relative error about 2^-22, subnormal
+// results flushed to zero; 2^-inf = 0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ uint32_t movtrans(uint32_t x) {
@@ -828,10 +838,15 @@ __device__ __forceinline__ void codes8(uint2 w, float2 (&u)[4]) {
 __device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
 
 // Dequantises the int8 record at `raw` (kq | vq | k_scale | k_zero | v_scale | v_zero, bs 16, d 64)
-// into bf16 K and V tiles in the swizzled layout. Lane: channel group lane & 7 (8 channels), tokens
-// (lane >> 3) + 4i.
+// into bf16 K and V tiles in the swizzled layout. Lane: channel group gq = lane & 7 (8 channels),
+// tokens 4 * (lane >> 3) + i, i = 0..3. Each value is (code + 128) * scale + zero in float32 (one
+// rounding, as quant.py's unpack), then rounded to bf16.
 __device__ __forceinline__ void dequant_record(const unsigned char* raw, unsigned char* kt, unsigned char* vt, int lane) {
-  const int gq = lane & 7, tb = lane >> 3;
+  const int gq = lane & 7, t0 = 4 * (lane >> 3);
+  // Swizzled chunk offsets of tokens t0 + i: t0 & 7 is 0 or 4, so (t & 7) = (t0 & 7) + i.
+  uint32_t dst[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = (uint32_t)((t0 + i) * 128 + ((gq ^ ((t0 & 7) + i)) << 4));
   float2 ks2[4], kz2[4];
   {
     const uint4 a = *reinterpret_cast<const uint4*>(raw + 2048 + 16 * gq);
@@ -845,9 +860,8 @@ __device__ __forceinline__ void dequant_record(const unsigned char* raw, unsigne
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int t = tb + 4 * i;
     float2 u[4];
-    codes8(*reinterpret_cast<const uint2*>(raw + t * 64 + 8 * gq), u);
+    codes8(*reinterpret_cast<const uint2*>(raw + (t0 + i) * 64 + 8 * gq), u);
     float2 k[4];
 #pragma unroll
     for (int x = 0; x < 4; ++x) k[x] = __ffma2_rn(u[x], ks2[x], kz2[x]);
@@ -856,16 +870,19 @@ __device__ __forceinline__ void dequant_record(const unsigned char* raw, unsigne
     o.y = pack_bf2(k[1].x, k[1].y);
     o.z = pack_bf2(k[2].x, k[2].y);
     o.w = pack_bf2(k[3].x, k[3].y);
-    *reinterpret_cast<uint4*>(kt + swz(t, gq)) = o;
+    *reinterpret_cast<uint4*>(kt + dst[i]) = o;
   }
-  const __half* vsc = reinterpret_cast<const __half*>(raw + 2304);
+  // Per-token V scales of tokens t0..t0+3: four f16 each, one 8-byte load.
+  const uint2 vsw = *reinterpret_cast<const uint2*>(raw + 2304 + 2 * t0);
+  const uint2 vzw = *reinterpret_cast<const uint2*>(raw + 2336 + 2 * t0);
+  const float2 vs01 = __half22float2(*reinterpret_cast<const __half2*>(&vsw.x)), vs23 = __half22float2(*reinterpret_cast<const __half2*>(&vsw.y));
+  const float2 vz01 = __half22float2(*reinterpret_cast<const __half2*>(&vzw.x)), vz23 = __half22float2(*reinterpret_cast<const __half2*>(&vzw.y));
+  const float vs[4] = {vs01.x, vs01.y, vs23.x, vs23.y}, vz[4] = {vz01.x, vz01.y, vz23.x, vz23.y};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int t = tb + 4 * i;
-    const float vs = __half2float(vsc[t]), vz = __half2float(vsc[16 + t]);
-    const float2 vs2 = f2(vs, vs), vz2 = f2(vz, vz);
+    const float2 vs2 = f2(vs[i], vs[i]), vz2 = f2(vz[i], vz[i]);
     float2 u[4];
-    codes8(*reinterpret_cast<const uint2*>(raw + 1024 + t * 64 + 8 * gq), u);
+    codes8(*reinterpret_cast<const uint2*>(raw + 1024 + (t0 + i) * 64 + 8 * gq), u);
     float2 v[4];
 #pragma unroll
     for (int x = 0; x < 4; ++x) v[x] = __ffma2_rn(u[x], vs2, vz2);
@@ -874,7 +891,7 @@ __device__ __forceinline__ void dequant_record(const unsigned char* raw, unsigne
     o.y = pack_bf2(v[1].x, v[1].y);
     o.z = pack_bf2(v[2].x, v[2].y);
     o.w = pack_bf2(v[3].x, v[3].y);
-    *reinterpret_cast<uint4*>(vt + swz(t, gq)) = o;
+    *reinterpret_cast<uint4*>(vt + dst[i]) = o;
   }
 }
 
@@ -1083,10 +1100,10 @@ __global__ void __launch_bounds__(kMmaThreads, kMmaCtasPerSm) attn_mma_kernel(co
         m1 = mb1;
       }
     }
-    const float p0 = m0 == -INFINITY ? 0.0f : exp2f(x0 - m0);
-    const float p2 = m0 == -INFINITY ? 0.0f : exp2f(x2 - m0);
-    const float p1 = m1 == -INFINITY ? 0.0f : exp2f(x1 - m1);
-    const float p3 = m1 == -INFINITY ? 0.0f : exp2f(x3 - m1);
+    const float p0 = m0 == -INFINITY ? 0.0f : ex2(x0 - m0);
+    const float p2 = m0 == -INFINITY ? 0.0f : ex2(x2 - m0);
+    const float p1 = m1 == -INFINITY ? 0.0f : ex2(x1 - m1);
+    const float p3 = m1 == -INFINITY ? 0.0f : ex2(x3 - m1);
     l0 += p0 + p2;
     l1 += p1 + p3;
     // ---- P^T operand: three bf16 terms, transposed into the B layout ----
@@ -1430,9 +1447,11 @@ int fill_cold(const char* who, Seg& S, int h, int d, int bs, int dtype, const lk
 }
 
 // Split the target CTA count between two segments in proportion to their bytes.
-void split_two(Seg& hot, Seg& cold, int h, int hot_item_bytes, int cold_item_bytes, int total_ctas) {
+// hot_item / cold_item: the cost of one item of each segment (bytes for the CUDA-core kernels, time
+// for the tensor-core one). Each segment gets at least one CTA; the total stays within total_ctas + 1.
+void split_two(Seg& hot, Seg& cold, int h, double hot_item, double cold_item, int total_ctas) {
   const int target = (total_ctas + h - 1) / h;
-  const double wh = (double)hot.n_items * hot_item_bytes, wc = (double)cold.n_items * cold_item_bytes;
+  const double wh = (double)hot.n_items * hot_item, wc = (double)cold.n_items * cold_item;
   int th = wh + wc > 0 ? (int)(target * wh / (wh + wc) + 0.5) : 0;
   if (hot.n_items > 0 && th < 1) th = 1;
   int tc = target - th;
@@ -1524,7 +1543,16 @@ int run_attention(const char* who, AttnParams& p, int g, int d, TO* out, float* 
     set_split(p.seg[0], (total + p.h - 1) / p.h);
     p.n_splits_total = p.seg[0].n_splits;
   } else {
-    split_two(p.seg[0], p.seg[1], p.h, 4096, 2368, total);
+    if (mma) {
+      // Tensor-core costs per item, relative: a listed block 1; a cold record about 2.5 (the fused
+      // dequantisation), of which the range's excluded blocks (about the listed ones) cost little.
+      const double n_cold = p.seg[1].n_items > 0 ? p.seg[1].n_items : 1;
+      const double live = fmax(0.0, n_cold - fmax(0.0, p.seg[0].n_items - 2.0)) / n_cold;
+      const double cold_cost = p.seg[1].kind == SEG_RANGE_REC ? 2.5 : 1.0;
+      split_two(p.seg[0], p.seg[1], p.h, 1.0, cold_cost * live + 0.05, total);
+    } else {
+      split_two(p.seg[0], p.seg[1], p.h, 4096, 2368, total);
+    }
     p.n_splits_total = p.seg[0].n_splits + p.seg[1].n_splits;
   }
   const size_t need = partial_bytes(p.h, g, d, p.n_splits_total);
@@ -1585,7 +1613,8 @@ size_t lkv_exact_attention_workspace(int h, int hq, int d, int n_list, int n_blo
   a.n_items = n_list;
   b.n_items = n_blocks;
   split_two(a, b, h, 4096, 2368, kMmaTargetCtas);
-  const size_t s = partial_bytes(h, hq / h, d, a.n_splits + b.n_splits);
+  const int per_head = (kMmaTargetCtas + h - 1) / h + 1;  // any split of the target between the segments
+  const size_t s = partial_bytes(h, hq / h, d, per_head > a.n_splits + b.n_splits ? per_head : a.n_splits + b.n_splits);
   return s > 0 ? s : 16;
 }
 

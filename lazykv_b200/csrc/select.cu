@@ -45,46 +45,78 @@ __device__ __forceinline__ int tile_pos(int t, int c, int chunks, int row_bytes)
   return t * row_bytes + cc * 16;
 }
 
-template <typename TQ, typename TM, int G>
-__global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin, const TM* __restrict__ kmax,
-                                   int64_t m_head, int first_block, int n_cand, int bound_mode, uint64_t* __restrict__ keys,
-                                   float* __restrict__ out_bound) {
-  extern __shared__ __align__(16) float qs[];  // qp [G][d], qn [G][d], then the two tiles
-  const int rows = blockDim.x;
-  const int row_bytes = d * (int)sizeof(TM);
-  const int chunks = row_bytes / 16;
-  unsigned char* tile_max = reinterpret_cast<unsigned char*>(qs + 2 * G * d);
-  unsigned char* tile_min = tile_max + (size_t)rows * row_bytes;
-  const int j = blockIdx.y;
-  const int c_first = blockIdx.x * rows;
-  const int n_rows = min(rows, n_cand - c_first);
-  for (int e = threadIdx.x; e < G * d; e += blockDim.x) {
-    const float v = to_f32<TQ>(q[(int64_t)j * G * d + e]);
+// Query staging for the scoring kernels: q+ and q- transposed to [channel][row] with the rows
+// padded to an even count GP, so one channel's rows are adjacent and pair up in float32x2 ops.
+template <int G>
+constexpr int qpad() { return G < 2 ? 2 : G; }
+
+template <typename TQ, int G>
+__device__ __forceinline__ void stage_query(const TQ* q, int j, int d, float* qs) {
+  constexpr int GP = qpad<G>();
+  for (int e = threadIdx.x; e < GP * d; e += blockDim.x) {
+    const int c = e / GP, r = e % GP;
+    const float v = r < G ? to_f32<TQ>(q[(int64_t)j * G * d + (int64_t)r * d + c]) : 0.0f;
     const float vp = fmaxf(v, 0.0f);   // q.clamp_min(0)
     qs[e] = vp;
-    qs[G * d + e] = __fsub_rn(v, vp);  // q - qp
+    qs[GP * d + e] = __fsub_rn(v, vp);  // q - qp
   }
-  const unsigned char* gmax = reinterpret_cast<const unsigned char*>(kmax + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
-  const unsigned char* gmin = reinterpret_cast<const unsigned char*>(kmin + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
-  for (int u = threadIdx.x; u < n_rows * chunks; u += blockDim.x) {
-    const int t = u / chunks, c = u % chunks;
-    const int pos = tile_pos(t, c, chunks, row_bytes);
-    cp_async16(tile_max + pos, reinterpret_cast<const uint4*>(gmax) + u);
-    cp_async16(tile_min + pos, reinterpret_cast<const uint4*>(gmin) + u);
+}
+
+// The bound of tile row t, in the channel order and with the roundings of the header comment.
+// When the query and the metadata are both bf16 every product is exact in float32 (8 x 8 significant
+// bits), so a fused multiply-add rounds exactly as the separate product and add do, and the rows
+// pair up in float32x2 FMAs. Otherwise products round, and separate scalar multiplies and adds are
+// used (a float32x2 multiply followed by a float32x2 add was measured to give fused results on this
+// toolchain, which that order rules out).
+template <typename TQ, typename TM, int G>
+__device__ __forceinline__ float row_bound(const unsigned char* tile_max, const unsigned char* tile_min, int t, int d, const float* qs,
+                                           int bound_mode) {
+  constexpr int GP = qpad<G>();
+  if constexpr (sizeof(TQ) == 2 && sizeof(TM) == 2) {
+    constexpr int NP = GP / 2;
+    const int chunks = d / 8;
+    float2 a[NP], b[NP];
+#pragma unroll
+    for (int r = 0; r < NP; ++r) a[r] = b[r] = make_float2(0.0f, 0.0f);
+    const float2* qp = reinterpret_cast<const float2*>(qs);
+    const float2* qn = reinterpret_cast<const float2*>(qs + GP * d);
+    for (int c = 0; c < chunks; ++c) {
+      const int pos = tile_pos(t, c, chunks, d * 2);
+      const uint4 x = *reinterpret_cast<const uint4*>(tile_max + pos), y = *reinterpret_cast<const uint4*>(tile_min + pos);
+      const uint32_t wx[4] = {x.x, x.y, x.z, x.w}, wy[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float mx = __uint_as_float((i & 1) ? (wx[i / 2] & 0xffff0000u) : (wx[i / 2] << 16));
+        const float mn = __uint_as_float((i & 1) ? (wy[i / 2] & 0xffff0000u) : (wy[i / 2] << 16));
+        const float2 x2 = make_float2(mx, mx), n2 = make_float2(mn, mn);
+#pragma unroll
+        for (int r = 0; r < NP; ++r) {
+          a[r] = __ffma2_rn(qp[(c * 8 + i) * NP + r], x2, a[r]);
+          b[r] = __ffma2_rn(qn[(c * 8 + i) * NP + r], n2, b[r]);
+        }
+      }
+    }
+    float best = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < G; ++r) {
+      const float ar = (r & 1) ? a[r / 2].y : a[r / 2].x, br = (r & 1) ? b[r / 2].y : b[r / 2].x;
+      const float sc = bound_mode == LKV_BF16 ? bf16_round(__fadd_rn(bf16_round(ar), bf16_round(br))) : __fadd_rn(ar, br);
+      best = fmaxf(best, sc);
+    }
+    return best;
   }
-  cp_async_wait_all();
-  __syncthreads();
-  const int t = threadIdx.x;
-  if (t >= n_rows) return;
+  const int row_bytes = d * (int)sizeof(TM);
+  const int chunks = row_bytes / 16;
   float a[G], b[G];
 #pragma unroll
   for (int r = 0; r < G; ++r) a[r] = b[r] = 0.0f;
-  constexpr int PER = 16 / (int)sizeof(TM);  // elements per 16-byte chunk
+  constexpr int PER = 16 / (int)sizeof(TM);
+  const float* qp = qs;
+  const float* qn = qs + GP * d;
   for (int c = 0; c < chunks; ++c) {
     const int pos = tile_pos(t, c, chunks, row_bytes);
     float mx[8], mn[8];
     if constexpr (PER == 8) {
-      // Plain shared-memory loads (the read-only global path cannot address shared memory).
       const uint4 x = *reinterpret_cast<const uint4*>(tile_max + pos), y = *reinterpret_cast<const uint4*>(tile_min + pos);
       const uint32_t wx[4] = {x.x, x.y, x.z, x.w}, wy[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
@@ -104,17 +136,47 @@ __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __
     for (int i = 0; i < PER; ++i) {
 #pragma unroll
       for (int r = 0; r < G; ++r) {
-        a[r] = __fadd_rn(a[r], __fmul_rn(qs[r * d + c0 + i], mx[i]));
-        b[r] = __fadd_rn(b[r], __fmul_rn(qs[G * d + r * d + c0 + i], mn[i]));
+        a[r] = __fadd_rn(a[r], __fmul_rn(qp[(c0 + i) * GP + r], mx[i]));
+        b[r] = __fadd_rn(b[r], __fmul_rn(qn[(c0 + i) * GP + r], mn[i]));
       }
     }
   }
   float best = -INFINITY;
 #pragma unroll
   for (int r = 0; r < G; ++r) {
-    float sc = bound_mode == LKV_BF16 ? bf16_round(__fadd_rn(bf16_round(a[r]), bf16_round(b[r]))) : __fadd_rn(a[r], b[r]);
+    const float sc = bound_mode == LKV_BF16 ? bf16_round(__fadd_rn(bf16_round(a[r]), bf16_round(b[r]))) : __fadd_rn(a[r], b[r]);
     best = fmaxf(best, sc);
   }
+  return best;
+}
+
+template <typename TQ, typename TM, int G>
+__global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin, const TM* __restrict__ kmax,
+                                   int64_t m_head, int first_block, int n_cand, int bound_mode, uint64_t* __restrict__ keys,
+                                   float* __restrict__ out_bound) {
+  extern __shared__ __align__(16) float qs[];  // q+ [d][GP], q- [d][GP], then the two tiles
+  const int rows = blockDim.x;
+  const int row_bytes = d * (int)sizeof(TM);
+  const int chunks = row_bytes / 16;
+  unsigned char* tile_max = reinterpret_cast<unsigned char*>(qs + 2 * qpad<G>() * d);
+  unsigned char* tile_min = tile_max + (size_t)rows * row_bytes;
+  const int j = blockIdx.y;
+  const int c_first = blockIdx.x * rows;
+  const int n_rows = min(rows, n_cand - c_first);
+  stage_query<TQ, G>(q, j, d, qs);
+  const unsigned char* gmax = reinterpret_cast<const unsigned char*>(kmax + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
+  const unsigned char* gmin = reinterpret_cast<const unsigned char*>(kmin + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
+  for (int u = threadIdx.x; u < n_rows * chunks; u += blockDim.x) {
+    const int t = u / chunks, c = u % chunks;
+    const int pos = tile_pos(t, c, chunks, row_bytes);
+    cp_async16(tile_max + pos, reinterpret_cast<const uint4*>(gmax) + u);
+    cp_async16(tile_min + pos, reinterpret_cast<const uint4*>(gmin) + u);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t >= n_rows) return;
+  const float best = row_bound<TQ, TM, G>(tile_max, tile_min, t, d, qs, bound_mode);
   const int ci = c_first + t;
   const uint64_t key = ((uint64_t)orderable(best) << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
   keys[(int64_t)j * n_cand + ci] = key;
@@ -318,52 +380,6 @@ constexpr int kClusterThreads = 256;
 constexpr int kClusterMax = 16;
 constexpr int kClusterMaxPer = 4096;  // candidates per CTA (their keys stay in shared memory)
 
-template <typename TM, int G>
-__device__ __forceinline__ float row_bound(const unsigned char* tile_max, const unsigned char* tile_min, int t, int d, const float* qs,
-                                           int bound_mode) {
-  const int row_bytes = d * (int)sizeof(TM);
-  const int chunks = row_bytes / 16;
-  float a[G], b[G];
-#pragma unroll
-  for (int r = 0; r < G; ++r) a[r] = b[r] = 0.0f;
-  constexpr int PER = 16 / (int)sizeof(TM);
-  for (int c = 0; c < chunks; ++c) {
-    const int pos = tile_pos(t, c, chunks, row_bytes);
-    float mx[8], mn[8];
-    if constexpr (PER == 8) {
-      const uint4 x = *reinterpret_cast<const uint4*>(tile_max + pos), y = *reinterpret_cast<const uint4*>(tile_min + pos);
-      const uint32_t wx[4] = {x.x, x.y, x.z, x.w}, wy[4] = {y.x, y.y, y.z, y.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        mx[2 * i] = __uint_as_float(wx[i] << 16);
-        mx[2 * i + 1] = __uint_as_float(wx[i] & 0xffff0000u);
-        mn[2 * i] = __uint_as_float(wy[i] << 16);
-        mn[2 * i + 1] = __uint_as_float(wy[i] & 0xffff0000u);
-      }
-    } else {
-      const float4 x = *reinterpret_cast<const float4*>(tile_max + pos), y = *reinterpret_cast<const float4*>(tile_min + pos);
-      mx[0] = x.x; mx[1] = x.y; mx[2] = x.z; mx[3] = x.w;
-      mn[0] = y.x; mn[1] = y.y; mn[2] = y.z; mn[3] = y.w;
-    }
-    const int c0 = c * PER;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-#pragma unroll
-      for (int r = 0; r < G; ++r) {
-        a[r] = __fadd_rn(a[r], __fmul_rn(qs[r * d + c0 + i], mx[i]));
-        b[r] = __fadd_rn(b[r], __fmul_rn(qs[G * d + r * d + c0 + i], mn[i]));
-      }
-    }
-  }
-  float best = -INFINITY;
-#pragma unroll
-  for (int r = 0; r < G; ++r) {
-    const float sc = bound_mode == LKV_BF16 ? bf16_round(__fadd_rn(bf16_round(a[r]), bf16_round(b[r]))) : __fadd_rn(a[r], b[r]);
-    best = fmaxf(best, sc);
-  }
-  return best;
-}
-
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -374,16 +390,18 @@ template <typename TQ, typename TM, int G>
 __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin,
                                                                                 const TM* __restrict__ kmax, int64_t m_head, int first_block,
                                                                                 int n_cand, int k, int bound_mode, int n_passes, int per, int rows,
-                                                                                int32_t* __restrict__ out_blocks, int out_ld,
+                                                                                int n_bufs, int32_t* __restrict__ out_blocks, int out_ld,
                                                                                 float* __restrict__ out_bound, uint32_t* __restrict__ bitmap,
                                                                                 int bitmap_words) {
   cg::cluster_group cluster = cg::this_cluster();
   const int c = (int)cluster.block_rank();
+  const int C = (int)cluster.num_blocks();  // a power of two <= 16
   const int j = blockIdx.y;
   const int tid = threadIdx.x;
   extern __shared__ __align__(16) unsigned char sm[];
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t ghist[4][256];         // rank 0: cluster totals, one array per pass
+  __shared__ uint32_t hist[256];             // this CTA's digit counts
+  __shared__ uint32_t red[256];              // rank c: totals of its share of the bins
+  __shared__ uint32_t ghist[256];            // the cluster totals of the current pass
   __shared__ uint32_t table[kClusterMax][2];  // rank 0: per-CTA (above, equal) counts
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total, sh_pos0, sh_eq0;
@@ -391,28 +409,20 @@ __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kerne
   const int row_bytes = d * (int)sizeof(TM);
   const int chunks = row_bytes / 16;
   const size_t buf_bytes = (size_t)rows * row_bytes * 2;
-  unsigned char* bufs = sm + (size_t)2 * G * d * sizeof(float);
-  uint64_t* keys = reinterpret_cast<uint64_t*>(bufs + 2 * buf_bytes);
+  unsigned char* bufs = sm + (size_t)2 * qpad<G>() * d * sizeof(float);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(bufs + n_bufs * buf_bytes);
 
   const int lo = min(n_cand, c * per);
   const int hi = min(n_cand, lo + per);
   const int cnt = hi - lo;
-  if (c == 0) {
-    for (int i = tid; i < 4 * 256; i += blockDim.x) (&ghist[0][0])[i] = 0u;
-    if (bitmap != nullptr)
-      for (int w = tid; w < bitmap_words; w += blockDim.x) bitmap[(int64_t)j * bitmap_words + w] = 0u;
-  }
-  for (int e = tid; e < G * d; e += blockDim.x) {
-    const float v = to_f32<TQ>(q[(int64_t)j * G * d + e]);
-    const float vp = fmaxf(v, 0.0f);
-    qs[e] = vp;
-    qs[G * d + e] = __fsub_rn(v, vp);
-  }
+  if (c == 0 && bitmap != nullptr)
+    for (int w = tid; w < bitmap_words; w += blockDim.x) bitmap[(int64_t)j * bitmap_words + w] = 0u;
+  stage_query<TQ, G>(q, j, d, qs);
 
-  // ---- scores of the slice, in sub-tiles of `rows` candidates, double-buffered ----
+  // ---- scores of the slice, in sub-tiles of `rows` candidates (double-buffered when n_bufs = 2) ----
   const int n_sub = (cnt + rows - 1) / rows;
   auto load = [&](int sub) {
-    unsigned char* tmax = bufs + (size_t)(sub & 1) * buf_bytes;
+    unsigned char* tmax = bufs + (size_t)(sub % n_bufs) * buf_bytes;
     unsigned char* tmin = tmax + (size_t)rows * row_bytes;
     const int base = lo + sub * rows;
     const int nr = min(rows, hi - base);
@@ -427,40 +437,42 @@ __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kerne
     cp_async_commit();
   };
   if (n_sub > 0) load(0);
-  __syncthreads();  // q split visible
   for (int sub = 0; sub < n_sub; ++sub) {
-    if (sub + 1 < n_sub) {
+    if (n_bufs == 2 && sub + 1 < n_sub) {
       load(sub + 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();
+    __syncthreads();  // the tile (and, the first time, the staged query) is visible
     const int base = lo + sub * rows;
     const int nr = min(rows, hi - base);
     if (tid < nr) {
-      const unsigned char* tmax = bufs + (size_t)(sub & 1) * buf_bytes;
-      const float best = row_bound<TM, G>(tmax, tmax + (size_t)rows * row_bytes, tid, d, qs, bound_mode);
+      const unsigned char* tmax = bufs + (size_t)(sub % n_bufs) * buf_bytes;
+      const float best = row_bound<TQ, TM, G>(tmax, tmax + (size_t)rows * row_bytes, tid, d, qs, bound_mode);
       const int ci = base + tid;
       keys[ci - lo] = ((uint64_t)orderable(best) << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
       if (out_bound != nullptr) out_bound[(int64_t)j * n_cand + ci] = best == 0.0f ? 0.0f : best;
     }
     __syncthreads();  // the buffer is read before it is refilled
+    if (n_bufs == 1 && sub + 1 < n_sub) load(sub + 1);
   }
-  cluster.sync();  // every slice scored; rank 0's totals and the bitmap row are zero
 
   // ---- cluster-wide radix select of the k-th key ----
-  uint32_t* g0 = cluster.map_shared_rank(&ghist[0][0], 0);
   const int kk = k < n_cand ? k : n_cand;
   if (tid == 0) {
     sh_remaining = (uint32_t)kk;
     sh_bincount = 0;
   }
+  const int bpc = 256 / C;  // bins each rank totals
   uint32_t prefix = 0, mask = 0;
   bool take_all = kk >= n_cand;
   for (int pass = 0; pass < n_passes && !take_all; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    for (int i = tid; i < 256; i += blockDim.x) {
+      hist[i] = 0;
+      red[i] = 0;
+    }
     __syncthreads();
     for (int i0 = 0; i0 < cnt; i0 += blockDim.x) {
       const int i = i0 + tid;
@@ -470,13 +482,21 @@ __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kerne
       const uint32_t peers = __match_any_sync(0xffffffffu, digit);
       if (counted && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
     }
+    cluster.sync();  // every rank's counts are final
+    // Reduce-scatter: rank c totals bins [c * bpc, (c + 1) * bpc) over the C ranks ...
+    for (int u = tid; u < 256; u += blockDim.x) {
+      const int src = u / bpc, bin = c * bpc + u % bpc;
+      const uint32_t v = *cluster.map_shared_rank(&hist[bin], src);
+      if (v) atomicAdd(&red[u % bpc], v);
+    }
     __syncthreads();
-    for (int b = tid; b < 256; b += blockDim.x)
-      if (hist[b]) atomicAdd(&g0[pass * 256 + b], hist[b]);
+    // ... and all-gather: it writes those totals into every rank's ghist.
+    for (int u = tid; u < 256; u += blockDim.x) {
+      const int dst = u / bpc, bin = c * bpc + u % bpc;
+      *cluster.map_shared_rank(&ghist[bin], dst) = red[u % bpc];
+    }
     cluster.sync();
-    for (int b = tid; b < 256; b += blockDim.x) hist[b] = g0[pass * 256 + b];
-    __syncthreads();
-    pick_digit(hist, &sh_digit, &sh_remaining, &sh_bincount);
+    pick_digit(ghist, &sh_digit, &sh_remaining, &sh_bincount);
     __syncthreads();
     prefix |= sh_digit << shift;
     mask |= 255u << shift;
@@ -498,8 +518,7 @@ __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kerne
   const uint32_t eq_before_t = block_scan(n_eq, warp_sums, &sh_total);
   const uint32_t cta_eq = sh_total;
   __syncthreads();
-  const uint32_t gt_before_t = block_scan(n_gt, warp_sums, &sh_total);
-  (void)gt_before_t;
+  (void)block_scan(n_gt, warp_sums, &sh_total);
   const uint32_t cta_gt = sh_total;
   if (tid == 0) {
     uint32_t* t0 = cluster.map_shared_rank(&table[0][0], 0);
@@ -535,17 +554,22 @@ __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kerne
       ++pos;
     }
   }
-  cluster.sync();  // rank 0's shared memory stays alive until every CTA has read it
+  cluster.sync();  // rank 0's table stays alive until every rank has read it
 }
 
-// Cluster size for n candidates: enough CTAs for ~512 candidates each, at most 16, or 0 when a CTA
-// would need more than kClusterMaxPer keys.
+// Cluster size for n candidates: a power of two giving ~512 candidates per CTA, at most max_c,
+// or 0 when a CTA would need more than kClusterMaxPer keys.
 inline int cluster_size_for(int n_cand, int max_c) {
-  int c = (n_cand + 511) / 512;
-  if (c < 1) c = 1;
-  if (c > max_c) c = max_c;
+  int c = 1;
+  while (c < max_c && (n_cand + c - 1) / c > 512) c <<= 1;
   if ((n_cand + c - 1) / c > kClusterMaxPer) return 0;
   return c;
+}
+
+// Dynamic shared memory of the cluster select: staged query, n_bufs metadata buffers, the keys.
+inline size_t cluster_smem(int g, int d, size_t es, int rows, int n_bufs, int per) {
+  const int gp = g < 2 ? 2 : g;
+  return (size_t)2 * gp * d * sizeof(float) + (size_t)n_bufs * rows * d * es * 2 + (size_t)per * sizeof(uint64_t);
 }
 
 template <typename TQ, typename TM, int G>
@@ -554,56 +578,64 @@ int launch_select_cluster(int h, int d, cudaStream_t st, const void* q, const vo
                           int bitmap_words, bool* handled) {
   *handled = false;
   auto kern = quest_select_cluster_kernel<TQ, TM, G>;
-  static int max_c[64];  // per device: the largest schedulable cluster (0 = not yet known, -1 = none)
+  static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   const int di = dev & 63;
-  const int rows = score_rows(d, sizeof(TM));
-  // The attribute is set once per device for every head_dim (up to 256): q split, two buffers of
-  // the two metadata tiles (each at most kScoreTileBytes), the slice's keys.
-  const size_t worst = (size_t)2 * G * 256 * sizeof(float) + (size_t)2 * 2 * kScoreTileBytes + (size_t)kClusterMaxPer * sizeof(uint64_t);
-  if (max_c[di] == 0) {
+  // The attribute is set once per device for every head_dim (up to 256): staged query, two
+  // buffers of the two metadata tiles (each at most kScoreTileBytes), the slice's keys.
+  const size_t worst = (size_t)2 * qpad<G>() * 256 * sizeof(float) + (size_t)2 * 2 * kScoreTileBytes + (size_t)kClusterMaxPer * sizeof(uint64_t);
+  if (!attr_set[di]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)worst);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    int best = -1;
-    for (int cs = kClusterMax; e == cudaSuccess && cs >= 1 && best < 0; cs >>= 1) {
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = cs;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(cs, 1);
-      cfg.blockDim = dim3(kClusterThreads);
-      cfg.dynamicSmemBytes = worst;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= 1) best = cs;
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return LKV_OK;  // not handled: the two-kernel select runs instead
     }
-    cudaGetLastError();
-    max_c[di] = best;
+    attr_set[di] = true;
   }
-  if (max_c[di] < 0) return LKV_OK;
-  const int C = cluster_size_for(n_cand, max_c[di]);
+  const int rows = score_rows(d, sizeof(TM));
+  int C = cluster_size_for(n_cand, kClusterMax);
   if (C == 0) return LKV_OK;
-  const int per = (n_cand + C - 1) / C;
-  const int rows_eff = per < rows ? per : rows;
-  const size_t smem = (size_t)2 * G * d * sizeof(float) + (size_t)2 * rows_eff * d * sizeof(TM) * 2 + (size_t)per * sizeof(uint64_t);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(C, h);
   cfg.blockDim = dim3(kClusterThreads);
-  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  // Largest cluster (down to 8) whose h clusters are all resident at once; then double buffering
+  // if that still holds with two buffers.
+  int per = 0, rows_eff = 0, n_bufs = 1;
+  size_t smem = 0;
+  for (;; C >>= 1) {
+    per = (n_cand + C - 1) / C;
+    rows_eff = per < rows ? per : rows;
+    attr[0].val.clusterDim.x = C;
+    cfg.gridDim = dim3(C, 1);
+    int fit1 = 0, fit2 = 0;
+    cfg.dynamicSmemBytes = smem = cluster_smem(G, d, sizeof(TM), rows_eff, 1, per);
+    if (cudaOccupancyMaxActiveClusters(&fit1, kern, &cfg) != cudaSuccess) fit1 = 0;
+    cfg.dynamicSmemBytes = cluster_smem(G, d, sizeof(TM), rows_eff, 2, per);
+    if (cudaOccupancyMaxActiveClusters(&fit2, kern, &cfg) != cudaSuccess) fit2 = 0;
+    cudaGetLastError();
+    if (fit2 >= h) {
+      n_bufs = 2;
+      smem = cfg.dynamicSmemBytes;
+      break;
+    }
+    if (fit1 >= h || C <= 8 || (n_cand + (C >> 1) - 1) / (C >> 1) > kClusterMaxPer) {
+      if (fit1 < 1) return LKV_OK;
+      n_bufs = 1;
+      break;
+    }
+  }
+  cfg.gridDim = dim3(C, h);
+  cfg.dynamicSmemBytes = smem;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin), static_cast<const TM*>(kmax), m_head,
-                                     first_block, n_cand, k, bound_mode, n_passes, per, rows_eff, out_blocks, out_ld, out_bound, bitmap,
+                                     first_block, n_cand, k, bound_mode, n_passes, per, rows_eff, n_bufs, out_blocks, out_ld, out_bound, bitmap,
                                      bitmap_words);
   if (e != cudaSuccess)
     return fail(LKV_ERR_CUDA, "lkv_quest_topk(cluster select, %d CTAs x %d heads, %zu B shared): %s", C, h, smem, cudaGetErrorString(e));
@@ -629,7 +661,7 @@ int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void
                  int n_cand, int bound_mode, uint64_t* keys, float* out_bound) {
   const int rows = score_rows(d, sizeof(TM));
   dim3 grid((n_cand + rows - 1) / rows, h);
-  const size_t smem = 2 * (size_t)g * d * sizeof(float) + 2 * (size_t)rows * d * sizeof(TM);
+  const size_t smem = 2 * (size_t)(g < 2 ? 2 : g) * d * sizeof(float) + 2 * (size_t)rows * d * sizeof(TM);
 #define LKV_SCORE(G)                                                                                                   \
   case G: {                                                                                                            \
     auto kern = quest_score_kernel<TQ, TM, G>;                                                                         \
