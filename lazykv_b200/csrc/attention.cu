@@ -1205,13 +1205,18 @@ __global__ void __launch_bounds__(kMmaThreads, kMmaCtasPerSm) attn_mma_kernel(co
 // Fold the splits of each segment (segment 0: [0, n0), segment 1: [n0, n0 + n1)) of each (head,
 // query row) into per-segment (out, lse) and their merge. One CTA per (head, row): the threads split
 // the channels x the splits so the partials are read with independent loads. Outputs may be null.
-constexpr int kCombineThreads = 256;
+constexpr int kCombineThreads = 1024;
+constexpr int kCombineMaxSplits = 1024;  // (m, l) of up to this many splits are staged in shared memory
 
+// One CTA per (KV head, query row): the splits' (m, l) are staged in shared memory, then
+// kCombineThreads / D split lanes per channel accumulate the rescaled partial outputs, so every
+// thread has only a few independent global loads in flight.
 template <typename TO, int G, int D>
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const float* __restrict__ part, int n0, int n1, TO* __restrict__ out,
                                                                        float* __restrict__ lse, float* __restrict__ seg_out,
                                                                        float* __restrict__ seg_lse, int hq) {
   constexpr int KS = kCombineThreads / D;  // split lanes per channel
+  __shared__ float sm_m[kCombineMaxSplits], sm_l[kCombineMaxSplits];
   __shared__ float red_m[kCombineThreads / 32];
   __shared__ float acc_o[KS][D];
   __shared__ float acc_l[KS];
@@ -1222,11 +1227,18 @@ __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const flo
   const int c = threadIdx.x % D, k = threadIdx.x / D;
   const int64_t stride = G * (D + 2);
   const float* base = part + (int64_t)j * nt * stride;
+  const bool staged = nt <= kCombineMaxSplits;
+  if (staged)
+    for (int sp = threadIdx.x; sp < nt; sp += kCombineThreads) {
+      sm_m[sp] = base[sp * stride + r];
+      sm_l[sp] = base[sp * stride + G + r];
+    }
+  __syncthreads();
 #pragma unroll
   for (int sgi = 0; sgi < 2; ++sgi) {
     const int a = sgi == 0 ? 0 : n0, b = sgi == 0 ? n0 : nt;
     float mloc = -INFINITY;
-    for (int sp = a + threadIdx.x; sp < b; sp += kCombineThreads) mloc = fmaxf(mloc, base[sp * stride + r]);
+    for (int sp = a + threadIdx.x; sp < b; sp += kCombineThreads) mloc = fmaxf(mloc, staged ? sm_m[sp] : base[sp * stride + r]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
     if ((threadIdx.x & 31) == 0) red_m[threadIdx.x >> 5] = mloc;
@@ -1239,10 +1251,10 @@ __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const flo
 #pragma unroll 4
       for (int sp = a + k; sp < b; sp += KS) {
         const float* ps = base + sp * stride;
-        const float ms = ps[r];
+        const float ms = staged ? sm_m[sp] : ps[r];
         const float f = ms == -INFINITY ? 0.0f : exp2f(ms - M);
         O = fmaf(ps[2 * G + r * D + c], f, O);
-        L = fmaf(ps[G + r], f, L);
+        L = fmaf(staged ? sm_l[sp] : ps[G + r], f, L);
       }
     }
     acc_o[k][c] = O;

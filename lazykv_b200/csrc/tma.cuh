@@ -10,7 +10,8 @@ namespace lkv {
 // and that entry point, is the only translation unit that includes this header.
 __device__ int g_device_status = 0;
 constexpr int LKV_DEV_WAIT_TIMEOUT = 1;       // an mbarrier wait ran out of iterations
-constexpr uint32_t kMaxWaitIters = 1u << 22;  // each try_wait also suspends for a bounded time
+constexpr uint32_t kMaxWaitIters = 1u << 21;  // tries; each may suspend up to kWaitHintNs
+constexpr uint32_t kWaitHintNs = 1000;        // suspend-time hint of one try (the wait ends sooner when the phase completes)
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -33,16 +34,18 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
                : "memory");
 }
 
-// Waits for the phase of `bar` with the given parity. Gives up after kMaxWaitIters tries, records
-// LKV_DEV_WAIT_TIMEOUT in g_device_status and returns false.
+// Waits for the phase of `bar` with the given parity. Each try may suspend the thread (up to the
+// hint) until the phase completes, so a waiting warp does not spin on issue slots. Gives up after
+// kMaxWaitIters tries (about two seconds at most), records LKV_DEV_WAIT_TIMEOUT in g_device_status
+// and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
   for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
-        : "r"(addr), "r"(parity)
+        : "r"(addr), "r"(parity), "r"(kWaitHintNs)
         : "memory");
     if (done) return true;
   }
