@@ -90,7 +90,9 @@ int lkv_fetch_pairs(const void* src, int src_kind, const int64_t* src_rows, void
  * id (the selected set is the same either way; ties at the k-th bound go to the lower ids), with
  * LKV_ORDER_BLOCK in ascending block id (no sort). Optional: out_bound [h, n_cand] float32;
  * bitmap [h, bitmap_words] set exactly at the selected block ids (the words are cleared first).
- * Workspace: lkv_quest_topk_workspace(h, n_cand) bytes.
+ * Workspace: lkv_quest_topk_workspace(h, n_cand) bytes, zero-filled once when allocated: its first
+ * 64 KiB hold per-head counters that the LKV_ORDER_BLOCK path expects at zero and leaves at zero
+ * (calls on one workspace must not overlap on the GPU).
  */
 size_t lkv_quest_topk_workspace(int h, int n_cand);
 int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,

@@ -150,10 +150,14 @@ __device__ __forceinline__ float row_bound(const unsigned char* tile_max, const 
   return best;
 }
 
+// hist0 (optional, [h][256], zero on entry): per KV head, the count of keys by the top 8 bits of the
+// orderable bound, i.e. the first radix pass of the select, accumulated with one global atomic per
+// non-empty bin and CTA.
 template <typename TQ, typename TM, int G>
 __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin, const TM* __restrict__ kmax,
                                    int64_t m_head, int first_block, int n_cand, int bound_mode, uint64_t* __restrict__ keys,
-                                   float* __restrict__ out_bound) {
+                                   float* __restrict__ out_bound, uint32_t* __restrict__ hist0) {
+  __shared__ uint32_t sh_hist[256];
   extern __shared__ __align__(16) float qs[];  // q+ [d][GP], q- [d][GP], then the two tiles
   const int rows = blockDim.x;
   const int row_bytes = d * (int)sizeof(TM);
@@ -172,15 +176,25 @@ __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __
     cp_async16(tile_max + pos, reinterpret_cast<const uint4*>(gmax) + u);
     cp_async16(tile_min + pos, reinterpret_cast<const uint4*>(gmin) + u);
   }
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) sh_hist[b] = 0;
   cp_async_wait_all();
   __syncthreads();
   const int t = threadIdx.x;
-  if (t >= n_rows) return;
-  const float best = row_bound<TQ, TM, G>(tile_max, tile_min, t, d, qs, bound_mode);
-  const int ci = c_first + t;
-  const uint64_t key = ((uint64_t)orderable(best) << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
-  keys[(int64_t)j * n_cand + ci] = key;
-  if (out_bound != nullptr) out_bound[(int64_t)j * n_cand + ci] = best == 0.0f ? 0.0f : best;
+  uint32_t digit = 256u;
+  if (t < n_rows) {
+    const float best = row_bound<TQ, TM, G>(tile_max, tile_min, t, d, qs, bound_mode);
+    const int ci = c_first + t;
+    const uint32_t ob = orderable(best);
+    keys[(int64_t)j * n_cand + ci] = ((uint64_t)ob << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
+    if (out_bound != nullptr) out_bound[(int64_t)j * n_cand + ci] = best == 0.0f ? 0.0f : best;
+    digit = ob >> 24;
+  }
+  if (hist0 == nullptr) return;
+  const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+  if (digit < 256u && (t & 31) == __ffs(peers) - 1) atomicAdd(&sh_hist[digit], __popc(peers));
+  __syncthreads();
+  for (int b = threadIdx.x; b < 256; b += blockDim.x)
+    if (sh_hist[b]) atomicAdd(&hist0[(int64_t)j * 256 + b], sh_hist[b]);
 }
 
 // Finds the digit (8 bits at `shift` of the 32-bit bound) holding the `remaining`-th largest among
@@ -364,138 +378,79 @@ __global__ void __launch_bounds__(kSelectThreads) topk_kernel(const uint64_t* __
   }
 }
 
-// ---- the fused, cluster-wide select (ascending block-id output) -------------------------------
+// ---- the cluster-wide select of the k smallest... largest keys, ascending block-id output ----------
 //
-// One thread-block cluster of C CTAs per KV head (C <= 16): CTA c scores a contiguous slice of the
-// candidates (metadata tiles double-buffered through cp.async, the same per-row arithmetic as
-// quest_score_kernel) and keeps its keys in shared memory. The radix passes of topk_kernel then run
-// cluster-wide: each CTA adds its digit histogram into rank 0's shared memory (distributed shared
-// memory atomics), a cluster barrier, and every CTA reads the totals and picks the same digit.
-// Compaction: each CTA publishes its counts of keys above the k-th bound and equal to it; the
-// exclusive sums over lower ranks give each CTA its output offset and its share of the tied keys
-// (lowest ids first), so the selected ids come out in ascending block-id order with no sort.
-// Every CTA reaches every cluster barrier (no early exit).
+// After the score kernel (keys in the workspace, L2-resident, and the first radix pass's histogram
+// per head), one thread-block cluster of C CTAs per KV head finishes the selection: CTA c stages a
+// contiguous slice of the keys in shared memory; every CTA reads the first pass's totals and picks
+// the same digit; each further pass counts its slice, a cluster barrier, and every CTA sums the C
+// histograms through distributed shared memory and picks the same digit. Compaction: one
+// block-wide scan of packed (above, equal) counts per CTA, the CTAs' totals exchanged the same way;
+// the exclusive sums over lower ranks give each CTA its output offset and its share of the tied keys
+// (lowest ids first), so the selected ids come out in ascending block-id order with no sort. Every
+// CTA reaches every cluster barrier (no early exit).
 
 constexpr int kClusterThreads = 256;
 constexpr int kClusterMax = 16;
-constexpr int kClusterMaxPer = 4096;  // candidates per CTA (their keys stay in shared memory)
+constexpr int kClusterMaxPer = 4096;   // keys per CTA (in shared memory)
+constexpr int kHistHeads = 64;         // heads the first-pass histograms are kept for
+constexpr size_t kHistBytes = (size_t)kHistHeads * 256 * sizeof(uint32_t);  // at the workspace's start
 
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-template <typename TQ, typename TM, int G>
-__global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin,
-                                                                                const TM* __restrict__ kmax, int64_t m_head, int first_block,
-                                                                                int n_cand, int k, int bound_mode, int n_passes, int per, int rows,
-                                                                                int n_bufs, int32_t* __restrict__ out_blocks, int out_ld,
-                                                                                float* __restrict__ out_bound, uint32_t* __restrict__ bitmap,
-                                                                                int bitmap_words) {
+__global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(const uint64_t* __restrict__ keys_all, uint32_t* __restrict__ hist0,
+                                                                     int n_cand, int k, int first_block, int n_passes, int per,
+                                                                     int32_t* __restrict__ out_blocks, int out_ld, uint32_t* __restrict__ bitmap,
+                                                                     int bitmap_words) {
   cg::cluster_group cluster = cg::this_cluster();
   const int c = (int)cluster.block_rank();
-  const int C = (int)cluster.num_blocks();  // a power of two <= 16
+  const int C = (int)cluster.num_blocks();
   const int j = blockIdx.y;
   const int tid = threadIdx.x;
-  extern __shared__ __align__(16) unsigned char sm[];
-  __shared__ uint32_t hist[256];             // this CTA's digit counts
-  __shared__ uint32_t red[256];              // rank c: totals of its share of the bins
-  __shared__ uint32_t ghist[256];            // the cluster totals of the current pass
-  __shared__ uint32_t table[kClusterMax][2];  // rank 0: per-CTA (above, equal) counts
+  extern __shared__ __align__(16) uint64_t keys[];  // [per]
+  __shared__ uint32_t hist[3][256];   // this rank's counts of passes 1..3
+  __shared__ uint32_t ghist[256];     // totals of the current pass
+  __shared__ uint32_t counts[2];      // this rank's (above, equal) totals
+  __shared__ uint32_t lower[kClusterMax][2];
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total, sh_pos0, sh_eq0;
-  float* qs = reinterpret_cast<float*>(sm);
-  const int row_bytes = d * (int)sizeof(TM);
-  const int chunks = row_bytes / 16;
-  const size_t buf_bytes = (size_t)rows * row_bytes * 2;
-  unsigned char* bufs = sm + (size_t)2 * qpad<G>() * d * sizeof(float);
-  uint64_t* keys = reinterpret_cast<uint64_t*>(bufs + n_bufs * buf_bytes);
 
   const int lo = min(n_cand, c * per);
   const int hi = min(n_cand, lo + per);
   const int cnt = hi - lo;
+  const uint64_t* src = keys_all + (int64_t)j * n_cand + lo;
+  for (int i = tid; i < cnt; i += blockDim.x) keys[i] = src[i];
   if (c == 0 && bitmap != nullptr)
     for (int w = tid; w < bitmap_words; w += blockDim.x) bitmap[(int64_t)j * bitmap_words + w] = 0u;
-  stage_query<TQ, G>(q, j, d, qs);
-
-  // ---- scores of the slice, in sub-tiles of `rows` candidates (double-buffered when n_bufs = 2) ----
-  const int n_sub = (cnt + rows - 1) / rows;
-  auto load = [&](int sub) {
-    unsigned char* tmax = bufs + (size_t)(sub % n_bufs) * buf_bytes;
-    unsigned char* tmin = tmax + (size_t)rows * row_bytes;
-    const int base = lo + sub * rows;
-    const int nr = min(rows, hi - base);
-    const uint4* gmax = reinterpret_cast<const uint4*>(kmax + (int64_t)j * m_head + (int64_t)(first_block + base) * d);
-    const uint4* gmin = reinterpret_cast<const uint4*>(kmin + (int64_t)j * m_head + (int64_t)(first_block + base) * d);
-    for (int u = tid; u < nr * chunks; u += blockDim.x) {
-      const int t = u / chunks, cc = u % chunks;
-      const int pos = tile_pos(t, cc, chunks, row_bytes);
-      cp_async16(tmax + pos, gmax + u);
-      cp_async16(tmin + pos, gmin + u);
-    }
-    cp_async_commit();
-  };
-  if (n_sub > 0) load(0);
-  for (int sub = 0; sub < n_sub; ++sub) {
-    if (n_bufs == 2 && sub + 1 < n_sub) {
-      load(sub + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();  // the tile (and, the first time, the staged query) is visible
-    const int base = lo + sub * rows;
-    const int nr = min(rows, hi - base);
-    if (tid < nr) {
-      const unsigned char* tmax = bufs + (size_t)(sub % n_bufs) * buf_bytes;
-      const float best = row_bound<TQ, TM, G>(tmax, tmax + (size_t)rows * row_bytes, tid, d, qs, bound_mode);
-      const int ci = base + tid;
-      keys[ci - lo] = ((uint64_t)orderable(best) << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
-      if (out_bound != nullptr) out_bound[(int64_t)j * n_cand + ci] = best == 0.0f ? 0.0f : best;
-    }
-    __syncthreads();  // the buffer is read before it is refilled
-    if (n_bufs == 1 && sub + 1 < n_sub) load(sub + 1);
-  }
-
-  // ---- cluster-wide radix select of the k-th key ----
+  for (int b = tid; b < 256; b += blockDim.x) ghist[b] = hist0[(int64_t)j * 256 + b];
   const int kk = k < n_cand ? k : n_cand;
   if (tid == 0) {
     sh_remaining = (uint32_t)kk;
     sh_bincount = 0;
   }
-  const int bpc = 256 / C;  // bins each rank totals
+  __syncthreads();
   uint32_t prefix = 0, mask = 0;
   bool take_all = kk >= n_cand;
   for (int pass = 0; pass < n_passes && !take_all; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int i = tid; i < 256; i += blockDim.x) {
-      hist[i] = 0;
-      red[i] = 0;
+    if (pass > 0) {
+      uint32_t* hp = hist[pass - 1];
+      for (int b = tid; b < 256; b += blockDim.x) hp[b] = 0;
+      __syncthreads();
+      for (int i0 = 0; i0 < cnt; i0 += blockDim.x) {
+        const int i = i0 + tid;
+        const uint32_t h32 = i < cnt ? (uint32_t)(keys[i] >> 32) : 0u;
+        const bool counted = i < cnt && (h32 & mask) == prefix;
+        const uint32_t digit = counted ? ((h32 >> shift) & 255u) : 256u;
+        const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+        if (counted && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hp[digit], __popc(peers));
+      }
+      cluster.sync();  // every rank's counts of this pass are final
+      for (int b = tid; b < 256; b += blockDim.x) {
+        uint32_t sum = 0;
+        for (int r = 0; r < C; ++r) sum += *cluster.map_shared_rank(&hp[b], r);
+        ghist[b] = sum;
+      }
+      __syncthreads();
     }
-    __syncthreads();
-    for (int i0 = 0; i0 < cnt; i0 += blockDim.x) {
-      const int i = i0 + tid;
-      const uint32_t h32 = i < cnt ? (uint32_t)(keys[i] >> 32) : 0u;
-      const bool counted = i < cnt && (h32 & mask) == prefix;
-      const uint32_t digit = counted ? ((h32 >> shift) & 255u) : 256u;
-      const uint32_t peers = __match_any_sync(0xffffffffu, digit);
-      if (counted && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
-    }
-    cluster.sync();  // every rank's counts are final
-    // Reduce-scatter: rank c totals bins [c * bpc, (c + 1) * bpc) over the C ranks ...
-    for (int u = tid; u < 256; u += blockDim.x) {
-      const int src = u / bpc, bin = c * bpc + u % bpc;
-      const uint32_t v = *cluster.map_shared_rank(&hist[bin], src);
-      if (v) atomicAdd(&red[u % bpc], v);
-    }
-    __syncthreads();
-    // ... and all-gather: it writes those totals into every rank's ghist.
-    for (int u = tid; u < 256; u += blockDim.x) {
-      const int dst = u / bpc, bin = c * bpc + u % bpc;
-      *cluster.map_shared_rank(&ghist[bin], dst) = red[u % bpc];
-    }
-    cluster.sync();
     pick_digit(ghist, &sh_digit, &sh_remaining, &sh_bincount);
     __syncthreads();
     prefix |= sh_digit << shift;
@@ -503,7 +458,7 @@ __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kerne
     take_all = (sh_bincount == sh_remaining);
     __syncthreads();
   }
-  const uint32_t need_equal = take_all ? 0xffffffffu : sh_remaining;
+  const uint32_t need = take_all ? 0xffffffffu : sh_remaining;
   const bool all = kk >= n_cand;
 
   // ---- compaction in candidate order across the cluster ----
@@ -515,33 +470,35 @@ __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kerne
     n_gt += all || h32 > prefix;
     n_eq += !all && h32 == prefix;
   }
-  const uint32_t eq_before_t = block_scan(n_eq, warp_sums, &sh_total);
-  const uint32_t cta_eq = sh_total;
-  __syncthreads();
-  (void)block_scan(n_gt, warp_sums, &sh_total);
-  const uint32_t cta_gt = sh_total;
+  const uint32_t pre = block_scan(n_gt | (n_eq << 16), warp_sums, &sh_total);  // per <= 4096: both fit 16 bits
   if (tid == 0) {
-    uint32_t* t0 = cluster.map_shared_rank(&table[0][0], 0);
-    t0[2 * c] = cta_gt;
-    t0[2 * c + 1] = cta_eq;
+    counts[0] = sh_total & 0xffffu;
+    counts[1] = sh_total >> 16;
   }
-  cluster.sync();
+  cluster.sync();  // every rank's totals are published; every rank has read the first-pass histogram
+  if (c == 0)
+    for (int b = tid; b < 256; b += blockDim.x) hist0[(int64_t)j * 256 + b] = 0u;  // zero for the next call
+  if (tid < c) {
+    lower[tid][0] = *cluster.map_shared_rank(&counts[0], tid);
+    lower[tid][1] = *cluster.map_shared_rank(&counts[1], tid);
+  }
+  __syncthreads();
   if (tid == 0) {
-    const uint32_t* t0 = cluster.map_shared_rank(&table[0][0], 0);
     uint32_t eqb = 0, posb = 0;
     for (int r = 0; r < c; ++r) {
-      const uint32_t gt = t0[2 * r], eq = t0[2 * r + 1];
-      const uint32_t take = eqb < need_equal ? min(eq, need_equal - eqb) : 0u;
-      posb += gt + take;
-      eqb += eq;
+      const uint32_t take = eqb < need ? min(lower[r][1], need - eqb) : 0u;
+      posb += lower[r][0] + take;
+      eqb += lower[r][1];
     }
     sh_pos0 = posb;
     sh_eq0 = eqb;
   }
   __syncthreads();
-  const uint32_t eq_before = sh_eq0 + eq_before_t;
-  const uint32_t take_eq = eq_before < need_equal ? min(n_eq, need_equal - eq_before) : 0u;
-  uint32_t pos = sh_pos0 + block_scan(n_gt + take_eq, warp_sums, &sh_total);
+  const uint32_t gt_before = pre & 0xffffu, eq_before_t = pre >> 16;
+  const uint32_t e0 = sh_eq0;
+  const uint32_t room = e0 < need ? need - e0 : 0u;  // tied keys this rank may still take
+  uint32_t pos = sh_pos0 + gt_before + min(eq_before_t, room);
+  const uint32_t take_eq = eq_before_t < room ? min(n_eq, room - eq_before_t) : 0u;
   uint32_t eq_seen = 0;
   for (int i = tlo; i < thi; ++i) {
     const uint32_t h32 = (uint32_t)(keys[i] >> 32) & mask;
@@ -554,111 +511,52 @@ __global__ void __launch_bounds__(kClusterThreads, 1) quest_select_cluster_kerne
       ++pos;
     }
   }
-  cluster.sync();  // rank 0's table stays alive until every rank has read it
+  cluster.sync();  // each rank's shared memory stays alive until every rank has read it
 }
 
-// Cluster size for n candidates: a power of two giving ~512 candidates per CTA, at most max_c,
-// or 0 when a CTA would need more than kClusterMaxPer keys.
-inline int cluster_size_for(int n_cand, int max_c) {
+// Cluster size for n candidates: a power of two giving ~512 keys per CTA, at most 16; 0 when a
+// CTA would need more than kClusterMaxPer keys.
+inline int cluster_size_for(int n_cand) {
   int c = 1;
-  while (c < max_c && (n_cand + c - 1) / c > 512) c <<= 1;
+  while (c < kClusterMax && (n_cand + c - 1) / c > 512) c <<= 1;
   if ((n_cand + c - 1) / c > kClusterMaxPer) return 0;
   return c;
 }
 
-// Dynamic shared memory of the cluster select: staged query, n_bufs metadata buffers, the keys.
-inline size_t cluster_smem(int g, int d, size_t es, int rows, int n_bufs, int per) {
-  const int gp = g < 2 ? 2 : g;
-  return (size_t)2 * gp * d * sizeof(float) + (size_t)n_bufs * rows * d * es * 2 + (size_t)per * sizeof(uint64_t);
-}
-
-template <typename TQ, typename TM, int G>
-int launch_select_cluster(int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
-                          int n_cand, int k, int bound_mode, int n_passes, int32_t* out_blocks, int out_ld, float* out_bound, uint32_t* bitmap,
-                          int bitmap_words, bool* handled) {
-  *handled = false;
-  auto kern = quest_select_cluster_kernel<TQ, TM, G>;
+int launch_topk_cluster(int h, cudaStream_t st, const uint64_t* keys, uint32_t* hist0, int n_cand, int k, int first_block, int n_passes,
+                        int32_t* out_blocks, int out_ld, uint32_t* bitmap, int bitmap_words) {
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  const int di = dev & 63;
-  // The attribute is set once per device for every head_dim (up to 256): staged query, two
-  // buffers of the two metadata tiles (each at most kScoreTileBytes), the slice's keys.
-  const size_t worst = (size_t)2 * qpad<G>() * 256 * sizeof(float) + (size_t)2 * 2 * kScoreTileBytes + (size_t)kClusterMaxPer * sizeof(uint64_t);
-  if (!attr_set[di]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)worst);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return LKV_OK;  // not handled: the two-kernel select runs instead
-    }
-    attr_set[di] = true;
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(topk_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(topk_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kClusterMaxPer * sizeof(uint64_t)));
+    if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk(cluster select) attributes: %s", cudaGetErrorString(e));
+    attr_set[dev & 63] = true;
   }
-  const int rows = score_rows(d, sizeof(TM));
-  int C = cluster_size_for(n_cand, kClusterMax);
-  if (C == 0) return LKV_OK;
+  const int C = cluster_size_for(n_cand);
+  const int per = (n_cand + C - 1) / C;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(C, h);
   cfg.blockDim = dim3(kClusterThreads);
+  cfg.dynamicSmemBytes = (size_t)per * sizeof(uint64_t);
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  // Largest cluster (down to 8) whose h clusters are all resident at once; then double buffering
-  // if that still holds with two buffers.
-  int per = 0, rows_eff = 0, n_bufs = 1;
-  size_t smem = 0;
-  for (;; C >>= 1) {
-    per = (n_cand + C - 1) / C;
-    rows_eff = per < rows ? per : rows;
-    attr[0].val.clusterDim.x = C;
-    cfg.gridDim = dim3(C, 1);
-    int fit1 = 0, fit2 = 0;
-    cfg.dynamicSmemBytes = smem = cluster_smem(G, d, sizeof(TM), rows_eff, 1, per);
-    if (cudaOccupancyMaxActiveClusters(&fit1, kern, &cfg) != cudaSuccess) fit1 = 0;
-    cfg.dynamicSmemBytes = cluster_smem(G, d, sizeof(TM), rows_eff, 2, per);
-    if (cudaOccupancyMaxActiveClusters(&fit2, kern, &cfg) != cudaSuccess) fit2 = 0;
-    cudaGetLastError();
-    if (fit2 >= h) {
-      n_bufs = 2;
-      smem = cfg.dynamicSmemBytes;
-      break;
-    }
-    if (fit1 >= h || C <= 8 || (n_cand + (C >> 1) - 1) / (C >> 1) > kClusterMaxPer) {
-      if (fit1 < 1) return LKV_OK;
-      n_bufs = 1;
-      break;
-    }
-  }
-  cfg.gridDim = dim3(C, h);
-  cfg.dynamicSmemBytes = smem;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin), static_cast<const TM*>(kmax), m_head,
-                                     first_block, n_cand, k, bound_mode, n_passes, per, rows_eff, n_bufs, out_blocks, out_ld, out_bound, bitmap,
+  cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel, keys, hist0, n_cand, k, first_block, n_passes, per, out_blocks, out_ld, bitmap,
                                      bitmap_words);
-  if (e != cudaSuccess)
-    return fail(LKV_ERR_CUDA, "lkv_quest_topk(cluster select, %d CTAs x %d heads, %zu B shared): %s", C, h, smem, cudaGetErrorString(e));
-  *handled = true;
+  if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk(cluster select, %d CTAs x %d heads): %s", C, h, cudaGetErrorString(e));
   return LKV_OK;
 }
 
 template <typename TQ, typename TM>
-int select_cluster(int g, int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
-                   int n_cand, int k, int bound_mode, int n_passes, int32_t* out_blocks, int out_ld, float* out_bound, uint32_t* bitmap,
-                   int bitmap_words, bool* handled) {
-  switch (g) {
-    case 1: return launch_select_cluster<TQ, TM, 1>(h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, handled);
-    case 2: return launch_select_cluster<TQ, TM, 2>(h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, handled);
-    case 4: return launch_select_cluster<TQ, TM, 4>(h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, handled);
-    case 8: return launch_select_cluster<TQ, TM, 8>(h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, handled);
-    default: *handled = false; return LKV_OK;
-  }
-}
-
-template <typename TQ, typename TM>
 int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
-                 int n_cand, int bound_mode, uint64_t* keys, float* out_bound) {
+                 int n_cand, int bound_mode, uint64_t* keys, float* out_bound, uint32_t* hist0) {
   const int rows = score_rows(d, sizeof(TM));
   dim3 grid((n_cand + rows - 1) / rows, h);
   const size_t smem = 2 * (size_t)(g < 2 ? 2 : g) * d * sizeof(float) + 2 * (size_t)rows * d * sizeof(TM);
@@ -667,7 +565,7 @@ int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void
     auto kern = quest_score_kernel<TQ, TM, G>;                                                                         \
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);          \
     kern<<<grid, rows, smem, st>>>(static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin), static_cast<const TM*>(kmax), \
-                                   m_head, first_block, n_cand, bound_mode, keys, out_bound);                          \
+                                   m_head, first_block, n_cand, bound_mode, keys, out_bound, hist0);                   \
     break;                                                                                                             \
   }
   switch (g) {
@@ -690,7 +588,7 @@ using namespace lkv;
 extern "C" {
 
 size_t lkv_quest_topk_workspace(int h, int n_cand) {
-  return (size_t)(h > 0 ? h : 0) * (size_t)(n_cand > 0 ? n_cand : 0) * sizeof(uint64_t);
+  return kHistBytes + (size_t)(h > 0 ? h : 0) * (size_t)(n_cand > 0 ? n_cand : 0) * sizeof(uint64_t);
 }
 
 int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax,
@@ -719,33 +617,28 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   // A bf16 bound's orderable 32-bit form has constant low 16 bits for a given sign, so its top 16
   // bits order the keys: two 8-bit passes reach the k-th bound; ties go to the scan.
   const int n_passes = bound_mode == LKV_BF16 ? 2 : 4;
-  if (order == LKV_ORDER_BLOCK) {
-    bool handled = false;
-    int rc2;
-    if (q_dtype == LKV_BF16 && meta_dtype == LKV_BF16)
-      rc2 = select_cluster<__nv_bfloat16, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, &handled);
-    else if (q_dtype == LKV_F32 && meta_dtype == LKV_F32)
-      rc2 = select_cluster<float, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, &handled);
-    else if (q_dtype == LKV_BF16 && meta_dtype == LKV_F32)
-      rc2 = select_cluster<__nv_bfloat16, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, &handled);
-    else
-      rc2 = select_cluster<float, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, k, bound_mode, n_passes, out_blocks, out_ld, out_bound, bitmap, bitmap_words, &handled);
-    if (rc2) return rc2;
-    if (handled) return launched("lkv_quest_topk(cluster select)");
-    if (k > kMaxK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
-  }
-  uint64_t* keys = static_cast<uint64_t*>(workspace);
+  uint32_t* hist0 = static_cast<uint32_t*>(workspace);  // first-pass histograms, zero between calls
+  uint64_t* keys = reinterpret_cast<uint64_t*>(static_cast<unsigned char*>(workspace) + kHistBytes);
+  // Ascending block-id order with at most kHistHeads heads: the score kernel also counts the first
+  // radix pass, and a cluster per head finishes the select from the keys.
+  const bool cluster = order == LKV_ORDER_BLOCK && h <= kHistHeads && cluster_size_for(n_cand) > 0;
+  if (!cluster && k > kMaxK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
+  uint32_t* h0 = cluster ? hist0 : nullptr;
   int rc;
   if (q_dtype == LKV_BF16 && meta_dtype == LKV_BF16)
-    rc = launch_score<__nv_bfloat16, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
+    rc = launch_score<__nv_bfloat16, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound, h0);
   else if (q_dtype == LKV_F32 && meta_dtype == LKV_F32)
-    rc = launch_score<float, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
+    rc = launch_score<float, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound, h0);
   else if (q_dtype == LKV_BF16 && meta_dtype == LKV_F32)
-    rc = launch_score<__nv_bfloat16, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
+    rc = launch_score<__nv_bfloat16, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound, h0);
   else
-    rc = launch_score<float, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound);
+    rc = launch_score<float, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, keys, out_bound, h0);
   if (rc) return rc;
   if ((rc = launched("lkv_quest_topk(score)"))) return rc;
+  if (cluster) {
+    if ((rc = launch_topk_cluster(h, st, keys, hist0, n_cand, k, first_block, n_passes, out_blocks, out_ld, bitmap, bitmap_words))) return rc;
+    return launched("lkv_quest_topk(cluster select)");
+  }
   int P = 1;
   while (P < k) P <<= 1;
   const size_t sel_smem = (size_t)(P < 2 ? 2 : P) * sizeof(uint64_t);
@@ -772,7 +665,7 @@ namespace {
 
 // 4 MiB of keys: h * n_cand <= 524,288 (e.g. 8 KV heads x 65,536 candidate blocks, a 1M-token
 // context in 16-token blocks). Every device that loads the library holds it until exit.
-constexpr size_t kNoAllocScratchBytes = 4u << 20;
+constexpr size_t kNoAllocScratchBytes = kHistBytes + (4u << 20);
 static __device__ __align__(256) uint64_t g_topk_scratch[kNoAllocScratchBytes / sizeof(uint64_t)];
 
 constexpr int kMaxDevices = 64;
@@ -808,7 +701,7 @@ extern "C" int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h,
   const size_t need = lkv_quest_topk_workspace(h, n_cand);
   if (need > kNoAllocScratchBytes)
     return fail(LKV_ERR_ARG, "lkv_quest_topk_noalloc: %d heads x %d candidates need %zu bytes of scratch, above its fixed %zu (h * n_cand <= %zu)",
-                h, n_cand, need, kNoAllocScratchBytes, kNoAllocScratchBytes / sizeof(uint64_t));
+                h, n_cand, need, kNoAllocScratchBytes, (kNoAllocScratchBytes - kHistBytes) / sizeof(uint64_t));
   void* scratch = nullptr;
   if (int rc = scratch_address(&scratch)) return rc;
   // Nothing in the scratch has to start at zero: the score kernel writes every key the select

@@ -26,7 +26,9 @@ def workspace(device: torch.device, nbytes: int, slot: int = 0) -> torch.Tensor:
     key = (device.index if device.index is not None else torch.cuda.current_device(), slot)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        # Zeroed once: the selection keeps counters at the start of its workspace that must read
+        # zero on entry and that its kernels leave zero.
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WS[key] = buf
     return buf
 
@@ -89,10 +91,13 @@ def fetch_pairs(src: torch.Tensor, src_rows: torch.Tensor, dst: torch.Tensor, ds
 
 def quest_topk(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int, n_cand: int, k: int,
                bound_dtype: torch.dtype | None = None, out_blocks: torch.Tensor | None = None, want_bound: bool = False,
-               bitmap: torch.Tensor | None = None, ws_slot: int = 0, by_block: bool = False) -> tuple[torch.Tensor, torch.Tensor | None]:
+               bitmap: torch.Tensor | None = None, ws_slot: int = 1, by_block: bool = False) -> tuple[torch.Tensor, torch.Tensor | None]:
     """Top-k block ids [h, k] (int32) over candidates [first_block, first_block + n_cand) of
     metadata [h, cap, d]: descending bound with ties to the lower id, or ascending id when
-    `by_block` (the same set, no sort); optionally the bounds [h, n_cand]."""
+    `by_block` (the same set, no sort); optionally the bounds [h, n_cand].
+
+    Its workspace (slot 1 by default) keeps zeroed counters between calls, so it is never shared
+    with the attention calls' workspace (slot 0)."""
     dev = require_cuda(query, kmin, kmax)
     hq, d = query.shape[-3] if query.dim() == 4 else query.shape[0], query.shape[-1]
     q = query.reshape(hq, d).contiguous()

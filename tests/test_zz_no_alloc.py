@@ -42,7 +42,7 @@ def _run(entry: str, q, kmin, kmax, first: int, n_cand: int, k: int, mode: int):
         _lib.call("lkv_quest_topk_noalloc", *common, stream)
         assert torch.cuda.memory_stats().get("allocation.all.allocated", 0) == before
     else:
-        ws = torch.empty(_lib.lib().lkv_quest_topk_workspace(h, n_cand), dtype=torch.uint8, device=DEV)
+        ws = torch.zeros(_lib.lib().lkv_quest_topk_workspace(h, n_cand), dtype=torch.uint8, device=DEV)
         _lib.call("lkv_quest_topk", *common, ws.data_ptr(), ws.numel(), stream)
     torch.cuda.synchronize()
     return out.cpu().numpy(), bound.cpu().numpy(), bitmap.cpu().numpy()
