@@ -44,6 +44,16 @@ size_t lkv_last_error(char* buf, size_t len);
 int64_t lkv_packed_pair_bytes(int bs, int d);
 
 /*
+ * Context-range sharding of one layer's sealed blocks over `world` GPUs (no reference
+ * counterpart: the reference runs on one GPU). Host-only. Rank r holds sealed blocks [lo, hi), the
+ * contiguous ranges of ceil(n_sealed / world) blocks; the sink (block 0) is on rank 0 and is never
+ * a candidate, and the current block belongs to the last rank. The budget k_total is shared in
+ * proportion to the candidates, the remainder one block each to the lowest ranks with room, so the
+ * local budgets sum to k_total. out[5] = {lo, hi, first candidate, candidates, local budget}.
+ */
+int lkv_shard_plan(int n_sealed, int k_total, int world, int rank, int32_t* out);
+
+/*
  * Channel-wise min/max of each block's keys. Replaces the amin/amax of
  * lazykv/selection.py:142-144, lazykv/tiered.py:173-175 and :369-370.
  * Key element (head j, block b, token t, channel c) is keys[j*s_head + b*s_block + t*s_tok + c];
@@ -116,6 +126,18 @@ int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h, int d, con
                            int n_cand, int k, int bound_mode, int order, int32_t* out_blocks,
                            int out_ld, float* out_bound, uint32_t* bitmap, int bitmap_words,
                            void* stream);
+
+/*
+ * Global top-k over candidates gathered from the shards (no reference counterpart): for KV head j
+ * the candidates are (bounds[j*ld + i], ids[j*ld + i]), i < n, listed in ascending id (as the
+ * shards' LKV_ORDER_BLOCK selections concatenate in rank order); the k with the highest bound,
+ * ties at the k-th bound to the lower ids, as lkv_quest_topk orders them. k <= 16384.
+ * Workspace: lkv_topk_merge_workspace(h, n) bytes (same contract as lkv_quest_topk's).
+ */
+size_t lkv_topk_merge_workspace(int h, int n);
+int lkv_topk_merge(const float* bounds, const int32_t* ids, int h, int n, int64_t ld, int k,
+                   int bound_mode, int order, int32_t* out_blocks, int out_ld, uint32_t* bitmap,
+                   int bitmap_words, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Split decode attention over listed blocks, emitting (normalised out, lse). Replaces the gather

@@ -4,7 +4,8 @@
 //  * hot segment (lazykv/tiered.py:465-487 + lazykv/attention.py:125-136): the key sequence of KV
 //    head j is the n_list listed blocks, read in place through an optional block->slot map (no
 //    gather copy); the last listed block is the current block with `last_fill` live tokens
-//    (selection.py:65-69);
+//    (selection.py:65-69); a listed id of -1 is padding (no load, no keys), which lets heads list
+//    different numbers of blocks (a shard's part of a global selection);
 //  * cold segment (lazykv/exact.py:88-127): blocks [first, first + n) minus a per-head exclusion
 //    bitmap, read from int8 records with the dequantisation fused (quant.py:103-104: float32
 //    affine, then rounded to the model dtype, i.e. what a fetch puts in a slot), or from pairs in
@@ -220,6 +221,7 @@ __global__ void __launch_bounds__(kThreads) attn_ldg_kernel(const AttnParams p) 
     int blk, live = p.bs;
     if (S.kind == SEG_LIST) {
       blk = __ldg(S.blocks + (int64_t)j * S.n_list + it);
+      if (blk < 0) continue;  // padding
       if (it == S.n_list - 1) live = S.last_fill;
     } else {
       blk = S.first_block + it;
@@ -484,19 +486,23 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
       int r = 0;
       if (my_it < end) {
         const int blk = __ldg(S.blocks + (int64_t)j * S.n_list + my_it);
-        r = S.slot_of != nullptr ? __ldg(S.slot_of + (int64_t)j * S.slot_stride + blk) : blk;
+        r = blk < 0 ? -1 : (S.slot_of != nullptr ? __ldg(S.slot_of + (int64_t)j * S.slot_stride + blk) : blk);
       }
       row_cache = r;
       cache_batch = batch;
     }
     return (int64_t)__shfl_sync(0xffffffffu, row_cache, n & 31);
   };
+  uint32_t pad_bits = 0;  // stages holding a padding item (no copy, nothing to attend)
   // Issue the copies of item `it` (the n-th of this warp) into stage `s`; lane 0 issues.
   auto issue = [&](int it, int n, int s) {
     unsigned char* dst = stages + (size_t)s * C::STAGE;
     if (list) {
       const int64_t row = list_row(it, n);
-      if (lane == 0) {
+      pad_bits = (pad_bits & ~(1u << s)) | ((row < 0 ? 1u : 0u) << s);
+      if (row < 0) {
+        if (lane == 0) mbar_arrive(&bars[s]);
+      } else if (lane == 0) {
         const T* kp = static_cast<const T*>(S.k_base) + row * S.s_row + (int64_t)j * S.s_head;
         const T* vp = static_cast<const T*>(S.v_base) + row * S.s_row + (int64_t)j * S.s_head;
         constexpr uint32_t half = BS * D * sizeof(T);
@@ -536,6 +542,15 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
     if (!ok) break;
     phase ^= 1u << s;
     ++n_done;
+    if ((pad_bits >> s) & 1u) {  // padding: nothing to attend; the stage is free
+      if (issue_it < end) {
+        issue(issue_it, n_issued, s);
+        ++n_issued;
+        issue_it = next_item(issue_it + kWarps);
+      }
+      s = (s + 1 == STAGES) ? 0 : s + 1;
+      continue;
+    }
     const unsigned char* st = stages + (size_t)s * C::STAGE;
     const int live = (list && it == S.n_list - 1) ? S.last_fill : BS;
 
@@ -993,17 +1008,21 @@ __global__ void __launch_bounds__(kMmaThreads, kMmaCtasPerSm) attn_mma_kernel(co
       int r = 0;
       if (my_it < end) {
         const int blk = __ldg(S.blocks + (int64_t)j * S.n_list + my_it);
-        r = S.slot_of != nullptr ? __ldg(S.slot_of + (int64_t)j * S.slot_stride + blk) : blk;
+        r = blk < 0 ? -1 : (S.slot_of != nullptr ? __ldg(S.slot_of + (int64_t)j * S.slot_stride + blk) : blk);
       }
       row_cache = r;
       cache_batch = batch;
     }
     return __shfl_sync(0xffffffffu, row_cache, n & 31);
   };
+  uint32_t pad_bits = 0;  // stages holding a padding item (no copy, nothing to attend)
   auto issue = [&](int it, int n, int s) {
     unsigned char* dst = stage0 + s * stage_stride;
     const int row = list ? list_row(n) : S.first_block + it;
-    if (lane == 0) {
+    pad_bits = (pad_bits & ~(1u << s)) | ((row < 0 ? 1u : 0u) << s);
+    if (row < 0) {
+      if (lane == 0) mbar_arrive(&bars[s]);
+    } else if (lane == 0) {
       if (rec) {
         mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaRec);
         tma_load_1d(dst, S.records + ((int64_t)row * p.h + j) * S.width, (uint32_t)kMmaRec, &bars[s]);
@@ -1036,6 +1055,15 @@ __global__ void __launch_bounds__(kMmaThreads, kMmaCtasPerSm) attn_mma_kernel(co
     phase ^= 1u << s;
     ++n_done;
     unsigned char* st = stage0 + s * stage_stride;
+    if ((pad_bits >> s) & 1u) {  // padding: nothing to attend; the stage is free
+      if (issue_it < end) {
+        issue(issue_it, n_issued, s);
+        ++n_issued;
+        issue_it = next_item(issue_it + kMmaWarps);
+      }
+      s = (s + 1 == kMmaStages) ? 0 : s + 1;
+      continue;
+    }
     uint32_t kt, vt;
     if (rec) {
       dequant_record(st, tiles, tiles + kMmaTile, lane);

@@ -25,9 +25,9 @@ namespace {
 
 constexpr int kSelectThreads = 1024;
 constexpr int kMaxK = 16384;             // shared-memory sort capacity (128 KiB of keys)
-constexpr int kScoreTileBytes = 32768;   // one metadata array's tile per CTA
+constexpr int kScoreTileBytes = 16384;   // one metadata array's tile per CTA
 
-// Rows (candidates) per scoring CTA: a 32 KiB tile of each of kmin and kmax, at most 256 rows.
+// Rows (candidates) per scoring CTA: a 16 KiB tile of each of kmin and kmax, at most 256 rows.
 inline int score_rows(int d, size_t es) {
   const int r = kScoreTileBytes / (int)(d * es);
   return r < 256 ? r : 256;
@@ -38,11 +38,25 @@ inline int score_rows(int d, size_t es) {
 // of row t at chunk position (c + t % 8) mod chunks (a rotation within the row, so rows of fewer
 // than 8 chunks stay in place): a quarter-warp reading chunk c of 8 consecutive rows then
 // touches 8 distinct bank groups, while each thread still walks its row's channels in order.
-// Position of 16-byte chunk c of tile row t (row_bytes = chunks * 16).
+// Position of 16-byte chunk c of tile row t (row_bytes = chunks * 16): a rotation by t when the
+// chunk count is a power of two (shift and mask), else by t % 8.
 __device__ __forceinline__ int tile_pos(int t, int c, int chunks, int row_bytes) {
+  if ((chunks & (chunks - 1)) == 0) return t * row_bytes + (((c + t) & (chunks - 1)) << 4);
   int cc = c + (t & 7) % chunks;
   if (cc >= chunks) cc -= chunks;
   return t * row_bytes + cc * 16;
+}
+
+// Row and chunk of the u-th 16-byte chunk of a tile.
+__device__ __forceinline__ void tile_rc(int u, int chunks, int& t, int& c) {
+  if ((chunks & (chunks - 1)) == 0) {
+    const int sh = __ffs(chunks) - 1;
+    t = u >> sh;
+    c = u & (chunks - 1);
+  } else {
+    t = u / chunks;
+    c = u % chunks;
+  }
 }
 
 // Query staging for the scoring kernels: q+ and q- transposed to [channel][row] with the rows
@@ -171,7 +185,8 @@ __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __
   const unsigned char* gmax = reinterpret_cast<const unsigned char*>(kmax + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
   const unsigned char* gmin = reinterpret_cast<const unsigned char*>(kmin + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
   for (int u = threadIdx.x; u < n_rows * chunks; u += blockDim.x) {
-    const int t = u / chunks, c = u % chunks;
+    int t, c;
+    tile_rc(u, chunks, t, c);
     const int pos = tile_pos(t, c, chunks, row_bytes);
     cp_async16(tile_max + pos, reinterpret_cast<const uint4*>(gmax) + u);
     cp_async16(tile_min + pos, reinterpret_cast<const uint4*>(gmin) + u);
@@ -554,6 +569,17 @@ int launch_topk_cluster(int h, cudaStream_t st, const uint64_t* keys, uint32_t* 
   return LKV_OK;
 }
 
+// Keys of gathered candidates: (orderable bound << 32) | ~id, so the select decodes the id itself.
+__global__ void merge_keys_kernel(const float* __restrict__ bounds, const int32_t* __restrict__ ids, int n, int64_t ld,
+                                  uint64_t* __restrict__ keys) {
+  const int j = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float b = bounds[(int64_t)j * ld + i];
+    const uint32_t id = (uint32_t)ids[(int64_t)j * ld + i];
+    keys[(int64_t)j * n + i] = ((uint64_t)orderable(b) << 32) | (uint64_t)(0xffffffffu - id);
+  }
+}
+
 template <typename TQ, typename TM>
 int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
                  int n_cand, int bound_mode, uint64_t* keys, float* out_bound, uint32_t* hist0) {
@@ -648,6 +674,33 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   topk_kernel<<<h, kSelectThreads, smem, st>>>(keys, n_cand, k, first_block, out_blocks, out_ld, bitmap, bitmap_words, stage_keys,
                                                 order == LKV_ORDER_BLOCK, n_passes);
   return launched("lkv_quest_topk(select)");
+}
+
+size_t lkv_topk_merge_workspace(int h, int n) { return lkv_quest_topk_workspace(h, n); }
+
+int lkv_topk_merge(const float* bounds, const int32_t* ids, int h, int n, int64_t ld, int k, int bound_mode, int order, int32_t* out_blocks,
+                   int out_ld, uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dtype_ok(bound_mode)) return fail(LKV_ERR_ARG, "lkv_topk_merge: bad bound mode %d", bound_mode);
+  if (h <= 0 || n <= 0 || k <= 0 || k > n || ld < n) return fail(LKV_ERR_ARG, "lkv_topk_merge: need 0 < k <= n <= ld (h=%d, n=%d, k=%d)", h, n, k);
+  if (k > kMaxK) return fail(LKV_ERR_ARG, "lkv_topk_merge: k=%d exceeds %d", k, kMaxK);
+  if (out_ld < k) return fail(LKV_ERR_ARG, "lkv_topk_merge: output row stride %d < k=%d", out_ld, k);
+  if (order != LKV_ORDER_BOUND && order != LKV_ORDER_BLOCK) return fail(LKV_ERR_ARG, "lkv_topk_merge: bad order %d", order);
+  if (bounds == nullptr || ids == nullptr || out_blocks == nullptr || workspace == nullptr) return fail(LKV_ERR_PTR, "lkv_topk_merge: null pointer");
+  if (workspace_bytes < lkv_topk_merge_workspace(h, n))
+    return fail(LKV_ERR_WORKSPACE, "lkv_topk_merge: workspace %zu < %zu bytes", workspace_bytes, lkv_topk_merge_workspace(h, n));
+  cudaStream_t st = as_stream(stream);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(static_cast<unsigned char*>(workspace) + kHistBytes);
+  merge_keys_kernel<<<dim3((n + 255) / 256, h), 256, 0, st>>>(bounds, ids, n, ld, keys);
+  if (int rc = launched("lkv_topk_merge(keys)")) return rc;
+  int P = 1;
+  while (P < k) P <<= 1;
+  const size_t sel_smem = (size_t)(P < 2 ? 2 : P) * sizeof(uint64_t);
+  const int stage_keys = sel_smem + (size_t)n * sizeof(uint64_t) <= 200 * 1024;
+  const size_t smem = sel_smem + (stage_keys ? (size_t)n * sizeof(uint64_t) : 0);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  topk_kernel<<<h, kSelectThreads, smem, st>>>(keys, n, k, 0, out_blocks, out_ld, bitmap, bitmap_words, stage_keys, order == LKV_ORDER_BLOCK,
+                                                bound_mode == LKV_BF16 ? 2 : 4);
+  return launched("lkv_topk_merge(select)");
 }
 
 }  // extern "C"
