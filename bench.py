@@ -135,13 +135,13 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev) -> tuple[
     nb = args.ctx // BS  # blocks in the context; the last one is the (full) current block
     n_sealed = nb - 1
     k_total = blocks_for_budget(args.budget, args.ctx, BS)
-    # Shard the sealed blocks 0..n_sealed-1 by contiguous range; the last rank also holds the current block.
-    per = -(-n_sealed // world)
-    lo, hi = rank * per, min(n_sealed, (rank + 1) * per)
-    has_sink, has_cur = lo == 0, rank == world - 1
-    cand_lo = max(lo, 1)
-    n_cand = hi - cand_lo
-    k_local = k_total // world
+    # Shard the sealed blocks 0..n_sealed-1 by contiguous range (lkv_shard_plan): the sink on rank 0,
+    # the current block on the last rank, the budget shared in proportion to the candidates.
+    from lazykv_b200.sharded import shard_plan
+
+    plan = shard_plan(n_sealed, k_total, world, rank)
+    lo, hi, has_sink, has_cur = plan.lo, plan.hi, plan.has_sink, plan.has_current
+    cand_lo, n_cand, k_local = plan.cand_first, plan.n_cand, plan.k_local
     if n_cand <= k_local:
         raise SystemExit(f"shard of {n_cand} candidates cannot select {k_local}")
     n_list = k_local + int(has_sink) + int(has_cur)
@@ -185,8 +185,16 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev) -> tuple[
             L.pool[n_slots - 1] = torch.randn(HKV, 2, BS, D, device=dev, generator=g).bfloat16()
         del kv
         L.deq = None
-        L.out = torch.empty((HQ, D), dtype=torch.bfloat16 if world == 1 else torch.float32, device=dev)
-        L.lse = torch.empty((HQ,), dtype=torch.float32, device=dev)
+        if world == 1:
+            L.out = torch.empty((HQ, D), dtype=torch.bfloat16, device=dev)
+            L.lse = torch.empty((HQ,), dtype=torch.float32, device=dev)
+            L.packed = None
+        else:
+            # One buffer per layer, out then lse: one all-gather per layer, merged in place.
+            from lazykv_b200.sharded import PackedPartial
+
+            L.packed = PackedPartial(HQ, D, world, dev)
+            L.out, L.lse = L.packed.out, L.packed.lse
         L.records_host = None
         layers.append(L)
     torch.cuda.synchronize(dev)
@@ -217,7 +225,7 @@ def layer_step(L, geo: dict, cold_store=None, events: list | None = None) -> Non
     mark()
 
 
-LAUNCHES_PER_LAYER_STEP = 3  # fused score + top-K (one cluster launch), attention partials (hot and cold) + combine
+LAUNCHES_PER_LAYER_STEP = 4  # score (+ first radix pass), cluster select, attention partials (hot and cold), combine
 
 
 def run_ours(args: argparse.Namespace) -> None:
@@ -241,8 +249,6 @@ def run_ours(args: argparse.Namespace) -> None:
         dist.barrier()
     layers, geo = build_layers(args, rank, world, dev)
     n_steps, n_warm = args.steps, args.warmup
-    gathered = [torch.empty((world, HQ, D), dtype=torch.float32, device=dev) for _ in layers]
-    gathered_lse = [torch.empty((world, HQ), dtype=torch.float32, device=dev) for _ in layers]
     finals = [torch.empty((HQ, D), dtype=torch.bfloat16, device=dev) for _ in layers]
 
     from lazykv_b200 import kernels as K
@@ -251,16 +257,16 @@ def run_ours(args: argparse.Namespace) -> None:
         for i, L in enumerate(layers):
             layer_step(L, geo, None if cold == "device" else L.records_host)
             if world > 1:
-                dist.all_gather_into_tensor(gathered[i], L.out)
-                dist.all_gather_into_tensor(gathered_lse[i], L.lse)
-                K.lse_merge(gathered[i], gathered_lse[i], torch.bfloat16, out=finals[i])
+                L.packed.exchange()
+                L.packed.merge(torch.bfloat16, out=finals[i])
 
-    # Warm-up (also compiles nothing: the library is prebuilt) and graph capture of one step.
+    # Warm-up (also compiles nothing: the library is prebuilt) and graph capture of one step (the
+    # NCCL all-gathers are captured too at N > 1; the graph is released before the process group).
     for _ in range(n_warm):
         step()
     torch.cuda.synchronize()
     graph = None
-    if world == 1:
+    if True:
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -336,9 +342,8 @@ def run_ours(args: argparse.Namespace) -> None:
             layer_step(L, geo)
             src = L.out if world == 1 else finals[i]
             if world > 1:
-                dist.all_gather_into_tensor(gathered[i], L.out)
-                dist.all_gather_into_tensor(gathered_lse[i], L.lse)
-                K.lse_merge(gathered[i], gathered_lse[i], torch.bfloat16, out=finals[i])
+                L.packed.exchange()
+                L.packed.merge(torch.bfloat16, out=finals[i])
             o_host[i].copy_(src, non_blocking=True)
 
     for _ in range(2):
@@ -362,7 +367,7 @@ def run_ours(args: argparse.Namespace) -> None:
         "config": {"workload": "tiered decode hot path, Llama-3.2-1B attention (32q/8kv/d64), 131072-token context, bs 16, 25% budget (K=2046), 14 selecting layers, int8 cold tier in HBM",
                    "ctx": args.ctx, "block_size": BS, "k_blocks": geo["k_total"], "selecting_layers": n_sel, "batch": 1,
                    "cold_placement": "device", "l2": "inputs larger than L2 (~2.8 GB read per step)", "parallelism": f"context-sharded x{world}",
-                   "timing": "CUDA graph of one step, CUDA events" if graph is not None else "eager, CUDA events, max over ranks"},
+                   "timing": "CUDA graph of one step (NCCL all-gathers captured at N > 1), CUDA events, max over ranks"},
         "kernel_us": {k: round(v, 3) for k, v in kernel_us.items()},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"],
@@ -372,7 +377,7 @@ def run_ours(args: argparse.Namespace) -> None:
                                 "frac": round(layer_bytes / (us_layer * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)},
         "e2e": {"value": round(1e3 / e2e_ms, 3), "unit": "tokens/s", "h2d_bytes_per_step": n_sel * HQ * D * 2,
                 "d2h_bytes_per_step": n_sel * HQ * D * 2, "path": "lazykv_b200.kernels (C ABI) per layer, eager, host q in / host out"},
-        "gpu_launches": n_steps * n_sel * (LAUNCHES_PER_LAYER_STEP + (1 if world > 1 else 0)),
+        "gpu_launches": n_steps * n_sel * (LAUNCHES_PER_LAYER_STEP + (1 if world > 1 else 0)),  # + the merge kernel at N > 1 (NCCL's own kernels not counted)
         "clocks": clocks.summary(),
     }
 
@@ -404,6 +409,8 @@ def run_ours(args: argparse.Namespace) -> None:
     if rank == 0 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, budget_s=12.0)
     if world > 1:
+        del graph  # a graph holding NCCL work is released before its process group
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

@@ -251,6 +251,14 @@ int lkv_device_status(int* status, int clear);
 int lkv_lse_merge(const float* outs, const float* lses, int n_parts, int64_t rows, int d,
                   void* out, int out_dtype, float* lse_out, void* stream);
 
+/*
+ * lkv_lse_merge over partials packed as each rank sends them in one collective: part k at
+ * parts + k * rows * (d + 1) holds out [rows, d] then lse [rows] (the per-rank partials of a
+ * context-sharded step after an all-gather; no reference counterpart).
+ */
+int lkv_lse_merge_packed(const float* parts, int n_parts, int64_t rows, int d, void* out, int out_dtype,
+                         float* lse_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

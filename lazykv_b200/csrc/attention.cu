@@ -1332,21 +1332,21 @@ __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const flo
 }
 
 template <typename T>
-__global__ void lse_merge_kernel(const float* __restrict__ outs, const float* __restrict__ lses, int n_parts, int64_t rows, int d,
-                                 T* __restrict__ out, float* __restrict__ lse_out) {
+__global__ void lse_merge_kernel(const float* __restrict__ outs, int64_t out_stride, const float* __restrict__ lses, int64_t lse_stride, int n_parts,
+                                 int64_t rows, int d, T* __restrict__ out, float* __restrict__ lse_out) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= rows * d) return;
   const int64_t r = e / d;
   float M = -INFINITY;
-  for (int k = 0; k < n_parts; ++k) M = fmaxf(M, lses[k * rows + r]);
+  for (int k = 0; k < n_parts; ++k) M = fmaxf(M, lses[k * lse_stride + r]);
   float acc = 0.0f, lse = -INFINITY;
   if (M != -INFINITY) {
     float sum = 0.0f;
-    for (int k = 0; k < n_parts; ++k) sum += expf(lses[k * rows + r] - M);
+    for (int k = 0; k < n_parts; ++k) sum += expf(lses[k * lse_stride + r] - M);
     lse = M + logf(sum);
     for (int k = 0; k < n_parts; ++k) {
-      const float w = expf(lses[k * rows + r] - lse);
-      acc = fmaf(w, outs[(int64_t)k * rows * d + e], acc);
+      const float w = expf(lses[k * lse_stride + r] - lse);
+      acc = fmaf(w, outs[(int64_t)k * out_stride + e], acc);
     }
   }
   out[e] = from_f32<T>(acc);
@@ -1724,10 +1724,26 @@ int lkv_lse_merge(const float* outs, const float* lses, int n_parts, int64_t row
   const int64_t n = rows * d;
   const unsigned blocks = (unsigned)((n + 255) / 256);
   if (out_dtype == LKV_BF16)
-    lse_merge_kernel<__nv_bfloat16><<<blocks, 256, 0, as_stream(stream)>>>(outs, lses, n_parts, rows, d, static_cast<__nv_bfloat16*>(out), lse_out);
+    lse_merge_kernel<__nv_bfloat16><<<blocks, 256, 0, as_stream(stream)>>>(outs, rows * d, lses, rows, n_parts, rows, d,
+                                                                          static_cast<__nv_bfloat16*>(out), lse_out);
   else
-    lse_merge_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(outs, lses, n_parts, rows, d, static_cast<float*>(out), lse_out);
+    lse_merge_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(outs, rows * d, lses, rows, n_parts, rows, d, static_cast<float*>(out), lse_out);
   return launched("lkv_lse_merge");
+}
+
+int lkv_lse_merge_packed(const float* parts, int n_parts, int64_t rows, int d, void* out, int out_dtype, float* lse_out, void* stream) {
+  if (!dtype_ok(out_dtype)) return fail(LKV_ERR_ARG, "lkv_lse_merge_packed: bad dtype %d", out_dtype);
+  if (n_parts <= 0 || rows < 0 || d <= 0) return fail(LKV_ERR_ARG, "lkv_lse_merge_packed: bad shape");
+  if (parts == nullptr || out == nullptr) return fail(LKV_ERR_PTR, "lkv_lse_merge_packed: null pointer");
+  if (rows == 0) return LKV_OK;
+  const int64_t n = rows * d, stride = rows * (d + 1);
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  if (out_dtype == LKV_BF16)
+    lse_merge_kernel<__nv_bfloat16><<<blocks, 256, 0, as_stream(stream)>>>(parts, stride, parts + n, stride, n_parts, rows, d,
+                                                                          static_cast<__nv_bfloat16*>(out), lse_out);
+  else
+    lse_merge_kernel<float><<<blocks, 256, 0, as_stream(stream)>>>(parts, stride, parts + n, stride, n_parts, rows, d, static_cast<float*>(out), lse_out);
+  return launched("lkv_lse_merge_packed");
 }
 
 }  // extern "C"

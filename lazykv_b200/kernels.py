@@ -196,6 +196,19 @@ def lse_merge(outs: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtype = t
     return out, lse_out
 
 
+def lse_merge_packed(parts: torch.Tensor, rows: int, d: int, out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None,
+                     lse_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Merge partials packed per part as out [rows, d] then lse [rows] (parts [p, rows * (d + 1)], float32)."""
+    dev = require_cuda(parts)
+    p = parts.shape[0]
+    if parts.stride(-1) != 1 or parts.numel() != p * rows * (d + 1) or not parts.is_contiguous():
+        raise ValueError("lse_merge_packed: parts must be contiguous [p, rows * (d + 1)] float32")
+    out = torch.empty((rows, d), dtype=out_dtype, device=dev) if out is None else out
+    lse_out = torch.empty((rows,), dtype=torch.float32, device=dev) if lse_out is None else lse_out
+    call("lkv_lse_merge_packed", ptr(parts), p, rows, d, ptr(out), dtype_code(out.dtype), ptr(lse_out), stream_handle(dev))
+    return out, lse_out
+
+
 def bitmap_words(n_blocks: int) -> int:
     """uint32 words of a per-head block bitmap covering block ids [0, n_blocks)."""
     return max(1, math.ceil(n_blocks / 32))

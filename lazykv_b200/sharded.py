@@ -79,6 +79,26 @@ def merge_partials(outs: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtyp
     return K.lse_merge(outs.contiguous(), lses.contiguous(), out_dtype, out=out)
 
 
+class PackedPartial:
+    """A rank's partial as one buffer [rows * (d + 1)] float32: out [rows, d] then lse [rows] (both
+    contiguous views), so the exchange is one all-gather into [world, rows * (d + 1)] and the merge
+    reads the gathered buffer in place (lkv_lse_merge_packed)."""
+
+    def __init__(self, rows: int, d: int, world: int, device: torch.device) -> None:
+        self.rows, self.d = rows, d
+        self.buf = torch.zeros(rows * (d + 1), dtype=torch.float32, device=device)
+        self.out = self.buf[: rows * d].view(rows, d)
+        self.lse = self.buf[rows * d :]
+        self.gathered = torch.zeros((world, rows * (d + 1)), dtype=torch.float32, device=device)
+
+    def exchange(self, group: dist.ProcessGroup | None = None) -> None:
+        dist.all_gather_into_tensor(self.gathered, self.buf, group=group)
+
+    def merge(self, out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+        merged, _ = K.lse_merge_packed(self.gathered, self.rows, self.d, out_dtype, out=out)
+        return merged
+
+
 def gather_candidates(ids: torch.Tensor, bounds: torch.Tensor, group: dist.ProcessGroup | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Every rank's local candidates (ids [h, k] int32, ascending; bounds [h, k] float32) as
     [h, world * k] in rank order, i.e. ascending id across the node (ranks hold ascending ranges)."""
@@ -161,12 +181,16 @@ class ShardedExactStep:
                                  out_dtype=torch.float32, out=out, lse=lse)
 
     def step(self, query: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
-        """Select, attend, all-gather the partials, merge: the layer's output [hq, d] on every rank."""
+        """Select, attend, all-gather the partials (one collective), merge: the layer's output
+        [hq, d] on every rank."""
+        hq = query.shape[-3] if query.dim() == 4 else query.shape[0]
+        if getattr(self, "_packed", None) is None:
+            self._packed = PackedPartial(hq, self.d, dist.get_world_size(self.group), query.device)
+        pk = self._packed
         self.select_local(query)
-        o, l = self.attend(query)
-        outs, lses = gather_partials(o, l, self.group)
-        merged, _ = merge_partials(outs, lses, out_dtype)
-        return merged
+        self.attend(query, out=pk.out, lse=pk.lse)
+        pk.exchange(self.group)
+        return pk.merge(out_dtype)
 
 
 def host_reference_global_topk(ids: np.ndarray, bounds: np.ndarray, k: int) -> np.ndarray:
