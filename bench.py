@@ -225,7 +225,7 @@ def layer_step(L, geo: dict, cold_store=None, events: list | None = None) -> Non
     mark()
 
 
-LAUNCHES_PER_LAYER_STEP = 4  # score (+ first radix pass), cluster select, attention partials (hot and cold), combine
+LAUNCHES_PER_LAYER_STEP = 3  # score (+ first radix pass), cluster select, attention (both passes; the head's last CTA folds)
 
 
 def run_ours(args: argparse.Namespace) -> None:
@@ -304,17 +304,33 @@ def run_ours(args: argparse.Namespace) -> None:
     us_layer = ms_step * 1e3 / n_sel
     tokens_per_s = 1e3 / ms_step
 
-    # Per-kernel durations (eager, events on the launching stream), averaged over steps.
+    # Per-kernel durations: each kernel group (selection: score + select; attention) captured alone
+    # over every layer in its own CUDA graph and replayed back to back, timed with CUDA events on
+    # the replaying stream, per layer-step (the local part at N > 1: no exchange).
     names = ["select", "attention"]
-    per_kernel = {n: [] for n in names}
-    for _ in range(max(3, min(n_steps, 10))):
+
+    def sel_only() -> None:
         for L in layers:
-            ev: list = []
-            layer_step(L, geo, None, ev)
-            torch.cuda.synchronize()
-            for n, (e0, e1) in zip(names, zip(ev[:-1], ev[1:])):
-                per_kernel[n].append(e0.elapsed_time(e1) * 1e3)
-    kernel_us = {n: statistics.median(v) for n, v in per_kernel.items()}
+            K.quest_topk(L.q, L.kmin, L.kmax, geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["k_local"],
+                         out_blocks=L.list[:, geo["sel_off"] : geo["sel_off"] + geo["k_local"]], bitmap=L.bitmap, by_block=True)
+
+    def attn_only() -> None:
+        for L in layers:
+            K.exact_attention(L.q, L.pool, L.pool[:, :, 1], (HKV * 2 * BS * D, 2 * BS * D, D), L.list, BS, L.records, geo["cand_lo"] - geo["lo"],
+                              geo["n_cand"], geo["scale"], BS, excluded=L.bitmap, slot_of=L.slot_of, out=L.out, lse=L.lse)
+
+    kernel_us = {}
+    for n, fn in zip(names, (sel_only, attn_only)):
+        fn()
+        torch.cuda.synchronize()
+        g_k = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_k):
+            fn()
+        for _ in range(3):
+            g_k.replay()
+        reps = max(5, n_steps)
+        kernel_us[n] = timed(g_k.replay, reps) / reps * 1e3 / len(layers)  # max over ranks at N > 1
+        del g_k
 
     peaks = load_peaks()
     k_local = geo["k_local"]

@@ -237,7 +237,9 @@ int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32
 
 /*
  * Status word of the kernels that wait on shared-memory barriers (bounded waits): 0 when no wait
- * ran out, else the first code recorded (1 = a wait timed out). Synchronous; clears it if asked.
+ * ran out, else the first code recorded (1 = a wait timed out; 2 = an attention CTA's item list
+ * overflowed its shared memory, a sizing error that leaves that call's output empty). Synchronous;
+ * clears it if asked.
  * No reference counterpart (the reference has no device-side waits).
  */
 int lkv_device_status(int* status, int clear);

@@ -10,13 +10,17 @@
 //    bitmap, read from int8 records with the dequantisation fused (quant.py:103-104: float32
 //    affine, then rounded to the model dtype, i.e. what a fetch puts in a slot), or from pairs in
 //    the model dtype.
-// Each CTA takes a chunk of one segment's items for one KV head and emits an online-softmax partial
-// (running max m in the log2 domain, sum l, unnormalised o) for the head's G query rows. A combine
-// kernel folds the chunks into per-segment (out = o / l, lse) and into their merge. A partial over
-// no key is (m = -inf, l = 0), which the combine turns into lse = -inf and out = 0, as
+// Each CTA takes a share of the items of one KV head and emits online-softmax partials (running
+// max m in the log2 domain, sum l, unnormalised o) for the head's G query rows, per segment; the
+// partials are folded into per-segment (out = o / l, lse) and into their merge. A partial over no
+// key is (m = -inf, l = 0), which the fold turns into lse = -inf and out = 0, as
 // cpu_partial_attention does (exact.py:108-110).
 //
-// Two kernels do the partial work:
+// Three kernels do the partial work:
+//  * attn_stream_kernel (bf16, d 64, bs 16, G <= 8, stores in device memory: the metric geometry):
+//    tensor-core contractions, int8 records dequantised straight into mma fragments, a balanced
+//    split of every segment over one 16-warp CTA per SM, and the fold done by the head's last CTA
+//    (no second launch); described at the kernel;
 //  * attn_tma_kernel (stores in device memory, G = 4, bs = 16, d in {64, 128}): each warp streams
 //    its items through a private ring of shared-memory stages filled by TMA bulk copies
 //    (cp.async.bulk, one mbarrier per stage, bounded waits); the block ids, slot rows and exclusion
@@ -24,7 +28,8 @@
 //    global load; dot products and accumulations use packed float32x2 FMAs;
 //  * attn_ldg_kernel (any other geometry, and stores in mapped host memory read over the link):
 //    the same arithmetic with vectorised loads straight from global memory.
-// Lane layout in a warp: CG = d/16 channel groups x TL = 32/CG token lanes; a lane holds 16
+// The last two emit one partial per CTA and a combine kernel folds them.
+// Lane layout (CUDA-core kernels) in a warp: CG = d/16 channel groups x TL = 32/CG token lanes; a lane holds 16
 // channels of the G query rows and of its accumulators and takes tokens tl, tl + TL, ... of a block.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -746,37 +751,23 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
 }
 
 // ============================================================================================
-// attn_mma_kernel: tensor-core split decode (bf16, d = 64, bs = 16, G <= 8), stores in device memory
+// tensor-core helpers (bf16, d = 64, bs = 16)
 // ============================================================================================
 //
 // Per item (one block of one KV head) a warp runs two small contractions on the tensor cores with
 // mma.sync.m16n8k16 (bf16 operands, float32 accumulators):
 //   S^T [16 tokens x 8 rows]   = K [16 x 64] . Q^T [64 x 8]      (4 k-steps; rows >= G are zero)
 //   O^T [64 channels x 8 rows] += V^T [64 x 16] . P^T [16 x 8]   (4 m-tiles)
-// K and V reach shared memory as bf16 tiles of 16 rows x 128 bytes in the 128-byte swizzle
-// (16-byte chunk c of row r stored at chunk c ^ (r & 7)), so ldmatrix reads them without bank
-// conflicts: hot blocks and cold pairs by tensor-map TMA loads (cp.async.bulk.tensor, SWIZZLE_128B),
-// int8 cold records by a bulk copy of the raw record that the warp dequantises into its own tile
-// (float32 affine of quant.py:103-104, rounded to bf16: what a fetch puts in a slot). The products
-// of bf16 operands are exact in float32; P (float32) enters the second contraction as the sum of
-// three bf16 terms (hi + mid + lo, 24 significant bits), each a separate MMA, so the result keeps
-// float32 accuracy. The score fragment becomes the P^T operand with movmatrix (an 8x8 transpose in
-// registers). Softmax bookkeeping follows the CUDA-core kernels: log2 domain, lazy rescaling.
+// bf16 K and V tiles reach shared memory as 16 rows x 128 bytes in the 128-byte swizzle (16-byte
+// chunk c of row r stored at chunk c ^ (r & 7)) by tensor-map TMA loads, so ldmatrix reads them
+// without bank conflicts. The products of bf16 operands are exact in float32; P (float32) enters
+// the second contraction as the sum of three bf16 terms (hi + mid + lo, 24 significant bits), each
+// a separate MMA, so the result keeps float32 accuracy. The score fragment becomes the P^T operand
+// with movmatrix (an 8x8 transpose in registers).
 
-constexpr int kMmaWarps = 4;
-constexpr int kMmaThreads = 32 * kMmaWarps;
-constexpr int kMmaStages = 2;
-constexpr int kMmaTile = 2048;                  // 16 x 64 bf16, swizzled
-constexpr int kMmaHotStage = 2 * kMmaTile;      // K tile + V tile
-constexpr int kMmaRec = 2368;                   // int8 record at bs 16, d 64
-constexpr int kMmaRecStage = 2432;              // record stage stride (a multiple of 128 bytes)
-constexpr int kMmaCtasPerSm = 6;
-constexpr int kMmaTargetCtas = kMmaCtasPerSm * kNumSMs;
-constexpr int kMmaHotBody = kMmaWarps * kMmaStages * kMmaHotStage;                            // hot / pairs stages
-constexpr int kMmaColdBody = kMmaWarps * 2 * kMmaTile + kMmaWarps * kMmaStages * kMmaRecStage;  // tiles + record stages
-constexpr int kMmaBody = kMmaHotBody > kMmaColdBody ? kMmaHotBody : kMmaColdBody;
-static_assert(kMmaBody >= kMmaWarps * 8 * 64 * 4 + kMmaWarps * 2 * 8 * 4, "epilogue scratch exceeds the body");
-constexpr size_t kMmaSmem = 1024 + kMmaBody + kMmaWarps * kMmaStages * 8;
+constexpr int kMmaTile = 2048;              // 16 x 64 bf16, swizzled
+constexpr int kMmaHotStage = 2 * kMmaTile;  // K tile + V tile
+constexpr int kMmaRec = 2368;               // int8 record at bs 16, d 64
 
 struct MmaParams {
   AttnParams p;
@@ -840,124 +831,312 @@ __device__ __forceinline__ void split3(float a, float b, uint32_t& hi, uint32_t&
   lo = pack_bf2(r2.x, r2.y);
 }
 
-// 8 int8 codes -> 4 float2 of (code + 128), exactly (2^23 magic, as codes16).
-__device__ __forceinline__ void codes8(uint2 w, float2 (&u)[4]) {
-  const uint32_t a = w.x ^ 0x80808080u, b = w.y ^ 0x80808080u;
-  const float2 mm = f2(-8388608.0f, -8388608.0f);
-  u[0] = __fadd2_rn(f2(__uint_as_float(__byte_perm(a, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(a, 0x4b000000u, 0x7651))), mm);
-  u[1] = __fadd2_rn(f2(__uint_as_float(__byte_perm(a, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(a, 0x4b000000u, 0x7653))), mm);
-  u[2] = __fadd2_rn(f2(__uint_as_float(__byte_perm(b, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(b, 0x4b000000u, 0x7651))), mm);
-  u[3] = __fadd2_rn(f2(__uint_as_float(__byte_perm(b, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(b, 0x4b000000u, 0x7653))), mm);
-}
-
 __device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
 
-// Dequantises the int8 record at `raw` (kq | vq | k_scale | k_zero | v_scale | v_zero, bs 16, d 64)
-// into bf16 K and V tiles in the swizzled layout. Lane: channel group gq = lane & 7 (8 channels),
-// tokens 4 * (lane >> 3) + i, i = 0..3. Each value is (code + 128) * scale + zero in float32 (one
-// rounding, as quant.py's unpack), then rounded to bf16.
-__device__ __forceinline__ void dequant_record(const unsigned char* raw, unsigned char* kt, unsigned char* vt, int lane) {
-  const int gq = lane & 7, t0 = 4 * (lane >> 3);
-  // Swizzled chunk offsets of tokens t0 + i: t0 & 7 is 0 or 4, so (t & 7) = (t0 & 7) + i.
-  uint32_t dst[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) dst[i] = (uint32_t)((t0 + i) * 128 + ((gq ^ ((t0 & 7) + i)) << 4));
-  float2 ks2[4], kz2[4];
-  {
-    const uint4 a = *reinterpret_cast<const uint4*>(raw + 2048 + 16 * gq);
-    const uint4 b = *reinterpret_cast<const uint4*>(raw + 2048 + 128 + 16 * gq);
-    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int x = 0; x < 4; ++x) {
-      ks2[x] = __half22float2(*reinterpret_cast<const __half2*>(&wa[x]));
-      kz2[x] = __half22float2(*reinterpret_cast<const __half2*>(&wb[x]));
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 u[4];
-    codes8(*reinterpret_cast<const uint2*>(raw + (t0 + i) * 64 + 8 * gq), u);
-    float2 k[4];
-#pragma unroll
-    for (int x = 0; x < 4; ++x) k[x] = __ffma2_rn(u[x], ks2[x], kz2[x]);
-    uint4 o;
-    o.x = pack_bf2(k[0].x, k[0].y);
-    o.y = pack_bf2(k[1].x, k[1].y);
-    o.z = pack_bf2(k[2].x, k[2].y);
-    o.w = pack_bf2(k[3].x, k[3].y);
-    *reinterpret_cast<uint4*>(kt + dst[i]) = o;
-  }
-  // Per-token V scales of tokens t0..t0+3: four f16 each, one 8-byte load.
-  const uint2 vsw = *reinterpret_cast<const uint2*>(raw + 2304 + 2 * t0);
-  const uint2 vzw = *reinterpret_cast<const uint2*>(raw + 2336 + 2 * t0);
-  const float2 vs01 = __half22float2(*reinterpret_cast<const __half2*>(&vsw.x)), vs23 = __half22float2(*reinterpret_cast<const __half2*>(&vsw.y));
-  const float2 vz01 = __half22float2(*reinterpret_cast<const __half2*>(&vzw.x)), vz23 = __half22float2(*reinterpret_cast<const __half2*>(&vzw.y));
-  const float vs[4] = {vs01.x, vs01.y, vs23.x, vs23.y}, vz[4] = {vz01.x, vz01.y, vz23.x, vz23.y};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 vs2 = f2(vs[i], vs[i]), vz2 = f2(vz[i], vz[i]);
-    float2 u[4];
-    codes8(*reinterpret_cast<const uint2*>(raw + 1024 + (t0 + i) * 64 + 8 * gq), u);
-    float2 v[4];
-#pragma unroll
-    for (int x = 0; x < 4; ++x) v[x] = __ffma2_rn(u[x], vs2, vz2);
-    uint4 o;
-    o.x = pack_bf2(v[0].x, v[0].y);
-    o.y = pack_bf2(v[1].x, v[1].y);
-    o.z = pack_bf2(v[2].x, v[2].y);
-    o.w = pack_bf2(v[3].x, v[3].y);
-    *reinterpret_cast<uint4*>(vt + dst[i]) = o;
-  }
-}
+// ============================================================================================
+// attn_stream_kernel: balanced, warp-streaming tensor-core split decode
+// (bf16, d = 64, bs = 16, G <= 8, stores in device memory)
+// ============================================================================================
+//
+// Grid: P CTAs per KV head (P = kStreamCtasPerSm x SMs / h, raised when a CTA's items would not
+// fit its list), kStreamWarps warps per CTA.
+//
+// Work split. A head's items are, per segment, the listed blocks (padding counted, then skipped)
+// or the blocks of the range that the exclusion bitmap leaves. CTA i of P takes the i-th P-th of
+// every segment's items: every CTA gets the same mix of bf16 tile pairs and int8 records whatever
+// the selection left in the range. One CTA per SM, so no CTA waits on another for issue slots.
+//
+// Set-up (whole CTA): the range's items are counted by a popcount over the bitmap; the CTA's items
+// are written to a shared-memory list as storage rows (list ids through the slot map; range blocks
+// as the complement of the bitmap, placed by a block-wide scan of per-word counts).
+// Streaming (each warp): warp w takes the w-th share of the CTA's items of each segment (segment 0's
+// first); its items pass through its private ring of StreamCfg::STAGES 4 KiB stages that lane 0 fills
+// by TMA (two tile-mode loads of the K and V tiles in the 128-byte swizzle, or one bulk
+// copy of the record) and refills as soon as the item in a stage has been used.
+//
+// Int8 records go from shared memory straight into mma fragments, with a fixed permutation of the
+// channels (the contraction does not depend on the order): for S^T = K . Q^T lane (g, t) holds the
+// 16 channels 16t .. 16t+15 of tokens g and g + 8 (two 16-byte code loads, the K scales of those
+// channels); for O^T += V^T . P^T lane g holds channels 8g .. 8g+7 of tokens 2t, 2t+1, 2t+8, 2t+9
+// (four 8-byte loads). The query fragments follow the same permutation and the output channels are
+// put back in order when the state is parked. Each value is (code + 128) * scale + zero in float32
+// (one rounding) and then rounded to bf16: what a fetch would put in a slot (quant.py:103-104).
+//
+// Each warp keeps one online-softmax state (log2 domain, lazy rescaling) and parks it in shared
+// memory when its items move to the next segment and at the end (then in the idle ring); the CTA
+// folds its warps' parked
+// states into one partial per segment in the workspace; the last CTA of the head (a per-head counter
+// in the workspace, zero before and after the call) folds the head's partials into the outputs.
+
+constexpr int kStreamWarps = 16;
+constexpr int kStreamThreads = 32 * kStreamWarps;
+constexpr int kStreamCtasPerSm = 1;
+constexpr int kStreamStage = 4096;
+constexpr int kStreamListCap = 3072;       // items per CTA
+constexpr int kStreamCounterBytes = 4096;  // per-head CTA counters at the workspace start (h <= 1024)
 
 template <int G>
-__global__ void __launch_bounds__(kMmaThreads, kMmaCtasPerSm) attn_mma_kernel(const __grid_constant__ MmaParams mp) {
-  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query group");
-  constexpr int D = 64, BS = 16;
-  const AttnParams& p = mp.p;
-  extern __shared__ unsigned char smem_raw[];
-  __shared__ int sh_bad;
-  unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g = lane >> 2, t = lane & 3;
-  const int j = blockIdx.y;
-  int split = blockIdx.x, si = 0;
-  if (p.n_segs > 1 && split >= p.seg[0].n_splits) {
-    si = 1;
-    split -= p.seg[0].n_splits;
-  }
-  const Seg& S = p.seg[si];
-  const bool list = S.kind == SEG_LIST;
-  const bool rec = S.kind == SEG_RANGE_REC;
-  const CUtensorMap* tk = &mp.tk[si];
-  const CUtensorMap* tv = &mp.tv[si];
-  const bool head_major = mp.head_major[si] != 0;
+struct StreamCfg {
+  static constexpr int STAGES = G <= 4 ? 3 : 2;  // per warp
+  static constexpr int SLOT = G * 64 + 2 * G;    // floats of a parked state: o [G][64], m [G], l [G]
+  static constexpr int RING = kStreamWarps * STAGES * kStreamStage;
+  static constexpr int PARK = kStreamWarps * SLOT * 4;  // a warp's state of segment 0 when it moves on
+  static constexpr int LIST = kStreamListCap * 4;
+  static constexpr int BARS = kStreamWarps * STAGES * 8;
+  static constexpr int SITEM = kStreamWarps * STAGES * 4;  // list index held by each stage
+  static constexpr size_t SMEM = 1024 + (size_t)RING + PARK + LIST + BARS + SITEM;
+  // Floats of one (CTA, set) partial in the workspace: o [G][64], m [G], l [G], padded to 16 bytes so
+  // the rows of o are float4-aligned for every G.
+  static constexpr int PART = (G * 64 + 2 * G + 3) / 4 * 4;
+  static_assert(kStreamWarps * 2 * SLOT * 4 <= RING, "final parked states live in the ring");
+};
 
-  // Shared memory: hot/pairs segments use kMmaStages stages of (K tile, V tile) per warp; record
-  // segments a (K tile, V tile) pair per warp followed by kMmaStages raw record stages per warp.
-  unsigned char* tiles = smem + warp * 2 * kMmaTile;  // record segments only
-  unsigned char* stage0 = rec ? smem + kMmaWarps * 2 * kMmaTile + warp * kMmaStages * kMmaRecStage : smem + warp * kMmaStages * kMmaHotStage;
-  const int stage_stride = rec ? kMmaRecStage : kMmaHotStage;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kMmaBody) + warp * kMmaStages;
-  if (threadIdx.x == 0) sh_bad = 0;
+struct StreamParams {
+  AttnParams p;              // segments in item order; segment s's partials are set s
+  CUtensorMap tk[2], tv[2];  // K / V maps of tile segments
+  int head_major[2];
+  int per_head;              // P
+  unsigned int* counters;    // [h]: zero on entry, left zero
+  float* part;               // [h][P][2][PART]: o [G][D], m [G], l [G] per (CTA, set)
+  void* out;                 // [hq, D] in TO (optional)
+  float* lse;                // [hq] (optional)
+  float* seg_out;            // [2, hq, D] (optional)
+  float* seg_lse;            // [2, hq] (optional)
+};
+
+// In-range blocks of bitmap word w that the exclusion bitmap of head j leaves.
+__device__ __forceinline__ uint32_t range_word_bits(const Seg& S, int j, int w) {
+  const int f = S.first_block, e = S.first_block + S.n_items;  // blocks [f, e)
+  const int lo = max(f, 32 * w) - 32 * w, hi = min(e, 32 * w + 32) - 32 * w;
+  if (hi <= lo) return 0u;
+  const uint32_t in = (hi - lo == 32 ? 0xffffffffu : ((1u << (hi - lo)) - 1u)) << lo;
+  const uint32_t ex = (S.excluded != nullptr && w < S.bitmap_words) ? __ldg(S.excluded + (int64_t)j * S.bitmap_words + w) : 0u;
+  return in & ~ex;
+}
+
+// Block-wide exclusive prefix sum of v (every thread of the CTA calls it); *total gets the sum.
+__device__ __forceinline__ int block_excl_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += u;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int s = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, s, off);
+      if (lane >= off) s += u;
+    }
+    if (lane < nw) warp_sums[lane] = s;  // inclusive
+    if (lane == nw - 1) *total = s;
+  }
+  __syncthreads();
+  const int before = (warp > 0 ? warp_sums[warp - 1] : 0) + incl - v;
+  __syncthreads();  // warp_sums may be reused right after
+  return before;
+}
+
+// 4 int8 codes (one word) -> (code + 128) as 4 floats (exact: 2^23 magic).
+__device__ __forceinline__ void codes4(uint32_t w, float2& lo, float2& hi) {
+  const uint32_t a = w ^ 0x80808080u;
+  const float2 mm = f2(-8388608.0f, -8388608.0f);
+  lo = __fadd2_rn(f2(__uint_as_float(__byte_perm(a, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(a, 0x4b000000u, 0x7651))), mm);
+  hi = __fadd2_rn(f2(__uint_as_float(__byte_perm(a, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(a, 0x4b000000u, 0x7653))), mm);
+}
+
+// (code + 128) of byte `sel` of words a and c (already xor-ed with 0x80808080), as a float pair.
+__device__ __forceinline__ float2 code_pair(uint32_t a, uint32_t c, uint32_t sel) {
+  return __fadd2_rn(f2(__uint_as_float(__byte_perm(a, 0x4b000000u, sel)), __uint_as_float(__byte_perm(c, 0x4b000000u, sel))),
+                    f2(-8388608.0f, -8388608.0f));
+}
+
+__device__ __forceinline__ float2 h2f2(uint32_t w) { return __half22float2(*reinterpret_cast<const __half2*>(&w)); }
+
+template <int G, typename TO>
+__global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_kernel(const __grid_constant__ StreamParams sp) {
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query group");
+  using C = StreamCfg<G>;
+  constexpr int D = 64;
+  constexpr int NW = kStreamWarps;
+  constexpr int NS = C::STAGES;
+  const AttnParams& p = sp.p;
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ int sh_bad, sh_last, sh_total, sh_lo[2];
+  __shared__ int warp_sums[32];
+  __shared__ uint64_t fold_bar;  // the last CTA's bulk copy of the head's partials
+  unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  unsigned char* ring = smem;
+  float* park = reinterpret_cast<float*>(smem + C::RING);
+  int* list = reinterpret_cast<int*>(smem + C::RING + C::PARK);
+  uint64_t* bars_all = reinterpret_cast<uint64_t*>(smem + C::RING + C::PARK + C::LIST);
+  int* stage_item = reinterpret_cast<int*>(smem + C::RING + C::PARK + C::LIST + C::BARS);
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = blockIdx.y, ci = blockIdx.x, P = sp.per_head;
+  uint64_t* bars = bars_all + warp * NS;
+  if (threadIdx.x == 0) {
+    sh_bad = 0;
+    mbar_init(&fold_bar, 1);
+  }
   if (lane == 0) {
 #pragma unroll
-    for (int s = 0; s < kMmaStages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < NS; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
+  }
+
+  // ---- set-up: counts, this CTA's item range, its list of storage rows ----
+  // A list segment's count is its length; a range's is a popcount over the bitmap. In the common
+  // case (segment 0 a list, segment 1 a range of at most kSetupWords words per thread) the list's
+  // loads are issued first and the range is listed in one pass over the bitmap while they fly.
+  constexpr int kSetupWords = 1;
+  const Seg& S0 = p.seg[0];
+  const Seg& S1 = p.seg[1];
+  const bool fast = p.n_segs == 2 && S0.kind == SEG_LIST && S1.kind != SEG_LIST &&
+                    (S1.n_items <= 0 || (S1.first_block + S1.n_items - 1) / 32 - S1.first_block / 32 < kSetupWords * kStreamThreads);
+  int64_t cnt0 = 0, cnt1 = 0, la0 = 0, lb0 = 0, la1 = 0, lb1 = 0;
+  int n_a = 0, n_b = 0;
+  if (fast) {
+    cnt0 = S0.n_items;
+    la0 = cnt0 * ci / P;
+    lb0 = cnt0 * (ci + 1) / P;
+    n_a = (int)(lb0 - la0);
+    // The list's first kStreamThreads items: id, then slot row (dependent loads, in flight during the scan).
+    int hot_row = -1;
+    const int64_t hit = la0 + threadIdx.x;
+    if (hit < lb0) {
+      const int blk = __ldg(S0.blocks + (int64_t)j * S0.n_list + hit);
+      int64_t row = blk < 0 ? -1 : (S0.slot_of != nullptr ? __ldg(S0.slot_of + (int64_t)j * S0.slot_stride + blk) : blk);
+      hot_row = row >= S0.n_rows ? -1 : (int)row;
+    }
+    // The range: this thread's kSetupWords consecutive words, their counts, a block-wide scan.
+    uint32_t bits[kSetupWords];
+    int mine = 0;
+    const int w0 = S1.first_block / 32 + threadIdx.x * kSetupWords;
+#pragma unroll
+    for (int k = 0; k < kSetupWords; ++k) {
+      bits[k] = S1.n_items > 0 ? range_word_bits(S1, j, w0 + k) : 0u;
+      mine += __popc(bits[k]);
+    }
+    const int before = block_excl_scan(mine, warp_sums, &sh_total);
+    cnt1 = sh_total;
+    la1 = cnt1 * ci / P;
+    lb1 = cnt1 * (ci + 1) / P;
+    n_b = (int)(lb1 - la1);
+    if (n_a + n_b <= kStreamListCap) {
+      int64_t ord = before;
+#pragma unroll
+      for (int k = 0; k < kSetupWords; ++k) {
+        uint32_t b = bits[k];
+        if (ord + __popc(b) <= la1 || ord >= lb1) {
+          ord += __popc(b);
+          continue;
+        }
+        while (b != 0u) {
+          const int bit = __ffs(b) - 1;
+          b &= b - 1u;
+          if (ord >= la1 && ord < lb1) {
+            const int blk = 32 * (w0 + k) + bit;
+            list[n_a + (ord - la1)] = S1.kind == SEG_RANGE_REC ? blk : (blk < S1.n_rows ? blk : -1);
+          }
+          ++ord;
+        }
+      }
+      if (hit < lb0) list[threadIdx.x] = hot_row;
+      for (int64_t it = lb0 > la0 + kStreamThreads ? la0 + kStreamThreads + threadIdx.x : lb0; it < lb0; it += blockDim.x) {
+        const int blk = __ldg(S0.blocks + (int64_t)j * S0.n_list + it);
+        int64_t row = blk < 0 ? -1 : (S0.slot_of != nullptr ? __ldg(S0.slot_of + (int64_t)j * S0.slot_stride + blk) : blk);
+        list[it - la0] = row >= S0.n_rows ? -1 : (int)row;
+      }
+    }
+  } else {
+    for (int s = 0; s < p.n_segs; ++s) {
+      const Seg& S = p.seg[s];
+      int64_t c = S.n_items;
+      if (S.kind != SEG_LIST && S.n_items > 0) {
+        const int w0 = S.first_block / 32, w1 = (S.first_block + S.n_items - 1) / 32;
+        int mine = 0;
+        for (int w = w0 + threadIdx.x; w <= w1; w += blockDim.x) mine += __popc(range_word_bits(S, j, w));
+        block_excl_scan(mine, warp_sums, &sh_total);
+        c = sh_total;
+      }
+      if (s == 0) cnt0 = c; else cnt1 = c;
+    }
+    // This CTA's share of each segment (ordinals [la, lb)); the list holds segment 0's items first.
+    la0 = cnt0 * ci / P;
+    lb0 = cnt0 * (ci + 1) / P;
+    la1 = cnt1 * ci / P;
+    lb1 = cnt1 * (ci + 1) / P;
+    n_a = (int)(lb0 - la0);
+    n_b = (int)(lb1 - la1);
+    if (n_a + n_b <= kStreamListCap) {
+      for (int s = 0; s < p.n_segs; ++s) {
+        const Seg& S = p.seg[s];
+        const int64_t la = s == 0 ? la0 : la1, lb = s == 0 ? lb0 : lb1;
+        int* dst = list + (s == 0 ? 0 : n_a);
+        if (la >= lb) continue;
+        if (S.kind == SEG_LIST) {
+          for (int64_t it = la + threadIdx.x; it < lb; it += blockDim.x) {
+            const int blk = __ldg(S.blocks + (int64_t)j * S.n_list + it);
+            int64_t row = blk < 0 ? -1 : (S.slot_of != nullptr ? __ldg(S.slot_of + (int64_t)j * S.slot_stride + blk) : blk);
+            if (row >= S.n_rows) row = -1;  // outside the tensor maps: nothing to load
+            dst[it - la] = (int)row;
+          }
+        } else {
+          // Ordinal of each word's first kept block by a block-wide scan, chunk by chunk.
+          const int w0 = S.first_block / 32, w1 = (S.first_block + S.n_items - 1) / 32;
+          int64_t run = 0;
+          for (int c0 = w0; c0 <= w1 && run < lb; c0 += blockDim.x) {
+            const int w = c0 + threadIdx.x;
+            uint32_t bits = w <= w1 ? range_word_bits(S, j, w) : 0u;
+            const int before = block_excl_scan(__popc(bits), warp_sums, &sh_total);
+            int64_t ord = run + before;
+            while (bits != 0u && ord < lb) {
+              const int b = __ffs(bits) - 1;
+              bits &= bits - 1u;
+              if (ord >= la) dst[ord - la] = S.kind == SEG_RANGE_REC ? 32 * w + b : (32 * w + b < S.n_rows ? 32 * w + b : -1);
+              ++ord;
+            }
+            run += sh_total;
+          }
+        }
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    sh_lo[0] = (int)la0;
+    sh_lo[1] = (int)la1;
+    if (n_a + n_b > kStreamListCap) {  // the host sizes P so that this cannot happen
+      sh_bad = 2;
+      atomicCAS(&g_device_status, 0, LKV_DEV_LIST_OVERFLOW);
+    }
   }
   __syncthreads();
 
-  // Q^T fragments (bf16, exact): b0 = q[g][16ks + 2t .. +1], b1 = q[g][16ks + 2t + 8 .. +9].
-  uint32_t bq[4][2];
+  // ---- streaming: this warp's share of the list ----
+  // Its items: list[ha, ha + hn) of segment 0, then list[n_a + ca, n_a + ca + cn) of segment 1. The
+  // split is fixed, so a call's result does not depend on timing.
+  const int ha = n_a * warp / NW, hn = sh_bad ? 0 : n_a * (warp + 1) / NW - ha;
+  const int ca = n_b * warp / NW, cn = sh_bad ? 0 : n_b * (warp + 1) / NW - ca;
+  const int n_mine = hn + cn;
+  auto list_index = [&](int k) { return k < hn ? ha + k : n_a + ca + (k - hn); };
+
+  const int g = lane >> 2, t = lane & 3;
+  uint32_t bq[4][2], bqp[4][2];
   {
     const uint32_t* q = reinterpret_cast<const uint32_t*>(static_cast<const __nv_bfloat16*>(p.q) + ((int64_t)j * G + (g < G ? g : 0)) * D);
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
       bq[ks][0] = g < G ? q[(16 * ks + 2 * t) / 2] : 0u;
       bq[ks][1] = g < G ? q[(16 * ks + 2 * t + 8) / 2] : 0u;
+      bqp[ks][0] = g < G ? q[(16 * t + 4 * ks) / 2] : 0u;
+      bqp[ks][1] = g < G ? q[(16 * t + 4 * ks + 2) / 2] : 0u;
     }
   }
-  // ldmatrix lane offsets within a tile: K (non-transposed, k-step ks) and V (transposed, m-tile mt).
   uint32_t koff[4], voff[4];
   {
     const int i = lane >> 3, r7 = lane & 7;
@@ -967,263 +1146,414 @@ __global__ void __launch_bounds__(kMmaThreads, kMmaCtasPerSm) attn_mma_kernel(co
       voff[x] = swz(r7 + 8 * (i >> 1), 2 * x + (i & 1));
     }
   }
+  unsigned char* stage0 = ring + warp * NS * kStreamStage;
+  int* my_items = stage_item + warp * NS;
+  // Lane 0 fills stage s with list item i (or arrives for a padding item).
+  auto issue = [&](int i, int s) {
+    if (lane != 0) return;
+    my_items[s] = i;
+    const int set = i < n_a ? 0 : 1;
+    const Seg& S = p.seg[set];
+    const int row = list[i];
+    if (row < 0) {
+      mbar_arrive(&bars[s]);
+      return;
+    }
+    unsigned char* dst = stage0 + s * kStreamStage;
+    if (S.kind == SEG_RANGE_REC) {
+      mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaRec);
+      tma_load_1d(dst, S.records + ((int64_t)row * p.h + j) * S.width, (uint32_t)kMmaRec, &bars[s]);
+    } else {
+      mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaHotStage);
+      const int hm = sp.head_major[set];
+      const int c2 = hm ? j : row, c3 = hm ? row : j;
+      tma_load_4d(smem_u32(dst), &sp.tk[set], 0, 0, c2, c3, &bars[s]);
+      tma_load_4d(smem_u32(dst + kMmaTile), &sp.tv[set], 0, 0, c2, c3, &bars[s]);
+    }
+  };
+  int n_issued = 0;
+#pragma unroll 1
+  for (int s = 0; s < NS && s < n_mine; ++s) {
+    issue(list_index(s), s);
+    ++n_issued;
+  }
 
   float o[4][4];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
     for (int b = 0; b < 4; ++b) o[a][b] = 0.0f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-
-  const int begin = split * S.chunk;
-  const int end = min(S.n_items, begin + S.chunk);
-  uint32_t excl_word = 0;
-  const int w0 = (S.first_block + begin) / 32;
-  if (!list) {
-    const int w = w0 + lane;
-    excl_word = (S.excluded != nullptr && w < S.bitmap_words && w * 32 < S.first_block + end)
-                    ? __ldg(S.excluded + (int64_t)j * S.bitmap_words + w) : 0u;
-  }
-  auto next_item = [&](int it) -> int {
-    if (list) return it < end ? it : end;
-    while (it < end) {
-      const int blk = S.first_block + it;
-      const int wi = blk / 32 - w0;
-      uint32_t word;
-      if (wi < 32) {
-        word = __shfl_sync(0xffffffffu, excl_word, wi);
-      } else {
-        word = (S.excluded != nullptr && blk / 32 < S.bitmap_words) ? __ldg(S.excluded + (int64_t)j * S.bitmap_words + blk / 32) : 0u;
-      }
-      if (!((word >> (blk % 32)) & 1u)) return it;
-      it += kMmaWarps;
-    }
-    return end;
-  };
-  int row_cache = 0, cache_batch = -1;
-  auto list_row = [&](int n) -> int {
-    const int batch = n >> 5;
-    if (batch != cache_batch) {
-      const int my_it = begin + warp + (batch * 32 + lane) * kMmaWarps;
-      int r = 0;
-      if (my_it < end) {
-        const int blk = __ldg(S.blocks + (int64_t)j * S.n_list + my_it);
-        r = blk < 0 ? -1 : (S.slot_of != nullptr ? __ldg(S.slot_of + (int64_t)j * S.slot_stride + blk) : blk);
-      }
-      row_cache = r;
-      cache_batch = batch;
-    }
-    return __shfl_sync(0xffffffffu, row_cache, n & 31);
-  };
-  uint32_t pad_bits = 0;  // stages holding a padding item (no copy, nothing to attend)
-  auto issue = [&](int it, int n, int s) {
-    unsigned char* dst = stage0 + s * stage_stride;
-    const int row = list ? list_row(n) : S.first_block + it;
-    pad_bits = (pad_bits & ~(1u << s)) | ((row < 0 ? 1u : 0u) << s);
-    if (row < 0) {
-      if (lane == 0) mbar_arrive(&bars[s]);
-    } else if (lane == 0) {
-      if (rec) {
-        mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaRec);
-        tma_load_1d(dst, S.records + ((int64_t)row * p.h + j) * S.width, (uint32_t)kMmaRec, &bars[s]);
-      } else {
-        mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaHotStage);
-        const int c2 = head_major ? j : row, c3 = head_major ? row : j;
-        tma_load_4d(smem_u32(dst), tk, 0, 0, c2, c3, &bars[s]);
-        tma_load_4d(smem_u32(dst + kMmaTile), tv, 0, 0, c2, c3, &bars[s]);
-      }
-    }
-  };
-
-  int issue_it = next_item(begin + warp), n_issued = 0;
-#pragma unroll 1
-  for (int s = 0; s < kMmaStages; ++s) {
-    if (issue_it < end) {
-      issue(issue_it, n_issued, s);
-      ++n_issued;
-      issue_it = next_item(issue_it + kMmaWarps);
-    }
-  }
-
-  uint32_t phase = 0;
-  int s = 0, n_done = 0;
-  bool ok = true;
-#pragma unroll 1
-  for (int it = next_item(begin + warp); it < end; it = next_item(it + kMmaWarps)) {
-    ok = __all_sync(0xffffffffu, mbar_wait(&bars[s], (phase >> s) & 1u));
-    if (!ok) break;
-    phase ^= 1u << s;
-    ++n_done;
-    unsigned char* st = stage0 + s * stage_stride;
-    if ((pad_bits >> s) & 1u) {  // padding: nothing to attend; the stage is free
-      if (issue_it < end) {
-        issue(issue_it, n_issued, s);
-        ++n_issued;
-        issue_it = next_item(issue_it + kMmaWarps);
-      }
-      s = (s + 1 == kMmaStages) ? 0 : s + 1;
-      continue;
-    }
-    uint32_t kt, vt;
-    if (rec) {
-      dequant_record(st, tiles, tiles + kMmaTile, lane);
-      __syncwarp();
-      // The raw stage is free again: refill it before the contractions.
-      if (issue_it < end) {
-        issue(issue_it, n_issued, s);
-        ++n_issued;
-        issue_it = next_item(issue_it + kMmaWarps);
-      }
-      kt = smem_u32(tiles);
-      vt = kt + kMmaTile;
-    } else {
-      kt = smem_u32(st);
-      vt = kt + kMmaTile;
-    }
-
-    // ---- S^T = K . Q^T ----
-    float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int cur_set = -1;
+  const int r0 = 2 * t, r1 = 2 * t + 1;
+  // Parks the state of `set` (channels back in natural order): in this warp's slot of the park area
+  // while other warps may still stream (dst_mid), else in the warp's final slot in the idle ring.
+  auto park_state = [&](int set, bool dst_mid) {
+    float la = l0, lb = l1;
 #pragma unroll
-    for (int ks = 0; ks < 4; ks += 2) {
-      uint32_t a[4], b[4];
-      ldsm_x4(kt + koff[ks], a);
-      ldsm_x4(kt + koff[ks + 1], b);
-      mma_bf16(sa, a, bq[ks][0], bq[ks][1]);
-      mma_bf16(sb, b, bq[ks + 1][0], bq[ks + 1][1]);
+    for (int off = 4; off < 32; off <<= 1) {
+      la += __shfl_xor_sync(0xffffffffu, la, off);
+      lb += __shfl_xor_sync(0xffffffffu, lb, off);
     }
-    // Lane scores: x0 (token g, row 2t), x1 (token g, row 2t+1), x2 / x3 (token g + 8).
-    float x0 = (sa[0] + sb[0]) * p.scale_log2, x1 = (sa[1] + sb[1]) * p.scale_log2;
-    float x2 = (sa[2] + sb[2]) * p.scale_log2, x3 = (sa[3] + sb[3]) * p.scale_log2;
-    if (list && it == S.n_list - 1) {
-      if (g >= S.last_fill) x0 = x1 = -INFINITY;
-      if (g + 8 >= S.last_fill) x2 = x3 = -INFINITY;
-    }
-    // ---- softmax update (lazy rescaling, as the CUDA-core kernels) ----
-    const bool need = x0 > m0 + kLazy || x2 > m0 + kLazy || x1 > m1 + kLazy || x3 > m1 + kLazy;
-    if (__any_sync(0xffffffffu, need)) {
-      float mb0 = fmaxf(x0, x2), mb1 = fmaxf(x1, x3);
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
-        mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
-      }
-      if (mb0 > m0 + kLazy) {
-        const float alpha = exp2f(m0 - mb0);  // 0 when m0 was -inf
-        l0 *= alpha;
-#pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-          o[mt][0] *= alpha;
-          o[mt][2] *= alpha;
-        }
-        m0 = mb0;
-      }
-      if (mb1 > m1 + kLazy) {
-        const float alpha = exp2f(m1 - mb1);
-        l1 *= alpha;
-#pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-          o[mt][1] *= alpha;
-          o[mt][3] *= alpha;
-        }
-        m1 = mb1;
-      }
-    }
-    const float p0 = m0 == -INFINITY ? 0.0f : ex2(x0 - m0);
-    const float p2 = m0 == -INFINITY ? 0.0f : ex2(x2 - m0);
-    const float p1 = m1 == -INFINITY ? 0.0f : ex2(x1 - m1);
-    const float p3 = m1 == -INFINITY ? 0.0f : ex2(x3 - m1);
-    l0 += p0 + p2;
-    l1 += p1 + p3;
-    // ---- P^T operand: three bf16 terms, transposed into the B layout ----
-    uint32_t h01, m01, s01, h23, m23, s23;
-    split3(p0, p1, h01, m01, s01);
-    split3(p2, p3, h23, m23, s23);
-    const uint32_t bh0 = movtrans(h01), bh1 = movtrans(h23);
-    const uint32_t bm0 = movtrans(m01), bm1 = movtrans(m23);
-    const uint32_t bl0 = movtrans(s01), bl1 = movtrans(s23);
-    // ---- O^T += V^T . P^T ----
+    float* slot = set == 0 && dst_mid ? park + warp * C::SLOT : reinterpret_cast<float*>(ring) + (warp * 2 + set) * C::SLOT;
+    const bool perm = p.seg[set].kind == SEG_RANGE_REC;
 #pragma unroll
     for (int mt = 0; mt < 4; ++mt) {
-      uint32_t a[4];
-      ldsm_x4_t(vt + voff[mt], a);
-      mma_bf16(o[mt], a, bl0, bl1);
-      mma_bf16(o[mt], a, bm0, bm1);
-      mma_bf16(o[mt], a, bh0, bh1);
+      const int c0 = perm ? 8 * g + 2 * mt : 16 * mt + g;
+      const int c1 = perm ? 8 * g + 2 * mt + 1 : 16 * mt + g + 8;
+      if (r0 < G) {
+        slot[r0 * D + c0] = o[mt][0];
+        slot[r0 * D + c1] = o[mt][2];
+      }
+      if (r1 < G) {
+        slot[r1 * D + c0] = o[mt][1];
+        slot[r1 * D + c1] = o[mt][3];
+      }
     }
-    __syncwarp();  // every lane is done with the stage (and the tiles) before they are refilled
-    if (!rec && issue_it < end) {
-      issue(issue_it, n_issued, s);
+    if (g == 0) {
+      if (r0 < G) {
+        slot[G * D + r0] = m0;
+        slot[G * D + G + r0] = la;
+      }
+      if (r1 < G) {
+        slot[G * D + r1] = m1;
+        slot[G * D + G + r1] = lb;
+      }
+    }
+  };
+
+  uint32_t phase = 0;
+  int n_done = 0, s = 0;
+  bool ok = true, parked_mid = false;
+#pragma unroll 1
+  while (n_done < n_issued) {
+    if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (phase >> s) & 1u))) {
+      ok = false;
+      break;
+    }
+    phase ^= 1u << s;
+    ++n_done;
+    const int i = my_items[s];
+    const int row = list[i];
+    const int set = i < n_a ? 0 : 1;
+    const Seg& S = p.seg[set];
+    if (row >= 0) {
+      if (set != cur_set) {
+        if (cur_set >= 0) {
+          park_state(cur_set, true);
+          parked_mid = true;
+        }
+        cur_set = set;
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.0f;
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) o[a][b] = 0.0f;
+      }
+      const int ord = sh_lo[set] + (set == 0 ? i : i - n_a);
+      const int fill = (S.kind == SEG_LIST && ord == S.n_list - 1) ? S.last_fill : 16;
+      const unsigned char* st = stage0 + s * kStreamStage;
+      const uint32_t st32 = smem_u32(st);
+      const bool rec = S.kind == SEG_RANGE_REC;
+
+      // ---- S^T = K . Q^T ----
+      float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (rec) {
+        const uint4 cg0 = *reinterpret_cast<const uint4*>(st + g * 64 + 16 * t);
+        const uint4 cg8 = *reinterpret_cast<const uint4*>(st + (g + 8) * 64 + 16 * t);
+        const uint4 s0 = *reinterpret_cast<const uint4*>(st + 2048 + 32 * t);
+        const uint4 s1 = *reinterpret_cast<const uint4*>(st + 2048 + 32 * t + 16);
+        const uint4 z0 = *reinterpret_cast<const uint4*>(st + 2176 + 32 * t);
+        const uint4 z1 = *reinterpret_cast<const uint4*>(st + 2176 + 32 * t + 16);
+        const uint32_t wg0[4] = {cg0.x, cg0.y, cg0.z, cg0.w}, wg8[4] = {cg8.x, cg8.y, cg8.z, cg8.w};
+        const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const uint32_t zw[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const float2 s01 = h2f2(sw[2 * ks]), s23 = h2f2(sw[2 * ks + 1]);
+          const float2 z01 = h2f2(zw[2 * ks]), z23 = h2f2(zw[2 * ks + 1]);
+          float2 ua, ub, va, vb;
+          codes4(wg0[ks], ua, ub);
+          codes4(wg8[ks], va, vb);
+          const float2 k0 = __ffma2_rn(ua, s01, z01), k1 = __ffma2_rn(va, s01, z01);
+          const float2 k2 = __ffma2_rn(ub, s23, z23), k3 = __ffma2_rn(vb, s23, z23);
+          const uint32_t a[4] = {pack_bf2(k0.x, k0.y), pack_bf2(k1.x, k1.y), pack_bf2(k2.x, k2.y), pack_bf2(k3.x, k3.y)};
+          if (ks & 1)
+            mma_bf16(sb, a, bqp[ks][0], bqp[ks][1]);
+          else
+            mma_bf16(sa, a, bqp[ks][0], bqp[ks][1]);
+        }
+      } else {
+#pragma unroll
+        for (int ks = 0; ks < 4; ks += 2) {
+          uint32_t a[4], b[4];
+          ldsm_x4(st32 + koff[ks], a);
+          ldsm_x4(st32 + koff[ks + 1], b);
+          mma_bf16(sa, a, bq[ks][0], bq[ks][1]);
+          mma_bf16(sb, b, bq[ks + 1][0], bq[ks + 1][1]);
+        }
+      }
+      float x0 = (sa[0] + sb[0]) * p.scale_log2, x1 = (sa[1] + sb[1]) * p.scale_log2;
+      float x2 = (sa[2] + sb[2]) * p.scale_log2, x3 = (sa[3] + sb[3]) * p.scale_log2;
+      if (fill < 16) {
+        if (g >= fill) x0 = x1 = -INFINITY;
+        if (g + 8 >= fill) x2 = x3 = -INFINITY;
+      }
+      // ---- softmax update (log2 domain, lazy rescaling) ----
+      const bool need = x0 > m0 + kLazy || x2 > m0 + kLazy || x1 > m1 + kLazy || x3 > m1 + kLazy;
+      if (__any_sync(0xffffffffu, need)) {
+        float mb0 = fmaxf(x0, x2), mb1 = fmaxf(x1, x3);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
+          mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
+        }
+        if (mb0 > m0 + kLazy) {
+          const float alpha = exp2f(m0 - mb0);
+          l0 *= alpha;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            o[mt][0] *= alpha;
+            o[mt][2] *= alpha;
+          }
+          m0 = mb0;
+        }
+        if (mb1 > m1 + kLazy) {
+          const float alpha = exp2f(m1 - mb1);
+          l1 *= alpha;
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            o[mt][1] *= alpha;
+            o[mt][3] *= alpha;
+          }
+          m1 = mb1;
+        }
+      }
+      const float p0 = m0 == -INFINITY ? 0.0f : ex2(x0 - m0);
+      const float p2 = m0 == -INFINITY ? 0.0f : ex2(x2 - m0);
+      const float p1 = m1 == -INFINITY ? 0.0f : ex2(x1 - m1);
+      const float p3 = m1 == -INFINITY ? 0.0f : ex2(x3 - m1);
+      l0 += p0 + p2;
+      l1 += p1 + p3;
+      uint32_t h01, md01, s01, h23, md23, s23;
+      split3(p0, p1, h01, md01, s01);
+      split3(p2, p3, h23, md23, s23);
+      const uint32_t bh0 = movtrans(h01), bh1 = movtrans(h23);
+      const uint32_t bm0 = movtrans(md01), bm1 = movtrans(md23);
+      const uint32_t bl0 = movtrans(s01), bl1 = movtrans(s23);
+
+      // ---- O^T += V^T . P^T ----
+      if (rec) {
+        const unsigned char* vq = st + 1024;
+        const uint2 c0 = *reinterpret_cast<const uint2*>(vq + (2 * t) * 64 + 8 * g);
+        const uint2 c1 = *reinterpret_cast<const uint2*>(vq + (2 * t + 1) * 64 + 8 * g);
+        const uint2 c2 = *reinterpret_cast<const uint2*>(vq + (2 * t + 8) * 64 + 8 * g);
+        const uint2 c3 = *reinterpret_cast<const uint2*>(vq + (2 * t + 9) * 64 + 8 * g);
+        const float2 vs01 = h2f2(*reinterpret_cast<const uint32_t*>(st + 2304 + 4 * t));
+        const float2 vs89 = h2f2(*reinterpret_cast<const uint32_t*>(st + 2304 + 4 * t + 16));
+        const float2 vz01 = h2f2(*reinterpret_cast<const uint32_t*>(st + 2336 + 4 * t));
+        const float2 vz89 = h2f2(*reinterpret_cast<const uint32_t*>(st + 2336 + 4 * t + 16));
+        const uint32_t e0[2] = {c0.x ^ 0x80808080u, c0.y ^ 0x80808080u}, e1[2] = {c1.x ^ 0x80808080u, c1.y ^ 0x80808080u};
+        const uint32_t e2[2] = {c2.x ^ 0x80808080u, c2.y ^ 0x80808080u}, e3[2] = {c3.x ^ 0x80808080u, c3.y ^ 0x80808080u};
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          const int wi = mt >> 1;
+          const uint32_t sel0 = 0x7650u + 2 * (mt & 1), sel1 = sel0 + 1;
+          const float2 v00 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel0), vs01, vz01);  // channel 8g+2mt, tokens 2t, 2t+1
+          const float2 v01 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel1), vs01, vz01);  // channel 8g+2mt+1
+          const float2 v80 = __ffma2_rn(code_pair(e2[wi], e3[wi], sel0), vs89, vz89);  // tokens 2t+8, 2t+9
+          const float2 v81 = __ffma2_rn(code_pair(e2[wi], e3[wi], sel1), vs89, vz89);
+          const uint32_t a[4] = {pack_bf2(v00.x, v00.y), pack_bf2(v01.x, v01.y), pack_bf2(v80.x, v80.y), pack_bf2(v81.x, v81.y)};
+          mma_bf16(o[mt], a, bl0, bl1);
+          mma_bf16(o[mt], a, bm0, bm1);
+          mma_bf16(o[mt], a, bh0, bh1);
+        }
+      } else {
+        const uint32_t vt = st32 + kMmaTile;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          uint32_t a[4];
+          ldsm_x4_t(vt + voff[mt], a);
+          mma_bf16(o[mt], a, bl0, bl1);
+          mma_bf16(o[mt], a, bm0, bm1);
+          mma_bf16(o[mt], a, bh0, bh1);
+        }
+      }
+    }
+    __syncwarp();  // every lane is done with the stage before it is refilled
+    if (n_issued < n_mine) {
+      issue(list_index(n_issued), s);
       ++n_issued;
-      issue_it = next_item(issue_it + kMmaWarps);
     }
-    s = (s + 1 == kMmaStages) ? 0 : s + 1;
+    s = s + 1 == NS ? 0 : s + 1;
   }
   // After a timed-out wait, wait (bounded) for the copies still in flight.
-  for (int k = n_done; !ok && k < n_issued; ++k) {
-    if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (phase >> s) & 1u))) break;
-    phase ^= 1u << s;
-    s = (s + 1 == kMmaStages) ? 0 : s + 1;
+  if (!ok) {
+    for (int k = n_done; k < n_issued; ++k) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (phase >> s) & 1u))) break;
+      phase ^= 1u << s;
+      s = s + 1 == NS ? 0 : s + 1;
+    }
+    if (lane == 0) atomicExch(&sh_bad, 1);
   }
-  if (!ok && lane == 0) atomicExch(&sh_bad, 1);
+  __syncthreads();  // every warp is done with the ring: final states go there
+  {
+    float* fin = reinterpret_cast<float*>(ring) + warp * 2 * C::SLOT;
+    if (parked_mid)
+      for (int e = lane; e < C::SLOT; e += 32) fin[e] = park[warp * C::SLOT + e];
+    if (cur_set >= 0) park_state(cur_set, false);
+    // A set this warp holds no state of: empty (m = -inf).
+    for (int set = 0; set < 2; ++set)
+      if (set != cur_set && !(set == 0 && parked_mid))
+        for (int r = lane; r < G; r += 32) fin[set * C::SLOT + G * D + r] = -INFINITY;
+  }
+  __syncthreads();
 
-  // ---- epilogue: per-warp partials through shared memory (the stages are idle now) ----
-#pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-  }
-  __syncthreads();
-  float* out = p.part + ((int64_t)j * p.n_splits_total + blockIdx.x) * G * (D + 2);
-  if (sh_bad) {
-    for (int e = threadIdx.x; e < G * (D + 2); e += blockDim.x) out[e] = e < G ? -INFINITY : 0.0f;
-    return;
-  }
-  float* sh_o = reinterpret_cast<float*>(smem);           // [warp][G][D]
-  float* sh_ml = sh_o + kMmaWarps * G * D;                // [warp][m(G) | l(G)]
-  const int r0 = 2 * t, r1 = 2 * t + 1;
-#pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
-    if (r0 < G) {
-      sh_o[(warp * G + r0) * D + 16 * mt + g] = o[mt][0];
-      sh_o[(warp * G + r0) * D + 16 * mt + g + 8] = o[mt][2];
-    }
-    if (r1 < G) {
-      sh_o[(warp * G + r1) * D + 16 * mt + g] = o[mt][1];
-      sh_o[(warp * G + r1) * D + 16 * mt + g + 8] = o[mt][3];
-    }
-  }
-  if (g == 0) {
-    if (r0 < G) {
-      sh_ml[warp * 2 * G + r0] = m0;
-      sh_ml[warp * 2 * G + G + r0] = l0;
-    }
-    if (r1 < G) {
-      sh_ml[warp * 2 * G + r1] = m1;
-      sh_ml[warp * 2 * G + G + r1] = l1;
-    }
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    const int r = e / D, c = e % D;
+  // ---- fold the warps' parked states: one partial per set for this CTA ----
+  const int64_t part_stride = C::PART;
+  const float* fin_all = reinterpret_cast<const float*>(ring);
+  float* mine = sp.part + (((int64_t)j * P + ci) * 2) * part_stride;
+  for (int e = threadIdx.x; e < 2 * G * D; e += blockDim.x) {
+    const int set = e / (G * D), r = (e / D) % G, c = e % D;
+    float* out = mine + set * part_stride;
     float M = -INFINITY;
+    if (!sh_bad)
 #pragma unroll
-    for (int w = 0; w < kMmaWarps; ++w) M = fmaxf(M, sh_ml[w * 2 * G + r]);
+      for (int w = 0; w < NW; ++w) M = fmaxf(M, fin_all[(w * 2 + set) * C::SLOT + G * D + r]);
     float O = 0.0f, Lr = 0.0f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < kMmaWarps; ++w) {
-        const float mw = sh_ml[w * 2 * G + r];
-        const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
-        O = fmaf(sh_o[(w * G + r) * D + c], f, O);
-        Lr = fmaf(sh_ml[w * 2 * G + G + r], f, Lr);
+      for (int w = 0; w < NW; ++w) {
+        const float* sl = fin_all + (w * 2 + set) * C::SLOT;
+        const float mw = sl[G * D + r];
+        if (mw == -INFINITY) continue;
+        const float f = exp2f(mw - M);
+        O = fmaf(sl[r * D + c], f, O);
+        Lr = fmaf(sl[G * D + G + r], f, Lr);
       }
     }
-    out[2 * G + r * D + c] = O;
+    out[r * D + c] = O;
     if (c == 0) {
-      out[r] = M;
-      out[G + r] = Lr;
+      out[G * D + r] = M;
+      out[G * D + G + r] = Lr;
     }
   }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) sh_last = atomicAdd(&sp.counters[j], 1u) == (unsigned)(P - 1);
+  __syncthreads();
+  if (!sh_last) return;
+  __threadfence();
+
+  // ---- the head's last CTA: fold its P partials per set into the outputs ----
+  // The head's partials are contiguous in the workspace: one bulk copy brings them into the idle
+  // ring (when they fit); then per (set, row) the maximum, the weights 2^(m - M) and the sum, and
+  // the outputs, all from shared memory. Otherwise they are read from the workspace directly.
+  const float* hp = sp.part + (int64_t)j * P * 2 * part_stride;
+  const int nset = p.n_segs;
+  const size_t head_bytes = (size_t)P * 2 * C::PART * sizeof(float);
+  const size_t wts_off = (head_bytes + 15) / 16 * 16;
+  const bool bulk = wts_off + (size_t)(2 * G * P + 4 * G) * sizeof(float) <= (size_t)C::RING;
+  bool got = true;
+  if (bulk && threadIdx.x == 0) {
+    asm volatile("fence.proxy.async;" ::: "memory");  // the partials (generic stores of other CTAs) before the bulk reads
+    mbar_arrive_expect_tx(&fold_bar, (uint32_t)head_bytes);
+    for (size_t off = 0; off < head_bytes; off += 32768) {
+      const uint32_t n = (uint32_t)(head_bytes - off < 32768 ? head_bytes - off : 32768);
+      tma_load_1d(ring + off, reinterpret_cast<const unsigned char*>(hp) + off, n, &fold_bar);
+    }
+  }
+  if (bulk) got = __syncthreads_and(mbar_wait(&fold_bar, 0));
+  const float* parts = bulk ? reinterpret_cast<const float*>(ring) : hp;
+  float* wts = reinterpret_cast<float*>(ring + wts_off);  // [2][G][P] (bulk only)
+  float* setM = wts + 2 * G * P;                          // [2][G]
+  float* setL = setM + 2 * G;                             // [2][G]
+  if (bulk && got) {
+    for (int e = threadIdx.x; e < 2 * G; e += blockDim.x) {
+      const int set = e / G, r = e % G;
+      float M = -INFINITY;
+      for (int k = 0; k < P; ++k) M = fmaxf(M, parts[(k * 2 + set) * part_stride + G * D + r]);
+      setM[e] = M;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < 2 * G * P; e += blockDim.x) {
+      const int set = e / (G * P), r = (e / P) % G, k = e % P;
+      const float M = setM[set * G + r], mk = parts[(k * 2 + set) * part_stride + G * D + r];
+      wts[e] = (M == -INFINITY || mk == -INFINITY) ? 0.0f : exp2f(mk - M);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < 2 * G; e += blockDim.x) {
+      const int set = e / G, r = e % G;
+      float L = 0.0f;
+      for (int k = 0; k < P; ++k) L = fmaf(parts[(k * 2 + set) * part_stride + G * D + G + r], wts[(set * G + r) * P + k], L);
+      setL[e] = L;
+    }
+    __syncthreads();
+  }
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int r = e / D, c = e % D;
+    float O0 = 0.0f, O1 = 0.0f, M0 = -INFINITY, M1 = -INFINITY, L0 = 0.0f, L1 = 0.0f;
+#pragma unroll
+    for (int set = 0; set < 2; ++set) {
+      if (set >= nset || !got) break;
+      float O = 0.0f, M = -INFINITY, L = 0.0f;
+      if (bulk) {
+        const float* wr = wts + (set * G + r) * P;
+#pragma unroll 4
+        for (int k = 0; k < P; ++k) O = fmaf(parts[(k * 2 + set) * part_stride + r * D + c], wr[k], O);
+        M = setM[set * G + r];
+        L = setL[set * G + r];
+      } else {  // more partials than the idle ring holds: straight from the workspace
+        for (int k = 0; k < P; ++k) M = fmaxf(M, __ldcg(hp + (k * 2 + set) * part_stride + G * D + r));
+        if (M != -INFINITY)
+          for (int k = 0; k < P; ++k) {
+            const float* pk = hp + (k * 2 + set) * part_stride;
+            const float mk = __ldcg(pk + G * D + r);
+            if (mk == -INFINITY) continue;
+            const float f = exp2f(mk - M);
+            O = fmaf(__ldcg(pk + r * D + c), f, O);
+            L = fmaf(__ldcg(pk + G * D + G + r), f, L);
+          }
+      }
+      if (set == 0) {
+        O0 = O; M0 = M; L0 = L;
+      } else {
+        O1 = O; M1 = M; L1 = L;
+      }
+    }
+    const int64_t row = (int64_t)j * G + r;
+    if (sp.seg_out != nullptr) {
+#pragma unroll
+      for (int set = 0; set < 2; ++set) {
+        if (set >= nset) break;
+        const float Os = set == 0 ? O0 : O1, Ms = set == 0 ? M0 : M1, Ls = set == 0 ? L0 : L1;
+        const bool empty = !(Ls > 0.0f);
+        sp.seg_out[(int64_t)set * p.hq * D + row * D + c] = empty ? 0.0f : Os / Ls;
+        if (c == 0 && sp.seg_lse != nullptr) sp.seg_lse[(int64_t)set * p.hq + row] = empty ? -INFINITY : (Ms + log2f(Ls)) * kLn2;
+      }
+    }
+    if (sp.out != nullptr || sp.lse != nullptr) {
+      const float M = fmaxf(M0, M1);
+      float O = 0.0f, L = 0.0f;
+      if (M != -INFINITY) {
+        if (M0 != -INFINITY) {
+          const float f = exp2f(M0 - M);
+          O = fmaf(O0, f, O);
+          L = fmaf(L0, f, L);
+        }
+        if (M1 != -INFINITY) {
+          const float f = exp2f(M1 - M);
+          O = fmaf(O1, f, O);
+          L = fmaf(L1, f, L);
+        }
+      }
+      const bool empty = !(L > 0.0f);
+      if (sp.out != nullptr) static_cast<TO*>(sp.out)[row * D + c] = from_f32<TO>(empty ? 0.0f : O / L);
+      if (c == 0 && sp.lse != nullptr) sp.lse[row] = empty ? -INFINITY : (M + log2f(L)) * kLn2;
+    }
+  }
+  if (threadIdx.x == 0) sp.counters[j] = 0u;  // ready for the next call
 }
 
 // ============================================================================================
@@ -1539,7 +1869,7 @@ bool make_kv_maps(const Seg& S, int h, CUtensorMap* tk, CUtensorMap* tv, int* he
   return true;
 }
 
-// Whether the tensor-core kernel takes this launch (bf16, d 64, bs 16, G <= 8, stores in device
+// Whether the stream kernel takes this launch (bf16, d 64, bs 16, G <= 8, stores in device
 // memory, 64-channel token rows); fills the tensor maps of its list / pairs segments.
 bool mma_plan(const AttnParams& p, int g, int d, bool bf16, MmaParams& mp) {
   if (!bf16 || d != 64 || p.bs != 16 || (g != 1 && g != 2 && g != 4 && g != 8)) return false;
@@ -1556,70 +1886,111 @@ bool mma_plan(const AttnParams& p, int g, int d, bool bf16, MmaParams& mp) {
   return true;
 }
 
-template <int G>
-int launch_mma(const MmaParams& mp, cudaStream_t st) {
+// SMs of the current device (cached per device; the B200 count when no device answers).
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return kNumSMs;
+  }
+  int& c = cached[dev & 63];
+  if (c == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+      cudaGetLastError();
+      v = kNumSMs;
+    }
+    c = v;
+  }
+  return c;
+}
+
+// CTAs per KV head of the stream kernel: kStreamCtasPerSm per SM over the heads, or more when a
+// CTA's items could exceed its list (n_ub: an upper bound of a head's items; a CTA holds at most
+// ceil(n / P) items of each of the two segments, so ceil(n_ub / P) + 2 in all).
+int stream_per_head(int h, int64_t n_ub) {
+  int per = kStreamCtasPerSm * sm_count() / (h > 0 ? h : 1);
+  const int64_t need = (n_ub + kStreamListCap - 3) / (kStreamListCap - 2);
+  if (need > per) per = (int)need;
+  return per < 1 ? 1 : per;
+}
+size_t stream_partial_bytes(int h, int g, int64_t n_ub) {
+  const int part = (g * 64 + 2 * g + 3) / 4 * 4;
+  return (size_t)h * stream_per_head(h, n_ub) * 2 * part * sizeof(float);
+}
+int64_t stream_item_bound(const AttnParams& p) {
+  int64_t n = 0;
+  for (int s = 0; s < p.n_segs; ++s) n += p.seg[s].n_items;
+  return n;
+}
+
+template <int G, typename TO>
+int launch_stream(const StreamParams& sp, cudaStream_t st) {
+  using C = StreamCfg<G>;
   static uint64_t attr_set = 0;  // one bit per device
-  auto k = attn_mma_kernel<G>;
+  auto k = attn_stream_kernel<G, TO>;
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMmaSmem);
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
     attr_set |= bit;
   }
-  k<<<dim3(mp.p.n_splits_total, mp.p.h), kMmaThreads, kMmaSmem, st>>>(mp);
-  return LKV_OK;
+  k<<<dim3(sp.per_head, sp.p.h), kStreamThreads, C::SMEM, st>>>(sp);
+  return launched("lkv attention");
 }
 
-// Splits, workspace check and launch of one attention call (partials + combine).
+// Splits, workspace check and launch of one attention call. The workspace starts with
+// kStreamCounterBytes of per-head counters (zero before and after every call), then the partials.
 template <typename T, typename TO>
-int run_attention(const char* who, AttnParams& p, int g, int d, TO* out, float* lse, float* seg_out, float* seg_lse, size_t workspace_bytes,
-                  cudaStream_t st) {
+int run_attention(const char* who, AttnParams& p, int g, int d, TO* out, float* lse, float* seg_out, float* seg_lse, void* workspace,
+                  size_t workspace_bytes, cudaStream_t st) {
+  if (workspace_bytes < (size_t)kStreamCounterBytes)
+    return fail(LKV_ERR_WORKSPACE, "%s: workspace %zu < %d bytes", who, workspace_bytes, kStreamCounterBytes);
+  if (!aligned(workspace, 16)) return fail(LKV_ERR_PTR, "%s: workspace must be 16-byte aligned", who);
+  p.part = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kStreamCounterBytes);
+  const size_t avail = workspace_bytes - kStreamCounterBytes;
   MmaParams mp{};
-  const bool mma = mma_plan(p, g, d, sizeof(T) == 2, mp);
-  const int total = mma ? kMmaTargetCtas : kTargetCtas;
+  const bool mma = p.h <= kStreamCounterBytes / 4 && mma_plan(p, g, d, sizeof(T) == 2, mp);
+  if (mma) {
+    if constexpr (sizeof(T) == 2) {
+      StreamParams sp{};
+      sp.p = p;
+      for (int i = 0; i < 2; ++i) {
+        sp.tk[i] = mp.tk[i];
+        sp.tv[i] = mp.tv[i];
+        sp.head_major[i] = mp.head_major[i];
+      }
+      const int64_t n_ub = stream_item_bound(p);
+      sp.per_head = stream_per_head(p.h, n_ub);
+      sp.counters = static_cast<unsigned int*>(workspace);
+      sp.part = p.part;
+      sp.out = out;
+      sp.lse = lse;
+      sp.seg_out = seg_out;
+      sp.seg_lse = seg_lse;
+      const size_t need = stream_partial_bytes(p.h, g, n_ub);
+      if (avail < need) return fail(LKV_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, need + kStreamCounterBytes);
+      switch (g) {
+        case 1: return launch_stream<1, TO>(sp, st);
+        case 2: return launch_stream<2, TO>(sp, st);
+        case 4: return launch_stream<4, TO>(sp, st);
+        default: return launch_stream<8, TO>(sp, st);
+      }
+    }
+  }
   if (p.n_segs == 1) {
-    set_split(p.seg[0], (total + p.h - 1) / p.h);
+    set_split(p.seg[0], (kTargetCtas + p.h - 1) / p.h);
     p.n_splits_total = p.seg[0].n_splits;
   } else {
-    if (mma) {
-      // Tensor-core costs per item, relative: a listed block 1; a cold record about 2.5 (the fused
-      // dequantisation), of which the range's excluded blocks (about the listed ones) cost little.
-      const double n_cold = p.seg[1].n_items > 0 ? p.seg[1].n_items : 1;
-      const double live = fmax(0.0, n_cold - fmax(0.0, p.seg[0].n_items - 2.0)) / n_cold;
-      const double cold_cost = p.seg[1].kind == SEG_RANGE_REC ? 2.5 : 1.0;
-      split_two(p.seg[0], p.seg[1], p.h, 1.0, cold_cost * live + 0.05, total);
-    } else {
-      split_two(p.seg[0], p.seg[1], p.h, 4096, 2368, total);
-    }
+    split_two(p.seg[0], p.seg[1], p.h, 4096, 2368, kTargetCtas);
     p.n_splits_total = p.seg[0].n_splits + p.seg[1].n_splits;
   }
   const size_t need = partial_bytes(p.h, g, d, p.n_splits_total);
-  if (workspace_bytes < need) return fail(LKV_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, need);
-  if (!mma) return dispatch<T, TO>(g, d, p, out, lse, seg_out, seg_lse, st);
-  if constexpr (sizeof(T) == 2) {
-    mp.p = p;
-    int rc = LKV_OK;
-    if (p.n_splits_total > 0) {
-      switch (g) {
-        case 1: rc = launch_mma<1>(mp, st); break;
-        case 2: rc = launch_mma<2>(mp, st); break;
-        case 4: rc = launch_mma<4>(mp, st); break;
-        default: rc = launch_mma<8>(mp, st); break;
-      }
-    }
-    if (rc) return rc;
-    const int n0 = p.seg[0].n_splits, n1 = p.n_segs > 1 ? p.seg[1].n_splits : 0;
-    switch (g) {
-      case 1: attn_combine_kernel<TO, 1, 64><<<dim3(p.h, 1), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq); break;
-      case 2: attn_combine_kernel<TO, 2, 64><<<dim3(p.h, 2), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq); break;
-      case 4: attn_combine_kernel<TO, 4, 64><<<dim3(p.h, 4), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq); break;
-      default: attn_combine_kernel<TO, 8, 64><<<dim3(p.h, 8), kCombineThreads, 0, st>>>(p.part, n0, n1, out, lse, seg_out, seg_lse, p.hq); break;
-    }
-    return launched("lkv attention");
-  }
-  return fail(LKV_ERR_ARG, "%s: unreachable", who);
+  if (avail < need) return fail(LKV_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, need + kStreamCounterBytes);
+  return dispatch<T, TO>(g, d, p, out, lse, seg_out, seg_lse, st);
 }
 
 }  // namespace
@@ -1642,20 +2013,17 @@ int lkv_device_status(int* status, int clear) {
 
 size_t lkv_attention_workspace(int h, int hq, int d, int n_items) {
   if (h <= 0 || hq <= 0) return 0;
-  const int s = splits_for(n_items, (kMmaTargetCtas + h - 1) / h);
-  const size_t b = partial_bytes(h, hq / h, d, s);
-  return b > 0 ? b : 16;
+  const int s = splits_for(n_items, (kTargetCtas + h - 1) / h);
+  const size_t a = partial_bytes(h, hq / h, d, s), b = stream_partial_bytes(h, hq / h, n_items > 0 ? n_items : 0);
+  return kStreamCounterBytes + (a > b ? a : b);
 }
 
 size_t lkv_exact_attention_workspace(int h, int hq, int d, int n_list, int n_blocks) {
   if (h <= 0 || hq <= 0) return 0;
-  Seg a{}, b{};
-  a.n_items = n_list;
-  b.n_items = n_blocks;
-  split_two(a, b, h, 4096, 2368, kMmaTargetCtas);
-  const int per_head = (kMmaTargetCtas + h - 1) / h + 1;  // any split of the target between the segments
-  const size_t s = partial_bytes(h, hq / h, d, per_head > a.n_splits + b.n_splits ? per_head : a.n_splits + b.n_splits);
-  return s > 0 ? s : 16;
+  const int per_head = (kTargetCtas + h - 1) / h + 1;  // any split of the target between the segments
+  const int64_t n_ub = (int64_t)(n_list > 0 ? n_list : 0) + (n_blocks > 0 ? n_blocks : 0);
+  const size_t a = partial_bytes(h, hq / h, d, per_head), b = stream_partial_bytes(h, hq / h, n_ub);
+  return kStreamCounterBytes + (a > b ? a : b);
 }
 
 int lkv_hot_attention(const void* q, int hq, int h, int d, int bs, const void* k_base, const void* v_base, int dtype, int64_t s_row,
@@ -1669,10 +2037,9 @@ int lkv_hot_attention(const void* q, int hq, int h, int d, int bs, const void* k
   p.q = q; p.hq = hq; p.h = h; p.bs = bs; p.scale_log2 = scale * kLog2e;
   if (int rc = fill_hot("lkv_hot_attention", p.seg[0], h, d, bs, &hs)) return rc;
   p.n_segs = 1;
-  p.part = static_cast<float*>(workspace);
   cudaStream_t st = as_stream(stream);
-  return dtype == LKV_BF16 ? run_attention<__nv_bfloat16, float>("lkv_hot_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace_bytes, st)
-                           : run_attention<float, float>("lkv_hot_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace_bytes, st);
+  return dtype == LKV_BF16 ? run_attention<__nv_bfloat16, float>("lkv_hot_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace, workspace_bytes, st)
+                           : run_attention<float, float>("lkv_hot_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace, workspace_bytes, st);
 }
 
 int lkv_cold_attention(const void* q, int hq, int h, int d, int bs, const void* cold, int cold_kind, int dtype, int first_block,
@@ -1685,10 +2052,9 @@ int lkv_cold_attention(const void* q, int hq, int h, int d, int bs, const void* 
   p.q = q; p.hq = hq; p.h = h; p.bs = bs; p.scale_log2 = scale * kLog2e;
   if (int rc = fill_cold("lkv_cold_attention", p.seg[0], h, d, bs, dtype, &cs)) return rc;
   p.n_segs = 1;
-  p.part = static_cast<float*>(workspace);
   cudaStream_t st = as_stream(stream);
-  return dtype == LKV_BF16 ? run_attention<__nv_bfloat16, float>("lkv_cold_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace_bytes, st)
-                           : run_attention<float, float>("lkv_cold_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace_bytes, st);
+  return dtype == LKV_BF16 ? run_attention<__nv_bfloat16, float>("lkv_cold_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace, workspace_bytes, st)
+                           : run_attention<float, float>("lkv_cold_attention", p, hq / h, d, out, lse, nullptr, nullptr, workspace, workspace_bytes, st);
 }
 
 int lkv_exact_attention(const void* q, int hq, int h, int d, int bs, const lkv_hot_set* hot, const lkv_cold_set* cold, float scale,
@@ -1703,16 +2069,15 @@ int lkv_exact_attention(const void* q, int hq, int h, int d, int bs, const lkv_h
   if (int rc = fill_hot("lkv_exact_attention", p.seg[0], h, d, bs, hot)) return rc;
   if (int rc = fill_cold("lkv_exact_attention", p.seg[1], h, d, bs, hot->dtype, cold)) return rc;
   p.n_segs = 2;
-  p.part = static_cast<float*>(workspace);
   cudaStream_t st = as_stream(stream);
   const int g = hq / h;
   const bool bf = hot->dtype == LKV_BF16;
   const char* who = "lkv_exact_attention";
   if (out_dtype == LKV_BF16)
-    return bf ? run_attention<__nv_bfloat16, __nv_bfloat16>(who, p, g, d, static_cast<__nv_bfloat16*>(out), lse, part_out, part_lse, workspace_bytes, st)
-              : run_attention<float, __nv_bfloat16>(who, p, g, d, static_cast<__nv_bfloat16*>(out), lse, part_out, part_lse, workspace_bytes, st);
-  return bf ? run_attention<__nv_bfloat16, float>(who, p, g, d, static_cast<float*>(out), lse, part_out, part_lse, workspace_bytes, st)
-            : run_attention<float, float>(who, p, g, d, static_cast<float*>(out), lse, part_out, part_lse, workspace_bytes, st);
+    return bf ? run_attention<__nv_bfloat16, __nv_bfloat16>(who, p, g, d, static_cast<__nv_bfloat16*>(out), lse, part_out, part_lse, workspace, workspace_bytes, st)
+              : run_attention<float, __nv_bfloat16>(who, p, g, d, static_cast<__nv_bfloat16*>(out), lse, part_out, part_lse, workspace, workspace_bytes, st);
+  return bf ? run_attention<__nv_bfloat16, float>(who, p, g, d, static_cast<float*>(out), lse, part_out, part_lse, workspace, workspace_bytes, st)
+            : run_attention<float, float>(who, p, g, d, static_cast<float*>(out), lse, part_out, part_lse, workspace, workspace_bytes, st);
 }
 
 int lkv_lse_merge(const float* outs, const float* lses, int n_parts, int64_t rows, int d, void* out, int out_dtype, float* lse_out,

@@ -10,6 +10,7 @@ namespace lkv {
 // and that entry point, is the only translation unit that includes this header.
 __device__ int g_device_status = 0;
 constexpr int LKV_DEV_WAIT_TIMEOUT = 1;       // an mbarrier wait ran out of iterations
+constexpr int LKV_DEV_LIST_OVERFLOW = 2;      // a CTA's item list would not fit its shared memory (host sizing error)
 constexpr uint32_t kMaxWaitIters = 1u << 21;  // tries; each may suspend up to kWaitHintNs
 constexpr uint32_t kWaitHintNs = 1000;        // suspend-time hint of one try (the wait ends sooner when the phase completes)
 

@@ -1,7 +1,7 @@
 """The attention kernels (tensor-core, TMA-pipelined and plain-load) and the fused exact call,
 against the oracle.
 
-The tensor-core kernel serves bf16 stores in device memory at d 64, bs 16, G <= 8; the TMA kernel
+The tensor-core stream kernel serves bf16 stores in device memory at d 64, bs 16, G <= 8; the TMA kernel
 the other device-memory cases at G = 4, bs = 16, d in {64, 128}; the plain-load kernel every other
 geometry and cold stores in mapped host memory. Every case is compared with float64 attention over
 the same values (1e-5 of the max; int8 cold blocks as unpack in the model dtype), and the fused call
@@ -116,7 +116,7 @@ def test_host_mapped_cold_store_reads_over_the_link() -> None:
     host.copy_(rec.cpu())
     mapped = device_view(host)
     bitmap = _bitmap(sel, n)
-    # Device records go to the tensor-core kernel, mapped ones to the plain-load kernel: the same
+    # Device records go to the tensor-core stream kernel, mapped ones to the plain-load kernel: the same
     # values, two summation orders.
     a, al = K.cold_attention(qd, rec, bs, 1, n - 2, d**-0.5, excluded=bitmap)
     b, bl = K.cold_attention(qd, mapped, bs, 1, n - 2, d**-0.5, excluded=bitmap)
