@@ -34,6 +34,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 #include "tma.cuh"
 
 namespace lkv {
@@ -822,12 +824,14 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
 }
 __device__ __forceinline__ float2 unpack_bf2(uint32_t w) { return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u)); }
 
-// Splits (a, b) into three bf16x2 terms whose sum is (a, b) to 24 significant bits.
+// Splits (a, b) into three bf16x2 terms whose sum is (a, b) to 24 significant bits: each term is the
+// bf16 rounding of what the previous ones left, and each residual (x - term) is exact in float32.
 __device__ __forceinline__ void split3(float a, float b, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+  const float2 neg1 = f2(-1.0f, -1.0f);
   hi = pack_bf2(a, b);
-  const float2 r = __fadd2_rn(f2(a, b), f2(-unpack_bf2(hi).x, -unpack_bf2(hi).y));
+  const float2 r = __ffma2_rn(unpack_bf2(hi), neg1, f2(a, b));
   mid = pack_bf2(r.x, r.y);
-  const float2 r2 = __fadd2_rn(r, f2(-unpack_bf2(mid).x, -unpack_bf2(mid).y));
+  const float2 r2 = __ffma2_rn(unpack_bf2(mid), neg1, r);
   lo = pack_bf2(r2.x, r2.y);
 }
 
@@ -877,14 +881,13 @@ constexpr int kStreamCounterBytes = 4096;  // per-head CTA counters at the works
 
 template <int G>
 struct StreamCfg {
-  static constexpr int STAGES = G <= 4 ? 3 : 2;  // per warp
+  static constexpr int STAGES = 2;  // per warp (the loop is unrolled over them)
   static constexpr int SLOT = G * 64 + 2 * G;    // floats of a parked state: o [G][64], m [G], l [G]
   static constexpr int RING = kStreamWarps * STAGES * kStreamStage;
   static constexpr int PARK = kStreamWarps * SLOT * 4;  // a warp's state of segment 0 when it moves on
   static constexpr int LIST = kStreamListCap * 4;
   static constexpr int BARS = kStreamWarps * STAGES * 8;
-  static constexpr int SITEM = kStreamWarps * STAGES * 4;  // list index held by each stage
-  static constexpr size_t SMEM = 1024 + (size_t)RING + PARK + LIST + BARS + SITEM;
+  static constexpr size_t SMEM = 1024 + (size_t)RING + PARK + LIST + BARS;
   // Floats of one (CTA, set) partial in the workspace: o [G][64], m [G], l [G], padded to 16 bytes so
   // the rows of o are float4-aligned for every G.
   static constexpr int PART = (G * 64 + 2 * G + 3) / 4 * 4;
@@ -974,7 +977,6 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   float* park = reinterpret_cast<float*>(smem + C::RING);
   int* list = reinterpret_cast<int*>(smem + C::RING + C::PARK);
   uint64_t* bars_all = reinterpret_cast<uint64_t*>(smem + C::RING + C::PARK + C::LIST);
-  int* stage_item = reinterpret_cast<int*>(smem + C::RING + C::PARK + C::LIST + C::BARS);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = blockIdx.y, ci = blockIdx.x, P = sp.per_head;
@@ -1147,20 +1149,23 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     }
   }
   unsigned char* stage0 = ring + warp * NS * kStreamStage;
-  int* my_items = stage_item + warp * NS;
-  // Lane 0 fills stage s with list item i (or arrives for a padding item).
-  auto issue = [&](int i, int s) {
+  // Per set: whether its items are int8 records (else bf16 tile pairs through the tensor maps).
+  const bool rec0 = p.seg[0].kind == SEG_RANGE_REC, rec1 = p.n_segs > 1 && p.seg[1].kind == SEG_RANGE_REC;
+  // The warp's item holding the current block (the last listed block, `last_fill` live tokens), if any.
+  const int fill_k = (p.seg[0].kind == SEG_LIST && lb0 == p.seg[0].n_list && hn > 0 && ha + hn == n_a) ? hn - 1 : -1;
+  const int last_fill = p.seg[0].last_fill;
+  // Lane 0 fills stage s with the warp's k-th item (or arrives for a padding item).
+  auto issue = [&](int k, int s) {
     if (lane != 0) return;
-    my_items[s] = i;
-    const int set = i < n_a ? 0 : 1;
-    const Seg& S = p.seg[set];
-    const int row = list[i];
+    const int set = k < hn ? 0 : 1;
+    const int row = list[list_index(k)];
     if (row < 0) {
       mbar_arrive(&bars[s]);
       return;
     }
     unsigned char* dst = stage0 + s * kStreamStage;
-    if (S.kind == SEG_RANGE_REC) {
+    if (set ? rec1 : rec0) {
+      const Seg& S = p.seg[set];
       mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaRec);
       tma_load_1d(dst, S.records + ((int64_t)row * p.h + j) * S.width, (uint32_t)kMmaRec, &bars[s]);
     } else {
@@ -1172,22 +1177,36 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     }
   };
   int n_issued = 0;
-#pragma unroll 1
-  for (int s = 0; s < NS && s < n_mine; ++s) {
-    issue(list_index(s), s);
-    ++n_issued;
-  }
+#pragma unroll
+  for (int s = 0; s < NS; ++s)
+    if (s < n_mine) {
+      issue(s, s);
+      ++n_issued;
+    }
 
+  // Online-softmax state. The running maxima m (log2 domain) start at a finite -1e30 so that no
+  // score needs a test for an empty state: the first finite score always rescales (by 2^-huge = 0),
+  // and a masked score (-inf) gives 2^-inf = 0. thr = (m + kLazy) / scale_log2 is the raw-score
+  // threshold of the lazy rescaling (scale_log2 > 0), nm = -m.
+  constexpr float kNoMax = -1e30f;
+  const float sl2 = p.scale_log2, inv_sl2 = 1.0f / p.scale_log2;
   float o[4][4];
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  float m0, m1, nm0, nm1, thr0, thr1, l0, l1;
+  auto reset_state = [&]() {
+    m0 = m1 = kNoMax;
+    nm0 = nm1 = -kNoMax;
+    thr0 = thr1 = (kNoMax + kLazy) * inv_sl2;
+    l0 = l1 = 0.0f;
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) o[a][b] = 0.0f;
-  int cur_set = -1;
+      for (int b = 0; b < 4; ++b) o[a][b] = 0.0f;
+  };
+  reset_state();
   const int r0 = 2 * t, r1 = 2 * t + 1;
   // Parks the state of `set` (channels back in natural order): in this warp's slot of the park area
-  // while other warps may still stream (dst_mid), else in the warp's final slot in the idle ring.
+  // while other warps may still stream (dst_mid), else in the warp's final slot in the idle ring. A
+  // row that saw no key is parked as (m = -inf, l = 0).
   auto park_state = [&](int set, bool dst_mid) {
     float la = l0, lb = l1;
 #pragma unroll
@@ -1196,7 +1215,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
       lb += __shfl_xor_sync(0xffffffffu, lb, off);
     }
     float* slot = set == 0 && dst_mid ? park + warp * C::SLOT : reinterpret_cast<float*>(ring) + (warp * 2 + set) * C::SLOT;
-    const bool perm = p.seg[set].kind == SEG_RANGE_REC;
+    const bool perm = set ? rec1 : rec0;
 #pragma unroll
     for (int mt = 0; mt < 4; ++mt) {
       const int c0 = perm ? 8 * g + 2 * mt : 16 * mt + g;
@@ -1212,188 +1231,198 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     }
     if (g == 0) {
       if (r0 < G) {
-        slot[G * D + r0] = m0;
+        slot[G * D + r0] = la > 0.0f ? m0 : -INFINITY;
         slot[G * D + G + r0] = la;
       }
       if (r1 < G) {
-        slot[G * D + r1] = m1;
+        slot[G * D + r1] = lb > 0.0f ? m1 : -INFINITY;
         slot[G * D + G + r1] = lb;
       }
     }
   };
 
-  uint32_t phase = 0;
-  int n_done = 0, s = 0;
-  bool ok = true, parked_mid = false;
+  // Lane offsets inside a stage (bytes): record K codes of tokens g and g + 8 at channels 16t..,
+  // V codes of tokens 2t, 2t+1, 2t+8, 2t+9 at channels 8g.., V scales / zeros of those tokens, and
+  // the float32 K scales / zeros of channels 16t.. in the stage's tail.
+  const int ok0 = g * 64 + 16 * t, ok8 = (g + 8) * 64 + 16 * t;
+  const int ov0 = 1024 + (2 * t) * 64 + 8 * g, ov1 = ov0 + 64, ov8 = ov0 + 8 * 64, ov9 = ov0 + 9 * 64;
+  const int ovs = 2304 + 4 * t, ovz = 2336 + 4 * t;
+  constexpr int kKf = 2432;  // float32 K scales [64] then zeros [64], after the 2368 record bytes
+
+  // One item in the stage at `st`: scores, softmax update and the O contraction. REC: an int8
+  // record dequantised in registers (permuted channels); else a bf16 tile pair read by ldmatrix.
+  auto item = [&](auto rec_tag, unsigned char* st, bool masked) {
+    constexpr bool REC = decltype(rec_tag)::value;
+    const uint32_t st32 = smem_u32(st);
+    float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if constexpr (REC) {
+      // The record's 64 K scales and 64 K zeros (float16) become float32 once per warp, in the
+      // stage's unused tail; lane (g, t) then reads those of its channels 16t .. 16t+15.
+      float* kf = reinterpret_cast<float*>(st + kKf);
+      {
+        const uint2 hw = *reinterpret_cast<const uint2*>(st + 2048 + 8 * lane);
+        const float2 f01 = h2f2(hw.x), f23 = h2f2(hw.y);
+        *reinterpret_cast<float4*>(kf + 4 * lane) = make_float4(f01.x, f01.y, f23.x, f23.y);
+      }
+      const uint4 cg0 = *reinterpret_cast<const uint4*>(st + ok0);
+      const uint4 cg8 = *reinterpret_cast<const uint4*>(st + ok8);
+      const uint32_t wg0[4] = {cg0.x, cg0.y, cg0.z, cg0.w}, wg8[4] = {cg8.x, cg8.y, cg8.z, cg8.w};
+      __syncwarp();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const float4 sc = *reinterpret_cast<const float4*>(kf + 16 * t + 4 * ks);
+        const float4 zc = *reinterpret_cast<const float4*>(kf + 64 + 16 * t + 4 * ks);
+        const float2 s01 = f2(sc.x, sc.y), s23 = f2(sc.z, sc.w), z01 = f2(zc.x, zc.y), z23 = f2(zc.z, zc.w);
+        float2 ua, ub, va, vb;
+        codes4(wg0[ks], ua, ub);
+        codes4(wg8[ks], va, vb);
+        const float2 k0 = __ffma2_rn(ua, s01, z01), k1 = __ffma2_rn(va, s01, z01);
+        const float2 k2 = __ffma2_rn(ub, s23, z23), k3 = __ffma2_rn(vb, s23, z23);
+        const uint32_t a[4] = {pack_bf2(k0.x, k0.y), pack_bf2(k1.x, k1.y), pack_bf2(k2.x, k2.y), pack_bf2(k3.x, k3.y)};
+        if (ks & 1)
+          mma_bf16(sb, a, bqp[ks][0], bqp[ks][1]);
+        else
+          mma_bf16(sa, a, bqp[ks][0], bqp[ks][1]);
+      }
+    } else {
+#pragma unroll
+      for (int ks = 0; ks < 4; ks += 2) {
+        uint32_t a[4], b[4];
+        ldsm_x4(st32 + koff[ks], a);
+        ldsm_x4(st32 + koff[ks + 1], b);
+        mma_bf16(sa, a, bq[ks][0], bq[ks][1]);
+        mma_bf16(sb, b, bq[ks + 1][0], bq[ks + 1][1]);
+      }
+    }
+    // Raw scores: a0, a1 (token g, rows 2t, 2t+1), a2, a3 (token g + 8).
+    float a0 = sa[0] + sb[0], a1 = sa[1] + sb[1], a2 = sa[2] + sb[2], a3 = sa[3] + sb[3];
+    if (!REC && masked) {
+      if (g >= last_fill) a0 = a1 = -INFINITY;
+      if (g + 8 >= last_fill) a2 = a3 = -INFINITY;
+    }
+    // ---- softmax update (log2 domain, lazy rescaling) ----
+    if (__any_sync(0xffffffffu, a0 > thr0 || a2 > thr0 || a1 > thr1 || a3 > thr1)) {
+      float mb0 = fmaxf(a0, a2) * sl2, mb1 = fmaxf(a1, a3) * sl2;
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
+        mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
+      }
+      if (mb0 > m0 + kLazy) {
+        const float alpha = exp2f(m0 - mb0);
+        l0 *= alpha;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          o[mt][0] *= alpha;
+          o[mt][2] *= alpha;
+        }
+        m0 = mb0;
+        nm0 = -mb0;
+        thr0 = (mb0 + kLazy) * inv_sl2;
+      }
+      if (mb1 > m1 + kLazy) {
+        const float alpha = exp2f(m1 - mb1);
+        l1 *= alpha;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          o[mt][1] *= alpha;
+          o[mt][3] *= alpha;
+        }
+        m1 = mb1;
+        nm1 = -mb1;
+        thr1 = (mb1 + kLazy) * inv_sl2;
+      }
+    }
+    const float p0 = ex2(fmaf(a0, sl2, nm0)), p2 = ex2(fmaf(a2, sl2, nm0));
+    const float p1 = ex2(fmaf(a1, sl2, nm1)), p3 = ex2(fmaf(a3, sl2, nm1));
+    l0 += p0 + p2;
+    l1 += p1 + p3;
+    uint32_t h01, md01, s01, h23, md23, s23;
+    split3(p0, p1, h01, md01, s01);
+    split3(p2, p3, h23, md23, s23);
+    const uint32_t bh0 = movtrans(h01), bh1 = movtrans(h23);
+    const uint32_t bm0 = movtrans(md01), bm1 = movtrans(md23);
+    const uint32_t bl0 = movtrans(s01), bl1 = movtrans(s23);
+
+    // ---- O^T += V^T . P^T ----
+    if constexpr (REC) {
+      const uint2 c0 = *reinterpret_cast<const uint2*>(st + ov0);
+      const uint2 c1 = *reinterpret_cast<const uint2*>(st + ov1);
+      const uint2 c2 = *reinterpret_cast<const uint2*>(st + ov8);
+      const uint2 c3 = *reinterpret_cast<const uint2*>(st + ov9);
+      const float2 vs01 = h2f2(*reinterpret_cast<const uint32_t*>(st + ovs));
+      const float2 vs89 = h2f2(*reinterpret_cast<const uint32_t*>(st + ovs + 16));
+      const float2 vz01 = h2f2(*reinterpret_cast<const uint32_t*>(st + ovz));
+      const float2 vz89 = h2f2(*reinterpret_cast<const uint32_t*>(st + ovz + 16));
+      const uint32_t e0[2] = {c0.x ^ 0x80808080u, c0.y ^ 0x80808080u}, e1[2] = {c1.x ^ 0x80808080u, c1.y ^ 0x80808080u};
+      const uint32_t e2[2] = {c2.x ^ 0x80808080u, c2.y ^ 0x80808080u}, e3[2] = {c3.x ^ 0x80808080u, c3.y ^ 0x80808080u};
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        const int wi = mt >> 1;
+        const uint32_t sel0 = 0x7650u + 2 * (mt & 1), sel1 = sel0 + 1;
+        const float2 v00 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel0), vs01, vz01);  // channel 8g+2mt, tokens 2t, 2t+1
+        const float2 v01 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel1), vs01, vz01);  // channel 8g+2mt+1
+        const float2 v80 = __ffma2_rn(code_pair(e2[wi], e3[wi], sel0), vs89, vz89);  // tokens 2t+8, 2t+9
+        const float2 v81 = __ffma2_rn(code_pair(e2[wi], e3[wi], sel1), vs89, vz89);
+        const uint32_t a[4] = {pack_bf2(v00.x, v00.y), pack_bf2(v01.x, v01.y), pack_bf2(v80.x, v80.y), pack_bf2(v81.x, v81.y)};
+        mma_bf16(o[mt], a, bl0, bl1);
+        mma_bf16(o[mt], a, bm0, bm1);
+        mma_bf16(o[mt], a, bh0, bh1);
+      }
+    } else {
+      const uint32_t vt = st32 + kMmaTile;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        uint32_t a[4];
+        ldsm_x4_t(vt + voff[mt], a);
+        mma_bf16(o[mt], a, bl0, bl1);
+        mma_bf16(o[mt], a, bm0, bm1);
+        mma_bf16(o[mt], a, bh0, bh1);
+      }
+    }
+  };
+
+  // The ring: item k sits in stage k % NS; the loop is unrolled over the stages so that every
+  // stage address and barrier is a constant, and the n-th use of a stage waits on parity n & 1.
+  int n_done = 0;
+  bool ok = true;
+  const bool parked_mid = hn > 0 && n_mine > hn;
 #pragma unroll 1
-  while (n_done < n_issued) {
-    if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (phase >> s) & 1u))) {
-      ok = false;
-      break;
-    }
-    phase ^= 1u << s;
-    ++n_done;
-    const int i = my_items[s];
-    const int row = list[i];
-    const int set = i < n_a ? 0 : 1;
-    const Seg& S = p.seg[set];
-    if (row >= 0) {
-      if (set != cur_set) {
-        if (cur_set >= 0) {
-          park_state(cur_set, true);
-          parked_mid = true;
-        }
-        cur_set = set;
-        m0 = m1 = -INFINITY;
-        l0 = l1 = 0.0f;
+  for (int base = 0; base < n_mine && ok; base += NS) {
+    const uint32_t par = (uint32_t)(base / NS) & 1u;
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int b = 0; b < 4; ++b) o[a][b] = 0.0f;
+    for (int u = 0; u < NS; ++u) {
+      const int k = base + u;
+      if (k >= n_mine) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars[u], par))) {
+        ok = false;
+        break;
       }
-      const int ord = sh_lo[set] + (set == 0 ? i : i - n_a);
-      const int fill = (S.kind == SEG_LIST && ord == S.n_list - 1) ? S.last_fill : 16;
-      const unsigned char* st = stage0 + s * kStreamStage;
-      const uint32_t st32 = smem_u32(st);
-      const bool rec = S.kind == SEG_RANGE_REC;
-
-      // ---- S^T = K . Q^T ----
-      float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      if (rec) {
-        const uint4 cg0 = *reinterpret_cast<const uint4*>(st + g * 64 + 16 * t);
-        const uint4 cg8 = *reinterpret_cast<const uint4*>(st + (g + 8) * 64 + 16 * t);
-        const uint4 s0 = *reinterpret_cast<const uint4*>(st + 2048 + 32 * t);
-        const uint4 s1 = *reinterpret_cast<const uint4*>(st + 2048 + 32 * t + 16);
-        const uint4 z0 = *reinterpret_cast<const uint4*>(st + 2176 + 32 * t);
-        const uint4 z1 = *reinterpret_cast<const uint4*>(st + 2176 + 32 * t + 16);
-        const uint32_t wg0[4] = {cg0.x, cg0.y, cg0.z, cg0.w}, wg8[4] = {cg8.x, cg8.y, cg8.z, cg8.w};
-        const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        const uint32_t zw[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const float2 s01 = h2f2(sw[2 * ks]), s23 = h2f2(sw[2 * ks + 1]);
-          const float2 z01 = h2f2(zw[2 * ks]), z23 = h2f2(zw[2 * ks + 1]);
-          float2 ua, ub, va, vb;
-          codes4(wg0[ks], ua, ub);
-          codes4(wg8[ks], va, vb);
-          const float2 k0 = __ffma2_rn(ua, s01, z01), k1 = __ffma2_rn(va, s01, z01);
-          const float2 k2 = __ffma2_rn(ub, s23, z23), k3 = __ffma2_rn(vb, s23, z23);
-          const uint32_t a[4] = {pack_bf2(k0.x, k0.y), pack_bf2(k1.x, k1.y), pack_bf2(k2.x, k2.y), pack_bf2(k3.x, k3.y)};
-          if (ks & 1)
-            mma_bf16(sb, a, bqp[ks][0], bqp[ks][1]);
-          else
-            mma_bf16(sa, a, bqp[ks][0], bqp[ks][1]);
-        }
-      } else {
-#pragma unroll
-        for (int ks = 0; ks < 4; ks += 2) {
-          uint32_t a[4], b[4];
-          ldsm_x4(st32 + koff[ks], a);
-          ldsm_x4(st32 + koff[ks + 1], b);
-          mma_bf16(sa, a, bq[ks][0], bq[ks][1]);
-          mma_bf16(sb, b, bq[ks + 1][0], bq[ks + 1][1]);
-        }
+      ++n_done;
+      if (k == hn && hn > 0) {  // segment 0 done: park its state, start segment 1's
+        park_state(0, true);
+        reset_state();
       }
-      float x0 = (sa[0] + sb[0]) * p.scale_log2, x1 = (sa[1] + sb[1]) * p.scale_log2;
-      float x2 = (sa[2] + sb[2]) * p.scale_log2, x3 = (sa[3] + sb[3]) * p.scale_log2;
-      if (fill < 16) {
-        if (g >= fill) x0 = x1 = -INFINITY;
-        if (g + 8 >= fill) x2 = x3 = -INFINITY;
+      if (list[list_index(k)] >= 0) {
+        unsigned char* st = stage0 + u * kStreamStage;
+        if (k < hn ? rec0 : rec1)
+          item(std::true_type{}, st, false);
+        else
+          item(std::false_type{}, st, k == fill_k);
       }
-      // ---- softmax update (log2 domain, lazy rescaling) ----
-      const bool need = x0 > m0 + kLazy || x2 > m0 + kLazy || x1 > m1 + kLazy || x3 > m1 + kLazy;
-      if (__any_sync(0xffffffffu, need)) {
-        float mb0 = fmaxf(x0, x2), mb1 = fmaxf(x1, x3);
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-          mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
-          mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
-        }
-        if (mb0 > m0 + kLazy) {
-          const float alpha = exp2f(m0 - mb0);
-          l0 *= alpha;
-#pragma unroll
-          for (int mt = 0; mt < 4; ++mt) {
-            o[mt][0] *= alpha;
-            o[mt][2] *= alpha;
-          }
-          m0 = mb0;
-        }
-        if (mb1 > m1 + kLazy) {
-          const float alpha = exp2f(m1 - mb1);
-          l1 *= alpha;
-#pragma unroll
-          for (int mt = 0; mt < 4; ++mt) {
-            o[mt][1] *= alpha;
-            o[mt][3] *= alpha;
-          }
-          m1 = mb1;
-        }
-      }
-      const float p0 = m0 == -INFINITY ? 0.0f : ex2(x0 - m0);
-      const float p2 = m0 == -INFINITY ? 0.0f : ex2(x2 - m0);
-      const float p1 = m1 == -INFINITY ? 0.0f : ex2(x1 - m1);
-      const float p3 = m1 == -INFINITY ? 0.0f : ex2(x3 - m1);
-      l0 += p0 + p2;
-      l1 += p1 + p3;
-      uint32_t h01, md01, s01, h23, md23, s23;
-      split3(p0, p1, h01, md01, s01);
-      split3(p2, p3, h23, md23, s23);
-      const uint32_t bh0 = movtrans(h01), bh1 = movtrans(h23);
-      const uint32_t bm0 = movtrans(md01), bm1 = movtrans(md23);
-      const uint32_t bl0 = movtrans(s01), bl1 = movtrans(s23);
-
-      // ---- O^T += V^T . P^T ----
-      if (rec) {
-        const unsigned char* vq = st + 1024;
-        const uint2 c0 = *reinterpret_cast<const uint2*>(vq + (2 * t) * 64 + 8 * g);
-        const uint2 c1 = *reinterpret_cast<const uint2*>(vq + (2 * t + 1) * 64 + 8 * g);
-        const uint2 c2 = *reinterpret_cast<const uint2*>(vq + (2 * t + 8) * 64 + 8 * g);
-        const uint2 c3 = *reinterpret_cast<const uint2*>(vq + (2 * t + 9) * 64 + 8 * g);
-        const float2 vs01 = h2f2(*reinterpret_cast<const uint32_t*>(st + 2304 + 4 * t));
-        const float2 vs89 = h2f2(*reinterpret_cast<const uint32_t*>(st + 2304 + 4 * t + 16));
-        const float2 vz01 = h2f2(*reinterpret_cast<const uint32_t*>(st + 2336 + 4 * t));
-        const float2 vz89 = h2f2(*reinterpret_cast<const uint32_t*>(st + 2336 + 4 * t + 16));
-        const uint32_t e0[2] = {c0.x ^ 0x80808080u, c0.y ^ 0x80808080u}, e1[2] = {c1.x ^ 0x80808080u, c1.y ^ 0x80808080u};
-        const uint32_t e2[2] = {c2.x ^ 0x80808080u, c2.y ^ 0x80808080u}, e3[2] = {c3.x ^ 0x80808080u, c3.y ^ 0x80808080u};
-#pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-          const int wi = mt >> 1;
-          const uint32_t sel0 = 0x7650u + 2 * (mt & 1), sel1 = sel0 + 1;
-          const float2 v00 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel0), vs01, vz01);  // channel 8g+2mt, tokens 2t, 2t+1
-          const float2 v01 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel1), vs01, vz01);  // channel 8g+2mt+1
-          const float2 v80 = __ffma2_rn(code_pair(e2[wi], e3[wi], sel0), vs89, vz89);  // tokens 2t+8, 2t+9
-          const float2 v81 = __ffma2_rn(code_pair(e2[wi], e3[wi], sel1), vs89, vz89);
-          const uint32_t a[4] = {pack_bf2(v00.x, v00.y), pack_bf2(v01.x, v01.y), pack_bf2(v80.x, v80.y), pack_bf2(v81.x, v81.y)};
-          mma_bf16(o[mt], a, bl0, bl1);
-          mma_bf16(o[mt], a, bm0, bm1);
-          mma_bf16(o[mt], a, bh0, bh1);
-        }
-      } else {
-        const uint32_t vt = st32 + kMmaTile;
-#pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-          uint32_t a[4];
-          ldsm_x4_t(vt + voff[mt], a);
-          mma_bf16(o[mt], a, bl0, bl1);
-          mma_bf16(o[mt], a, bm0, bm1);
-          mma_bf16(o[mt], a, bh0, bh1);
-        }
+      __syncwarp();  // every lane is done with the stage before it is refilled
+      if (k + NS < n_mine) {
+        issue(k + NS, u);
+        ++n_issued;
       }
     }
-    __syncwarp();  // every lane is done with the stage before it is refilled
-    if (n_issued < n_mine) {
-      issue(list_index(n_issued), s);
-      ++n_issued;
-    }
-    s = s + 1 == NS ? 0 : s + 1;
   }
-  // After a timed-out wait, wait (bounded) for the copies still in flight.
+  const int cur_set = n_mine == 0 ? -1 : (n_mine > hn ? 1 : 0);
+  // After a timed-out wait, wait (bounded) for the copies still in flight: items n_done .. n_issued-1.
   if (!ok) {
     for (int k = n_done; k < n_issued; ++k) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (phase >> s) & 1u))) break;
-      phase ^= 1u << s;
-      s = s + 1 == NS ? 0 : s + 1;
+      const int u = k % NS;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars[u], (uint32_t)(k / NS) & 1u))) break;
     }
     if (lane == 0) atomicExch(&sh_bad, 1);
   }
@@ -1873,6 +1902,7 @@ bool make_kv_maps(const Seg& S, int h, CUtensorMap* tk, CUtensorMap* tv, int* he
 // memory, 64-channel token rows); fills the tensor maps of its list / pairs segments.
 bool mma_plan(const AttnParams& p, int g, int d, bool bf16, MmaParams& mp) {
   if (!bf16 || d != 64 || p.bs != 16 || (g != 1 && g != 2 && g != 4 && g != 8)) return false;
+  if (!(p.scale_log2 > 0.0f)) return false;  // its lazy rescaling compares raw scores against (m + 8) / scale
   for (int i = 0; i < p.n_segs; ++i) {
     const Seg& S = p.seg[i];
     if (S.n_items == 0) continue;
