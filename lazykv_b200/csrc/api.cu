@@ -17,6 +17,21 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
 int launched(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));

@@ -991,6 +991,8 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     fence_mbar_init();
   }
 
+  pdl_wait();  // the lists, the bitmap and the workspace are the predecessor's to finish with
+  pdl_release();
   // ---- set-up: counts, this CTA's item range, its list of storage rows ----
   // A list segment's count is its length; a range's is a popcount over the bitmap. In the common
   // case (segment 0 a list, segment 1 a range of at most kSetupWords words per thread) the list's
@@ -1861,21 +1863,6 @@ void split_two(Seg& hot, Seg& cold, int h, double hot_item, double cold_item, in
 
 // ---- the tensor-core path -----------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    else
-      cudaGetLastError();
-  }
-  return fn;
-}
-
 // K and V maps of a list or pairs segment: 4-D bf16 tensors (channel, token, row, head) with a box of
 // one 16 x 64 block, 128-byte swizzle. The row and head dimensions are ordered by stride.
 bool make_kv_maps(const Seg& S, int h, CUtensorMap* tk, CUtensorMap* tv, int* head_major) {
@@ -1968,7 +1955,8 @@ int launch_stream(const StreamParams& sp, cudaStream_t st) {
     if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
     attr_set |= bit;
   }
-  k<<<dim3(sp.per_head, sp.p.h), kStreamThreads, C::SMEM, st>>>(sp);
+  cudaError_t e = launch_pdl(k, dim3(sp.per_head, sp.p.h), dim3(kStreamThreads), C::SMEM, st, 0, sp);
+  if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv attention: %s", cudaGetErrorString(e));
   return launched("lkv attention");
 }
 
@@ -2032,11 +2020,7 @@ extern "C" {
 
 int lkv_device_status(int* status, int clear) {
   if (status == nullptr) return fail(LKV_ERR_PTR, "lkv_device_status: null pointer");
-  cudaError_t e = cudaMemcpyFromSymbol(status, g_device_status, sizeof(int));
-  if (e == cudaSuccess && clear) {
-    const int zero = 0;
-    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
-  }
+  cudaError_t e = tu_device_status(status, clear);
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_device_status: %s", cudaGetErrorString(e));
   return LKV_OK;
 }

@@ -1,6 +1,8 @@
 // Shared helpers for the sm_100a kernels of liblkv_sm100.so.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -16,6 +18,9 @@ int fail(int code, const char* fmt, ...);
 int launched(const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// The driver's cuTensorMapEncodeTiled (null when the driver does not provide it).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 constexpr int kNumSMs = 148;  // B200
 
@@ -38,6 +43,38 @@ __device__ __forceinline__ uint32_t orderable(float x) {
 __device__ __forceinline__ float from_orderable(uint32_t o) {
   uint32_t u = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
   return __uint_as_float(u);
+}
+
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute may
+// start while its predecessor in the stream still runs. It calls pdl_wait() before it touches
+// anything the predecessor writes (or that a still-running earlier kernel reads), and pdl_release()
+// after that, so that its own dependent can start early; both are no-ops in an ordinary launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with the programmatic-serialization attribute (and a cluster of cluster_x CTAs when > 0).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster_x > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 // Loads of 8 consecutive elements as float (16 B of bf16 or 32 B of float32), read-only path.

@@ -181,6 +181,8 @@ __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __
   const int j = blockIdx.y;
   const int c_first = blockIdx.x * rows;
   const int n_rows = min(rows, n_cand - c_first);
+  pdl_wait();  // the query, the metadata and the workspace are the predecessor's to finish with
+  pdl_release();
   stage_query<TQ, G>(q, j, d, qs);
   const unsigned char* gmax = reinterpret_cast<const unsigned char*>(kmax + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
   const unsigned char* gmin = reinterpret_cast<const unsigned char*>(kmin + (int64_t)j * m_head + (int64_t)(first_block + c_first) * d);
@@ -432,6 +434,8 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(const uin
   const int hi = min(n_cand, lo + per);
   const int cnt = hi - lo;
   const uint64_t* src = keys_all + (int64_t)j * n_cand + lo;
+  pdl_wait();  // the keys and first-pass counts of the score kernel
+  pdl_release();
   for (int i = tid; i < cnt; i += blockDim.x) keys[i] = src[i];
   if (c == 0 && bitmap != nullptr)
     for (int w = tid; w < bitmap_words; w += blockDim.x) bitmap[(int64_t)j * bitmap_words + w] = 0u;
@@ -460,8 +464,12 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(const uin
       }
       cluster.sync();  // every rank's counts of this pass are final
       for (int b = tid; b < 256; b += blockDim.x) {
+        uint32_t v[kClusterMax];
+#pragma unroll
+        for (int r = 0; r < kClusterMax; ++r) v[r] = r < C ? *cluster.map_shared_rank(&hp[b], r) : 0u;  // all in flight at once
         uint32_t sum = 0;
-        for (int r = 0; r < C; ++r) sum += *cluster.map_shared_rank(&hp[b], r);
+#pragma unroll
+        for (int r = 0; r < kClusterMax; ++r) sum += v[r];
         ghist[b] = sum;
       }
       __syncthreads();
@@ -551,20 +559,8 @@ int launch_topk_cluster(int h, cudaStream_t st, const uint64_t* keys, uint32_t* 
   }
   const int C = cluster_size_for(n_cand);
   const int per = (n_cand + C - 1) / C;
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = C;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(C, h);
-  cfg.blockDim = dim3(kClusterThreads);
-  cfg.dynamicSmemBytes = (size_t)per * sizeof(uint64_t);
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, topk_cluster_kernel, keys, hist0, n_cand, k, first_block, n_passes, per, out_blocks, out_ld, bitmap,
-                                     bitmap_words);
+  cudaError_t e = launch_pdl(topk_cluster_kernel, dim3(C, h), dim3(kClusterThreads), (size_t)per * sizeof(uint64_t), st, C, keys, hist0, n_cand,
+                             k, first_block, n_passes, per, out_blocks, out_ld, bitmap, bitmap_words);
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk(cluster select, %d CTAs x %d heads): %s", C, h, cudaGetErrorString(e));
   return LKV_OK;
 }
@@ -590,8 +586,9 @@ int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void
   case G: {                                                                                                            \
     auto kern = quest_score_kernel<TQ, TM, G>;                                                                         \
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);          \
-    kern<<<grid, rows, smem, st>>>(static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin), static_cast<const TM*>(kmax), \
-                                   m_head, first_block, n_cand, bound_mode, keys, out_bound, hist0);                   \
+    cudaError_t le = launch_pdl(kern, grid, dim3(rows), smem, st, 0, static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin),      \
+                                static_cast<const TM*>(kmax), m_head, first_block, n_cand, bound_mode, keys, out_bound, hist0); \
+    if (le != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk(score): %s", cudaGetErrorString(le));             \
     break;                                                                                                             \
   }
   switch (g) {

@@ -6,13 +6,23 @@
 namespace lkv {
 
 // Status word of the kernels that wait on mbarriers: 0, or the first LKV_DEV_* code a kernel
-// recorded; read by lkv_device_status. Defined here because attention.cu, which holds those kernels
-// and that entry point, is the only translation unit that includes this header.
-__device__ int g_device_status = 0;
+// recorded. Internal linkage (the library is built without relocatable device code): attention.cu,
+// the one translation unit with such kernels, reads it for lkv_device_status with tu_device_status.
+static __device__ int g_device_status = 0;
 constexpr int LKV_DEV_WAIT_TIMEOUT = 1;       // an mbarrier wait ran out of iterations
 constexpr int LKV_DEV_LIST_OVERFLOW = 2;      // a CTA's item list would not fit its shared memory (host sizing error)
 constexpr uint32_t kMaxWaitIters = 1u << 21;  // tries; each may suspend up to kWaitHintNs
 constexpr uint32_t kWaitHintNs = 1000;        // suspend-time hint of one try (the wait ends sooner when the phase completes)
+
+// This translation unit's status word into *status (cleared after the read when `clear`).
+static inline cudaError_t tu_device_status(int* status, int clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_device_status, sizeof(int));
+  if (e == cudaSuccess && clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+  }
+  return e;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
