@@ -86,6 +86,11 @@ class Clocks:
             self.proc = None
         return self
 
+    def wait_first_sample(self, timeout: float) -> None:
+        t0 = time.perf_counter()
+        while self.proc is not None and not self.lines and time.perf_counter() - t0 < timeout:
+            time.sleep(0.01)
+
     def _read(self) -> None:
         assert self.proc is not None and self.proc.stdout is not None
         for line in self.proc.stdout:
@@ -280,6 +285,22 @@ def run_ours(args: argparse.Namespace) -> None:
             graph.replay()
         torch.cuda.synchronize()
 
+    def soak(fn, seconds: float) -> None:
+        # About `seconds` of back-to-back replays; the count is fixed from a short calibration and
+        # agreed across ranks (the graph holds collectives at N > 1, so every rank replays alike).
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        per = max((time.perf_counter() - t0) / 5, 1e-5)
+        n = torch.tensor([min(100000, int(seconds / per) + 1)], device=dev)
+        if world > 1:
+            dist.all_reduce(n, op=dist.ReduceOp.MAX)
+        for _ in range(int(n.item())):
+            fn()
+        torch.cuda.synchronize()
+
     def timed(fn, steps: int) -> float:
         if world > 1:
             dist.barrier()
@@ -297,8 +318,14 @@ def run_ours(args: argparse.Namespace) -> None:
             ms = float(t.item())
         return ms
 
+    # Clocks: nvidia-smi samples every 100 ms, so the sampler runs over a window of back-to-back
+    # replays (about half a second on either side) that contains the timed region.
+    run = graph.replay if graph is not None else step
     with Clocks(local) as clocks:
-        ms = timed(graph.replay if graph is not None else step, n_steps)
+        clocks.wait_first_sample(2.0)
+        soak(run, 0.5)
+        ms = timed(run, n_steps)
+        soak(run, 0.5)
     ms_step = ms / n_steps
     n_sel = args.layers
     us_layer = ms_step * 1e3 / n_sel

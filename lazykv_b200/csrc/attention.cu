@@ -884,14 +884,13 @@ struct StreamCfg {
   static constexpr int STAGES = 2;  // per warp (the loop is unrolled over them)
   static constexpr int SLOT = G * 64 + 2 * G;    // floats of a parked state: o [G][64], m [G], l [G]
   static constexpr int RING = kStreamWarps * STAGES * kStreamStage;
-  static constexpr int PARK = kStreamWarps * SLOT * 4;  // a warp's state of segment 0 when it moves on
+  static constexpr int PARK = kStreamWarps * 2 * SLOT * 4;  // each warp's state per segment
   static constexpr int LIST = kStreamListCap * 4;
   static constexpr int BARS = kStreamWarps * STAGES * 8;
   static constexpr size_t SMEM = 1024 + (size_t)RING + PARK + LIST + BARS;
   // Floats of one (CTA, set) partial in the workspace: o [G][64], m [G], l [G], padded to 16 bytes so
   // the rows of o are float4-aligned for every G.
   static constexpr int PART = (G * 64 + 2 * G + 3) / 4 * 4;
-  static_assert(kStreamWarps * 2 * SLOT * 4 <= RING, "final parked states live in the ring");
 };
 
 struct StreamParams {
@@ -1206,17 +1205,16 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   };
   reset_state();
   const int r0 = 2 * t, r1 = 2 * t + 1;
-  // Parks the state of `set` (channels back in natural order): in this warp's slot of the park area
-  // while other warps may still stream (dst_mid), else in the warp's final slot in the idle ring. A
-  // row that saw no key is parked as (m = -inf, l = 0).
-  auto park_state = [&](int set, bool dst_mid) {
+  // Parks the state of `set` in this warp's slot for it (channels back in natural order). A row that
+  // saw no key is parked as (m = -inf, l = 0).
+  auto park_state = [&](int set) {
     float la = l0, lb = l1;
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
       la += __shfl_xor_sync(0xffffffffu, la, off);
       lb += __shfl_xor_sync(0xffffffffu, lb, off);
     }
-    float* slot = set == 0 && dst_mid ? park + warp * C::SLOT : reinterpret_cast<float*>(ring) + (warp * 2 + set) * C::SLOT;
+    float* slot = park + (warp * 2 + set) * C::SLOT;
     const bool perm = set ? rec1 : rec0;
 #pragma unroll
     for (int mt = 0; mt < 4; ++mt) {
@@ -1402,7 +1400,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
       }
       ++n_done;
       if (k == hn && hn > 0) {  // segment 0 done: park its state, start segment 1's
-        park_state(0, true);
+        park_state(0);
         reset_state();
       }
       if (list[list_index(k)] >= 0) {
@@ -1428,47 +1426,48 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     }
     if (lane == 0) atomicExch(&sh_bad, 1);
   }
-  __syncthreads();  // every warp is done with the ring: final states go there
-  {
-    float* fin = reinterpret_cast<float*>(ring) + warp * 2 * C::SLOT;
-    if (parked_mid)
-      for (int e = lane; e < C::SLOT; e += 32) fin[e] = park[warp * C::SLOT + e];
-    if (cur_set >= 0) park_state(cur_set, false);
-    // A set this warp holds no state of: empty (m = -inf).
-    for (int set = 0; set < 2; ++set)
-      if (set != cur_set && !(set == 0 && parked_mid))
-        for (int r = lane; r < G; r += 32) fin[set * C::SLOT + G * D + r] = -INFINITY;
+  if (cur_set >= 0) park_state(cur_set);
+  // A set this warp holds no state of: empty (m = -inf).
+  if (lane < G) {
+    if (cur_set != 0 && !parked_mid) park[(warp * 2 + 0) * C::SLOT + G * D + lane] = -INFINITY;
+    if (cur_set != 1) park[(warp * 2 + 1) * C::SLOT + G * D + lane] = -INFINITY;
   }
   __syncthreads();
 
   // ---- fold the warps' parked states: one partial per set for this CTA ----
+  // Per (set, row), one warp: lane w reads warp w's maximum, the lanes agree on the maximum M and
+  // the sum L by shuffles, and lane w's weight 2^(m_w - M) goes to shared memory; then every thread
+  // folds one output element with those weights.
   const int64_t part_stride = C::PART;
-  const float* fin_all = reinterpret_cast<const float*>(ring);
   float* mine = sp.part + (((int64_t)j * P + ci) * 2) * part_stride;
+  __shared__ float fold_w[2 * 8][NW > 32 ? NW : 32];  // [(set, row)][warp or partial] weights
+  static_assert(NW <= 32, "one lane per warp");
+  for (int pr = warp; pr < 2 * G; pr += NW) {
+    const int set = pr / G, r = pr % G;
+    const float* sl = park + (lane * 2 + set) * C::SLOT;
+    const float mw = (lane < NW && !sh_bad) ? sl[G * D + r] : -INFINITY;
+    float M = mw;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float f = (M == -INFINITY || mw == -INFINITY) ? 0.0f : exp2f(mw - M);
+    float L = f != 0.0f ? f * sl[G * D + G + r] : 0.0f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    if (lane < NW) fold_w[pr][lane] = f;
+    if (lane == 0) {
+      mine[set * part_stride + G * D + r] = M;
+      mine[set * part_stride + G * D + G + r] = L;
+    }
+  }
+  __syncthreads();
   for (int e = threadIdx.x; e < 2 * G * D; e += blockDim.x) {
     const int set = e / (G * D), r = (e / D) % G, c = e % D;
-    float* out = mine + set * part_stride;
-    float M = -INFINITY;
-    if (!sh_bad)
+    const float* wr = fold_w[set * G + r];
+    float O = 0.0f;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) M = fmaxf(M, fin_all[(w * 2 + set) * C::SLOT + G * D + r]);
-    float O = 0.0f, Lr = 0.0f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float* sl = fin_all + (w * 2 + set) * C::SLOT;
-        const float mw = sl[G * D + r];
-        if (mw == -INFINITY) continue;
-        const float f = exp2f(mw - M);
-        O = fmaf(sl[r * D + c], f, O);
-        Lr = fmaf(sl[G * D + G + r], f, Lr);
-      }
-    }
-    out[r * D + c] = O;
-    if (c == 0) {
-      out[G * D + r] = M;
-      out[G * D + G + r] = Lr;
-    }
+    for (int w = 0; w < NW; ++w)
+      if (wr[w] != 0.0f) O = fmaf(park[(w * 2 + set) * C::SLOT + r * D + c], wr[w], O);  // a zero weight: the slot may be unset
+    mine[set * part_stride + r * D + c] = O;
   }
   __threadfence();
   __syncthreads();
@@ -1479,13 +1478,12 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
 
   // ---- the head's last CTA: fold its P partials per set into the outputs ----
   // The head's partials are contiguous in the workspace: one bulk copy brings them into the idle
-  // ring (when they fit); then per (set, row) the maximum, the weights 2^(m - M) and the sum, and
-  // the outputs, all from shared memory. Otherwise they are read from the workspace directly.
+  // ring (when they fit); per (set, row) a warp finds the maximum, the weights and the sum by
+  // shuffles (lanes over the partials); then every thread folds one output element.
   const float* hp = sp.part + (int64_t)j * P * 2 * part_stride;
   const int nset = p.n_segs;
   const size_t head_bytes = (size_t)P * 2 * C::PART * sizeof(float);
-  const size_t wts_off = (head_bytes + 15) / 16 * 16;
-  const bool bulk = wts_off + (size_t)(2 * G * P + 4 * G) * sizeof(float) <= (size_t)C::RING;
+  const bool bulk = head_bytes <= (size_t)C::RING;
   bool got = true;
   if (bulk && threadIdx.x == 0) {
     asm volatile("fence.proxy.async;" ::: "memory");  // the partials (generic stores of other CTAs) before the bulk reads
@@ -1497,28 +1495,26 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   }
   if (bulk) got = __syncthreads_and(mbar_wait(&fold_bar, 0));
   const float* parts = bulk ? reinterpret_cast<const float*>(ring) : hp;
-  float* wts = reinterpret_cast<float*>(ring + wts_off);  // [2][G][P] (bulk only)
-  float* setM = wts + 2 * G * P;                          // [2][G]
-  float* setL = setM + 2 * G;                             // [2][G]
-  if (bulk && got) {
-    for (int e = threadIdx.x; e < 2 * G; e += blockDim.x) {
-      const int set = e / G, r = e % G;
-      float M = -INFINITY;
-      for (int k = 0; k < P; ++k) M = fmaxf(M, parts[(k * 2 + set) * part_stride + G * D + r]);
-      setM[e] = M;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < 2 * G * P; e += blockDim.x) {
-      const int set = e / (G * P), r = (e / P) % G, k = e % P;
-      const float M = setM[set * G + r], mk = parts[(k * 2 + set) * part_stride + G * D + r];
-      wts[e] = (M == -INFINITY || mk == -INFINITY) ? 0.0f : exp2f(mk - M);
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < 2 * G; e += blockDim.x) {
-      const int set = e / G, r = e % G;
+  // The weights of up to 32 partials per (set, row) live in fold_w; more partials go through the
+  // workspace one pass per row (P <= 32 covers kStreamCtasPerSm x SMs / h for h >= 5 on B200).
+  __shared__ float setM[2 * 8], setL[2 * 8];
+  if (P <= 32 && got) {
+    for (int pr = warp; pr < 2 * G; pr += NW) {
+      const int set = pr / G, r = pr % G;
+      const float mk = (lane < P && set < nset) ? (bulk ? parts[(lane * 2 + set) * part_stride + G * D + r] : __ldcg(parts + (lane * 2 + set) * part_stride + G * D + r)) : -INFINITY;
+      float M = mk;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      const float f = (M == -INFINITY || mk == -INFINITY) ? 0.0f : exp2f(mk - M);
       float L = 0.0f;
-      for (int k = 0; k < P; ++k) L = fmaf(parts[(k * 2 + set) * part_stride + G * D + G + r], wts[(set * G + r) * P + k], L);
-      setL[e] = L;
+      if (f != 0.0f) L = f * (bulk ? parts[(lane * 2 + set) * part_stride + G * D + G + r] : __ldcg(parts + (lane * 2 + set) * part_stride + G * D + G + r));
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      if (lane < P) fold_w[pr][lane] = f;
+      if (lane == 0) {
+        setM[pr] = M;
+        setL[pr] = L;
+      }
     }
     __syncthreads();
   }
@@ -1529,13 +1525,16 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     for (int set = 0; set < 2; ++set) {
       if (set >= nset || !got) break;
       float O = 0.0f, M = -INFINITY, L = 0.0f;
-      if (bulk) {
-        const float* wr = wts + (set * G + r) * P;
+      if (P <= 32) {
+        const float* wr = fold_w[set * G + r];
 #pragma unroll 4
-        for (int k = 0; k < P; ++k) O = fmaf(parts[(k * 2 + set) * part_stride + r * D + c], wr[k], O);
+        for (int k = 0; k < P; ++k) {
+          const float* pk = parts + (k * 2 + set) * part_stride + r * D + c;
+          O = fmaf(bulk ? *pk : __ldcg(pk), wr[k], O);
+        }
         M = setM[set * G + r];
         L = setL[set * G + r];
-      } else {  // more partials than the idle ring holds: straight from the workspace
+      } else {  // more partials than a warp's lanes: straight from the workspace
         for (int k = 0; k < P; ++k) M = fmaxf(M, __ldcg(hp + (k * 2 + set) * part_stride + G * D + r));
         if (M != -INFINITY)
           for (int k = 0; k < P; ++k) {
