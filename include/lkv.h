@@ -101,8 +101,11 @@ int lkv_fetch_pairs(const void* src, int src_kind, const int64_t* src_rows, void
  * LKV_ORDER_BLOCK in ascending block id (no sort). Optional: out_bound [h, n_cand] float32;
  * bitmap [h, bitmap_words] set exactly at the selected block ids (the words are cleared first).
  * Workspace: lkv_quest_topk_workspace(h, n_cand) bytes, zero-filled once when allocated: its first
- * 64 KiB hold per-head counters that the LKV_ORDER_BLOCK path expects at zero and leaves at zero
- * (calls on one workspace must not overlap on the GPU).
+ * 64 KiB + 593,920 bytes hold per-head counters and state that the LKV_ORDER_BLOCK paths expect at
+ * zero (where they count) and leave so (calls on one workspace must not overlap on the GPU). With bf16 query and metadata
+ * at head_dim 64 in LKV_ORDER_BLOCK the selection is one launch whose CTAs wait for one another
+ * (bounded waits, a timeout recorded in lkv_device_status); it is taken only when all of its CTAs
+ * fit on the GPU at once.
  */
 size_t lkv_quest_topk_workspace(int h, int n_cand);
 int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
@@ -115,7 +118,8 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
  * lkv_quest_topk without a workspace argument, for callers that cannot allocate device memory
  * when they select (an allocator-free runtime, an allocator callback, a process that reserved all
  * device memory up front). No counterpart in the reference. Same arguments, results and errors
- * as lkv_quest_topk; its scratch is a fixed 4 MiB device array inside the library, so it takes
+ * as lkv_quest_topk; its scratch is a fixed device array inside the library (4 MiB of keys after
+ * the per-head counters, 4.3 MiB in all), so it takes
  * h * n_cand <= 524,288 and returns LKV_ERR_ARG above that. It allocates nothing. The first call
  * on a device looks up that array's device address (make it before any stream capture); calls
  * must run with the stream's device current. All calls share the array: calls that overlap on

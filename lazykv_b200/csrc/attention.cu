@@ -2019,8 +2019,11 @@ extern "C" {
 
 int lkv_device_status(int* status, int clear) {
   if (status == nullptr) return fail(LKV_ERR_PTR, "lkv_device_status: null pointer");
-  cudaError_t e = tu_device_status(status, clear);
+  int a = 0, b = 0;
+  cudaError_t e = tu_device_status(&a, clear);
+  if (e == cudaSuccess) e = select_device_status(&b, clear);
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_device_status: %s", cudaGetErrorString(e));
+  *status = a != 0 ? a : b;
   return LKV_OK;
 }
 

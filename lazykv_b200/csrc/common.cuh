@@ -21,6 +21,8 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 // The driver's cuTensorMapEncodeTiled (null when the driver does not provide it).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+// The status word of select.cu's kernels with bounded waits (see tma.cuh).
+cudaError_t select_device_status(int* status, int clear);
 
 constexpr int kNumSMs = 148;  // B200
 

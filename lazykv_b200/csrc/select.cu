@@ -17,6 +17,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -412,6 +413,16 @@ constexpr int kClusterMax = 16;
 constexpr int kClusterMaxPer = 4096;   // keys per CTA (in shared memory)
 constexpr int kHistHeads = 64;         // heads the first-pass histograms are kept for
 constexpr size_t kHistBytes = (size_t)kHistHeads * 256 * sizeof(uint32_t);  // at the workspace's start
+// Per-head state of the single-launch select, after the first-pass counters: [0] arrivals, [1]
+// departures, the head's counts of passes 0..3 (256 each) -- all zero between calls -- then, per CTA
+// (up to kCoopMaxP), its count of keys above the prefix of the earlier passes and the suffix sums of
+// its histogram of the current pass (256 x uint16), rewritten every pass. The keys of the two-launch
+// path follow.
+constexpr int kCoopMaxP = 64;
+constexpr int kCoopHeads = 16;
+constexpr int kCoopHeadWords = 2 + 4 * 256 + kCoopMaxP + kCoopMaxP * 128;
+constexpr size_t kCoopBytes = (size_t)kCoopHeads * kCoopHeadWords * sizeof(uint32_t);
+constexpr size_t kKeysOffset = kHistBytes + kCoopBytes;
 
 __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(const uint64_t* __restrict__ keys_all, uint32_t* __restrict__ hist0,
                                                                      int n_cand, int k, int first_block, int n_passes, int per,
@@ -565,6 +576,351 @@ int launch_topk_cluster(int h, cudaStream_t st, const uint64_t* keys, uint32_t* 
   return LKV_OK;
 }
 
+// ---- single-launch selection: scoring and a per-head radix select with in-kernel barriers --------
+//
+// For a bf16 query and bf16 metadata at head_dim 64, block-id order. The grid is h x P CTAs
+// (P = ceil(n_cand / 256)), launched only when the host finds that all of them fit on the GPU at
+// once, and not before its predecessor in the stream has finished, so every CTA is resident. CTA c
+// of head j brings its 256 candidates' kmax and kmin rows in by tensor-map TMA (boxes of 128 rows,
+// 128-byte swizzle: chunk x of row r at chunk x ^ (r & 7), conflict-free per-row reads), and thread t
+// scores row t as quest_score_kernel does (same order and roundings), keeping the 64-bit key in a
+// register. Each radix pass of the select is global per head: every CTA adds its histogram of the
+// current digit to the head's counts in the workspace, a per-head barrier (an arrival counter;
+// waits bounded, a timeout recorded in the status word) completes the pass, and every CTA reads the
+// counts and picks the same digit. The compaction publishes each CTA's (above, tied) totals behind
+// one more barrier; a CTA's output offset and its share of the tied keys (lowest ids first) come
+// from the totals of the CTAs before it, as in topk_cluster_kernel. The head's last CTA to leave
+// returns its counters and counts to zero.
+
+constexpr int kCoopThreads = 256;
+constexpr int kCoopBoxRows = 128;
+constexpr int kCoopBox = kCoopBoxRows * 128;               // bytes of one box: 128 rows of 64 bf16
+constexpr size_t kCoopSmem = 1024 + 4 * (size_t)kCoopBox;  // kmax boxes 0, 1 then kmin boxes 0, 1
+constexpr uint32_t kCoopWaitIters = 1u << 22;              // tries of a barrier wait (each sleeps ~64 ns)
+
+struct CoopParams {
+  CUtensorMap tmax, tmin;  // [h][rows][64] bf16, box {64, 128, 1}, 128-byte swizzle
+  const __nv_bfloat16* q;
+  int n_cand, k, first_block, n_passes, bound_mode;
+  int32_t* out_blocks;
+  int out_ld;
+  uint32_t* bitmap;
+  int bitmap_words;
+  float* out_bound;
+  uint32_t* state;  // [h][kCoopHeadWords], zero on entry, left zero
+};
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Arrive at the head's barrier and wait (bounded) for `target` arrivals; every thread of the CTA
+// calls it. Returns false when the wait ran out (recorded in the status word).
+__device__ bool coop_barrier(uint32_t* arrive, uint32_t target, int* sh_ok) {
+  __syncthreads();  // the CTA's global writes before the barrier are issued
+  if (threadIdx.x == 0) {
+    __threadfence();
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(arrive) : "memory");
+    bool ok = false;
+    for (uint32_t i = 0; i < kCoopWaitIters; ++i) {
+      if (ld_acquire_gpu(arrive) >= target) {
+        ok = true;
+        break;
+      }
+      if (i >= 256) __nanosleep(64);
+    }
+    if (!ok) atomicCAS(&g_device_status, 0, LKV_DEV_WAIT_TIMEOUT);
+    *sh_ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  return *sh_ok != 0;
+}
+
+// row_bound's bf16 x bf16 arithmetic on a swizzled box row (d = 64: 8 chunks of 16 bytes).
+template <int G>
+__device__ __forceinline__ float row_bound_swz(const unsigned char* bmax, const unsigned char* bmin, int r, const float* qs, int bound_mode) {
+  constexpr int GP = qpad<G>();
+  constexpr int NP = GP / 2;
+  float2 a[NP], b[NP];
+#pragma unroll
+  for (int x = 0; x < NP; ++x) a[x] = b[x] = make_float2(0.0f, 0.0f);
+  const float2* qp = reinterpret_cast<const float2*>(qs);
+  const float2* qn = reinterpret_cast<const float2*>(qs + GP * 64);
+#pragma unroll 2
+  for (int c = 0; c < 8; ++c) {
+    const int pos = r * 128 + ((c ^ (r & 7)) << 4);
+    const uint4 x = *reinterpret_cast<const uint4*>(bmax + pos), y = *reinterpret_cast<const uint4*>(bmin + pos);
+    const uint32_t wx[4] = {x.x, x.y, x.z, x.w}, wy[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float mx = __uint_as_float((i & 1) ? (wx[i / 2] & 0xffff0000u) : (wx[i / 2] << 16));
+      const float mn = __uint_as_float((i & 1) ? (wy[i / 2] & 0xffff0000u) : (wy[i / 2] << 16));
+      const float2 x2 = make_float2(mx, mx), n2 = make_float2(mn, mn);
+      if constexpr (NP % 2 == 0) {  // the rows' q+ and q- of one channel in 16-byte loads
+#pragma unroll
+        for (int w = 0; w < NP; w += 2) {
+          const float4 p4 = reinterpret_cast<const float4*>(qp)[((c * 8 + i) * NP + w) / 2];
+          const float4 n4 = reinterpret_cast<const float4*>(qn)[((c * 8 + i) * NP + w) / 2];
+          a[w] = __ffma2_rn(make_float2(p4.x, p4.y), x2, a[w]);
+          a[w + 1] = __ffma2_rn(make_float2(p4.z, p4.w), x2, a[w + 1]);
+          b[w] = __ffma2_rn(make_float2(n4.x, n4.y), n2, b[w]);
+          b[w + 1] = __ffma2_rn(make_float2(n4.z, n4.w), n2, b[w + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int w = 0; w < NP; ++w) {
+          a[w] = __ffma2_rn(qp[(c * 8 + i) * NP + w], x2, a[w]);
+          b[w] = __ffma2_rn(qn[(c * 8 + i) * NP + w], n2, b[w]);
+        }
+      }
+    }
+  }
+  float best = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < G; ++w) {
+    const float ar = (w & 1) ? a[w / 2].y : a[w / 2].x, br = (w & 1) ? b[w / 2].y : b[w / 2].x;
+    const float sc = bound_mode == LKV_BF16 ? bf16_round(__fadd_rn(bf16_round(ar), bf16_round(br))) : __fadd_rn(ar, br);
+    best = fmaxf(best, sc);
+  }
+  return best;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kCoopThreads) quest_select_coop_kernel(const __grid_constant__ CoopParams cp) {
+  const int j = blockIdx.y, c = blockIdx.x, P = gridDim.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  extern __shared__ unsigned char csmem_raw[];
+  unsigned char* tiles = csmem_raw + ((1024 - (smem_u32(csmem_raw) & 1023)) & 1023);
+  __shared__ __align__(16) float qs[2 * qpad<G>() * 64];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t hist[256], gh[256];
+  __shared__ uint32_t low[kCoopMaxP][2];
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total, sh_pos0, sh_eq0;
+  __shared__ int sh_ok, sh_last;
+
+  uint32_t* st = cp.state + (size_t)j * kCoopHeadWords;
+  uint32_t* arrive = st;
+  uint32_t* depart = st + 1;
+  uint32_t* counts = st + 2;                                                   // [pass][256]
+  uint32_t* above_g = st + 2 + 4 * 256;                                        // [P]
+  uint16_t* suf_g = reinterpret_cast<uint16_t*>(st + 2 + 4 * 256 + kCoopMaxP);  // [P][256]
+  const int n_cand = cp.n_cand;
+  const int lo = c * kCoopThreads;
+  const int cnt = min(kCoopThreads, n_cand - lo);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  pdl_wait();  // no-op: this kernel is launched without the programmatic attribute
+  stage_query<__nv_bfloat16, G>(cp.q, j, 64, qs);
+  hist[tid] = 0u;
+  if (c == 0 && cp.bitmap != nullptr)
+    for (int w = tid; w < cp.bitmap_words; w += blockDim.x) cp.bitmap[(int64_t)j * cp.bitmap_words + w] = 0u;
+  __syncthreads();
+  if (tid == 0) {
+    const int r0 = cp.first_block + lo;
+    mbar_arrive_expect_tx(&bar, 4u * kCoopBox);
+    tma_load_3d(tiles, &cp.tmax, 0, r0, j, &bar);
+    tma_load_3d(tiles + kCoopBox, &cp.tmax, 0, r0 + kCoopBoxRows, j, &bar);
+    tma_load_3d(tiles + 2 * kCoopBox, &cp.tmin, 0, r0, j, &bar);
+    tma_load_3d(tiles + 3 * kCoopBox, &cp.tmin, 0, r0 + kCoopBoxRows, j, &bar);
+  }
+  bool ok = __syncthreads_and(mbar_wait(&bar, 0)) != 0;
+
+  // ---- this thread's key ----
+  const bool have = tid < cnt;
+  uint32_t ob = 0;
+  if (have && ok) {
+    const int bx = tid / kCoopBoxRows, r = tid % kCoopBoxRows;
+    const float best = row_bound_swz<G>(tiles + bx * kCoopBox, tiles + (2 + bx) * kCoopBox, r, qs, cp.bound_mode);
+    ob = orderable(best);
+    if (cp.out_bound != nullptr) cp.out_bound[(int64_t)j * n_cand + lo + tid] = best == 0.0f ? 0.0f : best;
+  }
+
+  // ---- radix passes, global per head; the last one also yields the compaction offsets ----
+  // Each pass publishes this CTA's count of keys already above the prefix (from earlier passes) and
+  // the suffix sums of its histogram of the pass's digit, so that after the pass that fixes the
+  // k-th key no further barrier is needed: CTA c's offset is the lower CTAs' keys above the final
+  // prefix plus their share of the tied keys, read from what they published.
+  const int kk = cp.k < n_cand ? cp.k : n_cand;
+  if (tid == 0) {
+    sh_remaining = (uint32_t)kk;
+    sh_bincount = 0;
+  }
+  __shared__ uint32_t suf[257];
+  uint32_t prefix = 0, mask = 0, above = 0;
+  const bool all = kk >= n_cand;
+  bool take_all = all;
+  uint32_t barriers = 0, d_last = 0;
+  for (int pass = 0; pass < cp.n_passes && !all; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const bool counted = have && (ob & mask) == prefix;
+    const uint32_t digit = counted ? ((ob >> shift) & 255u) : 256u;
+    const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+    if (counted && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+    __syncthreads();
+    // suffix sums of the histogram: suf[b] = keys of this CTA at digit >= b (suf[256] = 0)
+    {
+      const uint32_t v = hist[255 - tid];
+      const uint32_t incl = block_scan(v, warp_sums, &sh_total) + v;  // over reversed bins
+      suf[255 - tid] = incl;
+      if (tid == 0) suf[256] = 0u;
+      const uint32_t hv = hist[tid];
+      if (hv != 0u) atomicAdd(&counts[pass * 256 + tid], hv);
+    }
+    __syncthreads();
+    suf_g[(size_t)c * 256 + tid] = (uint16_t)suf[tid];
+    if (tid == 0) above_g[c] = above;
+    ok = coop_barrier(arrive, ++barriers * (uint32_t)P, &sh_ok) && ok;
+    gh[tid] = __ldcg(&counts[pass * 256 + tid]);
+    hist[tid] = 0u;
+    __syncthreads();
+    pick_digit(gh, &sh_digit, &sh_remaining, &sh_bincount);
+    __syncthreads();
+    d_last = sh_digit;
+    prefix |= d_last << shift;
+    mask |= 255u << shift;
+    take_all = (sh_bincount == sh_remaining);
+    if (take_all || pass == cp.n_passes - 1) break;  // uniform: every CTA picked the same digit
+    above += suf[d_last + 1];
+    __syncthreads();
+  }
+  const uint32_t need = take_all ? 0xffffffffu : sh_remaining;
+
+  // ---- compaction in candidate order across the head's CTAs ----
+  const bool gt = have && (all || (ob & mask) > prefix || (take_all && (ob & mask) == prefix));
+  const bool eq = have && !all && !take_all && (ob & mask) == prefix;
+  const uint32_t pre = block_scan((gt ? 1u : 0u) | ((eq ? 1u : 0u) << 16), warp_sums, &sh_total);
+  if (all) {
+    // every candidate is taken: offsets are c * 256
+    if (tid == 0) {
+      sh_pos0 = (uint32_t)lo;
+      sh_eq0 = 0u;
+    }
+  } else {
+    if (tid < c) {
+      const uint32_t ab = __ldcg(&above_g[tid]);
+      const uint32_t s0 = __ldcg(&suf_g[(size_t)tid * 256 + d_last]);
+      const uint32_t s1 = d_last < 255 ? __ldcg(&suf_g[(size_t)tid * 256 + d_last + 1]) : 0u;
+      low[tid][0] = ab + (take_all ? s0 : s1);  // keys above the final prefix (a taken bin counts whole)
+      low[tid][1] = take_all ? 0u : s0 - s1;     // keys at the final prefix (tied)
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t eqb = 0, posb = 0;
+      for (int r = 0; r < c; ++r) {
+        const uint32_t take = eqb < need ? min(low[r][1], need - eqb) : 0u;
+        posb += low[r][0] + take;
+        eqb += low[r][1];
+      }
+      sh_pos0 = posb;
+      sh_eq0 = eqb;
+    }
+  }
+  __syncthreads();
+  pdl_release();  // every CTA of the grid is resident (all arrived): the attention may launch
+  const uint32_t gt_before = pre & 0xffffu, eq_before = pre >> 16;
+  const uint32_t room = sh_eq0 < need ? need - sh_eq0 : 0u;  // tied keys this CTA may still take
+  const bool take = gt || (eq && eq_before < room);
+  const uint32_t pos = sh_pos0 + gt_before + min(eq_before, room);
+  if (take && pos < (uint32_t)kk && ok) {
+    const int blk = cp.first_block + lo + tid;
+    cp.out_blocks[(int64_t)j * cp.out_ld + pos] = blk;
+    if (cp.bitmap != nullptr && blk / 32 < cp.bitmap_words) atomicOr(&cp.bitmap[(int64_t)j * cp.bitmap_words + blk / 32], 1u << (blk % 32));
+  }
+
+  // ---- the head's last CTA to leave zeroes its state ----
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    sh_last = atomicAdd(depart, 1u) == (uint32_t)(P - 1);
+  }
+  __syncthreads();
+  if (sh_last) {
+    for (int w = tid; w < 2 + 4 * 256; w += blockDim.x) st[w] = 0u;
+  }
+}
+
+// Whether the single-launch select takes this call (bf16 query and metadata, head_dim 64, block-id
+// order, at most 64 CTAs of 256 candidates per head and every CTA resident at once); fills its maps.
+template <int G>
+bool coop_fits(int h, int P) {
+  static int per_sm[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& m = per_sm[dev & 63];
+  if (m == 0) {
+    auto kern = quest_select_coop_kernel<G>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCoopSmem);
+    int n = 0;
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kCoopThreads, kCoopSmem);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      n = -1;
+    }
+    m = n > 0 ? n : -1;
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return m > 0 && (int64_t)m * sms >= (int64_t)h * P;
+}
+
+bool coop_plan(int g, int q_dtype, int meta_dtype, int h, int d, const void* kmin, const void* kmax, int64_t m_head, int first_block, int n_cand,
+               int order, CoopParams& cp) {
+  if (q_dtype != LKV_BF16 || meta_dtype != LKV_BF16 || d != 64 || order != LKV_ORDER_BLOCK || h > kCoopHeads) return false;
+  const int P = (n_cand + kCoopThreads - 1) / kCoopThreads;
+  if (P > kCoopMaxP || h > 65535) return false;
+  bool fits = false;
+  switch (g) {
+    case 1: fits = coop_fits<1>(h, P); break;
+    case 2: fits = coop_fits<2>(h, P); break;
+    case 4: fits = coop_fits<4>(h, P); break;
+    case 8: fits = coop_fits<8>(h, P); break;
+    default: return false;
+  }
+  if (!fits) return false;
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[3] = {64, (cuuint64_t)first_block + (cuuint64_t)n_cand, (cuuint64_t)h};
+  const cuuint64_t strides[2] = {128, (cuuint64_t)m_head * 2};
+  const cuuint32_t box[3] = {64, kCoopBoxRows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  for (int i = 0; i < 2; ++i) {
+    CUresult r = enc(i == 0 ? &cp.tmax : &cp.tmin, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(i == 0 ? kmax : kmin), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+  }
+  return true;
+}
+
+int launch_coop(int g, const CoopParams& cp, int h, int P, cudaStream_t st) {
+  cudaError_t e = cudaErrorInvalidValue;
+  const dim3 grid(P, h), block(kCoopThreads);
+  switch (g) {
+    case 1: quest_select_coop_kernel<1><<<grid, block, kCoopSmem, st>>>(cp); break;
+    case 2: quest_select_coop_kernel<2><<<grid, block, kCoopSmem, st>>>(cp); break;
+    case 4: quest_select_coop_kernel<4><<<grid, block, kCoopSmem, st>>>(cp); break;
+    case 8: quest_select_coop_kernel<8><<<grid, block, kCoopSmem, st>>>(cp); break;
+    default: return fail(LKV_ERR_ARG, "lkv_quest_topk: query group %d not in {1,2,4,8}", g);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk(single launch, %d x %d CTAs): %s", P, h, cudaGetErrorString(e));
+  return LKV_OK;
+}
+
 // Keys of gathered candidates: (orderable bound << 32) | ~id, so the select decodes the id itself.
 __global__ void merge_keys_kernel(const float* __restrict__ bounds, const int32_t* __restrict__ ids, int n, int64_t ld,
                                   uint64_t* __restrict__ keys) {
@@ -606,12 +962,16 @@ int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void
 }  // namespace
 }  // namespace lkv
 
+namespace lkv {
+cudaError_t select_device_status(int* status, int clear) { return tu_device_status(status, clear); }
+}  // namespace lkv
+
 using namespace lkv;
 
 extern "C" {
 
 size_t lkv_quest_topk_workspace(int h, int n_cand) {
-  return kHistBytes + (size_t)(h > 0 ? h : 0) * (size_t)(n_cand > 0 ? n_cand : 0) * sizeof(uint64_t);
+  return kKeysOffset + (size_t)(h > 0 ? h : 0) * (size_t)(n_cand > 0 ? n_cand : 0) * sizeof(uint64_t);
 }
 
 int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax,
@@ -641,9 +1001,30 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   // bits order the keys: two 8-bit passes reach the k-th bound; ties go to the scan.
   const int n_passes = bound_mode == LKV_BF16 ? 2 : 4;
   uint32_t* hist0 = static_cast<uint32_t*>(workspace);  // first-pass histograms, zero between calls
-  uint64_t* keys = reinterpret_cast<uint64_t*>(static_cast<unsigned char*>(workspace) + kHistBytes);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(static_cast<unsigned char*>(workspace) + kKeysOffset);
   // Ascending block-id order with at most kHistHeads heads: the score kernel also counts the first
   // radix pass, and a cluster per head finishes the select from the keys.
+  // bf16 query and metadata at head_dim 64, block-id order, when every CTA fits at once: one launch
+  // (scores and a per-head radix select with in-kernel barriers).
+  {
+    CoopParams cp{};
+    const int g0 = hq / h;
+    if ((g0 == 1 || g0 == 2 || g0 == 4 || g0 == 8) && coop_plan(g0, q_dtype, meta_dtype, h, d, kmin, kmax, m_head, first_block, n_cand, order, cp)) {
+      cp.q = static_cast<const __nv_bfloat16*>(q);
+      cp.n_cand = n_cand;
+      cp.k = k;
+      cp.first_block = first_block;
+      cp.n_passes = bound_mode == LKV_BF16 ? 2 : 4;
+      cp.bound_mode = bound_mode;
+      cp.out_blocks = out_blocks;
+      cp.out_ld = out_ld;
+      cp.bitmap = bitmap;
+      cp.bitmap_words = bitmap_words;
+      cp.out_bound = out_bound;
+      cp.state = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(workspace) + kHistBytes);
+      return launch_coop(g0, cp, h, (n_cand + kCoopThreads - 1) / kCoopThreads, as_stream(stream));
+    }
+  }
   const bool cluster = order == LKV_ORDER_BLOCK && h <= kHistHeads && cluster_size_for(n_cand) > 0;
   if (!cluster && k > kMaxK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
   uint32_t* h0 = cluster ? hist0 : nullptr;
@@ -686,7 +1067,7 @@ int lkv_topk_merge(const float* bounds, const int32_t* ids, int h, int n, int64_
   if (workspace_bytes < lkv_topk_merge_workspace(h, n))
     return fail(LKV_ERR_WORKSPACE, "lkv_topk_merge: workspace %zu < %zu bytes", workspace_bytes, lkv_topk_merge_workspace(h, n));
   cudaStream_t st = as_stream(stream);
-  uint64_t* keys = reinterpret_cast<uint64_t*>(static_cast<unsigned char*>(workspace) + kHistBytes);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(static_cast<unsigned char*>(workspace) + kKeysOffset);
   merge_keys_kernel<<<dim3((n + 255) / 256, h), 256, 0, st>>>(bounds, ids, n, ld, keys);
   if (int rc = launched("lkv_topk_merge(keys)")) return rc;
   int P = 1;
@@ -715,7 +1096,7 @@ namespace {
 
 // 4 MiB of keys: h * n_cand <= 524,288 (e.g. 8 KV heads x 65,536 candidate blocks, a 1M-token
 // context in 16-token blocks). Every device that loads the library holds it until exit.
-constexpr size_t kNoAllocScratchBytes = kHistBytes + (4u << 20);
+constexpr size_t kNoAllocScratchBytes = kKeysOffset + (4u << 20);
 static __device__ __align__(256) uint64_t g_topk_scratch[kNoAllocScratchBytes / sizeof(uint64_t)];
 
 constexpr int kMaxDevices = 64;
@@ -751,7 +1132,7 @@ extern "C" int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h,
   const size_t need = lkv_quest_topk_workspace(h, n_cand);
   if (need > kNoAllocScratchBytes)
     return fail(LKV_ERR_ARG, "lkv_quest_topk_noalloc: %d heads x %d candidates need %zu bytes of scratch, above its fixed %zu (h * n_cand <= %zu)",
-                h, n_cand, need, kNoAllocScratchBytes, (kNoAllocScratchBytes - kHistBytes) / sizeof(uint64_t));
+                h, n_cand, need, kNoAllocScratchBytes, (kNoAllocScratchBytes - kKeysOffset) / sizeof(uint64_t));
   void* scratch = nullptr;
   if (int rc = scratch_address(&scratch)) return rc;
   // Nothing in the scratch has to start at zero: the score kernel writes every key the select

@@ -5,9 +5,10 @@
 
 namespace lkv {
 
-// Status word of the kernels that wait on mbarriers: 0, or the first LKV_DEV_* code a kernel
-// recorded. Internal linkage (the library is built without relocatable device code): attention.cu,
-// the one translation unit with such kernels, reads it for lkv_device_status with tu_device_status.
+// Status word of the kernels with bounded waits: 0, or the first LKV_DEV_* code a kernel recorded.
+// Internal linkage (the library is built without relocatable device code): each translation unit
+// that includes this header has its own and reads it with tu_device_status; lkv_device_status
+// combines those of attention.cu and select.cu.
 static __device__ int g_device_status = 0;
 constexpr int LKV_DEV_WAIT_TIMEOUT = 1;       // an mbarrier wait ran out of iterations
 constexpr int LKV_DEV_LIST_OVERFLOW = 2;      // a CTA's item list would not fit its shared memory (host sizing error)
