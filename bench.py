@@ -55,7 +55,22 @@ def parse() -> argparse.Namespace:
     p.add_argument("--no-host-leg", action="store_true", help="skip the zero-copy (host cold tier) measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=N_LAYERS - DENSE, help="selecting layers (the metric runs all 14; fewer for profiling)")
+    p.add_argument("--profile-calls", action="store_true",
+                   help="profiling target: build the layers, then call, twice each and eagerly on the first layer, the selection, the hot "
+                        "pass alone, the cold pass alone and the fused attention; print nothing else")
     return p.parse_args()
+
+
+def attention_traffic() -> int | None:
+    """DRAM bytes (read + write) of one attention launch at this workload, from the committed ncu
+    summary of that launch (null when the summary is absent)."""
+    import re
+
+    f = ROOT / "profiles" / "attn_stream_ctx128k.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*=\s*(\d+)", f.read_text())
+    return int(m.group(1)) if m else None
 
 
 def load_peaks() -> dict:
@@ -231,6 +246,35 @@ def layer_step(L, geo: dict, cold_store=None, events: list | None = None) -> Non
 
 
 LAUNCHES_PER_LAYER_STEP = 3  # score (+ first radix pass), cluster select, attention (both passes; the head's last CTA folds)
+
+
+def profile_calls(args: argparse.Namespace) -> None:
+    """The kernel calls of one layer-step, each twice and eagerly, for a profiler to capture."""
+    import torch
+
+    from lazykv_b200 import kernels as K
+    from lazykv_b200.build import build
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    build()
+    layers, geo = build_layers(args, 0, 1, dev)
+    L = layers[0]
+    strides = (HKV * 2 * BS * D, 2 * BS * D, D)
+    out = torch.empty((HQ, D), dtype=torch.float32, device=dev)
+    lse = torch.empty((HQ,), dtype=torch.float32, device=dev)
+    first = geo["cand_lo"] - geo["lo"]
+    for _ in range(2):
+        K.quest_topk(L.q, L.kmin, L.kmax, first, geo["n_cand"], geo["k_local"],
+                     out_blocks=L.list[:, geo["sel_off"] : geo["sel_off"] + geo["k_local"]], bitmap=L.bitmap, by_block=True)
+    for _ in range(2):
+        K.hot_attention(L.q, L.pool, L.pool[:, :, 1], strides, L.list, BS, geo["scale"], BS, slot_of=L.slot_of, out=out, lse=lse)
+    for _ in range(2):
+        K.cold_attention(L.q, L.records, BS, first, geo["n_cand"], geo["scale"], excluded=L.bitmap, out=out, lse=lse)
+    for _ in range(2):
+        K.exact_attention(L.q, L.pool, L.pool[:, :, 1], strides, L.list, BS, L.records, first, geo["n_cand"], geo["scale"], BS,
+                          excluded=L.bitmap, slot_of=L.slot_of, out=L.out, lse=L.lse)
+    torch.cuda.synchronize()
 
 
 def run_ours(args: argparse.Namespace) -> None:
@@ -413,7 +457,10 @@ def run_ours(args: argparse.Namespace) -> None:
                    "timing": "CUDA graph of one step (NCCL all-gathers captured at N > 1), CUDA events, max over ranks"},
         "kernel_us": {k: round(v, 3) for k, v in kernel_us.items()},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "peak_source": peaks["source"],
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": attention_traffic() if dominant == "attention" and args.ctx == 131072 and world == 1 else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one attention launch at this workload",
+                     "peak_source": peaks["source"],
                      "algorithmic_bytes": algo[dominant]},
         "layer_step_roofline": {"algorithmic_bytes": layer_bytes, "us": round(us_layer, 3),
                                 "achieved_gbs": round(layer_bytes / (us_layer * 1e-6) / 1e9, 1),
@@ -556,6 +603,8 @@ def main() -> None:
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.profile_calls:
+        profile_calls(args)
     else:
         run_ours(args)
 
