@@ -783,6 +783,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
                : "memory");
 }
 
+// tma_load_4d under an L2 cache policy.
+__device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar,
+                                                 uint64_t pol) {
+  asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(
+                   dst),
+               "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(pol)
+               : "memory");
+}
+
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -1155,6 +1164,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   // The warp's item holding the current block (the last listed block, `last_fill` live tokens), if any.
   const int fill_k = (p.seg[0].kind == SEG_LIST && lb0 == p.seg[0].n_list && hn > 0 && ha + hn == n_a) ? hn - 1 : -1;
   const int last_fill = p.seg[0].last_fill;
+  const uint64_t stream_pol = l2_evict_first_policy();  // every item is read once
   // Lane 0 fills stage s with the warp's k-th item (or arrives for a padding item).
   auto issue = [&](int k, int s) {
     if (lane != 0) return;
@@ -1168,13 +1178,13 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     if (set ? rec1 : rec0) {
       const Seg& S = p.seg[set];
       mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaRec);
-      tma_load_1d(dst, S.records + ((int64_t)row * p.h + j) * S.width, (uint32_t)kMmaRec, &bars[s]);
+      tma_load_1d_hint(dst, S.records + ((int64_t)row * p.h + j) * S.width, (uint32_t)kMmaRec, &bars[s], stream_pol);
     } else {
       mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaHotStage);
       const int hm = sp.head_major[set];
       const int c2 = hm ? j : row, c3 = hm ? row : j;
-      tma_load_4d(smem_u32(dst), &sp.tk[set], 0, 0, c2, c3, &bars[s]);
-      tma_load_4d(smem_u32(dst + kMmaTile), &sp.tv[set], 0, 0, c2, c3, &bars[s]);
+      tma_load_4d_hint(smem_u32(dst), &sp.tk[set], 0, 0, c2, c3, &bars[s], stream_pol);
+      tma_load_4d_hint(smem_u32(dst + kMmaTile), &sp.tv[set], 0, 0, c2, c3, &bars[s], stream_pol);
     }
   };
   int n_issued = 0;

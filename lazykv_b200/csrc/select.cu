@@ -610,9 +610,11 @@ struct CoopParams {
   uint32_t* state;  // [h][kCoopHeadWords], zero on entry, left zero
 };
 
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
-  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-               "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+// One 3-D tile load global -> this CTA's shared memory under an L2 cache policy. No multicast.
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar, uint64_t pol) {
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
                : "memory");
 }
 
@@ -729,10 +731,11 @@ __global__ void __launch_bounds__(kCoopThreads) quest_select_coop_kernel(const _
   if (tid == 0) {
     const int r0 = cp.first_block + lo;
     mbar_arrive_expect_tx(&bar, 4u * kCoopBox);
-    tma_load_3d(tiles, &cp.tmax, 0, r0, j, &bar);
-    tma_load_3d(tiles + kCoopBox, &cp.tmax, 0, r0 + kCoopBoxRows, j, &bar);
-    tma_load_3d(tiles + 2 * kCoopBox, &cp.tmin, 0, r0, j, &bar);
-    tma_load_3d(tiles + 3 * kCoopBox, &cp.tmin, 0, r0 + kCoopBoxRows, j, &bar);
+    const uint64_t pol = l2_evict_first_policy();  // the bounds are read once per call
+    tma_load_3d_hint(tiles, &cp.tmax, 0, r0, j, &bar, pol);
+    tma_load_3d_hint(tiles + kCoopBox, &cp.tmax, 0, r0 + kCoopBoxRows, j, &bar, pol);
+    tma_load_3d_hint(tiles + 2 * kCoopBox, &cp.tmin, 0, r0, j, &bar, pol);
+    tma_load_3d_hint(tiles + 3 * kCoopBox, &cp.tmin, 0, r0 + kCoopBoxRows, j, &bar, pol);
   }
   bool ok = __syncthreads_and(mbar_wait(&bar, 0)) != 0;
 

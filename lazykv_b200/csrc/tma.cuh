@@ -51,6 +51,23 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
                : "memory");
 }
 
+// An L2 policy under which the lines a load brings in are the first to be evicted. The streamed
+// blocks, records and block bounds are read once per call; under this policy they do not push the
+// reused lines out of L2 (lists, bitmaps, partials, counters and the kernels' own instructions).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// tma_load_1d under an L2 cache policy.
+__device__ __forceinline__ void tma_load_1d_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+               : "memory");
+}
+
 // Waits for the phase of `bar` with the given parity. Each try may suspend the thread (up to the
 // hint) until the phase completes, so a waiting warp does not spin on issue slots. Gives up after
 // kMaxWaitIters tries (about two seconds at most), records LKV_DEV_WAIT_TIMEOUT in g_device_status
