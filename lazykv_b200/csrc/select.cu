@@ -722,13 +722,8 @@ __global__ void __launch_bounds__(kCoopThreads) quest_select_coop_kernel(const _
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
-  pdl_wait();  // no-op: this kernel is launched without the programmatic attribute
-  stage_query<__nv_bfloat16, G>(cp.q, j, 64, qs);
-  hist[tid] = 0u;
-  if (c == 0 && cp.bitmap != nullptr)
-    for (int w = tid; w < cp.bitmap_words; w += blockDim.x) cp.bitmap[(int64_t)j * cp.bitmap_words + w] = 0u;
-  __syncthreads();
-  if (tid == 0) {
+  pdl_wait();  // no-op: this kernel is launched without the programmatic attribute (measured slower with it)
+  if (tid == 0) {  // the bounds first: the query is staged while they are in flight
     const int r0 = cp.first_block + lo;
     mbar_arrive_expect_tx(&bar, 4u * kCoopBox);
     const uint64_t pol = l2_evict_first_policy();  // the bounds are read once per call
@@ -737,7 +732,21 @@ __global__ void __launch_bounds__(kCoopThreads) quest_select_coop_kernel(const _
     tma_load_3d_hint(tiles + 2 * kCoopBox, &cp.tmin, 0, r0, j, &bar, pol);
     tma_load_3d_hint(tiles + 3 * kCoopBox, &cp.tmin, 0, r0 + kCoopBoxRows, j, &bar, pol);
   }
-  bool ok = __syncthreads_and(mbar_wait(&bar, 0)) != 0;
+  stage_query<__nv_bfloat16, G>(cp.q, j, 64, qs);
+  hist[tid] = 0u;
+  // CTA 0 writes the head's bitmap: zero, or, when every candidate is taken (no barrier follows to
+  // order its stores before the other CTAs' bits), the candidates' bits.
+  const bool all_taken = cp.k >= n_cand;
+  if (c == 0 && cp.bitmap != nullptr)
+    for (int w = tid; w < cp.bitmap_words; w += blockDim.x) {
+      uint32_t v = 0u;
+      if (all_taken) {
+        const int64_t b0 = max((int64_t)cp.first_block, (int64_t)w * 32), b1 = min((int64_t)cp.first_block + n_cand, (int64_t)w * 32 + 32);
+        if (b0 < b1) v = (b1 - b0 == 32 ? 0xffffffffu : ((1u << (b1 - b0)) - 1u)) << (b0 - (int64_t)w * 32);
+      }
+      cp.bitmap[(int64_t)j * cp.bitmap_words + w] = v;
+    }
+  bool ok = __syncthreads_and(mbar_wait(&bar, 0)) != 0;  // also the barrier of the staged query
 
   // ---- this thread's key ----
   const bool have = tid < cnt;
@@ -838,7 +847,7 @@ __global__ void __launch_bounds__(kCoopThreads) quest_select_coop_kernel(const _
   if (take && pos < (uint32_t)kk && ok) {
     const int blk = cp.first_block + lo + tid;
     cp.out_blocks[(int64_t)j * cp.out_ld + pos] = blk;
-    if (cp.bitmap != nullptr && blk / 32 < cp.bitmap_words) atomicOr(&cp.bitmap[(int64_t)j * cp.bitmap_words + blk / 32], 1u << (blk % 32));
+    if (cp.bitmap != nullptr && !all_taken && blk / 32 < cp.bitmap_words) atomicOr(&cp.bitmap[(int64_t)j * cp.bitmap_words + blk / 32], 1u << (blk % 32));
   }
 
   // ---- the head's last CTA to leave zeroes its state ----
