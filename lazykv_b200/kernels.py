@@ -38,14 +38,23 @@ def packed_pair_bytes(block_size: int, head_dim: int) -> int:
 
 
 def block_minmax(keys: torch.Tensor, block_size: int, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int = 0) -> None:
-    """kmin/kmax[j, first_block + b] = channel min/max of block b of `keys` [h, n*bs, d] (any strides)."""
+    """kmin/kmax[j, first_block + b] = channel min/max of block b of `keys`: [h, n*bs, d] or
+    [h, n, bs, d] (any strides; the 4-D form reads blocks that are not evenly spaced tokens, such as
+    the keys of a store in its [n, h, 2, bs, d] layout)."""
     require_cuda(keys, kmin, kmax)
-    h, t, d = keys.shape
-    n = t // block_size
+    if keys.dim() == 4:
+        h, n, bs, d = keys.shape
+        if bs != block_size:
+            raise ValueError(f"block_minmax: blocks of {bs} tokens, block_size {block_size}")
+        s_head, s_blk, s_tok = keys.stride(0), keys.stride(1), keys.stride(2)
+    else:
+        h, t, d = keys.shape
+        n = t // block_size
+        s_head, s_tok = keys.stride(0), keys.stride(1)
+        s_blk = block_size * s_tok
     if kmin.shape[-1] != d or kmin.dtype != keys.dtype or kmax.dtype != keys.dtype or kmin.stride(-1) != 1 or keys.stride(-1) != 1:
         raise ValueError("block_minmax: metadata must be [h, cap, d] in the keys' dtype, contiguous in d")
-    s_head, s_tok = keys.stride(0), keys.stride(1)
-    call("lkv_block_minmax", ptr(keys), dtype_code(keys.dtype), h, n, block_size, d, s_head, block_size * s_tok, s_tok,
+    call("lkv_block_minmax", ptr(keys), dtype_code(keys.dtype), h, n, block_size, d, s_head, s_blk, s_tok,
          ptr(kmin), ptr(kmax), kmin.stride(-3) if kmin.dim() >= 3 else kmin.shape[-2] * d, first_block, stream_handle(keys.device))
 
 

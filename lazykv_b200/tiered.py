@@ -109,6 +109,50 @@ class TieredLayer:
         self.boundary_d2h_bytes = n_blocks * h * self.pair_bytes
         self._finish(n_blocks, tail, seed)
 
+    @classmethod
+    def from_store(cls, host: torch.Tensor, n_blocks: int, tail: torch.Tensor, k_blocks: int, block_size: int, capacity_tokens: int,
+                   device: torch.device, n_slots: int | None = None, quant: str | None = None, sink: torch.Tensor | None = None,
+                   cold_placement: str = "host") -> TieredLayer:
+        """A layer whose pinned host store already holds its `n_blocks` sealed blocks (a restored
+        snapshot); the classmethod of lazykv/tiered.py:209-241, extended to the int8 store.
+
+        The result is the layer the constructor builds from the same KV: the metadata and the seeded
+        slots are derived on the device from the store's bytes (the bf16 pairs, or the int8 records
+        dequantised as a fetch does, whose min/max are the metadata the constructor writes), and the
+        residency tables are seeded the same way. `tail` is the unsealed block [h, 2, fill, d]. An
+        int8 store also needs `sink`, the exact first block [h, 2, bs, d]: its record is lossy and the
+        sink stays exact in VRAM. Nothing here waits for the device.
+        """
+        if (quant == "int8") != (host.dtype == torch.uint8):
+            raise ValueError(f"a {host.dtype} store does not hold a quant={quant!r} tier")
+        if quant == "int8" and sink is None:
+            raise ValueError("an int8 store needs the exact sink block: its record is lossy")
+        self = cls.__new__(cls)
+        h, bs, fill = host.shape[1], block_size, tail.shape[2]
+        d, dt = tail.shape[3], tail.dtype
+        self._allocate(h, d, n_blocks, k_blocks, bs, capacity_tokens, device, dt, host, n_slots, quant, cold_placement)
+        seed = min(self.n_slots, n_blocks - 1)
+        lo_seed = n_blocks - seed
+        for c0 in range(0, n_blocks, BOUNDARY_CHUNK):
+            c1 = min(n_blocks, c0 + BOUNDARY_CHUNK)
+            g = host[c0:c1].to(device, non_blocking=True)  # [n, h, 2, bs, d] pairs or [n, h, W] records
+            if self.dev_store is not None:
+                self.dev_store[c0:c1].copy_(g)
+            pairs = g if quant is None else K.unpack_int8(g.flatten(0, 1), bs, d, dt).view(c1 - c0, h, 2, bs, d)
+            K.block_minmax(pairs[:, :, 0].transpose(0, 1), bs, self.kmin[0], self.kmax[0], first_block=c0)
+            lo = max(c0, lo_seed)
+            if lo < c1 and seed > 0:
+                self.pool[1 + lo - lo_seed : 1 + c1 - lo_seed] = pairs[lo - c0 :]
+            if c0 == 0 and quant is None:
+                self.pool[0] = pairs[0]
+        if quant is not None:
+            self.pool[0] = sink.to(device, non_blocking=True)
+        if fill:
+            self.pool[self.tail_slot, :, :, :fill] = tail.to(device, non_blocking=True)
+        self.boundary_d2h_s, self.boundary_d2h_bytes = 0.0, 0  # nothing crossed device to host
+        self._finish(n_blocks, fill, seed)
+        return self
+
     # -- set-up ----------------------------------------------------------------------------------
 
     def _allocate(self, h: int, d: int, n_blocks: int, k_blocks: int, bs: int, capacity_tokens: int, dev: torch.device, dt: torch.dtype,
