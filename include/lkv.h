@@ -220,6 +220,61 @@ int lkv_exact_attention(const void* q, int hq, int h, int d, int bs, const lkv_h
                         size_t workspace_bytes, void* stream);
 
 /*
+ * Ragged rows: many sequences of different lengths in one decode step (continuous batching). The
+ * reference is batch-1 only; per sequence these calls compute what lkv_quest_topk and
+ * lkv_exact_attention compute for one (lazykv/selection.py:38-62 top_blocks over the Quest bound,
+ * lazykv/exact.py:225-264 with the int8 cold tier), over all sequences in one launch each.
+ * Row r = seq * heads + head. A sequence's blocks live anywhere in a paged store: its block table
+ * table[seq * table_stride + b] gives the store row of its logical block b. Candidates of row r are
+ * logical blocks 1 .. n_cand(r).
+ *
+ * lkv_ragged_quest_topk: q [rows * g, d]; kmin / kmax [heads][store rows][d] (row stride m_head per
+ * head) in q's dtype; row_sel [rows][2] = (n_cand, k), n_cand <= max_cand <= 16384; work
+ * [n_work][2] = (row, first candidate) chunks of 256 candidates covering every row's candidates
+ * (a row with n candidates has ceil(n / 256) chunks at 0, 256, ...). out_blocks [rows][out_stride]
+ * receives each row's k kept logical blocks in ascending order (the top k by bound, ties to the
+ * lowest ids) and bitmap [rows][bitmap_words] (optional) their bits. Workspace:
+ * lkv_ragged_topk_workspace(rows, max_cand) bytes.
+ */
+size_t lkv_ragged_topk_workspace(int rows, int max_cand);
+int lkv_ragged_quest_topk(const void* q, int q_dtype, int rows, int g, int d, int heads,
+                          const void* kmin, const void* kmax, int meta_dtype, int64_t m_head,
+                          int64_t n_store, const int32_t* table, int64_t table_stride,
+                          const int32_t* row_sel, int max_cand, const int32_t* work, int n_work,
+                          int bound_mode, int32_t* out_blocks, int64_t out_stride,
+                          uint32_t* bitmap, int bitmap_words, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/*
+ * lkv_ragged_schedule (host memory, no device work): the CTAs of one ragged attention launch.
+ * row_items [rows] = a row's hot items plus an upper bound of its cold items; writes sched
+ * [n][4] = (row, index in the row, the row's CTAs, the row's first partial) and *n_parts, and
+ * returns n (the CTA count; at most max_ctas) or a negative status.
+ */
+int lkv_ragged_schedule(const int32_t* row_items, int rows, int n_sms, int32_t* sched, int max_ctas,
+                        int* n_parts);
+size_t lkv_ragged_attention_workspace(int g, int n_parts);
+
+/*
+ * lkv_ragged_exact_attention: every row's hot set and int8 cold set with their merge, in one
+ * launch of the tensor-core stream kernel (bf16, d 64, bs 16, g in {1, 2, 4, 8}, device-resident
+ * stores). hot: the pool of bf16 pairs as in lkv_exact_attention, `blocks` [rows][n_list] holding
+ * pool rows directly (slot_of NULL; n_list is the row stride), each row's count in row_info.
+ * records [n_records, heads, W] int8 records read through the block tables; excluded [rows]
+ * [bitmap_words] the blocks of each row's hot set. row_info [rows][4] = (hot items, fill of the
+ * current block, n_cand, 0): the hot list's last item is the current block, masked past its fill.
+ * sched (device copy of lkv_ragged_schedule's output, n_ctas entries, n_parts partials). out
+ * [rows * g, d] in out_dtype and lse [rows * g] (optional). Workspace:
+ * lkv_ragged_attention_workspace(g, n_parts) bytes, zero-filled once (counters kept at zero).
+ */
+int lkv_ragged_exact_attention(const void* q, int rows, int g, int d, int bs, int heads,
+                               const lkv_hot_set* hot, const uint8_t* records, int64_t n_records,
+                               const int32_t* table, int64_t table_stride, const uint32_t* excluded,
+                               int bitmap_words, const int32_t* row_info, const int32_t* sched,
+                               int n_ctas, int n_parts, float scale, void* out, int out_dtype,
+                               float* lse, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Residency admit on the device, fused with the fetch of the misses. Replaces the host side of
  * lazykv/tiered.py:383-487 (rank's device-to-host copy, the numpy LRU of admit, the staged H2D and
  * index_copy_, and the gather's last_used update), with the same LRU rule: for KV head j, chosen

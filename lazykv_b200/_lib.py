@@ -44,6 +44,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_exact_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "lkv_exact_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_device_status": (c_int, [c_void_p, c_int]),
+    "lkv_ragged_topk_workspace": (c_size_t, [c_int, c_int]),
+    "lkv_ragged_quest_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int64,
+                                      c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "lkv_ragged_schedule": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
+    "lkv_ragged_attention_workspace": (c_size_t, [c_int, c_int]),
+    "lkv_ragged_exact_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int,
+                                           c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_tier_admit": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int,
                                c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
 }

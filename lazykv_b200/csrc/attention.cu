@@ -777,13 +777,7 @@ struct MmaParams {
   int head_major[2];         // map coordinate order: (0, 0, head, row) instead of (0, 0, row, head)
 };
 
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar) {
-  asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
-               "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
-               : "memory");
-}
-
-// tma_load_4d under an L2 cache policy.
+// One 4-D tile load global -> this CTA's shared memory under an L2 cache policy. No multicast.
 __device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* bar,
                                                  uint64_t pol) {
   asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(
@@ -913,11 +907,18 @@ struct StreamParams {
   float* lse;                // [hq] (optional)
   float* seg_out;            // [2, hq, D] (optional)
   float* seg_lse;            // [2, hq] (optional)
+  // Ragged rows (batched sequences, one row per (sequence, KV head) = seq * heads + head); all null
+  // for a single sequence, where row = KV head = blockIdx.y, CTA = blockIdx.x and P = per_head.
+  const int4* sched;         // per CTA: (row, index in the row, the row's CTAs, the row's first partial)
+  const int4* row_info;      // per row: (items of the list segment, last_fill, blocks of the range, 0)
+  const int32_t* table;      // range blocks through block tables: record row = table[seq * table_stride + block]
+  int64_t table_stride;
+  int heads;                 // KV heads of a sequence (the pool's and the records' head index is row % heads)
 };
 
-// In-range blocks of bitmap word w that the exclusion bitmap of head j leaves.
-__device__ __forceinline__ uint32_t range_word_bits(const Seg& S, int j, int w) {
-  const int f = S.first_block, e = S.first_block + S.n_items;  // blocks [f, e)
+// In-range blocks of bitmap word w that the exclusion bitmap of row j leaves (n_items: the row's blocks).
+__device__ __forceinline__ uint32_t range_word_bits(const Seg& S, int n_items, int j, int w) {
+  const int f = S.first_block, e = S.first_block + n_items;  // blocks [f, e)
   const int lo = max(f, 32 * w) - 32 * w, hi = min(e, 32 * w + 32) - 32 * w;
   if (hi <= lo) return 0u;
   const uint32_t in = (hi - lo == 32 ? 0xffffffffu : ((1u << (hi - lo)) - 1u)) << lo;
@@ -987,11 +988,24 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   uint64_t* bars_all = reinterpret_cast<uint64_t*>(smem + C::RING + C::PARK + C::LIST);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int j = blockIdx.y, ci = blockIdx.x, P = sp.per_head;
+  // The CTA's row: j (query group, lists, bitmap, outputs, counter), its KV head hj in the pool and
+  // the records, the CTA's index ci among the row's P, the row's first partial pbase, the fill of its
+  // current block. Kept in shared memory and read where used, so that none stays in a register
+  // across the streaming loop.
+  __shared__ int sh_rp[6];  // j, ci, P, pbase, hj, last_fill
+  auto rp = [&](int i) { return *reinterpret_cast<volatile int*>(&sh_rp[i]); };
   uint64_t* bars = bars_all + warp * NS;
   if (threadIdx.x == 0) {
     sh_bad = 0;
     mbar_init(&fold_bar, 1);
+    if (sp.sched != nullptr) {
+      const int4 e = sp.sched[blockIdx.x];
+      sh_rp[0] = e.x, sh_rp[1] = e.y, sh_rp[2] = e.z, sh_rp[3] = e.w, sh_rp[4] = e.x % sp.heads;
+      sh_rp[5] = sp.row_info != nullptr ? sp.row_info[e.x].y : p.seg[0].last_fill;
+    } else {
+      sh_rp[0] = blockIdx.y, sh_rp[1] = blockIdx.x, sh_rp[2] = sp.per_head, sh_rp[3] = blockIdx.y * sp.per_head, sh_rp[4] = blockIdx.y;
+      sh_rp[5] = p.seg[0].last_fill;
+    }
   }
   if (lane == 0) {
 #pragma unroll
@@ -1001,6 +1015,8 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
 
   pdl_wait();  // the lists, the bitmap and the workspace are the predecessor's to finish with
   pdl_release();
+  __syncthreads();  // sh_rp
+  const int j = rp(0);
   // ---- set-up: counts, this CTA's item range, its list of storage rows ----
   // A list segment's count is its length; a range's is a popcount over the bitmap. In the common
   // case (segment 0 a list, segment 1 a range of at most kSetupWords words per thread) the list's
@@ -1008,14 +1024,22 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   constexpr int kSetupWords = 1;
   const Seg& S0 = p.seg[0];
   const Seg& S1 = p.seg[1];
+  // The row's item counts (list length, range blocks) and the fill of its current block.
+  int n_seg[2] = {S0.n_items, p.n_segs > 1 ? S1.n_items : 0};
+  if (sp.row_info != nullptr) {
+    const int4 ri = sp.row_info[j];
+    n_seg[0] = ri.x, n_seg[1] = ri.z;
+  }
+  // A range block's record row: the block itself, or its entry in the sequence's block table.
+  const int32_t* table = sp.table != nullptr ? sp.table + (int64_t)(j / sp.heads) * sp.table_stride : nullptr;
   const bool fast = p.n_segs == 2 && S0.kind == SEG_LIST && S1.kind != SEG_LIST &&
-                    (S1.n_items <= 0 || (S1.first_block + S1.n_items - 1) / 32 - S1.first_block / 32 < kSetupWords * kStreamThreads);
+                    (n_seg[1] <= 0 || (S1.first_block + n_seg[1] - 1) / 32 - S1.first_block / 32 < kSetupWords * kStreamThreads);
   int64_t cnt0 = 0, cnt1 = 0, la0 = 0, lb0 = 0, la1 = 0, lb1 = 0;
   int n_a = 0, n_b = 0;
   if (fast) {
-    cnt0 = S0.n_items;
-    la0 = cnt0 * ci / P;
-    lb0 = cnt0 * (ci + 1) / P;
+    cnt0 = n_seg[0];
+    la0 = cnt0 * rp(1) / rp(2);
+    lb0 = cnt0 * (rp(1) + 1) / rp(2);
     n_a = (int)(lb0 - la0);
     // The list's first kStreamThreads items: id, then slot row (dependent loads, in flight during the scan).
     int hot_row = -1;
@@ -1031,13 +1055,13 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     const int w0 = S1.first_block / 32 + threadIdx.x * kSetupWords;
 #pragma unroll
     for (int k = 0; k < kSetupWords; ++k) {
-      bits[k] = S1.n_items > 0 ? range_word_bits(S1, j, w0 + k) : 0u;
+      bits[k] = n_seg[1] > 0 ? range_word_bits(S1, n_seg[1], j, w0 + k) : 0u;
       mine += __popc(bits[k]);
     }
     const int before = block_excl_scan(mine, warp_sums, &sh_total);
     cnt1 = sh_total;
-    la1 = cnt1 * ci / P;
-    lb1 = cnt1 * (ci + 1) / P;
+    la1 = cnt1 * rp(1) / rp(2);
+    lb1 = cnt1 * (rp(1) + 1) / rp(2);
     n_b = (int)(lb1 - la1);
     if (n_a + n_b <= kStreamListCap) {
       int64_t ord = before;
@@ -1053,7 +1077,12 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
           b &= b - 1u;
           if (ord >= la1 && ord < lb1) {
             const int blk = 32 * (w0 + k) + bit;
-            list[n_a + (ord - la1)] = S1.kind == SEG_RANGE_REC ? blk : (blk < S1.n_rows ? blk : -1);
+            int rrow = blk;
+            if (table != nullptr) {  // a table entry outside the store lists nothing
+              rrow = __ldg(table + blk);
+              if (rrow < 0 || rrow >= S1.n_rows) rrow = -1;
+            }
+            list[n_a + (ord - la1)] = S1.kind == SEG_RANGE_REC ? rrow : (rrow < S1.n_rows ? rrow : -1);
           }
           ++ord;
         }
@@ -1068,21 +1097,21 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   } else {
     for (int s = 0; s < p.n_segs; ++s) {
       const Seg& S = p.seg[s];
-      int64_t c = S.n_items;
-      if (S.kind != SEG_LIST && S.n_items > 0) {
-        const int w0 = S.first_block / 32, w1 = (S.first_block + S.n_items - 1) / 32;
+      int64_t c = n_seg[s];
+      if (S.kind != SEG_LIST && n_seg[s] > 0) {
+        const int w0 = S.first_block / 32, w1 = (S.first_block + n_seg[s] - 1) / 32;
         int mine = 0;
-        for (int w = w0 + threadIdx.x; w <= w1; w += blockDim.x) mine += __popc(range_word_bits(S, j, w));
+        for (int w = w0 + threadIdx.x; w <= w1; w += blockDim.x) mine += __popc(range_word_bits(S, n_seg[s], j, w));
         block_excl_scan(mine, warp_sums, &sh_total);
         c = sh_total;
       }
       if (s == 0) cnt0 = c; else cnt1 = c;
     }
     // This CTA's share of each segment (ordinals [la, lb)); the list holds segment 0's items first.
-    la0 = cnt0 * ci / P;
-    lb0 = cnt0 * (ci + 1) / P;
-    la1 = cnt1 * ci / P;
-    lb1 = cnt1 * (ci + 1) / P;
+    la0 = cnt0 * rp(1) / rp(2);
+    lb0 = cnt0 * (rp(1) + 1) / rp(2);
+    la1 = cnt1 * rp(1) / rp(2);
+    lb1 = cnt1 * (rp(1) + 1) / rp(2);
     n_a = (int)(lb0 - la0);
     n_b = (int)(lb1 - la1);
     if (n_a + n_b <= kStreamListCap) {
@@ -1100,17 +1129,24 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
           }
         } else {
           // Ordinal of each word's first kept block by a block-wide scan, chunk by chunk.
-          const int w0 = S.first_block / 32, w1 = (S.first_block + S.n_items - 1) / 32;
+          const int w0 = S.first_block / 32, w1 = (S.first_block + n_seg[s] - 1) / 32;
           int64_t run = 0;
           for (int c0 = w0; c0 <= w1 && run < lb; c0 += blockDim.x) {
             const int w = c0 + threadIdx.x;
-            uint32_t bits = w <= w1 ? range_word_bits(S, j, w) : 0u;
+            uint32_t bits = w <= w1 ? range_word_bits(S, n_seg[s], j, w) : 0u;
             const int before = block_excl_scan(__popc(bits), warp_sums, &sh_total);
             int64_t ord = run + before;
             while (bits != 0u && ord < lb) {
               const int b = __ffs(bits) - 1;
               bits &= bits - 1u;
-              if (ord >= la) dst[ord - la] = S.kind == SEG_RANGE_REC ? 32 * w + b : (32 * w + b < S.n_rows ? 32 * w + b : -1);
+              if (ord >= la) {
+                int rrow = 32 * w + b;
+                if (table != nullptr) {
+                  rrow = __ldg(table + rrow);
+                  if (rrow < 0 || rrow >= S.n_rows) rrow = -1;
+                }
+                dst[ord - la] = S.kind == SEG_RANGE_REC ? rrow : (rrow < S.n_rows ? rrow : -1);
+              }
               ++ord;
             }
             run += sh_total;
@@ -1162,8 +1198,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   // Per set: whether its items are int8 records (else bf16 tile pairs through the tensor maps).
   const bool rec0 = p.seg[0].kind == SEG_RANGE_REC, rec1 = p.n_segs > 1 && p.seg[1].kind == SEG_RANGE_REC;
   // The warp's item holding the current block (the last listed block, `last_fill` live tokens), if any.
-  const int fill_k = (p.seg[0].kind == SEG_LIST && lb0 == p.seg[0].n_list && hn > 0 && ha + hn == n_a) ? hn - 1 : -1;
-  const int last_fill = p.seg[0].last_fill;
+  const int fill_k = (p.seg[0].kind == SEG_LIST && lb0 == n_seg[0] && hn > 0 && ha + hn == n_a) ? hn - 1 : -1;
   const uint64_t stream_pol = l2_evict_first_policy();  // every item is read once
   // Lane 0 fills stage s with the warp's k-th item (or arrives for a padding item).
   auto issue = [&](int k, int s) {
@@ -1178,11 +1213,12 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     if (set ? rec1 : rec0) {
       const Seg& S = p.seg[set];
       mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaRec);
-      tma_load_1d_hint(dst, S.records + ((int64_t)row * p.h + j) * S.width, (uint32_t)kMmaRec, &bars[s], stream_pol);
+      tma_load_1d_hint(dst, S.records + ((int64_t)row * p.h + rp(4)) * S.width, (uint32_t)kMmaRec, &bars[s], stream_pol);
     } else {
       mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaHotStage);
       const int hm = sp.head_major[set];
-      const int c2 = hm ? j : row, c3 = hm ? row : j;
+      const int hj = rp(4);
+      const int c2 = hm ? hj : row, c3 = hm ? row : hj;
       tma_load_4d_hint(smem_u32(dst), &sp.tk[set], 0, 0, c2, c3, &bars[s], stream_pol);
       tma_load_4d_hint(smem_u32(dst + kMmaTile), &sp.tv[set], 0, 0, c2, c3, &bars[s], stream_pol);
     }
@@ -1307,6 +1343,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     // Raw scores: a0, a1 (token g, rows 2t, 2t+1), a2, a3 (token g + 8).
     float a0 = sa[0] + sb[0], a1 = sa[1] + sb[1], a2 = sa[2] + sb[2], a3 = sa[3] + sb[3];
     if (!REC && masked) {
+      const int last_fill = rp(5);
       if (g >= last_fill) a0 = a1 = -INFINITY;
       if (g + 8 >= last_fill) a2 = a3 = -INFINITY;
     }
@@ -1449,7 +1486,8 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   // the sum L by shuffles, and lane w's weight 2^(m_w - M) goes to shared memory; then every thread
   // folds one output element with those weights.
   const int64_t part_stride = C::PART;
-  float* mine = sp.part + (((int64_t)j * P + ci) * 2) * part_stride;
+  const int ci = rp(1), P = rp(2), pbase = rp(3);
+  float* mine = sp.part + (((int64_t)pbase + ci) * 2) * part_stride;
   __shared__ float fold_w[2 * 8][NW > 32 ? NW : 32];  // [(set, row)][warp or partial] weights
   static_assert(NW <= 32, "one lane per warp");
   for (int pr = warp; pr < 2 * G; pr += NW) {
@@ -1490,7 +1528,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   // The head's partials are contiguous in the workspace: one bulk copy brings them into the idle
   // ring (when they fit); per (set, row) a warp finds the maximum, the weights and the sum by
   // shuffles (lanes over the partials); then every thread folds one output element.
-  const float* hp = sp.part + (int64_t)j * P * 2 * part_stride;
+  const float* hp = sp.part + (int64_t)pbase * 2 * part_stride;
   const int nset = p.n_segs;
   const size_t head_bytes = (size_t)P * 2 * C::PART * sizeof(float);
   const bool bulk = head_bytes <= (size_t)C::RING;
@@ -1964,7 +2002,8 @@ int launch_stream(const StreamParams& sp, cudaStream_t st) {
     if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
     attr_set |= bit;
   }
-  cudaError_t e = launch_pdl(k, dim3(sp.per_head, sp.p.h), dim3(kStreamThreads), C::SMEM, st, 0, sp);
+  const dim3 grid = sp.sched != nullptr ? dim3(sp.per_head) : dim3(sp.per_head, sp.p.h);  // ragged: per_head holds the CTAs
+  cudaError_t e = launch_pdl(k, grid, dim3(kStreamThreads), C::SMEM, st, 0, sp);
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv attention: %s", cudaGetErrorString(e));
   return launched("lkv attention");
 }
@@ -2020,12 +2059,116 @@ int run_attention(const char* who, AttnParams& p, int g, int d, TO* out, float* 
   return dispatch<T, TO>(g, d, p, out, lse, seg_out, seg_lse, st);
 }
 
+// Ragged rows: one launch of the stream kernel over a host-built schedule (see lkv_ragged_schedule).
+template <typename TO>
+int run_attention_ragged(const char* who, AttnParams& p, int g, int d, const int4* sched, int n_ctas, int n_parts, const int4* row_info,
+                         const int32_t* table, int64_t table_stride, int heads, TO* out, float* lse, void* workspace, size_t workspace_bytes,
+                         cudaStream_t st) {
+  const int rows = p.hq / g;
+  if (rows > kStreamCounterBytes / 4) return fail(LKV_ERR_ARG, "%s: %d rows > %d", who, rows, kStreamCounterBytes / 4);
+  const size_t need = (size_t)kStreamCounterBytes + (size_t)n_parts * 2 * ((g * 64 + 2 * g + 3) / 4 * 4) * sizeof(float);
+  if (workspace_bytes < need) return fail(LKV_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, need);
+  if (!aligned(workspace, 16)) return fail(LKV_ERR_PTR, "%s: workspace must be 16-byte aligned", who);
+  p.part = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kStreamCounterBytes);
+  MmaParams mp{};
+  if (!mma_plan(p, g, d, true, mp))
+    return fail(LKV_ERR_ARG, "%s: ragged rows need bf16, head_dim 64, block size 16, a group of 1, 2, 4 or 8, a positive scale and device-resident stores", who);
+  StreamParams sp{};
+  sp.p = p;
+  for (int i = 0; i < 2; ++i) {
+    sp.tk[i] = mp.tk[i];
+    sp.tv[i] = mp.tv[i];
+    sp.head_major[i] = mp.head_major[i];
+  }
+  sp.per_head = n_ctas;
+  sp.counters = static_cast<unsigned int*>(workspace);
+  sp.part = p.part;
+  sp.out = out;
+  sp.lse = lse;
+  sp.sched = sched;
+  sp.row_info = row_info;
+  sp.table = table;
+  sp.table_stride = table_stride;
+  sp.heads = heads;
+  switch (g) {
+    case 1: return launch_stream<1, TO>(sp, st);
+    case 2: return launch_stream<2, TO>(sp, st);
+    case 4: return launch_stream<4, TO>(sp, st);
+    default: return launch_stream<8, TO>(sp, st);
+  }
+}
+
 }  // namespace
 }  // namespace lkv
 
 using namespace lkv;
 
 extern "C" {
+
+int lkv_ragged_schedule(const int32_t* row_items, int rows, int n_sms, int32_t* sched, int max_ctas, int* n_parts) {
+  if (row_items == nullptr || sched == nullptr || n_parts == nullptr || rows <= 0 || n_sms <= 0)
+    return fail(LKV_ERR_ARG, "lkv_ragged_schedule: bad arguments");
+  int64_t total = 0;
+  for (int r = 0; r < rows; ++r) {
+    if (row_items[r] < 0) return fail(LKV_ERR_ARG, "lkv_ragged_schedule: row %d has %d items", r, row_items[r]);
+    total += row_items[r];
+  }
+  // Items per CTA: about four waves of one CTA per SM, at least 64 items and at most what a CTA's
+  // list holds (two segments, each rounded up).
+  int64_t chunk = (total + 4LL * n_sms - 1) / (4LL * n_sms);
+  if (chunk < 64) chunk = 64;
+  if (chunk > kStreamListCap - 2) chunk = kStreamListCap - 2;
+  int n = 0, parts = 0;
+  for (int r = 0; r < rows; ++r) {
+    const int P = (int)((row_items[r] + chunk - 1) / chunk) > 0 ? (int)((row_items[r] + chunk - 1) / chunk) : 1;
+    if (n + P > max_ctas) return fail(LKV_ERR_WORKSPACE, "lkv_ragged_schedule: more than %d CTAs", max_ctas);
+    for (int c = 0; c < P; ++c, ++n) {
+      sched[4 * n + 0] = r;
+      sched[4 * n + 1] = c;
+      sched[4 * n + 2] = P;
+      sched[4 * n + 3] = parts;
+    }
+    parts += P;
+  }
+  *n_parts = parts;
+  return n;
+}
+
+size_t lkv_ragged_attention_workspace(int g, int n_parts) {
+  if (g <= 0 || n_parts < 0) return 0;
+  return (size_t)kStreamCounterBytes + (size_t)n_parts * 2 * ((g * 64 + 2 * g + 3) / 4 * 4) * sizeof(float);
+}
+
+int lkv_ragged_exact_attention(const void* q, int rows, int g, int d, int bs, int heads, const lkv_hot_set* hot, const uint8_t* records,
+                               int64_t n_records, const int32_t* table, int64_t table_stride, const uint32_t* excluded, int bitmap_words,
+                               const int32_t* row_info, const int32_t* sched, int n_ctas, int n_parts, float scale, void* out, int out_dtype,
+                               float* lse, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* who = "lkv_ragged_exact_attention";
+  if (hot == nullptr || records == nullptr || table == nullptr || row_info == nullptr || sched == nullptr || q == nullptr)
+    return fail(LKV_ERR_PTR, "%s: null pointer", who);
+  if (rows <= 0 || heads <= 0 || rows % heads != 0 || n_ctas <= 0 || n_parts < n_ctas || n_records <= 0)
+    return fail(LKV_ERR_ARG, "%s: bad shape (rows %d, heads %d, CTAs %d, partials %d)", who, rows, heads, n_ctas, n_parts);
+  if (int rc = common_checks(who, q, rows * g, heads, d, bs, hot->dtype, workspace)) return rc;
+  if (hot->dtype != LKV_BF16 || !dtype_ok(out_dtype)) return fail(LKV_ERR_ARG, "%s: ragged rows are bf16", who);
+  if (out == nullptr && lse == nullptr) return fail(LKV_ERR_PTR, "%s: no output", who);
+  AttnParams p{};
+  p.q = q; p.hq = rows * g; p.h = heads; p.bs = bs; p.scale_log2 = scale * kLog2e;
+  if (int rc = fill_hot(who, p.seg[0], heads, d, bs, hot)) return rc;
+  // The range: candidate blocks from 1, as many as the longest row; each row's own count is in row_info.
+  lkv_cold_set cs{records, LKV_COLD_INT8, 1, (int)(n_records > INT32_MAX ? INT32_MAX : n_records), excluded, bitmap_words};
+  if (int rc = fill_cold(who, p.seg[1], heads, d, bs, LKV_BF16, &cs)) return rc;
+  p.seg[1].n_rows = n_records;  // bounds the table's entries
+  p.n_segs = 2;
+  cudaStream_t st = as_stream(stream);
+  const int4* sc = reinterpret_cast<const int4*>(sched);
+  const int4* ri = reinterpret_cast<const int4*>(row_info);
+  if (!aligned(sched, 16) || !aligned(row_info, 16)) return fail(LKV_ERR_PTR, "%s: schedule and row info must be 16-byte aligned", who);
+  if (out_dtype == LKV_BF16)
+    return run_attention_ragged<__nv_bfloat16>(who, p, g, d, sc, n_ctas, n_parts, ri, table, table_stride, heads, static_cast<__nv_bfloat16*>(out), lse,
+                                               workspace, workspace_bytes, st);
+  return run_attention_ragged<float>(who, p, g, d, sc, n_ctas, n_parts, ri, table, table_stride, heads, static_cast<float*>(out), lse, workspace,
+                                     workspace_bytes, st);
+}
 
 int lkv_device_status(int* status, int clear) {
   if (status == nullptr) return fail(LKV_ERR_PTR, "lkv_device_status: null pointer");

@@ -1152,3 +1152,218 @@ extern "C" int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h,
   return lkv_quest_topk(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode, order,
                         out_blocks, out_ld, out_bound, bitmap, bitmap_words, scratch, kNoAllocScratchBytes, stream);
 }
+
+// ---- ragged rows: many sequences' selections in two launches -------------------------------
+//
+// Continuous batching puts sequences of different lengths in one decode step. Row r = seq * heads
+// + head has n_cand(r) candidate blocks (logical blocks 1 .. n_cand) and keeps k(r) of them; its
+// blocks live anywhere in a paged store, found through the sequence's block table (logical block ->
+// store row), and the metadata kmin / kmax are [heads][store rows][d]. The score kernel takes a
+// flattened list of (row, first candidate) chunks of up to 256 candidates, so long and short rows
+// cost in proportion to their candidates; it computes each candidate's bound exactly as
+// quest_score_kernel does (same channel order and roundings) and stores its orderable form. The
+// select kernel is one CTA per row: a radix select over its keys in shared memory, then the kept
+// blocks in ascending id order (ties to the lowest ids, as the single-sequence select), and the
+// row's bitmap.
+
+namespace lkv {
+namespace {
+
+constexpr int kRaggedMaxCand = 16384;  // candidates of a row: the select keeps its keys in shared memory
+
+template <typename TQ, typename TM, int G>
+__global__ void ragged_score_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin, const TM* __restrict__ kmax, int64_t m_head,
+                                    int64_t n_store, int heads, const int32_t* __restrict__ table, int64_t table_stride,
+                                    const int2* __restrict__ work, const int2* __restrict__ row_sel, int bound_mode, uint32_t* __restrict__ keys,
+                                    int64_t key_stride) {
+  extern __shared__ __align__(16) float qs[];  // q+ [d][GP], q- [d][GP], then the two tiles
+  __shared__ int sh_store[256];
+  const int rows = blockDim.x;
+  const int row_bytes = d * (int)sizeof(TM);
+  const int chunks = row_bytes / 16;
+  unsigned char* tile_max = reinterpret_cast<unsigned char*>(qs + 2 * qpad<G>() * d);
+  unsigned char* tile_min = tile_max + (size_t)rows * row_bytes;
+  const int2 w = work[blockIdx.x];
+  const int r = w.x, c_first = w.y;
+  const int n_cand = row_sel[r].x;
+  const int n_rows = min(rows, n_cand - c_first);
+  if (n_rows <= 0) return;
+  const int head = r % heads;
+  const int32_t* tab = table + (int64_t)(r / heads) * table_stride;
+  stage_query<TQ, G>(q, r, d, qs);
+  for (int t = threadIdx.x; t < n_rows; t += blockDim.x) {
+    const int srow = __ldg(tab + 1 + c_first + t);
+    sh_store[t] = (srow >= 0 && srow < n_store) ? srow : -1;  // outside the store: no load, lowest key
+  }
+  __syncthreads();
+  for (int u = threadIdx.x; u < n_rows * chunks; u += blockDim.x) {
+    int t, c;
+    tile_rc(u, chunks, t, c);
+    const int srow = sh_store[t];
+    if (srow < 0) continue;
+    const int pos = tile_pos(t, c, chunks, row_bytes);
+    const int64_t off = (int64_t)head * m_head + (int64_t)srow * d;
+    cp_async16(tile_max + pos, reinterpret_cast<const uint4*>(kmax + off) + c);
+    cp_async16(tile_min + pos, reinterpret_cast<const uint4*>(kmin + off) + c);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < n_rows) {
+    uint32_t key = 0u;
+    if (sh_store[t] >= 0) key = orderable(row_bound<TQ, TM, G>(tile_max, tile_min, t, d, qs, bound_mode));
+    keys[(int64_t)r * key_stride + c_first + t] = key;
+  }
+}
+
+// One CTA (kSelectThreads) per row: out[r][0 .. k) the kept logical blocks ascending, bitmap row r.
+__global__ void __launch_bounds__(kSelectThreads) ragged_topk_kernel(const uint32_t* __restrict__ keys, int64_t key_stride,
+                                                                      const int2* __restrict__ row_sel, int n_passes, int32_t* __restrict__ out,
+                                                                      int64_t out_stride, uint32_t* __restrict__ bitmap, int bitmap_words) {
+  extern __shared__ uint32_t ks[];
+  __shared__ uint32_t hist[256], warp_sums[32];
+  __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total;
+  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const int n = min(row_sel[r].x, kRaggedMaxCand);
+  const int k = min(row_sel[r].y, n);
+  const uint32_t* src = keys + (int64_t)r * key_stride;
+  for (int i = tid; i < n; i += blockDim.x) ks[i] = src[i];
+  if (bitmap != nullptr)
+    for (int wd = tid; wd < bitmap_words; wd += blockDim.x) bitmap[(int64_t)r * bitmap_words + wd] = 0u;
+  if (tid == 0) {
+    sh_remaining = (uint32_t)k;
+    sh_bincount = 0u;
+  }
+  __syncthreads();
+  uint32_t prefix = 0u, mask = 0u;
+  bool take_all = k >= n;
+  for (int pass = 0; pass < n_passes && !take_all && k > 0; ++pass) {
+    const int shift = 24 - 8 * pass;
+    if (tid < 256) hist[tid] = 0u;
+    __syncthreads();
+    for (int base = 0; base < n; base += blockDim.x) {
+      const int i = base + tid;
+      const uint32_t key = i < n ? ks[i] : 0u;
+      const bool counted = i < n && (key & mask) == prefix;
+      const uint32_t digit = counted ? ((key >> shift) & 255u) : 256u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+      if (counted && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+    }
+    __syncthreads();
+    pick_digit(hist, &sh_digit, &sh_remaining, &sh_bincount);
+    __syncthreads();
+    prefix |= sh_digit << shift;
+    mask |= 255u << shift;
+    take_all = sh_bincount == sh_remaining;  // uniform: every thread read the same shared values
+    __syncthreads();
+  }
+  // Taken: keys above the prefix, then the first `need` keys at it in id order (all when take_all).
+  const uint32_t need = take_all ? 0xffffffffu : sh_remaining;
+  const bool all = k >= n;
+  const int per = (n + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
+  uint32_t gt = 0, eq = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t m = ks[i] & mask;
+    if (all || m > prefix || (take_all && m == prefix)) ++gt;
+    else if (m == prefix) ++eq;
+  }
+  const uint32_t pre = block_scan(gt | (eq << 16), warp_sums, &sh_total);
+  uint32_t pos_gt = pre & 0xffffu, pos_eq = pre >> 16;  // taken-above and tied keys before this thread's ids
+  if (k > 0)
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t m = ks[i] & mask;
+      const bool above = all || m > prefix || (take_all && m == prefix);
+      uint32_t pos = 0xffffffffu;
+      if (above) {
+        pos = pos_gt + min(pos_eq, need);
+        ++pos_gt;
+      } else if (m == prefix) {
+        if (pos_eq < need) pos = pos_gt + pos_eq;
+        ++pos_eq;
+      }
+      if (pos < (uint32_t)k) {
+        const int blk = 1 + i;
+        out[(int64_t)r * out_stride + pos] = blk;
+        if (bitmap != nullptr && blk / 32 < bitmap_words) atomicOr(&bitmap[(int64_t)r * bitmap_words + blk / 32], 1u << (blk % 32));
+      }
+    }
+}
+
+template <typename TQ, typename TM>
+int launch_ragged_score(int g, int d, int heads, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head,
+                        int64_t n_store, const int32_t* table, int64_t table_stride, const int2* work, int n_work, const int2* row_sel,
+                        int bound_mode, uint32_t* keys, int64_t key_stride) {
+  const int rows = 256;
+  auto smem_for = [&](int gp) { return (size_t)2 * gp * d * sizeof(float) + 2 * (size_t)rows * d * sizeof(TM); };
+  const TQ* qq = static_cast<const TQ*>(q);
+  const TM* mn = static_cast<const TM*>(kmin);
+  const TM* mx = static_cast<const TM*>(kmax);
+#define LKV_RAGGED_SCORE(GG)                                                                                                       \
+  {                                                                                                                                \
+    auto kern = ragged_score_kernel<TQ, TM, GG>;                                                                                   \
+    const size_t smem = smem_for(qpad<GG>());                                                                                      \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                    \
+    kern<<<n_work, rows, smem, st>>>(qq, d, mn, mx, m_head, n_store, heads, table, table_stride, work, row_sel, bound_mode, keys, \
+                                     key_stride);                                                                                  \
+    return launched("lkv_ragged_quest_topk(score)");                                                                              \
+  }
+  switch (g) {
+    case 1: LKV_RAGGED_SCORE(1)
+    case 2: LKV_RAGGED_SCORE(2)
+    case 4: LKV_RAGGED_SCORE(4)
+    case 8: LKV_RAGGED_SCORE(8)
+    default: return fail(LKV_ERR_ARG, "lkv_ragged_quest_topk: query group %d not in {1,2,4,8}", g);
+  }
+#undef LKV_RAGGED_SCORE
+}
+
+}  // namespace
+}  // namespace lkv
+
+extern "C" {
+
+size_t lkv_ragged_topk_workspace(int rows, int max_cand) {
+  if (rows <= 0 || max_cand <= 0) return 0;
+  return (size_t)rows * (size_t)max_cand * sizeof(uint32_t);
+}
+
+int lkv_ragged_quest_topk(const void* q, int q_dtype, int rows, int g, int d, int heads, const void* kmin, const void* kmax, int meta_dtype,
+                          int64_t m_head, int64_t n_store, const int32_t* table, int64_t table_stride, const int32_t* row_sel, int max_cand,
+                          const int32_t* work, int n_work, int bound_mode, int32_t* out_blocks, int64_t out_stride, uint32_t* bitmap,
+                          int bitmap_words, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* who = "lkv_ragged_quest_topk";
+  if (!dtype_ok(q_dtype) || !dtype_ok(meta_dtype) || !dtype_ok(bound_mode) || q_dtype != meta_dtype)
+    return fail(LKV_ERR_ARG, "%s: query and metadata must share a dtype (q %d, meta %d, bound %d)", who, q_dtype, meta_dtype, bound_mode);
+  if (rows <= 0 || heads <= 0 || rows % heads != 0) return fail(LKV_ERR_ARG, "%s: %d rows do not group over %d KV heads", who, rows, heads);
+  if (d <= 0 || d % 8 != 0 || d > 256) return fail(LKV_ERR_ARG, "%s: head_dim %d unsupported", who, d);
+  if (max_cand <= 0 || max_cand > kRaggedMaxCand) return fail(LKV_ERR_ARG, "%s: max_cand %d outside [1, %d]", who, max_cand, kRaggedMaxCand);
+  if (n_work <= 0 || n_store <= 0 || table_stride <= max_cand || out_stride <= 0)
+    return fail(LKV_ERR_ARG, "%s: bad sizes (work %d, store %lld, table stride %lld)", who, n_work, (long long)n_store, (long long)table_stride);
+  if (q == nullptr || kmin == nullptr || kmax == nullptr || table == nullptr || row_sel == nullptr || work == nullptr || out_blocks == nullptr ||
+      workspace == nullptr)
+    return fail(LKV_ERR_PTR, "%s: null pointer", who);
+  if (!aligned(kmin, 16) || !aligned(kmax, 16) || (m_head * (int64_t)dtype_size(meta_dtype)) % 16 != 0)
+    return fail(LKV_ERR_PTR, "%s: metadata rows must be 16-byte aligned", who);
+  if (!aligned(work, 8) || !aligned(row_sel, 8)) return fail(LKV_ERR_PTR, "%s: work and row_sel must be 8-byte aligned", who);
+  if (workspace_bytes < lkv_ragged_topk_workspace(rows, max_cand))
+    return fail(LKV_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, lkv_ragged_topk_workspace(rows, max_cand));
+  if (bitmap != nullptr && bitmap_words * 32ll < (int64_t)max_cand + 1)
+    return fail(LKV_ERR_ARG, "%s: bitmap of %d words cannot hold block %d", who, bitmap_words, max_cand);
+  cudaStream_t st = as_stream(stream);
+  uint32_t* keys = static_cast<uint32_t*>(workspace);
+  const int2* wk = reinterpret_cast<const int2*>(work);
+  const int2* rs = reinterpret_cast<const int2*>(row_sel);
+  int rc = q_dtype == LKV_BF16 ? launch_ragged_score<__nv_bfloat16, __nv_bfloat16>(g, d, heads, st, q, kmin, kmax, m_head, n_store, table, table_stride,
+                                                                                  wk, n_work, rs, bound_mode, keys, max_cand)
+                               : launch_ragged_score<float, float>(g, d, heads, st, q, kmin, kmax, m_head, n_store, table, table_stride, wk, n_work,
+                                                                  rs, bound_mode, keys, max_cand);
+  if (rc) return rc;
+  const size_t smem = (size_t)max_cand * sizeof(uint32_t);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(ragged_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  ragged_topk_kernel<<<rows, kSelectThreads, smem, st>>>(keys, max_cand, rs, bound_mode == LKV_BF16 ? 2 : 4, out_blocks, out_stride, bitmap,
+                                                         bitmap_words);
+  return launched("lkv_ragged_quest_topk(select)");
+}
+
+}  // extern "C"
