@@ -969,7 +969,7 @@ __device__ __forceinline__ float2 code_pair(uint32_t a, uint32_t c, uint32_t sel
 
 __device__ __forceinline__ float2 h2f2(uint32_t w) { return __half22float2(*reinterpret_cast<const __half2*>(&w)); }
 
-template <int G, typename TO>
+template <int G, typename TO, bool RAGGED>
 __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_kernel(const __grid_constant__ StreamParams sp) {
   static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query group");
   using C = StreamCfg<G>;
@@ -990,21 +990,28 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // The CTA's row: j (query group, lists, bitmap, outputs, counter), its KV head hj in the pool and
   // the records, the CTA's index ci among the row's P, the row's first partial pbase, the fill of its
-  // current block. Kept in shared memory and read where used, so that none stays in a register
-  // across the streaming loop.
+  // current block. A single sequence (RAGGED false) has them from the grid and the parameters; ragged
+  // rows from the schedule, kept in shared memory and read where used, so that none stays in a
+  // register across the streaming loop.
   __shared__ int sh_rp[6];  // j, ci, P, pbase, hj, last_fill
-  auto rp = [&](int i) { return *reinterpret_cast<volatile int*>(&sh_rp[i]); };
+  auto rp = [&](int i) -> int {
+    if constexpr (RAGGED) return *reinterpret_cast<volatile int*>(&sh_rp[i]);
+    switch (i) {
+      case 0: case 4: return (int)blockIdx.y;
+      case 1: return (int)blockIdx.x;
+      case 2: return sp.per_head;
+      case 3: return (int)blockIdx.y * sp.per_head;
+      default: return p.seg[0].last_fill;
+    }
+  };
   uint64_t* bars = bars_all + warp * NS;
   if (threadIdx.x == 0) {
     sh_bad = 0;
     mbar_init(&fold_bar, 1);
-    if (sp.sched != nullptr) {
+    if constexpr (RAGGED) {
       const int4 e = sp.sched[blockIdx.x];
       sh_rp[0] = e.x, sh_rp[1] = e.y, sh_rp[2] = e.z, sh_rp[3] = e.w, sh_rp[4] = e.x % sp.heads;
-      sh_rp[5] = sp.row_info != nullptr ? sp.row_info[e.x].y : p.seg[0].last_fill;
-    } else {
-      sh_rp[0] = blockIdx.y, sh_rp[1] = blockIdx.x, sh_rp[2] = sp.per_head, sh_rp[3] = blockIdx.y * sp.per_head, sh_rp[4] = blockIdx.y;
-      sh_rp[5] = p.seg[0].last_fill;
+      sh_rp[5] = sp.row_info[e.x].y;
     }
   }
   if (lane == 0) {
@@ -1015,7 +1022,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
 
   pdl_wait();  // the lists, the bitmap and the workspace are the predecessor's to finish with
   pdl_release();
-  __syncthreads();  // sh_rp
+  if constexpr (RAGGED) __syncthreads();  // sh_rp
   const int j = rp(0);
   // ---- set-up: counts, this CTA's item range, its list of storage rows ----
   // A list segment's count is its length; a range's is a popcount over the bitmap. In the common
@@ -1025,19 +1032,20 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   const Seg& S0 = p.seg[0];
   const Seg& S1 = p.seg[1];
   // The row's item counts (list length, range blocks) and the fill of its current block.
-  int n_seg[2] = {S0.n_items, p.n_segs > 1 ? S1.n_items : 0};
-  if (sp.row_info != nullptr) {
-    const int4 ri = sp.row_info[j];
-    n_seg[0] = ri.x, n_seg[1] = ri.z;
-  }
+  int n_seg0 = S0.n_items, n_seg1 = p.n_segs > 1 ? S1.n_items : 0;  // the row's list items and range blocks
   // A range block's record row: the block itself, or its entry in the sequence's block table.
-  const int32_t* table = sp.table != nullptr ? sp.table + (int64_t)(j / sp.heads) * sp.table_stride : nullptr;
+  const int32_t* table = nullptr;
+  if constexpr (RAGGED) {
+    const int4 ri = sp.row_info[j];
+    n_seg0 = ri.x, n_seg1 = ri.z;
+    table = sp.table + (int64_t)(j / sp.heads) * sp.table_stride;
+  }
   const bool fast = p.n_segs == 2 && S0.kind == SEG_LIST && S1.kind != SEG_LIST &&
-                    (n_seg[1] <= 0 || (S1.first_block + n_seg[1] - 1) / 32 - S1.first_block / 32 < kSetupWords * kStreamThreads);
+                    (n_seg1 <= 0 || (S1.first_block + n_seg1 - 1) / 32 - S1.first_block / 32 < kSetupWords * kStreamThreads);
   int64_t cnt0 = 0, cnt1 = 0, la0 = 0, lb0 = 0, la1 = 0, lb1 = 0;
   int n_a = 0, n_b = 0;
   if (fast) {
-    cnt0 = n_seg[0];
+    cnt0 = n_seg0;
     la0 = cnt0 * rp(1) / rp(2);
     lb0 = cnt0 * (rp(1) + 1) / rp(2);
     n_a = (int)(lb0 - la0);
@@ -1055,7 +1063,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     const int w0 = S1.first_block / 32 + threadIdx.x * kSetupWords;
 #pragma unroll
     for (int k = 0; k < kSetupWords; ++k) {
-      bits[k] = n_seg[1] > 0 ? range_word_bits(S1, n_seg[1], j, w0 + k) : 0u;
+      bits[k] = n_seg1 > 0 ? range_word_bits(S1, n_seg1, j, w0 + k) : 0u;
       mine += __popc(bits[k]);
     }
     const int before = block_excl_scan(mine, warp_sums, &sh_total);
@@ -1097,11 +1105,11 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   } else {
     for (int s = 0; s < p.n_segs; ++s) {
       const Seg& S = p.seg[s];
-      int64_t c = n_seg[s];
-      if (S.kind != SEG_LIST && n_seg[s] > 0) {
-        const int w0 = S.first_block / 32, w1 = (S.first_block + n_seg[s] - 1) / 32;
+      int64_t c = (s == 0 ? n_seg0 : n_seg1);
+      if (S.kind != SEG_LIST && (s == 0 ? n_seg0 : n_seg1) > 0) {
+        const int w0 = S.first_block / 32, w1 = (S.first_block + (s == 0 ? n_seg0 : n_seg1) - 1) / 32;
         int mine = 0;
-        for (int w = w0 + threadIdx.x; w <= w1; w += blockDim.x) mine += __popc(range_word_bits(S, n_seg[s], j, w));
+        for (int w = w0 + threadIdx.x; w <= w1; w += blockDim.x) mine += __popc(range_word_bits(S, (s == 0 ? n_seg0 : n_seg1), j, w));
         block_excl_scan(mine, warp_sums, &sh_total);
         c = sh_total;
       }
@@ -1129,11 +1137,11 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
           }
         } else {
           // Ordinal of each word's first kept block by a block-wide scan, chunk by chunk.
-          const int w0 = S.first_block / 32, w1 = (S.first_block + n_seg[s] - 1) / 32;
+          const int w0 = S.first_block / 32, w1 = (S.first_block + (s == 0 ? n_seg0 : n_seg1) - 1) / 32;
           int64_t run = 0;
           for (int c0 = w0; c0 <= w1 && run < lb; c0 += blockDim.x) {
             const int w = c0 + threadIdx.x;
-            uint32_t bits = w <= w1 ? range_word_bits(S, n_seg[s], j, w) : 0u;
+            uint32_t bits = w <= w1 ? range_word_bits(S, (s == 0 ? n_seg0 : n_seg1), j, w) : 0u;
             const int before = block_excl_scan(__popc(bits), warp_sums, &sh_total);
             int64_t ord = run + before;
             while (bits != 0u && ord < lb) {
@@ -1198,7 +1206,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   // Per set: whether its items are int8 records (else bf16 tile pairs through the tensor maps).
   const bool rec0 = p.seg[0].kind == SEG_RANGE_REC, rec1 = p.n_segs > 1 && p.seg[1].kind == SEG_RANGE_REC;
   // The warp's item holding the current block (the last listed block, `last_fill` live tokens), if any.
-  const int fill_k = (p.seg[0].kind == SEG_LIST && lb0 == n_seg[0] && hn > 0 && ha + hn == n_a) ? hn - 1 : -1;
+  const int fill_k = (p.seg[0].kind == SEG_LIST && lb0 == n_seg0 && hn > 0 && ha + hn == n_a) ? hn - 1 : -1;
   const uint64_t stream_pol = l2_evict_first_policy();  // every item is read once
   // Lane 0 fills stage s with the warp's k-th item (or arrives for a padding item).
   auto issue = [&](int k, int s) {
@@ -1993,12 +2001,13 @@ template <int G, typename TO>
 int launch_stream(const StreamParams& sp, cudaStream_t st) {
   using C = StreamCfg<G>;
   static uint64_t attr_set = 0;  // one bit per device
-  auto k = attn_stream_kernel<G, TO>;
+  auto k = sp.sched != nullptr ? attn_stream_kernel<G, TO, true> : attn_stream_kernel<G, TO, false>;
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_set & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  if (!(attr_set & bit)) {  // both instances: a single sequence's and ragged rows'
+    cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel<G, TO, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_stream_kernel<G, TO, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
     attr_set |= bit;
   }
