@@ -19,7 +19,13 @@ Layout (one selecting layer):
   - pool [max_seqs * (k_max + 2), h, 2, bs, d] in the model dtype: per sequence slot s, pool row
     s * (k_max + 2) holds the exact sink, the next k_max rows the blocks kept this step, the last
     the current (unsealed) block.
-Residency is fetch-on-select: the kept blocks are fetched every step (no cross-step LRU here).
+The store lives in HBM, so by default the kept blocks are attended in place: their records are
+dequantised in the attention kernel exactly as a fetch would dequantise them into a slot, so the
+step attends [sink, current] from the pool and every candidate block from the store (kept or not),
+which is the same set of values as the hot/cold split; the selection is still computed and returned
+(for a caller whose residency decides what to fetch). `decode(..., fetch=True)` runs the split as
+the batch-1 tier does instead: the kept blocks are fetched into the sequence's HBM slots every step
+(fetch-on-select, no cross-step LRU) and excluded from the cold pass.
 """
 
 from __future__ import annotations
@@ -155,7 +161,7 @@ class RaggedTier:
         seq = self.seqs[s]
         return max(0, min(blocks_for_budget(self.budget, seq.length, self.bs), seq.n_sealed - 1))
 
-    def decode(self, seq_ids: list[int], query: torch.Tensor, scale: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    def decode(self, seq_ids: list[int], query: torch.Tensor, scale: float, fetch: bool = False) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """Attention of `query` [n * h * g, d] (sequence seq_ids[i]'s query heads in block i) over each
         sequence's tier: out [n * h * g, d] float32, lse [n * h * g] float32 and the kept blocks
         [n * h, k_max] (row i * h + head; entries past the row's K are unspecified)."""
@@ -172,8 +178,12 @@ class RaggedTier:
         k = np.array([self.k_of(s) for s in seq_ids], dtype=np.int32).repeat(h)
         fill = np.array([self.seqs[s].fill for s in seq_ids], dtype=np.int32).repeat(h)
         # host-built arrays, uploaded together: row_sel, work, row_info, sched
-        work = np.array([(r, c) for r in range(rows) for c in range(0, int(n_cand[r]), CHUNK)], dtype=np.int32).reshape(-1, 2)
-        items = (k + 2 + (n_cand - k)).astype(np.int32)
+        per_row = (n_cand + CHUNK - 1) // CHUNK
+        starts = np.cumsum(per_row) - per_row
+        row_of = np.repeat(np.arange(rows, dtype=np.int32), per_row)
+        work = np.stack([row_of, (np.arange(int(per_row.sum()), dtype=np.int32) - np.repeat(starts, per_row).astype(np.int32)) * CHUNK], axis=1)
+        n_hot = (k + 2) if fetch else np.full_like(k, 2)  # [sink, kept..., current] or [sink, current]
+        items = (n_hot + n_cand - (k if fetch else 0)).astype(np.int32)
         sm = torch.cuda.get_device_properties(dev).multi_processor_count
         max_ctas = int(items.sum()) // 64 + rows + 1
         sched = np.zeros((max_ctas, 4), dtype=np.int32)
@@ -182,7 +192,7 @@ class RaggedTier:
         if n_ctas <= 0:
             raise L.LkvError(f"lkv_ragged_schedule failed ({n_ctas}): {L.last_error()}")
         row_sel = np.stack([n_cand, k], axis=1)
-        row_info = np.stack([k + 2, fill, n_cand, np.zeros_like(k)], axis=1)
+        row_info = np.stack([n_hot, fill, n_cand, np.zeros_like(k)], axis=1)
         host = np.concatenate([row_sel.ravel(), work.ravel(), row_info.ravel(), sched[:n_ctas].ravel()]).astype(np.int32)
         dmeta = torch.from_numpy(host).to(dev, non_blocking=False)
         o1 = row_sel.size
@@ -201,30 +211,36 @@ class RaggedTier:
         call("lkv_ragged_quest_topk", ptr(query), dtype_code(query.dtype), rows, g, self.d, h, ptr(self.kmin), ptr(self.kmax), dtype_code(self.dtype),
              self.kmin.stride(0), self.kmin.shape[1], ptr(table), table.stride(0), ptr(d_row_sel), max_cand, ptr(d_work), work.shape[0],
              dtype_code(self.dtype), ptr(sel), sel.stride(0), ptr(bitmap), self.words, ptr(ws), ws.numel(), stream_handle(dev))
-        # 2. fetch-on-select: kept block i of row (seq b, head j) -> pool row base(seq) + 1 + i
-        kk = torch.from_numpy(k).to(dev).long()
-        i = torch.arange(self.k_max, device=dev)
-        last = sel.gather(1, (kk - 1).clamp(min=0)[:, None])
-        blk = torch.where(i[None, :] < kk[:, None], sel, last).long()  # past K: repeat the last kept block (same copy)
-        i_c = torch.minimum(i[None, :], (kk - 1).clamp(min=0)[:, None])
         b_of_row = torch.arange(rows, device=dev) // h
-        head = torch.arange(rows, device=dev) % h
-        src = table.long()[b_of_row[:, None], blk] * h + head[:, None]
         base = (sid * self.per_seq)[b_of_row]
-        dst = (base[:, None] + 1 + i_c) * h + head[:, None]
-        K.fetch_pairs(self.records.view(-1, self.W), src.reshape(-1).contiguous(), self.pool.view(-1, 2, self.bs, self.d),
-                      dst.reshape(-1).contiguous(), self.bs, self.d)
-        # 3. attention: hot list of pool rows [sink, kept..., current]
-        hot = (base[:, None] + torch.arange(self.k_max + 2, device=dev)[None, :]).to(torch.int32)
-        hot[torch.arange(rows, device=dev), kk + 1] = (base + self.per_seq - 1).to(torch.int32)
+        if fetch:
+            # 2. fetch-on-select: kept block i of row (seq b, head j) -> pool row base(seq) + 1 + i
+            kk = torch.from_numpy(k).to(dev).long()
+            i = torch.arange(self.k_max, device=dev)
+            last = sel.gather(1, (kk - 1).clamp(min=0)[:, None])
+            blk = torch.where(i[None, :] < kk[:, None], sel, last).long()  # past K: repeat the last kept block (same copy)
+            i_c = torch.minimum(i[None, :], (kk - 1).clamp(min=0)[:, None])
+            head = torch.arange(rows, device=dev) % h
+            src = table.long()[b_of_row[:, None], blk] * h + head[:, None]
+            dst = (base[:, None] + 1 + i_c) * h + head[:, None]
+            K.fetch_pairs(self.records.view(-1, self.W), src.reshape(-1).contiguous(), self.pool.view(-1, 2, self.bs, self.d),
+                          dst.reshape(-1).contiguous(), self.bs, self.d)
+            # 3. attention: hot list of pool rows [sink, kept..., current], the kept blocks excluded from the store pass
+            hot = (base[:, None] + torch.arange(self.k_max + 2, device=dev)[None, :]).to(torch.int32)
+            hot[torch.arange(rows, device=dev), kk + 1] = (base + self.per_seq - 1).to(torch.int32)
+            excluded = bitmap
+        else:
+            # 3. attention: [sink, current] from the pool, every candidate from the store
+            hot = torch.stack([base, base + self.per_seq - 1], dim=1).to(torch.int32)
+            excluded = None
         hot = hot.contiguous()
         out = torch.empty((rows * g, self.d), dtype=torch.float32, device=dev)
         lse = torch.empty((rows * g,), dtype=torch.float32, device=dev)
         s_row, s_head, s_tok = h * 2 * self.bs * self.d, 2 * self.bs * self.d, self.d
-        hs = L.HotSet(ptr(self.pool), ptr(self.pool[:, :, 1]), dtype_code(self.dtype), s_row, s_head, s_tok, ptr(hot), self.k_max + 2, None, 0, 0,
+        hs = L.HotSet(ptr(self.pool), ptr(self.pool[:, :, 1]), dtype_code(self.dtype), s_row, s_head, s_tok, ptr(hot), hot.shape[1], None, 0, 0,
                       self.pool.shape[0])
         ws2 = K.workspace(dev, L.lib().lkv_ragged_attention_workspace(g, n_parts.value), slot=6)
         call("lkv_ragged_exact_attention", ptr(query), rows, g, self.d, self.bs, h, ctypes.byref(hs), ptr(self.records), self.records.shape[0],
-             ptr(table), table.stride(0), ptr(bitmap), self.words, ptr(d_row_info), ptr(d_sched), n_ctas, n_parts.value, float(scale), ptr(out),
+             ptr(table), table.stride(0), ptr(excluded), self.words, ptr(d_row_info), ptr(d_sched), n_ctas, n_parts.value, float(scale), ptr(out),
              L.LKV_F32, ptr(lse), ptr(ws2), ws2.numel(), stream_handle(dev))
         return out, lse, sel

@@ -33,9 +33,9 @@ def _oracle(keys: torch.Tensor, values: torch.Tensor, query: torch.Tensor, k: in
     return O.tiered_decode(query.float().cpu().numpy(), sealed, current, fill, k, SCALE, model_dtype="bfloat16", quant="int8")
 
 
-def _check(tier, ids: list[int], kv: dict, gen: torch.Generator) -> None:  # noqa: ANN001
+def _check(tier, ids: list[int], kv: dict, gen: torch.Generator, fetch: bool) -> None:  # noqa: ANN001
     q = torch.randn((len(ids) * H * G, D), generator=gen, device="cuda").bfloat16()
-    out, lse, sel = tier.decode(ids, q, SCALE)
+    out, lse, sel = tier.decode(ids, q, SCALE, fetch=fetch)
     torch.cuda.synchronize()
     for b, s in enumerate(ids):
         k = tier.k_of(s)
@@ -48,7 +48,8 @@ def _check(tier, ids: list[int], kv: dict, gen: torch.Generator) -> None:  # noq
         np.testing.assert_allclose(lse[b * H * G : (b + 1) * H * G].double().cpu().numpy().reshape(H, G), want["lse"], rtol=1e-5, atol=1e-5)
 
 
-def test_one_launch_matches_each_sequence_decoded_alone() -> None:
+@pytest.mark.parametrize("fetch", [False, True])  # kept blocks read in place from the store, or fetched into HBM slots
+def test_one_launch_matches_each_sequence_decoded_alone(fetch: bool) -> None:
     from lazykv_b200 import kernels
     from lazykv_b200.ragged import RaggedTier
 
@@ -62,11 +63,12 @@ def test_one_launch_matches_each_sequence_decoded_alone() -> None:
         s = tier.add(keys, values)
         kv[s] = (keys, values)
         ids.append(s)
-    _check(tier, ids, kv, gen)
+    _check(tier, ids, kv, gen, fetch)
     assert kernels.device_status() == 0
 
 
-def test_sequences_grow_seal_finish_and_are_replaced() -> None:
+@pytest.mark.parametrize("fetch", [False, True])
+def test_sequences_grow_seal_finish_and_are_replaced(fetch: bool) -> None:
     from lazykv_b200 import kernels
     from lazykv_b200.ragged import RaggedTier
 
@@ -88,7 +90,7 @@ def test_sequences_grow_seal_finish_and_are_replaced() -> None:
             keys, values = _kv(gen, 90 + 7 * step)
             kv[tier.add(keys, values)] = (keys, values)
         if step % 4 == 3 or step == 19:
-            _check(tier, sorted(kv), kv, gen)
+            _check(tier, sorted(kv), kv, gen, fetch)
     assert kernels.device_status() == 0
 
 
