@@ -247,7 +247,7 @@ def layer_step(L, geo: dict, cold_store=None, events: list | None = None) -> Non
     mark()
 
 
-LAUNCHES_PER_LAYER_STEP = 3  # score (+ first radix pass), cluster select, attention (both passes; the head's last CTA folds)
+LAUNCHES_PER_LAYER_STEP = 2  # the single-launch selection (scores and radix select) and the attention (both passes; the head's last CTA folds)
 
 
 def profile_calls(args: argparse.Namespace) -> None:
