@@ -2116,10 +2116,10 @@ extern "C" {
 
 int lkv_ragged_schedule(const int32_t* row_items, int rows, int n_sms, int32_t* sched, int max_ctas, int* n_parts) {
   if (row_items == nullptr || sched == nullptr || n_parts == nullptr || rows <= 0 || n_sms <= 0)
-    return fail(LKV_ERR_ARG, "lkv_ragged_schedule: bad arguments");
+    return -fail(LKV_ERR_ARG, "lkv_ragged_schedule: bad arguments");
   int64_t total = 0;
   for (int r = 0; r < rows; ++r) {
-    if (row_items[r] < 0) return fail(LKV_ERR_ARG, "lkv_ragged_schedule: row %d has %d items", r, row_items[r]);
+    if (row_items[r] < 0) return -fail(LKV_ERR_ARG, "lkv_ragged_schedule: row %d has %d items", r, row_items[r]);
     total += row_items[r];
   }
   // Items per CTA: about four waves of one CTA per SM, at least 64 items and at most what a CTA's
@@ -2130,7 +2130,7 @@ int lkv_ragged_schedule(const int32_t* row_items, int rows, int n_sms, int32_t* 
   int n = 0, parts = 0;
   for (int r = 0; r < rows; ++r) {
     const int P = (int)((row_items[r] + chunk - 1) / chunk) > 0 ? (int)((row_items[r] + chunk - 1) / chunk) : 1;
-    if (n + P > max_ctas) return fail(LKV_ERR_WORKSPACE, "lkv_ragged_schedule: more than %d CTAs", max_ctas);
+    if (n + P > max_ctas) return -fail(LKV_ERR_WORKSPACE, "lkv_ragged_schedule: more than %d CTAs", max_ctas);
     for (int c = 0; c < P; ++c, ++n) {
       sched[4 * n + 0] = r;
       sched[4 * n + 1] = c;

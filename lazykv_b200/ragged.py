@@ -44,6 +44,30 @@ from lazykv_b200.selection import blocks_for_budget
 CHUNK = 256  # candidates per CTA of the ragged score kernel
 
 
+def work_list(n_cand: np.ndarray) -> np.ndarray:
+    """The score kernel's chunks [n, 2] int32: (row, first candidate) for every CHUNK candidates of
+    each row, rows in order (a row with n candidates has ceil(n / CHUNK) chunks at 0, CHUNK, ...)."""
+    n_cand = np.asarray(n_cand, dtype=np.int64)
+    per_row = (n_cand + CHUNK - 1) // CHUNK
+    starts = np.cumsum(per_row) - per_row
+    row_of = np.repeat(np.arange(len(n_cand)), per_row)
+    first = (np.arange(int(per_row.sum())) - np.repeat(starts, per_row)) * CHUNK
+    return np.stack([row_of, first], axis=1).astype(np.int32)
+
+
+def schedule(row_items: np.ndarray, n_sms: int) -> tuple[np.ndarray, int]:
+    """The ragged attention's CTAs (lkv_ragged_schedule, host only): [n, 4] int32 rows of (row, index
+    in the row, the row's CTAs, the row's first partial), and the number of partials."""
+    items = np.ascontiguousarray(row_items, dtype=np.int32)
+    max_ctas = int(items.sum()) // 64 + len(items) + 1
+    sched = np.zeros((max_ctas, 4), dtype=np.int32)
+    n_parts = ctypes.c_int(0)
+    n = L.lib().lkv_ragged_schedule(items.ctypes.data, len(items), n_sms, sched.ctypes.data, max_ctas, ctypes.byref(n_parts))
+    if n <= 0:
+        raise L.LkvError(f"lkv_ragged_schedule failed ({n}): {L.last_error()}")
+    return sched[:n], n_parts.value
+
+
 @dataclass
 class _Seq:
     length: int
@@ -178,22 +202,15 @@ class RaggedTier:
         k = np.array([self.k_of(s) for s in seq_ids], dtype=np.int32).repeat(h)
         fill = np.array([self.seqs[s].fill for s in seq_ids], dtype=np.int32).repeat(h)
         # host-built arrays, uploaded together: row_sel, work, row_info, sched
-        per_row = (n_cand + CHUNK - 1) // CHUNK
-        starts = np.cumsum(per_row) - per_row
-        row_of = np.repeat(np.arange(rows, dtype=np.int32), per_row)
-        work = np.stack([row_of, (np.arange(int(per_row.sum()), dtype=np.int32) - np.repeat(starts, per_row).astype(np.int32)) * CHUNK], axis=1)
+        work = work_list(n_cand)
         n_hot = (k + 2) if fetch else np.full_like(k, 2)  # [sink, kept..., current] or [sink, current]
         items = (n_hot + n_cand - (k if fetch else 0)).astype(np.int32)
         sm = torch.cuda.get_device_properties(dev).multi_processor_count
-        max_ctas = int(items.sum()) // 64 + rows + 1
-        sched = np.zeros((max_ctas, 4), dtype=np.int32)
-        n_parts = ctypes.c_int(0)
-        n_ctas = L.lib().lkv_ragged_schedule(items.ctypes.data, rows, sm, sched.ctypes.data, max_ctas, ctypes.byref(n_parts))
-        if n_ctas <= 0:
-            raise L.LkvError(f"lkv_ragged_schedule failed ({n_ctas}): {L.last_error()}")
+        sched, n_parts = schedule(items, sm)
+        n_ctas = sched.shape[0]
         row_sel = np.stack([n_cand, k], axis=1)
         row_info = np.stack([n_hot, fill, n_cand, np.zeros_like(k)], axis=1)
-        host = np.concatenate([row_sel.ravel(), work.ravel(), row_info.ravel(), sched[:n_ctas].ravel()]).astype(np.int32)
+        host = np.concatenate([row_sel.ravel(), work.ravel(), row_info.ravel(), sched.ravel()]).astype(np.int32)
         dmeta = torch.from_numpy(host).to(dev, non_blocking=False)
         o1 = row_sel.size
         o2 = o1 + work.size
@@ -239,8 +256,8 @@ class RaggedTier:
         s_row, s_head, s_tok = h * 2 * self.bs * self.d, 2 * self.bs * self.d, self.d
         hs = L.HotSet(ptr(self.pool), ptr(self.pool[:, :, 1]), dtype_code(self.dtype), s_row, s_head, s_tok, ptr(hot), hot.shape[1], None, 0, 0,
                       self.pool.shape[0])
-        ws2 = K.workspace(dev, L.lib().lkv_ragged_attention_workspace(g, n_parts.value), slot=6)
+        ws2 = K.workspace(dev, L.lib().lkv_ragged_attention_workspace(g, n_parts), slot=6)
         call("lkv_ragged_exact_attention", ptr(query), rows, g, self.d, self.bs, h, ctypes.byref(hs), ptr(self.records), self.records.shape[0],
-             ptr(table), table.stride(0), ptr(excluded), self.words, ptr(d_row_info), ptr(d_sched), n_ctas, n_parts.value, float(scale), ptr(out),
+             ptr(table), table.stride(0), ptr(excluded), self.words, ptr(d_row_info), ptr(d_sched), n_ctas, n_parts, float(scale), ptr(out),
              L.LKV_F32, ptr(lse), ptr(ws2), ws2.numel(), stream_handle(dev))
         return out, lse, sel
