@@ -500,13 +500,18 @@ def run_ours(args: argparse.Namespace) -> None:
 
     if rank == 0 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, budget_s=12.0)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
     if world > 1:
-        del graph  # a graph holding NCCL work is released before its process group
+        # The graph holds NCCL work: every reference to it (the graph and its bound replay) goes
+        # before the process group does, or the group's destruction waits for it for good.
+        import gc
+
+        del run, graph
+        gc.collect()
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(result))
 
 
 # ---------------------------------------------------------------------------------------------
