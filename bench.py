@@ -609,8 +609,8 @@ def run_reference(args: argparse.Namespace) -> None:
 def run_ragged(args: argparse.Namespace) -> None:
     """ragged continuous batching. 64 sequences with lengths uniform in [4,096,
     131,072] (seeded), Llama-3.2-1B attention shapes, 6.25% budget, the int8 store in HBM, one
-    selecting layer. A step is one decode token of every sequence through that layer (selection,
-    fetch of the kept blocks, exact attention with the cold merge), timed with CUDA events; between
+    selecting layer. A step is one decode token of every sequence through that layer (selection and
+    the exact attention, the kept blocks read in place from the store), timed with CUDA events; between
     timed steps each sequence appends its token and, at random, a sequence finishes and a new one of
     random length takes its slot (untimed, as a prefill would be). Prints one JSON line."""
     import torch
