@@ -101,11 +101,15 @@ int lkv_fetch_pairs(const void* src, int src_kind, const int64_t* src_rows, void
  * LKV_ORDER_BLOCK in ascending block id (no sort). Optional: out_bound [h, n_cand] float32;
  * bitmap [h, bitmap_words] set exactly at the selected block ids (the words are cleared first).
  * Workspace: lkv_quest_topk_workspace(h, n_cand) bytes, zero-filled once when allocated: its first
- * 64 KiB + 593,920 bytes hold per-head counters and state that the LKV_ORDER_BLOCK paths expect at
- * zero (where they count) and leave so (calls on one workspace must not overlap on the GPU). With bf16 query and metadata
- * at head_dim 64 in LKV_ORDER_BLOCK the selection is one launch whose CTAs wait for one another
- * (bounded waits, a timeout recorded in lkv_device_status); it is taken only when all of its CTAs
- * fit on the GPU at once.
+ * 64 KiB + 256 bytes hold per-head counters that the LKV_ORDER_BLOCK paths expect at zero and
+ * leave so (calls on one workspace must not overlap on the GPU; re-zero them after a call that
+ * returned an error). With bf16 query and metadata at head_dim 64 in LKV_ORDER_BLOCK (G in
+ * {1, 2, 4, 8}, n_cand <= 16,384, h <= 64) the selection is a TMA scoring kernel (CTAs of 256
+ * candidates) followed, by programmatic dependent launch, by a select kernel of one 8-CTA cluster
+ * per head; no CTA waits for a CTA outside its cluster. The scoring's tile loads are bounded waits:
+ * a wait that runs out records status 1 (lkv_device_status, lkv_status_poll) and the head's output
+ * becomes every listed id -1 and an empty bitmap, so an exact pass over the complement still
+ * covers every candidate.
  */
 size_t lkv_quest_topk_workspace(int h, int n_cand);
 int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
@@ -119,11 +123,13 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
  * when they select (an allocator-free runtime, an allocator callback, a process that reserved all
  * device memory up front). No counterpart in the reference. Same arguments, results and errors
  * as lkv_quest_topk; its scratch is a fixed device array inside the library (4 MiB of keys after
- * the per-head counters, 4.3 MiB in all), so it takes
- * h * n_cand <= 524,288 and returns LKV_ERR_ARG above that. It allocates nothing. The first call
- * on a device looks up that array's device address (make it before any stream capture); calls
- * must run with the stream's device current. All calls share the array: calls that overlap on
- * the GPU race, so serialise them (one stream, or events).
+ * 64 KiB + 256 bytes of counters), so it takes h * n_cand <= 524,288 and returns LKV_ERR_ARG above
+ * that. It allocates nothing. The first call on a device looks up that array's device address
+ * (make it before any stream capture); calls must run with the stream's device current. All calls
+ * share the array: calls that overlap on the GPU race, so serialise them (one stream, or events).
+ * The counters must read zero when a call starts: the array starts zeroed, every complete call
+ * leaves them zero, and a call that returns an error clears them (an asynchronous memset on the
+ * stream, which allocates nothing).
  */
 int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
                            const void* kmax, int meta_dtype, int64_t m_head, int first_block,
@@ -302,6 +308,29 @@ int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32
  * No reference counterpart (the reference has no device-side waits).
  */
 int lkv_device_status(int* status, int clear);
+
+/*
+ * A mirror of the status word in pinned, mapped host memory: after lkv_status_attach() (once per
+ * device, with that device current; allocates the host word on the first call in the process),
+ * every kernel that records a status also sets the mirror with a system-scope atomic, and
+ * lkv_status_poll() reads it without synchronising (it sees a kernel's status once that kernel has
+ * run), clearing it if asked. A decode loop polls it once per step to turn a bounded wait that ran
+ * out into an error on the host without a device synchronisation per step.
+ * No reference counterpart (the reference has no device-side waits).
+ */
+int lkv_status_attach(void);
+int lkv_status_poll(int* status, int clear);
+
+/*
+ * Test hooks of the bounded waits (no reference counterpart). key LKV_DEBUG_SELECT_WAIT_ITERS sets
+ * the bound (tries, 1 .. 2^21) of the TMA-scored selection's tile waits, for every later call in
+ * the process; LKV_DEBUG_SELECT_STALL_NEXT = 1 makes every scoring CTA of the next TMA-scored
+ * selection first wait on a barrier that nothing completes, so that the wait runs out and the
+ * failure path runs (status 1, poisoned output) with the GPU left usable. Not for production use;
+ * not thread-safe.
+ */
+enum { LKV_DEBUG_SELECT_WAIT_ITERS = 1, LKV_DEBUG_SELECT_STALL_NEXT = 2 };
+int lkv_debug_set(int key, int64_t value);
 
 /*
  * Log-sum-exp merge of n_parts partials. Replaces lazykv/exact.py:69-85 merge_lse (n_parts = 2)

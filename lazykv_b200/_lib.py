@@ -18,6 +18,8 @@ LIB_PATH = Path(__file__).resolve().parent / "liblkv_sm100.so"
 LKV_F32, LKV_BF16 = 0, 1
 LKV_COLD_INT8, LKV_COLD_PAIRS = 0, 1
 LKV_ORDER_BOUND, LKV_ORDER_BLOCK = 0, 1
+LKV_DEBUG_SELECT_WAIT_ITERS, LKV_DEBUG_SELECT_STALL_NEXT = 1, 2
+LKV_DEV_WAIT_TIMEOUT, LKV_DEV_LIST_OVERFLOW = 1, 2
 
 _lib: ctypes.CDLL | None = None
 
@@ -44,6 +46,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_exact_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "lkv_exact_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_device_status": (c_int, [c_void_p, c_int]),
+    "lkv_status_attach": (c_int, []),
+    "lkv_status_poll": (c_int, [c_void_p, c_int]),
+    "lkv_debug_set": (c_int, [c_int, c_int64]),
     "lkv_ragged_topk_workspace": (c_size_t, [c_int, c_int]),
     "lkv_ragged_quest_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int64,
                                       c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),

@@ -35,11 +35,14 @@
 #include <cudaTypedefs.h>
 
 #include <type_traits>
+#include <mutex>
 
 #include "tma.cuh"
 
 namespace lkv {
 namespace {
+
+int* g_status_word = nullptr;  // the host mirror of the status word (lkv_status_attach)
 
 constexpr int kWarps = 4;
 constexpr int kThreads = 32 * kWarps;
@@ -1168,7 +1171,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     sh_lo[1] = (int)la1;
     if (n_a + n_b > kStreamListCap) {  // the host sizes P so that this cannot happen
       sh_bad = 2;
-      atomicCAS(&g_device_status, 0, LKV_DEV_LIST_OVERFLOW);
+      record_status(LKV_DEV_LIST_OVERFLOW);
     }
   }
   __syncthreads();
@@ -2186,6 +2189,35 @@ int lkv_device_status(int* status, int clear) {
   if (e == cudaSuccess) e = select_device_status(&b, clear);
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_device_status: %s", cudaGetErrorString(e));
   *status = a != 0 ? a : b;
+  return LKV_OK;
+}
+
+int lkv_status_attach(void) {
+  static std::mutex mu;
+  static int* host_word = nullptr;  // pinned, mapped, portable: one word for every device
+  std::lock_guard<std::mutex> lock(mu);
+  cudaError_t e = cudaSuccess;
+  if (host_word == nullptr) {
+    void* p = nullptr;
+    e = cudaHostAlloc(&p, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_status_attach: cudaHostAlloc: %s", cudaGetErrorString(e));
+    host_word = static_cast<int*>(p);
+    __atomic_store_n(host_word, 0, __ATOMIC_SEQ_CST);
+    g_status_word = host_word;
+  }
+  int* dev_word = nullptr;
+  e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev_word), host_word, 0);
+  if (e == cudaSuccess) e = tu_status_attach(dev_word);
+  if (e == cudaSuccess) e = select_status_attach(dev_word);
+  if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_status_attach: %s", cudaGetErrorString(e));
+  return LKV_OK;
+}
+
+int lkv_status_poll(int* status, int clear) {
+  if (status == nullptr) return fail(LKV_ERR_PTR, "lkv_status_poll: null pointer");
+  int* w = g_status_word;
+  if (w == nullptr) return fail(LKV_ERR_ARG, "lkv_status_poll: lkv_status_attach has not been called");
+  *status = clear ? __atomic_exchange_n(w, 0, __ATOMIC_SEQ_CST) : __atomic_load_n(w, __ATOMIC_SEQ_CST);
   return LKV_OK;
 }
 

@@ -23,6 +23,8 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 // The status word of select.cu's kernels with bounded waits (see tma.cuh).
 cudaError_t select_device_status(int* status, int clear);
+// Points select.cu's kernels on the current device at the host mirror of the status word.
+cudaError_t select_status_attach(int* mirror);
 
 constexpr int kNumSMs = 148;  // B200
 

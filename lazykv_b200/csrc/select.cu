@@ -413,16 +413,8 @@ constexpr int kClusterMax = 16;
 constexpr int kClusterMaxPer = 4096;   // keys per CTA (in shared memory)
 constexpr int kHistHeads = 64;         // heads the first-pass histograms are kept for
 constexpr size_t kHistBytes = (size_t)kHistHeads * 256 * sizeof(uint32_t);  // at the workspace's start
-// Per-head state of the single-launch select, after the first-pass counters: [0] arrivals, [1]
-// departures, the head's counts of passes 0..3 (256 each) -- all zero between calls -- then, per CTA
-// (up to kCoopMaxP), its count of keys above the prefix of the earlier passes and the suffix sums of
-// its histogram of the current pass (256 x uint16), rewritten every pass. The keys of the two-launch
-// path follow.
-constexpr int kCoopMaxP = 64;
-constexpr int kCoopHeads = 16;
-constexpr int kCoopHeadWords = 2 + 4 * 256 + kCoopMaxP + kCoopMaxP * 128;
-constexpr size_t kCoopBytes = (size_t)kCoopHeads * kCoopHeadWords * sizeof(uint32_t);
-constexpr size_t kKeysOffset = kHistBytes + kCoopBytes;
+constexpr size_t kFailOffset = kHistBytes;       // per-head failure words of the TMA-scored selection
+constexpr size_t kKeysOffset = kHistBytes + 256;  // then the keys (64-bit, or 32-bit in the TMA-scored selection)
 
 __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(const uint64_t* __restrict__ keys_all, uint32_t* __restrict__ hist0,
                                                                      int n_cand, int k, int first_block, int n_passes, int per,
@@ -576,29 +568,46 @@ int launch_topk_cluster(int h, cudaStream_t st, const uint64_t* keys, uint32_t* 
   return LKV_OK;
 }
 
-// ---- single-launch selection: scoring and a per-head radix select with in-kernel barriers --------
+// ---- selection in two launches: TMA scoring, then a cluster select per head ------------------------
 //
-// For a bf16 query and bf16 metadata at head_dim 64, block-id order. The grid is h x P CTAs
-// (P = ceil(n_cand / 256)), launched only when the host finds that all of them fit on the GPU at
-// once, and not before its predecessor in the stream has finished, so every CTA is resident. CTA c
-// of head j brings its 256 candidates' kmax and kmin rows in by tensor-map TMA (boxes of 128 rows,
-// 128-byte swizzle: chunk x of row r at chunk x ^ (r & 7), conflict-free per-row reads), and thread t
-// scores row t as quest_score_kernel does (same order and roundings), keeping the 64-bit key in a
-// register. Each radix pass of the select is global per head: every CTA adds its histogram of the
-// current digit to the head's counts in the workspace, a per-head barrier (an arrival counter;
-// waits bounded, a timeout recorded in the status word) completes the pass, and every CTA reads the
-// counts and picks the same digit. The compaction publishes each CTA's (above, tied) totals behind
-// one more barrier; a CTA's output offset and its share of the tied keys (lowest ids first) come
-// from the totals of the CTAs before it, as in topk_cluster_kernel. The head's last CTA to leave
-// returns its counters and counts to zero.
+// For a bf16 query and bf16 metadata at head_dim 64, block-id order, at most 16,384 candidates per
+// head and 64 heads.
+//
+// quest_score_tma_kernel: P x h CTAs (P = ceil(n_cand / 256)); CTA c of head j scores its 256
+// candidates. Their kmax and kmin rows arrive by tensor-map TMA (boxes of 128 rows, 128-byte
+// swizzle: chunk x of row r at chunk x ^ (r & 7)), and thread t scores row t as quest_score_kernel
+// does (same channel order and roundings). The orderable 32-bit bound goes to the head's keys in the
+// workspace and its top 8 bits to the head's first-pass histogram (one global atomic per non-empty
+// bin and CTA).
+//
+// quest_pick_kernel, launched right behind it (programmatic dependent launch: its CTAs are placed
+// while the scoring runs and wait for its completion): a cluster of 8 CTAs x 1024 threads per head,
+// one key per thread (two above 8,192 candidates). Every CTA picks the first digit from the
+// histogram; each further radix pass counts the CTA's keys in shared memory, a cluster barrier
+// completes the pass and every CTA sums the cluster's histograms through distributed shared memory.
+// The compaction exchanges each CTA's (above, tied) totals the same way: a CTA's output offset and
+// its share of the tied keys (lowest ids first) come from the totals of the CTAs before it, so the
+// ids come out in ascending block-id order; each warp ORs its 32 candidates' bits into the bitmap.
+// Rank 0 returns the histogram and the head's failure word to zero for the next call.
+//
+// No CTA waits for a CTA outside its cluster, and a cluster's CTAs are scheduled together. The
+// scoring's TMA waits are bounded: a wait that runs out records LKV_DEV_WAIT_TIMEOUT (status word
+// and host mirror) and sets the head's failure word, and the select then writes the failure's
+// poison for the head (every listed id -1 and an empty bitmap, so that an exact pass over the
+// complement still covers every candidate). A CTA whose wait ran out waits (bounded) for its copy
+// before it exits, so no bulk copy lands in the shared memory of a finished CTA.
 
-constexpr int kCoopThreads = 256;
-constexpr int kCoopBoxRows = 128;
-constexpr int kCoopBox = kCoopBoxRows * 128;               // bytes of one box: 128 rows of 64 bf16
-constexpr size_t kCoopSmem = 1024 + 4 * (size_t)kCoopBox;  // kmax boxes 0, 1 then kmin boxes 0, 1
-constexpr uint32_t kCoopWaitIters = 1u << 22;              // tries of a barrier wait (each sleeps ~64 ns)
+constexpr int kScThreads = 256;
+constexpr int kScBoxRows = 128;
+constexpr int kScBox = kScBoxRows * 128;              // bytes of one box: 128 rows of 64 bf16
+constexpr size_t kScSmem = 1024 + 4 * (size_t)kScBox;  // kmax boxes 0, 1 then kmin boxes 0, 1
+constexpr int kPkThreads = 1024;
+constexpr int kPkCluster = 8;
+constexpr int kPkMaxKpt = 2;
+constexpr int kPkMaxCand = kPkCluster * kPkThreads * kPkMaxKpt;  // 16,384
+constexpr uint32_t kScExitWaitIters = 1u << 22;      // bound of the wait for a copy still in flight at exit
 
-struct CoopParams {
+struct SelParams {
   CUtensorMap tmax, tmin;  // [h][rows][64] bf16, box {64, 128, 1}, 128-byte swizzle
   const __nv_bfloat16* q;
   int n_cand, k, first_block, n_passes, bound_mode;
@@ -607,7 +616,11 @@ struct CoopParams {
   uint32_t* bitmap;
   int bitmap_words;
   float* out_bound;
-  uint32_t* state;  // [h][kCoopHeadWords], zero on entry, left zero
+  uint32_t* hist0;  // [h][256] first-pass counts: zero on entry, left zero
+  uint32_t* fail;   // [h] set when a scoring wait ran out: zero on entry, left zero
+  uint32_t* keys;   // [h][n_cand] orderable bounds
+  uint32_t wait_iters;  // bound of each TMA wait (tries)
+  int stall;            // test hook: 1 = wait on a barrier that nothing completes before scoring
 };
 
 // One 3-D tile load global -> this CTA's shared memory under an L2 cache policy. No multicast.
@@ -616,34 +629,6 @@ __device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* m
                    smem_u32(dst)),
                "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(pol)
                : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Arrive at the head's barrier and wait (bounded) for `target` arrivals; every thread of the CTA
-// calls it. Returns false when the wait ran out (recorded in the status word).
-__device__ bool coop_barrier(uint32_t* arrive, uint32_t target, int* sh_ok) {
-  __syncthreads();  // the CTA's global writes before the barrier are issued
-  if (threadIdx.x == 0) {
-    __threadfence();
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(arrive) : "memory");
-    bool ok = false;
-    for (uint32_t i = 0; i < kCoopWaitIters; ++i) {
-      if (ld_acquire_gpu(arrive) >= target) {
-        ok = true;
-        break;
-      }
-      if (i >= 256) __nanosleep(64);
-    }
-    if (!ok) atomicCAS(&g_device_status, 0, LKV_DEV_WAIT_TIMEOUT);
-    *sh_ok = ok ? 1 : 0;
-  }
-  __syncthreads();
-  return *sh_ok != 0;
 }
 
 // row_bound's bf16 x bf16 arithmetic on a swizzled box row (d = 64: 8 chunks of 16 bytes).
@@ -696,221 +681,223 @@ __device__ __forceinline__ float row_bound_swz(const unsigned char* bmax, const 
 }
 
 template <int G>
-__global__ void __launch_bounds__(kCoopThreads) quest_select_coop_kernel(const __grid_constant__ CoopParams cp) {
-  const int j = blockIdx.y, c = blockIdx.x, P = gridDim.x;
+__global__ void __launch_bounds__(kScThreads) quest_score_tma_kernel(const __grid_constant__ SelParams sp) {
+  const int j = blockIdx.y, c = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31;
-  extern __shared__ unsigned char csmem_raw[];
-  unsigned char* tiles = csmem_raw + ((1024 - (smem_u32(csmem_raw) & 1023)) & 1023);
+  extern __shared__ unsigned char sc_raw[];
+  unsigned char* tiles = sc_raw + ((1024 - (smem_u32(sc_raw) & 1023)) & 1023);
   __shared__ __align__(16) float qs[2 * qpad<G>() * 64];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ uint32_t hist[256], gh[256];
-  __shared__ uint32_t low[kCoopMaxP][2];
-  __shared__ uint32_t warp_sums[32];
-  __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total, sh_pos0, sh_eq0;
-  __shared__ int sh_ok, sh_last;
+  __shared__ __align__(8) uint64_t bar[2];  // [0] the tiles; [1] the test hook's (never completed)
+  __shared__ uint32_t hist[256];
 
-  uint32_t* st = cp.state + (size_t)j * kCoopHeadWords;
-  uint32_t* arrive = st;
-  uint32_t* depart = st + 1;
-  uint32_t* counts = st + 2;                                                   // [pass][256]
-  uint32_t* above_g = st + 2 + 4 * 256;                                        // [P]
-  uint16_t* suf_g = reinterpret_cast<uint16_t*>(st + 2 + 4 * 256 + kCoopMaxP);  // [P][256]
-  const int n_cand = cp.n_cand;
-  const int lo = c * kCoopThreads;
-  const int cnt = min(kCoopThreads, n_cand - lo);
+  const int n_cand = sp.n_cand;
+  const int lo = c * kScThreads;
+  const int cnt = min(kScThreads, n_cand - lo);
   if (tid == 0) {
-    mbar_init(&bar, 1);
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
     fence_mbar_init();
   }
-  pdl_wait();  // no-op: this kernel is launched without the programmatic attribute (measured slower with it)
+  __syncthreads();
+  pdl_wait();  // the query, the metadata and the workspace are the predecessor's to finish with
+  pdl_release();  // the select's CTAs may be placed now (they wait for this grid's completion)
   if (tid == 0) {  // the bounds first: the query is staged while they are in flight
-    const int r0 = cp.first_block + lo;
-    mbar_arrive_expect_tx(&bar, 4u * kCoopBox);
+    const int r0 = sp.first_block + lo;
     const uint64_t pol = l2_evict_first_policy();  // the bounds are read once per call
-    tma_load_3d_hint(tiles, &cp.tmax, 0, r0, j, &bar, pol);
-    tma_load_3d_hint(tiles + kCoopBox, &cp.tmax, 0, r0 + kCoopBoxRows, j, &bar, pol);
-    tma_load_3d_hint(tiles + 2 * kCoopBox, &cp.tmin, 0, r0, j, &bar, pol);
-    tma_load_3d_hint(tiles + 3 * kCoopBox, &cp.tmin, 0, r0 + kCoopBoxRows, j, &bar, pol);
+    mbar_arrive_expect_tx(&bar[0], 4u * kScBox);
+    tma_load_3d_hint(tiles, &sp.tmax, 0, r0, j, &bar[0], pol);
+    tma_load_3d_hint(tiles + kScBox, &sp.tmax, 0, r0 + kScBoxRows, j, &bar[0], pol);
+    tma_load_3d_hint(tiles + 2 * kScBox, &sp.tmin, 0, r0, j, &bar[0], pol);
+    tma_load_3d_hint(tiles + 3 * kScBox, &sp.tmin, 0, r0 + kScBoxRows, j, &bar[0], pol);
   }
-  stage_query<__nv_bfloat16, G>(cp.q, j, 64, qs);
+  stage_query<__nv_bfloat16, G>(sp.q, j, 64, qs);
   hist[tid] = 0u;
-  // CTA 0 writes the head's bitmap: zero, or, when every candidate is taken (no barrier follows to
-  // order its stores before the other CTAs' bits), the candidates' bits.
-  const bool all_taken = cp.k >= n_cand;
-  if (c == 0 && cp.bitmap != nullptr)
-    for (int w = tid; w < cp.bitmap_words; w += blockDim.x) {
-      uint32_t v = 0u;
-      if (all_taken) {
-        const int64_t b0 = max((int64_t)cp.first_block, (int64_t)w * 32), b1 = min((int64_t)cp.first_block + n_cand, (int64_t)w * 32 + 32);
-        if (b0 < b1) v = (b1 - b0 == 32 ? 0xffffffffu : ((1u << (b1 - b0)) - 1u)) << (b0 - (int64_t)w * 32);
-      }
-      cp.bitmap[(int64_t)j * cp.bitmap_words + w] = v;
+  uint32_t got = 1u;
+  if (sp.stall && tid == 0) got = mbar_wait_n(&bar[1], 0, sp.wait_iters) ? 1u : 0u;  // test hook: runs out
+  if (got) got = mbar_wait_n(&bar[0], 0, sp.wait_iters) ? 1u : 0u;
+  const bool ok = __syncthreads_and((int)got) != 0;  // also the barrier of the staged query and the histogram
+
+  uint32_t key = 0u;
+  if (tid < cnt) {
+    if (ok) {
+      const int bx = tid / kScBoxRows, r = tid % kScBoxRows;
+      const float best = row_bound_swz<G>(tiles + bx * kScBox, tiles + (2 + bx) * kScBox, r, qs, sp.bound_mode);
+      key = orderable(best);
+      if (sp.out_bound != nullptr) sp.out_bound[(int64_t)j * n_cand + lo + tid] = best == 0.0f ? 0.0f : best;
     }
-  bool ok = __syncthreads_and(mbar_wait(&bar, 0)) != 0;  // also the barrier of the staged query
-
-  // ---- this thread's key ----
-  const bool have = tid < cnt;
-  uint32_t ob = 0;
-  if (have && ok) {
-    const int bx = tid / kCoopBoxRows, r = tid % kCoopBoxRows;
-    const float best = row_bound_swz<G>(tiles + bx * kCoopBox, tiles + (2 + bx) * kCoopBox, r, qs, cp.bound_mode);
-    ob = orderable(best);
-    if (cp.out_bound != nullptr) cp.out_bound[(int64_t)j * n_cand + lo + tid] = best == 0.0f ? 0.0f : best;
+    sp.keys[(int64_t)j * n_cand + lo + tid] = key;
   }
+  const uint32_t digit = tid < cnt ? key >> 24 : 256u;
+  const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+  if (digit < 256u && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+  __syncthreads();
+  if (hist[tid] != 0u) atomicAdd(&sp.hist0[(int64_t)j * 256 + tid], hist[tid]);
+  if (tid == 0 && !ok) {
+    atomicOr(&sp.fail[j], 1u);
+    mbar_wait_n(&bar[0], 0, kScExitWaitIters);  // the copy may still be landing: no exit before it does
+  }
+}
 
-  // ---- radix passes, global per head; the last one also yields the compaction offsets ----
-  // Each pass publishes this CTA's count of keys already above the prefix (from earlier passes) and
-  // the suffix sums of its histogram of the pass's digit, so that after the pass that fixes the
-  // k-th key no further barrier is needed: CTA c's offset is the lower CTAs' keys above the final
-  // prefix plus their share of the tied keys, read from what they published.
-  const int kk = cp.k < n_cand ? cp.k : n_cand;
+// The cluster barrier that only keeps shared memory alive: arrive without release semantics (no
+// data is published by it), so it does not wait for this CTA's global stores to complete.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\nbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
+// CTA c of the head's cluster owns whole bitmap words: words [w_c, w_{c+1}) of the words the
+// candidates span, 32 x KPT per CTA at most. Thread t holds block 32 * w_c + t (+ 1024 per further
+// key), a candidate when it lies in [first_block, first_block + n_cand); so a warp's 32 blocks are
+// exactly one bitmap word, which its lane 0 stores whole (no zeroing pass, no atomics), and the
+// CTAs' candidates follow one another in block order.
+template <int KPT>
+__global__ void __launch_bounds__(kPkThreads) quest_pick_kernel(const __grid_constant__ SelParams sp) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int c = (int)cluster.block_rank(), C = (int)cluster.num_blocks();
+  const int j = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
+  __shared__ uint32_t hist[2][256];  // this CTA's counts of the current pass (alternating buffers)
+  __shared__ uint32_t ghist[256];    // the cluster's totals (the first pass: the scoring's histogram)
+  __shared__ uint32_t counts[2];     // this CTA's (above, tied) totals
+  __shared__ uint32_t lower[kPkCluster][2];
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total, sh_pos0, sh_eq0;
+
+  const int n_cand = sp.n_cand, first = sp.first_block;
+  const int wf = first / 32, wl = (first + n_cand - 1) / 32;  // the words the candidates span
+  const int nw = wl - wf + 1;
+  const int w_lo = wf + (int)((int64_t)nw * c / C), w_hi = wf + (int)((int64_t)nw * (c + 1) / C);
+  const int W = sp.bitmap_words;
+  pdl_wait();  // the keys, the histogram and the failure word of the scoring
+  pdl_release();  // the attention's CTAs may be placed now (they wait for this grid's completion)
+  const bool failed = __ldcg(&sp.fail[j]) != 0u;
+  uint32_t keys[KPT];
+  bool have[KPT];
+#pragma unroll
+  for (int kp = 0; kp < KPT; ++kp) {
+    const int b = 32 * w_lo + kp * kPkThreads + tid;  // block id
+    have[kp] = b < 32 * w_hi && b >= first && b < first + n_cand;
+    keys[kp] = have[kp] ? __ldcg(sp.keys + (int64_t)j * n_cand + (b - first)) : 0u;
+  }
+  if (tid < 256) ghist[tid] = __ldcg(&sp.hist0[(int64_t)j * 256 + tid]);
+  const int kk = sp.k < n_cand ? sp.k : n_cand;
   if (tid == 0) {
     sh_remaining = (uint32_t)kk;
-    sh_bincount = 0;
+    sh_bincount = 0u;
   }
-  __shared__ uint32_t suf[257];
-  uint32_t prefix = 0, mask = 0, above = 0;
+  __syncthreads();
+  uint32_t prefix = 0u, mask = 0u;
   const bool all = kk >= n_cand;
   bool take_all = all;
-  uint32_t barriers = 0, d_last = 0;
-  for (int pass = 0; pass < cp.n_passes && !all; ++pass) {
+  for (int pass = 0; pass < sp.n_passes && !take_all; ++pass) {  // the same digits in every CTA of the cluster
     const int shift = 24 - 8 * pass;
-    const bool counted = have && (ob & mask) == prefix;
-    const uint32_t digit = counted ? ((ob >> shift) & 255u) : 256u;
-    const uint32_t peers = __match_any_sync(0xffffffffu, digit);
-    if (counted && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
-    __syncthreads();
-    // suffix sums of the histogram: suf[b] = keys of this CTA at digit >= b (suf[256] = 0)
-    {
-      const uint32_t v = hist[255 - tid];
-      const uint32_t incl = block_scan(v, warp_sums, &sh_total) + v;  // over reversed bins
-      suf[255 - tid] = incl;
-      if (tid == 0) suf[256] = 0u;
-      const uint32_t hv = hist[tid];
-      if (hv != 0u) atomicAdd(&counts[pass * 256 + tid], hv);
+    if (pass > 0) {
+      uint32_t* hp = hist[pass & 1];
+      if (tid < 256) hp[tid] = 0u;
+      __syncthreads();
+#pragma unroll
+      for (int kp = 0; kp < KPT; ++kp) {
+        const bool counted = have[kp] && (keys[kp] & mask) == prefix;
+        const uint32_t digit = counted ? ((keys[kp] >> shift) & 255u) : 256u;
+        const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+        if (counted && lane == __ffs(peers) - 1) atomicAdd(&hp[digit], __popc(peers));
+      }
+      cluster.sync();  // every CTA's counts of this pass are final
+      if (tid < 256) {
+        uint32_t v[kPkCluster];
+#pragma unroll
+        for (int r = 0; r < kPkCluster; ++r) v[r] = r < C ? *cluster.map_shared_rank(&hp[tid], r) : 0u;  // all in flight at once
+        uint32_t sum = 0;
+#pragma unroll
+        for (int r = 0; r < kPkCluster; ++r) sum += v[r];
+        ghist[tid] = sum;
+      }
+      __syncthreads();
     }
+    pick_digit(ghist, &sh_digit, &sh_remaining, &sh_bincount);
     __syncthreads();
-    suf_g[(size_t)c * 256 + tid] = (uint16_t)suf[tid];
-    if (tid == 0) above_g[c] = above;
-    ok = coop_barrier(arrive, ++barriers * (uint32_t)P, &sh_ok) && ok;
-    gh[tid] = __ldcg(&counts[pass * 256 + tid]);
-    hist[tid] = 0u;
-    __syncthreads();
-    pick_digit(gh, &sh_digit, &sh_remaining, &sh_bincount);
-    __syncthreads();
-    d_last = sh_digit;
-    prefix |= d_last << shift;
+    prefix |= sh_digit << shift;
     mask |= 255u << shift;
-    take_all = (sh_bincount == sh_remaining);
-    if (take_all || pass == cp.n_passes - 1) break;  // uniform: every CTA picked the same digit
-    above += suf[d_last + 1];
+    take_all = (sh_bincount == sh_remaining);  // uniform: every CTA summed the same counts
     __syncthreads();
   }
   const uint32_t need = take_all ? 0xffffffffu : sh_remaining;
 
-  // ---- compaction in candidate order across the head's CTAs ----
-  const bool gt = have && (all || (ob & mask) > prefix || (take_all && (ob & mask) == prefix));
-  const bool eq = have && !all && !take_all && (ob & mask) == prefix;
-  const uint32_t pre = block_scan((gt ? 1u : 0u) | ((eq ? 1u : 0u) << 16), warp_sums, &sh_total);
-  if (all) {
-    // every candidate is taken: offsets are c * 256
-    if (tid == 0) {
-      sh_pos0 = (uint32_t)lo;
-      sh_eq0 = 0u;
-    }
-  } else {
-    if (tid < c) {
-      const uint32_t ab = __ldcg(&above_g[tid]);
-      const uint32_t s0 = __ldcg(&suf_g[(size_t)tid * 256 + d_last]);
-      const uint32_t s1 = d_last < 255 ? __ldcg(&suf_g[(size_t)tid * 256 + d_last + 1]) : 0u;
-      low[tid][0] = ab + (take_all ? s0 : s1);  // keys above the final prefix (a taken bin counts whole)
-      low[tid][1] = take_all ? 0u : s0 - s1;     // keys at the final prefix (tied)
-    }
-    __syncthreads();
-    if (tid == 0) {
-      uint32_t eqb = 0, posb = 0;
-      for (int r = 0; r < c; ++r) {
-        const uint32_t take = eqb < need ? min(low[r][1], need - eqb) : 0u;
-        posb += low[r][0] + take;
-        eqb += low[r][1];
-      }
-      sh_pos0 = posb;
-      sh_eq0 = eqb;
-    }
+  // ---- compaction in candidate order across the cluster ----
+  uint32_t pre[KPT], run = 0u;
+  bool gt[KPT], eq[KPT];
+#pragma unroll
+  for (int kp = 0; kp < KPT; ++kp) {
+    const uint32_t km = keys[kp] & mask;
+    gt[kp] = have[kp] && (all || km > prefix || (take_all && km == prefix));
+    eq[kp] = have[kp] && !all && !take_all && km == prefix;
+    pre[kp] = run + block_scan((gt[kp] ? 1u : 0u) | ((eq[kp] ? 1u : 0u) << 16), warp_sums, &sh_total);  // <= 2,048 each: 16 bits
+    run += sh_total;
   }
-  __syncthreads();
-  pdl_release();  // every CTA of the grid is resident (all arrived): the attention may launch
-  const uint32_t gt_before = pre & 0xffffu, eq_before = pre >> 16;
-  const uint32_t room = sh_eq0 < need ? need - sh_eq0 : 0u;  // tied keys this CTA may still take
-  const bool take = gt || (eq && eq_before < room);
-  const uint32_t pos = sh_pos0 + gt_before + min(eq_before, room);
-  if (take && pos < (uint32_t)kk && ok) {
-    const int blk = cp.first_block + lo + tid;
-    cp.out_blocks[(int64_t)j * cp.out_ld + pos] = blk;
-    if (cp.bitmap != nullptr && !all_taken && blk / 32 < cp.bitmap_words) atomicOr(&cp.bitmap[(int64_t)j * cp.bitmap_words + blk / 32], 1u << (blk % 32));
+  if (tid == 0) {
+    counts[0] = run & 0xffffu;
+    counts[1] = run >> 16;
   }
-
-  // ---- the head's last CTA to leave zeroes its state ----
+  cluster.sync();  // every CTA's totals are published; every CTA has read the histogram
+  if (tid < C) {
+    lower[tid][0] = *cluster.map_shared_rank(&counts[0], tid);
+    lower[tid][1] = *cluster.map_shared_rank(&counts[1], tid);
+  }
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    sh_last = atomicAdd(depart, 1u) == (uint32_t)(P - 1);
+    uint32_t eqb = 0, posb = 0;
+    for (int r = 0; r < c; ++r) {
+      const uint32_t take = eqb < need ? min(lower[r][1], need - eqb) : 0u;
+      posb += lower[r][0] + take;
+      eqb += lower[r][1];
+    }
+    sh_pos0 = posb;
+    sh_eq0 = eqb;
   }
   __syncthreads();
-  if (sh_last) {
-    for (int w = tid; w < 2 + 4 * 256; w += blockDim.x) st[w] = 0u;
+  // Every exchange is done: from here on only global stores, then a barrier that keeps the shared
+  // memory alive for the other CTAs' reads above.
+  const uint32_t room = sh_eq0 < need ? need - sh_eq0 : 0u;  // tied keys this CTA may still take
+#pragma unroll
+  for (int kp = 0; kp < KPT; ++kp) {
+    const int b = 32 * w_lo + kp * kPkThreads + tid;
+    const uint32_t gt_before = pre[kp] & 0xffffu, eq_before = pre[kp] >> 16;
+    const uint32_t pos = sh_pos0 + gt_before + min(eq_before, room);
+    const bool take = !failed && (gt[kp] || (eq[kp] && eq_before < room)) && pos < (uint32_t)kk;
+    if (take) sp.out_blocks[(int64_t)j * sp.out_ld + pos] = b;
+    const uint32_t word = __ballot_sync(0xffffffffu, take);  // bit l: block 32 * (b / 32) + l
+    if (sp.bitmap != nullptr && lane == 0 && b < 32 * w_hi && b / 32 < W) sp.bitmap[(int64_t)j * W + b / 32] = word;
   }
+  if (sp.bitmap != nullptr) {  // the words outside the candidates' span: zero (first and last CTA)
+    if (c == 0)
+      for (int w = tid; w < min(wf, W); w += blockDim.x) sp.bitmap[(int64_t)j * W + w] = 0u;
+    if (c == C - 1)
+      for (int w = wl + 1 + tid; w < W; w += blockDim.x) sp.bitmap[(int64_t)j * W + w] = 0u;
+  }
+  if (failed) {  // a scoring wait ran out: every listed id -1 (the bitmap words above are empty)
+    const int p0 = (int)((int64_t)sp.k * c / C), p1 = (int)((int64_t)sp.k * (c + 1) / C);
+    for (int p = p0 + tid; p < p1; p += blockDim.x) sp.out_blocks[(int64_t)j * sp.out_ld + p] = -1;
+  }
+  if (c == 0 && tid < 256) sp.hist0[(int64_t)j * 256 + tid] = 0u;  // zero for the next call (every CTA read it before the barrier above)
+  cluster_sync_relaxed();  // no CTA leaves while another may still read its shared memory; every CTA read the failure word
+  if (c == 0 && tid == 0) sp.fail[j] = 0u;
 }
 
-// Whether the single-launch select takes this call (bf16 query and metadata, head_dim 64, block-id
-// order, at most 64 CTAs of 256 candidates per head and every CTA resident at once); fills its maps.
-template <int G>
-bool coop_fits(int h, int P) {
-  static int per_sm[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int& m = per_sm[dev & 63];
-  if (m == 0) {
-    auto kern = quest_select_coop_kernel<G>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCoopSmem);
-    int n = 0;
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kCoopThreads, kCoopSmem);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      n = -1;
-    }
-    m = n > 0 ? n : -1;
-  }
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  return m > 0 && (int64_t)m * sms >= (int64_t)h * P;
-}
-
-bool coop_plan(int g, int q_dtype, int meta_dtype, int h, int d, const void* kmin, const void* kmax, int64_t m_head, int first_block, int n_cand,
-               int order, CoopParams& cp) {
-  if (q_dtype != LKV_BF16 || meta_dtype != LKV_BF16 || d != 64 || order != LKV_ORDER_BLOCK || h > kCoopHeads) return false;
-  const int P = (n_cand + kCoopThreads - 1) / kCoopThreads;
-  if (P > kCoopMaxP || h > 65535) return false;
-  bool fits = false;
-  switch (g) {
-    case 1: fits = coop_fits<1>(h, P); break;
-    case 2: fits = coop_fits<2>(h, P); break;
-    case 4: fits = coop_fits<4>(h, P); break;
-    case 8: fits = coop_fits<8>(h, P); break;
-    default: return false;
-  }
-  if (!fits) return false;
+// Whether the TMA-scored select takes this call (bf16 query and metadata, head_dim 64, block-id
+// order, G in {1, 2, 4, 8}, at most kPkMaxCand candidates and kHistHeads heads); fills its maps.
+bool select_plan(int g, int q_dtype, int meta_dtype, int h, int d, const void* kmin, const void* kmax, int64_t m_head, int first_block,
+                 int n_cand, int order, SelParams& sp) {
+  if (q_dtype != LKV_BF16 || meta_dtype != LKV_BF16 || d != 64 || order != LKV_ORDER_BLOCK) return false;
+  if (g != 1 && g != 2 && g != 4 && g != 8) return false;
+  if (n_cand > kPkMaxCand || h > kHistHeads) return false;
+  const int nw = (first_block + n_cand - 1) / 32 - first_block / 32 + 1;  // bitmap words the candidates span
+  if ((nw + kPkCluster - 1) / kPkCluster > kPkMaxKpt * kPkThreads / 32) return false;
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return false;
   const cuuint64_t dims[3] = {64, (cuuint64_t)first_block + (cuuint64_t)n_cand, (cuuint64_t)h};
   const cuuint64_t strides[2] = {128, (cuuint64_t)m_head * 2};
-  const cuuint32_t box[3] = {64, kCoopBoxRows, 1};
+  const cuuint32_t box[3] = {64, kScBoxRows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   for (int i = 0; i < 2; ++i) {
-    CUresult r = enc(i == 0 ? &cp.tmax : &cp.tmin, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(i == 0 ? kmax : kmin), dims, strides, box,
+    CUresult r = enc(i == 0 ? &sp.tmax : &sp.tmin, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(i == 0 ? kmax : kmin), dims, strides, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return false;
@@ -918,18 +905,47 @@ bool coop_plan(int g, int q_dtype, int meta_dtype, int h, int d, const void* kmi
   return true;
 }
 
-int launch_coop(int g, const CoopParams& cp, int h, int P, cudaStream_t st) {
+// Test hooks (lkv_debug_set): the bound of the selection's TMA waits, and a one-shot stall.
+uint32_t g_sel_wait_iters = kMaxWaitIters;
+int g_sel_stall_next = 0;
+
+template <int G>
+cudaError_t launch_score_tma_g(const SelParams& sp, int h, cudaStream_t st) {
+  static bool attr_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(quest_score_tma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScSmem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev & 63] = true;
+  }
+  const int P = (sp.n_cand + kScThreads - 1) / kScThreads;
+  return launch_pdl(quest_score_tma_kernel<G>, dim3(P, h), dim3(kScThreads), kScSmem, st, 0, sp);
+}
+
+int launch_select(int g, const SelParams& sp, int h, cudaStream_t st) {
   cudaError_t e = cudaErrorInvalidValue;
-  const dim3 grid(P, h), block(kCoopThreads);
   switch (g) {
-    case 1: quest_select_coop_kernel<1><<<grid, block, kCoopSmem, st>>>(cp); break;
-    case 2: quest_select_coop_kernel<2><<<grid, block, kCoopSmem, st>>>(cp); break;
-    case 4: quest_select_coop_kernel<4><<<grid, block, kCoopSmem, st>>>(cp); break;
-    case 8: quest_select_coop_kernel<8><<<grid, block, kCoopSmem, st>>>(cp); break;
+    case 1: e = launch_score_tma_g<1>(sp, h, st); break;
+    case 2: e = launch_score_tma_g<2>(sp, h, st); break;
+    case 4: e = launch_score_tma_g<4>(sp, h, st); break;
+    case 8: e = launch_score_tma_g<8>(sp, h, st); break;
     default: return fail(LKV_ERR_ARG, "lkv_quest_topk: query group %d not in {1,2,4,8}", g);
   }
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk(single launch, %d x %d CTAs): %s", P, h, cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_quest_topk(score, %d heads): %s", h, cudaGetErrorString(e));
+  }
+  // The select: 8-CTA clusters, one per head (a portable cluster size: always schedulable); each
+  // CTA takes ceil(words / 8) bitmap words, 32 blocks a word, 1,024 blocks a key per thread.
+  const int nw = (sp.first_block + sp.n_cand - 1) / 32 - sp.first_block / 32 + 1;
+  const int kpt = (nw + kPkCluster - 1) / kPkCluster > kPkThreads / 32 ? 2 : 1;
+  e = kpt == 1 ? launch_pdl(quest_pick_kernel<1>, dim3(kPkCluster, h), dim3(kPkThreads), 0, st, kPkCluster, sp)
+               : launch_pdl(quest_pick_kernel<2>, dim3(kPkCluster, h), dim3(kPkThreads), 0, st, kPkCluster, sp);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_quest_topk(select, %d heads): %s", h, cudaGetErrorString(e));
+  }
   return LKV_OK;
 }
 
@@ -976,11 +992,26 @@ int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void
 
 namespace lkv {
 cudaError_t select_device_status(int* status, int clear) { return tu_device_status(status, clear); }
+cudaError_t select_status_attach(int* mirror) { return tu_status_attach(mirror); }
 }  // namespace lkv
 
 using namespace lkv;
 
 extern "C" {
+
+int lkv_debug_set(int key, int64_t value) {
+  switch (key) {
+    case LKV_DEBUG_SELECT_WAIT_ITERS:
+      if (value < 1 || value > (int64_t)kMaxWaitIters) return fail(LKV_ERR_ARG, "lkv_debug_set: wait bound %lld outside [1, %u]", (long long)value, kMaxWaitIters);
+      g_sel_wait_iters = (uint32_t)value;
+      return LKV_OK;
+    case LKV_DEBUG_SELECT_STALL_NEXT:
+      g_sel_stall_next = value != 0;
+      return LKV_OK;
+    default:
+      return fail(LKV_ERR_ARG, "lkv_debug_set: unknown key %d", key);
+  }
+}
 
 size_t lkv_quest_topk_workspace(int h, int n_cand) {
   return kKeysOffset + (size_t)(h > 0 ? h : 0) * (size_t)(n_cand > 0 ? n_cand : 0) * sizeof(uint64_t);
@@ -1014,29 +1045,33 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   const int n_passes = bound_mode == LKV_BF16 ? 2 : 4;
   uint32_t* hist0 = static_cast<uint32_t*>(workspace);  // first-pass histograms, zero between calls
   uint64_t* keys = reinterpret_cast<uint64_t*>(static_cast<unsigned char*>(workspace) + kKeysOffset);
-  // Ascending block-id order with at most kHistHeads heads: the score kernel also counts the first
-  // radix pass, and a cluster per head finishes the select from the keys.
-  // bf16 query and metadata at head_dim 64, block-id order, when every CTA fits at once: one launch
-  // (scores and a per-head radix select with in-kernel barriers).
+  // bf16 query and metadata at head_dim 64, block-id order: TMA scoring, then a cluster per head
+  // selects (its launch placed while the scoring runs).
   {
-    CoopParams cp{};
-    const int g0 = hq / h;
-    if ((g0 == 1 || g0 == 2 || g0 == 4 || g0 == 8) && coop_plan(g0, q_dtype, meta_dtype, h, d, kmin, kmax, m_head, first_block, n_cand, order, cp)) {
-      cp.q = static_cast<const __nv_bfloat16*>(q);
-      cp.n_cand = n_cand;
-      cp.k = k;
-      cp.first_block = first_block;
-      cp.n_passes = bound_mode == LKV_BF16 ? 2 : 4;
-      cp.bound_mode = bound_mode;
-      cp.out_blocks = out_blocks;
-      cp.out_ld = out_ld;
-      cp.bitmap = bitmap;
-      cp.bitmap_words = bitmap_words;
-      cp.out_bound = out_bound;
-      cp.state = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(workspace) + kHistBytes);
-      return launch_coop(g0, cp, h, (n_cand + kCoopThreads - 1) / kCoopThreads, as_stream(stream));
+    SelParams sp{};
+    if (select_plan(g, q_dtype, meta_dtype, h, d, kmin, kmax, m_head, first_block, n_cand, order, sp)) {
+      sp.q = static_cast<const __nv_bfloat16*>(q);
+      sp.n_cand = n_cand;
+      sp.k = k;
+      sp.first_block = first_block;
+      sp.n_passes = n_passes;
+      sp.bound_mode = bound_mode;
+      sp.out_blocks = out_blocks;
+      sp.out_ld = out_ld;
+      sp.bitmap = bitmap;
+      sp.bitmap_words = bitmap_words;
+      sp.out_bound = out_bound;
+      sp.hist0 = hist0;
+      sp.fail = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(workspace) + kFailOffset);
+      sp.keys = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(workspace) + kKeysOffset);
+      sp.wait_iters = g_sel_wait_iters;
+      sp.stall = g_sel_stall_next;
+      g_sel_stall_next = 0;
+      return launch_select(g, sp, h, st);
     }
   }
+  // Ascending block-id order with at most kHistHeads heads: the score kernel also counts the first
+  // radix pass, and a cluster per head finishes the select from the keys.
   const bool cluster = order == LKV_ORDER_BLOCK && h <= kHistHeads && cluster_size_for(n_cand) > 0;
   if (!cluster && k > kMaxK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
   uint32_t* h0 = cluster ? hist0 : nullptr;
@@ -1147,10 +1182,18 @@ extern "C" int lkv_quest_topk_noalloc(const void* q, int q_dtype, int hq, int h,
                 h, n_cand, need, kNoAllocScratchBytes, (kNoAllocScratchBytes - kKeysOffset) / sizeof(uint64_t));
   void* scratch = nullptr;
   if (int rc = scratch_address(&scratch)) return rc;
-  // Nothing in the scratch has to start at zero: the score kernel writes every key the select
-  // kernel reads. Calls whose kernels overlap on the GPU share the array and race.
-  return lkv_quest_topk(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode, order,
-                        out_blocks, out_ld, out_bound, bitmap, bitmap_words, scratch, kNoAllocScratchBytes, stream);
+  // The array's first kKeysOffset bytes are the block-order paths' counters (the first-pass
+  // histograms and the TMA-scored selection's failure words), which must read zero on entry:
+  // __device__ storage starts zeroed and every complete call leaves them zero (a call whose bounded
+  // wait ran out too: its select resets them). A call that returns an error may have launched a
+  // kernel that counts without the one that zeroes, so they are cleared then (an asynchronous memset
+  // on the stream, which allocates nothing). The keys after the counters need no clearing: every key
+  // a select reads was written by the same call. Calls whose kernels overlap on the GPU share the
+  // array and race.
+  const int rc = lkv_quest_topk(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode, order,
+                                out_blocks, out_ld, out_bound, bitmap, bitmap_words, scratch, kNoAllocScratchBytes, stream);
+  if (rc != LKV_OK) cudaMemsetAsync(scratch, 0, kKeysOffset, as_stream(stream));
+  return rc;
 }
 
 // ---- ragged rows: many sequences' selections in two launches -------------------------------

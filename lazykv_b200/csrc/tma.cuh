@@ -10,6 +10,10 @@ namespace lkv {
 // that includes this header has its own and reads it with tu_device_status; lkv_device_status
 // combines those of attention.cu and select.cu.
 static __device__ int g_device_status = 0;
+// Optional mirror of the status word in pinned, mapped host memory (set by lkv_status_attach): a
+// kernel that records a status also sets it with a system-scope atomic, so the host can poll it
+// between steps without synchronising with the device.
+static __device__ int* g_status_host = nullptr;
 constexpr int LKV_DEV_WAIT_TIMEOUT = 1;       // an mbarrier wait ran out of iterations
 constexpr int LKV_DEV_LIST_OVERFLOW = 2;      // a CTA's item list would not fit its shared memory (host sizing error)
 constexpr uint32_t kMaxWaitIters = 1u << 21;  // tries; each may suspend up to kWaitHintNs
@@ -23,6 +27,17 @@ static inline cudaError_t tu_device_status(int* status, int clear) {
     e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
   }
   return e;
+}
+
+// Points this translation unit's kernels on the current device at the host mirror (device address
+// of a mapped host int, or null to detach).
+static inline cudaError_t tu_status_attach(int* mirror) { return cudaMemcpyToSymbol(g_status_host, &mirror, sizeof(mirror)); }
+
+// Records `code` in the status word (the first code wins) and in its host mirror, if attached.
+__device__ __forceinline__ void record_status(int code) {
+  atomicCAS(&g_device_status, 0, code);
+  int* h = g_status_host;
+  if (h != nullptr) atomicCAS_system(h, 0, code);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -70,11 +85,11 @@ __device__ __forceinline__ void tma_load_1d_hint(void* dst, const void* src, uin
 
 // Waits for the phase of `bar` with the given parity. Each try may suspend the thread (up to the
 // hint) until the phase completes, so a waiting warp does not spin on issue slots. Gives up after
-// kMaxWaitIters tries (about two seconds at most), records LKV_DEV_WAIT_TIMEOUT in g_device_status
-// and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// `iters` tries (kMaxWaitIters: about two seconds at most), records LKV_DEV_WAIT_TIMEOUT and
+// returns false.
+__device__ __forceinline__ bool mbar_wait_n(uint64_t* bar, uint32_t parity, uint32_t iters) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < kMaxWaitIters; ++i) {
+  for (uint32_t i = 0; i < iters; ++i) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -83,8 +98,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     if (done) return true;
   }
-  atomicCAS(&g_device_status, 0, LKV_DEV_WAIT_TIMEOUT);
+  record_status(LKV_DEV_WAIT_TIMEOUT);
   return false;
 }
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) { return mbar_wait_n(bar, parity, kMaxWaitIters); }
 
 }  // namespace lkv

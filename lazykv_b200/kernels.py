@@ -260,6 +260,47 @@ def device_status(clear: bool = True) -> int:
     return st.value
 
 
+_ATTACHED: set[int] = set()
+
+
+def status_attach(device: torch.device | int | None = None) -> None:
+    """Points the kernels on `device` at the host mirror of the status word (once per device)."""
+    idx = torch.cuda.current_device() if device is None else (device if isinstance(device, int) else device.index)
+    idx = torch.cuda.current_device() if idx is None else idx
+    if idx in _ATTACHED:
+        return
+    with torch.cuda.device(idx):
+        call("lkv_status_attach")
+    _ATTACHED.add(idx)
+
+
+def status_poll(clear: bool = True) -> int:
+    """The host mirror of the status word, read without synchronising (0 when nothing was recorded,
+    or when no device has been attached yet)."""
+    if not _ATTACHED:
+        return 0
+    st = ctypes.c_int(0)
+    call("lkv_status_poll", ctypes.byref(st), int(clear))
+    return st.value
+
+
+class DeviceWaitError(RuntimeError):
+    """A kernel's bounded wait ran out (or a CTA's list overflowed): its output was poisoned."""
+
+
+def raise_on_status(where: str) -> None:
+    """Raises DeviceWaitError when the status mirror holds a code (clearing it)."""
+    code = status_poll(clear=True)
+    if code:
+        what = {L.LKV_DEV_WAIT_TIMEOUT: "a bounded wait on the GPU ran out", L.LKV_DEV_LIST_OVERFLOW: "an attention CTA's item list overflowed"}
+        raise DeviceWaitError(f"{where}: {what.get(code, f'device status {code}')} (an earlier step's output is not valid)")
+
+
+def debug_set(key: int, value: int) -> None:
+    """Test hooks of the bounded waits (lkv_debug_set)."""
+    call("lkv_debug_set", key, value)
+
+
 def tier_admit(chosen: torch.Tensor, block_slot: torch.Tensor, slot_block: torch.Tensor, last_used: torch.Tensor, evicted_at: torch.Tensor | None,
                step: int, store: torch.Tensor, pool: torch.Tensor, miss_blk: torch.Tensor, miss_slot: torch.Tensor, n_miss: torch.Tensor,
                slots_out: torch.Tensor | None = None) -> None:

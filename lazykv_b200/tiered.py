@@ -70,44 +70,88 @@ class TieredLayer:
 
     def __init__(self, keys: torch.Tensor, values: torch.Tensor, k_blocks: int, block_size: int, capacity_tokens: int,
                  host: torch.Tensor | None = None, n_slots: int | None = None, quant: str | None = None, cold_placement: str = "host") -> None:
-        _, h, length, d = keys.shape
-        bs = block_size
-        n_blocks, tail = divmod(length, bs)
-        dev, dt = keys.device, keys.dtype
-        self._allocate(h, d, n_blocks, k_blocks, bs, capacity_tokens, dev, dt, host, n_slots, quant, cold_placement)
-        seed = min(self.n_slots, n_blocks - 1)
-        lo_seed = n_blocks - seed
-        torch.cuda.synchronize(dev)
+        """The layer at the boundary from its whole prompt KV [1, h, T, d] (lazykv/tiered.py:161-206):
+        every sealed block into the store with its metadata, the newest blocks seeded into slots,
+        the exact sink and the unsealed tail into the pool."""
+        self._open_boundary(keys, keys.shape[2], k_blocks, block_size, capacity_tokens, host, n_slots, quant, cold_placement)
+        self.close_boundary(keys, values)
+
+    @classmethod
+    def open_boundary(cls, like: torch.Tensor, total_tokens: int, k_blocks: int, block_size: int, capacity_tokens: int,
+                      host: torch.Tensor | None = None, n_slots: int | None = None, quant: str | None = None,
+                      cold_placement: str = "host") -> TieredLayer:
+        """A layer whose boundary is written while its prompt is still being prefilled: `ingest` after
+        each chunk stores the blocks that chunk completed, `close_boundary` after the last one. `like`
+        ([1, h, *, d]) gives the heads, head_dim, dtype and device; `total_tokens` is the prompt's length."""
+        self = cls.__new__(cls)
+        self._open_boundary(like, total_tokens, k_blocks, block_size, capacity_tokens, host, n_slots, quant, cold_placement)
+        return self
+
+    def _open_boundary(self, like: torch.Tensor, total_tokens: int, k_blocks: int, bs: int, capacity_tokens: int, host: torch.Tensor | None,
+                       n_slots: int | None, quant: str | None, cold_placement: str) -> None:
+        n_blocks = total_tokens // bs
+        self._allocate(like.shape[1], like.shape[3], n_blocks, k_blocks, bs, capacity_tokens, like.device, like.dtype, host, n_slots, quant,
+                       cold_placement)
+        self._bd_tokens, self._bd_blocks = total_tokens, n_blocks
+        self._bd_seed = min(self.n_slots, n_blocks - 1)  # the newest blocks start resident (tiered.py:176-180)
+        self._bd_done = 0  # blocks already in the store
+        self._bd_s = 0.0
+
+    def ingest(self, keys: torch.Tensor, values: torch.Tensor, upto: int) -> None:
+        """Stores the sealed blocks that tokens [0, upto) of keys/values [1, h, >= upto, d] complete
+        and that are not stored yet, in pieces of BOUNDARY_CHUNK blocks; a block among the seeded
+        newest ones also goes to its slot, holding what a fetch of it would (its dequantised record
+        under int8). Nothing here waits for the device."""
         t0 = time.perf_counter()
-        for c0 in range(0, n_blocks, BOUNDARY_CHUNK):
-            c1 = min(n_blocks, c0 + BOUNDARY_CHUNK)
-            chunk = torch.stack([keys[0, :, c0 * bs : c1 * bs], values[0, :, c0 * bs : c1 * bs]], dim=1)  # [h, 2, n*bs, d]
-            chunk = chunk.unflatten(2, (c1 - c0, bs)).permute(2, 0, 1, 3, 4).contiguous()  # [n, h, 2, bs, d]
-            if quant is None:
-                self.host[c0:c1].copy_(chunk, non_blocking=True)
-                if self.dev_store is not None:
-                    self.dev_store[c0:c1].copy_(chunk)
-                K.block_minmax(keys[0, :, c0 * bs : c1 * bs], bs, self.kmin[0], self.kmax[0], first_block=c0)
-                seeded = chunk
-            else:
-                # Records are written straight into the pinned store through its device view; the
-                # metadata and the seeded slots come from the dequantised keys (tiered.py:182-197).
-                seeded = torch.empty_like(chunk)
-                K.pack_int8(chunk, records=self.host_dev[c0:c1], kmin=self.kmin[0], kmax=self.kmax[0], first_block=c0, deq=seeded)
-                if self.dev_store is not None:
-                    self.dev_store[c0:c1].copy_(self.host_dev[c0:c1])
-            lo, hi = max(c0, lo_seed), c1
-            if lo < hi and seed > 0:
-                self.pool[1 + lo - lo_seed : 1 + hi - lo_seed] = seeded[lo - c0 : hi - c0]
-        # The sink never leaves VRAM and stays exact, even under int8 (tiered.py:200-202).
-        self.pool[0] = torch.stack([keys[0, :, :bs], values[0, :, :bs]], dim=1)
-        if tail:
-            self.pool[self.tail_slot, :, 0, :tail] = keys[0, :, n_blocks * bs : length]
-            self.pool[self.tail_slot, :, 1, :tail] = values[0, :, n_blocks * bs : length]
-        torch.cuda.synchronize(dev)
-        self.boundary_d2h_s = time.perf_counter() - t0
-        self.boundary_d2h_bytes = n_blocks * h * self.pair_bytes
-        self._finish(n_blocks, tail, seed)
+        bs = self.bs
+        last = min(upto // bs, self._bd_blocks)
+        first_seeded = self._bd_blocks - self._bd_seed
+        while self._bd_done < last:
+            c0 = self._bd_done
+            c1 = min(last, c0 + BOUNDARY_CHUNK)
+            span = slice(c0 * bs, c1 * bs)
+            pairs = torch.stack((keys[0, :, span], values[0, :, span]), dim=1).unflatten(2, (c1 - c0, bs)).permute(2, 0, 1, 3, 4).contiguous()
+            resident = self._store_blocks(pairs, c0)
+            a = max(c0, first_seeded)
+            if a < c1 and self._bd_seed > 0:
+                self.pool[1 + a - first_seeded : 1 + c1 - first_seeded] = resident[a - c0 :]
+            self._bd_done = c1
+        self._bd_s += time.perf_counter() - t0
+
+    def _store_blocks(self, pairs: torch.Tensor, c0: int) -> torch.Tensor:
+        """Blocks c0 .. c0 + n of `pairs` [n, h, 2, bs, d] into the store, with their min/max key
+        metadata; returns the values a slot holds for them. The int8 records are written straight
+        into the pinned store through its device view, and their metadata is taken over the
+        dequantised keys (tiered.py:182-197)."""
+        c1 = c0 + pairs.shape[0]
+        if self.quant is None:
+            self.host[c0:c1].copy_(pairs, non_blocking=True)
+            if self.dev_store is not None:
+                self.dev_store[c0:c1].copy_(pairs)
+            K.block_minmax(pairs[:, :, 0].transpose(0, 1), self.bs, self.kmin[0], self.kmax[0], first_block=c0)
+            return pairs
+        deq = torch.empty_like(pairs)
+        K.pack_int8(pairs, records=self.host_dev[c0:c1], kmin=self.kmin[0], kmax=self.kmax[0], first_block=c0, deq=deq)
+        if self.dev_store is not None:
+            self.dev_store[c0:c1].copy_(self.host_dev[c0:c1])
+        return deq
+
+    def close_boundary(self, keys: torch.Tensor, values: torch.Tensor) -> None:
+        """The boundary's end: any blocks not yet stored, the sink (which never leaves VRAM and stays
+        exact, even under int8: tiered.py:200-202), the unsealed tail into the current slot, and the
+        residency tables. Waits for the device once."""
+        self.ingest(keys, values, self._bd_tokens)
+        t0 = time.perf_counter()
+        bs, n_blocks = self.bs, self._bd_blocks
+        tail = self._bd_tokens - n_blocks * bs
+        for half, src in enumerate((keys, values)):
+            self.pool[0, :, half] = src[0, :, :bs]
+            if tail:
+                self.pool[self.tail_slot, :, half, :tail] = src[0, :, n_blocks * bs : self._bd_tokens]
+        torch.cuda.synchronize(self.pool.device)
+        self.boundary_d2h_s = self._bd_s + time.perf_counter() - t0
+        self.boundary_d2h_bytes = n_blocks * self.h * self.pair_bytes
+        self._finish(n_blocks, tail, self._bd_seed)
 
     @classmethod
     def from_store(cls, host: torch.Tensor, n_blocks: int, tail: torch.Tensor, k_blocks: int, block_size: int, capacity_tokens: int,
@@ -244,29 +288,29 @@ class TieredLayer:
 
     # -- writes (tiered.py:306-375) ---------------------------------------------------------------
 
-    def append(self, key: torch.Tensor, value: torch.Tensor, counters: TierCounters) -> None:
-        """Write one decode token; seal the current block first if it is full (lazily)."""
-        if self.fill == self.bs:
-            self._seal(counters)
-        t = self.pool[self.tail_slot]
-        t[:, 0, self.fill].copy_(key[0, :, 0])
-        t[:, 1, self.fill].copy_(value[0, :, 0])
-        self.fill += 1
-        self.length += 1
-
-    def extend(self, keys: torch.Tensor, values: torch.Tensor, counters: TierCounters) -> None:
-        """Write a multi-token forward's KV [1, h, T, d] as T appends would."""
-        n, i = keys.shape[2], 0
-        while i < n:
+    def _write_tokens(self, keys: torch.Tensor, values: torch.Tensor, counters: TierCounters) -> None:
+        """Tokens [1, h, T, d] into the current block, in spans that fit it. A full block is sealed
+        lazily, when the next token needs its space (tiered.py:306-334), so the block being filled
+        is always the pool's current slot."""
+        done, total = 0, keys.shape[2]
+        while done < total:
             if self.fill == self.bs:
                 self._seal(counters)
-            m = min(self.bs - self.fill, n - i)
-            t = self.pool[self.tail_slot]
-            t[:, 0, self.fill : self.fill + m].copy_(keys[0, :, i : i + m])
-            t[:, 1, self.fill : self.fill + m].copy_(values[0, :, i : i + m])
-            self.fill += m
-            self.length += m
-            i += m
+            span = min(self.bs - self.fill, total - done)
+            dst = self.pool[self.tail_slot, :, :, self.fill : self.fill + span]  # [h, 2, span, d]
+            for half, src in enumerate((keys, values)):
+                dst[:, half].copy_(src[0, :, done : done + span])
+            self.fill += span
+            self.length += span
+            done += span
+
+    def append(self, key: torch.Tensor, value: torch.Tensor, counters: TierCounters) -> None:
+        """One decode token's KV [1, h, 1, d]."""
+        self._write_tokens(key, value, counters)
+
+    def extend(self, keys: torch.Tensor, values: torch.Tensor, counters: TierCounters) -> None:
+        """A multi-token forward's KV [1, h, T, d], as T appends would write it."""
+        self._write_tokens(keys, values, counters)
 
     def dense_kv(self, keys: torch.Tensor, values: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, int]:
         """The layer's whole KV from the host store, then the tail and `keys`/`values` (bf16 tier)."""
@@ -465,6 +509,8 @@ class TieredCache(Cache):
             self.counters.boundary_d2h_s += layer.boundary_d2h_s
             self.counters.boundary_d2h_bytes += layer.boundary_d2h_bytes
         self.n_slots = next(iter(self.tiers.values())).n_slots
+        # The kernels' bounded waits report to a host-mapped status word, polled once per step.
+        K.status_attach(next(iter(self.tiers.values())).pool.device)
         self._mask_cache: dict[str, Any] = {}
         self._step = 0
         self._step_marks: list[torch.Tensor] = []  # device totals of fetched pairs at each step's end
@@ -503,6 +549,9 @@ class TieredCache(Cache):
             self._step = 0
 
     def _begin_step(self) -> None:
+        # A bounded wait that ran out on the device during an earlier step poisoned that step's
+        # selection; it surfaces here, without a device synchronisation.
+        K.raise_on_status("TieredCache")
         if self._step > 0:
             self._flush_step()
         self._step += 1

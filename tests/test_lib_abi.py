@@ -59,8 +59,8 @@ def test_invalid_arguments_return_a_status_and_a_message(lib) -> None:  # noqa: 
     assert rc == 2 and "null" in _lib.last_error()
     rc = lib.lkv_lse_merge(None, None, 0, 4, 64, None, 0, None, None)
     assert rc == 1
-    # first-pass counters (64 heads x 256), the single-launch select's per-head state (16 x 9,282 words), keys
-    assert lib.lkv_quest_topk_workspace(8, 8190) == 64 * 1024 + 16 * 9282 * 4 + 8 * 8190 * 8
+    # first-pass counters (64 heads x 256), the selection's failure words (64 heads), then the keys
+    assert lib.lkv_quest_topk_workspace(8, 8190) == 64 * 1024 + 256 + 8 * 8190 * 8
     assert lib.lkv_attention_workspace(8, 32, 64, 2048) > 0
     buf = ctypes.create_string_buffer(4)
     assert lib.lkv_last_error(buf, 4) > 3 and len(buf.value) == 3

@@ -26,7 +26,7 @@ def _case(seed: int, h: int, nb: int, hq: int, d: int, dtype: torch.dtype) -> tu
     return q, keys.amin(2).contiguous(), keys.amax(2).contiguous()
 
 
-def _run(entry: str, q, kmin, kmax, first: int, n_cand: int, k: int, mode: int):  # noqa: ANN001, ANN202
+def _run(entry: str, q, kmin, kmax, first: int, n_cand: int, k: int, mode: int, order: int = 0):  # noqa: ANN001, ANN202
     from lazykv_b200 import _lib
 
     h, _, d = kmin.shape
@@ -35,7 +35,7 @@ def _run(entry: str, q, kmin, kmax, first: int, n_cand: int, k: int, mode: int):
     words = (kmin.shape[1] + 31) // 32
     bitmap = torch.full((h, words), -1, dtype=torch.int32, device=DEV)
     common = (q.data_ptr(), _lib.dtype_code(q.dtype), q.shape[0], h, d, kmin.data_ptr(), kmax.data_ptr(), _lib.dtype_code(kmin.dtype),
-              kmin.stride(0), first, n_cand, k, mode, _lib.LKV_ORDER_BOUND, out.data_ptr(), k, bound.data_ptr(), bitmap.data_ptr(), words)
+              kmin.stride(0), first, n_cand, k, mode, order, out.data_ptr(), k, bound.data_ptr(), bitmap.data_ptr(), words)
     stream = torch.cuda.current_stream().cuda_stream
     if entry == "noalloc":
         before = torch.cuda.memory_stats().get("allocation.all.allocated", 0)
@@ -65,6 +65,23 @@ def test_noalloc_top_k_equals_the_workspace_entry_point_on_two_calls_in_a_row() 
     b = _run("workspace", q, kmin, kmax, 1, 598, 100, _lib.LKV_F32)
     for x, y in zip(a, b):
         assert np.array_equal(x, y)
+
+
+def test_noalloc_block_order_equals_the_workspace_entry_point() -> None:
+    """Ascending block-id order, both of its paths, each twice in a row and bit for bit: bf16 at
+    head_dim 64 (one launch, a thread-block cluster per head, no scratch) and bf16 at head_dim 128
+    (scores, then a cluster select that counts in the array's first-pass counters, which must read
+    zero on entry and which every complete call leaves zero)."""
+    from lazykv_b200 import _lib
+
+    _lib.lib()
+    for seed, d, nb, k in ((3, 64, 8192, 2046), (4, 64, 4100, 1000), (5, 128, 8192, 2046), (6, 128, 3000, 700)):
+        q, kmin, kmax = _case(seed, 8, nb, 32, d, torch.bfloat16)
+        a = _run("noalloc", q, kmin, kmax, 1, nb - 2, k, _lib.LKV_BF16, _lib.LKV_ORDER_BLOCK)
+        b = _run("workspace", q, kmin, kmax, 1, nb - 2, k, _lib.LKV_BF16, _lib.LKV_ORDER_BLOCK)
+        for x, y in zip(a, b):
+            assert np.array_equal(x, y), (seed, d)
+        assert (np.diff(a[0], axis=1) > 0).all()
 
 
 def test_noalloc_rejects_inputs_beyond_its_fixed_scratch() -> None:
