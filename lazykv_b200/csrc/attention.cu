@@ -1075,29 +1075,42 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     lb1 = cnt1 * (rp(1) + 1) / rp(2);
     n_b = (int)(lb1 - la1);
     if (n_a + n_b <= kStreamListCap) {
-      int64_t ord = before;
-#pragma unroll
-      for (int k = 0; k < kSetupWords; ++k) {
-        uint32_t b = bits[k];
-        if (ord + __popc(b) <= la1 || ord >= lb1) {
-          ord += __popc(b);
-          continue;
-        }
-        while (b != 0u) {
-          const int bit = __ffs(b) - 1;
-          b &= b - 1u;
-          if (ord >= la1 && ord < lb1) {
-            const int blk = 32 * (w0 + k) + bit;
-            int rrow = blk;
-            if (table != nullptr) {  // a table entry outside the store lists nothing
-              rrow = __ldg(table + blk);
-              if (rrow < 0 || rrow >= S1.n_rows) rrow = -1;
-            }
-            list[n_a + (ord - la1)] = S1.kind == SEG_RANGE_REC ? rrow : (rrow < S1.n_rows ? rrow : -1);
-          }
-          ++ord;
-        }
+      // The range's items in [la1, lb1) lie in a contiguous run of words. Each word's bits and first
+      // ordinal go to shared memory (the ring, idle until streaming starts); then warp w lists the
+      // run's words w, w + NW, ..., one lane per bit (its ordinal: the word's plus the set bits below it).
+      static_assert(kSetupWords == 1, "one word per thread in the warp-cooperative listing");
+      uint32_t* wbits = reinterpret_cast<uint32_t*>(ring);
+      int* word_ord = reinterpret_cast<int*>(ring) + kStreamThreads;
+      __shared__ int sh_wrun[2];
+      if (threadIdx.x == 0) {
+        sh_wrun[0] = kStreamThreads;
+        sh_wrun[1] = -1;
       }
+      wbits[threadIdx.x] = bits[0];
+      word_ord[threadIdx.x] = before;
+      __syncthreads();
+      if (before < lb1 && before + __popc(bits[0]) > la1) {  // this word holds items of the slice
+        atomicMin(&sh_wrun[0], (int)threadIdx.x);
+        atomicMax(&sh_wrun[1], (int)threadIdx.x);
+      }
+      __syncthreads();
+      const uint32_t below = (1u << lane) - 1u;
+      for (int t = sh_wrun[0] + warp; t <= sh_wrun[1]; t += NW) {
+        const uint32_t b = wbits[t];
+        if (!((b >> lane) & 1u)) continue;
+        const int64_t ord = word_ord[t] + __popc(b & below);
+        if (ord < la1 || ord >= lb1) continue;
+        const int blk = 32 * (S1.first_block / 32 + t) + lane;
+        int rrow = blk;
+        if (table != nullptr) {  // a table entry outside the store lists nothing
+          rrow = __ldg(table + blk);
+          if (rrow < 0 || rrow >= S1.n_rows) rrow = -1;
+        }
+        list[n_a + (ord - la1)] = S1.kind == SEG_RANGE_REC ? rrow : (rrow < S1.n_rows ? rrow : -1);
+      }
+      // The ring's words were written through the generic proxy; the tile copies that refill it go
+      // through the async proxy after the barrier that ends the set-up.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       if (hit < lb0) list[threadIdx.x] = hot_row;
       for (int64_t it = lb0 > la0 + kStreamThreads ? la0 + kStreamThreads + threadIdx.x : lb0; it < lb0; it += blockDim.x) {
         const int blk = __ldg(S0.blocks + (int64_t)j * S0.n_list + it);
@@ -1492,19 +1505,28 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   }
   __syncthreads();
 
-  // ---- fold the warps' parked states: one partial per set for this CTA ----
-  // Per (set, row), one warp: lane w reads warp w's maximum, the lanes agree on the maximum M and
-  // the sum L by shuffles, and lane w's weight 2^(m_w - M) goes to shared memory; then every thread
-  // folds one output element with those weights.
+  // ---- fold the warps' parked states into this CTA's partials ----
+  // Partials live set-major per row: set s of CTA ci at part[(2 * pbase + s * P + ci) * PART], so a
+  // head's set-0 partials are contiguous. When only the merged output is wanted (no per-set
+  // outputs), the CTA folds both sets into ONE partial (set 0): per row, lane l of one warp holds
+  // the maximum of warp (l % NW)'s state of set (l / NW); the lanes agree on the maximum M and the
+  // sum L by shuffles, the weights 2^(m - M) go to shared memory, and every thread folds output
+  // elements with them. Otherwise each set is folded on its own, one partial per set.
   const int64_t part_stride = C::PART;
   const int ci = rp(1), P = rp(2), pbase = rp(3);
-  float* mine = sp.part + (((int64_t)pbase + ci) * 2) * part_stride;
-  __shared__ float fold_w[2 * 8][NW > 32 ? NW : 32];  // [(set, row)][warp or partial] weights
-  static_assert(NW <= 32, "one lane per warp");
-  for (int pr = warp; pr < 2 * G; pr += NW) {
-    const int set = pr / G, r = pr % G;
-    const float* sl = park + (lane * 2 + set) * C::SLOT;
-    const float mw = (lane < NW && !sh_bad) ? sl[G * D + r] : -INFINITY;
+  const bool merge_sets = sp.seg_out == nullptr;
+  const int n_folds = merge_sets ? 1 : 2;  // partials this CTA writes
+  const int per_fold = merge_sets ? 2 * NW : NW;  // parked states per partial
+  auto mine = [&](int set) { return sp.part + ((int64_t)2 * pbase + (int64_t)set * P + ci) * part_stride; };
+  __shared__ float fold_w[2 * 8][2 * NW > 32 ? 2 * NW : 32];  // [(partial, row)][state] weights
+  static_assert(2 * NW <= 32, "one lane per parked state");
+  for (int pr = warp; pr < n_folds * G; pr += NW) {
+    const int f_set = pr / G, r = pr % G;
+    // lane -> (warp, set) of the parked state it weighs
+    const int sw = merge_sets ? lane % NW : lane, sset = merge_sets ? lane / NW : f_set;
+    const bool live = lane < per_fold && !sh_bad;
+    const float* sl = park + (sw * 2 + sset) * C::SLOT;
+    const float mw = live ? sl[G * D + r] : -INFINITY;
     float M = mw;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
@@ -1512,21 +1534,23 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     float L = f != 0.0f ? f * sl[G * D + G + r] : 0.0f;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    if (lane < NW) fold_w[pr][lane] = f;
+    if (lane < per_fold) fold_w[pr][lane] = f;
     if (lane == 0) {
-      mine[set * part_stride + G * D + r] = M;
-      mine[set * part_stride + G * D + G + r] = L;
+      mine(f_set)[G * D + r] = M;
+      mine(f_set)[G * D + G + r] = L;
     }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < 2 * G * D; e += blockDim.x) {
-    const int set = e / (G * D), r = (e / D) % G, c = e % D;
-    const float* wr = fold_w[set * G + r];
+  for (int e = threadIdx.x; e < n_folds * G * D; e += blockDim.x) {
+    const int f_set = e / (G * D), r = (e / D) % G, c = e % D;
+    const float* wr = fold_w[f_set * G + r];
     float O = 0.0f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w)
-      if (wr[w] != 0.0f) O = fmaf(park[(w * 2 + set) * C::SLOT + r * D + c], wr[w], O);  // a zero weight: the slot may be unset
-    mine[set * part_stride + r * D + c] = O;
+    for (int w = 0; w < per_fold; ++w) {
+      const int sw = merge_sets ? w % NW : w, sset = merge_sets ? w / NW : f_set;
+      if (wr[w] != 0.0f) O = fmaf(park[(sw * 2 + sset) * C::SLOT + r * D + c], wr[w], O);  // a zero weight: the slot may be unset
+    }
+    mine(f_set)[r * D + c] = O;
   }
   __threadfence();
   __syncthreads();
@@ -1536,12 +1560,12 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   __threadfence();
 
   // ---- the head's last CTA: fold its P partials per set into the outputs ----
-  // The head's partials are contiguous in the workspace: one bulk copy brings them into the idle
-  // ring (when they fit); per (set, row) a warp finds the maximum, the weights and the sum by
-  // shuffles (lanes over the partials); then every thread folds one output element.
-  const float* hp = sp.part + (int64_t)pbase * 2 * part_stride;
-  const int nset = p.n_segs;
-  const size_t head_bytes = (size_t)P * 2 * C::PART * sizeof(float);
+  // The head's partials of each folded set are contiguous in the workspace: one bulk copy brings
+  // them into the idle ring (when they fit); per (set, row) a warp finds the maximum, the weights
+  // and the sum by shuffles (lanes over the partials); then every thread folds one output element.
+  const float* hp = sp.part + (int64_t)2 * pbase * part_stride;  // set s, partial k at hp + (s * P + k) * PART
+  const int nset = merge_sets ? 1 : p.n_segs;
+  const size_t head_bytes = (size_t)nset * P * C::PART * sizeof(float);
   const bool bulk = head_bytes <= (size_t)C::RING;
   bool got = true;
   if (bulk && threadIdx.x == 0) {
@@ -1554,19 +1578,20 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   }
   if (bulk) got = __syncthreads_and(mbar_wait(&fold_bar, 0));
   const float* parts = bulk ? reinterpret_cast<const float*>(ring) : hp;
+  auto part_at = [&](int set, int k) { return parts + ((int64_t)set * P + k) * part_stride; };
   // The weights of up to 32 partials per (set, row) live in fold_w; more partials go through the
   // workspace one pass per row (P <= 32 covers kStreamCtasPerSm x SMs / h for h >= 5 on B200).
   __shared__ float setM[2 * 8], setL[2 * 8];
   if (P <= 32 && got) {
-    for (int pr = warp; pr < 2 * G; pr += NW) {
+    for (int pr = warp; pr < nset * G; pr += NW) {
       const int set = pr / G, r = pr % G;
-      const float mk = (lane < P && set < nset) ? (bulk ? parts[(lane * 2 + set) * part_stride + G * D + r] : __ldcg(parts + (lane * 2 + set) * part_stride + G * D + r)) : -INFINITY;
+      const float mk = lane < P ? (bulk ? part_at(set, lane)[G * D + r] : __ldcg(part_at(set, lane) + G * D + r)) : -INFINITY;
       float M = mk;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
       const float f = (M == -INFINITY || mk == -INFINITY) ? 0.0f : exp2f(mk - M);
       float L = 0.0f;
-      if (f != 0.0f) L = f * (bulk ? parts[(lane * 2 + set) * part_stride + G * D + G + r] : __ldcg(parts + (lane * 2 + set) * part_stride + G * D + G + r));
+      if (f != 0.0f) L = f * (bulk ? part_at(set, lane)[G * D + G + r] : __ldcg(part_at(set, lane) + G * D + G + r));
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
       if (lane < P) fold_w[pr][lane] = f;
@@ -1588,16 +1613,16 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
         const float* wr = fold_w[set * G + r];
 #pragma unroll 4
         for (int k = 0; k < P; ++k) {
-          const float* pk = parts + (k * 2 + set) * part_stride + r * D + c;
+          const float* pk = part_at(set, k) + r * D + c;
           O = fmaf(bulk ? *pk : __ldcg(pk), wr[k], O);
         }
         M = setM[set * G + r];
         L = setL[set * G + r];
       } else {  // more partials than a warp's lanes: straight from the workspace
-        for (int k = 0; k < P; ++k) M = fmaxf(M, __ldcg(hp + (k * 2 + set) * part_stride + G * D + r));
+        for (int k = 0; k < P; ++k) M = fmaxf(M, __ldcg(hp + ((int64_t)set * P + k) * part_stride + G * D + r));
         if (M != -INFINITY)
           for (int k = 0; k < P; ++k) {
-            const float* pk = hp + (k * 2 + set) * part_stride;
+            const float* pk = hp + ((int64_t)set * P + k) * part_stride;
             const float mk = __ldcg(pk + G * D + r);
             if (mk == -INFINITY) continue;
             const float f = exp2f(mk - M);
@@ -1812,7 +1837,10 @@ int launch_tma(const AttnParams& p, cudaStream_t st) {
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set & bit)) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // not left behind for a later launch check
+      return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
+    }
     attr_set |= bit;
   }
   k<<<dim3(p.n_splits_total, p.h), kThreads, C::SMEM, st>>>(p);
@@ -2011,12 +2039,18 @@ int launch_stream(const StreamParams& sp, cudaStream_t st) {
   if (!(attr_set & bit)) {  // both instances: a single sequence's and ragged rows'
     cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel<G, TO, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_stream_kernel<G, TO, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // not left behind for a later launch check
+      return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
+    }
     attr_set |= bit;
   }
   const dim3 grid = sp.sched != nullptr ? dim3(sp.per_head) : dim3(sp.per_head, sp.p.h);  // ragged: per_head holds the CTAs
   cudaError_t e = launch_pdl(k, grid, dim3(kStreamThreads), C::SMEM, st, 0, sp);
-  if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv attention: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv attention: %s", cudaGetErrorString(e));
+  }
   return launched("lkv attention");
 }
 
