@@ -56,6 +56,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--no-host-leg", action="store_true", help="skip the zero-copy (host cold tier) measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=N_LAYERS - DENSE, help="selecting layers (the metric runs all 14; fewer for profiling)")
+    p.add_argument("--queries", type=int, default=8, help="queries in each layer's ring: decode token s uses query s mod this")
+    p.add_argument("--drift", type=float, default=0.15, help="a ring query is a base query + drift x N(0,1) (0.15: a hit rate near 0.84, inside the 0.79-1.0 the reference measured with real models)")
     p.add_argument("--workload", choices=["metric", "ragged"], default="metric",
                    help="ragged: BASELINE config 3 instead of the metric (64 sequences of 4K-128K tokens, 6.25%% budget, one layer)")
     p.add_argument("--profile-calls", action="store_true",
@@ -149,9 +151,17 @@ class Layer:
     """One selecting layer's device state for one rank's shard of the context."""
 
 
+NEVER = -(2**40)  # "evicted at" of a block never evicted (the tier's convention)
+
+
 def build_layers(args: argparse.Namespace, rank: int, world: int, dev, keep_source: bool = False) -> tuple[list, dict]:
-    """Every selecting layer's device state for this rank's shard; with `keep_source`, each layer also
-    keeps its sealed blocks (L.kv, bf16 [blocks, h, 2, bs, d]) and its current block (L.cur)."""
+    """Every selecting layer's device state for this rank's shard, laid out as the tier keeps it:
+    int8 records of the sealed blocks (local ids) in HBM, the bf16 min/max key metadata, a slot pool
+    [K + 2, h, 2, bs, d] (slot 0 the exact sink on rank 0, slots 1..K the admitted blocks, slot K + 1
+    the current block on the last rank), the residency tables of the device admit, and a ring of
+    `args.queries` queries (a base query plus `args.drift` x N(0, 1), rounded to bf16: the queries of
+    successive decode steps, which select overlapping but different blocks). With `keep_source`, a
+    layer also keeps its sealed blocks (L.kv, bf16 [blocks, h, 2, bs, d]) and its current block (L.cur)."""
     import torch
 
     from lazykv_b200 import kernels as K
@@ -170,8 +180,10 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev, keep_sour
     if n_cand <= k_local:
         raise SystemExit(f"shard of {n_cand} candidates cannot select {k_local}")
     n_list = k_local + int(has_sink) + int(has_cur)
-    n_slots = n_list
+    sel_off = int(has_sink)
     scale = D**-0.5
+    n_q = max(1, getattr(args, "queries", 1))
+    drift = getattr(args, "drift", 0.5)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     layers = []
     torch.cuda.synchronize(dev)
@@ -184,34 +196,33 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev, keep_sour
         kv = kv.bfloat16()
         L.kmin = torch.empty((HKV, nblk, D), dtype=torch.bfloat16, device=dev)
         L.kmax = torch.empty_like(L.kmin)
-        L.deq = torch.empty_like(kv)
-        L.records = K.pack_int8(kv, kmin=L.kmin, kmax=L.kmax, deq=L.deq)  # [nblk, h, W], local block ids
-        L.q = torch.randn(HQ, D, device=dev, generator=g).bfloat16()
-        # Hot list [sink?, selected..., current?] (local block ids) and the bitmap of the cold pass.
+        L.records = K.pack_int8(kv, kmin=L.kmin, kmax=L.kmax)  # [nblk, h, W], local block ids
+        q_base = torch.randn(HQ, D, device=dev, generator=g)
+        L.q_ring = (q_base[None] + drift * torch.randn(n_q, HQ, D, device=dev, generator=g)).bfloat16()
+        L.q = L.q_ring[0]
+        # Hot list [sink slot?, admitted slots..., current slot?] and the bitmap of the cold pass.
         L.list = torch.zeros((HKV, n_list), dtype=torch.int32, device=dev)
+        if has_cur:
+            L.list[:, -1] = k_local + 1
+        L.chosen = torch.zeros((HKV, k_local), dtype=torch.int32, device=dev)  # the selection, local block ids ascending
         L.words = K.bitmap_words(nblk + 1)
         L.bitmap = torch.zeros((HKV, L.words), dtype=torch.int32, device=dev)
-        sel_off = int(has_sink)
-        if has_cur:
-            L.list[:, -1] = nblk  # local id of the current block
-        K.quest_topk(L.q, L.kmin, L.kmax, cand_lo - lo, n_cand, k_local, out_blocks=L.list[:, sel_off : sel_off + k_local], bitmap=L.bitmap,
-                     by_block=True)
-        # Steady-state residency: slot s holds the s-th listed block of each head.
-        L.pool = torch.zeros((n_slots, HKV, 2, BS, D), dtype=torch.bfloat16, device=dev)
-        L.slot_of = torch.zeros((HKV, nblk + 1), dtype=torch.int32, device=dev)
-        heads = torch.arange(HKV, device=dev)[:, None].expand(HKV, n_list)
-        slots = torch.arange(n_list, device=dev, dtype=torch.int32)[None].expand(HKV, n_list)
-        L.slot_of[heads, L.list.long()] = slots
-        ids = L.list.long().clamp(max=nblk - 1)
-        L.pool.view(n_slots, HKV, -1)[slots.long(), heads] = L.deq.view(nblk, HKV, -1)[ids, heads]
+        L.pool = torch.zeros((k_local + 2, HKV, 2, BS, D), dtype=torch.bfloat16, device=dev)
         if has_sink:
             L.pool[0] = kv[0]  # the sink stays exact
         if has_cur:
-            L.pool[n_slots - 1] = torch.randn(HKV, 2, BS, D, device=dev, generator=g).bfloat16()
+            L.pool[k_local + 1] = torch.randn(HKV, 2, BS, D, device=dev, generator=g).bfloat16()
+        # Residency tables (lazykv/tiered.py:281-288): nothing resident yet; the first step admits.
+        L.block_slot = torch.full((HKV, nblk), -1, dtype=torch.int32, device=dev)
+        L.slot_block = torch.full((HKV, k_local), -1, dtype=torch.int32, device=dev)
+        L.last_used = torch.full((HKV, k_local), -2, dtype=torch.int64, device=dev)
+        L.evicted_at = torch.full((HKV, nblk), NEVER, dtype=torch.int64, device=dev)
+        L.miss_blk = torch.zeros((HKV, k_local), dtype=torch.int32, device=dev)
+        L.miss_slot = torch.zeros((HKV, k_local), dtype=torch.int32, device=dev)
+        L.n_miss = torch.zeros((HKV,), dtype=torch.int32, device=dev)
         L.kv = kv if keep_source else None
-        L.cur = L.pool[n_slots - 1].clone() if keep_source and has_cur else None
+        L.cur = L.pool[k_local + 1].clone() if keep_source and has_cur else None
         del kv
-        L.deq = None
         if world == 1:
             L.out = torch.empty((HQ, D), dtype=torch.bfloat16, device=dev)
             L.lse = torch.empty((HQ,), dtype=torch.float32, device=dev)
@@ -226,14 +237,40 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev, keep_sour
         layers.append(L)
     torch.cuda.synchronize(dev)
     geo = dict(nb=nb, n_sealed=n_sealed, k_total=k_total, k_local=k_local, lo=lo, hi=hi, cand_lo=cand_lo, n_cand=n_cand, n_list=n_list,
-               sel_off=int(has_sink), scale=scale, has_cur=has_cur)
+               sel_off=sel_off, scale=scale, has_cur=has_cur, n_q=n_q)
     return layers, geo
 
 
-def layer_step(L, geo: dict, cold_store=None, events: list | None = None) -> None:
-    """One layer-step of the hot path (all launches on the current stream): score + top-K, then
-    the hot and cold passes and their merge in one attention launch plus its combine."""
+def select_call(L, geo: dict, r: int = 0) -> None:  # noqa: ANN001
+    """Quest bound + device top-K of query r (block order) into L.chosen, and the bitmap."""
     from lazykv_b200 import kernels as K
+
+    K.quest_topk(L.q_ring[r], L.kmin, L.kmax, geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["k_local"], out_blocks=L.chosen, bitmap=L.bitmap,
+                 by_block=True)
+
+
+def admit_call(L, geo: dict, step: int, cold_store=None) -> None:  # noqa: ANN001
+    """The device admit of L.chosen (lazykv/tiered.py:389-463: LRU victims, the misses fetched from
+    the store and dequantised into their slots); the admitted slots go to the hot list."""
+    from lazykv_b200 import kernels as K
+
+    so = geo["sel_off"]
+    K.tier_admit(L.chosen, L.block_slot, L.slot_block, L.last_used, L.evicted_at, step, L.records if cold_store is None else cold_store, L.pool,
+                 L.miss_blk, L.miss_slot, L.n_miss, slots_out=L.list[:, so : so + geo["k_local"]])
+
+
+def attention_call(L, geo: dict, r: int = 0, cold_store=None) -> None:  # noqa: ANN001
+    """Hot pass over the listed slots, cold pass over the bitmap's complement, merge: one launch."""
+    from lazykv_b200 import kernels as K
+
+    K.exact_attention(L.q_ring[r], L.pool, L.pool[:, :, 1], (HKV * 2 * BS * D, 2 * BS * D, D), L.list, BS, L.records if cold_store is None else cold_store,
+                      geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["scale"], BS, excluded=L.bitmap, out=L.out, lse=L.lse)
+
+
+def layer_step(L, geo: dict, r: int = 0, step: int = 1, cold_store=None, events: list | None = None) -> None:  # noqa: ANN001
+    """One layer-step of the hot path with query r (all launches on the current stream): score +
+    top-K, the device admit (and fetch of misses), then the hot and cold passes and their merge in
+    one attention launch."""
 
     def mark() -> None:
         if events is not None:
@@ -244,15 +281,15 @@ def layer_step(L, geo: dict, cold_store=None, events: list | None = None) -> Non
             events.append(e)
 
     mark()
-    K.quest_topk(L.q, L.kmin, L.kmax, geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["k_local"],
-                 out_blocks=L.list[:, geo["sel_off"] : geo["sel_off"] + geo["k_local"]], bitmap=L.bitmap, by_block=True)
+    select_call(L, geo, r)
     mark()
-    K.exact_attention(L.q, L.pool, L.pool[:, :, 1], (HKV * 2 * BS * D, 2 * BS * D, D), L.list, BS, L.records if cold_store is None else cold_store,
-                      geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["scale"], BS, excluded=L.bitmap, slot_of=L.slot_of, out=L.out, lse=L.lse)
+    admit_call(L, geo, step, cold_store)
+    mark()
+    attention_call(L, geo, r, cold_store)
     mark()
 
 
-LAUNCHES_PER_LAYER_STEP = 3  # the selection (TMA scoring, then a cluster select per head) and the attention (both passes; the head's last CTA folds)
+LAUNCHES_PER_LAYER_STEP = 4  # the selection (TMA scoring, then a cluster select per head), the admit (LRU and fetch of misses), the attention (both passes and their merge)
 
 
 def dequant_records(records, dtype):  # noqa: ANN001, ANN201
@@ -276,8 +313,8 @@ def dequant_records(records, dtype):  # noqa: ANN001, ANN201
     return torch.stack([k, v], dim=1).to(dtype).view(n, h, 2, BS, D)
 
 
-def shard_reference(L, geo: dict):  # noqa: ANN001, ANN201
-    """float64 (out [HQ, D], lse [HQ]) of this rank's shard of one layer, computed from the layer's
+def shard_reference(L, geo: dict, r: int = 0):  # noqa: ANN001, ANN201
+    """float64 (out [HQ, D], lse [HQ]) of this rank's shard of one layer for query r, from the layer's
     stores with torch on the device: the sink (exact, in the pool) on rank 0, every candidate block as
     its record dequantised to bf16 (what the hot slots and the cold pass both hold), and the current
     block (exact) on the last rank; softmax attention in float64. Independent of the kernels."""
@@ -290,11 +327,11 @@ def shard_reference(L, geo: dict):  # noqa: ANN001, ANN201
         parts.append(L.pool[0].unsqueeze(0))
     parts.append(deq)
     if geo["has_cur"]:
-        parts.append(L.pool[-1].unsqueeze(0))
+        parts.append(L.pool[geo["k_local"] + 1].unsqueeze(0))
     blocks = torch.cat(parts, dim=0).double()  # [m, h, 2, bs, d]
     keys = blocks[:, :, 0].permute(1, 0, 2, 3).reshape(HKV, -1, D)
     vals = blocks[:, :, 1].permute(1, 0, 2, 3).reshape(HKV, -1, D)
-    q = L.q.double().view(HKV, HQ // HKV, D)
+    q = L.q_ring[r].double().view(HKV, HQ // HKV, D)
     s = torch.einsum("hgd,htd->hgt", q, keys) * geo["scale"]
     m = s.amax(dim=-1, keepdim=True)
     p = torch.exp(s - m)
@@ -322,7 +359,10 @@ def parity_check(got, parts: list) -> dict:  # noqa: ANN001
 
 
 def profile_calls(args: argparse.Namespace) -> None:
-    """The kernel calls of one layer-step, each twice and eagerly, for a profiler to capture."""
+    """The kernel calls of one layer-step, each twice and eagerly, for a profiler to capture: the
+    selection, the admit (the first with misses), the hot pass alone, the cold pass alone and the
+    fused attention; then the codec and merge kernels at sizes above L2: pack and unpack of 4,096
+    blocks x 8 heads, block min/max over them, and an 8-part LSE merge."""
     import torch
 
     from lazykv_b200 import kernels as K
@@ -337,16 +377,34 @@ def profile_calls(args: argparse.Namespace) -> None:
     out = torch.empty((HQ, D), dtype=torch.float32, device=dev)
     lse = torch.empty((HQ,), dtype=torch.float32, device=dev)
     first = geo["cand_lo"] - geo["lo"]
+    r1 = 1 % geo["n_q"]
+    layer_step(L, geo, 0, 1)  # residency of query 0
     for _ in range(2):
-        K.quest_topk(L.q, L.kmin, L.kmax, first, geo["n_cand"], geo["k_local"],
-                     out_blocks=L.list[:, geo["sel_off"] : geo["sel_off"] + geo["k_local"]], bitmap=L.bitmap, by_block=True)
+        select_call(L, geo, r1)
+    for st in range(2):
+        admit_call(L, geo, 2 + st)  # query 1's misses, then all hits
     for _ in range(2):
-        K.hot_attention(L.q, L.pool, L.pool[:, :, 1], strides, L.list, BS, geo["scale"], BS, slot_of=L.slot_of, out=out, lse=lse)
+        K.hot_attention(L.q_ring[r1], L.pool, L.pool[:, :, 1], strides, L.list, BS, geo["scale"], BS, out=out, lse=lse)
     for _ in range(2):
-        K.cold_attention(L.q, L.records, BS, first, geo["n_cand"], geo["scale"], excluded=L.bitmap, out=out, lse=lse)
+        K.cold_attention(L.q_ring[r1], L.records, BS, first, geo["n_cand"], geo["scale"], excluded=L.bitmap, out=out, lse=lse)
     for _ in range(2):
-        K.exact_attention(L.q, L.pool, L.pool[:, :, 1], strides, L.list, BS, L.records, first, geo["n_cand"], geo["scale"], BS,
-                          excluded=L.bitmap, slot_of=L.slot_of, out=L.out, lse=L.lse)
+        attention_call(L, geo, r1)
+    torch.cuda.synchronize()
+    n = 4096
+    g = torch.Generator(device=dev).manual_seed(5)
+    pairs = torch.randn((n, HKV, 2, BS, D), device=dev, generator=g).bfloat16()
+    kmin = torch.empty((HKV, n, D), dtype=torch.bfloat16, device=dev)
+    kmax = torch.empty_like(kmin)
+    for _ in range(2):
+        rec = K.pack_int8(pairs, kmin=kmin, kmax=kmax)
+    for _ in range(2):
+        K.unpack_int8(rec.view(-1, rec.shape[-1]), BS, D, torch.bfloat16)
+    for _ in range(2):
+        K.block_minmax(pairs[:, :, 0].transpose(0, 1), BS, kmin, kmax)
+    outs = torch.randn((8, 4096, D), device=dev, generator=g)
+    lses = torch.randn((8, 4096), device=dev, generator=g)
+    for _ in range(2):
+        K.lse_merge(outs, lses, torch.bfloat16)
     torch.cuda.synchronize()
 
 
@@ -369,45 +427,58 @@ def run_ours(args: argparse.Namespace) -> None:
         build()
     if world > 1:
         dist.barrier()
-    from lazykv_b200 import kernels as K0
-
-    K0.status_attach(dev)
-    layers, geo = build_layers(args, rank, world, dev)
-    n_steps, n_warm = args.steps, args.warmup
-    finals = [torch.empty((HQ, D), dtype=torch.bfloat16, device=dev) for _ in layers]
-
     from lazykv_b200 import kernels as K
 
-    def step(cold: str = "device") -> None:
+    K.status_attach(dev)
+    layers, geo = build_layers(args, rank, world, dev)
+    n_steps, n_warm = args.steps, args.warmup
+    R = geo["n_q"]
+    finals = [torch.empty((HQ, D), dtype=torch.bfloat16, device=dev) for _ in layers]
+
+    def token(r: int, step_no: int, cold_of=None) -> None:
+        """One decode token with query r of the ring: every selecting layer's hot path (and, at N > 1,
+        the all-gather of the layer's partials and their merge on every rank)."""
         for i, L in enumerate(layers):
-            layer_step(L, geo, None if cold == "device" else L.records_host)
+            layer_step(L, geo, r, step_no, None if cold_of is None else cold_of(L))
             if world > 1:
                 L.packed.exchange()
                 L.packed.merge(torch.bfloat16, out=finals[i])
 
-    # Warm-up (also compiles nothing: the library is prebuilt) and graph capture of one step (the
-    # NCCL all-gathers are captured too at N > 1; the graph is released before the process group).
-    for _ in range(n_warm):
-        step()
+    # Warm-up: the first token admits every selected block of query 0; then the ring of queries.
+    step_no = 0
+    for w in range(max(n_warm, R)):
+        step_no += 1
+        token(w % R, step_no)
     torch.cuda.synchronize()
-    graph = None
-    if True:
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            step()
-        torch.cuda.current_stream().wait_stream(s)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        for _ in range(n_warm):
-            graph.replay()
-        torch.cuda.synchronize()
+
+    # One CUDA graph per query of the ring, each a whole decode token (the NCCL all-gathers are
+    # captured too at N > 1; the graphs are released before the process group). A graph's admit step
+    # number is fixed at capture, so the LRU clock cycles with the ring.
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        token(0, step_no + 1)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graphs = []
+    for r in range(R):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph):
+            token(r, step_no + 1 + r)
+        graphs.append(gph)
+    ring_pos = [0]
+
+    def run() -> None:
+        graphs[ring_pos[0] % R].replay()
+        ring_pos[0] += 1
+
+    for _ in range(max(n_warm, R)):
+        run()
+    torch.cuda.synchronize()
 
     def soak(fn, seconds: float) -> None:
         # About `seconds` of back-to-back replays; the count is fixed from a short calibration and
-        # agreed across ranks (the graph holds collectives at N > 1, so every rank replays alike).
+        # agreed across ranks (the graphs hold collectives at N > 1, so every rank replays alike).
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for _ in range(5):
@@ -440,7 +511,6 @@ def run_ours(args: argparse.Namespace) -> None:
 
     # Clocks: nvidia-smi samples every 100 ms, so the sampler runs over a window of back-to-back
     # replays (about half a second on either side) that contains the timed region.
-    run = graph.replay if graph is not None else step
     with Clocks(local) as clocks:
         clocks.wait_first_sample(2.0)
         soak(run, 0.5)
@@ -451,39 +521,57 @@ def run_ours(args: argparse.Namespace) -> None:
     us_layer = ms_step * 1e3 / n_sel
     tokens_per_s = 1e3 / ms_step
 
-    # Per-kernel durations: each kernel group (selection: score + select; attention) captured alone
-    # over every layer in its own CUDA graph and replayed back to back, timed with CUDA events on
-    # the replaying stream, per layer-step (the local part at N > 1: no exchange).
-    names = ["select", "attention"]
+    # Per-kernel durations: each kernel group captured alone over every layer, one graph per query of
+    # the ring, replayed in turn and timed with CUDA events on the replaying stream, per layer-step
+    # (the local part at N > 1: no exchange). The admit is the difference between selection + admit
+    # and the selection alone.
+    def group_us(body) -> float:
+        gs = []
+        for r in range(R):
+            body(r, step_no + 1 + r)
+            torch.cuda.synchronize()
+            gk = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gk):
+                body(r, step_no + 1 + r)
+            gs.append(gk)
+        pos = [0]
 
-    def sel_only() -> None:
+        def rep() -> None:
+            gs[pos[0] % R].replay()
+            pos[0] += 1
+
+        for _ in range(R):
+            rep()
+        reps = max(5 * R, n_steps)
+        us = timed(rep, reps) / reps * 1e3 / len(layers)  # max over ranks at N > 1
+        del gs
+        return us
+
+    sel_us = group_us(lambda r, st: [select_call(L, geo, r) for L in layers])
+    sel_admit_us = group_us(lambda r, st: [(select_call(L, geo, r), admit_call(L, geo, st)) for L in layers])
+    attn_us = group_us(lambda r, st: [attention_call(L, geo, r) for L in layers])
+    kernel_us = {"select": sel_us, "admit": max(0.0, sel_admit_us - sel_us), "attention": attn_us}
+
+    # Residency churn over the ring (eager, after the timing): the share of selected (block, head)
+    # pairs already resident, and the bytes the admit's fetch moves per layer-step.
+    misses = torch.zeros((), dtype=torch.int64, device=dev)
+    for r in range(R):
+        step_no += 1
         for L in layers:
-            K.quest_topk(L.q, L.kmin, L.kmax, geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["k_local"],
-                         out_blocks=L.list[:, geo["sel_off"] : geo["sel_off"] + geo["k_local"]], bitmap=L.bitmap, by_block=True)
-
-    def attn_only() -> None:
-        for L in layers:
-            K.exact_attention(L.q, L.pool, L.pool[:, :, 1], (HKV * 2 * BS * D, 2 * BS * D, D), L.list, BS, L.records, geo["cand_lo"] - geo["lo"],
-                              geo["n_cand"], geo["scale"], BS, excluded=L.bitmap, slot_of=L.slot_of, out=L.out, lse=L.lse)
-
-    kernel_us = {}
-    for n, fn in zip(names, (sel_only, attn_only)):
-        fn()
-        torch.cuda.synchronize()
-        g_k = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_k):
-            fn()
-        for _ in range(3):
-            g_k.replay()
-        reps = max(5, n_steps)
-        kernel_us[n] = timed(g_k.replay, reps) / reps * 1e3 / len(layers)  # max over ranks at N > 1
-        del g_k
-
-    # Correctness of what was timed: layer 0's merged output (the last replay's) against a float64
-    # restatement over every rank's shard, gathered to every rank; and the status word of the
-    # kernels' bounded waits (host mirror, then the device word).
+            select_call(L, geo, r)
+            admit_call(L, geo, step_no)
+            misses += L.n_miss.sum()
     torch.cuda.synchronize()
-    ref_o, ref_l = shard_reference(layers[0], geo)
+    miss_pairs = float(misses.item()) / (R * len(layers))
+    hit_rate = 1.0 - miss_pairs / (HKV * geo["k_local"])
+
+    # Correctness of what was timed: a fresh token (query 0), layer 0's merged output against a
+    # float64 restatement over every rank's shard, gathered to every rank; and the status word of the
+    # kernels' bounded waits (host mirror, then the device word).
+    step_no += 1
+    token(0, step_no)
+    torch.cuda.synchronize()
+    ref_o, ref_l = shard_reference(layers[0], geo, 0)
     if world > 1:
         packed = torch.cat([ref_o, ref_l[:, None]], dim=1).contiguous()
         allp = torch.empty((world, *packed.shape), dtype=packed.dtype, device=dev)
@@ -502,6 +590,7 @@ def run_ours(args: argparse.Namespace) -> None:
         parity["ok"] = parity["ok"] and not bad
     parity["device_status"] = status
     parity["ok"] = parity["ok"] and status == 0
+    parity["query"] = 0
     del ref_o, ref_l, parts
 
     peaks = load_peaks()
@@ -512,35 +601,46 @@ def run_ours(args: argparse.Namespace) -> None:
     bytes_hot = hot_blocks * HKV * 2 * BS * D * 2
     rec_w = K.packed_pair_bytes(BS, D)
     bytes_cold = cold_blocks * HKV * rec_w
+    bytes_fetch = int(miss_pairs * (rec_w + 2 * BS * D * 2))  # a miss: its record read, its slot written
     algo = {"select": bytes_meta, "attention": bytes_hot + bytes_cold}
     dominant = max(("select", "attention"), key=lambda n: kernel_us[n])
     achieved = algo[dominant] / (kernel_us[dominant] * 1e-6) / 1e9
-    layer_bytes = bytes_meta + bytes_hot + bytes_cold
+    layer_bytes = bytes_meta + bytes_hot + bytes_cold + bytes_fetch
 
-    # End to end through the public API with host buffers: per step, every layer's query comes
-    # from pinned host memory and its output goes back to pinned host memory.
-    q_host = [torch.empty((HQ, D), dtype=torch.bfloat16).pin_memory() for _ in layers]
-    o_host = [torch.empty((HQ, D), dtype=torch.bfloat16).pin_memory() for _ in layers]
-    for qh, L in zip(q_host, layers):
-        qh.copy_(L.q.cpu())
+    # End to end. At N = 1 through the drop-in API, as a model calls it each decode step: for every
+    # layer the new token's KV goes to ExactTieredCache.update (the tier appends it; a full block is
+    # sealed, packed and its metadata written), and for every selecting layer ExactTieredCache.decode
+    # runs the hot path (selection, admit, exact attention) on a query copied from pinned host memory,
+    # whose output is copied back to pinned host memory. At N > 1, the sharded kernels' path above,
+    # eager, with the same host copies.
+    if world == 1:
+        e2e = run_e2e_api(args, geo, layers, dev, timed)
+    else:
+        q_host = torch.stack([L.q_ring for L in layers], dim=1).cpu().pin_memory()  # [R, layers, HQ, D]
+        o_host = torch.empty((len(layers), HQ, D), dtype=torch.bfloat16).pin_memory()
+        e_pos = [0]
 
-    def e2e_step() -> None:
-        for i, L in enumerate(layers):
-            L.q.copy_(q_host[i], non_blocking=True)
-            layer_step(L, geo)
-            src = L.out if world == 1 else finals[i]
-            if world > 1:
+        def e2e_step() -> None:
+            r = e_pos[0] % R
+            e_pos[0] += 1
+            for i, L in enumerate(layers):
+                L.q_ring[r].copy_(q_host[r, i], non_blocking=True)
+                layer_step(L, geo, r, 10**9 + e_pos[0])
                 L.packed.exchange()
                 L.packed.merge(torch.bfloat16, out=finals[i])
-            o_host[i].copy_(src, non_blocking=True)
+                o_host[i].copy_(finals[i], non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    e2e_ms = timed(e2e_step, max(3, n_steps // 2)) / max(3, n_steps // 2)
+        for _ in range(2):
+            e2e_step()
+        n_e = max(3, n_steps // 2)
+        e2e_ms = timed(e2e_step, n_e) / n_e
+        e2e = {"value": round(1e3 / e2e_ms, 3), "unit": "tokens/s", "h2d_bytes_per_step": n_sel * HQ * D * 2,
+               "d2h_bytes_per_step": n_sel * HQ * D * 2,
+               "path": "lazykv_b200.kernels (C ABI) per layer with the NCCL all-gather and merge, eager, host q in / host out"}
 
     result = {
         "metric": METRIC,
-        "value": round(tokens_per_s * (1 if world == 1 else 1), 3),
+        "value": round(tokens_per_s, 3),
         "unit": "tokens/s",
         "n_gpus": world,
         "steps": n_steps,
@@ -551,29 +651,30 @@ def run_ours(args: argparse.Namespace) -> None:
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) K/V with key offsets, random queries; no weights involved)",
-        "config": {"workload": "tiered decode hot path, Llama-3.2-1B attention (32q/8kv/d64), 131072-token context, bs 16, 25% budget (K=2046), 14 selecting layers, int8 cold tier in HBM",
-                   "ctx": args.ctx, "block_size": BS, "k_blocks": geo["k_total"], "selecting_layers": n_sel, "batch": 1,
+        "data": f"synthetic (seeded N(0,1) K/V with key offsets; per layer a ring of {R} queries, base + {args.drift} x N(0,1); no weights involved)",
+        "config": {"workload": "tiered decode hot path, Llama-3.2-1B attention (32q/8kv/d64), 131072-token context, bs 16, 25% budget (K=2046), 14 selecting layers, int8 cold tier in HBM, device admit with a fresh query every step",
+                   "ctx": args.ctx, "block_size": BS, "k_blocks": geo["k_total"], "selecting_layers": n_sel, "batch": 1, "queries_in_ring": R,
                    "cold_placement": "device", "l2": "inputs larger than L2 (~2.8 GB read per step)", "parallelism": f"context-sharded x{world}",
-                   "timing": "CUDA graph of one step (NCCL all-gathers captured at N > 1), CUDA events, max over ranks"},
+                   "timing": "one CUDA graph per decode token (select, admit, attention per layer; NCCL all-gathers captured at N > 1), CUDA events, max over ranks"},
         "kernel_us": {k: round(v, 3) for k, v in kernel_us.items()},
+        "residency": {"hit_rate": round(hit_rate, 4), "fetched_pairs_per_layer_step": round(miss_pairs, 1), "fetch_bytes_per_layer_step": bytes_fetch},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "traffic": attention_traffic() if dominant == "attention" and args.ctx == 131072 and world == 1 else None,
                      "traffic_source": "not measured by this run: dram__bytes_read.sum + dram__bytes_write.sum of one attention launch at this workload from the ncu capture committed in profiles/attn_stream_ctx128k.md (the build profiled there)",
                      "peak_source": peaks["source"],
                      "algorithmic_bytes": algo[dominant]},
-        "layer_step_roofline": {"algorithmic_bytes": layer_bytes, "us": round(us_layer, 3),
+        "layer_step_roofline": {"algorithmic_bytes": layer_bytes, "of_which_fetch": bytes_fetch, "us": round(us_layer, 3),
                                 "achieved_gbs": round(layer_bytes / (us_layer * 1e-6) / 1e9, 1),
                                 "frac": round(layer_bytes / (us_layer * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)},
-        "e2e": {"value": round(1e3 / e2e_ms, 3), "unit": "tokens/s", "h2d_bytes_per_step": n_sel * HQ * D * 2,
-                "d2h_bytes_per_step": n_sel * HQ * D * 2, "path": "lazykv_b200.kernels (C ABI) per layer, eager, host q in / host out"},
+        "e2e": e2e,
         "gpu_launches": n_steps * n_sel * (LAUNCHES_PER_LAYER_STEP + (1 if world > 1 else 0)),  # + the merge kernel at N > 1 (NCCL's own kernels not counted)
         "clocks": clocks.summary(),
         "parity": parity,
     }
 
-    # Zero-copy leg: the same step with the cold records in pinned host memory.
+    # Zero-copy leg: the same step with the cold records in pinned host memory (the admit's fetch
+    # and the cold pass read them over the link).
     if world == 1 and not args.no_host_leg:
         from lazykv_b200.pinned import device_view, pinned_empty
 
@@ -583,35 +684,121 @@ def run_ours(args: argparse.Namespace) -> None:
             L.records_host_cpu = h
             L.records_host = device_view(h)
         torch.cuda.synchronize()
-        for _ in range(2):
-            step("host")
+        host_of = lambda L: L.records_host  # noqa: E731
+        for r in range(2):
+            step_no += 1
+            token(r % R, step_no, host_of)
         hs = max(2, n_steps // 4)
-        hms = timed(lambda: step("host"), hs) / hs
+        h_pos = [0]
+
+        def host_token() -> None:
+            h_pos[0] += 1
+            token(h_pos[0] % R, step_no + h_pos[0], host_of)
+
+        hms = timed(host_token, hs) / hs
         cold_us = []
         for L in layers[:4]:
             ev: list = []
-            layer_step(L, geo, L.records_host, ev)
+            layer_step(L, geo, 0, step_no + 10**6, L.records_host, ev)
             torch.cuda.synchronize()
-            cold_us.append(ev[1].elapsed_time(ev[2]) * 1e3)
+            cold_us.append(ev[2].elapsed_time(ev[3]) * 1e3)
         cu = statistics.median(cold_us)
+        link = measure_link_gbs(dev)
         result["host_cold_tier"] = {"value": round(1e3 / hms, 3), "unit": "tokens/s", "us_per_layer_step": round(hms * 1e3 / n_sel, 1),
                                     "attention_us": round(cu, 1), "link_gbs": round(bytes_cold / (cu * 1e-6) / 1e9, 2),
-                                    "link_peak_gbs": 55.5, "link_peak_source": "pinned H2D copy measured on this pool's B200 hosts (PCIe 5 x16)"}
+                                    "link_peak_gbs": link, "link_peak_source": "measured by this run: pinned host -> device copy of 1 GiB, best of 5, CUDA events"}
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, budget_s=12.0)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
-        # The graph holds NCCL work: every reference to it (the graph and its bound replay) goes
-        # before the process group does, or the group's destruction waits for it for good.
+        # The graphs hold NCCL work: every reference to them (the graphs and the replay closure) goes
+        # before the process group does, or the group's destruction waits for them for good.
         import gc
 
-        del run, graph
+        del run, graphs
         gc.collect()
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
+
+
+def measure_link_gbs(dev) -> float:  # noqa: ANN001
+    """Host-link bandwidth of this box: a 1 GiB copy from pinned host memory to the device, best of 5."""
+    import torch
+
+    src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        b.synchronize()
+        best = max(best, (1 << 30) / (a.elapsed_time(b) * 1e-3) / 1e9)
+    del src, dst
+    return round(best, 2)
+
+
+def run_e2e_api(args: argparse.Namespace, geo: dict, layers: list, dev, timed) -> dict:  # noqa: ANN001
+    """End to end through the drop-in API at N = 1: an ExactTieredCache over 14 int8 tiers of a
+    131,071-token prompt (seeded like the bench's layers), stepped one decode token at a time with
+    the calls a model makes: update() for every layer's new KV, decode() for every selecting layer,
+    with the queries from pinned host memory and the outputs copied back to it."""
+    import torch
+
+    from lazykv_b200.cache import FullGPUCache
+    from lazykv_b200.exact import ExactTieredCache
+    from lazykv_b200.tiered import TieredLayer
+
+    R = geo["n_q"]
+    n_sel = len(layers)
+    n_e = max(3, args.steps // 2)
+    prompt = args.ctx - 1  # the first decode token completes the current block: the metric geometry
+    cap = args.ctx + 4 * (n_e + 8) + 64
+    g = torch.Generator(device=dev).manual_seed(4321)
+    tiers = {}
+    for i in range(n_sel):
+        off = torch.randn(1, HKV, 1, D, device=dev, generator=g) * 0.5**0.5
+        keys = (torch.randn(1, HKV, prompt, D, device=dev, generator=g) + off).bfloat16()
+        values = torch.randn(1, HKV, prompt, D, device=dev, generator=g).bfloat16()
+        tiers[DENSE + i] = TieredLayer(keys, values, geo["k_total"], BS, cap, quant="int8", cold_placement="device")
+        del keys, values
+    full = FullGPUCache(DENSE + n_sel, cap)
+    cache = ExactTieredCache(full, geo["k_total"], BS, cap, dense_layers=DENSE, quant="int8", fetch="gather", tiers=tiers)
+    q_host = torch.stack([L.q_ring for L in layers], dim=1).cpu().pin_memory()  # [R, layers, HQ, D]
+    kv_host = torch.randn((R, DENSE + n_sel, 2, 1, HKV, 1, D), generator=torch.Generator().manual_seed(7)).bfloat16().pin_memory()
+    o_host = torch.empty((n_sel, HQ, D), dtype=torch.bfloat16).pin_memory()
+    q_dev = torch.empty((1, HQ, 1, D), dtype=torch.bfloat16, device=dev)
+    kv_dev = torch.empty((2, 1, HKV, 1, D), dtype=torch.bfloat16, device=dev)
+    scale = D**-0.5
+    pos = [0]
+
+    def e2e_step() -> None:
+        r = pos[0] % R
+        pos[0] += 1
+        for layer in range(DENSE + n_sel):
+            kv_dev.copy_(kv_host[r, layer], non_blocking=True)
+            cache.update(kv_dev[0], kv_dev[1], layer)
+            if layer >= DENSE:
+                q_dev.copy_(q_host[r, layer - DENSE].view(1, HQ, 1, D), non_blocking=True)
+                out = cache.decode(layer, q_dev, kv_dev[0], kv_dev[1], scale)
+                o_host[layer - DENSE].copy_(out.view(HQ, D), non_blocking=True)
+
+    for _ in range(2 + R):
+        e2e_step()
+    e2e_ms = timed(e2e_step, n_e) / n_e
+    cache.close()
+    h2d = (DENSE + n_sel) * 2 * HKV * D * 2 + n_sel * HQ * D * 2
+    d2h = n_sel * HQ * D * 2
+    value = round(1e3 / e2e_ms, 3)
+    del cache, tiers, full
+    torch.cuda.empty_cache()
+    return {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "ExactTieredCache.update (every layer) + ExactTieredCache.decode (every selecting layer): the drop-in API a model's "
+                    "attention hook calls, eager, host q and KV in / host out; int8 tier with the cold store in HBM"}
 
 
 # ---------------------------------------------------------------------------------------------

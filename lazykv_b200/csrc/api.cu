@@ -3,6 +3,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace lkv {
@@ -30,6 +32,78 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
       cudaGetLastError();
   }
   return fn;
+}
+
+// ---- tensor maps, encoded once per distinct set of arguments ------------------------------------
+//
+// cuTensorMapEncodeTiled is a pure function of its arguments (the address, sizes, strides, box and
+// modes), so a map encoded once can be reused by every later launch over the same buffer: an eager
+// decode loop that calls the kernels with the same stores every step then pays the encoding once.
+// A fixed table of the most recent distinct argument sets, replaced round-robin, under a mutex.
+
+namespace {
+
+struct MapKey {
+  CUtensorMapDataType dt;
+  cuuint32_t rank;
+  void* base;
+  cuuint64_t dims[5];
+  cuuint64_t strides[4];
+  cuuint32_t box[5];
+  cuuint32_t estr[5];
+  CUtensorMapInterleave il;
+  CUtensorMapSwizzle sw;
+  CUtensorMapL2promotion l2;
+  CUtensorMapFloatOOBfill oob;
+};
+
+constexpr int kMapCacheSize = 512;
+struct MapEntry {
+  bool used;
+  MapKey key;
+  CUtensorMap map;
+};
+MapEntry g_maps[kMapCacheSize];
+int g_map_next = 0;
+std::mutex g_map_mu;
+
+}  // namespace
+
+CUresult encode_tiled(CUtensorMap* out, CUtensorMapDataType dt, cuuint32_t rank, void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                      const cuuint32_t* box, const cuuint32_t* estr, CUtensorMapInterleave il, CUtensorMapSwizzle sw, CUtensorMapL2promotion l2,
+                      CUtensorMapFloatOOBfill oob) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr || rank < 1 || rank > 5) return CUDA_ERROR_NOT_SUPPORTED;
+  MapKey key;
+  memset(&key, 0, sizeof(key));  // padding and unused dimensions compare equal
+  key.dt = dt;
+  key.rank = rank;
+  key.base = base;
+  for (cuuint32_t i = 0; i < rank; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+    key.estr[i] = estr[i];
+    if (i + 1 < rank) key.strides[i] = strides[i];
+  }
+  key.il = il;
+  key.sw = sw;
+  key.l2 = l2;
+  key.oob = oob;
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  for (int i = 0; i < kMapCacheSize; ++i)
+    if (g_maps[i].used && memcmp(&g_maps[i].key, &key, sizeof(key)) == 0) {
+      *out = g_maps[i].map;
+      return CUDA_SUCCESS;
+    }
+  const CUresult r = enc(out, dt, rank, base, dims, strides, box, estr, il, sw, l2, oob);
+  if (r == CUDA_SUCCESS) {
+    MapEntry& e = g_maps[g_map_next];
+    g_map_next = (g_map_next + 1) % kMapCacheSize;
+    e.used = true;
+    e.key = key;
+    e.map = *out;
+  }
+  return r;
 }
 
 int launched(const char* what) {

@@ -1962,7 +1962,7 @@ bool make_kv_maps(const Seg& S, int h, CUtensorMap* tk, CUtensorMap* tv, int* he
   const cuuint32_t box[4] = {64, 16, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   for (int i = 0; i < 2; ++i) {
-    CUresult r = enc(i == 0 ? tk : tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(i == 0 ? S.k_base : S.v_base), dims, strides, box,
+    CUresult r = encode_tiled(i == 0 ? tk : tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(i == 0 ? S.k_base : S.v_base), dims, strides, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return false;

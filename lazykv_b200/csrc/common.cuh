@@ -21,6 +21,10 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 // The driver's cuTensorMapEncodeTiled (null when the driver does not provide it).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+// cuTensorMapEncodeTiled through a cache of recently encoded argument sets (same arguments, same map).
+CUresult encode_tiled(CUtensorMap* out, CUtensorMapDataType dt, cuuint32_t rank, void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                      const cuuint32_t* box, const cuuint32_t* estr, CUtensorMapInterleave il, CUtensorMapSwizzle sw, CUtensorMapL2promotion l2,
+                      CUtensorMapFloatOOBfill oob);
 // The status word of select.cu's kernels with bounded waits (see tma.cuh).
 cudaError_t select_device_status(int* status, int clear);
 // Points select.cu's kernels on the current device at the host mirror of the status word.

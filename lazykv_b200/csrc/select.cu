@@ -897,7 +897,7 @@ bool select_plan(int g, int q_dtype, int meta_dtype, int h, int d, const void* k
   const cuuint32_t box[3] = {64, kScBoxRows, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   for (int i = 0; i < 2; ++i) {
-    CUresult r = enc(i == 0 ? &sp.tmax : &sp.tmin, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(i == 0 ? kmax : kmin), dims, strides, box,
+    CUresult r = encode_tiled(i == 0 ? &sp.tmax : &sp.tmin, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(i == 0 ? kmax : kmin), dims, strides, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return false;

@@ -152,6 +152,127 @@ __global__ void __launch_bounds__(kAdmitThreads) admit_kernel(const int32_t* __r
   if (threadIdx.x == 0) n_miss[j] = (int)min(sh_nmiss, (uint32_t)n_free);
 }
 
+// admit_kernel with the head's tables staged in shared memory: the chosen ids, each chosen block's
+// current slot (one gather of block_slot), slot_block and last_used are read once, every phase
+// works on the staged copies, and the changes go back at the end (block_slot and evicted_at by
+// single stores). Same rule, same victims in the same order, same tables afterwards. Used when the
+// staged tables fit in shared memory.
+__global__ void __launch_bounds__(kAdmitThreads) admit_staged_kernel(const int32_t* __restrict__ chosen, int k, int64_t chosen_ld,
+                                                                      int32_t* __restrict__ block_slot, int cap, int32_t* __restrict__ slot_block,
+                                                                      int64_t* __restrict__ last_used, int n_slots, int64_t* __restrict__ evicted_at,
+                                                                      int64_t step, int32_t* __restrict__ miss_blk, int32_t* __restrict__ miss_slot,
+                                                                      int32_t* __restrict__ n_miss, int32_t* __restrict__ slots_out, int64_t slots_ld) {
+  extern __shared__ uint64_t keys[];  // [P] LRU keys, then lu_s [n_slots] int64, ch_s [k], cs_s [k], sb_s [n_slots] int32, kept [n_slots]
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sh_nfree, sh_nmiss;
+  const int j = blockIdx.x;
+  int P = 1;
+  while (P < n_slots) P <<= 1;
+  int64_t* lu_s = reinterpret_cast<int64_t*>(keys + P);
+  int32_t* ch_s = reinterpret_cast<int32_t*>(lu_s + n_slots);
+  int32_t* cs_s = ch_s + k;
+  int32_t* sb_s = cs_s + k;
+  unsigned char* kept = reinterpret_cast<unsigned char*>(sb_s + n_slots);
+  const int32_t* ch = chosen + (int64_t)j * chosen_ld;
+  int32_t* bslot = block_slot + (int64_t)j * cap;
+  int32_t* sblock = slot_block + (int64_t)j * n_slots;
+  int64_t* lu = last_used + (int64_t)j * n_slots;
+  pdl_wait();  // the selection's chosen ids
+  for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
+    sb_s[s] = sblock[s];
+    lu_s[s] = lu[s];
+    kept[s] = 0;
+  }
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const int b = ch[i];
+    ch_s[i] = b;
+    const int sl = (b >= 0 && b < cap) ? bslot[b] : -1;
+    cs_s[i] = sl;
+  }
+  __syncthreads();
+  pdl_release();  // the fetch may be placed (it waits for this grid's completion)
+  // Hits mark their slot kept.
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const int sl = cs_s[i];
+    if (sl >= 1 && sl <= n_slots) kept[sl - 1] = 1;
+  }
+  __syncthreads();
+  // Free slots, compacted in slot order, then sorted by (last_used, slot).
+  const int seg = (n_slots + blockDim.x - 1) / blockDim.x;
+  const int lo = threadIdx.x * seg, hi = min(n_slots, lo + seg);
+  uint32_t nf = 0;
+  for (int s = lo; s < hi; ++s) nf += !kept[s];
+  uint32_t pos = admit_scan(nf, warp_sums);
+  for (int s = lo; s < hi; ++s)
+    if (!kept[s]) keys[pos++] = ((uint64_t)(lu_s[s] + 4) << 24) | (uint64_t)s;
+  if (threadIdx.x == blockDim.x - 1) sh_nfree = pos;
+  __syncthreads();
+  const int n_free = (int)sh_nfree;
+  // Only the free slots are sorted (with as many slots as the selection keeps, they are exactly the
+  // victims): a bitonic sort over the next power of two above their count.
+  int PF = 1;
+  while (PF < n_free) PF <<= 1;
+  for (int i = n_free + threadIdx.x; i < PF; i += blockDim.x) keys[i] = ~0ull;
+  __syncthreads();
+  for (int size = 2; size <= PF; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < PF / 2; i += blockDim.x) {
+        const int a = 2 * i - (i & (stride - 1)), b = a + stride;
+        const bool asc = (a & size) == 0;
+        const uint64_t x = keys[a], y = keys[b];
+        if ((x > y) == asc) {
+          keys[a] = y;
+          keys[b] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // Misses, ranked in chosen order; each takes the next victim: the victim's old block is evicted,
+  // the slot gets the missed block (old blocks are never chosen, so no entry is written twice).
+  const int segk = (k + blockDim.x - 1) / blockDim.x;
+  const int klo = threadIdx.x * segk, khi = min(k, klo + segk);
+  uint32_t nm = 0;
+  for (int i = klo; i < khi; ++i) {
+    const int b = ch_s[i];
+    nm += (b >= 0 && b < cap && cs_s[i] < 1);
+  }
+  uint32_t rank = admit_scan(nm, warp_sums);
+  if (threadIdx.x == blockDim.x - 1) sh_nmiss = rank + nm;
+  for (int i = klo; i < khi; ++i) {
+    const int b = ch_s[i];
+    if (!(b >= 0 && b < cap && cs_s[i] < 1)) continue;
+    const int v = rank < (uint32_t)n_free ? (int)(keys[rank] & 0xffffffull) : -1;
+    if (v >= 0) {
+      const int old = sb_s[v];
+      if (old >= 0) {
+        bslot[old] = -1;
+        if (evicted_at != nullptr) evicted_at[(int64_t)j * cap + old] = step;
+      }
+      sb_s[v] = b;
+      lu_s[v] = step;
+      cs_s[i] = v + 1;
+      bslot[b] = v + 1;
+      miss_blk[(int64_t)j * k + rank] = b;
+      miss_slot[(int64_t)j * k + rank] = v + 1;
+    }
+    ++rank;
+  }
+  __syncthreads();
+  // Every chosen slot was used at this step.
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const int sl = cs_s[i];
+    if (sl >= 1 && sl <= n_slots) lu_s[sl - 1] = step;
+    if (slots_out != nullptr) slots_out[(int64_t)j * slots_ld + i] = sl;
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
+    sblock[s] = sb_s[s];
+    lu[s] = lu_s[s];
+  }
+  if (threadIdx.x == 0) n_miss[j] = (int)min(sh_nmiss, (uint32_t)n_free);
+}
+
 // Copy (or dequantise) the misses of every head into their slots; warps stride over the misses.
 // An int8 record is first staged whole in the warp's shared memory (16-byte loads, once over the
 // link when the store is host memory), then dequantised from there.
@@ -167,6 +288,8 @@ __global__ void __launch_bounds__(32 * kFetchWarps) fetch_misses_kernel(const vo
   const int j = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned char* stage = stage_all + (size_t)warp * ((width + 15) / 16 * 16);
+  pdl_wait();  // the admit's miss lists
+  pdl_release();  // the attention's CTAs may be placed (they wait for this grid's completion)
   const int n = n_miss[j];
   const int n1 = bs * d, n2 = 2 * n1;
   for (int m = blockIdx.x * kFetchWarps + warp; m < n; m += gridDim.x * kFetchWarps) {
@@ -180,6 +303,44 @@ __global__ void __launch_bounds__(32 * kFetchWarps) fetch_misses_kernel(const vo
       const __half* kz = ks + d;
       const __half* vs = ks + 2 * d;
       const __half* vz = vs + bs;
+      if constexpr (sizeof(T) == 2) {
+        // bf16 slots (d a multiple of 8): lane e takes 8 consecutive values of one token, so one
+        // 8-byte code load, the scales as 16-byte loads (keys: per channel) or one value (values:
+        // per token), and one 16-byte store. Same arithmetic as below: (q + 128) * scale (exact),
+        // then + zero (one rounding), then rounded to bf16.
+        for (int e8 = lane; e8 < n2 / 8; e8 += 32) {
+          const int e = 8 * e8;
+          const int kv = e / n1, rem = e - kv * n1, t = rem / d, c = rem - t * d;
+          const uint2 cw = *reinterpret_cast<const uint2*>(stage + e);
+          const uint32_t w[2] = {cw.x ^ 0x80808080u, cw.y ^ 0x80808080u};  // (q + 128) as unsigned bytes
+          float sc[8], z[8];
+          if (kv == 0) {
+            const uint4 sv = *reinterpret_cast<const uint4*>(ks + c), zv = *reinterpret_cast<const uint4*>(kz + c);
+            const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&sw[i]));
+              const float2 bz = __half22float2(*reinterpret_cast<const __half2*>(&zw[i]));
+              sc[2 * i] = a.x, sc[2 * i + 1] = a.y, z[2 * i] = bz.x, z[2 * i + 1] = bz.y;
+            }
+          } else {
+            const float s1 = __half2float(vs[t]), z1 = __half2float(vz[t]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sc[i] = s1, z[i] = z1;
+          }
+          uint32_t out[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float q0 = (float)((w[i / 2] >> (16 * (i & 1))) & 0xffu), q1 = (float)((w[i / 2] >> (16 * (i & 1) + 8)) & 0xffu);
+            const float v0 = __fadd_rn(__fmul_rn(q0, sc[2 * i]), z[2 * i]), v1 = __fadd_rn(__fmul_rn(q1, sc[2 * i + 1]), z[2 * i + 1]);
+            const __nv_bfloat162 pr = __floats2bfloat162_rn(v0, v1);
+            out[i] = *reinterpret_cast<const uint32_t*>(&pr);
+          }
+          *reinterpret_cast<uint4*>(dst + e) = make_uint4(out[0], out[1], out[2], out[3]);
+        }
+        __syncwarp();
+        continue;
+      }
       for (int e = lane; e < n2; e += 32) {
         const int kv = e / n1, rem = e % n1, t = rem / d, c = rem % d;
         const float q = (float)reinterpret_cast<const int8_t*>(stage)[e];
@@ -192,6 +353,79 @@ __global__ void __launch_bounds__(32 * kFetchWarps) fetch_misses_kernel(const vo
       uint4* o = reinterpret_cast<uint4*>(dst);
       for (int e = lane; e < n2 * (int)sizeof(T) / 16; e += 32) o[e] = src[e];
     }
+  }
+}
+
+// fetch_misses_kernel for int8 records into bf16 slots at bs 16, d 64 (the record is 2,368 bytes).
+// A warp takes one miss at a time: the record is staged in shared memory by 16-byte loads, its 64
+// key scales and zeros become float32 there once, then lane l writes 16-byte chunks l, l + 32, ...
+// of the slot (8 values of one token each). A code becomes (q + 128) as a float exactly by a byte
+// permute into 2^23 + (q + 128) and one subtraction (two values at a time), then (q + 128) * scale +
+// zero (the product is exact, so the fused form rounds once as the product and sum do) and the bf16
+// rounding: unpack's values bit for bit.
+constexpr int kFetchRec = 2368;
+constexpr int kFetchStage = 2944;  // the record, then 64 float32 key scales and 64 zeros (16-byte multiple)
+
+__global__ void __launch_bounds__(32 * kFetchWarps) fetch_misses_i8_bf16_kernel(const uint8_t* __restrict__ store, __nv_bfloat16* __restrict__ pool,
+                                                                               int h, int k, const int32_t* __restrict__ miss_blk,
+                                                                               const int32_t* __restrict__ miss_slot,
+                                                                               const int32_t* __restrict__ n_miss) {
+  __shared__ __align__(16) unsigned char stage_all[kFetchWarps * kFetchStage];
+  const int j = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* stage = stage_all + warp * kFetchStage;
+  float* kf = reinterpret_cast<float*>(stage + kFetchRec + 64);  // 16-byte aligned: 2432
+  pdl_wait();  // the admit's miss lists
+  pdl_release();  // the attention's CTAs may be placed (they wait for this grid's completion)
+  const int n = n_miss[j];
+  for (int m = blockIdx.x * kFetchWarps + warp; m < n; m += gridDim.x * kFetchWarps) {
+    const int b = miss_blk[(int64_t)j * k + m], slot = miss_slot[(int64_t)j * k + m];
+    const uint4* rec = reinterpret_cast<const uint4*>(store + ((int64_t)b * h + j) * kFetchRec);
+#pragma unroll
+    for (int e = lane; e < kFetchRec / 16; e += 32) reinterpret_cast<uint4*>(stage)[e] = rec[e];
+    __syncwarp();
+    {  // key scales and zeros (float16 at 2048 and 2176) as float32: lane l converts channels 2l, 2l + 1
+      const __half2 sc2 = reinterpret_cast<const __half2*>(stage + 2048)[lane];
+      const __half2 zr2 = reinterpret_cast<const __half2*>(stage + 2176)[lane];
+      reinterpret_cast<float2*>(kf)[lane] = __half22float2(sc2);
+      reinterpret_cast<float2*>(kf + 64)[lane] = __half22float2(zr2);
+    }
+    __syncwarp();
+    uint4* dst = reinterpret_cast<uint4*>(pool + ((int64_t)slot * h + j) * 2048);
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int e8 = lane + 32 * it;  // chunk: 8 values; chunks 0..127 keys, 128..255 values
+      const int kv = e8 >> 7, t = (e8 >> 3) & 15, c = (e8 & 7) * 8;
+      const uint2 cw = *reinterpret_cast<const uint2*>(stage + 8 * e8);
+      const uint32_t a0 = cw.x ^ 0x80808080u, a1 = cw.y ^ 0x80808080u;
+      const float2 m23 = make_float2(-8388608.0f, -8388608.0f);
+      float2 q[4];
+      q[0] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(a0, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(a0, 0x4b000000u, 0x7651))), m23);
+      q[1] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(a0, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(a0, 0x4b000000u, 0x7653))), m23);
+      q[2] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(a1, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(a1, 0x4b000000u, 0x7651))), m23);
+      q[3] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(a1, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(a1, 0x4b000000u, 0x7653))), m23);
+      float2 sc[4], zr[4];
+      if (kv == 0) {  // keys: per channel
+        const float4 s0 = *reinterpret_cast<const float4*>(kf + c), s1 = *reinterpret_cast<const float4*>(kf + c + 4);
+        const float4 z0 = *reinterpret_cast<const float4*>(kf + 64 + c), z1 = *reinterpret_cast<const float4*>(kf + 64 + c + 4);
+        sc[0] = make_float2(s0.x, s0.y), sc[1] = make_float2(s0.z, s0.w), sc[2] = make_float2(s1.x, s1.y), sc[3] = make_float2(s1.z, s1.w);
+        zr[0] = make_float2(z0.x, z0.y), zr[1] = make_float2(z0.z, z0.w), zr[2] = make_float2(z1.x, z1.y), zr[3] = make_float2(z1.z, z1.w);
+      } else {  // values: per token (float16 at 2304 and 2336)
+        const float s1 = __half2float(reinterpret_cast<const __half*>(stage + 2304)[t]);
+        const float z1 = __half2float(reinterpret_cast<const __half*>(stage + 2336)[t]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[i] = make_float2(s1, s1), zr[i] = make_float2(z1, z1);
+      }
+      uint32_t out[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 v = __ffma2_rn(q[i], sc[i], zr[i]);
+        const __nv_bfloat162 pr = __floats2bfloat162_rn(v.x, v.y);
+        out[i] = *reinterpret_cast<const uint32_t*>(&pr);
+      }
+      dst[e8] = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+    __syncwarp();  // the stage is read before the next record lands in it
   }
 }
 
@@ -215,25 +449,61 @@ extern "C" int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chose
   if (bs % 8 || d % 8 || bs > 128 || d > 256) return fail(LKV_ERR_ARG, "lkv_tier_admit: bs and d must be multiples of 8 (bs <= 128, d <= 256)");
   int P = 1;
   while (P < n_slots) P <<= 1;
-  const size_t smem = (size_t)P * 8 + (size_t)((n_slots + 15) / 16 * 16);
   cudaStream_t st = as_stream(stream);
-  if (smem > 48 * 1024) cudaFuncSetAttribute(admit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  admit_kernel<<<h, kAdmitThreads, smem, st>>>(chosen, k, chosen_ld, block_slot, cap, slot_block, last_used, n_slots, evicted_at, step,
-                                                miss_blk, miss_slot, n_miss, slots_out, slots_ld);
-  if (int rc = launched("lkv_tier_admit(admit)")) return rc;
+  // The staged admit when its tables fit in shared memory (keys, last_used, chosen, their slots,
+  // slot_block, the kept flags); else the one that works on the tables in global memory.
+  const size_t staged = (size_t)P * 8 + (size_t)n_slots * 8 + (size_t)k * 8 + (size_t)n_slots * 4 + (size_t)((n_slots + 15) / 16 * 16);
+  if (staged <= 200 * 1024) {
+    cudaError_t e = cudaSuccess;
+    if (staged > 48 * 1024) e = cudaFuncSetAttribute(admit_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged);
+    if (e == cudaSuccess)
+      e = launch_pdl(admit_staged_kernel, dim3(h), dim3(kAdmitThreads), staged, st, 0, chosen, k, chosen_ld, block_slot, cap, slot_block, last_used,
+                     n_slots, evicted_at, step, miss_blk, miss_slot, n_miss, slots_out, slots_ld);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(LKV_ERR_CUDA, "lkv_tier_admit(admit): %s", cudaGetErrorString(e));
+    }
+  } else {
+    const size_t smem = (size_t)P * 8 + (size_t)((n_slots + 15) / 16 * 16);
+    if (smem > 200 * 1024) return fail(LKV_ERR_ARG, "lkv_tier_admit: %d slots need %zu bytes of shared memory", n_slots, smem);
+    if (smem > 48 * 1024) cudaFuncSetAttribute(admit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    admit_kernel<<<h, kAdmitThreads, smem, st>>>(chosen, k, chosen_ld, block_slot, cap, slot_block, last_used, n_slots, evicted_at, step,
+                                                  miss_blk, miss_slot, n_miss, slots_out, slots_ld);
+    if (int rc = launched("lkv_tier_admit(admit)")) return rc;
+  }
   const int64_t width = lkv_packed_pair_bytes(bs, d);
+  if (store_kind == LKV_COLD_INT8 && dtype == LKV_BF16 && bs == 16 && d == 64) {
+    // Up to four CTAs per SM over the heads, enough for every selected block to miss.
+    int per_head = (k + kFetchWarps - 1) / kFetchWarps;
+    const int cap_ctas = (4 * kNumSMs + h - 1) / h;
+    if (per_head > cap_ctas) per_head = cap_ctas;
+    cudaError_t e = launch_pdl(fetch_misses_i8_bf16_kernel, dim3(per_head, h), dim3(32 * kFetchWarps), 0, st, 0, static_cast<const uint8_t*>(store),
+                               static_cast<__nv_bfloat16*>(pool), h, k, (const int32_t*)miss_blk, (const int32_t*)miss_slot, (const int32_t*)n_miss);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(LKV_ERR_CUDA, "lkv_tier_admit(fetch): %s", cudaGetErrorString(e));
+    }
+    return launched("lkv_tier_admit(fetch)");
+  }
   const int fetch_ctas = (k + kFetchWarps - 1) / kFetchWarps < 32 ? (k + kFetchWarps - 1) / kFetchWarps : 32;
   dim3 grid(fetch_ctas, h);
   const size_t fsmem = store_kind == LKV_COLD_INT8 ? (size_t)kFetchWarps * ((width + 15) / 16 * 16) : 0;
   if (fsmem > 200 * 1024) return fail(LKV_ERR_ARG, "lkv_tier_admit: records of %lld bytes are too wide to stage", (long long)width);
+  cudaError_t e = cudaSuccess;
   if (dtype == LKV_BF16) {
     auto kern = fetch_misses_kernel<__nv_bfloat16>;
     if (fsmem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
-    kern<<<grid, 32 * kFetchWarps, fsmem, st>>>(store, store_kind, width, static_cast<__nv_bfloat16*>(pool), h, bs, d, k, miss_blk, miss_slot, n_miss);
+    e = launch_pdl(kern, grid, dim3(32 * kFetchWarps), fsmem, st, 0, store, store_kind, width, static_cast<__nv_bfloat16*>(pool), h, bs, d, k,
+                   (const int32_t*)miss_blk, (const int32_t*)miss_slot, (const int32_t*)n_miss);
   } else {
     auto kern = fetch_misses_kernel<float>;
     if (fsmem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
-    kern<<<grid, 32 * kFetchWarps, fsmem, st>>>(store, store_kind, width, static_cast<float*>(pool), h, bs, d, k, miss_blk, miss_slot, n_miss);
+    e = launch_pdl(kern, grid, dim3(32 * kFetchWarps), fsmem, st, 0, store, store_kind, width, static_cast<float*>(pool), h, bs, d, k,
+                   (const int32_t*)miss_blk, (const int32_t*)miss_slot, (const int32_t*)n_miss);
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_tier_admit(fetch): %s", cudaGetErrorString(e));
   }
   return launched("lkv_tier_admit(fetch)");
 }

@@ -1,15 +1,17 @@
 """The bench's own launches at the metric geometry, against the oracle.
 
 One selecting layer exactly as `bench.py` builds and runs it (131,072 tokens, 16-token blocks, 8 KV
-heads, G = 4, d = 64, 25% budget: K = 2,046 of 8,190 candidates, the int8 cold tier in HBM, the hot
-slot pool holding the selected blocks, read through the slot map): the TMA-scored selection in
-block order, then the fused attention (hot pass, cold pass over the complement of the bitmap and
-their merge in one launch, 18 CTAs per head with their per-CTA lists, rings and fold at full size).
+heads, G = 4, d = 64, 25% budget: K = 2,046 of 8,190 candidates, the int8 cold tier in HBM): the
+TMA-scored selection in block order, the device admit that fetches the selected blocks into the slot
+pool (dequantised from their records), then the fused attention (hot pass over the listed slots,
+cold pass over the complement of the bitmap and their merge in one launch, 18 CTAs per head with
+their per-CTA lists, rings and fold at full size).
 The same seeded layer goes through `oracle.tiered_decode` (float64 attention over the reference's
 pieces: `unpack(pack(block))` in bf16 for the sealed blocks, the exact sink and current block),
 which makes its own selection. Held:
   * int8 records and block metadata byte/bit-exact with the oracle's `pack` and min/max;
   * the Quest bounds bit-exact and the selected set equal to the oracle's top-K (ties to the lower ids);
+  * every selected block in a slot of the pool, holding its record dequantised to bf16;
   * the float32 merged output within 1e-5 of max|out| (and lse within 1e-5), the bf16 output the
     bf16 rounding of a value within 2e-5 of the oracle (at most half a bf16 unit plus 2e-5 of the max).
 """
@@ -37,7 +39,7 @@ def metric_layer():
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    args = argparse.Namespace(ctx=CTX, budget=0.25, layers=1)
+    args = argparse.Namespace(ctx=CTX, budget=0.25, layers=1, queries=1, drift=0.5)
     layers, geo = bench.build_layers(args, 0, 1, dev, keep_source=True)
     L = layers[0]
     assert geo["n_cand"] == 8190 and geo["k_local"] == 2046 and geo["n_list"] == 2048
@@ -53,7 +55,7 @@ def metric_layer():
     out32 = torch.empty((HQ, D), dtype=torch.float32, device=dev)
     lse32 = torch.empty((HQ,), dtype=torch.float32, device=dev)
     K.exact_attention(L.q, L.pool, L.pool[:, :, 1], (HKV * 2 * BS * D, 2 * BS * D, D), L.list, BS, L.records, 1, geo["n_cand"],
-                      geo["scale"], BS, excluded=L.bitmap, slot_of=L.slot_of, out_dtype=torch.float32, out=out32, lse=lse32)
+                      geo["scale"], BS, excluded=L.bitmap, out_dtype=torch.float32, out=out32, lse=lse32)
     torch.cuda.synchronize()
     status = K.device_status(clear=True)
     got = {
@@ -62,7 +64,10 @@ def metric_layer():
         "kmax": L.kmax.float().cpu().numpy(),
         "bound": bound.cpu().numpy(),
         "list": L.list.cpu().numpy(),
+        "chosen": L.chosen.cpu().numpy(),
         "sel_call": sel.cpu().numpy(),
+        "pool": L.pool.cpu(),
+        "deq": K.unpack_int8(L.records.view(-1, L.records.shape[-1]), BS, D, torch.bfloat16).view(L.records.shape[0], HKV, 2, BS, D).cpu(),
         "bitmap": L.bitmap.cpu().numpy(),
         "out_bf16": out_bf16.float().cpu().numpy(),
         "out32": out32.cpu().numpy(),
@@ -89,14 +94,24 @@ def test_bounds_bit_exact_and_the_selected_set_is_the_oracles(metric_layer) -> N
     got, want, geo = metric_layer
     assert np.array_equal(got["bound"], want["bound"].astype(np.float32))
     k = geo["k_local"]
-    sel = got["list"][:, 1 : 1 + k]
     want_sel = np.sort(want["selected"], axis=1)
-    assert np.array_equal(sel, want_sel)
+    assert np.array_equal(got["chosen"], want_sel)
     assert np.array_equal(got["sel_call"], want_sel)
-    assert (got["list"][:, 0] == 0).all() and (got["list"][:, -1] == geo["nb"] - 1).all()
+    # hot list: the sink's slot, the admitted slots, the current block's slot
+    assert (got["list"][:, 0] == 0).all() and (got["list"][:, -1] == k + 1).all()
     bits = np.unpackbits(got["bitmap"].view(np.uint8), bitorder="little").reshape(HKV, -1)
     for j in range(HKV):
         assert np.array_equal(np.nonzero(bits[j])[0], want_sel[j])
+
+
+def test_the_admit_put_every_selected_block_in_a_slot(metric_layer) -> None:  # noqa: ANN001
+    got, _, geo = metric_layer
+    k = geo["k_local"]
+    slots = got["list"][:, 1 : 1 + k]
+    for j in range(HKV):
+        assert sorted(slots[j].tolist()) == list(range(1, k + 1))  # every slot holds one selected block
+        for s_, b in zip(slots[j].tolist(), got["chosen"][j].tolist()):
+            assert torch.equal(got["pool"][s_, j], got["deq"][b, j]), (j, s_, b)
 
 
 def test_fused_attention_matches_the_oracle_at_full_size(metric_layer) -> None:  # noqa: ANN001
