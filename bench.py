@@ -267,10 +267,20 @@ def attention_call(L, geo: dict, r: int = 0, cold_store=None) -> None:  # noqa: 
                       geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["scale"], BS, excluded=L.bitmap, out=L.out, lse=L.lse)
 
 
+def select_admit_call(L, geo: dict, r: int, step: int, cold_store=None) -> None:  # noqa: ANN001
+    """The selection of query r and its admit in one call (lkv_quest_topk_admit)."""
+    from lazykv_b200 import kernels as K
+
+    so = geo["sel_off"]
+    K.quest_topk_admit(L.q_ring[r], L.kmin, L.kmax, geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["k_local"], L.chosen, L.bitmap, L.block_slot,
+                       L.slot_block, L.last_used, L.evicted_at, step, L.records if cold_store is None else cold_store, L.pool, L.miss_blk,
+                       L.miss_slot, L.n_miss, slots_out=L.list[:, so : so + geo["k_local"]])
+
+
 def layer_step(L, geo: dict, r: int = 0, step: int = 1, cold_store=None, events: list | None = None) -> None:  # noqa: ANN001
     """One layer-step of the hot path with query r (all launches on the current stream): score +
-    top-K, the device admit (and fetch of misses), then the hot and cold passes and their merge in
-    one attention launch."""
+    top-K, then the device admit and the fetch of misses (one call), then the hot and cold passes
+    and their merge in one attention launch."""
 
     def mark() -> None:
         if events is not None:
@@ -281,15 +291,13 @@ def layer_step(L, geo: dict, r: int = 0, step: int = 1, cold_store=None, events:
             events.append(e)
 
     mark()
-    select_call(L, geo, r)
-    mark()
-    admit_call(L, geo, step, cold_store)
+    select_admit_call(L, geo, r, step, cold_store)
     mark()
     attention_call(L, geo, r, cold_store)
     mark()
 
 
-LAUNCHES_PER_LAYER_STEP = 4  # the selection (TMA scoring, then a cluster select per head), the admit (LRU and fetch of misses), the attention (both passes and their merge)
+LAUNCHES_PER_LAYER_STEP = 5  # the selection (TMA scoring, a cluster select per head), the admit and the fetch of misses, the attention (both passes and their merge)
 
 
 def dequant_records(records, dtype):  # noqa: ANN001, ANN201
@@ -548,7 +556,7 @@ def run_ours(args: argparse.Namespace) -> None:
         return us
 
     sel_us = group_us(lambda r, st: [select_call(L, geo, r) for L in layers])
-    sel_admit_us = group_us(lambda r, st: [(select_call(L, geo, r), admit_call(L, geo, st)) for L in layers])
+    sel_admit_us = group_us(lambda r, st: [select_admit_call(L, geo, r, st) for L in layers])
     attn_us = group_us(lambda r, st: [attention_call(L, geo, r) for L in layers])
     kernel_us = {"select": sel_us, "admit": max(0.0, sel_admit_us - sel_us), "attention": attn_us}
 
@@ -558,8 +566,7 @@ def run_ours(args: argparse.Namespace) -> None:
     for r in range(R):
         step_no += 1
         for L in layers:
-            select_call(L, geo, r)
-            admit_call(L, geo, step_no)
+            select_admit_call(L, geo, r, step_no)
             misses += L.n_miss.sum()
     torch.cuda.synchronize()
     miss_pairs = float(misses.item()) / (R * len(layers))
@@ -701,7 +708,7 @@ def run_ours(args: argparse.Namespace) -> None:
             ev: list = []
             layer_step(L, geo, 0, step_no + 10**6, L.records_host, ev)
             torch.cuda.synchronize()
-            cold_us.append(ev[2].elapsed_time(ev[3]) * 1e3)
+            cold_us.append(ev[1].elapsed_time(ev[2]) * 1e3)
         cu = statistics.median(cold_us)
         link = measure_link_gbs(dev)
         result["host_cold_tier"] = {"value": round(1e3 / hms, 3), "unit": "tokens/s", "us_per_layer_step": round(hms * 1e3 / n_sel, 1),

@@ -301,6 +301,25 @@ int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32
                    int32_t* slots_out, int64_t slots_ld, void* stream);
 
 /*
+ * lkv_quest_topk in block order followed by lkv_tier_admit of its selection, in one call: the
+ * selection written to out_blocks (and the bitmap) is made resident (LRU victims, misses fetched and
+ * dequantised into their slots, slots_out = the slots of the selected blocks). Replaces
+ * lazykv/tiered.py:383-463 (rank, then admit). Same arguments and results as the two calls (the
+ * selection's chosen_ld is out_ld, its k the admit's k); the admit's arguments are checked before
+ * anything runs, so an invalid call launches nothing.
+ * No reference counterpart as one call (the reference ranks on the device, then admits on the host).
+ */
+int lkv_quest_topk_admit(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
+                         const void* kmax, int meta_dtype, int64_t m_head, int first_block,
+                         int n_cand, int k, int bound_mode, int32_t* out_blocks, int out_ld,
+                         float* out_bound, uint32_t* bitmap, int bitmap_words, void* workspace,
+                         size_t workspace_bytes, int32_t* block_slot, int cap, int32_t* slot_block,
+                         int64_t* last_used, int n_slots, int64_t* evicted_at, int64_t step,
+                         const void* store, int store_kind, void* pool, int bs, int dtype,
+                         int32_t* miss_blk, int32_t* miss_slot, int32_t* n_miss, int32_t* slots_out,
+                         int64_t slots_ld, void* stream);
+
+/*
  * Status word of the kernels that wait on shared-memory barriers (bounded waits): 0 when no wait
  * ran out, else the first code recorded (1 = a wait timed out; 2 = an attention CTA's item list
  * overflowed its shared memory, a sizing error that leaves that call's output empty). Synchronous;

@@ -58,6 +58,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                            c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_tier_admit": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int,
                                c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "lkv_quest_topk_admit": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_int,
+                                     c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64,
+                                     c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
 }
 
 

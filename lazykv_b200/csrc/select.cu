@@ -767,7 +767,7 @@ __global__ void __launch_bounds__(kPkThreads) quest_pick_kernel(const __grid_con
   const int w_lo = wf + (int)((int64_t)nw * c / C), w_hi = wf + (int)((int64_t)nw * (c + 1) / C);
   const int W = sp.bitmap_words;
   pdl_wait();  // the keys, the histogram and the failure word of the scoring
-  pdl_release();  // the attention's CTAs may be placed now (they wait for this grid's completion)
+  pdl_release();  // the next kernel's CTAs may be placed now (they wait for this grid's completion)
   const bool failed = __ldcg(&sp.fail[j]) != 0u;
   uint32_t keys[KPT];
   bool have[KPT];
@@ -1017,10 +1017,14 @@ size_t lkv_quest_topk_workspace(int h, int n_cand) {
   return kKeysOffset + (size_t)(h > 0 ? h : 0) * (size_t)(n_cand > 0 ? n_cand : 0) * sizeof(uint64_t);
 }
 
-int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax,
-                   int meta_dtype, int64_t m_head, int first_block, int n_cand, int k, int bound_mode, int order,
-                   int32_t* out_blocks, int out_ld, float* out_bound, uint32_t* bitmap, int bitmap_words,
-                   void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace lkv {
+namespace {
+
+int quest_topk_impl(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax, int meta_dtype, int64_t m_head,
+                    int first_block, int n_cand, int k, int bound_mode, int order, int32_t* out_blocks, int out_ld, float* out_bound,
+                    uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes, void* stream) {
   if (!dtype_ok(q_dtype) || !dtype_ok(meta_dtype) || !dtype_ok(bound_mode))
     return fail(LKV_ERR_ARG, "lkv_quest_topk: bad dtype (q %d, meta %d, bound %d)", q_dtype, meta_dtype, bound_mode);
   if (h <= 0 || hq <= 0 || hq % h != 0) return fail(LKV_ERR_ARG, "lkv_quest_topk: %d query heads do not group over %d KV heads", hq, h);
@@ -1099,6 +1103,43 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
   topk_kernel<<<h, kSelectThreads, smem, st>>>(keys, n_cand, k, first_block, out_blocks, out_ld, bitmap, bitmap_words, stage_keys,
                                                 order == LKV_ORDER_BLOCK, n_passes);
   return launched("lkv_quest_topk(select)");
+}
+
+}  // namespace
+}  // namespace lkv
+
+extern "C" {
+
+int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax,
+                   int meta_dtype, int64_t m_head, int first_block, int n_cand, int k, int bound_mode, int order,
+                   int32_t* out_blocks, int out_ld, float* out_bound, uint32_t* bitmap, int bitmap_words,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  return quest_topk_impl(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode, order, out_blocks, out_ld,
+                         out_bound, bitmap, bitmap_words, workspace, workspace_bytes, stream);
+}
+
+int lkv_quest_topk_admit(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax, int meta_dtype, int64_t m_head,
+                         int first_block, int n_cand, int k, int bound_mode, int32_t* out_blocks, int out_ld, float* out_bound,
+                         uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes, int32_t* block_slot, int cap,
+                         int32_t* slot_block, int64_t* last_used, int n_slots, int64_t* evicted_at, int64_t step, const void* store,
+                         int store_kind, void* pool, int bs, int dtype, int32_t* miss_blk, int32_t* miss_slot, int32_t* n_miss,
+                         int32_t* slots_out, int64_t slots_ld, void* stream) {
+  // The admit's arguments are checked before anything is launched, as lkv_tier_admit checks them.
+  if (!dtype_ok(dtype)) return fail(LKV_ERR_ARG, "lkv_quest_topk_admit: bad dtype %d", dtype);
+  if (store_kind != LKV_COLD_INT8 && store_kind != LKV_COLD_PAIRS) return fail(LKV_ERR_ARG, "lkv_quest_topk_admit: bad store kind %d", store_kind);
+  if (h <= 0 || k <= 0 || cap <= 0 || n_slots < k) return fail(LKV_ERR_ARG, "lkv_quest_topk_admit: need h, k, cap > 0 and n_slots >= k (%d < %d)", n_slots, k);
+  if (n_slots > (1 << 16)) return fail(LKV_ERR_ARG, "lkv_quest_topk_admit: %d slots above 65536", n_slots);
+  if (block_slot == nullptr || slot_block == nullptr || last_used == nullptr || store == nullptr || pool == nullptr || miss_blk == nullptr ||
+      miss_slot == nullptr || n_miss == nullptr)
+    return fail(LKV_ERR_PTR, "lkv_quest_topk_admit: null pointer");
+  if (!aligned(store, 16) || !aligned(pool, 16)) return fail(LKV_ERR_PTR, "lkv_quest_topk_admit: store and pool must be 16-byte aligned");
+  if (bs % 8 || d % 8 || bs > 128 || d > 256) return fail(LKV_ERR_ARG, "lkv_quest_topk_admit: bs and d must be multiples of 8 (bs <= 128, d <= 256)");
+  if ((int64_t)first_block + n_cand > cap) return fail(LKV_ERR_ARG, "lkv_quest_topk_admit: candidates end past the %d blocks of block_slot", cap);
+  const int rc = quest_topk_impl(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode, LKV_ORDER_BLOCK,
+                                 out_blocks, out_ld, out_bound, bitmap, bitmap_words, workspace, workspace_bytes, stream);
+  if (rc != LKV_OK) return rc;
+  return lkv_tier_admit(out_blocks, h, k, out_ld, block_slot, cap, slot_block, last_used, n_slots, evicted_at, step, store, store_kind, pool, bs, d,
+                        dtype, miss_blk, miss_slot, n_miss, slots_out, slots_ld, stream);
 }
 
 size_t lkv_topk_merge_workspace(int h, int n) { return lkv_quest_topk_workspace(h, n); }

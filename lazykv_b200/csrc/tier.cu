@@ -13,6 +13,7 @@
 // The fetch kernel then copies each miss from the host store (pairs in the model dtype, or int8
 // records dequantised exactly as lazykv/quant.py:unpack) into its slot of the pool
 // [n_slots + 2, h, 2, bs, d].
+#include "admit.cuh"
 #include "common.cuh"
 
 namespace lkv {
@@ -152,125 +153,16 @@ __global__ void __launch_bounds__(kAdmitThreads) admit_kernel(const int32_t* __r
   if (threadIdx.x == 0) n_miss[j] = (int)min(sh_nmiss, (uint32_t)n_free);
 }
 
-// admit_kernel with the head's tables staged in shared memory: the chosen ids, each chosen block's
-// current slot (one gather of block_slot), slot_block and last_used are read once, every phase
-// works on the staged copies, and the changes go back at the end (block_slot and evicted_at by
-// single stores). Same rule, same victims in the same order, same tables afterwards. Used when the
-// staged tables fit in shared memory.
-__global__ void __launch_bounds__(kAdmitThreads) admit_staged_kernel(const int32_t* __restrict__ chosen, int k, int64_t chosen_ld,
-                                                                      int32_t* __restrict__ block_slot, int cap, int32_t* __restrict__ slot_block,
-                                                                      int64_t* __restrict__ last_used, int n_slots, int64_t* __restrict__ evicted_at,
-                                                                      int64_t step, int32_t* __restrict__ miss_blk, int32_t* __restrict__ miss_slot,
-                                                                      int32_t* __restrict__ n_miss, int32_t* __restrict__ slots_out, int64_t slots_ld) {
-  extern __shared__ uint64_t keys[];  // [P] LRU keys, then lu_s [n_slots] int64, ch_s [k], cs_s [k], sb_s [n_slots] int32, kept [n_slots]
-  __shared__ uint32_t warp_sums[32];
-  __shared__ uint32_t sh_nfree, sh_nmiss;
+// The admit with the head's tables staged in shared memory (admit.cuh: admit_head), one CTA per
+// KV head, used when the staged tables fit in shared memory.
+__global__ void __launch_bounds__(kAdmitCtaThreads) admit_staged_kernel(const int32_t* __restrict__ chosen, int k, int64_t chosen_ld,
+                                                                         const __grid_constant__ AdmitArgs a) {
+  extern __shared__ __align__(16) unsigned char admit_smem[];
   const int j = blockIdx.x;
-  int P = 1;
-  while (P < n_slots) P <<= 1;
-  int64_t* lu_s = reinterpret_cast<int64_t*>(keys + P);
-  int32_t* ch_s = reinterpret_cast<int32_t*>(lu_s + n_slots);
-  int32_t* cs_s = ch_s + k;
-  int32_t* sb_s = cs_s + k;
-  unsigned char* kept = reinterpret_cast<unsigned char*>(sb_s + n_slots);
-  const int32_t* ch = chosen + (int64_t)j * chosen_ld;
-  int32_t* bslot = block_slot + (int64_t)j * cap;
-  int32_t* sblock = slot_block + (int64_t)j * n_slots;
-  int64_t* lu = last_used + (int64_t)j * n_slots;
-  pdl_wait();  // the selection's chosen ids
-  for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
-    sb_s[s] = sblock[s];
-    lu_s[s] = lu[s];
-    kept[s] = 0;
-  }
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const int b = ch[i];
-    ch_s[i] = b;
-    const int sl = (b >= 0 && b < cap) ? bslot[b] : -1;
-    cs_s[i] = sl;
-  }
-  __syncthreads();
-  pdl_release();  // the fetch may be placed (it waits for this grid's completion)
-  // Hits mark their slot kept.
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const int sl = cs_s[i];
-    if (sl >= 1 && sl <= n_slots) kept[sl - 1] = 1;
-  }
-  __syncthreads();
-  // Free slots, compacted in slot order, then sorted by (last_used, slot).
-  const int seg = (n_slots + blockDim.x - 1) / blockDim.x;
-  const int lo = threadIdx.x * seg, hi = min(n_slots, lo + seg);
-  uint32_t nf = 0;
-  for (int s = lo; s < hi; ++s) nf += !kept[s];
-  uint32_t pos = admit_scan(nf, warp_sums);
-  for (int s = lo; s < hi; ++s)
-    if (!kept[s]) keys[pos++] = ((uint64_t)(lu_s[s] + 4) << 24) | (uint64_t)s;
-  if (threadIdx.x == blockDim.x - 1) sh_nfree = pos;
-  __syncthreads();
-  const int n_free = (int)sh_nfree;
-  // Only the free slots are sorted (with as many slots as the selection keeps, they are exactly the
-  // victims): a bitonic sort over the next power of two above their count.
-  int PF = 1;
-  while (PF < n_free) PF <<= 1;
-  for (int i = n_free + threadIdx.x; i < PF; i += blockDim.x) keys[i] = ~0ull;
-  __syncthreads();
-  for (int size = 2; size <= PF; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < PF / 2; i += blockDim.x) {
-        const int a = 2 * i - (i & (stride - 1)), b = a + stride;
-        const bool asc = (a & size) == 0;
-        const uint64_t x = keys[a], y = keys[b];
-        if ((x > y) == asc) {
-          keys[a] = y;
-          keys[b] = x;
-        }
-      }
-      __syncthreads();
-    }
-  }
-  // Misses, ranked in chosen order; each takes the next victim: the victim's old block is evicted,
-  // the slot gets the missed block (old blocks are never chosen, so no entry is written twice).
-  const int segk = (k + blockDim.x - 1) / blockDim.x;
-  const int klo = threadIdx.x * segk, khi = min(k, klo + segk);
-  uint32_t nm = 0;
-  for (int i = klo; i < khi; ++i) {
-    const int b = ch_s[i];
-    nm += (b >= 0 && b < cap && cs_s[i] < 1);
-  }
-  uint32_t rank = admit_scan(nm, warp_sums);
-  if (threadIdx.x == blockDim.x - 1) sh_nmiss = rank + nm;
-  for (int i = klo; i < khi; ++i) {
-    const int b = ch_s[i];
-    if (!(b >= 0 && b < cap && cs_s[i] < 1)) continue;
-    const int v = rank < (uint32_t)n_free ? (int)(keys[rank] & 0xffffffull) : -1;
-    if (v >= 0) {
-      const int old = sb_s[v];
-      if (old >= 0) {
-        bslot[old] = -1;
-        if (evicted_at != nullptr) evicted_at[(int64_t)j * cap + old] = step;
-      }
-      sb_s[v] = b;
-      lu_s[v] = step;
-      cs_s[i] = v + 1;
-      bslot[b] = v + 1;
-      miss_blk[(int64_t)j * k + rank] = b;
-      miss_slot[(int64_t)j * k + rank] = v + 1;
-    }
-    ++rank;
-  }
-  __syncthreads();
-  // Every chosen slot was used at this step.
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const int sl = cs_s[i];
-    if (sl >= 1 && sl <= n_slots) lu_s[sl - 1] = step;
-    if (slots_out != nullptr) slots_out[(int64_t)j * slots_ld + i] = sl;
-  }
-  __syncthreads();
-  for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
-    sblock[s] = sb_s[s];
-    lu[s] = lu_s[s];
-  }
-  if (threadIdx.x == 0) n_miss[j] = (int)min(sh_nmiss, (uint32_t)n_free);
+  admit_stage_lu(a, j, admit_smem);  // last_used is the predecessor's to leave alone: only the chosen ids are its
+  pdl_wait();                        // the selection's chosen ids
+  pdl_release();                     // the fetch may be placed (it waits for this grid's completion)
+  admit_head(a, j, chosen + (int64_t)j * chosen_ld, k, admit_smem, true);
 }
 
 // Copy (or dequantise) the misses of every head into their slots; warps stride over the misses.
@@ -356,76 +248,22 @@ __global__ void __launch_bounds__(32 * kFetchWarps) fetch_misses_kernel(const vo
   }
 }
 
-// fetch_misses_kernel for int8 records into bf16 slots at bs 16, d 64 (the record is 2,368 bytes).
-// A warp takes one miss at a time: the record is staged in shared memory by 16-byte loads, its 64
-// key scales and zeros become float32 there once, then lane l writes 16-byte chunks l, l + 32, ...
-// of the slot (8 values of one token each). A code becomes (q + 128) as a float exactly by a byte
-// permute into 2^23 + (q + 128) and one subtraction (two values at a time), then (q + 128) * scale +
-// zero (the product is exact, so the fused form rounds once as the product and sum do) and the bf16
-// rounding: unpack's values bit for bit.
-constexpr int kFetchRec = 2368;
-constexpr int kFetchStage = 2944;  // the record, then 64 float32 key scales and 64 zeros (16-byte multiple)
-
+// fetch_misses_kernel for int8 records into bf16 slots at bs 16, d 64: a warp takes one miss at a
+// time (admit.cuh: fetch_record_i8_bf16).
 __global__ void __launch_bounds__(32 * kFetchWarps) fetch_misses_i8_bf16_kernel(const uint8_t* __restrict__ store, __nv_bfloat16* __restrict__ pool,
                                                                                int h, int k, const int32_t* __restrict__ miss_blk,
                                                                                const int32_t* __restrict__ miss_slot,
                                                                                const int32_t* __restrict__ n_miss) {
-  __shared__ __align__(16) unsigned char stage_all[kFetchWarps * kFetchStage];
+  __shared__ __align__(16) unsigned char stage_all[kFetchWarps * kFetchStageBytes];
   const int j = blockIdx.y;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  unsigned char* stage = stage_all + warp * kFetchStage;
-  float* kf = reinterpret_cast<float*>(stage + kFetchRec + 64);  // 16-byte aligned: 2432
-  pdl_wait();  // the admit's miss lists
+  const int warp = threadIdx.x >> 5;
+  unsigned char* stage = stage_all + warp * kFetchStageBytes;
+  pdl_wait();     // the admit's miss lists
   pdl_release();  // the attention's CTAs may be placed (they wait for this grid's completion)
   const int n = n_miss[j];
   for (int m = blockIdx.x * kFetchWarps + warp; m < n; m += gridDim.x * kFetchWarps) {
     const int b = miss_blk[(int64_t)j * k + m], slot = miss_slot[(int64_t)j * k + m];
-    const uint4* rec = reinterpret_cast<const uint4*>(store + ((int64_t)b * h + j) * kFetchRec);
-#pragma unroll
-    for (int e = lane; e < kFetchRec / 16; e += 32) reinterpret_cast<uint4*>(stage)[e] = rec[e];
-    __syncwarp();
-    {  // key scales and zeros (float16 at 2048 and 2176) as float32: lane l converts channels 2l, 2l + 1
-      const __half2 sc2 = reinterpret_cast<const __half2*>(stage + 2048)[lane];
-      const __half2 zr2 = reinterpret_cast<const __half2*>(stage + 2176)[lane];
-      reinterpret_cast<float2*>(kf)[lane] = __half22float2(sc2);
-      reinterpret_cast<float2*>(kf + 64)[lane] = __half22float2(zr2);
-    }
-    __syncwarp();
-    uint4* dst = reinterpret_cast<uint4*>(pool + ((int64_t)slot * h + j) * 2048);
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int e8 = lane + 32 * it;  // chunk: 8 values; chunks 0..127 keys, 128..255 values
-      const int kv = e8 >> 7, t = (e8 >> 3) & 15, c = (e8 & 7) * 8;
-      const uint2 cw = *reinterpret_cast<const uint2*>(stage + 8 * e8);
-      const uint32_t a0 = cw.x ^ 0x80808080u, a1 = cw.y ^ 0x80808080u;
-      const float2 m23 = make_float2(-8388608.0f, -8388608.0f);
-      float2 q[4];
-      q[0] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(a0, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(a0, 0x4b000000u, 0x7651))), m23);
-      q[1] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(a0, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(a0, 0x4b000000u, 0x7653))), m23);
-      q[2] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(a1, 0x4b000000u, 0x7650)), __uint_as_float(__byte_perm(a1, 0x4b000000u, 0x7651))), m23);
-      q[3] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(a1, 0x4b000000u, 0x7652)), __uint_as_float(__byte_perm(a1, 0x4b000000u, 0x7653))), m23);
-      float2 sc[4], zr[4];
-      if (kv == 0) {  // keys: per channel
-        const float4 s0 = *reinterpret_cast<const float4*>(kf + c), s1 = *reinterpret_cast<const float4*>(kf + c + 4);
-        const float4 z0 = *reinterpret_cast<const float4*>(kf + 64 + c), z1 = *reinterpret_cast<const float4*>(kf + 64 + c + 4);
-        sc[0] = make_float2(s0.x, s0.y), sc[1] = make_float2(s0.z, s0.w), sc[2] = make_float2(s1.x, s1.y), sc[3] = make_float2(s1.z, s1.w);
-        zr[0] = make_float2(z0.x, z0.y), zr[1] = make_float2(z0.z, z0.w), zr[2] = make_float2(z1.x, z1.y), zr[3] = make_float2(z1.z, z1.w);
-      } else {  // values: per token (float16 at 2304 and 2336)
-        const float s1 = __half2float(reinterpret_cast<const __half*>(stage + 2304)[t]);
-        const float z1 = __half2float(reinterpret_cast<const __half*>(stage + 2336)[t]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sc[i] = make_float2(s1, s1), zr[i] = make_float2(z1, z1);
-      }
-      uint32_t out[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 v = __ffma2_rn(q[i], sc[i], zr[i]);
-        const __nv_bfloat162 pr = __floats2bfloat162_rn(v.x, v.y);
-        out[i] = *reinterpret_cast<const uint32_t*>(&pr);
-      }
-      dst[e8] = make_uint4(out[0], out[1], out[2], out[3]);
-    }
-    __syncwarp();  // the stage is read before the next record lands in it
+    fetch_record_i8_bf16(store + ((int64_t)b * h + j) * kRecBytes16x64, pool + ((int64_t)slot * h + j) * 2048, stage);
   }
 }
 
@@ -452,13 +290,24 @@ extern "C" int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chose
   cudaStream_t st = as_stream(stream);
   // The staged admit when its tables fit in shared memory (keys, last_used, chosen, their slots,
   // slot_block, the kept flags); else the one that works on the tables in global memory.
-  const size_t staged = (size_t)P * 8 + (size_t)n_slots * 8 + (size_t)k * 8 + (size_t)n_slots * 4 + (size_t)((n_slots + 15) / 16 * 16);
+  const size_t staged = admit_smem_bytes(n_slots, k);
   if (staged <= 200 * 1024) {
+    AdmitArgs aa{};
+    aa.block_slot = block_slot;
+    aa.cap = cap;
+    aa.slot_block = slot_block;
+    aa.last_used = last_used;
+    aa.n_slots = n_slots;
+    aa.evicted_at = evicted_at;
+    aa.step = step;
+    aa.miss_blk = miss_blk;
+    aa.miss_slot = miss_slot;
+    aa.n_miss = n_miss;
+    aa.slots_out = slots_out;
+    aa.slots_ld = slots_ld;
     cudaError_t e = cudaSuccess;
     if (staged > 48 * 1024) e = cudaFuncSetAttribute(admit_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged);
-    if (e == cudaSuccess)
-      e = launch_pdl(admit_staged_kernel, dim3(h), dim3(kAdmitThreads), staged, st, 0, chosen, k, chosen_ld, block_slot, cap, slot_block, last_used,
-                     n_slots, evicted_at, step, miss_blk, miss_slot, n_miss, slots_out, slots_ld);
+    if (e == cudaSuccess) e = launch_pdl(admit_staged_kernel, dim3(h), dim3(kAdmitCtaThreads), staged, st, 0, chosen, k, chosen_ld, aa);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return fail(LKV_ERR_CUDA, "lkv_tier_admit(admit): %s", cudaGetErrorString(e));

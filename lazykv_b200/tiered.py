@@ -355,6 +355,15 @@ class TieredLayer:
                      by_block=True)
         return self.chosen
 
+    def choose_and_admit(self, query: torch.Tensor, step: int, bitmap: bool = False) -> torch.Tensor:
+        """choose() then admit_device() in one library call (lkv_quest_topk_admit)."""
+        n_full, _ = self.candidates()
+        K.quest_topk_admit(query, self.kmin[0], self.kmax[0], 1, n_full - 1, self.k, self.chosen, self.bitmap if bitmap else None, self._block_slot,
+                           self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool, self.miss_blk, self.miss_slot,
+                           self.n_miss, slots_out=self.hot_list[:, 1 : self.k + 1])
+        self.fetched_total += self.n_miss.sum()
+        return self.chosen
+
     def admit_device(self, step: int) -> None:
         """Device-side admit of self.chosen and the fetch of its misses; fills the hot list."""
         K.tier_admit(self.chosen, self._block_slot, self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool,
@@ -367,11 +376,11 @@ class TieredLayer:
         if self.out is None or self.out.shape != (hq, d):
             self.out = torch.empty((hq, d), dtype=torch.float32, device=query.device)
             self.lse = torch.empty((hq,), dtype=torch.float32, device=query.device)
-        self.choose(query, bitmap=exact)
         pool_strides = (self.h * 2 * self.bs * d, 2 * self.bs * d, d)
         if zerocopy:
+            self.choose(query, bitmap=exact)
             return self._attend_zerocopy(query, scale, exact, pool_strides)
-        self.admit_device(step)
+        self.choose_and_admit(query, step, bitmap=exact)
         if exact:
             K.exact_attention(query, self.pool, self.pool[:, :, 1], pool_strides, self.hot_list, self.fill, self.store, 1, self.n_sealed - 1,
                               scale, self.bs, excluded=self.bitmap, out_dtype=torch.float32, out=self.out, lse=self.lse)

@@ -1,0 +1,74 @@
+"""lkv_quest_topk_admit against lkv_quest_topk followed by lkv_tier_admit.
+
+Over a run of decode steps whose queries select overlapping but different blocks, from the same
+starting state, the one call and the two must leave the same selection and bitmap, the same
+residency tables (block_slot, slot_block, last_used, evicted_at), the same miss lists and hot-list
+slots, and the same slot pool, bit for bit, at head_dim 64 (the TMA-scored selection, the staged
+admit and the vectorised fetch) and 128 (the other selection and fetch paths).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+NEVER = -(2**40)
+
+
+def _state(h: int, nblk: int, k: int, d: int, seed: int):  # noqa: ANN202
+    from lazykv_b200 import kernels as K
+
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    kv = torch.randn(nblk, h, 2, 16, d, device=DEV, generator=g)
+    kv[:, :, 0] += torch.randn(1, h, 1, d, device=DEV, generator=g) * 0.7
+    kv = kv.bfloat16()
+    kmin = torch.empty((h, nblk, d), dtype=torch.bfloat16, device=DEV)
+    kmax = torch.empty_like(kmin)
+    rec = K.pack_int8(kv, kmin=kmin, kmax=kmax)
+    q_base = torch.randn(4 * h, d, device=DEV, generator=g)
+    queries = [(q_base + 0.2 * torch.randn(4 * h, d, device=DEV, generator=g)).bfloat16() for _ in range(6)]
+    st = {
+        "chosen": torch.zeros((h, k), dtype=torch.int32, device=DEV),
+        "bitmap": torch.zeros((h, K.bitmap_words(nblk + 1)), dtype=torch.int32, device=DEV),
+        "block_slot": torch.full((h, nblk), -1, dtype=torch.int32, device=DEV),
+        "slot_block": torch.full((h, k), -1, dtype=torch.int32, device=DEV),
+        "last_used": torch.full((h, k), -2, dtype=torch.int64, device=DEV),
+        "evicted_at": torch.full((h, nblk), NEVER, dtype=torch.int64, device=DEV),
+        "pool": torch.zeros((k + 2, h, 2, 16, d), dtype=torch.bfloat16, device=DEV),
+        "miss_blk": torch.zeros((h, k), dtype=torch.int32, device=DEV),
+        "miss_slot": torch.zeros((h, k), dtype=torch.int32, device=DEV),
+        "n_miss": torch.zeros((h,), dtype=torch.int32, device=DEV),
+        "slots": torch.zeros((h, k), dtype=torch.int32, device=DEV),
+    }
+    return kmin, kmax, rec, queries, st
+
+
+def _compare(a: dict, b: dict) -> None:
+    for name in ("chosen", "bitmap", "block_slot", "slot_block", "last_used", "evicted_at", "n_miss", "slots", "pool"):
+        assert torch.equal(a[name], b[name]), name
+    for j in range(a["n_miss"].shape[0]):
+        n = int(a["n_miss"][j])
+        assert torch.equal(a["miss_blk"][j, :n], b["miss_blk"][j, :n]) and torch.equal(a["miss_slot"][j, :n], b["miss_slot"][j, :n])
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_select_admit_equals_the_two_calls(d: int) -> None:
+    from lazykv_b200 import kernels as K
+
+    h, nblk, k = 8, 4096, 1022
+    kmin, kmax, rec, queries, a = _state(h, nblk, k, d, seed=d)
+    b = {n: t.clone() for n, t in a.items()}
+    total_miss = 0
+    for step, q in enumerate(queries + queries[:2], start=1):
+        K.quest_topk(q, kmin, kmax, 1, nblk - 2, k, out_blocks=a["chosen"], bitmap=a["bitmap"], by_block=True)
+        K.tier_admit(a["chosen"], a["block_slot"], a["slot_block"], a["last_used"], a["evicted_at"], step, rec, a["pool"], a["miss_blk"],
+                     a["miss_slot"], a["n_miss"], slots_out=a["slots"])
+        K.quest_topk_admit(q, kmin, kmax, 1, nblk - 2, k, b["chosen"], b["bitmap"], b["block_slot"], b["slot_block"], b["last_used"],
+                           b["evicted_at"], step, rec, b["pool"], b["miss_blk"], b["miss_slot"], b["n_miss"], slots_out=b["slots"])
+        torch.cuda.synchronize()
+        _compare(a, b)
+        total_miss += int(a["n_miss"].sum())
+    assert total_miss > h * k  # the first step misses everything, later steps some
+    assert K.device_status() == 0
