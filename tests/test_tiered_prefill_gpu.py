@@ -95,3 +95,40 @@ def test_prompt_longer_than_capacity_is_refused(tiny) -> None:  # noqa: ANN001
     cfg, model = tiny
     with pytest.raises(ValueError, match="exceeds capacity"):
         tiered_prefill(model, ids_for(cfg)[:, :PROMPT], 32, K, BS, capacity_tokens=64, dense_layers=1)
+
+
+def test_layer_major_prefill_stores_what_the_oracle_packs(tiny) -> None:  # noqa: ANN001
+    """The tier the layer-major prefill writes, against the oracle (lazykv/quant.py:73-105 pack and
+    unpack, lazykv/selection.py:142-144 min/max, lazykv/tiered.py:187-202): each selecting layer's int8
+    records byte-exact with the oracle's pack of the KV the model computed (read from a chunk-major
+    prefill's full cache), the metadata the min/max of the dequantised keys, the sink slot the exact
+    first block and the current slot the unsealed tail."""
+    import numpy as np
+
+    import oracle as O
+    from lazykv_b200.cache import FullGPUCache
+    from lazykv_b200.generate import prefill
+    from lazykv_b200.tiered_prefill import tiered_prefill
+
+    cfg, model = tiny
+    ids = ids_for(cfg)
+    full = FullGPUCache(cfg.num_hidden_layers, CAP)
+    prefill(model, full, ids[:, :PROMPT], chunk_size=32)
+    got = tiered_prefill(model, ids[:, :PROMPT], 32, K, BS, CAP, dense_layers=1, fetch="gather", quant="int8")
+    n_blocks, tail = divmod(PROMPT, BS)
+    for i, t in got.cache.tiers.items():
+        keys = full.layers[i].keys[0, :, :PROMPT].float().cpu().numpy()  # [h, T, d]
+        values = full.layers[i].values[0, :, :PROMPT].float().cpu().numpy()
+        h, _, d = keys.shape
+        pairs = np.stack([keys[:, : n_blocks * BS], values[:, : n_blocks * BS]], axis=1).reshape(h, 2, n_blocks, BS, d).transpose(2, 0, 1, 3, 4)
+        want = O.pack(pairs)  # [n, h, W]
+        assert t.n_sealed == n_blocks and t.fill == tail
+        assert np.array_equal(t.host[:n_blocks].numpy(), want)
+        deq = O.unpack(want.reshape(n_blocks * h, -1), BS, d, "bfloat16").reshape(n_blocks, h, 2, BS, d)
+        kmin, kmax = O.block_minmax(deq[:, :, 0].transpose(1, 0, 2, 3).reshape(h, n_blocks * BS, d), BS)
+        assert np.array_equal(t.kmin[0, :, 1:n_blocks].float().cpu().numpy(), kmin[:, 1:])
+        assert np.array_equal(t.kmax[0, :, 1:n_blocks].float().cpu().numpy(), kmax[:, 1:])
+        assert np.array_equal(t.pool[0].float().cpu().numpy(), pairs[0])  # the sink stays exact
+        cur = t.pool[t.tail_slot, :, :, :tail].float().cpu().numpy()
+        assert np.array_equal(cur[:, 0], keys[:, n_blocks * BS :]) and np.array_equal(cur[:, 1], values[:, n_blocks * BS :])
+    got.cache.close()
