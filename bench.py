@@ -58,6 +58,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--layers", type=int, default=N_LAYERS - DENSE, help="selecting layers (the metric runs all 14; fewer for profiling)")
     p.add_argument("--queries", type=int, default=8, help="queries in each layer's ring: decode token s uses query s mod this")
     p.add_argument("--drift", type=float, default=0.15, help="a ring query is a base query + drift x N(0,1) (0.15: a hit rate near 0.84, inside the 0.79-1.0 the reference measured with real models)")
+    p.add_argument("--no-long-ctx", action="store_true", help="skip the 1,048,576-token leg (8 sequences, head_dim 128, global top-K)")
+    p.add_argument("--long-layers", type=int, default=4, help="layers of the long-context leg held and timed (each 30 GB at N = 1)")
+    p.add_argument("--long-steps", type=int, default=32, help="timed decode steps of the long-context leg")
     p.add_argument("--workload", choices=["metric", "ragged"], default="metric",
                    help="ragged: BASELINE config 3 instead of the metric (64 sequences of 4K-128K tokens, 6.25%% budget, one layer)")
     p.add_argument("--profile-calls", action="store_true",
@@ -154,22 +157,37 @@ class Layer:
 NEVER = -(2**40)  # "evicted at" of a block never evicted (the tier's convention)
 
 
-def build_layers(args: argparse.Namespace, rank: int, world: int, dev, keep_source: bool = False) -> tuple[list, dict]:
+def metric_shape(args: argparse.Namespace) -> dict:
+    """The metric's geometry: Llama-3.2-1B attention at the bench's context, budget and layer count."""
+    return dict(ctx=args.ctx, h=HKV, hq=HQ, d=D, layers=args.layers, budget=args.budget, queries=max(1, getattr(args, "queries", 1)),
+                drift=getattr(args, "drift", 0.15), seed=1234)
+
+
+def build_layers(args: argparse.Namespace, rank: int, world: int, dev, keep_source: bool = False, shape: dict | None = None,
+                 global_select: bool = False) -> tuple[list, dict]:
     """Every selecting layer's device state for this rank's shard, laid out as the tier keeps it:
     int8 records of the sealed blocks (local ids) in HBM, the bf16 min/max key metadata, a slot pool
     [K + 2, h, 2, bs, d] (slot 0 the exact sink on rank 0, slots 1..K the admitted blocks, slot K + 1
     the current block on the last rank), the residency tables of the device admit, and a ring of
-    `args.queries` queries (a base query plus `args.drift` x N(0, 1), rounded to bf16: the queries of
-    successive decode steps, which select overlapping but different blocks). With `keep_source`, a
-    layer also keeps its sealed blocks (L.kv, bf16 [blocks, h, 2, bs, d]) and its current block (L.cur)."""
+    `queries` queries (a base query plus `drift` x N(0, 1), rounded to bf16: the queries of
+    successive decode steps, which select overlapping but different blocks). `shape` gives the
+    geometry (context, KV rows h, query rows hq, head_dim d, layers, budget; the metric's by
+    default); rows may be several sequences' KV heads, which every kernel takes as more heads. The
+    blocks are generated and packed in chunks. With `keep_source`, a layer also keeps its sealed
+    blocks (L.kv, bf16 [blocks, h, 2, bs, d]) and its current block (L.cur). With `global_select`
+    the rank holds whatever part of one global top-K falls in its range (sharded.GlobalSelection):
+    its slots, chosen ids and hot list take min(K, candidates) entries per row instead of its
+    proportional share."""
     import torch
 
     from lazykv_b200 import kernels as K
     from lazykv_b200.selection import blocks_for_budget
 
-    nb = args.ctx // BS  # blocks in the context; the last one is the (full) current block
+    sh = shape or metric_shape(args)
+    h, hq, d = sh["h"], sh["hq"], sh["d"]
+    nb = sh["ctx"] // BS  # blocks in the context; the last one is the (full) current block
     n_sealed = nb - 1
-    k_total = blocks_for_budget(args.budget, args.ctx, BS)
+    k_total = blocks_for_budget(sh["budget"], sh["ctx"], BS)
     # Shard the sealed blocks 0..n_sealed-1 by contiguous range (lkv_shard_plan): the sink on rank 0,
     # the current block on the last rank, the budget shared in proportion to the candidates.
     from lazykv_b200.sharded import shard_plan
@@ -177,67 +195,79 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev, keep_sour
     plan = shard_plan(n_sealed, k_total, world, rank)
     lo, hi, has_sink, has_cur = plan.lo, plan.hi, plan.has_sink, plan.has_current
     cand_lo, n_cand, k_local = plan.cand_first, plan.n_cand, plan.k_local
-    if n_cand <= k_local:
+    if global_select:
+        k_local = min(k_total, n_cand)
+    elif n_cand <= k_local:
         raise SystemExit(f"shard of {n_cand} candidates cannot select {k_local}")
     n_list = k_local + int(has_sink) + int(has_cur)
     sel_off = int(has_sink)
-    scale = D**-0.5
-    n_q = max(1, getattr(args, "queries", 1))
-    drift = getattr(args, "drift", 0.5)
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    scale = d**-0.5
+    n_q, drift = sh["queries"], sh["drift"]
+    g = torch.Generator(device=dev).manual_seed(sh["seed"] + rank)
+    nblk = hi - lo
+    chunk = max(1, (1 << 31) // (h * 2 * BS * d * 2))  # blocks generated at once: 2 GiB of bf16 pairs
     layers = []
     torch.cuda.synchronize(dev)
-    for li in range(args.layers):
+    for li in range(sh["layers"]):
         L = Layer()
-        nblk = hi - lo
-        off = torch.randn(HKV, 1, D, device=dev, generator=g) * 0.5**0.5
-        kv = torch.randn(nblk, HKV, 2, BS, D, device=dev, generator=g)
-        kv[:, :, 0] += off.view(1, HKV, 1, D)
-        kv = kv.bfloat16()
-        L.kmin = torch.empty((HKV, nblk, D), dtype=torch.bfloat16, device=dev)
+        off = torch.randn(h, 1, d, device=dev, generator=g) * 0.5**0.5
+        L.kmin = torch.empty((h, nblk, d), dtype=torch.bfloat16, device=dev)
         L.kmax = torch.empty_like(L.kmin)
-        L.records = K.pack_int8(kv, kmin=L.kmin, kmax=L.kmax)  # [nblk, h, W], local block ids
-        q_base = torch.randn(HQ, D, device=dev, generator=g)
-        L.q_ring = (q_base[None] + drift * torch.randn(n_q, HQ, D, device=dev, generator=g)).bfloat16()
+        L.records = torch.empty((nblk, h, K.packed_pair_bytes(BS, d)), dtype=torch.uint8, device=dev)  # local block ids
+        kv_all = []
+        sink = None
+        for c0 in range(0, nblk, chunk):
+            c1 = min(nblk, c0 + chunk)
+            kv = torch.randn(c1 - c0, h, 2, BS, d, device=dev, generator=g)
+            kv[:, :, 0] += off.view(1, h, 1, d)
+            kv = kv.bfloat16()
+            K.pack_int8(kv, records=L.records[c0:c1], kmin=L.kmin, kmax=L.kmax, first_block=c0)
+            if c0 == 0:
+                sink = kv[0].clone()
+            if keep_source:
+                kv_all.append(kv)
+            del kv
+        q_base = torch.randn(hq, d, device=dev, generator=g)
+        L.q_ring = (q_base[None] + drift * torch.randn(n_q, hq, d, device=dev, generator=g)).bfloat16()
         L.q = L.q_ring[0]
         # Hot list [sink slot?, admitted slots..., current slot?] and the bitmap of the cold pass.
-        L.list = torch.zeros((HKV, n_list), dtype=torch.int32, device=dev)
+        L.list = torch.zeros((h, n_list), dtype=torch.int32, device=dev)
         if has_cur:
             L.list[:, -1] = k_local + 1
-        L.chosen = torch.zeros((HKV, k_local), dtype=torch.int32, device=dev)  # the selection, local block ids ascending
+        L.chosen = torch.zeros((h, k_local), dtype=torch.int32, device=dev)  # the selection, local block ids ascending
         L.words = K.bitmap_words(nblk + 1)
-        L.bitmap = torch.zeros((HKV, L.words), dtype=torch.int32, device=dev)
-        L.pool = torch.zeros((k_local + 2, HKV, 2, BS, D), dtype=torch.bfloat16, device=dev)
+        L.bitmap = torch.zeros((h, L.words), dtype=torch.int32, device=dev)
+        L.pool = torch.zeros((k_local + 2, h, 2, BS, d), dtype=torch.bfloat16, device=dev)
         if has_sink:
-            L.pool[0] = kv[0]  # the sink stays exact
+            L.pool[0] = sink  # the sink stays exact
         if has_cur:
-            L.pool[k_local + 1] = torch.randn(HKV, 2, BS, D, device=dev, generator=g).bfloat16()
+            L.pool[k_local + 1] = torch.randn(h, 2, BS, d, device=dev, generator=g).bfloat16()
         # Residency tables (lazykv/tiered.py:281-288): nothing resident yet; the first step admits.
-        L.block_slot = torch.full((HKV, nblk), -1, dtype=torch.int32, device=dev)
-        L.slot_block = torch.full((HKV, k_local), -1, dtype=torch.int32, device=dev)
-        L.last_used = torch.full((HKV, k_local), -2, dtype=torch.int64, device=dev)
-        L.evicted_at = torch.full((HKV, nblk), NEVER, dtype=torch.int64, device=dev)
-        L.miss_blk = torch.zeros((HKV, k_local), dtype=torch.int32, device=dev)
-        L.miss_slot = torch.zeros((HKV, k_local), dtype=torch.int32, device=dev)
-        L.n_miss = torch.zeros((HKV,), dtype=torch.int32, device=dev)
-        L.kv = kv if keep_source else None
+        L.block_slot = torch.full((h, nblk), -1, dtype=torch.int32, device=dev)
+        L.slot_block = torch.full((h, k_local), -1, dtype=torch.int32, device=dev)
+        L.last_used = torch.full((h, k_local), -2, dtype=torch.int64, device=dev)
+        L.evicted_at = torch.full((h, nblk), NEVER, dtype=torch.int64, device=dev)
+        L.miss_blk = torch.zeros((h, k_local), dtype=torch.int32, device=dev)
+        L.miss_slot = torch.zeros((h, k_local), dtype=torch.int32, device=dev)
+        L.n_miss = torch.zeros((h,), dtype=torch.int32, device=dev)
+        L.kv = torch.cat(kv_all) if keep_source else None
         L.cur = L.pool[k_local + 1].clone() if keep_source and has_cur else None
-        del kv
+        del kv_all, sink
         if world == 1:
-            L.out = torch.empty((HQ, D), dtype=torch.bfloat16, device=dev)
-            L.lse = torch.empty((HQ,), dtype=torch.float32, device=dev)
+            L.out = torch.empty((hq, d), dtype=torch.bfloat16, device=dev)
+            L.lse = torch.empty((hq,), dtype=torch.float32, device=dev)
             L.packed = None
         else:
             # One buffer per layer, out then lse: one all-gather per layer, merged in place.
             from lazykv_b200.sharded import PackedPartial
 
-            L.packed = PackedPartial(HQ, D, world, dev)
+            L.packed = PackedPartial(hq, d, world, dev)
             L.out, L.lse = L.packed.out, L.packed.lse
         L.records_host = None
         layers.append(L)
     torch.cuda.synchronize(dev)
     geo = dict(nb=nb, n_sealed=n_sealed, k_total=k_total, k_local=k_local, lo=lo, hi=hi, cand_lo=cand_lo, n_cand=n_cand, n_list=n_list,
-               sel_off=sel_off, scale=scale, has_cur=has_cur, n_q=n_q)
+               sel_off=sel_off, scale=scale, has_cur=has_cur, n_q=n_q, h=h, hq=hq, d=d, global_select=global_select)
     return layers, geo
 
 
@@ -263,7 +293,8 @@ def attention_call(L, geo: dict, r: int = 0, cold_store=None) -> None:  # noqa: 
     """Hot pass over the listed slots, cold pass over the bitmap's complement, merge: one launch."""
     from lazykv_b200 import kernels as K
 
-    K.exact_attention(L.q_ring[r], L.pool, L.pool[:, :, 1], (HKV * 2 * BS * D, 2 * BS * D, D), L.list, BS, L.records if cold_store is None else cold_store,
+    h, d = geo["h"], geo["d"]
+    K.exact_attention(L.q_ring[r], L.pool, L.pool[:, :, 1], (h * 2 * BS * d, 2 * BS * d, d), L.list, BS, L.records if cold_store is None else cold_store,
                       geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["scale"], BS, excluded=L.bitmap, out=L.out, lse=L.lse)
 
 
@@ -300,52 +331,60 @@ def layer_step(L, geo: dict, r: int = 0, step: int = 1, cold_store=None, events:
 LAUNCHES_PER_LAYER_STEP = 5  # the selection (TMA scoring, a cluster select per head), the admit and the fetch of misses, the attention (both passes and their merge)
 
 
-def dequant_records(records, dtype):  # noqa: ANN001, ANN201
-    """[n, h, 2368] int8 records -> [n, h, 2, bs, d] in `dtype`, restated in torch from the record
+def dequant_records(records, dtype, d: int = D):  # noqa: ANN001, ANN201
+    """[n, h, W] int8 records -> [n, h, 2, bs, d] in `dtype`, restated in torch from the record
     layout (kq | vq | k scale | k zero | v scale | v zero; lazykv/quant.py:90-105): (code + 128) *
     scale + zero in float32, then rounded to the model dtype. Used only to check the kernels' output."""
     import torch
 
     n, h, _ = records.shape
     r = records.reshape(n * h, -1)
-    nk = BS * D
-    kq = r[:, :nk].contiguous().view(torch.int8).view(-1, BS, D).float()
-    vq = r[:, nk : 2 * nk].contiguous().view(torch.int8).view(-1, BS, D).float()
+    nk = BS * d
+    kq = r[:, :nk].contiguous().view(torch.int8).view(-1, BS, d).float()
+    vq = r[:, nk : 2 * nk].contiguous().view(torch.int8).view(-1, BS, d).float()
     o = 2 * nk
-    ks = r[:, o : o + 2 * D].contiguous().view(torch.float16).float()
-    kz = r[:, o + 2 * D : o + 4 * D].contiguous().view(torch.float16).float()
-    vs = r[:, o + 4 * D : o + 4 * D + 2 * BS].contiguous().view(torch.float16).float()
-    vz = r[:, o + 4 * D + 2 * BS : o + 4 * D + 4 * BS].contiguous().view(torch.float16).float()
+    ks = r[:, o : o + 2 * d].contiguous().view(torch.float16).float()
+    kz = r[:, o + 2 * d : o + 4 * d].contiguous().view(torch.float16).float()
+    vs = r[:, o + 4 * d : o + 4 * d + 2 * BS].contiguous().view(torch.float16).float()
+    vz = r[:, o + 4 * d + 2 * BS : o + 4 * d + 4 * BS].contiguous().view(torch.float16).float()
     k = (kq + 128.0) * ks[:, None, :] + kz[:, None, :]
     v = (vq + 128.0) * vs[:, :, None] + vz[:, :, None]
-    return torch.stack([k, v], dim=1).to(dtype).view(n, h, 2, BS, D)
+    return torch.stack([k, v], dim=1).to(dtype).view(n, h, 2, BS, d)
 
 
-def shard_reference(L, geo: dict, r: int = 0):  # noqa: ANN001, ANN201
-    """float64 (out [HQ, D], lse [HQ]) of this rank's shard of one layer for query r, from the layer's
-    stores with torch on the device: the sink (exact, in the pool) on rank 0, every candidate block as
-    its record dequantised to bf16 (what the hot slots and the cold pass both hold), and the current
-    block (exact) on the last rank; softmax attention in float64. Independent of the kernels."""
+def shard_reference(L, geo: dict, r: int = 0, rows: list | None = None):  # noqa: ANN001, ANN201
+    """float64 (out [rows * G, d], lse [rows * G]) of this rank's shard of one layer for query r, for
+    the KV rows `rows` (all by default), from the layer's stores with torch on the device: the sink
+    (exact, in the pool) on rank 0, every candidate block as its record dequantised to bf16 (what the
+    hot slots and the cold pass both hold), and the current block (exact) on the last rank; softmax
+    attention in float64. Independent of the kernels."""
     import torch
 
+    h, hq, d = geo["h"], geo["hq"], geo["d"]
+    g = hq // h
+    rows = list(range(h)) if rows is None else list(rows)
+    ri = torch.tensor(rows, device=L.records.device)
     c0 = geo["cand_lo"] - geo["lo"]
-    deq = dequant_records(L.records[c0 : c0 + geo["n_cand"]], torch.bfloat16)  # [n, h, 2, bs, d]
+    deq = dequant_records(L.records[c0 : c0 + geo["n_cand"]].index_select(1, ri), torch.bfloat16, d)  # [n, rows, 2, bs, d]
     parts = []
     if geo["sel_off"]:
-        parts.append(L.pool[0].unsqueeze(0))
+        parts.append(L.pool[0].index_select(0, ri).unsqueeze(0))
     parts.append(deq)
     if geo["has_cur"]:
-        parts.append(L.pool[geo["k_local"] + 1].unsqueeze(0))
-    blocks = torch.cat(parts, dim=0).double()  # [m, h, 2, bs, d]
-    keys = blocks[:, :, 0].permute(1, 0, 2, 3).reshape(HKV, -1, D)
-    vals = blocks[:, :, 1].permute(1, 0, 2, 3).reshape(HKV, -1, D)
-    q = L.q_ring[r].double().view(HKV, HQ // HKV, D)
-    s = torch.einsum("hgd,htd->hgt", q, keys) * geo["scale"]
-    m = s.amax(dim=-1, keepdim=True)
-    p = torch.exp(s - m)
+        parts.append(L.pool[geo["k_local"] + 1].index_select(0, ri).unsqueeze(0))
+    blocks = torch.cat(parts, dim=0).double()  # [m, rows, 2, bs, d]
+    del deq, parts
+    nr = len(rows)
+    keys = blocks[:, :, 0].permute(1, 0, 2, 3).reshape(nr, -1, d)
+    vals = blocks[:, :, 1].permute(1, 0, 2, 3).reshape(nr, -1, d)
+    del blocks
+    q = L.q_ring[r].view(h, g, d).index_select(0, ri).double()
+    s_ = torch.einsum("hgd,htd->hgt", q, keys) * geo["scale"]
+    m = s_.amax(dim=-1, keepdim=True)
+    p = torch.exp(s_ - m)
     l = p.sum(dim=-1, keepdim=True)
-    out = torch.einsum("hgt,htd->hgd", p / l, vals).reshape(HQ, D)
-    lse = (m + torch.log(l)).reshape(HQ)
+    out = torch.einsum("hgt,htd->hgd", p / l, vals).reshape(nr * g, d)
+    lse = (m + torch.log(l)).reshape(nr * g)
     return out, lse
 
 
@@ -474,6 +513,7 @@ def run_ours(args: argparse.Namespace) -> None:
         with torch.cuda.graph(gph):
             token(r, step_no + 1 + r)
         graphs.append(gph)
+    del gph  # the graphs hold NCCL work at N > 1: only `graphs` may keep them, so that dropping it frees them
     ring_pos = [0]
 
     def run() -> None:
@@ -570,7 +610,7 @@ def run_ours(args: argparse.Namespace) -> None:
             misses += L.n_miss.sum()
     torch.cuda.synchronize()
     miss_pairs = float(misses.item()) / (R * len(layers))
-    hit_rate = 1.0 - miss_pairs / (HKV * geo["k_local"])
+    hit_rate = 1.0 - miss_pairs / (geo["h"] * geo["k_local"])
 
     # Correctness of what was timed: a fresh token (query 0), layer 0's merged output against a
     # float64 restatement over every rank's shard, gathered to every rank; and the status word of the
@@ -715,6 +755,8 @@ def run_ours(args: argparse.Namespace) -> None:
                                     "attention_us": round(cu, 1), "link_gbs": round(bytes_cold / (cu * 1e-6) / 1e9, 2),
                                     "link_peak_gbs": link, "link_peak_source": "measured by this run: pinned host -> device copy of 1 GiB, best of 5, CUDA events"}
 
+    if not args.no_long_ctx:
+        result["long_ctx"] = run_long_ctx(args, rank, world, dev, timed)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, budget_s=12.0)
     if rank == 0:
@@ -729,6 +771,208 @@ def run_ours(args: argparse.Namespace) -> None:
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
+
+
+# The long-context leg: 8 sequences of 1,048,576 tokens with Llama-3.1-8B attention shapes (32 query
+# heads, 8 KV heads, head_dim 128) in 16-token blocks, 25% of each (sequence, KV head)'s blocks hot.
+# The 8 sequences' KV heads are the kernels' 64 rows (rows are independent in the selection, the
+# admit and the attention), their query heads the 256 query rows.
+LONG_SEQS, LONG_CTX = 8, 1 << 20
+LONG_SHAPE = dict(ctx=LONG_CTX, h=8 * LONG_SEQS, hq=32 * LONG_SEQS, d=128, budget=0.25, queries=4, drift=0.15, seed=4321)
+LONG_MODEL_LAYERS = 32
+
+
+def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) -> dict:  # noqa: ANN001
+    """The long-context leg at this world size: `--long-layers` layers sharded by block range over
+    the ranks, the top-K chosen globally across shards at N > 1 (every rank's bounds all-gathered,
+    the same select on every rank, each admitting and attending its part), the int8 cold tier in
+    HBM, a fresh query of the ring each step, the partials all-gathered and merged per layer. Each
+    layer holds its own stores (about 30 GB at N = 1), so no layer-step reads another's data from
+    L2. Reported per layer-step and as decode tokens/s of the 32-layer model (8 sequences per step,
+    32 layer-steps each at the measured time)."""
+    import torch
+    import torch.distributed as dist
+
+    from lazykv_b200 import kernels as K
+    from lazykv_b200.sharded import GlobalSelection, shard_plan
+
+    shape = dict(LONG_SHAPE, layers=args.long_layers)
+    glob = world > 1
+    t_build = time.perf_counter()
+    layers, geo = build_layers(args, rank, world, dev, shape=shape, global_select=glob)
+    build_s = time.perf_counter() - t_build
+    h, hq, d = geo["h"], geo["hq"], geo["d"]
+    R = geo["n_q"]
+    gsel = None
+    if glob:
+        plans = [shard_plan(geo["n_sealed"], geo["k_total"], world, r) for r in range(world)]
+        gsel = GlobalSelection(plans, rank, h, geo["k_total"], dev)
+    finals = [torch.empty((hq, d), dtype=torch.bfloat16, device=dev) for _ in layers]
+
+    def select_admit(L, r: int, step: int) -> None:  # noqa: ANN001
+        if gsel is None:
+            select_admit_call(L, geo, r, step)
+        else:
+            gsel.select(L.q_ring[r], L.kmin, L.kmax, L.chosen, L.bitmap)
+            admit_call(L, geo, step)
+
+    def token(r: int, step_no: int) -> None:
+        for i, L in enumerate(layers):
+            select_admit(L, r, step_no)
+            attention_call(L, geo, r)
+            if world > 1:
+                L.packed.exchange()
+                L.packed.merge(torch.bfloat16, out=finals[i])
+
+    step_no = 0
+    for w in range(max(args.warmup, R)):
+        step_no += 1
+        token(w % R, step_no)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        token(0, step_no + 1)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graphs = []
+    for r in range(R):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph):
+            token(r, step_no + 1 + r)
+        graphs.append(gph)
+    del gph  # the graphs hold NCCL work at N > 1: only `graphs` may keep them, so that dropping it frees them
+    pos = [0]
+
+    def run() -> None:
+        graphs[pos[0] % R].replay()
+        pos[0] += 1
+
+    for _ in range(max(args.warmup, R)):
+        run()
+    torch.cuda.synchronize()
+    n_steps = args.long_steps
+    with Clocks(dev.index) as clocks:
+        clocks.wait_first_sample(2.0)
+        for _ in range(2 * R):
+            run()
+        ms = timed(run, n_steps)
+        for _ in range(2 * R):
+            run()
+        torch.cuda.synchronize()
+    ms_step = ms / n_steps
+    us_layer = ms_step * 1e3 / len(layers)
+
+    # Per kernel group, eager, layer 0 (the device-side split of one layer-step; max over ranks).
+    def ev_pair():
+        return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    sel_ms, att_ms = [], []
+    for r in range(R):
+        step_no += 1
+        (a, b), (c, e) = ev_pair(), ev_pair()
+        a.record()
+        select_admit(layers[0], r, step_no)
+        b.record()
+        c.record()
+        attention_call(layers[0], geo, r)
+        e.record()
+        e.synchronize()
+        sel_ms.append(a.elapsed_time(b))
+        att_ms.append(c.elapsed_time(e))
+    k_us = torch.tensor([statistics.median(sel_ms) * 1e3, statistics.median(att_ms) * 1e3], device=dev)
+    if world > 1:
+        dist.all_reduce(k_us, op=dist.ReduceOp.MAX)
+
+    # Residency over the ring, and how many blocks each row selected on this rank.
+    misses = torch.zeros((), dtype=torch.int64, device=dev)
+    chosen = torch.zeros((), dtype=torch.int64, device=dev)
+    for r in range(R):
+        step_no += 1
+        for L in layers:
+            select_admit(L, r, step_no)
+            misses += L.n_miss.sum()
+            chosen += (L.chosen >= 0).sum()
+    # The rows' selections add up to K on every row (global), or are the local budget.
+    per_row = (layers[0].chosen >= 0).sum(dim=1).to(torch.int64)
+    tot = torch.stack([misses, chosen]).to(torch.float64)
+    if world > 1:
+        dist.all_reduce(per_row)
+        dist.all_reduce(tot)
+    k_ok = bool((per_row == geo["k_total"]).all()) if glob else True
+    miss_pairs = float(tot[0].item()) / (R * len(layers))  # all ranks
+    sel_pairs = float(tot[1].item()) / (R * len(layers))
+    hit_rate = 1.0 - miss_pairs / max(1.0, sel_pairs)
+
+    # Parity of what was timed: a fresh token with query 0, layer 0's merged output on KV rows 0 and
+    # h - 1 (the first and the last sequence) against the float64 restatement over every shard.
+    step_no += 1
+    token(0, step_no)
+    torch.cuda.synchronize()
+    rows = [0, h - 1]
+    g = hq // h
+    qrows = torch.tensor([r * g + i for r in rows for i in range(g)], device=dev)
+    ref_o, ref_l = shard_reference(layers[0], geo, 0, rows=rows)
+    got = (finals[0] if world > 1 else layers[0].out).index_select(0, qrows)
+    if world > 1:
+        packed = torch.cat([ref_o, ref_l[:, None]], dim=1).contiguous()
+        allp = torch.empty((world, *packed.shape), dtype=packed.dtype, device=dev)
+        dist.all_gather_into_tensor(allp, packed)
+        parts = [(allp[r, :, :d], allp[r, :, d]) for r in range(world)]
+    else:
+        parts = [(ref_o, ref_l)]
+    parity = parity_check(got, parts)
+    status = max(K.status_poll(clear=True), K.device_status(clear=True))
+    flags = torch.tensor([status, int(not parity["ok"]), int(not k_ok)], device=dev)
+    if world > 1:
+        dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+    parity.update(kv_rows=rows, device_status=int(flags[0].item()), global_k_ok=not bool(flags[2].item()))
+    parity["ok"] = not bool(flags[1].item()) and int(flags[0].item()) == 0 and parity["global_k_ok"]
+    del ref_o, ref_l, parts
+
+    # Algorithmic bytes of one layer-step, summed over the ranks: the metadata, the selected blocks
+    # (bf16 slots) and the sink/current blocks, the other candidates' int8 records, the fetch of misses.
+    rec_w = K.packed_pair_bytes(BS, d)
+    pair_b = 2 * BS * d * 2
+    n_cand_all = geo["n_sealed"] - 1
+    sel_rows = sel_pairs  # selected (block, row) pairs per layer-step, all ranks
+    bytes_layer = (h * n_cand_all * d * 2 * 2 + (sel_rows + 2 * h) * pair_b + (h * n_cand_all - sel_rows) * rec_w
+                   + miss_pairs * (rec_w + pair_b))
+    peaks = load_peaks()
+    achieved = bytes_layer / (us_layer * 1e-6) / 1e9
+    mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
+    out = {
+        "workload": f"{LONG_SEQS} sequences x {LONG_CTX} tokens, Llama-3.1-8B attention (32q/8kv/d128; the 8 sequences' KV heads as 64 rows), "
+                    f"bs 16, 25% budget (K={geo['k_total']} blocks per row), int8 cold tier in HBM, device admit, a fresh query each step",
+        "selection": "global top-K: every rank's bounds all-gathered (bf16), the same select on every rank (lkv_topk_gathered)" if glob
+                     else "single GPU (lkv_quest_topk_admit)",
+        "value": round(LONG_SEQS / (LONG_MODEL_LAYERS * us_layer * 1e-6), 3),
+        "unit": "tokens/s",
+        "value_rule": f"decode tokens/s of the {LONG_MODEL_LAYERS}-layer model: {LONG_SEQS} tokens per step, {LONG_MODEL_LAYERS} layer-steps "
+                      f"at the measured layer-step time ({len(layers)} layers held and timed, each with its own stores)",
+        "us_per_layer_step": round(us_layer, 2),
+        "layers_timed": len(layers),
+        "steps": n_steps,
+        "ms_per_step_timed_layers": round(ms_step, 3),
+        "kernel_us": {"select_admit": round(float(k_us[0].item()), 1), "attention": round(float(k_us[1].item()), 1)},
+        "residency": {"hit_rate": round(hit_rate, 4), "fetched_pairs_per_layer_step": round(miss_pairs, 1)},
+        "layer_step_roofline": {"algorithmic_bytes": int(bytes_layer), "achieved_gbs": round(achieved, 1), "peak": peaks["hbm_gbs"] * world,
+                                "frac": round(achieved / (peaks["hbm_gbs"] * world), 4), "peak_rule": "measured HBM copy GB/s x GPUs"},
+        "parity": parity,
+        "clocks": clocks.summary(),
+        "build_s": round(build_s, 1),
+        "max_memory_gb_rank0": round(mem_gb, 1),
+        "timing": "one CUDA graph per query of the ring (selection, admit, attention per layer; at N > 1 the bounds and partials all-gathers "
+                  "captured too), CUDA events over the timed steps, max over ranks",
+    }
+    del graphs, run
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    return out
 
 
 def measure_link_gbs(dev) -> float:  # noqa: ANN001

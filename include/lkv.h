@@ -150,6 +150,33 @@ int lkv_topk_merge(const float* bounds, const int32_t* ids, int h, int n, int64_
                    int bitmap_words, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The Quest bound of every candidate, and nothing else (the scoring half of lkv_quest_topk;
+ * lazykv/selection.py:38-53, quest_bound, computes the same scores): bounds[j*bounds_ld + i] is
+ * candidate first_block + i's bound for KV head j, computed and rounded exactly as lkv_quest_topk
+ * ranks it (bound_mode), stored as bounds_dtype (bf16 only in the bf16 bound mode, where it is
+ * exact; or float32). One launch, no workspace. A shard's input to lkv_topk_gathered.
+ */
+int lkv_quest_bounds(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
+                     const void* kmax, int meta_dtype, int64_t m_head, int first_block, int n_cand,
+                     int bound_mode, void* bounds, int bounds_dtype, int64_t bounds_ld,
+                     void* stream);
+
+/*
+ * Global top-k of a context-sharded layer from every shard's bounds (no reference counterpart;
+ * the reference is single-device): bounds [world][h][ld] as all-gathered from lkv_quest_bounds,
+ * rank r holding seg_n[r] candidates that follow rank r-1's in block order. The selection is the
+ * k highest bounds over all ranks, ties at the k-th bound to the lower block ids: the set
+ * lkv_quest_topk picks over the unsharded candidates. Every rank computes it from the same
+ * gathered bounds; this call writes rank `rank`'s part: out_local [h, out_ld] gets, per head, the
+ * chosen candidates of that rank as local ids (out_base + index within the rank) in ascending
+ * order, then -1 up to out_cols (out_cols >= min(k, seg_n[rank])); the bitmap (optional) is
+ * cleared and set at those local ids. world <= 64. One launch of one CTA per head, no workspace.
+ */
+int lkv_topk_gathered(const void* bounds, int bounds_dtype, int world, int h, int64_t ld,
+                      const int32_t* seg_n, int k, int rank, int out_base, int32_t* out_local,
+                      int out_ld, int out_cols, uint32_t* bitmap, int bitmap_words, void* stream);
+
+/*
  * Split decode attention over listed blocks, emitting (normalised out, lse). Replaces the gather
  * + SDPA + GPU log-sum-exp of lazykv/tiered.py:465-487, lazykv/attention.py:97-136 and
  * lazykv/exact.py:380-393.

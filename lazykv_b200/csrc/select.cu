@@ -167,11 +167,13 @@ __device__ __forceinline__ float row_bound(const unsigned char* tile_max, const 
 
 // hist0 (optional, [h][256], zero on entry): per KV head, the count of keys by the top 8 bits of the
 // orderable bound, i.e. the first radix pass of the select, accumulated with one global atomic per
-// non-empty bin and CTA.
+// non-empty bin and CTA. keys (optional) [h][n_cand]; the bounds (optional) go to out_bound (float32)
+// or out_bound16 (bf16, bf16 bound mode only) with row stride bound_ld.
 template <typename TQ, typename TM, int G>
 __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __restrict__ kmin, const TM* __restrict__ kmax,
                                    int64_t m_head, int first_block, int n_cand, int bound_mode, uint64_t* __restrict__ keys,
-                                   float* __restrict__ out_bound, uint32_t* __restrict__ hist0) {
+                                   float* __restrict__ out_bound, uint32_t* __restrict__ hist0, __nv_bfloat16* __restrict__ out_bound16,
+                                   int64_t bound_ld) {
   __shared__ uint32_t sh_hist[256];
   extern __shared__ __align__(16) float qs[];  // q+ [d][GP], q- [d][GP], then the two tiles
   const int rows = blockDim.x;
@@ -203,8 +205,10 @@ __global__ void quest_score_kernel(const TQ* __restrict__ q, int d, const TM* __
     const float best = row_bound<TQ, TM, G>(tile_max, tile_min, t, d, qs, bound_mode);
     const int ci = c_first + t;
     const uint32_t ob = orderable(best);
-    keys[(int64_t)j * n_cand + ci] = ((uint64_t)ob << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
-    if (out_bound != nullptr) out_bound[(int64_t)j * n_cand + ci] = best == 0.0f ? 0.0f : best;
+    if (keys != nullptr) keys[(int64_t)j * n_cand + ci] = ((uint64_t)ob << 32) | (uint64_t)(0xffffffffu - (uint32_t)ci);
+    const float nb = best == 0.0f ? 0.0f : best;
+    if (out_bound != nullptr) out_bound[(int64_t)j * bound_ld + ci] = nb;
+    if (out_bound16 != nullptr) out_bound16[(int64_t)j * bound_ld + ci] = __float2bfloat16_rn(nb);  // exact: a bf16-rounded bound
     digit = ob >> 24;
   }
   if (hist0 == nullptr) return;
@@ -962,7 +966,9 @@ __global__ void merge_keys_kernel(const float* __restrict__ bounds, const int32_
 
 template <typename TQ, typename TM>
 int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void* kmin, const void* kmax, int64_t m_head, int first_block,
-                 int n_cand, int bound_mode, uint64_t* keys, float* out_bound, uint32_t* hist0) {
+                 int n_cand, int bound_mode, uint64_t* keys, float* out_bound, uint32_t* hist0, __nv_bfloat16* out_bound16 = nullptr,
+                 int64_t bound_ld = -1) {
+  if (bound_ld < 0) bound_ld = n_cand;
   const int rows = score_rows(d, sizeof(TM));
   dim3 grid((n_cand + rows - 1) / rows, h);
   const size_t smem = 2 * (size_t)(g < 2 ? 2 : g) * d * sizeof(float) + 2 * (size_t)rows * d * sizeof(TM);
@@ -971,7 +977,7 @@ int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void
     auto kern = quest_score_kernel<TQ, TM, G>;                                                                         \
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);          \
     cudaError_t le = launch_pdl(kern, grid, dim3(rows), smem, st, 0, static_cast<const TQ*>(q), d, static_cast<const TM*>(kmin),      \
-                                static_cast<const TM*>(kmax), m_head, first_block, n_cand, bound_mode, keys, out_bound, hist0); \
+                                static_cast<const TM*>(kmax), m_head, first_block, n_cand, bound_mode, keys, out_bound, hist0, out_bound16, bound_ld); \
     if (le != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk(score): %s", cudaGetErrorString(le));             \
     break;                                                                                                             \
   }
@@ -985,6 +991,135 @@ int launch_score(int g, int h, int d, cudaStream_t st, const void* q, const void
   }
 #undef LKV_SCORE
   return LKV_OK;
+}
+
+
+// ---- global top-k over every shard's gathered bounds --------------------------------------------
+//
+// The shards of a context-sharded layer hold contiguous, ascending candidate ranges, rank after
+// rank. Each rank scores its own candidates (lkv_quest_bounds) and the bounds of all ranks are
+// all-gathered into [world][h][ld]; every rank then runs this kernel on the same gathered bounds, so
+// all of them agree on one selection: the k highest bounds of the whole context, ties at the k-th
+// bound to the lower block ids, i.e. the set lkv_quest_topk picks over the unsharded candidates.
+// Each rank writes only its own part: the chosen candidates inside its range, as local ids in
+// ascending order, padded with -1, and its own bitmap.
+//
+// One CTA of kSelectThreads threads per KV head, no shared key copy: MSB-first radix passes over the
+// orderable 32-bit form of the bound (2 for bf16 bounds, 4 for float32), each a histogram of the
+// keys that match the digits found so far; then the number of keys at the threshold in lower ranks
+// (the ties they take first) and a block-wide scan over this rank's range in candidate order.
+constexpr int kMaxWorld = 64;
+
+struct GatherSel {
+  const void* bounds;   // [world][h][ld], bf16 or float32
+  int bf16;             // bounds are bf16
+  int world, h;
+  int64_t ld;           // row stride (elements)
+  int seg_start[kMaxWorld + 1];  // prefix sums of the ranks' candidate counts
+  int k, n_passes, rank;
+  int out_base;         // local id of the rank's first candidate
+  int32_t* out;         // [h][out_ld]
+  int out_ld, out_cols; // columns written (chosen ids, then -1)
+  uint32_t* bitmap;     // [h][bitmap_words] or null
+  int bitmap_words;
+};
+
+__device__ __forceinline__ uint32_t gathered_key(const GatherSel& p, int r, int j, int i) {
+  const int64_t at = ((int64_t)r * p.h + j) * p.ld + i;
+  if (p.bf16) {
+    const uint16_t u = static_cast<const uint16_t*>(p.bounds)[at];
+    return orderable(__uint_as_float((uint32_t)u << 16));
+  }
+  return orderable(static_cast<const float*>(p.bounds)[at]);
+}
+
+__global__ void __launch_bounds__(kSelectThreads) topk_gathered_kernel(const __grid_constant__ GatherSel p) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t warp_sums[32];
+  __shared__ uint32_t sh_digit, sh_remaining, sh_bincount, sh_total, sh_eq_before;
+  const int j = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int n_total = p.seg_start[p.world];
+  const int kk = p.k < n_total ? p.k : n_total;
+  pdl_wait();  // the gathered bounds are the collective's to finish writing
+  pdl_release();
+  if (tid == 0) {
+    sh_remaining = (uint32_t)kk;
+    sh_bincount = 0;
+    sh_eq_before = 0;
+  }
+  uint32_t prefix = 0, mask = 0;
+  bool take_all = kk >= n_total;
+  for (int pass = 0; pass < p.n_passes && !take_all; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int b = tid; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    for (int r = 0; r < p.world; ++r) {
+      const int n_r = p.seg_start[r + 1] - p.seg_start[r];
+      for (int i0 = 0; i0 < n_r; i0 += blockDim.x) {
+        const int i = i0 + tid;
+        const uint32_t key = i < n_r ? gathered_key(p, r, j, i) : 0u;
+        const bool counted = i < n_r && (key & mask) == prefix;
+        const uint32_t digit = counted ? ((key >> shift) & 255u) : 256u;
+        const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+        if (counted && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
+      }
+    }
+    __syncthreads();
+    pick_digit(hist, &sh_digit, &sh_remaining, &sh_bincount);
+    __syncthreads();
+    prefix |= sh_digit << shift;
+    mask |= 255u << shift;
+    take_all = (sh_bincount == sh_remaining);
+    __syncthreads();
+  }
+  const bool all = kk >= n_total;
+  const uint32_t need = take_all ? 0xffffffffu : sh_remaining;  // keys at the threshold to take, lowest ids first
+  // Keys at the threshold in the lower ranks: they come first.
+  if (!all && !take_all) {
+    uint32_t eq = 0;
+    for (int r = 0; r < p.rank; ++r) {
+      const int n_r = p.seg_start[r + 1] - p.seg_start[r];
+      for (int i = tid; i < n_r; i += blockDim.x) eq += (gathered_key(p, r, j, i) & mask) == prefix;
+    }
+    eq = __reduce_add_sync(0xffffffffu, eq);
+    if ((tid & 31) == 0 && eq) atomicAdd(&sh_eq_before, eq);
+  }
+  if (p.bitmap != nullptr)
+    for (int w = tid; w < p.bitmap_words; w += blockDim.x) p.bitmap[(int64_t)j * p.bitmap_words + w] = 0u;
+  __syncthreads();
+  // This rank's range, in candidate order: thread t owns a contiguous piece.
+  const int n_my = p.seg_start[p.rank + 1] - p.seg_start[p.rank];
+  const int seg = (n_my + blockDim.x - 1) / blockDim.x;
+  const int tlo = min(n_my, tid * seg), thi = min(n_my, tlo + seg);
+  uint32_t n_gt = 0, n_eq = 0;
+  for (int i = tlo; i < thi; ++i) {
+    const uint32_t key = gathered_key(p, p.rank, j, i) & mask;
+    n_gt += all || key > prefix;
+    n_eq += !all && key == prefix;
+  }
+  const uint32_t gt_before = block_scan(n_gt, warp_sums, &sh_total);
+  const uint32_t n_gt_all = sh_total;
+  const uint32_t eq_before_t = block_scan(n_eq, warp_sums, &sh_total);
+  const uint32_t e0 = sh_eq_before;
+  const uint32_t room = need == 0xffffffffu ? 0xffffffffu : (e0 < need ? need - e0 : 0u);  // ties this rank may take
+  const uint32_t n_sel = n_gt_all + min(sh_total, room);
+  uint32_t pos = gt_before + min(eq_before_t, room);
+  const uint32_t take_eq = eq_before_t < room ? min(n_eq, room - eq_before_t) : 0u;
+  uint32_t eq_seen = 0;
+  int32_t* out = p.out + (int64_t)j * p.out_ld;
+  for (int i = tlo; i < thi; ++i) {
+    const uint32_t key = gathered_key(p, p.rank, j, i) & mask;
+    bool take = all || key > prefix;
+    if (!take && key == prefix) take = eq_seen++ < take_eq;
+    if (take && pos < (uint32_t)p.out_cols) {
+      const int blk = p.out_base + i;
+      out[pos] = blk;
+      if (p.bitmap != nullptr && blk / 32 < p.bitmap_words) atomicOr(&p.bitmap[(int64_t)j * p.bitmap_words + blk / 32], 1u << (blk % 32));
+      ++pos;
+    }
+  }
+  for (int c = (int)n_sel + tid; c < p.out_cols; c += blockDim.x) out[c] = -1;
 }
 
 }  // namespace
@@ -1167,6 +1302,78 @@ int lkv_topk_merge(const float* bounds, const int32_t* ids, int h, int n, int64_
   topk_kernel<<<h, kSelectThreads, smem, st>>>(keys, n, k, 0, out_blocks, out_ld, bitmap, bitmap_words, stage_keys, order == LKV_ORDER_BLOCK,
                                                 bound_mode == LKV_BF16 ? 2 : 4);
   return launched("lkv_topk_merge(select)");
+}
+
+int lkv_quest_bounds(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax, int meta_dtype, int64_t m_head,
+                     int first_block, int n_cand, int bound_mode, void* bounds, int bounds_dtype, int64_t bounds_ld, void* stream) {
+  if (!dtype_ok(q_dtype) || !dtype_ok(meta_dtype) || !dtype_ok(bound_mode) || !dtype_ok(bounds_dtype))
+    return fail(LKV_ERR_ARG, "lkv_quest_bounds: bad dtype (q %d, meta %d, bound %d, out %d)", q_dtype, meta_dtype, bound_mode, bounds_dtype);
+  if (bounds_dtype == LKV_BF16 && bound_mode != LKV_BF16) return fail(LKV_ERR_ARG, "lkv_quest_bounds: float32 bounds do not fit bf16 output");
+  if (h <= 0 || hq <= 0 || hq % h != 0) return fail(LKV_ERR_ARG, "lkv_quest_bounds: %d query heads do not group over %d KV heads", hq, h);
+  if (d <= 0 || d % 8 != 0 || d > 256) return fail(LKV_ERR_ARG, "lkv_quest_bounds: head_dim %d unsupported", d);
+  if (n_cand <= 0 || first_block < 0 || bounds_ld < n_cand)
+    return fail(LKV_ERR_ARG, "lkv_quest_bounds: need n_cand > 0, first_block >= 0, bounds_ld >= n_cand (%d, %d, %lld)", n_cand, first_block,
+                (long long)bounds_ld);
+  if (q == nullptr || kmin == nullptr || kmax == nullptr || bounds == nullptr) return fail(LKV_ERR_PTR, "lkv_quest_bounds: null pointer");
+  if (!aligned(kmin, 16) || !aligned(kmax, 16) || (m_head * (int64_t)dtype_size(meta_dtype)) % 16 != 0)
+    return fail(LKV_ERR_PTR, "lkv_quest_bounds: metadata rows must be 16-byte aligned");
+  const int g = hq / h;
+  cudaStream_t st = as_stream(stream);
+  float* b32 = bounds_dtype == LKV_F32 ? static_cast<float*>(bounds) : nullptr;
+  __nv_bfloat16* b16 = bounds_dtype == LKV_BF16 ? static_cast<__nv_bfloat16*>(bounds) : nullptr;
+  int rc;
+  if (q_dtype == LKV_BF16 && meta_dtype == LKV_BF16)
+    rc = launch_score<__nv_bfloat16, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, nullptr, b32, nullptr, b16, bounds_ld);
+  else if (q_dtype == LKV_F32 && meta_dtype == LKV_F32)
+    rc = launch_score<float, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, nullptr, b32, nullptr, b16, bounds_ld);
+  else if (q_dtype == LKV_BF16 && meta_dtype == LKV_F32)
+    rc = launch_score<__nv_bfloat16, float>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, nullptr, b32, nullptr, b16, bounds_ld);
+  else
+    rc = launch_score<float, __nv_bfloat16>(g, h, d, st, q, kmin, kmax, m_head, first_block, n_cand, bound_mode, nullptr, b32, nullptr, b16, bounds_ld);
+  if (rc) return rc;
+  return launched("lkv_quest_bounds");
+}
+
+int lkv_topk_gathered(const void* bounds, int bounds_dtype, int world, int h, int64_t ld, const int32_t* seg_n, int k, int rank, int out_base,
+                      int32_t* out_local, int out_ld, int out_cols, uint32_t* bitmap, int bitmap_words, void* stream) {
+  if (bounds_dtype != LKV_BF16 && bounds_dtype != LKV_F32) return fail(LKV_ERR_ARG, "lkv_topk_gathered: bounds must be bf16 or float32");
+  if (world <= 0 || world > kMaxWorld || rank < 0 || rank >= world) return fail(LKV_ERR_ARG, "lkv_topk_gathered: rank %d of %d (at most %d)", rank, world, kMaxWorld);
+  if (h <= 0 || k <= 0 || out_base < 0 || seg_n == nullptr) return fail(LKV_ERR_ARG, "lkv_topk_gathered: need h, k > 0, out_base >= 0, counts");
+  if (bounds == nullptr || out_local == nullptr) return fail(LKV_ERR_PTR, "lkv_topk_gathered: null pointer");
+  GatherSel p{};
+  p.seg_start[0] = 0;
+  for (int r = 0; r < world; ++r) {
+    if (seg_n[r] < 0 || seg_n[r] > ld) return fail(LKV_ERR_ARG, "lkv_topk_gathered: rank %d has %d candidates (row stride %lld)", r, seg_n[r], (long long)ld);
+    if ((int64_t)p.seg_start[r] + seg_n[r] > INT32_MAX) return fail(LKV_ERR_ARG, "lkv_topk_gathered: too many candidates");
+    p.seg_start[r + 1] = p.seg_start[r] + seg_n[r];
+  }
+  if (p.seg_start[world] <= 0) return fail(LKV_ERR_ARG, "lkv_topk_gathered: no candidates");
+  const int n_my = seg_n[rank];
+  const int most = k < n_my ? k : n_my;  // at most this many of the chosen fall in this rank's range
+  if (out_cols < most || out_ld < out_cols)
+    return fail(LKV_ERR_ARG, "lkv_topk_gathered: %d output columns (row stride %d) cannot hold up to %d chosen ids", out_cols, out_ld, most);
+  if (bitmap != nullptr && bitmap_words * 32ll < (int64_t)out_base + n_my)
+    return fail(LKV_ERR_ARG, "lkv_topk_gathered: bitmap of %d words cannot hold local block %d", bitmap_words, out_base + n_my - 1);
+  p.bounds = bounds;
+  p.bf16 = bounds_dtype == LKV_BF16;
+  p.world = world;
+  p.h = h;
+  p.ld = ld;
+  p.k = k;
+  p.n_passes = bounds_dtype == LKV_BF16 ? 2 : 4;
+  p.rank = rank;
+  p.out_base = out_base;
+  p.out = out_local;
+  p.out_ld = out_ld;
+  p.out_cols = out_cols;
+  p.bitmap = bitmap;
+  p.bitmap_words = bitmap_words;
+  cudaError_t e = launch_pdl(topk_gathered_kernel, dim3(h), dim3(kSelectThreads), 0, as_stream(stream), 0, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_topk_gathered: %s", cudaGetErrorString(e));
+  }
+  return LKV_OK;
 }
 
 }  // extern "C"

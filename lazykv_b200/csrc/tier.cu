@@ -87,11 +87,13 @@ __global__ void __launch_bounds__(kAdmitThreads) admit_kernel(const int32_t* __r
   if (threadIdx.x == blockDim.x - 1) sh_nfree = pos;
   __syncthreads();
   const int n_free = (int)sh_nfree;
-  for (int i = n_free + threadIdx.x; i < P; i += blockDim.x) keys[i] = ~0ull;
+  int PF = 1;  // only the free slots are sorted: the next power of two above their count
+  while (PF < n_free) PF <<= 1;
+  for (int i = n_free + threadIdx.x; i < PF; i += blockDim.x) keys[i] = ~0ull;
   __syncthreads();
-  for (int size = 2; size <= P; size <<= 1) {
+  for (int size = 2; size <= PF; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < P / 2; i += blockDim.x) {
+      for (int i = threadIdx.x; i < PF / 2; i += blockDim.x) {
         const int a = 2 * i - (i & (stride - 1)), b = a + stride;
         const bool asc = (a & size) == 0;
         const uint64_t x = keys[a], y = keys[b];

@@ -127,6 +127,41 @@ def quest_topk(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, firs
     return out_blocks, bound
 
 
+def quest_bounds(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int, n_cand: int, out: torch.Tensor,
+                 bound_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """The Quest bound of candidates [first_block, first_block + n_cand) into out [h, >= n_cand]
+    (bf16 or float32; bf16 only with bf16 bounds), ranked as quest_topk ranks them; nothing else."""
+    dev = require_cuda(query, kmin, kmax, out)
+    hq, d = query.shape[-3] if query.dim() == 4 else query.shape[0], query.shape[-1]
+    q = query.reshape(hq, d).contiguous()
+    h = kmin.shape[-3]
+    bound_dtype = bound_dtype or q.dtype
+    if out.dim() != 2 or out.shape[0] != h or out.shape[1] < n_cand or out.stride(-1) != 1:
+        raise ValueError(f"quest_bounds: out must be [{h}, >={n_cand}] with unit column stride, got {tuple(out.shape)}")
+    call("lkv_quest_bounds", ptr(q), dtype_code(q.dtype), hq, h, d, ptr(kmin), ptr(kmax), dtype_code(kmin.dtype), kmin.stride(-3), first_block,
+         n_cand, dtype_code(bound_dtype), ptr(out), dtype_code(out.dtype), out.stride(0), stream_handle(dev))
+    return out
+
+
+def topk_gathered(gathered: torch.Tensor, seg_n: list[int], k: int, rank: int, out_base: int, out: torch.Tensor,
+                  bitmap: torch.Tensor | None = None, out_cols: int | None = None) -> torch.Tensor:
+    """Rank `rank`'s part of the global top-k over every rank's bounds gathered as [world, h, ld]
+    (rank r holding seg_n[r] candidates after rank r-1's): out [h, >= out_cols] gets the chosen local
+    ids (out_base + index in the rank), ascending, then -1; the bitmap those ids."""
+    import ctypes
+
+    dev = require_cuda(gathered, out)
+    world, h, ld = gathered.shape
+    if len(seg_n) != world or gathered.stride(-1) != 1 or not gathered.is_contiguous():
+        raise ValueError("topk_gathered: gathered must be a contiguous [world, h, ld] with one count per rank")
+    out_cols = out.shape[-1] if out_cols is None else out_cols
+    counts = (ctypes.c_int32 * world)(*seg_n)
+    words = 0 if bitmap is None else bitmap.shape[-1]
+    call("lkv_topk_gathered", ptr(gathered), dtype_code(gathered.dtype), world, h, ld, ctypes.cast(counts, ctypes.c_void_p), k, rank, out_base,
+         ptr(out), out.stride(0), out_cols, ptr(bitmap), words, stream_handle(dev))
+    return out
+
+
 def attention_workspace_bytes(h: int, hq: int, d: int, n_items: int) -> int:
     return int(L.lib().lkv_attention_workspace(h, hq, d, n_items))
 

@@ -12,10 +12,13 @@ Selection across shards has two modes:
     (`shard_plan`'s k_local, in proportion to its candidates). In the exact tier the output does
     not depend on which blocks are selected (every sealed block is attended once, hot or cold), so
     this is exact and needs no exchange before the attention;
-  * global (`global_topk`): every rank's top-min(K, n_local) candidates with their bounds are
-    all-gathered and every rank runs the same top-K over them (`lkv_topk_merge`), so the selection
-    equals the single-GPU one; each rank then attends the selected blocks of its range (a
-    different count per head: the hot list is padded with -1).
+  * global (`GlobalSelection`): every rank's candidate bounds are all-gathered ([h, n_local]
+    bf16 per rank, a quarter of the bytes of top-K (bound, id) pairs at a 25% budget) and every
+    rank runs the same select over them (`lkv_topk_gathered`), so the selection equals the
+    single-GPU one; each rank then admits and attends the selected blocks of its range (a
+    different count per head: its lists are padded with -1). The candidate form of the same
+    exchange (`local_candidates`, `gather_candidates`, `topk_merge`: top-min(K, n_local)
+    (bound, id) pairs, one CTA per head) is kept for callers that hold only their local top-K.
 """
 
 from __future__ import annotations
@@ -144,6 +147,39 @@ def shard_hot_list(global_ids: torch.Tensor, plan: ShardPlan, k_pad: int | None 
     ids = torch.gather(torch.where(inside, global_ids, torch.full_like(global_ids, -1)), 1, order)
     k_pad = kk if k_pad is None else k_pad
     return ids[:, :k_pad].contiguous()
+
+
+class GlobalSelection:
+    """The global top-k of a context-sharded layer: every rank scores its own candidates into a
+    send buffer [h, ld] (lkv_quest_bounds), one all-gather gives every rank all the bounds
+    [world, h, ld], and every rank runs the same select over them (lkv_topk_gathered), keeping its
+    own part as local ids. The selection is the one lkv_quest_topk makes over the unsharded
+    candidates (ties at the k-th bound to the lower block ids), so the ranks agree and their parts
+    add up to it. The per-rank hot list then holds between 0 and min(k, n_cand) blocks: `cols`."""
+
+    def __init__(self, plans: list[ShardPlan], rank: int, h: int, k_total: int, device: torch.device,
+                 bound_dtype: torch.dtype = torch.bfloat16) -> None:
+        self.plans, self.rank, self.k = plans, rank, k_total
+        self.plan = plans[rank]
+        self.seg_n = [p.n_cand for p in plans]
+        self.ld = max(self.seg_n)
+        self.cols = min(k_total, self.plan.n_cand)
+        self.bound_dtype = bound_dtype
+        self.send = torch.zeros((h, self.ld), dtype=bound_dtype, device=device)
+        self.gathered = torch.zeros((len(plans), h, self.ld), dtype=bound_dtype, device=device)
+
+    def select(self, query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, chosen: torch.Tensor, bitmap: torch.Tensor | None = None,
+               group: dist.ProcessGroup | None = None) -> torch.Tensor:
+        """This rank's part of the global selection of `query` into chosen [h, >= cols] (local ids
+        ascending, then -1) and the bitmap; kmin/kmax are the rank's metadata (local ids)."""
+        p = self.plan
+        first = p.cand_first - p.lo
+        K.quest_bounds(query, kmin, kmax, first, p.n_cand, self.send, self.bound_dtype)
+        if len(self.plans) > 1:
+            dist.all_gather_into_tensor(self.gathered, self.send, group=group)
+        else:
+            self.gathered[0].copy_(self.send)
+        return K.topk_gathered(self.gathered, self.seg_n, self.k, self.rank, first, chosen, bitmap, out_cols=self.cols)
 
 
 class ShardedExactStep:
