@@ -17,9 +17,9 @@
 // cpu_partial_attention does (exact.py:108-110).
 //
 // Three kernels do the partial work:
-//  * attn_stream_kernel (bf16, d 64, bs 16, G <= 8, stores in device memory: the metric geometry):
-//    tensor-core contractions, int8 records dequantised straight into mma fragments, a balanced
-//    split of every segment over one 16-warp CTA per SM, and the fold done by the head's last CTA
+//  * attn_stream_kernel (bf16, d 64 or 128, bs 16, G <= 8, stores in device memory: the metric's
+//    and the long-context geometry): tensor-core contractions, int8 records dequantised straight
+//    into mma fragments, a balanced split of every segment over one CTA per SM, and the fold done by the head's last CTA
 //    (no second launch); described at the kernel;
 //  * attn_tma_kernel (stores in device memory, G = 4, bs = 16, d in {64, 128}): each warp streams
 //    its items through a private ring of shared-memory stages filled by TMA bulk copies
@@ -770,9 +770,24 @@ __global__ void __launch_bounds__(kThreads) attn_tma_kernel(const AttnParams p) 
 // a separate MMA, so the result keeps float32 accuracy. The score fragment becomes the P^T operand
 // with movmatrix (an 8x8 transpose in registers).
 
-constexpr int kMmaTile = 2048;              // 16 x 64 bf16, swizzled
-constexpr int kMmaHotStage = 2 * kMmaTile;  // K tile + V tile
-constexpr int kMmaRec = 2368;               // int8 record at bs 16, d 64
+// The stream kernel's geometry per head_dim (bs 16). A bf16 K or V tile is 16 tokens x D channels
+// in 128-byte swizzled rows of 64 channels: one 2 KiB sub-tile per 64 channels, each its own tile
+// load. An int8 record is K codes [16][D], V codes [16][D], then the K scales and zeros (fp16 [D]
+// each) and the V scales and zeros (fp16 [16] each) (lazykv/quant.py:90-105).
+template <int D>
+struct MmaGeom {
+  static_assert(D == 64 || D == 128, "head_dim");
+  static constexpr int HALVES = D / 64;                 // 64-channel sub-tiles per tile
+  static constexpr int TILE = 16 * D * 2;               // one K or V tile (bytes)
+  static constexpr int HOT = 2 * TILE;                  // K tile + V tile
+  static constexpr int REC = 32 * D + 4 * D + 64;       // int8 record: 2,368 bytes at D 64, 4,672 at D 128
+  static constexpr int OFF_KS = 32 * D, OFF_VS = 36 * D, OFF_VZ = 36 * D + 32;
+  static constexpr int KF = (REC + 127) / 128 * 128;    // the record's K scales, zeros as float32 [D] each
+  static constexpr int STAGE = HOT;                     // a stage holds a tile pair or a record
+  static constexpr int WARPS = D == 64 ? 16 : 8;        // WARPS x 2 stages of ring in shared memory
+  static_assert(KF + 8 * D <= STAGE, "the record and its float32 scales inside one stage");
+};
+constexpr int kMmaRec = MmaGeom<64>::REC;  // int8 record at bs 16, d 64
 
 struct MmaParams {
   AttnParams p;
@@ -845,11 +860,12 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(
 
 // ============================================================================================
 // attn_stream_kernel: balanced, warp-streaming tensor-core split decode
-// (bf16, d = 64, bs = 16, G <= 8, stores in device memory)
+// (bf16, d = 64 or 128, bs = 16, G <= 8, stores in device memory)
 // ============================================================================================
 //
 // Grid: P CTAs per KV head (P = kStreamCtasPerSm x SMs / h, raised when a CTA's items would not
-// fit its list), kStreamWarps warps per CTA.
+// fit its list), MmaGeom<D>::WARPS warps per CTA (16 at d 64, 8 at d 128, so that two stages per
+// warp fit in shared memory).
 //
 // Work split. A head's items are, per segment, the listed blocks (padding counted, then skipped)
 // or the blocks of the range that the exclusion bitmap leaves. CTA i of P takes the i-th P-th of
@@ -860,14 +876,15 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(
 // are written to a shared-memory list as storage rows (list ids through the slot map; range blocks
 // as the complement of the bitmap, placed by a block-wide scan of per-word counts).
 // Streaming (each warp): warp w takes the w-th share of the CTA's items of each segment (segment 0's
-// first); its items pass through its private ring of StreamCfg::STAGES 4 KiB stages that lane 0 fills
-// by TMA (two tile-mode loads of the K and V tiles in the 128-byte swizzle, or one bulk
-// copy of the record) and refills as soon as the item in a stage has been used.
+// first); its items pass through its private ring of StreamCfg::STAGES stages (4 KiB at d 64, 8 KiB
+// at d 128) that lane 0 fills by TMA (tile-mode loads of the K and V tiles in the 128-byte swizzle,
+// one per 64 channels, or one bulk copy of the record) and refills as soon as the item in a stage
+// has been used.
 //
 // Int8 records go from shared memory straight into mma fragments, with a fixed permutation of the
 // channels (the contraction does not depend on the order): for S^T = K . Q^T lane (g, t) holds the
-// 16 channels 16t .. 16t+15 of tokens g and g + 8 (two 16-byte code loads, the K scales of those
-// channels); for O^T += V^T . P^T lane g holds channels 8g .. 8g+7 of tokens 2t, 2t+1, 2t+8, 2t+9
+// D/4 channels (D/4)t .. (D/4)t + D/4 - 1 of tokens g and g + 8 (16-byte code loads, the K scales of
+// those channels); for O^T += V^T . P^T lane g holds channels (D/8)g .. (D/8)g + D/8 - 1 of tokens 2t, 2t+1, 2t+8, 2t+9
 // (four 8-byte loads). The query fragments follow the same permutation and the output channels are
 // put back in order when the state is parked. Each value is (code + 128) * scale + zero in float32
 // (one rounding) and then rounded to bf16: what a fetch would put in a slot (quant.py:103-104).
@@ -878,25 +895,26 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(
 // states into one partial per segment in the workspace; the last CTA of the head (a per-head counter
 // in the workspace, zero before and after the call) folds the head's partials into the outputs.
 
-constexpr int kStreamWarps = 16;
-constexpr int kStreamThreads = 32 * kStreamWarps;
 constexpr int kStreamCtasPerSm = 1;
-constexpr int kStreamStage = 4096;
 constexpr int kStreamListCap = 3072;       // items per CTA
 constexpr int kStreamCounterBytes = 4096;  // per-head CTA counters at the workspace start (h <= 1024)
 
-template <int G>
+template <int G, int D>
 struct StreamCfg {
+  static constexpr int NW = MmaGeom<D>::WARPS;
+  static constexpr int THREADS = 32 * NW;
   static constexpr int STAGES = 2;  // per warp (the loop is unrolled over them)
-  static constexpr int SLOT = G * 64 + 2 * G;    // floats of a parked state: o [G][64], m [G], l [G]
-  static constexpr int RING = kStreamWarps * STAGES * kStreamStage;
-  static constexpr int PARK = kStreamWarps * 2 * SLOT * 4;  // each warp's state per segment
+  static constexpr int STAGE = MmaGeom<D>::STAGE;
+  static constexpr int SLOT = G * D + 2 * G;    // floats of a parked state: o [G][D], m [G], l [G]
+  static constexpr int RING = NW * STAGES * STAGE;
+  static constexpr int PARK = NW * 2 * SLOT * 4;  // each warp's state per segment
   static constexpr int LIST = kStreamListCap * 4;
-  static constexpr int BARS = kStreamWarps * STAGES * 8;
+  static constexpr int BARS = NW * STAGES * 8;
   static constexpr size_t SMEM = 1024 + (size_t)RING + PARK + LIST + BARS;
-  // Floats of one (CTA, set) partial in the workspace: o [G][64], m [G], l [G], padded to 16 bytes so
+  // Floats of one (CTA, set) partial in the workspace: o [G][D], m [G], l [G], padded to 16 bytes so
   // the rows of o are float4-aligned for every G.
-  static constexpr int PART = (G * 64 + 2 * G + 3) / 4 * 4;
+  static constexpr int PART = (G * D + 2 * G + 3) / 4 * 4;
+  static_assert(SMEM <= 227 * 1024, "shared memory of one CTA");
 };
 
 struct StreamParams {
@@ -972,12 +990,14 @@ __device__ __forceinline__ float2 code_pair(uint32_t a, uint32_t c, uint32_t sel
 
 __device__ __forceinline__ float2 h2f2(uint32_t w) { return __half22float2(*reinterpret_cast<const __half2*>(&w)); }
 
-template <int G, typename TO, bool RAGGED>
-__global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_kernel(const __grid_constant__ StreamParams sp) {
+template <int G, int D, typename TO, bool RAGGED>
+__global__ void __launch_bounds__(MmaGeom<D>::WARPS * 32, kStreamCtasPerSm) attn_stream_kernel(const __grid_constant__ StreamParams sp) {
   static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query group");
-  using C = StreamCfg<G>;
-  constexpr int D = 64;
-  constexpr int NW = kStreamWarps;
+  using C = StreamCfg<G, D>;
+  using GM = MmaGeom<D>;
+  constexpr int NW = C::NW;
+  constexpr int KS = D / 16;  // k-steps of S^T = K . Q^T, and m-tiles of O^T
+  constexpr int CH = D / 4;   // channels of a record's K row that lane (g, t) holds
   constexpr int NS = C::STAGES;
   const AttnParams& p = sp.p;
   extern __shared__ unsigned char smem_raw[];
@@ -1044,7 +1064,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     table = sp.table + (int64_t)(j / sp.heads) * sp.table_stride;
   }
   const bool fast = p.n_segs == 2 && S0.kind == SEG_LIST && S1.kind != SEG_LIST &&
-                    (n_seg1 <= 0 || (S1.first_block + n_seg1 - 1) / 32 - S1.first_block / 32 < kSetupWords * kStreamThreads);
+                    (n_seg1 <= 0 || (S1.first_block + n_seg1 - 1) / 32 - S1.first_block / 32 < kSetupWords * C::THREADS);
   int64_t cnt0 = 0, cnt1 = 0, la0 = 0, lb0 = 0, la1 = 0, lb1 = 0;
   int n_a = 0, n_b = 0;
   if (fast) {
@@ -1052,7 +1072,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     la0 = cnt0 * rp(1) / rp(2);
     lb0 = cnt0 * (rp(1) + 1) / rp(2);
     n_a = (int)(lb0 - la0);
-    // The list's first kStreamThreads items: id, then slot row (dependent loads, in flight during the scan).
+    // The list's first C::THREADS items: id, then slot row (dependent loads, in flight during the scan).
     int hot_row = -1;
     const int64_t hit = la0 + threadIdx.x;
     if (hit < lb0) {
@@ -1080,10 +1100,10 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
       // run's words w, w + NW, ..., one lane per bit (its ordinal: the word's plus the set bits below it).
       static_assert(kSetupWords == 1, "one word per thread in the warp-cooperative listing");
       uint32_t* wbits = reinterpret_cast<uint32_t*>(ring);
-      int* word_ord = reinterpret_cast<int*>(ring) + kStreamThreads;
+      int* word_ord = reinterpret_cast<int*>(ring) + C::THREADS;
       __shared__ int sh_wrun[2];
       if (threadIdx.x == 0) {
-        sh_wrun[0] = kStreamThreads;
+        sh_wrun[0] = C::THREADS;
         sh_wrun[1] = -1;
       }
       wbits[threadIdx.x] = bits[0];
@@ -1112,7 +1132,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
       // through the async proxy after the barrier that ends the set-up.
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       if (hit < lb0) list[threadIdx.x] = hot_row;
-      for (int64_t it = lb0 > la0 + kStreamThreads ? la0 + kStreamThreads + threadIdx.x : lb0; it < lb0; it += blockDim.x) {
+      for (int64_t it = lb0 > la0 + C::THREADS ? la0 + C::THREADS + threadIdx.x : lb0; it < lb0; it += blockDim.x) {
         const int blk = __ldg(S0.blocks + (int64_t)j * S0.n_list + it);
         int64_t row = blk < 0 ? -1 : (S0.slot_of != nullptr ? __ldg(S0.slot_of + (int64_t)j * S0.slot_stride + blk) : blk);
         list[it - la0] = row >= S0.n_rows ? -1 : (int)row;
@@ -1198,15 +1218,15 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   auto list_index = [&](int k) { return k < hn ? ha + k : n_a + ca + (k - hn); };
 
   const int g = lane >> 2, t = lane & 3;
-  uint32_t bq[4][2], bqp[4][2];
+  uint32_t bq[KS][2], bqp[KS][2];
   {
     const uint32_t* q = reinterpret_cast<const uint32_t*>(static_cast<const __nv_bfloat16*>(p.q) + ((int64_t)j * G + (g < G ? g : 0)) * D);
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
+    for (int ks = 0; ks < KS; ++ks) {
       bq[ks][0] = g < G ? q[(16 * ks + 2 * t) / 2] : 0u;
       bq[ks][1] = g < G ? q[(16 * ks + 2 * t + 8) / 2] : 0u;
-      bqp[ks][0] = g < G ? q[(16 * t + 4 * ks) / 2] : 0u;
-      bqp[ks][1] = g < G ? q[(16 * t + 4 * ks + 2) / 2] : 0u;
+      bqp[ks][0] = g < G ? q[(CH * t + 4 * ks) / 2] : 0u;
+      bqp[ks][1] = g < G ? q[(CH * t + 4 * ks + 2) / 2] : 0u;
     }
   }
   uint32_t koff[4], voff[4];
@@ -1218,7 +1238,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
       voff[x] = swz(r7 + 8 * (i >> 1), 2 * x + (i & 1));
     }
   }
-  unsigned char* stage0 = ring + warp * NS * kStreamStage;
+  unsigned char* stage0 = ring + warp * NS * C::STAGE;
   // Per set: whether its items are int8 records (else bf16 tile pairs through the tensor maps).
   const bool rec0 = p.seg[0].kind == SEG_RANGE_REC, rec1 = p.n_segs > 1 && p.seg[1].kind == SEG_RANGE_REC;
   // The warp's item holding the current block (the last listed block, `last_fill` live tokens), if any.
@@ -1233,18 +1253,21 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
       mbar_arrive(&bars[s]);
       return;
     }
-    unsigned char* dst = stage0 + s * kStreamStage;
+    unsigned char* dst = stage0 + s * C::STAGE;
     if (set ? rec1 : rec0) {
       const Seg& S = p.seg[set];
-      mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaRec);
-      tma_load_1d_hint(dst, S.records + ((int64_t)row * p.h + rp(4)) * S.width, (uint32_t)kMmaRec, &bars[s], stream_pol);
+      mbar_arrive_expect_tx(&bars[s], (uint32_t)GM::REC);
+      tma_load_1d_hint(dst, S.records + ((int64_t)row * p.h + rp(4)) * S.width, (uint32_t)GM::REC, &bars[s], stream_pol);
     } else {
-      mbar_arrive_expect_tx(&bars[s], (uint32_t)kMmaHotStage);
+      mbar_arrive_expect_tx(&bars[s], (uint32_t)GM::HOT);
       const int hm = sp.head_major[set];
       const int hj = rp(4);
       const int c2 = hm ? hj : row, c3 = hm ? row : hj;
-      tma_load_4d_hint(smem_u32(dst), &sp.tk[set], 0, 0, c2, c3, &bars[s], stream_pol);
-      tma_load_4d_hint(smem_u32(dst + kMmaTile), &sp.tv[set], 0, 0, c2, c3, &bars[s], stream_pol);
+#pragma unroll
+      for (int hf = 0; hf < GM::HALVES; ++hf) {  // channels 64 hf .. 64 hf + 63 of the K and V tiles
+        tma_load_4d_hint(smem_u32(dst + 2048 * hf), &sp.tk[set], 64 * hf, 0, c2, c3, &bars[s], stream_pol);
+        tma_load_4d_hint(smem_u32(dst + GM::TILE + 2048 * hf), &sp.tv[set], 64 * hf, 0, c2, c3, &bars[s], stream_pol);
+      }
     }
   };
   int n_issued = 0;
@@ -1261,7 +1284,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
   // threshold of the lazy rescaling (scale_log2 > 0), nm = -m.
   constexpr float kNoMax = -1e30f;
   const float sl2 = p.scale_log2, inv_sl2 = 1.0f / p.scale_log2;
-  float o[4][4];
+  float o[KS][4];
   float m0, m1, nm0, nm1, thr0, thr1, l0, l1;
   auto reset_state = [&]() {
     m0 = m1 = kNoMax;
@@ -1269,7 +1292,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     thr0 = thr1 = (kNoMax + kLazy) * inv_sl2;
     l0 = l1 = 0.0f;
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < KS; ++a)
 #pragma unroll
       for (int b = 0; b < 4; ++b) o[a][b] = 0.0f;
   };
@@ -1287,9 +1310,9 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     float* slot = park + (warp * 2 + set) * C::SLOT;
     const bool perm = set ? rec1 : rec0;
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-      const int c0 = perm ? 8 * g + 2 * mt : 16 * mt + g;
-      const int c1 = perm ? 8 * g + 2 * mt + 1 : 16 * mt + g + 8;
+    for (int mt = 0; mt < KS; ++mt) {
+      const int c0 = perm ? (D / 8) * g + 2 * mt : 16 * mt + g;
+      const int c1 = perm ? (D / 8) * g + 2 * mt + 1 : 16 * mt + g + 8;
       if (r0 < G) {
         slot[r0 * D + c0] = o[mt][0];
         slot[r0 * D + c1] = o[mt][2];
@@ -1311,13 +1334,12 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     }
   };
 
-  // Lane offsets inside a stage (bytes): record K codes of tokens g and g + 8 at channels 16t..,
-  // V codes of tokens 2t, 2t+1, 2t+8, 2t+9 at channels 8g.., V scales / zeros of those tokens, and
-  // the float32 K scales / zeros of channels 16t.. in the stage's tail.
-  const int ok0 = g * 64 + 16 * t, ok8 = (g + 8) * 64 + 16 * t;
-  const int ov0 = 1024 + (2 * t) * 64 + 8 * g, ov1 = ov0 + 64, ov8 = ov0 + 8 * 64, ov9 = ov0 + 9 * 64;
-  const int ovs = 2304 + 4 * t, ovz = 2336 + 4 * t;
-  constexpr int kKf = 2432;  // float32 K scales [64] then zeros [64], after the 2368 record bytes
+  // Lane offsets inside a stage (bytes): record K codes of tokens g and g + 8 at channels CH t..,
+  // V codes of tokens 2t, 2t+1, 2t+8, 2t+9 at channels (D/8)g.., V scales / zeros of those tokens,
+  // and the float32 K scales / zeros of channels CH t.. in the stage's tail.
+  const int ok0 = g * D + CH * t, ok8 = (g + 8) * D + CH * t;
+  const int ov0 = 16 * D + (2 * t) * D + (D / 8) * g, ov1 = ov0 + D, ov8 = ov0 + 8 * D, ov9 = ov0 + 9 * D;
+  const int ovs = GM::OFF_VS + 4 * t, ovz = GM::OFF_VZ + 4 * t;
 
   // One item in the stage at `st`: scores, softmax update and the O contraction. REC: an int8
   // record dequantised in registers (permuted channels); else a bf16 tile pair read by ldmatrix.
@@ -1327,21 +1349,31 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
     float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if constexpr (REC) {
       // The record's 64 K scales and 64 K zeros (float16) become float32 once per warp, in the
-      // stage's unused tail; lane (g, t) then reads those of its channels 16t .. 16t+15.
-      float* kf = reinterpret_cast<float*>(st + kKf);
-      {
-        const uint2 hw = *reinterpret_cast<const uint2*>(st + 2048 + 8 * lane);
+      // stage's unused tail; lane (g, t) then reads those of its channels CH t .. CH t + CH - 1.
+      float* kf = reinterpret_cast<float*>(st + GM::KF);
+      if constexpr (D == 64) {
+        const uint2 hw = *reinterpret_cast<const uint2*>(st + GM::OFF_KS + 8 * lane);
         const float2 f01 = h2f2(hw.x), f23 = h2f2(hw.y);
         *reinterpret_cast<float4*>(kf + 4 * lane) = make_float4(f01.x, f01.y, f23.x, f23.y);
+      } else {
+        const uint4 hw = *reinterpret_cast<const uint4*>(st + GM::OFF_KS + 16 * lane);
+        const float2 f01 = h2f2(hw.x), f23 = h2f2(hw.y), f45 = h2f2(hw.z), f67 = h2f2(hw.w);
+        *reinterpret_cast<float4*>(kf + 8 * lane) = make_float4(f01.x, f01.y, f23.x, f23.y);
+        *reinterpret_cast<float4*>(kf + 8 * lane + 4) = make_float4(f45.x, f45.y, f67.x, f67.y);
       }
-      const uint4 cg0 = *reinterpret_cast<const uint4*>(st + ok0);
-      const uint4 cg8 = *reinterpret_cast<const uint4*>(st + ok8);
-      const uint32_t wg0[4] = {cg0.x, cg0.y, cg0.z, cg0.w}, wg8[4] = {cg8.x, cg8.y, cg8.z, cg8.w};
+      uint32_t wg0[KS], wg8[KS];
+#pragma unroll
+      for (int v = 0; v < KS / 4; ++v) {
+        const uint4 cg0 = *reinterpret_cast<const uint4*>(st + ok0 + 16 * v);
+        const uint4 cg8 = *reinterpret_cast<const uint4*>(st + ok8 + 16 * v);
+        wg0[4 * v] = cg0.x, wg0[4 * v + 1] = cg0.y, wg0[4 * v + 2] = cg0.z, wg0[4 * v + 3] = cg0.w;
+        wg8[4 * v] = cg8.x, wg8[4 * v + 1] = cg8.y, wg8[4 * v + 2] = cg8.z, wg8[4 * v + 3] = cg8.w;
+      }
       __syncwarp();
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const float4 sc = *reinterpret_cast<const float4*>(kf + 16 * t + 4 * ks);
-        const float4 zc = *reinterpret_cast<const float4*>(kf + 64 + 16 * t + 4 * ks);
+      for (int ks = 0; ks < KS; ++ks) {
+        const float4 sc = *reinterpret_cast<const float4*>(kf + CH * t + 4 * ks);
+        const float4 zc = *reinterpret_cast<const float4*>(kf + D + CH * t + 4 * ks);
         const float2 s01 = f2(sc.x, sc.y), s23 = f2(sc.z, sc.w), z01 = f2(zc.x, zc.y), z23 = f2(zc.z, zc.w);
         float2 ua, ub, va, vb;
         codes4(wg0[ks], ua, ub);
@@ -1356,10 +1388,10 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
       }
     } else {
 #pragma unroll
-      for (int ks = 0; ks < 4; ks += 2) {
+      for (int ks = 0; ks < KS; ks += 2) {
         uint32_t a[4], b[4];
-        ldsm_x4(st32 + koff[ks], a);
-        ldsm_x4(st32 + koff[ks + 1], b);
+        ldsm_x4(st32 + 2048 * (ks >> 2) + koff[ks & 3], a);
+        ldsm_x4(st32 + 2048 * ((ks + 1) >> 2) + koff[(ks + 1) & 3], b);
         mma_bf16(sa, a, bq[ks][0], bq[ks][1]);
         mma_bf16(sb, b, bq[ks + 1][0], bq[ks + 1][1]);
       }
@@ -1383,7 +1415,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
         const float alpha = exp2f(m0 - mb0);
         l0 *= alpha;
 #pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
+        for (int mt = 0; mt < KS; ++mt) {
           o[mt][0] *= alpha;
           o[mt][2] *= alpha;
         }
@@ -1395,7 +1427,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
         const float alpha = exp2f(m1 - mb1);
         l1 *= alpha;
 #pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
+        for (int mt = 0; mt < KS; ++mt) {
           o[mt][1] *= alpha;
           o[mt][3] *= alpha;
         }
@@ -1417,22 +1449,35 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
 
     // ---- O^T += V^T . P^T ----
     if constexpr (REC) {
-      const uint2 c0 = *reinterpret_cast<const uint2*>(st + ov0);
-      const uint2 c1 = *reinterpret_cast<const uint2*>(st + ov1);
-      const uint2 c2 = *reinterpret_cast<const uint2*>(st + ov8);
-      const uint2 c3 = *reinterpret_cast<const uint2*>(st + ov9);
+      // Lane g's D / 8 channels of tokens 2t, 2t+1, 2t+8, 2t+9, as D / 32 words each.
+      uint32_t e0[D / 32], e1[D / 32], e2[D / 32], e3[D / 32];
+      if constexpr (D == 64) {
+        const uint2 c0 = *reinterpret_cast<const uint2*>(st + ov0);
+        const uint2 c1 = *reinterpret_cast<const uint2*>(st + ov1);
+        const uint2 c2 = *reinterpret_cast<const uint2*>(st + ov8);
+        const uint2 c3 = *reinterpret_cast<const uint2*>(st + ov9);
+        e0[0] = c0.x ^ 0x80808080u, e0[1] = c0.y ^ 0x80808080u, e1[0] = c1.x ^ 0x80808080u, e1[1] = c1.y ^ 0x80808080u;
+        e2[0] = c2.x ^ 0x80808080u, e2[1] = c2.y ^ 0x80808080u, e3[0] = c3.x ^ 0x80808080u, e3[1] = c3.y ^ 0x80808080u;
+      } else {
+        const uint4 c0 = *reinterpret_cast<const uint4*>(st + ov0);
+        const uint4 c1 = *reinterpret_cast<const uint4*>(st + ov1);
+        const uint4 c2 = *reinterpret_cast<const uint4*>(st + ov8);
+        const uint4 c3 = *reinterpret_cast<const uint4*>(st + ov9);
+        e0[0] = c0.x ^ 0x80808080u, e0[1] = c0.y ^ 0x80808080u, e0[2] = c0.z ^ 0x80808080u, e0[3] = c0.w ^ 0x80808080u;
+        e1[0] = c1.x ^ 0x80808080u, e1[1] = c1.y ^ 0x80808080u, e1[2] = c1.z ^ 0x80808080u, e1[3] = c1.w ^ 0x80808080u;
+        e2[0] = c2.x ^ 0x80808080u, e2[1] = c2.y ^ 0x80808080u, e2[2] = c2.z ^ 0x80808080u, e2[3] = c2.w ^ 0x80808080u;
+        e3[0] = c3.x ^ 0x80808080u, e3[1] = c3.y ^ 0x80808080u, e3[2] = c3.z ^ 0x80808080u, e3[3] = c3.w ^ 0x80808080u;
+      }
       const float2 vs01 = h2f2(*reinterpret_cast<const uint32_t*>(st + ovs));
       const float2 vs89 = h2f2(*reinterpret_cast<const uint32_t*>(st + ovs + 16));
       const float2 vz01 = h2f2(*reinterpret_cast<const uint32_t*>(st + ovz));
       const float2 vz89 = h2f2(*reinterpret_cast<const uint32_t*>(st + ovz + 16));
-      const uint32_t e0[2] = {c0.x ^ 0x80808080u, c0.y ^ 0x80808080u}, e1[2] = {c1.x ^ 0x80808080u, c1.y ^ 0x80808080u};
-      const uint32_t e2[2] = {c2.x ^ 0x80808080u, c2.y ^ 0x80808080u}, e3[2] = {c3.x ^ 0x80808080u, c3.y ^ 0x80808080u};
 #pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
+      for (int mt = 0; mt < KS; ++mt) {
         const int wi = mt >> 1;
         const uint32_t sel0 = 0x7650u + 2 * (mt & 1), sel1 = sel0 + 1;
-        const float2 v00 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel0), vs01, vz01);  // channel 8g+2mt, tokens 2t, 2t+1
-        const float2 v01 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel1), vs01, vz01);  // channel 8g+2mt+1
+        const float2 v00 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel0), vs01, vz01);  // channel (D/8)g+2mt, tokens 2t, 2t+1
+        const float2 v01 = __ffma2_rn(code_pair(e0[wi], e1[wi], sel1), vs01, vz01);  // channel (D/8)g+2mt+1
         const float2 v80 = __ffma2_rn(code_pair(e2[wi], e3[wi], sel0), vs89, vz89);  // tokens 2t+8, 2t+9
         const float2 v81 = __ffma2_rn(code_pair(e2[wi], e3[wi], sel1), vs89, vz89);
         const uint32_t a[4] = {pack_bf2(v00.x, v00.y), pack_bf2(v01.x, v01.y), pack_bf2(v80.x, v80.y), pack_bf2(v81.x, v81.y)};
@@ -1441,11 +1486,11 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
         mma_bf16(o[mt], a, bh0, bh1);
       }
     } else {
-      const uint32_t vt = st32 + kMmaTile;
+      const uint32_t vt = st32 + GM::TILE;
 #pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
+      for (int mt = 0; mt < KS; ++mt) {
         uint32_t a[4];
-        ldsm_x4_t(vt + voff[mt], a);
+        ldsm_x4_t(vt + 2048 * (mt >> 2) + voff[mt & 3], a);
         mma_bf16(o[mt], a, bl0, bl1);
         mma_bf16(o[mt], a, bm0, bm1);
         mma_bf16(o[mt], a, bh0, bh1);
@@ -1475,7 +1520,7 @@ __global__ void __launch_bounds__(kStreamThreads, kStreamCtasPerSm) attn_stream_
         reset_state();
       }
       if (list[list_index(k)] >= 0) {
-        unsigned char* st = stage0 + u * kStreamStage;
+        unsigned char* st = stage0 + u * C::STAGE;
         if (k < hn ? rec0 : rec1)
           item(std::true_type{}, st, false);
         else
@@ -1951,13 +1996,14 @@ void split_two(Seg& hot, Seg& cold, int h, double hot_item, double cold_item, in
 
 // K and V maps of a list or pairs segment: 4-D bf16 tensors (channel, token, row, head) with a box of
 // one 16 x 64 block, 128-byte swizzle. The row and head dimensions are ordered by stride.
-bool make_kv_maps(const Seg& S, int h, CUtensorMap* tk, CUtensorMap* tv, int* head_major) {
+bool make_kv_maps(const Seg& S, int h, int d, CUtensorMap* tk, CUtensorMap* tv, int* head_major) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr || S.n_rows <= 0) return false;
   const int64_t es = 2;
   const int64_t st = S.s_tok * es, sr = S.s_row * es, sh = S.s_head * es;
   const bool hm = sh < sr;
-  const cuuint64_t dims[4] = {64, 16, (cuuint64_t)(hm ? h : S.n_rows), (cuuint64_t)(hm ? S.n_rows : h)};
+  // Boxes of 64 channels x 16 tokens (128-byte swizzled rows); a 128-channel tile is two boxes.
+  const cuuint64_t dims[4] = {(cuuint64_t)d, 16, (cuuint64_t)(hm ? h : S.n_rows), (cuuint64_t)(hm ? S.n_rows : h)};
   const cuuint64_t strides[3] = {(cuuint64_t)st, (cuuint64_t)(hm ? sh : sr), (cuuint64_t)(hm ? sr : sh)};
   const cuuint32_t box[4] = {64, 16, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -1971,19 +2017,19 @@ bool make_kv_maps(const Seg& S, int h, CUtensorMap* tk, CUtensorMap* tv, int* he
   return true;
 }
 
-// Whether the stream kernel takes this launch (bf16, d 64, bs 16, G <= 8, stores in device
-// memory, 64-channel token rows); fills the tensor maps of its list / pairs segments.
+// Whether the stream kernel takes this launch (bf16, d 64 or 128, bs 16, G <= 8, stores in device
+// memory, d-channel token rows); fills the tensor maps of its list / pairs segments.
 bool mma_plan(const AttnParams& p, int g, int d, bool bf16, MmaParams& mp) {
-  if (!bf16 || d != 64 || p.bs != 16 || (g != 1 && g != 2 && g != 4 && g != 8)) return false;
+  if (!bf16 || (d != 64 && d != 128) || p.bs != 16 || (g != 1 && g != 2 && g != 4 && g != 8)) return false;
   if (!(p.scale_log2 > 0.0f)) return false;  // its lazy rescaling compares raw scores against (m + 8) / scale
   for (int i = 0; i < p.n_segs; ++i) {
     const Seg& S = p.seg[i];
     if (S.n_items == 0) continue;
     if (S.kind == SEG_RANGE_REC) {
-      if (S.width != kMmaRec || is_host_mapped(S.records)) return false;
+      if (S.width != (d == 64 ? MmaGeom<64>::REC : MmaGeom<128>::REC) || is_host_mapped(S.records)) return false;
     } else {
       if (S.s_tok != d || is_host_mapped(S.k_base) || is_host_mapped(S.v_base)) return false;
-      if (!make_kv_maps(S, p.h, &mp.tk[i], &mp.tv[i], &mp.head_major[i])) return false;
+      if (!make_kv_maps(S, p.h, d, &mp.tk[i], &mp.tv[i], &mp.head_major[i])) return false;
     }
   }
   return true;
@@ -2018,8 +2064,8 @@ int stream_per_head(int h, int64_t n_ub) {
   if (need > per) per = (int)need;
   return per < 1 ? 1 : per;
 }
-size_t stream_partial_bytes(int h, int g, int64_t n_ub) {
-  const int part = (g * 64 + 2 * g + 3) / 4 * 4;
+size_t stream_partial_bytes(int h, int g, int d, int64_t n_ub) {
+  const int part = (g * d + 2 * g + 3) / 4 * 4;
   return (size_t)h * stream_per_head(h, n_ub) * 2 * part * sizeof(float);
 }
 int64_t stream_item_bound(const AttnParams& p) {
@@ -2028,17 +2074,21 @@ int64_t stream_item_bound(const AttnParams& p) {
   return n;
 }
 
-template <int G, typename TO>
+template <int G, int D, typename TO>
 int launch_stream(const StreamParams& sp, cudaStream_t st) {
-  using C = StreamCfg<G>;
+  using C = StreamCfg<G, D>;
   static uint64_t attr_set = 0;  // one bit per device
-  auto k = sp.sched != nullptr ? attn_stream_kernel<G, TO, true> : attn_stream_kernel<G, TO, false>;
+  // Ragged rows run at head_dim 64 only (run_attention_ragged checks it).
+  auto k = attn_stream_kernel<G, D, TO, false>;
+  if constexpr (D == 64)
+    if (sp.sched != nullptr) k = attn_stream_kernel<G, D, TO, true>;
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_set & bit)) {  // both instances: a single sequence's and ragged rows'
-    cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel<G, TO, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_stream_kernel<G, TO, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  if (!(attr_set & bit)) {  // every instance: a single sequence's and (head_dim 64) ragged rows'
+    cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel<G, D, TO, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if constexpr (D == 64)
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_stream_kernel<G, D, TO, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) {
       cudaGetLastError();  // not left behind for a later launch check
       return fail(LKV_ERR_CUDA, "attention: shared memory attribute: %s", cudaGetErrorString(e));
@@ -2046,7 +2096,7 @@ int launch_stream(const StreamParams& sp, cudaStream_t st) {
     attr_set |= bit;
   }
   const dim3 grid = sp.sched != nullptr ? dim3(sp.per_head) : dim3(sp.per_head, sp.p.h);  // ragged: per_head holds the CTAs
-  cudaError_t e = launch_pdl(k, grid, dim3(kStreamThreads), C::SMEM, st, 0, sp);
+  cudaError_t e = launch_pdl(k, grid, dim3(C::THREADS), C::SMEM, st, 0, sp);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(LKV_ERR_CUDA, "lkv attention: %s", cudaGetErrorString(e));
@@ -2083,13 +2133,21 @@ int run_attention(const char* who, AttnParams& p, int g, int d, TO* out, float* 
       sp.lse = lse;
       sp.seg_out = seg_out;
       sp.seg_lse = seg_lse;
-      const size_t need = stream_partial_bytes(p.h, g, n_ub);
+      const size_t need = stream_partial_bytes(p.h, g, d, n_ub);
       if (avail < need) return fail(LKV_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", who, workspace_bytes, need + kStreamCounterBytes);
+      if (d == 128) {
+        switch (g) {
+          case 1: return launch_stream<1, 128, TO>(sp, st);
+          case 2: return launch_stream<2, 128, TO>(sp, st);
+          case 4: return launch_stream<4, 128, TO>(sp, st);
+          default: return launch_stream<8, 128, TO>(sp, st);
+        }
+      }
       switch (g) {
-        case 1: return launch_stream<1, TO>(sp, st);
-        case 2: return launch_stream<2, TO>(sp, st);
-        case 4: return launch_stream<4, TO>(sp, st);
-        default: return launch_stream<8, TO>(sp, st);
+        case 1: return launch_stream<1, 64, TO>(sp, st);
+        case 2: return launch_stream<2, 64, TO>(sp, st);
+        case 4: return launch_stream<4, 64, TO>(sp, st);
+        default: return launch_stream<8, 64, TO>(sp, st);
       }
     }
   }
@@ -2117,7 +2175,7 @@ int run_attention_ragged(const char* who, AttnParams& p, int g, int d, const int
   if (!aligned(workspace, 16)) return fail(LKV_ERR_PTR, "%s: workspace must be 16-byte aligned", who);
   p.part = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kStreamCounterBytes);
   MmaParams mp{};
-  if (!mma_plan(p, g, d, true, mp))
+  if (d != 64 || !mma_plan(p, g, d, true, mp))
     return fail(LKV_ERR_ARG, "%s: ragged rows need bf16, head_dim 64, block size 16, a group of 1, 2, 4 or 8, a positive scale and device-resident stores", who);
   StreamParams sp{};
   sp.p = p;
@@ -2137,10 +2195,10 @@ int run_attention_ragged(const char* who, AttnParams& p, int g, int d, const int
   sp.table_stride = table_stride;
   sp.heads = heads;
   switch (g) {
-    case 1: return launch_stream<1, TO>(sp, st);
-    case 2: return launch_stream<2, TO>(sp, st);
-    case 4: return launch_stream<4, TO>(sp, st);
-    default: return launch_stream<8, TO>(sp, st);
+    case 1: return launch_stream<1, 64, TO>(sp, st);
+    case 2: return launch_stream<2, 64, TO>(sp, st);
+    case 4: return launch_stream<4, 64, TO>(sp, st);
+    default: return launch_stream<8, 64, TO>(sp, st);
   }
 }
 
@@ -2258,7 +2316,7 @@ int lkv_status_poll(int* status, int clear) {
 size_t lkv_attention_workspace(int h, int hq, int d, int n_items) {
   if (h <= 0 || hq <= 0) return 0;
   const int s = splits_for(n_items, (kTargetCtas + h - 1) / h);
-  const size_t a = partial_bytes(h, hq / h, d, s), b = stream_partial_bytes(h, hq / h, n_items > 0 ? n_items : 0);
+  const size_t a = partial_bytes(h, hq / h, d, s), b = stream_partial_bytes(h, hq / h, d, n_items > 0 ? n_items : 0);
   return kStreamCounterBytes + (a > b ? a : b);
 }
 
@@ -2266,7 +2324,7 @@ size_t lkv_exact_attention_workspace(int h, int hq, int d, int n_list, int n_blo
   if (h <= 0 || hq <= 0) return 0;
   const int per_head = (kTargetCtas + h - 1) / h + 1;  // any split of the target between the segments
   const int64_t n_ub = (int64_t)(n_list > 0 ? n_list : 0) + (n_blocks > 0 ? n_blocks : 0);
-  const size_t a = partial_bytes(h, hq / h, d, per_head), b = stream_partial_bytes(h, hq / h, n_ub);
+  const size_t a = partial_bytes(h, hq / h, d, per_head), b = stream_partial_bytes(h, hq / h, d, n_ub);
   return kStreamCounterBytes + (a > b ? a : b);
 }
 

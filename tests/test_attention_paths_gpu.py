@@ -1,8 +1,8 @@
 """The attention kernels (tensor-core, TMA-pipelined and plain-load) and the fused exact call,
 against the oracle.
 
-The tensor-core stream kernel serves bf16 stores in device memory at d 64, bs 16, G <= 8; the TMA kernel
-the other device-memory cases at G = 4, bs = 16, d in {64, 128}; the plain-load kernel every other
+The tensor-core stream kernel serves bf16 stores in device memory at d 64 or 128, bs 16, G <= 8; the TMA
+kernel the other device-memory cases at G = 4, bs = 16, d in {64, 128}; the plain-load kernel every other
 geometry and cold stores in mapped host memory. Every case is compared with float64 attention over
 the same values (1e-5 of the max; int8 cold blocks as unpack in the model dtype), and the fused call
 with the separate calls and their merge.
@@ -76,8 +76,19 @@ def _bitmap(sel: torch.Tensor, n: int) -> torch.Tensor:
 @pytest.mark.parametrize("d,bs,dtype,int8", [(64, 16, torch.bfloat16, True), (128, 16, torch.bfloat16, True), (64, 16, torch.float32, False),
                                              (64, 16, torch.bfloat16, False), (16, 8, torch.bfloat16, True), (64, 8, torch.float32, True)])
 def test_hot_cold_and_fused_match_float64(d: int, bs: int, dtype: torch.dtype, int8: bool) -> None:
+    _check_paths(d, bs, dtype, int8, 4)
+
+
+@pytest.mark.parametrize("g", [1, 2, 8])
+@pytest.mark.parametrize("int8", [True, False])
+def test_head_dim_128_in_every_query_group(g: int, int8: bool) -> None:
+    """head_dim 128 (the long-context geometry) through the tensor-core stream kernel at every group."""
+    _check_paths(128, 16, torch.bfloat16, int8, g)
+
+
+def _check_paths(d: int, bs: int, dtype: torch.dtype, int8: bool, g: int) -> None:
     K = _k()
-    h, g, n, k, fill = 4, 4, 300, 40, 5
+    h, n, k, fill = 4, 300, 40, 5
     kv, q, sel = _setup(h, g, d, bs, n, k, dtype, seed=d + bs + int(int8))
     kvd, qd = kv.to(DEV), q.to(DEV)
     if int8:
