@@ -58,6 +58,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--layers", type=int, default=N_LAYERS - DENSE, help="selecting layers (the metric runs all 14; fewer for profiling)")
     p.add_argument("--queries", type=int, default=8, help="queries in each layer's ring: decode token s uses query s mod this")
     p.add_argument("--drift", type=float, default=0.15, help="a ring query is a base query + drift x N(0,1) (0.15: a hit rate near 0.84, inside the 0.79-1.0 the reference measured with real models)")
+    p.add_argument("--no-model", action="store_true", help="skip the model legs (32K-token greedy decode; the 130,048-token capacity sweep)")
     p.add_argument("--no-long-ctx", action="store_true", help="skip the 1,048,576-token leg (8 sequences, head_dim 128, global top-K)")
     p.add_argument("--long-layers", type=int, default=4, help="layers of the long-context leg held and timed (each 30 GB at N = 1)")
     p.add_argument("--long-steps", type=int, default=32, help="timed decode steps of the long-context leg")
@@ -757,6 +758,12 @@ def run_ours(args: argparse.Namespace) -> None:
 
     if not args.no_long_ctx:
         result["long_ctx"] = run_long_ctx(args, rank, world, dev, timed)
+    if world == 1 and not args.no_model:
+        cfg, model = random_llama(dev)
+        result["model_decode"] = run_model_decode(dev, cfg, model)
+        result["capacity_sweep"] = run_capacity_sweep(dev, cfg, model)
+        del model
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, budget_s=12.0)
     if rank == 0:
@@ -973,6 +980,151 @@ def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) ->
     if world > 1:
         dist.barrier()
     return out
+
+
+# The model legs: the random-init Llama-3.2-1B architecture through the drop-in API (the attention
+# hook, layer-major prefill into the tier, greedy decode), as a user of the reference runs it.
+LLAMA_1B = dict(hidden_size=2048, intermediate_size=8192, num_hidden_layers=16, num_attention_heads=32, num_key_value_heads=8, head_dim=64,
+                vocab_size=128256, max_position_embeddings=131072, tie_word_embeddings=True, rms_norm_eps=1e-5,
+                rope_parameters={"rope_type": "llama3", "rope_theta": 500000.0, "factor": 32.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                                 "original_max_position_embeddings": 8192})
+
+
+def random_llama(dev):  # noqa: ANN001, ANN201
+    """Llama-3.2-1B's architecture with seeded random weights in bf16 (no checkpoint), its attention
+    routed through lazykv_b200's hook (tiered decode on the selecting layers, SDPA elsewhere)."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from lazykv_b200.attention import IMPLEMENTATION_NAME, install
+
+    cfg = LlamaConfig(**LLAMA_1B)
+    install(None, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim)
+    torch.manual_seed(1234)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg)
+    model = model.to(torch.bfloat16).eval()
+    model.set_attn_implementation(IMPLEMENTATION_NAME)
+    return cfg, model
+
+
+def _decode_timed(model, cache, first_logits, n_new: int, warm: int = 4):  # noqa: ANN001, ANN202
+    """warm + n_new greedy decode steps through the model (the loop of generate.greedy_decode); the
+    time of the last n_new, from CUDA events (every step syncs on its argmax)."""
+    import torch
+
+    from lazykv_b200.generate import cache_model_kwargs
+
+    tok = int(torch.argmax(first_logits).item())
+    toks = [tok]
+    ids = torch.empty((1, 1), dtype=torch.long, device=model.device)
+    extra = cache_model_kwargs(cache)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.inference_mode():
+        for i in range(warm + n_new):
+            if i == warm:
+                a.record()
+            ids.fill_(tok)
+            out = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1, **extra)
+            tok = int(torch.argmax(out.logits[0, -1]).item())
+            toks.append(tok)
+    b.record()
+    b.synchronize()
+    return toks, a.elapsed_time(b)
+
+
+def run_model_decode(dev, cfg, model, prompt: int = 32768, n_new: int = 128, budget: float = 0.25, chunk: int = 4096) -> dict:  # noqa: ANN001
+    """The 16-layer model at a 32,768-token random prompt: layer-major prefill straight into int8
+    tiers (cold blocks in pinned host memory, 25% hot), then 128 greedy decode steps through the
+    hook (selection, admit, exact attention over the cold blocks and the merge on every selecting
+    layer and step); beside it the same prompt and steps with every token in HBM (FullGPUCache,
+    SDPA decode), and how many greedy tokens the two agree on."""
+    import torch
+
+    from lazykv_b200.cache import FullGPUCache
+    from lazykv_b200.exact import ExactTieredCache
+    from lazykv_b200.generate import prefill
+    from lazykv_b200.selection import blocks_for_budget
+    from lazykv_b200.tiered_prefill import tiered_prefill
+
+    gen = torch.Generator(device=dev).manual_seed(99)
+    ids = torch.randint(0, cfg.vocab_size, (1, prompt), device=dev, generator=gen)
+    k_blocks = blocks_for_budget(budget, prompt, BS)
+    cap = prompt + n_new + 128
+    out = {"workload": f"Llama-3.2-1B architecture (16 layers, 32q/8kv/d64, vocab 128256), random bf16 weights, {prompt}-token random prompt, "
+                       f"{n_new} greedy decode steps, int8 tiers with {int(budget * 100)}% of the blocks hot (K={k_blocks}), exact merge every step",
+           "path": "lazykv_b200.tiered_prefill(cache_cls=ExactTieredCache), then greedy decode through the transformers attention hook "
+                   "(4 warm-up steps, then the timed ones)"}
+    for placement in ("device", "host"):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = tiered_prefill(model, ids, chunk, k_blocks, BS, cap, quant="int8", cache_cls=ExactTieredCache, cold_placement=placement, fetch="gather")
+        torch.cuda.synchronize()
+        pre_s = time.perf_counter() - t0
+        toks, ms = _decode_timed(model, res.cache, res.last_logits, n_new)
+        st = res.cache.stats()
+        out[f"cold_{placement}"] = {"decode_tokens_per_s": round(n_new * 1e3 / ms, 2), "prefill_s": round(pre_s, 2),
+                                    "gpu_resident_kv_bytes": st.gpu_resident_kv_bytes, "host_kv_bytes": st.host_kv_bytes}
+        if placement == "device":
+            lazy_toks, lazy_first = toks, res.last_logits.clone()
+        res.cache.close()
+        del res
+        torch.cuda.empty_cache()
+    full = FullGPUCache(cfg.num_hidden_layers, cap)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    pre = prefill(model, full, ids, chunk)
+    torch.cuda.synchronize()
+    pre_s = time.perf_counter() - t0
+    toks, ms = _decode_timed(model, full, pre.last_logits, n_new)
+    diverge = next((i for i, (a, b) in enumerate(zip(lazy_toks, toks)) if a != b), len(toks))
+    out["full_gpu_cache"] = {"decode_tokens_per_s": round(n_new * 1e3 / ms, 2), "prefill_s": round(pre_s, 2),
+                             "gpu_resident_kv_bytes": full.stats().gpu_resident_kv_bytes}
+    # The prefill is exact in both (the tier is written from the same prompt KV), so the first
+    # logits agree; decode then differs by the int8 rounding of the cold blocks, and a random
+    # model's nearly flat logits let greedy choices part soon after.
+    out["agreement_with_full_cache"] = {"prefill_logits_max_abs_diff": float((lazy_first - pre.last_logits).abs().max().item()),
+                                        "first_differing_greedy_token": diverge, "tokens": len(toks)}
+    del full, pre
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_capacity_sweep(dev, cfg, model, prompt: int = 130048, n_new: int = 64, budgets=(0.0625, 0.25, 0.5, 0.75), chunk: int = 4096) -> dict:  # noqa: ANN001
+    """The capacity sweep: a 130,048-token random prompt prefilled layer by layer straight into int8
+    tiers whose cold blocks live in pinned host memory (the full KV is never resident), then 64
+    greedy decode steps with the exact merge, at each budget."""
+    import torch
+
+    from lazykv_b200.exact import ExactTieredCache
+    from lazykv_b200.selection import blocks_for_budget
+    from lazykv_b200.tiered_prefill import tiered_prefill
+
+    gen = torch.Generator(device=dev).manual_seed(98)
+    ids = torch.randint(0, cfg.vocab_size, (1, prompt), device=dev, generator=gen)
+    cap = prompt + n_new + 128
+    rows = []
+    for b in budgets:
+        k_blocks = blocks_for_budget(b, prompt, BS)
+        torch.cuda.reset_peak_memory_stats(dev)
+        base = torch.cuda.memory_allocated(dev)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = tiered_prefill(model, ids, chunk, k_blocks, BS, cap, quant="int8", cache_cls=ExactTieredCache, cold_placement="host", fetch="gather")
+        torch.cuda.synchronize()
+        pre_s = time.perf_counter() - t0
+        toks, ms = _decode_timed(model, res.cache, res.last_logits, n_new)
+        st = res.cache.stats()
+        rows.append({"budget": b, "k_blocks": k_blocks, "decode_tokens_per_s": round(n_new * 1e3 / ms, 2), "prefill_s": round(pre_s, 2),
+                     "gpu_resident_kv_bytes": st.gpu_resident_kv_bytes, "host_kv_bytes": st.host_kv_bytes,
+                     "peak_device_bytes_above_weights": int(torch.cuda.max_memory_allocated(dev) - base)})
+        res.cache.close()
+        del res
+        torch.cuda.empty_cache()
+    full_kv = cfg.num_hidden_layers * 2 * cfg.num_key_value_heads * prompt * cfg.head_dim * 2
+    return {"workload": f"Llama-3.2-1B architecture, random bf16 weights, {prompt}-token random prompt prefilled layer by layer into int8 tiers "
+                        f"(cold blocks in pinned host memory), {n_new} greedy decode steps with the exact merge, per budget",
+            "full_kv_bytes_bf16": full_kv, "budgets": rows}
 
 
 def measure_link_gbs(dev) -> float:  # noqa: ANN001
