@@ -4,18 +4,27 @@ Workload (BASELINE config 2 shapes at the metric's context): Llama-3.2-1B attent
 8 KV heads, head_dim 64), 131,072-token context in 16-token blocks, 25% budget
 (K = blocks_for_budget = 2,046 selected of 8,190 candidates), 14 selecting layers (16 layers, the
 first 2 dense). One step = one decode token through the hot path of the 14 selecting layers:
-Quest scoring + device top-K -> split decode over the HBM-resident hot blocks -> exact pass over the
-int8 cold blocks -> log-sum-exp merge. Data are seeded synthetic K/V (N(0,1), keys with a
-per-(head, channel) offset of variance 0.5) with random queries, bf16; every layer has its own
-buffers, so one step reads ~2.8 GB, far above the 126 MB L2 (no flush needed).
+Quest scoring + device top-K -> device LRU admit and the fetch of the missed blocks into HBM slots
+-> split decode over the hot blocks -> exact pass over the int8 cold blocks -> log-sum-exp merge.
+Data are seeded synthetic K/V (N(0,1), keys with a per-(head, channel) offset of variance 0.5),
+bf16; every layer has its own buffers, so one step reads ~2.8 GB, far above the 126 MB L2 (no
+flush needed).
 
-Residency: the hot slot pool holds exactly the blocks the step selects (the steady state in which
-every selected block is already resident); the cold records live in HBM (`--cold device`, the
-headline) or in pinned host memory read through zero-copy loads (`--cold host`, also reported).
+Residency churn: each layer holds a ring of queries (a base query plus a drift of N(0,1) noise),
+decode token s uses query s mod the ring, and the admit runs in every layer-step, so each step
+fetches the blocks its selection newly wants (a hit rate near 0.84 at the default drift; the
+reference measured 0.79-1.0 with real models). The cold records live in HBM (`--cold device`, the
+headline) or, in a second leg, in pinned host memory read through zero-copy loads.
 
 Multi-GPU (torchrun): the context is sharded by block range across ranks (strong scaling of the
 same 128K sequence); each rank selects K/N of its own candidates, runs both passes on its shard,
-merges locally, and the per-rank (out, lse) partials are all-gathered with NCCL and merged.
+and one launch per layer pushes its (out, lse) partial to every peer over NVLink and merges what
+arrived (lkv_exchange_merge: peer stores, no collective in the step).
+
+Further legs in the same JSON line: `long_ctx` (8 sequences of 1,048,576 tokens at head_dim 128,
+a global top-K across the shards, at every N), and at N = 1 `model_decode` (the random-init
+16-layer model through the attention hook: 32,768-token prefill, 128 greedy steps) and
+`capacity_sweep` (130,048-token layer-major prefill, four budgets).
 
 `--impl reference` times the reference's own CPU implementation of the path on the host cores instead:
 the unmodified reference installed under baseline/_ref (lazykv.selection.top_blocks, two
@@ -64,6 +73,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--long-steps", type=int, default=32, help="timed decode steps of the long-context leg")
     p.add_argument("--workload", choices=["metric", "ragged"], default="metric",
                    help="ragged: BASELINE config 3 instead of the metric (64 sequences of 4K-128K tokens, 6.25%% budget, one layer)")
+    p.add_argument("--profile-long", action="store_true",
+                   help="with --profile-calls: the long-context geometry (64 rows, d 128) at --ctx tokens, its selection, global select, "
+                        "admit, attention and exchange kernels")
     p.add_argument("--profile-calls", action="store_true",
                    help="profiling target: build the layers, then call, twice each and eagerly on the first layer, the selection, the hot "
                         "pass alone, the cold pass alone and the fused attention; print nothing else")
@@ -257,13 +269,14 @@ def build_layers(args: argparse.Namespace, rank: int, world: int, dev, keep_sour
         if world == 1:
             L.out = torch.empty((hq, d), dtype=torch.bfloat16, device=dev)
             L.lse = torch.empty((hq,), dtype=torch.float32, device=dev)
-            L.packed = None
+            L.xchg = None
         else:
-            # One buffer per layer, out then lse: one all-gather per layer, merged in place.
-            from lazykv_b200.sharded import PackedPartial
+            # The rank's partial lives in its exchange buffer; one launch per layer pushes it to
+            # every peer over NVLink and merges what arrived (lkv_exchange_merge).
+            from lazykv_b200.sharded import PeerExchange
 
-            L.packed = PackedPartial(hq, d, world, dev)
-            L.out, L.lse = L.packed.out, L.packed.lse
+            L.xchg = PeerExchange(hq, d, device=dev)
+            L.out, L.lse = L.xchg.out, L.xchg.lse
         L.records_host = None
         layers.append(L)
     torch.cuda.synchronize(dev)
@@ -406,6 +419,44 @@ def parity_check(got, parts: list) -> dict:  # noqa: ANN001
             "rule": "bf16 output within half a bf16 unit + 2e-5 max|ref| of a float64 torch restatement over the layer's stores"}
 
 
+def profile_long_calls(args: argparse.Namespace) -> None:
+    """The long-context layer-step's kernels at --ctx tokens (64 rows, head_dim 128, one layer),
+    each twice and eagerly, for a profiler: the selection with its admit (misses, then hits), the
+    bounds alone, the gathered select (one rank), the attention, and the peer-store exchange of
+    one rank (its own partial only)."""
+    import torch
+
+    from lazykv_b200 import kernels as K
+    from lazykv_b200.build import build
+    from lazykv_b200.sharded import PeerExchange
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    build()
+    shape = dict(LONG_SHAPE, ctx=args.ctx, layers=1, queries=2)
+    layers, geo = build_layers(args, 0, 1, dev, shape=shape)
+    L = layers[0]
+    first = geo["cand_lo"] - geo["lo"]
+    layer_step(L, geo, 0, 1)
+    for st in range(2):
+        select_admit_call(L, geo, 1, 2 + st)  # query 1's misses, then all hits
+    bounds = torch.empty((geo["h"], geo["n_cand"]), dtype=torch.bfloat16, device=dev)
+    for _ in range(2):
+        K.quest_bounds(L.q_ring[1], L.kmin, L.kmax, first, geo["n_cand"], bounds, torch.bfloat16)
+    gathered = bounds.view(1, geo["h"], geo["n_cand"])
+    chosen = torch.empty((geo["h"], geo["k_local"]), dtype=torch.int32, device=dev)
+    for _ in range(2):
+        K.topk_gathered(gathered, [geo["n_cand"]], geo["k_total"], 0, first, chosen, L.bitmap)
+    for _ in range(2):
+        attention_call(L, geo, 1)
+    x = PeerExchange(geo["hq"], geo["d"], device=dev)
+    merged = torch.empty((geo["hq"], geo["d"]), dtype=torch.bfloat16, device=dev)
+    for _ in range(2):
+        x.exchange(merged)
+    torch.cuda.synchronize()
+    x.close()
+
+
 def profile_calls(args: argparse.Namespace) -> None:
     """The kernel calls of one layer-step, each twice and eagerly, for a profiler to capture: the
     selection, the admit (the first with misses), the hot pass alone, the cold pass alone and the
@@ -485,12 +536,11 @@ def run_ours(args: argparse.Namespace) -> None:
 
     def token(r: int, step_no: int, cold_of=None) -> None:
         """One decode token with query r of the ring: every selecting layer's hot path (and, at N > 1,
-        the all-gather of the layer's partials and their merge on every rank)."""
+        the exchange of the layer's partials over NVLink and their merge on every rank)."""
         for i, L in enumerate(layers):
             layer_step(L, geo, r, step_no, None if cold_of is None else cold_of(L))
             if world > 1:
-                L.packed.exchange()
-                L.packed.merge(torch.bfloat16, out=finals[i])
+                L.xchg.exchange(finals[i])
 
     # Warm-up: the first token admits every selected block of query 0; then the ring of queries.
     step_no = 0
@@ -499,7 +549,7 @@ def run_ours(args: argparse.Namespace) -> None:
         token(w % R, step_no)
     torch.cuda.synchronize()
 
-    # One CUDA graph per query of the ring, each a whole decode token (the NCCL all-gathers are
+    # One CUDA graph per query of the ring, each a whole decode token (the exchanges are
     # captured too at N > 1; the graphs are released before the process group). A graph's admit step
     # number is fixed at capture, so the LRU clock cycles with the ring.
     side = torch.cuda.Stream()
@@ -514,7 +564,7 @@ def run_ours(args: argparse.Namespace) -> None:
         with torch.cuda.graph(gph):
             token(r, step_no + 1 + r)
         graphs.append(gph)
-    del gph  # the graphs hold NCCL work at N > 1: only `graphs` may keep them, so that dropping it frees them
+    del gph  # the graphs hold cross-rank work at N > 1: only `graphs` may keep them, so that dropping it frees them
     ring_pos = [0]
 
     def run() -> None:
@@ -674,8 +724,7 @@ def run_ours(args: argparse.Namespace) -> None:
             for i, L in enumerate(layers):
                 L.q_ring[r].copy_(q_host[r, i], non_blocking=True)
                 layer_step(L, geo, r, 10**9 + e_pos[0])
-                L.packed.exchange()
-                L.packed.merge(torch.bfloat16, out=finals[i])
+                L.xchg.exchange(finals[i])
                 o_host[i].copy_(finals[i], non_blocking=True)
 
         for _ in range(2):
@@ -684,7 +733,7 @@ def run_ours(args: argparse.Namespace) -> None:
         e2e_ms = timed(e2e_step, n_e) / n_e
         e2e = {"value": round(1e3 / e2e_ms, 3), "unit": "tokens/s", "h2d_bytes_per_step": n_sel * HQ * D * 2,
                "d2h_bytes_per_step": n_sel * HQ * D * 2,
-               "path": "lazykv_b200.kernels (C ABI) per layer with the NCCL all-gather and merge, eager, host q in / host out"}
+               "path": "lazykv_b200.kernels (C ABI) per layer with the peer-store exchange and merge, eager, host q in / host out"}
 
     result = {
         "metric": METRIC,
@@ -703,7 +752,7 @@ def run_ours(args: argparse.Namespace) -> None:
         "config": {"workload": "tiered decode hot path, Llama-3.2-1B attention (32q/8kv/d64), 131072-token context, bs 16, 25% budget (K=2046), 14 selecting layers, int8 cold tier in HBM, device admit with a fresh query every step",
                    "ctx": args.ctx, "block_size": BS, "k_blocks": geo["k_total"], "selecting_layers": n_sel, "batch": 1, "queries_in_ring": R,
                    "cold_placement": "device", "l2": "inputs larger than L2 (~2.8 GB read per step)", "parallelism": f"context-sharded x{world}",
-                   "timing": "one CUDA graph per decode token (select, admit, attention per layer; NCCL all-gathers captured at N > 1), CUDA events, max over ranks"},
+                   "timing": "one CUDA graph per decode token (select, admit, attention per layer; the exchange launch at N > 1), CUDA events, max over ranks"},
         "kernel_us": {k: round(v, 3) for k, v in kernel_us.items()},
         "residency": {"hit_rate": round(hit_rate, 4), "fetched_pairs_per_layer_step": round(miss_pairs, 1), "fetch_bytes_per_layer_step": bytes_fetch},
         "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -716,7 +765,7 @@ def run_ours(args: argparse.Namespace) -> None:
                                 "achieved_gbs": round(layer_bytes / (us_layer * 1e-6) / 1e9, 1),
                                 "frac": round(layer_bytes / (us_layer * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)},
         "e2e": e2e,
-        "gpu_launches": n_steps * n_sel * (LAUNCHES_PER_LAYER_STEP + (1 if world > 1 else 0)),  # + the merge kernel at N > 1 (NCCL's own kernels not counted)
+        "gpu_launches": n_steps * n_sel * (LAUNCHES_PER_LAYER_STEP + (1 if world > 1 else 0)),  # + the exchange-and-merge kernel at N > 1
         "clocks": clocks.summary(),
         "parity": parity,
     }
@@ -769,14 +818,17 @@ def run_ours(args: argparse.Namespace) -> None:
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
-        # The graphs hold NCCL work: every reference to them (the graphs and the replay closure) goes
-        # before the process group does, or the group's destruction waits for them for good.
+        # The graphs hold cross-rank work: every reference to them (the graphs and the replay
+        # closure) goes first; each rank's exchange region is released only after every rank has
+        # finished its last exchange (the barrier), then the process group goes.
         import gc
 
         del run, graphs
         gc.collect()
         torch.cuda.synchronize()
         dist.barrier()
+        for L in layers:
+            L.xchg.close()
         dist.destroy_process_group()
 
 
@@ -793,7 +845,7 @@ def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) ->
     """The long-context leg at this world size: `--long-layers` layers sharded by block range over
     the ranks, the top-K chosen globally across shards at N > 1 (every rank's bounds all-gathered,
     the same select on every rank, each admitting and attending its part), the int8 cold tier in
-    HBM, a fresh query of the ring each step, the partials all-gathered and merged per layer. Each
+    HBM, a fresh query of the ring each step, the partials exchanged over NVLink and merged per layer. Each
     layer holds its own stores (about 30 GB at N = 1), so no layer-step reads another's data from
     L2. Reported per layer-step and as decode tokens/s of the 32-layer model (8 sequences per step,
     32 layer-steps each at the measured time)."""
@@ -828,8 +880,7 @@ def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) ->
             select_admit(L, r, step_no)
             attention_call(L, geo, r)
             if world > 1:
-                L.packed.exchange()
-                L.packed.merge(torch.bfloat16, out=finals[i])
+                L.xchg.exchange(finals[i])
 
     step_no = 0
     for w in range(max(args.warmup, R)):
@@ -848,7 +899,7 @@ def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) ->
         with torch.cuda.graph(gph):
             token(r, step_no + 1 + r)
         graphs.append(gph)
-    del gph  # the graphs hold NCCL work at N > 1: only `graphs` may keep them, so that dropping it frees them
+    del gph  # the graphs hold cross-rank work at N > 1: only `graphs` may keep them, so that dropping it frees them
     pos = [0]
 
     def run() -> None:
@@ -969,8 +1020,8 @@ def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) ->
         "clocks": clocks.summary(),
         "build_s": round(build_s, 1),
         "max_memory_gb_rank0": round(mem_gb, 1),
-        "timing": "one CUDA graph per query of the ring (selection, admit, attention per layer; at N > 1 the bounds and partials all-gathers "
-                  "captured too), CUDA events over the timed steps, max over ranks",
+        "timing": "one CUDA graph per query of the ring (selection, admit, attention per layer; at N > 1 the NCCL all-gather of the bounds "
+                  "and the peer-store exchange of the partials captured too), CUDA events over the timed steps, max over ranks",
     }
     del graphs, run
     import gc
@@ -1427,7 +1478,7 @@ def main() -> None:
     elif args.workload == "ragged":
         run_ragged(args)
     elif args.profile_calls:
-        profile_calls(args)
+        profile_long_calls(args) if args.profile_long else profile_calls(args)
     else:
         run_ours(args)
 

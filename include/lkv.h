@@ -372,11 +372,37 @@ int lkv_status_poll(int* status, int clear);
  * the bound (tries, 1 .. 2^21) of the TMA-scored selection's tile waits, for every later call in
  * the process; LKV_DEBUG_SELECT_STALL_NEXT = 1 makes every scoring CTA of the next TMA-scored
  * selection first wait on a barrier that nothing completes, so that the wait runs out and the
- * failure path runs (status 1, poisoned output) with the GPU left usable. Not for production use;
- * not thread-safe.
+ * failure path runs (status 1, poisoned output) with the GPU left usable.
+ * LKV_DEBUG_EXCHANGE_WAIT_ITERS sets the bound (polls, 1 .. 2^22) of lkv_exchange_merge's wait for
+ * its peers. Not for production use; not thread-safe.
  */
-enum { LKV_DEBUG_SELECT_WAIT_ITERS = 1, LKV_DEBUG_SELECT_STALL_NEXT = 2 };
+enum { LKV_DEBUG_SELECT_WAIT_ITERS = 1, LKV_DEBUG_SELECT_STALL_NEXT = 2, LKV_DEBUG_EXCHANGE_WAIT_ITERS = 3 };
 int lkv_debug_set(int key, int64_t value);
+
+/*
+ * The cross-GPU exchange of a context-sharded layer's partials by peer stores over NVLink, merged
+ * by log-sum-exp (the n-way merge_lse of lazykv/exact.py:69-85; the reference is single-device and
+ * has no counterpart). Each rank allocates one region (lkv_exchange_alloc: cudaMalloc'd, zeroed,
+ * lkv_exchange_region_bytes(rows, d, world) bytes) and gets its 64-byte CUDA IPC handle; the ranks
+ * swap handles (any host channel) and open their peers' regions (lkv_exchange_open; closed with
+ * lkv_exchange_close, freed with lkv_exchange_free). lkv_exchange_merge, one launch per layer and
+ * step, takes this rank's partial (out [rows, d] float32, lse [rows]) and the regions of every rank
+ * in rank order (bases[rank] its own): it stores the rank's rows into every region, adds one to a
+ * per-row-group arrival counter there, waits until every rank's rows of this exchange have
+ * arrived (a bounded wait: on timeout the status word gets 1 and the rows become this rank's own
+ * partial), and writes the merge (merged [rows, d] in out_dtype, merged_lse [rows] optional).
+ * Every rank calls it the same number of times per region, with the same rows and d; consecutive
+ * calls alternate between two halves of the inbox, so one rank may run one exchange ahead of
+ * another. d % 4 == 0; world <= 64; rows <= 4,096. Graph-capturable (no host state per call).
+ */
+size_t lkv_exchange_region_bytes(int rows, int d, int world);
+int lkv_exchange_alloc(int rows, int d, int world, void** base, void* ipc_handle);
+int lkv_exchange_open(const void* ipc_handle, void** peer_base);
+int lkv_exchange_close(void* peer_base);
+int lkv_exchange_free(void* base);
+int lkv_exchange_merge(const float* out, const float* lse, int rows, int d, int world, int rank,
+                       void* const* bases, void* merged, int out_dtype, float* merged_lse,
+                       void* stream);
 
 /*
  * Log-sum-exp merge of n_parts partials. Replaces lazykv/exact.py:69-85 merge_lse (n_parts = 2)

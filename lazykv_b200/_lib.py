@@ -18,7 +18,7 @@ LIB_PATH = Path(__file__).resolve().parent / "liblkv_sm100.so"
 LKV_F32, LKV_BF16 = 0, 1
 LKV_COLD_INT8, LKV_COLD_PAIRS = 0, 1
 LKV_ORDER_BOUND, LKV_ORDER_BLOCK = 0, 1
-LKV_DEBUG_SELECT_WAIT_ITERS, LKV_DEBUG_SELECT_STALL_NEXT = 1, 2
+LKV_DEBUG_SELECT_WAIT_ITERS, LKV_DEBUG_SELECT_STALL_NEXT, LKV_DEBUG_EXCHANGE_WAIT_ITERS = 1, 2, 3
 LKV_DEV_WAIT_TIMEOUT, LKV_DEV_LIST_OVERFLOW = 1, 2
 
 _lib: ctypes.CDLL | None = None
@@ -39,6 +39,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_shard_plan": (c_int, [c_int, c_int, c_int, c_int, c_void_p]),
     "lkv_topk_merge_workspace": (c_size_t, [c_int, c_int]),
     "lkv_topk_merge": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int64, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "lkv_exchange_region_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "lkv_exchange_alloc": (c_int, [c_int, c_int, c_int, c_void_p, c_void_p]),
+    "lkv_exchange_open": (c_int, [c_void_p, c_void_p]),
+    "lkv_exchange_close": (c_int, [c_void_p]),
+    "lkv_exchange_free": (c_int, [c_void_p]),
+    "lkv_exchange_merge": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "lkv_quest_bounds": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p, c_int, c_int64, c_void_p]),
     "lkv_topk_gathered": (c_int, [c_void_p, c_int, c_int, c_int, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     "lkv_hot_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

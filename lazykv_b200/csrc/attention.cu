@@ -2057,12 +2057,29 @@ int sm_count() {
 
 // CTAs per KV head of the stream kernel: kStreamCtasPerSm per SM over the heads, or more when a
 // CTA's items could exceed its list (n_ub: an upper bound of a head's items; a CTA holds at most
-// ceil(n / P) items of each of the two segments, so ceil(n_ub / P) + 2 in all).
+// ceil(n / P) items of each of the two segments, so ceil(n_ub / P) + 2 in all). When the list
+// forces more than one wave of CTAs, P is chosen among [need, 3 need] (at most 32, the fold's fast
+// path, unless need is more) to minimise the waves times
+// a CTA's share (items plus a fixed cost of kStreamCtaCost items for its set-up and fold), so that
+// the last wave is not left mostly empty (64 heads x 4 CTAs on 148 SMs would be 1.73 waves).
+constexpr int64_t kStreamCtaCost = 64;
 int stream_per_head(int h, int64_t n_ub) {
-  int per = kStreamCtasPerSm * sm_count() / (h > 0 ? h : 1);
+  const int sms = kStreamCtasPerSm * sm_count();
+  const int hh = h > 0 ? h : 1;
+  int per = sms / hh;
   const int64_t need = (n_ub + kStreamListCap - 3) / (kStreamListCap - 2);
-  if (need > per) per = (int)need;
-  return per < 1 ? 1 : per;
+  if (need <= per) return per < 1 ? 1 : per;
+  int64_t best_p = need, best_cost = -1;
+  const int64_t top = 3 * need < 32 ? 3 * need : (need > 32 ? need : 32);
+  for (int64_t P = need; P <= top; ++P) {
+    const int64_t waves = (hh * P + sms - 1) / sms;
+    const int64_t cost = waves * (kStreamCtaCost + (n_ub + P - 1) / P);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_p = P;
+    }
+  }
+  return (int)best_p;
 }
 size_t stream_partial_bytes(int h, int g, int d, int64_t n_ub) {
   const int part = (g * d + 2 * g + 3) / 4 * 4;
@@ -2276,11 +2293,12 @@ int lkv_ragged_exact_attention(const void* q, int rows, int g, int d, int bs, in
 
 int lkv_device_status(int* status, int clear) {
   if (status == nullptr) return fail(LKV_ERR_PTR, "lkv_device_status: null pointer");
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   cudaError_t e = tu_device_status(&a, clear);
   if (e == cudaSuccess) e = select_device_status(&b, clear);
+  if (e == cudaSuccess) e = exchange_device_status(&c, clear);
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_device_status: %s", cudaGetErrorString(e));
-  *status = a != 0 ? a : b;
+  *status = a != 0 ? a : (b != 0 ? b : c);
   return LKV_OK;
 }
 
@@ -2301,6 +2319,7 @@ int lkv_status_attach(void) {
   e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev_word), host_word, 0);
   if (e == cudaSuccess) e = tu_status_attach(dev_word);
   if (e == cudaSuccess) e = select_status_attach(dev_word);
+  if (e == cudaSuccess) e = exchange_status_attach(dev_word);
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_status_attach: %s", cudaGetErrorString(e));
   return LKV_OK;
 }

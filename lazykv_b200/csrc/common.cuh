@@ -29,6 +29,10 @@ CUresult encode_tiled(CUtensorMap* out, CUtensorMapDataType dt, cuuint32_t rank,
 cudaError_t select_device_status(int* status, int clear);
 // Points select.cu's kernels on the current device at the host mirror of the status word.
 cudaError_t select_status_attach(int* mirror);
+// The exchange's status word (exchange.cu), its host mirror, and the bound of its wait.
+cudaError_t exchange_device_status(int* status, int clear);
+cudaError_t exchange_status_attach(int* mirror);
+int exchange_set_wait_iters(int64_t iters);
 
 constexpr int kNumSMs = 148;  // B200
 

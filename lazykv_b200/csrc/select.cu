@@ -1143,6 +1143,8 @@ int lkv_debug_set(int key, int64_t value) {
     case LKV_DEBUG_SELECT_STALL_NEXT:
       g_sel_stall_next = value != 0;
       return LKV_OK;
+    case LKV_DEBUG_EXCHANGE_WAIT_ITERS:
+      return exchange_set_wait_iters(value);
     default:
       return fail(LKV_ERR_ARG, "lkv_debug_set: unknown key %d", key);
   }

@@ -102,6 +102,70 @@ class PackedPartial:
         return merged
 
 
+class PeerExchange:
+    """The per-layer exchange of partials by peer stores over NVLink (lkv_exchange_merge): a rank's
+    (out, lse) go straight into every peer's inbox and each rank merges what arrived, in one
+    launch, instead of an NCCL all-gather and a merge launch. Built collectively: every rank
+    allocates its region, the 64-byte IPC handles are all-gathered over `group` (once, at set-up),
+    and every rank opens its peers'. `exchange` is graph-capturable. `close` (or garbage
+    collection) releases the peers' mappings and the region; every rank must stop calling
+    `exchange` first."""
+
+    def __init__(self, rows: int, d: int, group: dist.ProcessGroup | None = None, device: torch.device | None = None) -> None:
+        self.rows, self.d = rows, d
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(self.device):
+            L.call("lkv_exchange_alloc", rows, d, self.world, ctypes.byref(base), handle)
+        self._own = base.value
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        bases = []
+        self._opened = []
+        with torch.cuda.device(self.device):
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self._own)
+                    continue
+                peer = ctypes.c_void_p()
+                L.call("lkv_exchange_open", (ctypes.c_char * 64).from_buffer_copy(hb), ctypes.byref(peer))
+                self._opened.append(peer.value)
+                bases.append(peer.value)
+        self._bases = (ctypes.c_void_p * self.world)(*bases)
+        # This rank's partial, float32: out [rows, d] then lse [rows] (one buffer, as PackedPartial).
+        self.buf = torch.zeros(rows * (d + 1), dtype=torch.float32, device=self.device)
+        self.out = self.buf[: rows * d].view(rows, d)
+        self.lse = self.buf[rows * d :]
+
+    def exchange(self, merged: torch.Tensor, merged_lse: torch.Tensor | None = None) -> torch.Tensor:
+        """Push this rank's partial (self.out, self.lse) to every rank, wait for theirs, merge into
+        `merged` [rows, d] (bf16 or float32) and optionally `merged_lse` [rows]."""
+        L.call("lkv_exchange_merge", L.ptr(self.out), L.ptr(self.lse), self.rows, self.d, self.world, self.rank, self._bases, L.ptr(merged),
+               L.dtype_code(merged.dtype), L.ptr(merged_lse), L.stream_handle(self.device))
+        return merged
+
+    def close(self) -> None:
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                L.call("lkv_exchange_close", ctypes.c_void_p(p))
+            L.call("lkv_exchange_free", ctypes.c_void_p(self._own))
+        self._opened, self._own = [], None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
 def gather_candidates(ids: torch.Tensor, bounds: torch.Tensor, group: dist.ProcessGroup | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Every rank's local candidates (ids [h, k] int32, ascending; bounds [h, k] float32) as
     [h, world * k] in rank order, i.e. ascending id across the node (ranks hold ascending ranges)."""
