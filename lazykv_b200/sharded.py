@@ -302,3 +302,28 @@ def host_reference_global_topk(ids: np.ndarray, bounds: np.ndarray, k: int) -> n
         order = np.lexsort((ids[j], -bounds[j].astype(np.float64)))
         out[j] = np.sort(ids[j][order[:k]])
     return out
+
+
+def gathered_layout(plans: list[ShardPlan]) -> tuple[list[int], int]:
+    """The ranks' candidate counts and the common row stride of the gathered bounds buffer
+    [world, h, ld] that GlobalSelection all-gathers."""
+    seg_n = [p.n_cand for p in plans]
+    return seg_n, max(seg_n)
+
+
+def host_reference_gathered_topk(gathered: np.ndarray, seg_n: list[int], k: int, rank: int, out_base: int) -> np.ndarray:
+    """What lkv_topk_gathered writes for `rank`, on the host, for tests and tooling: over every
+    rank's bounds (gathered [world, h, ld], rank r's first seg_n[r] entries, in block order), the k
+    highest per row with ties to the lower block id; rank's chosen as local ids (out_base + index
+    in its range) ascending, then -1, min(k, seg_n[rank]) columns."""
+    world, h, _ = gathered.shape
+    starts = np.concatenate([[0], np.cumsum(seg_n)])
+    cols = min(k, seg_n[rank])
+    out = np.full((h, cols), -1, dtype=np.int64)
+    for j in range(h):
+        row = np.concatenate([gathered[r, j, : seg_n[r]].astype(np.float64) for r in range(world)])
+        row = np.where(row == 0.0, 0.0, row)  # +0 and -0 tie
+        order = np.lexsort((np.arange(len(row)), -row))[: min(k, len(row))]
+        mine = np.sort(order[(order >= starts[rank]) & (order < starts[rank + 1])]) - starts[rank]
+        out[j, : len(mine)] = mine + out_base
+    return out

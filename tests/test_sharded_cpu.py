@@ -17,7 +17,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle as O
-from lazykv_b200.sharded import gather_candidates, gather_partials, host_reference_global_topk, shard_plan
+from lazykv_b200.sharded import (gather_candidates, gather_partials, gathered_layout, host_reference_gathered_topk, host_reference_global_topk,
+                                 shard_plan)
 
 
 @pytest.mark.parametrize("n_sealed", [2, 3, 17, 1000, 8191])
@@ -155,3 +156,49 @@ def test_gathered_candidates_give_the_single_gpu_selection() -> None:
     got = host_reference_global_topk(ids, bounds, k_total)
     want = np.sort(O.top_blocks(bound, k_total) + 1, axis=1)
     assert np.array_equal(got, want)
+
+
+def _rank_gathered_bounds(rank: int, world: int, port: int, results: dict) -> None:  # noqa: ANN001
+    """GlobalSelection's protocol with the oracle's bounds in place of the kernel's: each rank scores
+    its own candidates into a [h, ld] buffer (bf16-rounded, as the kernel stores them), one
+    all-gather, then every rank's part of the global selection (host reference of
+    lkv_topk_gathered)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, k, _, _, _, _ = _layer(seed=7, n=61)
+        h, t, d = k.shape
+        bs, n = 16, t // 16
+        k = (np.round(k * 2) / 2).astype(np.float32)  # coarse keys: ties at the threshold across ranks
+        kmin, kmax = O.block_minmax(k, bs)
+        k_total = 13
+        plans = [shard_plan(n, k_total, world, r) for r in range(world)]
+        seg_n, ld = gathered_layout(plans)
+        p = plans[rank]
+        bound = O.quest_bound(q.astype(np.float32), kmin[:, p.cand_first : p.cand_first + p.n_cand], kmax[:, p.cand_first : p.cand_first + p.n_cand],
+                              "bfloat16")
+        send = torch.zeros((h, ld), dtype=torch.float32)
+        send[:, : p.n_cand] = torch.from_numpy(np.asarray(bound, dtype=np.float32))
+        gathered = torch.zeros((world * h, ld), dtype=torch.float32)
+        dist.all_gather_into_tensor(gathered, send)
+        mine = host_reference_gathered_topk(gathered.view(world, h, ld).numpy(), seg_n, k_total, rank, p.cand_first - p.lo)
+        parts = [None] * world
+        dist.all_gather_object(parts, (mine, p.lo))
+        results[rank] = (parts, k_total, q, kmin, kmax)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gathered_bounds_give_the_single_gpu_selection(world: int) -> None:
+    """The ranks' parts of the global selection over all-gathered bounds, mapped back to block ids
+    and concatenated in rank order, are the unsharded top-K (ties to the lower block ids)."""
+    res = _spawn(_rank_gathered_bounds, world)
+    parts, k_total, q, kmin, kmax = res[0]
+    got = np.concatenate([np.where(m >= 0, m + lo, -1) for m, lo in parts], axis=1)
+    bound = O.quest_bound(q.astype(np.float32), kmin[:, 1:], kmax[:, 1:], "bfloat16")
+    want = np.sort(O.top_blocks(bound, k_total) + 1, axis=1)
+    for j in range(got.shape[0]):
+        row = got[j][got[j] >= 0]
+        assert np.array_equal(row, want[j])
+    assert all(np.array_equal(a[0], b[0]) for a, b in zip(parts, res[1][0]))  # every rank computed the same parts
