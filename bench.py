@@ -67,6 +67,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--layers", type=int, default=N_LAYERS - DENSE, help="selecting layers (the metric runs all 14; fewer for profiling)")
     p.add_argument("--queries", type=int, default=8, help="queries in each layer's ring: decode token s uses query s mod this")
     p.add_argument("--drift", type=float, default=0.15, help="a ring query is a base query + drift x N(0,1) (0.15: a hit rate near 0.84, inside the 0.79-1.0 the reference measured with real models)")
+    p.add_argument("--admit-first", action="store_true",
+                   help="admit and fetch before the attention on one stream (default: the resident selection, the attention, and the admit "
+                        "beside it on a side stream)")
     p.add_argument("--no-model", action="store_true", help="skip the model legs (32K-token greedy decode; the 130,048-token capacity sweep)")
     p.add_argument("--no-long-ctx", action="store_true", help="skip the 1,048,576-token leg (8 sequences, head_dim 128, global top-K)")
     p.add_argument("--long-layers", type=int, default=4, help="layers of the long-context leg held and timed (each 30 GB at N = 1)")
@@ -293,14 +296,25 @@ def select_call(L, geo: dict, r: int = 0) -> None:  # noqa: ANN001
                  by_block=True)
 
 
-def admit_call(L, geo: dict, step: int, cold_store=None) -> None:  # noqa: ANN001
+def admit_call(L, geo: dict, step: int, cold_store=None, hot: bool = True) -> None:  # noqa: ANN001
     """The device admit of L.chosen (lazykv/tiered.py:389-463: LRU victims, the misses fetched from
-    the store and dequantised into their slots); the admitted slots go to the hot list."""
+    the store and dequantised into their slots); with `hot`, the admitted slots go to the hot list."""
     from lazykv_b200 import kernels as K
 
     so = geo["sel_off"]
     K.tier_admit(L.chosen, L.block_slot, L.slot_block, L.last_used, L.evicted_at, step, L.records if cold_store is None else cold_store, L.pool,
-                 L.miss_blk, L.miss_slot, L.n_miss, slots_out=L.list[:, so : so + geo["k_local"]])
+                 L.miss_blk, L.miss_slot, L.n_miss, slots_out=L.list[:, so : so + geo["k_local"]] if hot else None)
+
+
+def resident_select_call(L, geo: dict, r: int = 0) -> None:  # noqa: ANN001
+    """The selection of query r for an attention before the admit (lkv_quest_topk_resident): the
+    hot list gets the chosen blocks' current slots (-1 for those not resident), the bitmap only the
+    resident ones, so the exact pass covers the misses from their records."""
+    from lazykv_b200 import kernels as K
+
+    so = geo["sel_off"]
+    K.quest_topk_resident(L.q_ring[r], L.kmin, L.kmax, geo["cand_lo"] - geo["lo"], geo["n_cand"], geo["k_local"], L.chosen, L.block_slot,
+                          L.list[:, so : so + geo["k_local"]], L.bitmap)
 
 
 def attention_call(L, geo: dict, r: int = 0, cold_store=None) -> None:  # noqa: ANN001
@@ -322,10 +336,22 @@ def select_admit_call(L, geo: dict, r: int, step: int, cold_store=None) -> None:
                        L.miss_slot, L.n_miss, slots_out=L.list[:, so : so + geo["k_local"]])
 
 
-def layer_step(L, geo: dict, r: int = 0, step: int = 1, cold_store=None, events: list | None = None) -> None:  # noqa: ANN001
-    """One layer-step of the hot path with query r (all launches on the current stream): score +
-    top-K, then the device admit and the fetch of misses (one call), then the hot and cold passes
-    and their merge in one attention launch."""
+def layer_step(L, geo: dict, r: int = 0, step: int = 1, cold_store=None, events: list | None = None, side=None) -> None:  # noqa: ANN001
+    """One layer-step of the hot path with query r. Without `side` (all launches on the current
+    stream): score + top-K, then the device admit and the fetch of misses (one call), then the hot
+    and cold passes and their merge in one attention launch. With a side stream: the resident
+    selection, then the attention on the current stream while the admit and the fetch run on
+    `side` (forked after the selection; the caller joins `side` before the layer's next step)."""
+    if side is not None:
+        import torch
+
+        resident_select_call(L, geo, r)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            admit_call(L, geo, step, cold_store, hot=False)
+        attention_call(L, geo, r, cold_store)
+        return
+
 
     def mark() -> None:
         if events is not None:
@@ -534,13 +560,18 @@ def run_ours(args: argparse.Namespace) -> None:
     R = geo["n_q"]
     finals = [torch.empty((HQ, D), dtype=torch.bfloat16, device=dev) for _ in layers]
 
+    admit_side = None if args.admit_first else torch.cuda.Stream()
+
     def token(r: int, step_no: int, cold_of=None) -> None:
         """One decode token with query r of the ring: every selecting layer's hot path (and, at N > 1,
-        the exchange of the layer's partials over NVLink and their merge on every rank)."""
+        the exchange of the layer's partials over NVLink and their merge on every rank); the
+        admits run beside the attentions on a side stream, joined at the token's end."""
         for i, L in enumerate(layers):
-            layer_step(L, geo, r, step_no, None if cold_of is None else cold_of(L))
+            layer_step(L, geo, r, step_no, None if cold_of is None else cold_of(L), side=admit_side)
             if world > 1:
                 L.xchg.exchange(finals[i])
+        if admit_side is not None:
+            torch.cuda.current_stream().wait_stream(admit_side)
 
     # Warm-up: the first token admits every selected block of query 0; then the ring of queries.
     step_no = 0
@@ -646,8 +677,12 @@ def run_ours(args: argparse.Namespace) -> None:
         del gs
         return us
 
-    sel_us = group_us(lambda r, st: [select_call(L, geo, r) for L in layers])
-    sel_admit_us = group_us(lambda r, st: [select_admit_call(L, geo, r, st) for L in layers])
+    if args.admit_first:
+        sel_us = group_us(lambda r, st: [select_call(L, geo, r) for L in layers])
+        sel_admit_us = group_us(lambda r, st: [select_admit_call(L, geo, r, st) for L in layers])
+    else:  # the resident selection, and the admit (with the fetch) after it on the same stream
+        sel_us = group_us(lambda r, st: [resident_select_call(L, geo, r) for L in layers])
+        sel_admit_us = group_us(lambda r, st: [(resident_select_call(L, geo, r), admit_call(L, geo, st, hot=False)) for L in layers])
     attn_us = group_us(lambda r, st: [attention_call(L, geo, r) for L in layers])
     kernel_us = {"select": sel_us, "admit": max(0.0, sel_admit_us - sel_us), "attention": attn_us}
 
@@ -723,9 +758,11 @@ def run_ours(args: argparse.Namespace) -> None:
             e_pos[0] += 1
             for i, L in enumerate(layers):
                 L.q_ring[r].copy_(q_host[r, i], non_blocking=True)
-                layer_step(L, geo, r, 10**9 + e_pos[0])
+                layer_step(L, geo, r, 10**9 + e_pos[0], side=admit_side)
                 L.xchg.exchange(finals[i])
                 o_host[i].copy_(finals[i], non_blocking=True)
+            if admit_side is not None:
+                torch.cuda.current_stream().wait_stream(admit_side)
 
         for _ in range(2):
             e2e_step()

@@ -328,6 +328,24 @@ int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32
                    int32_t* slots_out, int64_t slots_ld, void* stream);
 
 /*
+ * The selection for an attention that runs before (or beside) the step's admit: lkv_quest_topk in
+ * LKV_ORDER_BLOCK, plus, for the j-th chosen block b of head h, hot[h * hot_ld + j] =
+ * block_slot[h * cap + b] when that is a slot (>= 1), else -1, and a bitmap that marks only those
+ * resident blocks. An exact pass over the bitmap's complement then covers the chosen blocks that
+ * are not resident yet (from their records: the values a fetch would put in a slot), so the
+ * output equals the admit-first order's, and lkv_tier_admit (with slots_out null) can run after
+ * the attention or on another stream: its victims are never slots this hot list names. Same
+ * selection paths and workspace as lkv_quest_topk (block order, h <= 64). The reference admits
+ * before it attends (lazykv/tiered.py:389-487); no counterpart for the split.
+ */
+int lkv_quest_topk_resident(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,
+                            const void* kmax, int meta_dtype, int64_t m_head, int first_block,
+                            int n_cand, int k, int bound_mode, int32_t* out_blocks, int out_ld,
+                            const int32_t* block_slot, int cap, int32_t* hot, int64_t hot_ld,
+                            uint32_t* bitmap, int bitmap_words, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/*
  * lkv_quest_topk in block order followed by lkv_tier_admit of its selection, in one call: the
  * selection written to out_blocks (and the bitmap) is made resident (LRU victims, misses fetched and
  * dequantised into their slots, slots_out = the slots of the selected blocks). Replaces

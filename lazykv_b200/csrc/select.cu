@@ -412,6 +412,17 @@ __global__ void __launch_bounds__(kSelectThreads) topk_kernel(const uint64_t* __
 // (lowest ids first), so the selected ids come out in ascending block-id order with no sort. Every
 // CTA reaches every cluster barrier (no early exit).
 
+// The resident split (lkv_quest_topk_resident): for each chosen block, its slot before this step's
+// admit (block_slot [h, bs_ld], 1.. or -1) goes to hot [h, hot_ld] at the block's position, -1 for a
+// block not resident, and the bitmap marks only the resident ones, so that an exact pass over the
+// bitmap's complement covers the misses and the admit can run after, or beside, the attention.
+struct ResidentOut {
+  const int32_t* block_slot;  // null: the plain selection
+  int64_t bs_ld;
+  int32_t* hot;
+  int64_t hot_ld;
+};
+
 constexpr int kClusterThreads = 256;
 constexpr int kClusterMax = 16;
 constexpr int kClusterMaxPer = 4096;   // keys per CTA (in shared memory)
@@ -423,7 +434,7 @@ constexpr size_t kKeysOffset = kHistBytes + 256;  // then the keys (64-bit, or 3
 __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(const uint64_t* __restrict__ keys_all, uint32_t* __restrict__ hist0,
                                                                      int n_cand, int k, int first_block, int n_passes, int per,
                                                                      int32_t* __restrict__ out_blocks, int out_ld, uint32_t* __restrict__ bitmap,
-                                                                     int bitmap_words) {
+                                                                     int bitmap_words, const ResidentOut res) {
   cg::cluster_group cluster = cg::this_cluster();
   const int c = (int)cluster.block_rank();
   const int C = (int)cluster.num_blocks();
@@ -537,7 +548,12 @@ __global__ void __launch_bounds__(kClusterThreads) topk_cluster_kernel(const uin
     if (take && pos < (uint32_t)kk) {
       const int blk = first_block + lo + i;
       out_blocks[(int64_t)j * out_ld + pos] = blk;
-      if (bitmap != nullptr && blk / 32 < bitmap_words) atomicOr(&bitmap[(int64_t)j * bitmap_words + blk / 32], 1u << (blk % 32));
+      int32_t slot = 1;
+      if (res.block_slot != nullptr) {
+        slot = __ldcg(res.block_slot + (int64_t)j * res.bs_ld + blk);
+        res.hot[(int64_t)j * res.hot_ld + pos] = slot >= 1 ? slot : -1;
+      }
+      if (bitmap != nullptr && slot >= 1 && blk / 32 < bitmap_words) atomicOr(&bitmap[(int64_t)j * bitmap_words + blk / 32], 1u << (blk % 32));
       ++pos;
     }
   }
@@ -554,7 +570,7 @@ inline int cluster_size_for(int n_cand) {
 }
 
 int launch_topk_cluster(int h, cudaStream_t st, const uint64_t* keys, uint32_t* hist0, int n_cand, int k, int first_block, int n_passes,
-                        int32_t* out_blocks, int out_ld, uint32_t* bitmap, int bitmap_words) {
+                        int32_t* out_blocks, int out_ld, uint32_t* bitmap, int bitmap_words, const ResidentOut& res) {
   static bool attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -567,7 +583,7 @@ int launch_topk_cluster(int h, cudaStream_t st, const uint64_t* keys, uint32_t* 
   const int C = cluster_size_for(n_cand);
   const int per = (n_cand + C - 1) / C;
   cudaError_t e = launch_pdl(topk_cluster_kernel, dim3(C, h), dim3(kClusterThreads), (size_t)per * sizeof(uint64_t), st, C, keys, hist0, n_cand,
-                             k, first_block, n_passes, per, out_blocks, out_ld, bitmap, bitmap_words);
+                             k, first_block, n_passes, per, out_blocks, out_ld, bitmap, bitmap_words, res);
   if (e != cudaSuccess) return fail(LKV_ERR_CUDA, "lkv_quest_topk(cluster select, %d CTAs x %d heads): %s", C, h, cudaGetErrorString(e));
   return LKV_OK;
 }
@@ -625,6 +641,7 @@ struct SelParams {
   uint32_t* keys;   // [h][n_cand] orderable bounds
   uint32_t wait_iters;  // bound of each TMA wait (tries)
   int stall;            // test hook: 1 = wait on a barrier that nothing completes before scoring
+  ResidentOut res;      // the resident split (null block_slot: off)
 };
 
 // One 3-D tile load global -> this CTA's shared memory under an L2 cache policy. No multicast.
@@ -867,7 +884,13 @@ __global__ void __launch_bounds__(kPkThreads) quest_pick_kernel(const __grid_con
     const uint32_t pos = sh_pos0 + gt_before + min(eq_before, room);
     const bool take = !failed && (gt[kp] || (eq[kp] && eq_before < room)) && pos < (uint32_t)kk;
     if (take) sp.out_blocks[(int64_t)j * sp.out_ld + pos] = b;
-    const uint32_t word = __ballot_sync(0xffffffffu, take);  // bit l: block 32 * (b / 32) + l
+    bool mark = take;
+    if (take && sp.res.block_slot != nullptr) {  // the resident split: the slot before this step's admit
+      const int32_t slot = __ldcg(sp.res.block_slot + (int64_t)j * sp.res.bs_ld + b);
+      sp.res.hot[(int64_t)j * sp.res.hot_ld + pos] = slot >= 1 ? slot : -1;
+      mark = slot >= 1;
+    }
+    const uint32_t word = __ballot_sync(0xffffffffu, mark);  // bit l: block 32 * (b / 32) + l
     if (sp.bitmap != nullptr && lane == 0 && b < 32 * w_hi && b / 32 < W) sp.bitmap[(int64_t)j * W + b / 32] = word;
   }
   if (sp.bitmap != nullptr) {  // the words outside the candidates' span: zero (first and last CTA)
@@ -878,7 +901,10 @@ __global__ void __launch_bounds__(kPkThreads) quest_pick_kernel(const __grid_con
   }
   if (failed) {  // a scoring wait ran out: every listed id -1 (the bitmap words above are empty)
     const int p0 = (int)((int64_t)sp.k * c / C), p1 = (int)((int64_t)sp.k * (c + 1) / C);
-    for (int p = p0 + tid; p < p1; p += blockDim.x) sp.out_blocks[(int64_t)j * sp.out_ld + p] = -1;
+    for (int p = p0 + tid; p < p1; p += blockDim.x) {
+      sp.out_blocks[(int64_t)j * sp.out_ld + p] = -1;
+      if (sp.res.block_slot != nullptr) sp.res.hot[(int64_t)j * sp.res.hot_ld + p] = -1;
+    }
   }
   if (c == 0 && tid < 256) sp.hist0[(int64_t)j * 256 + tid] = 0u;  // zero for the next call (every CTA read it before the barrier above)
   cluster_sync_relaxed();  // no CTA leaves while another may still read its shared memory; every CTA read the failure word
@@ -1161,7 +1187,8 @@ namespace {
 
 int quest_topk_impl(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax, int meta_dtype, int64_t m_head,
                     int first_block, int n_cand, int k, int bound_mode, int order, int32_t* out_blocks, int out_ld, float* out_bound,
-                    uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes, void* stream) {
+                    uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes, void* stream,
+                    const ResidentOut& res = ResidentOut{nullptr, 0, nullptr, 0}) {
   if (!dtype_ok(q_dtype) || !dtype_ok(meta_dtype) || !dtype_ok(bound_mode))
     return fail(LKV_ERR_ARG, "lkv_quest_topk: bad dtype (q %d, meta %d, bound %d)", q_dtype, meta_dtype, bound_mode);
   if (h <= 0 || hq <= 0 || hq % h != 0) return fail(LKV_ERR_ARG, "lkv_quest_topk: %d query heads do not group over %d KV heads", hq, h);
@@ -1207,6 +1234,7 @@ int quest_topk_impl(const void* q, int q_dtype, int hq, int h, int d, const void
       sp.keys = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(workspace) + kKeysOffset);
       sp.wait_iters = g_sel_wait_iters;
       sp.stall = g_sel_stall_next;
+      sp.res = res;
       g_sel_stall_next = 0;
       return launch_select(g, sp, h, st);
     }
@@ -1215,6 +1243,8 @@ int quest_topk_impl(const void* q, int q_dtype, int hq, int h, int d, const void
   // radix pass, and a cluster per head finishes the select from the keys.
   const bool cluster = order == LKV_ORDER_BLOCK && h <= kHistHeads && cluster_size_for(n_cand) > 0;
   if (!cluster && k > kMaxK) return fail(LKV_ERR_ARG, "lkv_quest_topk: k=%d exceeds %d", k, kMaxK);
+  if (!cluster && res.block_slot != nullptr)
+    return fail(LKV_ERR_ARG, "lkv_quest_topk_resident: needs block order, at most %d heads and %d candidates", kHistHeads, kClusterMax * kClusterMaxPer);
   uint32_t* h0 = cluster ? hist0 : nullptr;
   int rc;
   if (q_dtype == LKV_BF16 && meta_dtype == LKV_BF16)
@@ -1228,7 +1258,7 @@ int quest_topk_impl(const void* q, int q_dtype, int hq, int h, int d, const void
   if (rc) return rc;
   if ((rc = launched("lkv_quest_topk(score)"))) return rc;
   if (cluster) {
-    if ((rc = launch_topk_cluster(h, st, keys, hist0, n_cand, k, first_block, n_passes, out_blocks, out_ld, bitmap, bitmap_words))) return rc;
+    if ((rc = launch_topk_cluster(h, st, keys, hist0, n_cand, k, first_block, n_passes, out_blocks, out_ld, bitmap, bitmap_words, res))) return rc;
     return launched("lkv_quest_topk(cluster select)");
   }
   int P = 1;
@@ -1253,6 +1283,18 @@ int lkv_quest_topk(const void* q, int q_dtype, int hq, int h, int d, const void*
                    void* workspace, size_t workspace_bytes, void* stream) {
   return quest_topk_impl(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode, order, out_blocks, out_ld,
                          out_bound, bitmap, bitmap_words, workspace, workspace_bytes, stream);
+}
+
+int lkv_quest_topk_resident(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax, int meta_dtype, int64_t m_head,
+                            int first_block, int n_cand, int k, int bound_mode, int32_t* out_blocks, int out_ld, const int32_t* block_slot,
+                            int cap, int32_t* hot, int64_t hot_ld, uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (block_slot == nullptr || hot == nullptr) return fail(LKV_ERR_PTR, "lkv_quest_topk_resident: null pointer");
+  if (cap < first_block + n_cand || hot_ld < k) return fail(LKV_ERR_ARG, "lkv_quest_topk_resident: block_slot of %d blocks or hot row of %lld < k", cap,
+                                                           (long long)hot_ld);
+  const ResidentOut res{block_slot, (int64_t)cap, hot, hot_ld};
+  return quest_topk_impl(q, q_dtype, hq, h, d, kmin, kmax, meta_dtype, m_head, first_block, n_cand, k, bound_mode, LKV_ORDER_BLOCK, out_blocks,
+                         out_ld, nullptr, bitmap, bitmap_words, workspace, workspace_bytes, stream, res);
 }
 
 int lkv_quest_topk_admit(const void* q, int q_dtype, int hq, int h, int d, const void* kmin, const void* kmax, int meta_dtype, int64_t m_head,

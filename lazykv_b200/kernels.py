@@ -127,6 +127,26 @@ def quest_topk(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, firs
     return out_blocks, bound
 
 
+def quest_topk_resident(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int, n_cand: int, k: int,
+                        out_blocks: torch.Tensor, block_slot: torch.Tensor, hot: torch.Tensor, bitmap: torch.Tensor,
+                        bound_dtype: torch.dtype | None = None, ws_slot: int = 1) -> torch.Tensor:
+    """The selection (block order) for an attention before the admit: out_blocks [h, k] the chosen
+    ids, hot [h, >= k] (a view, unit column stride) each chosen block's current slot or -1, and the
+    bitmap of the resident chosen blocks only (lkv_quest_topk_resident)."""
+    dev = require_cuda(query, kmin, kmax, out_blocks, block_slot, hot, bitmap)
+    hq, d = query.shape[-3] if query.dim() == 4 else query.shape[0], query.shape[-1]
+    q = query.reshape(hq, d).contiguous()
+    h = kmin.shape[-3]
+    bound_dtype = bound_dtype or q.dtype
+    if hot.stride(-1) != 1 or hot.shape[-1] < k or block_slot.stride(-1) != 1 or not block_slot.is_contiguous():
+        raise ValueError("quest_topk_resident: hot must be [h, >=k] with unit column stride and block_slot contiguous [h, cap]")
+    ws = workspace(dev, int(L.lib().lkv_quest_topk_workspace(h, n_cand)), ws_slot)
+    call("lkv_quest_topk_resident", ptr(q), dtype_code(q.dtype), hq, h, d, ptr(kmin), ptr(kmax), dtype_code(kmin.dtype), kmin.stride(-3), first_block,
+         n_cand, k, dtype_code(bound_dtype), ptr(out_blocks), out_blocks.stride(0), ptr(block_slot), block_slot.shape[-1], ptr(hot), hot.stride(0),
+         ptr(bitmap), bitmap.shape[-1], ptr(ws), ws.numel(), stream_handle(dev))
+    return out_blocks
+
+
 def quest_bounds(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int, n_cand: int, out: torch.Tensor,
                  bound_dtype: torch.dtype | None = None) -> torch.Tensor:
     """The Quest bound of candidates [first_block, first_block + n_cand) into out [h, >= n_cand]

@@ -72,3 +72,50 @@ def test_select_admit_equals_the_two_calls(d: int) -> None:
         total_miss += int(a["n_miss"].sum())
     assert total_miss > h * k  # the first step misses everything, later steps some
     assert K.device_status() == 0
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_resident_split_attends_as_the_admit_first_order(d: int) -> None:
+    """lkv_quest_topk_resident: the chosen ids equal lkv_quest_topk's; the hot list holds each chosen
+    block's slot before the admit (or -1) and the bitmap only the resident ones; the attention over
+    them (misses in the exact pass, from their records) equals the attention after the admit, and
+    the admit run afterwards (without a hot list) leaves the same tables and pool."""
+    from lazykv_b200 import kernels as K
+
+    h, nblk, k = 8, 4096, 1022
+    kmin, kmax, rec, queries, a = _state(h, nblk, k, d, seed=d + 1)
+    b = {n: t.clone() for n, t in a.items()}
+    strides = (h * 2 * 16 * d, 2 * 16 * d, d)
+    for step, q in enumerate(queries, start=1):
+        # a: admit first, then attend the slots it wrote
+        K.quest_topk_admit(q, kmin, kmax, 1, nblk - 2, k, a["chosen"], a["bitmap"], a["block_slot"], a["slot_block"], a["last_used"],
+                           a["evicted_at"], step, rec, a["pool"], a["miss_blk"], a["miss_slot"], a["n_miss"], slots_out=a["slots"])
+        oa, la = K.exact_attention(q, a["pool"], a["pool"][:, :, 1], strides, a["slots"], 16, rec, 1, nblk - 2, d**-0.5, 16, excluded=a["bitmap"],
+                                   out_dtype=torch.float32)
+        # b: the resident split, the attention, then the admit
+        before = b["block_slot"].clone()
+        K.quest_topk_resident(q, kmin, kmax, 1, nblk - 2, k, b["chosen"], b["block_slot"], b["slots"], b["bitmap"])
+        ob, lb = K.exact_attention(q, b["pool"], b["pool"][:, :, 1], strides, b["slots"], 16, rec, 1, nblk - 2, d**-0.5, 16, excluded=b["bitmap"],
+                                   out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        want_hot = torch.gather(before, 1, b["chosen"].long())
+        want_hot = torch.where(want_hot >= 1, want_hot, torch.full_like(want_hot, -1))
+        assert torch.equal(b["slots"], want_hot)
+        bits = torch.zeros((h, b["bitmap"].shape[1] * 32), dtype=torch.bool, device=DEV)
+        for j in range(h):
+            res = b["chosen"][j][want_hot[j] >= 1].long()
+            bits[j, res] = True
+        words = b["bitmap"].view(torch.int32).cpu().numpy().view("uint32")
+        import numpy as np
+
+        got_bits = np.unpackbits(words.view(np.uint8), bitorder="little").reshape(h, -1).astype(bool)
+        assert np.array_equal(got_bits, bits.cpu().numpy())
+        assert torch.equal(a["chosen"], b["chosen"])
+        scale = oa.abs().max()
+        assert (ob - oa).abs().max() <= 1e-5 * scale and (lb - la).abs().max() <= 1e-5 * la.abs().max()
+        K.tier_admit(b["chosen"], b["block_slot"], b["slot_block"], b["last_used"], b["evicted_at"], step, rec, b["pool"], b["miss_blk"],
+                     b["miss_slot"], b["n_miss"])
+        torch.cuda.synchronize()
+        for name in ("block_slot", "slot_block", "last_used", "evicted_at", "n_miss", "pool"):
+            assert torch.equal(a[name], b[name]), name
+    assert K.device_status() == 0
