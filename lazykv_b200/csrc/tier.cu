@@ -47,6 +47,78 @@ __device__ uint32_t admit_scan(uint32_t v, uint32_t* warp_sums) {
   return r;
 }
 
+// The m smallest of n distinct 64-bit keys in keys[0, n) (shared memory) move to keys[0, m), in no
+// particular order: a radix select of the m-th smallest over the bits in which the keys differ (8
+// per pass, from the top), then a stable compaction of the keys at or below it. Each thread holds
+// its contiguous share of at most kAdmitSelPer keys in registers across the compaction.
+constexpr int kAdmitSelPer = 16;
+constexpr int kAdmitSelMax = kAdmitSelPer * kAdmitThreads;
+
+__device__ void select_smallest(uint64_t* keys, int n, int m, uint32_t* warp_sums) {
+  __shared__ unsigned long long sh_min, sh_max;
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sh_rem;
+  __shared__ uint64_t sh_prefix;
+  if (threadIdx.x == 0) {
+    sh_min = ~0ull;
+    sh_max = 0ull;
+    sh_rem = (uint32_t)m;
+  }
+  __syncthreads();
+  unsigned long long lmin = ~0ull, lmax = 0ull;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    lmin = min(lmin, (unsigned long long)keys[i]);
+    lmax = max(lmax, (unsigned long long)keys[i]);
+  }
+  atomicMin(&sh_min, lmin);
+  atomicMax(&sh_max, lmax);
+  __syncthreads();
+  const int hb = 63 - __clzll((long long)(sh_min ^ sh_max));  // the top bit in which keys differ (n >= 2 distinct keys)
+  uint64_t mask = hb >= 63 ? 0ull : ~((2ull << hb) - 1ull);    // the bits above it, equal in every key
+  uint64_t prefix = (uint64_t)sh_min & mask;
+  for (int shift = (hb / 8) * 8; shift >= 0; shift -= 8) {
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint64_t x = keys[i];
+      if ((x & mask) == prefix) atomicAdd(&hist[(x >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // the digit holding the rem-th smallest of the keys under the prefix
+      uint32_t rem = sh_rem, acc = 0u;
+      int dg = 255;
+      for (int b = 0; b < 256; ++b) {
+        if (acc + hist[b] >= rem) {
+          dg = b;
+          break;
+        }
+        acc += hist[b];
+      }
+      sh_rem = rem - acc;
+      sh_prefix = prefix | ((uint64_t)dg << shift);
+    }
+    __syncthreads();
+    prefix = sh_prefix;
+    mask |= 255ull << shift;
+  }
+  const uint64_t t = prefix;  // the m-th smallest key
+  // Stable compaction of the keys <= t (exactly m: the keys are distinct).
+  const int seg = (n + blockDim.x - 1) / blockDim.x;
+  const int lo = min(n, (int)threadIdx.x * seg), hi = min(n, lo + seg);
+  uint64_t mine[kAdmitSelPer];
+  uint32_t cnt = 0;
+#pragma unroll
+  for (int e = 0; e < kAdmitSelPer; ++e) {
+    mine[e] = lo + e < hi ? keys[lo + e] : ~0ull;
+    cnt += (lo + e < hi && mine[e] <= t) ? 1u : 0u;
+  }
+  uint32_t pos = admit_scan(cnt, warp_sums);  // barriers: every read above precedes every write below
+#pragma unroll
+  for (int e = 0; e < kAdmitSelPer; ++e)
+    if (lo + e < hi && mine[e] <= t) keys[pos++] = mine[e];
+  __syncthreads();
+}
+
 // One CTA per KV head. Shared memory: per slot a 64-bit LRU key (last_used + 4 << 24 | slot), and a
 // kept flag; the free slots are bitonic-sorted by key.
 __global__ void __launch_bounds__(kAdmitThreads) admit_kernel(const int32_t* __restrict__ chosen, int k, int64_t chosen_ld,
@@ -85,9 +157,28 @@ __global__ void __launch_bounds__(kAdmitThreads) admit_kernel(const int32_t* __r
   for (int s = lo; s < hi; ++s)
     if (!kept[s]) keys[pos++] = ((uint64_t)(lu[s] + 4) << 24) | (uint64_t)s;
   if (threadIdx.x == blockDim.x - 1) sh_nfree = pos;
+  // The misses' count first: only that many victims are needed, the smallest keys in order.
+  {
+    const int segm = (k + blockDim.x - 1) / blockDim.x;
+    const int mlo = threadIdx.x * segm, mhi = min(k, mlo + segm);
+    uint32_t nm0 = 0;
+    for (int i = mlo; i < mhi; ++i) {
+      const int b = ch[i];
+      nm0 += (b >= 0 && b < cap && bslot[b] < 1);
+    }
+    const uint32_t before = admit_scan(nm0, warp_sums);
+    if (threadIdx.x == blockDim.x - 1) sh_nmiss = before + nm0;
+  }
   __syncthreads();
-  const int n_free = (int)sh_nfree;
-  int PF = 1;  // only the free slots are sorted: the next power of two above their count
+  int n_free = (int)sh_nfree;
+  const int m = (int)min(sh_nmiss, (uint32_t)n_free);
+  if (m == 0) {
+    n_free = 0;  // all hits: no victim needed, nothing to sort
+  } else if (m < n_free && n_free > 2048 && n_free <= kAdmitSelMax) {
+    select_smallest(keys, n_free, m, warp_sums);  // keys[0, m) = the m smallest, unsorted
+    n_free = m;
+  }
+  int PF = 1;  // the keys left are sorted: the next power of two above their count
   while (PF < n_free) PF <<= 1;
   for (int i = n_free + threadIdx.x; i < PF; i += blockDim.x) keys[i] = ~0ull;
   __syncthreads();
