@@ -320,12 +320,14 @@ int lkv_ragged_exact_attention(const void* q, int rows, int g, int d, int bs, in
  * lazykv/quant.py:unpack, or pairs in `dtype`) into pool [n_slots + 2, h, 2, bs, d] row slot*h + head.
  * miss_blk / miss_slot [h, k] receive the misses in chosen order and n_miss [h] their count;
  * slots_out [h, k] (row stride slots_ld, optional) the pool index of every chosen block afterwards.
+ * miss_total (optional, int64): every head's miss count is added to it on the device, a running
+ * count of fetched pairs that needs no per-step host work (the reference's fetch counters).
  */
 int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32_t* block_slot,
                    int cap, int32_t* slot_block, int64_t* last_used, int n_slots,
                    int64_t* evicted_at, int64_t step, const void* store, int store_kind, void* pool,
                    int bs, int d, int dtype, int32_t* miss_blk, int32_t* miss_slot, int32_t* n_miss,
-                   int32_t* slots_out, int64_t slots_ld, void* stream);
+                   int32_t* slots_out, int64_t slots_ld, int64_t* miss_total, void* stream);
 
 /*
  * The selection for an attention that runs before (or beside) the step's admit: lkv_quest_topk in
@@ -362,7 +364,7 @@ int lkv_quest_topk_admit(const void* q, int q_dtype, int hq, int h, int d, const
                          int64_t* last_used, int n_slots, int64_t* evicted_at, int64_t step,
                          const void* store, int store_kind, void* pool, int bs, int dtype,
                          int32_t* miss_blk, int32_t* miss_slot, int32_t* n_miss, int32_t* slots_out,
-                         int64_t slots_ld, void* stream);
+                         int64_t slots_ld, int64_t* miss_total, void* stream);
 
 /*
  * Status word of the kernels that wait on shared-memory barriers (bounded waits): 0 when no wait

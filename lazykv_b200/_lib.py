@@ -67,10 +67,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_ragged_exact_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int,
                                            c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_tier_admit": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int,
-                               c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+                               c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "lkv_quest_topk_admit": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_int,
                                      c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64,
-                                     c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+                                     c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
 }
 
 
@@ -126,7 +126,11 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 def stream_handle(device: torch.device | None = None) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The raw handle of torch's current stream on `device` (the current device by default)."""
+    if device is None:
+        return torch.cuda.current_stream().cuda_stream
+    idx = device.index if isinstance(device, torch.device) else int(device)
+    return torch._C._cuda_getCurrentRawStream(torch.cuda.current_device() if idx is None else idx)
 
 
 def dtype_code(dt: torch.dtype) -> int:

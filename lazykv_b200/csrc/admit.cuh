@@ -32,6 +32,7 @@ struct AdmitArgs {
   int32_t* n_miss;     // [h]
   int32_t* slots_out;  // [h, slots_ld] (optional)
   int64_t slots_ld;
+  int64_t* miss_total;  // optional: every head's misses added to it (a running count)
 };
 
 // Shared-memory bytes of admit_head for n_slots slots and k chosen blocks.
@@ -186,7 +187,11 @@ static __device__ void admit_head(const AdmitArgs& a, int j, const int32_t* ch, 
     sblock[s] = sb_s[s];
     lu[s] = lu_s[s];
   }
-  if (threadIdx.x == 0) a.n_miss[j] = (int)min(sh_nmiss, (uint32_t)n_free);
+  if (threadIdx.x == 0) {
+    const int nm_j = (int)min(sh_nmiss, (uint32_t)n_free);
+    a.n_miss[j] = nm_j;
+    if (a.miss_total != nullptr && nm_j > 0) atomicAdd(reinterpret_cast<unsigned long long*>(a.miss_total), (unsigned long long)nm_j);
+  }
 }
 
 // One warp dequantises the int8 record at `rec` (global, 2,368 bytes: bs 16, d 64) into the bf16

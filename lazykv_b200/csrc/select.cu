@@ -1302,7 +1302,7 @@ int lkv_quest_topk_admit(const void* q, int q_dtype, int hq, int h, int d, const
                          uint32_t* bitmap, int bitmap_words, void* workspace, size_t workspace_bytes, int32_t* block_slot, int cap,
                          int32_t* slot_block, int64_t* last_used, int n_slots, int64_t* evicted_at, int64_t step, const void* store,
                          int store_kind, void* pool, int bs, int dtype, int32_t* miss_blk, int32_t* miss_slot, int32_t* n_miss,
-                         int32_t* slots_out, int64_t slots_ld, void* stream) {
+                         int32_t* slots_out, int64_t slots_ld, int64_t* miss_total, void* stream) {
   // The admit's arguments are checked before anything is launched, as lkv_tier_admit checks them.
   if (!dtype_ok(dtype)) return fail(LKV_ERR_ARG, "lkv_quest_topk_admit: bad dtype %d", dtype);
   if (store_kind != LKV_COLD_INT8 && store_kind != LKV_COLD_PAIRS) return fail(LKV_ERR_ARG, "lkv_quest_topk_admit: bad store kind %d", store_kind);
@@ -1318,7 +1318,7 @@ int lkv_quest_topk_admit(const void* q, int q_dtype, int hq, int h, int d, const
                                  out_blocks, out_ld, out_bound, bitmap, bitmap_words, workspace, workspace_bytes, stream);
   if (rc != LKV_OK) return rc;
   return lkv_tier_admit(out_blocks, h, k, out_ld, block_slot, cap, slot_block, last_used, n_slots, evicted_at, step, store, store_kind, pool, bs, d,
-                        dtype, miss_blk, miss_slot, n_miss, slots_out, slots_ld, stream);
+                        dtype, miss_blk, miss_slot, n_miss, slots_out, slots_ld, miss_total, stream);
 }
 
 size_t lkv_topk_merge_workspace(int h, int n) { return lkv_quest_topk_workspace(h, n); }

@@ -125,7 +125,8 @@ __global__ void __launch_bounds__(kAdmitThreads) admit_kernel(const int32_t* __r
                                                                int32_t* __restrict__ block_slot, int cap, int32_t* __restrict__ slot_block,
                                                                int64_t* __restrict__ last_used, int n_slots, int64_t* __restrict__ evicted_at,
                                                                int64_t step, int32_t* __restrict__ miss_blk, int32_t* __restrict__ miss_slot,
-                                                               int32_t* __restrict__ n_miss, int32_t* __restrict__ slots_out, int64_t slots_ld) {
+                                                               int32_t* __restrict__ n_miss, int32_t* __restrict__ slots_out, int64_t slots_ld,
+                                                               int64_t* __restrict__ miss_total) {
   extern __shared__ uint64_t keys[];  // [P]
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t sh_nfree, sh_nmiss;
@@ -243,7 +244,11 @@ __global__ void __launch_bounds__(kAdmitThreads) admit_kernel(const int32_t* __r
     if (s >= 1 && s <= n_slots) lu[s - 1] = step;
     if (slots_out != nullptr) slots_out[(int64_t)j * slots_ld + i] = s;
   }
-  if (threadIdx.x == 0) n_miss[j] = (int)min(sh_nmiss, (uint32_t)n_free);
+  if (threadIdx.x == 0) {
+    const int nm_j = (int)min(sh_nmiss, (uint32_t)n_free);
+    n_miss[j] = nm_j;
+    if (miss_total != nullptr && nm_j > 0) atomicAdd(reinterpret_cast<unsigned long long*>(miss_total), (unsigned long long)nm_j);
+  }
 }
 
 // The admit with the head's tables staged in shared memory (admit.cuh: admit_head), one CTA per
@@ -368,7 +373,7 @@ using namespace lkv;
 extern "C" int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32_t* block_slot, int cap, int32_t* slot_block,
                               int64_t* last_used, int n_slots, int64_t* evicted_at, int64_t step, const void* store, int store_kind,
                               void* pool, int bs, int d, int dtype, int32_t* miss_blk, int32_t* miss_slot, int32_t* n_miss,
-                              int32_t* slots_out, int64_t slots_ld, void* stream) {
+                              int32_t* slots_out, int64_t slots_ld, int64_t* miss_total, void* stream) {
   if (!dtype_ok(dtype)) return fail(LKV_ERR_ARG, "lkv_tier_admit: bad dtype %d", dtype);
   if (store_kind != LKV_COLD_INT8 && store_kind != LKV_COLD_PAIRS) return fail(LKV_ERR_ARG, "lkv_tier_admit: bad store kind %d", store_kind);
   if (h <= 0 || k <= 0 || cap <= 0 || n_slots < k) return fail(LKV_ERR_ARG, "lkv_tier_admit: need h, k, cap > 0 and n_slots >= k (%d < %d)", n_slots, k);
@@ -398,6 +403,7 @@ extern "C" int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chose
     aa.n_miss = n_miss;
     aa.slots_out = slots_out;
     aa.slots_ld = slots_ld;
+    aa.miss_total = miss_total;
     cudaError_t e = cudaSuccess;
     if (staged > 48 * 1024) e = cudaFuncSetAttribute(admit_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged);
     if (e == cudaSuccess) e = launch_pdl(admit_staged_kernel, dim3(h), dim3(kAdmitCtaThreads), staged, st, 0, chosen, k, chosen_ld, aa);
@@ -410,7 +416,7 @@ extern "C" int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chose
     if (smem > 200 * 1024) return fail(LKV_ERR_ARG, "lkv_tier_admit: %d slots need %zu bytes of shared memory", n_slots, smem);
     if (smem > 48 * 1024) cudaFuncSetAttribute(admit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     admit_kernel<<<h, kAdmitThreads, smem, st>>>(chosen, k, chosen_ld, block_slot, cap, slot_block, last_used, n_slots, evicted_at, step,
-                                                  miss_blk, miss_slot, n_miss, slots_out, slots_ld);
+                                                  miss_blk, miss_slot, n_miss, slots_out, slots_ld, miss_total);
     if (int rc = launched("lkv_tier_admit(admit)")) return rc;
   }
   const int64_t width = lkv_packed_pair_bytes(bs, d);

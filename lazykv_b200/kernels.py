@@ -358,8 +358,9 @@ def debug_set(key: int, value: int) -> None:
 
 def tier_admit(chosen: torch.Tensor, block_slot: torch.Tensor, slot_block: torch.Tensor, last_used: torch.Tensor, evicted_at: torch.Tensor | None,
                step: int, store: torch.Tensor, pool: torch.Tensor, miss_blk: torch.Tensor, miss_slot: torch.Tensor, n_miss: torch.Tensor,
-               slots_out: torch.Tensor | None = None) -> None:
-    """Device-side residency admit of `chosen` [h, k] plus the fetch of the misses (see lkv_tier_admit)."""
+               slots_out: torch.Tensor | None = None, miss_total: torch.Tensor | None = None) -> None:
+    """Device-side residency admit of `chosen` [h, k] plus the fetch of the misses (see lkv_tier_admit);
+    `miss_total` (int64 scalar on the device, optional) accumulates the misses."""
     dev = require_cuda(chosen, block_slot, slot_block, last_used, store, pool)
     h, k = chosen.shape
     n_slots = slot_block.shape[1]
@@ -367,14 +368,14 @@ def tier_admit(chosen: torch.Tensor, block_slot: torch.Tensor, slot_block: torch
     kind = L.LKV_COLD_INT8 if store.dtype == torch.uint8 else L.LKV_COLD_PAIRS
     call("lkv_tier_admit", ptr(chosen), h, k, chosen.stride(0), ptr(block_slot), block_slot.shape[1], ptr(slot_block), ptr(last_used), n_slots,
          ptr(evicted_at), step, ptr(store), kind, ptr(pool), bs, d, dtype_code(pool.dtype), ptr(miss_blk), ptr(miss_slot), ptr(n_miss),
-         ptr(slots_out), 0 if slots_out is None else slots_out.stride(0), stream_handle(dev))
+         ptr(slots_out), 0 if slots_out is None else slots_out.stride(0), ptr(miss_total), stream_handle(dev))
 
 
 def quest_topk_admit(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int, n_cand: int, k: int, chosen: torch.Tensor,
                      bitmap: torch.Tensor | None, block_slot: torch.Tensor, slot_block: torch.Tensor, last_used: torch.Tensor,
                      evicted_at: torch.Tensor | None, step: int, store: torch.Tensor, pool: torch.Tensor, miss_blk: torch.Tensor,
                      miss_slot: torch.Tensor, n_miss: torch.Tensor, slots_out: torch.Tensor | None = None,
-                     bound_dtype: torch.dtype | None = None, ws_slot: int = 1) -> torch.Tensor:
+                     bound_dtype: torch.dtype | None = None, ws_slot: int = 1, miss_total: torch.Tensor | None = None) -> torch.Tensor:
     """quest_topk in block order into `chosen` [h, k] (and the bitmap), then tier_admit of that
     selection, in one library call (lkv_quest_topk_admit). Returns `chosen`."""
     dev = require_cuda(query, kmin, kmax, chosen, block_slot, slot_block, last_used, store, pool)
@@ -391,5 +392,5 @@ def quest_topk_admit(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor
          n_cand, k, dtype_code(bound_dtype), ptr(chosen), chosen.stride(0), None, ptr(bitmap), words, ptr(ws), ws.numel(), ptr(block_slot),
          block_slot.shape[1], ptr(slot_block), ptr(last_used), slot_block.shape[1], ptr(evicted_at), step, ptr(store), kind, ptr(pool),
          pool.shape[-2], dtype_code(pool.dtype), ptr(miss_blk), ptr(miss_slot), ptr(n_miss), ptr(slots_out),
-         0 if slots_out is None else slots_out.stride(0), stream_handle(dev))
+         0 if slots_out is None else slots_out.stride(0), ptr(miss_total), stream_handle(dev))
     return chosen

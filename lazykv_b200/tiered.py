@@ -33,6 +33,7 @@ import torch
 from transformers import PreTrainedModel
 from transformers.cache_utils import Cache
 
+from lazykv_b200 import _lib as L
 from lazykv_b200 import kernels as K
 from lazykv_b200.cache import CacheStats, FullGPUCache
 from lazykv_b200.pinned import device_view, pinned_empty
@@ -257,6 +258,7 @@ class TieredLayer:
         self.fetched_total = torch.zeros((), dtype=torch.int64, device=dev)
         self.ends = torch.tensor([0, self.tail_slot], dtype=torch.int32, device=dev).repeat(h, 1).contiguous()  # sink, current
         self.out: torch.Tensor | None = None  # [hq, d] float32, allocated on first use
+        self.out_q: torch.Tensor | None = None  # [hq, d] in the query dtype: the fused exact call writes it
         self.lse: torch.Tensor | None = None
 
     # -- residency tables, as numpy copies (synchronising) -----------------------------------------
@@ -360,33 +362,104 @@ class TieredLayer:
         n_full, _ = self.candidates()
         K.quest_topk_admit(query, self.kmin[0], self.kmax[0], 1, n_full - 1, self.k, self.chosen, self.bitmap if bitmap else None, self._block_slot,
                            self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool, self.miss_blk, self.miss_slot,
-                           self.n_miss, slots_out=self.hot_list[:, 1 : self.k + 1])
-        self.fetched_total += self.n_miss.sum()
+                           self.n_miss, slots_out=self.hot_list[:, 1 : self.k + 1], miss_total=self.fetched_total)
         return self.chosen
 
     def admit_device(self, step: int) -> None:
         """Device-side admit of self.chosen and the fetch of its misses; fills the hot list."""
         K.tier_admit(self.chosen, self._block_slot, self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool,
-                     self.miss_blk, self.miss_slot, self.n_miss, slots_out=self.hot_list[:, 1 : self.k + 1])
-        self.fetched_total += self.n_miss.sum()
+                     self.miss_blk, self.miss_slot, self.n_miss, slots_out=self.hot_list[:, 1 : self.k + 1], miss_total=self.fetched_total)
 
-    def attend(self, query: torch.Tensor, scale: float, step: int, exact: bool, zerocopy: bool = False) -> torch.Tensor:
-        """One decode step of this layer on the device; returns out [hq, d] float32."""
+    def attend(self, query: torch.Tensor, scale: float, step: int, exact: bool, zerocopy: bool = False,
+               out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """One decode step of this layer on the device; returns out [hq, d] float32, or in `out_dtype`
+        (bf16 or float32) from the exact tier's fused call, which then writes that dtype directly."""
         hq, d = query.shape[1], self.d
         if self.out is None or self.out.shape != (hq, d):
             self.out = torch.empty((hq, d), dtype=torch.float32, device=query.device)
             self.lse = torch.empty((hq,), dtype=torch.float32, device=query.device)
+        if out_dtype == torch.float32:
+            self.out_q = self.out
+        elif self.out_q is None or self.out_q.shape != (hq, d) or self.out_q.dtype != out_dtype:
+            self.out_q = torch.empty((hq, d), dtype=out_dtype, device=query.device)
         pool_strides = (self.h * 2 * self.bs * d, 2 * self.bs * d, d)
         if zerocopy:
             self.choose(query, bitmap=exact)
             return self._attend_zerocopy(query, scale, exact, pool_strides)
+        if exact:  # choose_and_admit, then K.exact_attention into out_q: the two calls, argument lists cached
+            return self._exact_step(query, scale, step)
         self.choose_and_admit(query, step, bitmap=exact)
-        if exact:
-            K.exact_attention(query, self.pool, self.pool[:, :, 1], pool_strides, self.hot_list, self.fill, self.store, 1, self.n_sealed - 1,
-                              scale, self.bs, excluded=self.bitmap, out_dtype=torch.float32, out=self.out, lse=self.lse)
-        else:
-            K.hot_attention(query, self.pool, self.pool[:, :, 1], pool_strides, self.hot_list, self.fill, scale, self.bs, out=self.out, lse=self.lse)
+        K.hot_attention(query, self.pool, self.pool[:, :, 1], pool_strides, self.hot_list, self.fill, scale, self.bs, out=self.out, lse=self.lse)
         return self.out
+
+    def _exact_step(self, query: torch.Tensor, scale: float, step: int) -> torch.Tensor:
+        """choose_and_admit then the fused exact attention, as two library calls whose argument
+        lists are built once per (query shape, dtype, sealed count) and only patched per step (the
+        query's address, the step, the current block's fill, the stream): a decode step's host cost
+        is then little more than the two calls. Same launches and results as the wrappers."""
+        hq, d = query.shape[1], self.d
+        dev = self.pool.device
+        q = query.reshape(hq, d)
+        if not q.is_contiguous():
+            q = q.contiguous()
+        key = (hq, query.dtype, self.n_sealed, self.out_q.data_ptr())
+        plan = getattr(self, "_plan", None)
+        n_cand = self.n_sealed - 1
+        ws_sel = K.workspace(dev, self._ws_bytes(("sel", n_cand), lambda: int(L.lib().lkv_quest_topk_workspace(self.h, n_cand))), 1)
+        n_list = self.hot_list.shape[1]
+        ws_att = K.workspace(dev, self._ws_bytes(("att", hq, n_cand), lambda: int(L.lib().lkv_exact_attention_workspace(self.h, hq, d, n_list, n_cand))),
+                             0)
+        if plan is None or plan["key"] != key or plan["ws"] != (ws_sel.data_ptr(), ws_att.data_ptr()):
+            plan = self._plan = self._build_plan(key, q, n_cand, ws_sel, ws_att)
+        stream = L.stream_handle(dev)
+        sel, att, hot = plan["sel"], plan["att"], plan["hot"]
+        sel[0] = q.data_ptr()
+        sel[26] = step
+        sel[-1] = stream
+        rc = plan["sel_fn"](*sel)
+        if rc != 0:
+            raise L.LkvError(f"lkv_quest_topk_admit failed ({rc}): {L.last_error()}")
+        hot.last_fill = self.fill
+        att[0] = q.data_ptr()
+        att[7] = scale
+        att[-1] = stream
+        rc = plan["att_fn"](*att)
+        if rc != 0:
+            raise L.LkvError(f"lkv_exact_attention failed ({rc}): {L.last_error()}")
+        return self.out_q
+
+    def _ws_bytes(self, key: tuple, size_of) -> int:  # noqa: ANN001
+        cache = self.__dict__.setdefault("_ws_cache", {})
+        v = cache.get(key)
+        if v is None:
+            v = cache[key] = size_of()
+        return v
+
+    def _build_plan(self, key: tuple, q: torch.Tensor, n_cand: int, ws_sel: torch.Tensor, ws_att: torch.Tensor) -> dict:
+        import ctypes
+
+        hq, d, h = q.shape[0], self.d, self.h
+        kind = L.LKV_COLD_INT8 if self.store.dtype == torch.uint8 else L.LKV_COLD_PAIRS
+        kmin, kmax = self.kmin[0], self.kmax[0]
+        slots = self.hot_list[:, 1 : self.k + 1]
+        qd = L.dtype_code(q.dtype)
+        sel = [q.data_ptr(), qd, hq, h, d, kmin.data_ptr(), kmax.data_ptr(), L.dtype_code(kmin.dtype), kmin.stride(-3), 1, n_cand, self.k, qd,
+               self.chosen.data_ptr(), self.chosen.stride(0), None, self.bitmap.data_ptr(), self.bitmap.shape[-1], ws_sel.data_ptr(), ws_sel.numel(),
+               self._block_slot.data_ptr(), self._block_slot.shape[1], self._slot_block.data_ptr(), self._last_used.data_ptr(),
+               self._slot_block.shape[1], self._evicted_at.data_ptr(), 0, self.store.data_ptr(), kind, self.pool.data_ptr(), self.pool.shape[-2],
+               L.dtype_code(self.pool.dtype), self.miss_blk.data_ptr(), self.miss_slot.data_ptr(), self.n_miss.data_ptr(), slots.data_ptr(),
+               slots.stride(0), self.fetched_total.data_ptr(), 0]
+        strides = (h * 2 * self.bs * d, 2 * self.bs * d, d)
+        hot = L.HotSet(self.pool.data_ptr(), self.pool[:, :, 1].data_ptr(), L.dtype_code(self.pool.dtype), strides[0], strides[1], strides[2],
+                       self.hot_list.data_ptr(), self.hot_list.shape[1], None, 0, self.fill,
+                       K.storage_rows(self.pool, self.pool[:, :, 1], strides, h, self.bs, d))
+        cold = L.ColdSet(self.store.data_ptr(), kind, 1, n_cand, self.bitmap.data_ptr(), self.bitmap.shape[-1])
+        att = [q.data_ptr(), hq, h, d, self.bs, ctypes.byref(hot), ctypes.byref(cold), 1.0, self.out_q.data_ptr(), L.dtype_code(self.out_q.dtype),
+               self.lse.data_ptr(), None, None,
+               ws_att.data_ptr(), ws_att.numel(), 0]
+        lib = L.lib()
+        return {"key": key, "ws": (ws_sel.data_ptr(), ws_att.data_ptr()), "sel": sel, "att": att, "hot": hot, "cold": cold,
+                "sel_fn": lib.lkv_quest_topk_admit, "att_fn": lib.lkv_exact_attention}
 
     def _attend_zerocopy(self, query: torch.Tensor, scale: float, exact: bool, pool_strides: tuple[int, int, int]) -> torch.Tensor:
         """No slots: the selected blocks are read in place from the host store, the sink and the
@@ -423,8 +496,7 @@ class TieredLayer:
         """
         ch = torch.from_numpy(np.ascontiguousarray(chosen)).to(device=self.pool.device, dtype=torch.int32)
         K.tier_admit(ch, self._block_slot, self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool,
-                     self.miss_blk, self.miss_slot, self.n_miss)
-        self.fetched_total += self.n_miss.sum()
+                     self.miss_blk, self.miss_slot, self.n_miss, miss_total=self.fetched_total)
         n = self.n_miss.cpu().numpy()
         blk = self.miss_blk.cpu().numpy()
         # Head-major, chosen order within a head: the order of np.nonzero(miss) in the reference.
@@ -523,6 +595,10 @@ class TieredCache(Cache):
         self._mask_cache: dict[str, Any] = {}
         self._step = 0
         self._step_marks: list[torch.Tensor] = []  # device totals of fetched pairs at each step's end
+        # One running count of fetched pairs for every tier, added to by the admit kernels themselves.
+        self._fetched = sum(t.fetched_total for t in self.tiers.values()).clone()  # what they fetched before, if anything
+        for t in self.tiers.values():
+            t.fetched_total = self._fetched
         self._last_chosen: torch.Tensor | None = None
 
     # -- transformers plumbing ------------------------------------------------------------------------
@@ -568,7 +644,7 @@ class TieredCache(Cache):
     def _flush_step(self) -> None:
         # The step's fetch total stays on the device until the counters are read: no host sync here.
         if self.fetch != "zerocopy":
-            self._step_marks.append(sum(t.fetched_total for t in self.tiers.values()).clone())
+            self._step_marks.append(self._fetched.clone())
 
     # -- decode ---------------------------------------------------------------------------------------------
 
@@ -581,7 +657,8 @@ class TieredCache(Cache):
             return None
         t0 = time.perf_counter()
         scale = scaling if scaling is not None else tier.d**-0.5
-        out = tier.attend(query, scale, self._step, self.exact_pass, zerocopy=self.fetch == "zerocopy")
+        out_dtype = query.dtype if self.exact_pass and self.fetch != "zerocopy" else torch.float32
+        out = tier.attend(query, scale, self._step, self.exact_pass, zerocopy=self.fetch == "zerocopy", out_dtype=out_dtype)
         c = self.counters
         c.selections += 1
         c.selected_pairs += tier.h * tier.k
@@ -611,7 +688,7 @@ class TieredCache(Cache):
         if self.fetch != "zerocopy":
             marks = [int(m.item()) for m in self._step_marks]
             self.counters.fetched_pairs_per_step = [b - a for a, b in zip([0] + marks[:-1], marks)]
-            total = int(sum(t.fetched_total for t in self.tiers.values()).item())
+            total = int(self._fetched.item())
             self.counters.fetched_pairs = total
             self.counters.hit_pairs = self.counters.selected_pairs - total
             self.counters.fetch_bytes = total * next(iter(self.tiers.values())).pair_bytes
