@@ -12,10 +12,12 @@ the dense layers attend densely with torch's scaled_dot_product_attention (lower
 from __future__ import annotations
 
 import torch
+from torch.nn.attention import SDPBackend, sdpa_kernel
 from torch.nn.attention.bias import causal_lower_right
 from transformers import AttentionInterface
 
 IMPLEMENTATION_NAME = "lazykv_b200"
+_DECODE_BACKENDS = [SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
 
 
 def attend(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, scaling: float | None, mask: torch.Tensor | None = None) -> torch.Tensor:
@@ -30,7 +32,10 @@ def attend(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, scaling:
         # the model dtype; the gathered set is small, so it is attended in float32 instead, as the
         # device decode path does.
         return F(query.float(), key.float(), value.float(), attn_mask=mask.float(), scale=scaling, enable_gqa=True).to(query.dtype)
-    return F(query, key, value, scale=scaling, enable_gqa=True)
+    # A dense decode step (the dense layers) grows the KV by one token every step: a backend that
+    # builds an execution plan per shape (cuDNN's) would build one every step, so it is left out.
+    with sdpa_kernel(_DECODE_BACKENDS):
+        return F(query, key, value, scale=scaling, enable_gqa=True)
 
 
 def lazykv_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,

@@ -70,6 +70,8 @@ def test_absent_peer_times_out_then_its_late_rows_merge() -> None:
                L.ptr(lses[0]), L.stream_handle())
         torch.cuda.synchronize()
         assert K.device_status(clear=True) == 1
+        K.status_attach(torch.device(DEV, torch.cuda.current_device()))
+        K.status_poll(clear=True)  # the host mirror too, so that no later caller sees this planned timeout
         assert torch.equal(outs[0], parts[0][0]) and torch.equal(lses[0], parts[0][1])
         # Rank 1 arrives late: rank 0's rows are already in its inbox, so it merges both at once.
         L.call("lkv_exchange_merge", L.ptr(parts[1][0]), L.ptr(parts[1][1]), rows, d, 2, 1, arr, L.ptr(outs[1]), L.dtype_code(torch.float32),
