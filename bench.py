@@ -486,8 +486,9 @@ def profile_long_calls(args: argparse.Namespace) -> None:
 def profile_calls(args: argparse.Namespace) -> None:
     """The kernel calls of one layer-step, each twice and eagerly, for a profiler to capture: the
     selection, the admit (the first with misses), the hot pass alone, the cold pass alone and the
-    fused attention; then the codec and merge kernels at sizes above L2: pack and unpack of 4,096
-    blocks x 8 heads, block min/max over them, and an 8-part LSE merge."""
+    fused attention; the resident split (a third query's selection, the fused attention twice with
+    its misses in the exact pass, the admit); then the codec and merge kernels at sizes above L2:
+    pack and unpack of 4,096 blocks x 8 heads, block min/max over them, and an 8-part LSE merge."""
     import torch
 
     from lazykv_b200 import kernels as K
@@ -514,6 +515,13 @@ def profile_calls(args: argparse.Namespace) -> None:
         K.cold_attention(L.q_ring[r1], L.records, BS, first, geo["n_cand"], geo["scale"], excluded=L.bitmap, out=out, lse=lse)
     for _ in range(2):
         attention_call(L, geo, r1)
+    # The bench's order (the resident split): another query's selection, the attention with its
+    # misses in the exact pass, then the admit.
+    r2 = 2 % geo["n_q"]
+    resident_select_call(L, geo, r2)
+    for _ in range(2):
+        attention_call(L, geo, r2)
+    admit_call(L, geo, 4, hot=False)
     torch.cuda.synchronize()
     n = 4096
     g = torch.Generator(device=dev).manual_seed(5)
@@ -728,12 +736,15 @@ def run_ours(args: argparse.Namespace) -> None:
 
     peaks = load_peaks()
     k_local = geo["k_local"]
-    hot_blocks = geo["n_list"]
-    cold_blocks = geo["n_cand"] - k_local
+    # The attention's blocks per head: the listed slots and the range's records. In the resident
+    # split the misses are attended from their records (the fetch fills their slots beside it).
+    moved = 0.0 if args.admit_first else miss_pairs / HKV
+    hot_blocks = geo["n_list"] - moved
+    cold_blocks = geo["n_cand"] - k_local + moved
     bytes_meta = HKV * geo["n_cand"] * D * 2 * 2
-    bytes_hot = hot_blocks * HKV * 2 * BS * D * 2
+    bytes_hot = int(hot_blocks * HKV * 2 * BS * D * 2)
     rec_w = K.packed_pair_bytes(BS, D)
-    bytes_cold = cold_blocks * HKV * rec_w
+    bytes_cold = int(cold_blocks * HKV * rec_w)
     bytes_fetch = int(miss_pairs * (rec_w + 2 * BS * D * 2))  # a miss: its record read, its slot written
     algo = {"select": bytes_meta, "attention": bytes_hot + bytes_cold}
     dominant = max(("select", "attention"), key=lambda n: kernel_us[n])
