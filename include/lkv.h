@@ -352,8 +352,8 @@ int lkv_quest_topk_resident(const void* q, int q_dtype, int hq, int h, int d, co
  * selection written to out_blocks (and the bitmap) is made resident (LRU victims, misses fetched and
  * dequantised into their slots, slots_out = the slots of the selected blocks). Replaces
  * lazykv/tiered.py:383-463 (rank, then admit). Same arguments and results as the two calls (the
- * selection's chosen_ld is out_ld, its k the admit's k); the admit's arguments are checked before
- * anything runs, so an invalid call launches nothing.
+ * selection's chosen_ld is out_ld, its k the admit's k, miss_total as lkv_tier_admit's); the admit's
+ * arguments are checked before anything runs, so an invalid call launches nothing.
  * No reference counterpart as one call (the reference ranks on the device, then admits on the host).
  */
 int lkv_quest_topk_admit(const void* q, int q_dtype, int hq, int h, int d, const void* kmin,

@@ -108,3 +108,26 @@ def test_bad_arguments_raise() -> None:
         K.topk_gathered(gathered, [61, 30], 10, 0, 0, torch.empty((h, 10), dtype=torch.int32, device=DEV))
     with pytest.raises(LkvError):  # too few output columns for min(k, n_rank)
         K.topk_gathered(gathered, [50, 30], 20, 1, 0, torch.empty((h, 10), dtype=torch.int32, device=DEV))
+
+
+def test_global_selection_of_one_rank_is_the_plain_selection() -> None:
+    """sharded.GlobalSelection with a single rank (no process group): its chosen ids and bitmap are
+    lkv_quest_topk's over the rank's candidates, -1 past K."""
+    from lazykv_b200 import kernels as K
+    from lazykv_b200.sharded import GlobalSelection, shard_plan
+
+    h, d, n_sealed, k_total = 8, 64, 2049, 300
+    kmin, kmax = _metadata(h, n_sealed, d, seed=21, ties="runs")
+    q = torch.randn((h * 4, d), generator=torch.Generator(device=DEV).manual_seed(5), device=DEV).bfloat16()
+    plan = shard_plan(n_sealed, k_total, 1, 0)
+    sel = GlobalSelection([plan], 0, h, k_total, torch.device(DEV))
+    chosen = torch.full((h, sel.cols + 2), -7, dtype=torch.int32, device=DEV)
+    bm = torch.full((h, K.bitmap_words(n_sealed + 1)), -1, dtype=torch.int32, device=DEV)
+    sel.select(q, kmin, kmax, chosen, bm)
+    want_bm = torch.zeros_like(bm)
+    want, _ = K.quest_topk(q, kmin, kmax, plan.cand_first - plan.lo, plan.n_cand, k_total, out_blocks=None, bitmap=want_bm, by_block=True)
+    torch.cuda.synchronize()
+    got = chosen.cpu().numpy()
+    assert np.array_equal(got[:, :k_total], want.cpu().numpy())
+    assert (got[:, k_total : sel.cols] == -1).all() and (got[:, sel.cols :] == -7).all()
+    assert torch.equal(bm, want_bm)
