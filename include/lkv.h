@@ -104,7 +104,7 @@ int lkv_fetch_pairs(const void* src, int src_kind, const int64_t* src_rows, void
  * 64 KiB + 256 bytes hold per-head counters that the LKV_ORDER_BLOCK paths expect at zero and
  * leave so (calls on one workspace must not overlap on the GPU; re-zero them after a call that
  * returned an error). With bf16 query and metadata at head_dim 64 in LKV_ORDER_BLOCK (G in
- * {1, 2, 4, 8}, n_cand <= 16,384, h <= 64) the selection is a TMA scoring kernel (CTAs of 256
+ * {1, 2, 4, 8}, n_cand <= 16,384, h <= 64) the selection is a TMA scoring kernel (CTAs of 128
  * candidates) followed, by programmatic dependent launch, by a select kernel of one 8-CTA cluster
  * per head; no CTA waits for a CTA outside its cluster. The scoring's tile loads are bounded waits:
  * a wait that runs out records status 1 (lkv_device_status, lkv_status_poll) and the head's output

@@ -617,10 +617,11 @@ int launch_topk_cluster(int h, cudaStream_t st, const uint64_t* keys, uint32_t* 
 // complement still covers every candidate). A CTA whose wait ran out waits (bounded) for its copy
 // before it exits, so no bulk copy lands in the shared memory of a finished CTA.
 
-constexpr int kScThreads = 256;
+constexpr int kScThreads = 128;                        // candidates per CTA (one thread each)
 constexpr int kScBoxRows = 128;
-constexpr int kScBox = kScBoxRows * 128;              // bytes of one box: 128 rows of 64 bf16
-constexpr size_t kScSmem = 1024 + 4 * (size_t)kScBox;  // kmax boxes 0, 1 then kmin boxes 0, 1
+constexpr int kScBoxes = kScThreads / kScBoxRows;       // boxes per metadata array
+constexpr int kScBox = kScBoxRows * 128;               // bytes of one box: 128 rows of 64 bf16
+constexpr size_t kScSmem = 1024 + 2 * kScBoxes * (size_t)kScBox;  // the kmax boxes, then the kmin boxes
 constexpr int kPkThreads = 1024;
 constexpr int kPkCluster = 8;
 constexpr int kPkMaxKpt = 2;
@@ -725,14 +726,15 @@ __global__ void __launch_bounds__(kScThreads) quest_score_tma_kernel(const __gri
   if (tid == 0) {  // the bounds first: the query is staged while they are in flight
     const int r0 = sp.first_block + lo;
     const uint64_t pol = l2_evict_first_policy();  // the bounds are read once per call
-    mbar_arrive_expect_tx(&bar[0], 4u * kScBox);
-    tma_load_3d_hint(tiles, &sp.tmax, 0, r0, j, &bar[0], pol);
-    tma_load_3d_hint(tiles + kScBox, &sp.tmax, 0, r0 + kScBoxRows, j, &bar[0], pol);
-    tma_load_3d_hint(tiles + 2 * kScBox, &sp.tmin, 0, r0, j, &bar[0], pol);
-    tma_load_3d_hint(tiles + 3 * kScBox, &sp.tmin, 0, r0 + kScBoxRows, j, &bar[0], pol);
+    mbar_arrive_expect_tx(&bar[0], (uint32_t)(2 * kScBoxes * kScBox));
+#pragma unroll
+    for (int bx = 0; bx < kScBoxes; ++bx) {
+      tma_load_3d_hint(tiles + bx * kScBox, &sp.tmax, 0, r0 + bx * kScBoxRows, j, &bar[0], pol);
+      tma_load_3d_hint(tiles + (kScBoxes + bx) * kScBox, &sp.tmin, 0, r0 + bx * kScBoxRows, j, &bar[0], pol);
+    }
   }
   stage_query<__nv_bfloat16, G>(sp.q, j, 64, qs);
-  hist[tid] = 0u;
+  for (int b = tid; b < 256; b += kScThreads) hist[b] = 0u;
   uint32_t got = 1u;
   if (sp.stall && tid == 0) got = mbar_wait_n(&bar[1], 0, sp.wait_iters) ? 1u : 0u;  // test hook: runs out
   if (got) got = mbar_wait_n(&bar[0], 0, sp.wait_iters) ? 1u : 0u;
@@ -742,7 +744,7 @@ __global__ void __launch_bounds__(kScThreads) quest_score_tma_kernel(const __gri
   if (tid < cnt) {
     if (ok) {
       const int bx = tid / kScBoxRows, r = tid % kScBoxRows;
-      const float best = row_bound_swz<G>(tiles + bx * kScBox, tiles + (2 + bx) * kScBox, r, qs, sp.bound_mode);
+      const float best = row_bound_swz<G>(tiles + bx * kScBox, tiles + (kScBoxes + bx) * kScBox, r, qs, sp.bound_mode);
       key = orderable(best);
       if (sp.out_bound != nullptr) sp.out_bound[(int64_t)j * n_cand + lo + tid] = best == 0.0f ? 0.0f : best;
     }
@@ -752,7 +754,8 @@ __global__ void __launch_bounds__(kScThreads) quest_score_tma_kernel(const __gri
   const uint32_t peers = __match_any_sync(0xffffffffu, digit);
   if (digit < 256u && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
   __syncthreads();
-  if (hist[tid] != 0u) atomicAdd(&sp.hist0[(int64_t)j * 256 + tid], hist[tid]);
+  for (int b = tid; b < 256; b += kScThreads)
+    if (hist[b] != 0u) atomicAdd(&sp.hist0[(int64_t)j * 256 + b], hist[b]);
   if (tid == 0 && !ok) {
     atomicOr(&sp.fail[j], 1u);
     mbar_wait_n(&bar[0], 0, kScExitWaitIters);  // the copy may still be landing: no exit before it does
