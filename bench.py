@@ -797,7 +797,8 @@ def run_ours(args: argparse.Namespace) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": f"synthetic (seeded N(0,1) K/V with key offsets; per layer a ring of {R} queries, base + {args.drift} x N(0,1); no weights involved)",
-        "config": {"workload": "tiered decode hot path, Llama-3.2-1B attention (32q/8kv/d64), 131072-token context, bs 16, 25% budget (K=2046), 14 selecting layers, int8 cold tier in HBM, device admit with a fresh query every step",
+        "config": {"workload": "tiered decode hot path, Llama-3.2-1B attention (32q/8kv/d64), 131072-token context, bs 16, 25% budget (K=2046), 14 selecting layers, int8 cold tier in HBM, device admit with a fresh query every step"
+                               + (" (admit first)" if args.admit_first else " (resident split: the admit beside the attention)"),
                    "ctx": args.ctx, "block_size": BS, "k_blocks": geo["k_total"], "selecting_layers": n_sel, "batch": 1, "queries_in_ring": R,
                    "cold_placement": "device", "l2": "inputs larger than L2 (~2.8 GB read per step)", "parallelism": f"context-sharded x{world}",
                    "timing": "one CUDA graph per decode token (select, admit, attention per layer; the exchange launch at N > 1), CUDA events, max over ranks"},
