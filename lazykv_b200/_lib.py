@@ -125,12 +125,15 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)  # torch's own fast accessor, where it has one
+
+
 def stream_handle(device: torch.device | None = None) -> int:
     """The raw handle of torch's current stream on `device` (the current device by default)."""
-    if device is None:
-        return torch.cuda.current_stream().cuda_stream
+    if device is None or _RAW_STREAM is None:
+        return torch.cuda.current_stream(device).cuda_stream
     idx = device.index if isinstance(device, torch.device) else int(device)
-    return torch._C._cuda_getCurrentRawStream(torch.cuda.current_device() if idx is None else idx)
+    return _RAW_STREAM(torch.cuda.current_device() if idx is None else idx)
 
 
 def dtype_code(dt: torch.dtype) -> int:
