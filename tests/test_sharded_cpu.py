@@ -202,3 +202,20 @@ def test_gathered_bounds_give_the_single_gpu_selection(world: int) -> None:
         row = got[j][got[j] >= 0]
         assert np.array_equal(row, want[j])
     assert all(np.array_equal(a[0], b[0]) for a, b in zip(parts, res[1][0]))  # every rank computed the same parts
+
+
+def test_gathered_reference_edge_cases() -> None:
+    """host_reference_gathered_topk: k at or above the candidates takes everything; all-equal bounds
+    take the lowest ids across ranks; a rank with no candidates gets an empty, all -1 part."""
+    g = np.zeros((3, 2, 5), dtype=np.float32)
+    seg_n = [4, 0, 5]
+    everything = [host_reference_gathered_topk(g, seg_n, 99, r, 0) for r in range(3)]
+    assert everything[0].shape == (2, 4) and (everything[0] == np.arange(4)).all()
+    assert everything[1].shape == (2, 0)
+    assert (everything[2] == np.arange(5)).all()
+    low = [host_reference_gathered_topk(g, seg_n, 6, r, 10) for r in range(3)]
+    assert (low[0] == np.arange(10, 14)).all()  # the 4 lowest ids are rank 0's
+    assert (low[2][:, :2] == [10, 11]).all() and (low[2][:, 2:] == -1).all()  # then rank 2's first 2
+    g[2, 1, 4] = 1.0  # one higher bound on rank 2, head 1: it is taken first, a tie at the end drops
+    part = host_reference_gathered_topk(g, seg_n, 6, 2, 0)
+    assert part[1].tolist() == [0, 4, -1, -1, -1]
