@@ -918,18 +918,39 @@ def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) ->
     finals = [torch.empty((hq, d), dtype=torch.bfloat16, device=dev) for _ in layers]
 
     def select_admit(L, r: int, step: int) -> None:  # noqa: ANN001
+        """The selection then the admit, admit first (also the residency pass below)."""
         if gsel is None:
             select_admit_call(L, geo, r, step)
         else:
             gsel.select(L.q_ring[r], L.kmin, L.kmax, L.chosen, L.bitmap)
             admit_call(L, geo, step)
 
+    so, kl = geo["sel_off"], geo["k_local"]
+    admit_side = None if args.admit_first else torch.cuda.Stream()
+
+    def layer(L, r: int, step: int) -> None:  # noqa: ANN001
+        """One layer-step in the main leg's order: the resident selection (local or global), the
+        attention, the admit and fetch beside it on the side stream; or admit first."""
+        if admit_side is None:
+            select_admit(L, r, step)
+            attention_call(L, geo, r)
+            return
+        if gsel is None:
+            resident_select_call(L, geo, r)
+        else:
+            gsel.select(L.q_ring[r], L.kmin, L.kmax, L.chosen, L.bitmap, block_slot=L.block_slot, hot=L.list[:, so : so + kl])
+        admit_side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(admit_side):
+            admit_call(L, geo, step, hot=False)
+        attention_call(L, geo, r)
+
     def token(r: int, step_no: int) -> None:
         for i, L in enumerate(layers):
-            select_admit(L, r, step_no)
-            attention_call(L, geo, r)
+            layer(L, r, step_no)
             if world > 1:
                 L.xchg.exchange(finals[i])
+        if admit_side is not None:
+            torch.cuda.current_stream().wait_stream(admit_side)
 
     step_no = 0
     for w in range(max(args.warmup, R)):
@@ -1038,12 +1059,13 @@ def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) ->
     del ref_o, ref_l, parts
 
     # Algorithmic bytes of one layer-step, summed over the ranks: the metadata, the selected blocks
-    # (bf16 slots) and the sink/current blocks, the other candidates' int8 records, the fetch of misses.
+    # (bf16 slots) and the sink/current blocks, the other candidates' int8 records, the fetch of
+    # misses. In the resident split the misses are attended from their records.
     rec_w = K.packed_pair_bytes(BS, d)
     pair_b = 2 * BS * d * 2
     n_cand_all = geo["n_sealed"] - 1
-    sel_rows = sel_pairs  # selected (block, row) pairs per layer-step, all ranks
-    bytes_layer = (h * n_cand_all * d * 2 * 2 + (sel_rows + 2 * h) * pair_b + (h * n_cand_all - sel_rows) * rec_w
+    hot_rows = sel_pairs - (0.0 if args.admit_first else miss_pairs)  # (block, row) pairs read from slots, all ranks
+    bytes_layer = (h * n_cand_all * d * 2 * 2 + (hot_rows + 2 * h) * pair_b + (h * n_cand_all - hot_rows) * rec_w
                    + miss_pairs * (rec_w + pair_b))
     peaks = load_peaks()
     achieved = bytes_layer / (us_layer * 1e-6) / 1e9
@@ -1069,8 +1091,9 @@ def run_long_ctx(args: argparse.Namespace, rank: int, world: int, dev, timed) ->
         "clocks": clocks.summary(),
         "build_s": round(build_s, 1),
         "max_memory_gb_rank0": round(mem_gb, 1),
-        "timing": "one CUDA graph per query of the ring (selection, admit, attention per layer; at N > 1 the NCCL all-gather of the bounds "
-                  "and the peer-store exchange of the partials captured too), CUDA events over the timed steps, max over ranks",
+        "timing": "one CUDA graph per query of the ring (per layer the resident selection, the attention, and the admit with the fetch beside it "
+                  "on a side stream, unless --admit-first; at N > 1 the NCCL all-gather of the bounds and the peer-store exchange of the "
+                  "partials captured too), CUDA events over the timed steps, max over ranks; kernel_us: eager, admit first",
     }
     del graphs, run
     import gc

@@ -177,6 +177,17 @@ int lkv_topk_gathered(const void* bounds, int bounds_dtype, int world, int h, in
                       int out_ld, int out_cols, uint32_t* bitmap, int bitmap_words, void* stream);
 
 /*
+ * lkv_topk_gathered for an attention before the admit (as lkv_quest_topk_resident): for each chosen
+ * local id b written at column c, hot[h * hot_ld + c] = block_slot[h * cap + b] when that is a slot
+ * (>= 1), else -1 (and -1 in the padding columns); the bitmap marks only the resident ones.
+ */
+int lkv_topk_gathered_resident(const void* bounds, int bounds_dtype, int world, int h, int64_t ld,
+                               const int32_t* seg_n, int k, int rank, int out_base,
+                               int32_t* out_local, int out_ld, int out_cols, uint32_t* bitmap,
+                               int bitmap_words, const int32_t* block_slot, int cap, int32_t* hot,
+                               int64_t hot_ld, void* stream);
+
+/*
  * Split decode attention over listed blocks, emitting (normalised out, lse). Replaces the gather
  * + SDPA + GPU log-sum-exp of lazykv/tiered.py:465-487, lazykv/attention.py:97-136 and
  * lazykv/exact.py:380-393.

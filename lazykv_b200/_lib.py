@@ -49,6 +49,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "lkv_quest_bounds": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p, c_int, c_int64, c_void_p]),
     "lkv_topk_gathered": (c_int, [c_void_p, c_int, c_int, c_int, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
+    "lkv_topk_gathered_resident": (c_int, [c_void_p, c_int, c_int, c_int, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int,
+                                           c_void_p, c_int, c_void_p, c_int64, c_void_p]),
     "lkv_hot_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int64, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_cold_attention": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "lkv_lse_merge_packed": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_int, c_void_p, c_void_p]),

@@ -1051,6 +1051,7 @@ struct GatherSel {
   int out_ld, out_cols; // columns written (chosen ids, then -1)
   uint32_t* bitmap;     // [h][bitmap_words] or null
   int bitmap_words;
+  ResidentOut res;      // the resident split (null block_slot: off), on local ids
 };
 
 __device__ __forceinline__ uint32_t gathered_key(const GatherSel& p, int r, int j, int i) {
@@ -1144,11 +1145,19 @@ __global__ void __launch_bounds__(kSelectThreads) topk_gathered_kernel(const __g
     if (take && pos < (uint32_t)p.out_cols) {
       const int blk = p.out_base + i;
       out[pos] = blk;
-      if (p.bitmap != nullptr && blk / 32 < p.bitmap_words) atomicOr(&p.bitmap[(int64_t)j * p.bitmap_words + blk / 32], 1u << (blk % 32));
+      int32_t slot = 1;
+      if (p.res.block_slot != nullptr) {
+        slot = __ldcg(p.res.block_slot + (int64_t)j * p.res.bs_ld + blk);
+        p.res.hot[(int64_t)j * p.res.hot_ld + pos] = slot >= 1 ? slot : -1;
+      }
+      if (p.bitmap != nullptr && slot >= 1 && blk / 32 < p.bitmap_words) atomicOr(&p.bitmap[(int64_t)j * p.bitmap_words + blk / 32], 1u << (blk % 32));
       ++pos;
     }
   }
-  for (int c = (int)n_sel + tid; c < p.out_cols; c += blockDim.x) out[c] = -1;
+  for (int c = (int)n_sel + tid; c < p.out_cols; c += blockDim.x) {
+    out[c] = -1;
+    if (p.res.block_slot != nullptr) p.res.hot[(int64_t)j * p.res.hot_ld + c] = -1;
+  }
 }
 
 }  // namespace
@@ -1383,6 +1392,13 @@ int lkv_quest_bounds(const void* q, int q_dtype, int hq, int h, int d, const voi
 
 int lkv_topk_gathered(const void* bounds, int bounds_dtype, int world, int h, int64_t ld, const int32_t* seg_n, int k, int rank, int out_base,
                       int32_t* out_local, int out_ld, int out_cols, uint32_t* bitmap, int bitmap_words, void* stream) {
+  return lkv_topk_gathered_resident(bounds, bounds_dtype, world, h, ld, seg_n, k, rank, out_base, out_local, out_ld, out_cols, bitmap, bitmap_words,
+                                    nullptr, 0, nullptr, 0, stream);
+}
+
+int lkv_topk_gathered_resident(const void* bounds, int bounds_dtype, int world, int h, int64_t ld, const int32_t* seg_n, int k, int rank,
+                               int out_base, int32_t* out_local, int out_ld, int out_cols, uint32_t* bitmap, int bitmap_words,
+                               const int32_t* block_slot, int cap, int32_t* hot, int64_t hot_ld, void* stream) {
   if (bounds_dtype != LKV_BF16 && bounds_dtype != LKV_F32) return fail(LKV_ERR_ARG, "lkv_topk_gathered: bounds must be bf16 or float32");
   if (world <= 0 || world > kMaxWorld || rank < 0 || rank >= world) return fail(LKV_ERR_ARG, "lkv_topk_gathered: rank %d of %d (at most %d)", rank, world, kMaxWorld);
   if (h <= 0 || k <= 0 || out_base < 0 || seg_n == nullptr) return fail(LKV_ERR_ARG, "lkv_topk_gathered: need h, k > 0, out_base >= 0, counts");
@@ -1415,6 +1431,11 @@ int lkv_topk_gathered(const void* bounds, int bounds_dtype, int world, int h, in
   p.out_cols = out_cols;
   p.bitmap = bitmap;
   p.bitmap_words = bitmap_words;
+  if (block_slot != nullptr) {
+    if (hot == nullptr || hot_ld < out_cols || cap < out_base + n_my)
+      return fail(LKV_ERR_ARG, "lkv_topk_gathered_resident: hot rows of %lld < %d columns, or block_slot of %d blocks", (long long)hot_ld, out_cols, cap);
+    p.res = ResidentOut{block_slot, (int64_t)cap, hot, hot_ld};
+  }
   cudaError_t e = launch_pdl(topk_gathered_kernel, dim3(h), dim3(kSelectThreads), 0, as_stream(stream), 0, p);
   if (e != cudaSuccess) {
     cudaGetLastError();

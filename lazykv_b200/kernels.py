@@ -164,10 +164,13 @@ def quest_bounds(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, fi
 
 
 def topk_gathered(gathered: torch.Tensor, seg_n: list[int], k: int, rank: int, out_base: int, out: torch.Tensor,
-                  bitmap: torch.Tensor | None = None, out_cols: int | None = None) -> torch.Tensor:
+                  bitmap: torch.Tensor | None = None, out_cols: int | None = None, block_slot: torch.Tensor | None = None,
+                  hot: torch.Tensor | None = None) -> torch.Tensor:
     """Rank `rank`'s part of the global top-k over every rank's bounds gathered as [world, h, ld]
     (rank r holding seg_n[r] candidates after rank r-1's): out [h, >= out_cols] gets the chosen local
-    ids (out_base + index in the rank), ascending, then -1; the bitmap those ids."""
+    ids (out_base + index in the rank), ascending, then -1; the bitmap those ids. With `block_slot`
+    [h, cap] and `hot` [h, >= out_cols] (the resident split, lkv_topk_gathered_resident): hot gets
+    each chosen block's current slot or -1, and the bitmap marks only the resident ones."""
     import ctypes
 
     dev = require_cuda(gathered, out)
@@ -177,8 +180,15 @@ def topk_gathered(gathered: torch.Tensor, seg_n: list[int], k: int, rank: int, o
     out_cols = out.shape[-1] if out_cols is None else out_cols
     counts = (ctypes.c_int32 * world)(*seg_n)
     words = 0 if bitmap is None else bitmap.shape[-1]
-    call("lkv_topk_gathered", ptr(gathered), dtype_code(gathered.dtype), world, h, ld, ctypes.cast(counts, ctypes.c_void_p), k, rank, out_base,
-         ptr(out), out.stride(0), out_cols, ptr(bitmap), words, stream_handle(dev))
+    if block_slot is None:
+        call("lkv_topk_gathered", ptr(gathered), dtype_code(gathered.dtype), world, h, ld, ctypes.cast(counts, ctypes.c_void_p), k, rank, out_base,
+             ptr(out), out.stride(0), out_cols, ptr(bitmap), words, stream_handle(dev))
+    else:
+        if hot is None or hot.stride(-1) != 1 or not block_slot.is_contiguous():
+            raise ValueError("topk_gathered: the resident split needs hot [h, >=out_cols] (unit column stride) and a contiguous block_slot")
+        call("lkv_topk_gathered_resident", ptr(gathered), dtype_code(gathered.dtype), world, h, ld, ctypes.cast(counts, ctypes.c_void_p), k, rank,
+             out_base, ptr(out), out.stride(0), out_cols, ptr(bitmap), words, ptr(block_slot), block_slot.shape[-1], ptr(hot), hot.stride(0),
+             stream_handle(dev))
     return out
 
 

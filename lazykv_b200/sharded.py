@@ -233,9 +233,11 @@ class GlobalSelection:
         self.gathered = torch.zeros((len(plans), h, self.ld), dtype=bound_dtype, device=device)
 
     def select(self, query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, chosen: torch.Tensor, bitmap: torch.Tensor | None = None,
-               group: dist.ProcessGroup | None = None) -> torch.Tensor:
+               group: dist.ProcessGroup | None = None, block_slot: torch.Tensor | None = None, hot: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's part of the global selection of `query` into chosen [h, >= cols] (local ids
-        ascending, then -1) and the bitmap; kmin/kmax are the rank's metadata (local ids)."""
+        ascending, then -1) and the bitmap; kmin/kmax are the rank's metadata (local ids). With
+        `block_slot` and `hot`, the resident split (hot: the chosen blocks' current slots or -1; the
+        bitmap: only the resident ones)."""
         p = self.plan
         first = p.cand_first - p.lo
         K.quest_bounds(query, kmin, kmax, first, p.n_cand, self.send, self.bound_dtype)
@@ -243,7 +245,7 @@ class GlobalSelection:
             dist.all_gather_into_tensor(self.gathered, self.send, group=group)
         else:
             self.gathered[0].copy_(self.send)
-        return K.topk_gathered(self.gathered, self.seg_n, self.k, self.rank, first, chosen, bitmap, out_cols=self.cols)
+        return K.topk_gathered(self.gathered, self.seg_n, self.k, self.rank, first, chosen, bitmap, out_cols=self.cols, block_slot=block_slot, hot=hot)
 
 
 class ShardedExactStep:

@@ -131,3 +131,41 @@ def test_global_selection_of_one_rank_is_the_plain_selection() -> None:
     assert np.array_equal(got[:, :k_total], want.cpu().numpy())
     assert (got[:, k_total : sel.cols] == -1).all() and (got[:, sel.cols :] == -7).all()
     assert torch.equal(bm, want_bm)
+
+
+def test_gathered_resident_split_lists_the_resident_slots() -> None:
+    """lkv_topk_gathered_resident: the same chosen ids; hot holds each chosen block's slot from
+    block_slot or -1 (and -1 in the padding); the bitmap marks only the resident chosen blocks."""
+    from lazykv_b200 import kernels as K
+    from lazykv_b200.sharded import shard_plan
+
+    h, d, n_sealed, k_total, world = 8, 64, 3001, 500, 2
+    kmin, kmax = _metadata(h, n_sealed, d, seed=9, ties="runs")
+    q = torch.randn((h * 4, d), generator=torch.Generator(device=DEV).manual_seed(6), device=DEV).bfloat16()
+    plans = [shard_plan(n_sealed, k_total, world, r) for r in range(world)]
+    seg_n = [p.n_cand for p in plans]
+    gathered = torch.zeros((world, h, max(seg_n)), dtype=torch.bfloat16, device=DEV)
+    for r, p in enumerate(plans):
+        K.quest_bounds(q, kmin[:, p.lo : p.hi].contiguous(), kmax[:, p.lo : p.hi].contiguous(), p.cand_first - p.lo, p.n_cand, gathered[r])
+    gen = torch.Generator(device=DEV).manual_seed(12)
+    for r, p in enumerate(plans):
+        cols = min(k_total, p.n_cand)
+        nb = p.hi - p.lo
+        block_slot = torch.where(torch.rand((h, nb), generator=gen, device=DEV) < 0.5,
+                                 torch.randint(1, 4000, (h, nb), generator=gen, device=DEV), torch.full((h, nb), -1, device=DEV)).int().contiguous()
+        plain = torch.empty((h, cols), dtype=torch.int32, device=DEV)
+        bm_plain = torch.zeros((h, K.bitmap_words(nb + 1)), dtype=torch.int32, device=DEV)
+        K.topk_gathered(gathered, seg_n, k_total, r, p.cand_first - p.lo, plain, bm_plain, out_cols=cols)
+        out = torch.empty((h, cols), dtype=torch.int32, device=DEV)
+        hot = torch.full((h, cols), -7, dtype=torch.int32, device=DEV)
+        bm = torch.full((h, K.bitmap_words(nb + 1)), -1, dtype=torch.int32, device=DEV)
+        K.topk_gathered(gathered, seg_n, k_total, r, p.cand_first - p.lo, out, bm, out_cols=cols, block_slot=block_slot, hot=hot)
+        torch.cuda.synchronize()
+        assert torch.equal(out, plain)
+        ids = out.long().clamp(min=0)
+        want_hot = torch.where(out >= 0, torch.gather(block_slot, 1, ids), torch.full_like(out, -1))
+        want_hot = torch.where(want_hot >= 1, want_hot, torch.full_like(want_hot, -1))
+        assert torch.equal(hot, want_hot)
+        for j in range(h):
+            res = out[j][(out[j] >= 0) & (want_hot[j] >= 1)].cpu().numpy()
+            assert np.array_equal(np.nonzero(_bits(bm)[j])[0], np.sort(res))
