@@ -341,6 +341,16 @@ int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32
                    int32_t* slots_out, int64_t slots_ld, int64_t* miss_total, void* stream);
 
 /*
+ * The bitmap of a selection made elsewhere (a recorded one replayed, lazykv/tiered.py:715-724):
+ * for head j, bitmap [h, bitmap_words] row j is cleared, then the bit of every id in ids [h, k]
+ * (row stride ids_ld) is set, as lkv_quest_topk sets it for its own selection; -1 entries and ids
+ * at or past 32 * bitmap_words are skipped. An exact pass then skips exactly those blocks
+ * (lazykv/exact.py:371-378). One launch of h CTAs.
+ */
+int lkv_mark_blocks(const int32_t* ids, int h, int k, int64_t ids_ld, uint32_t* bitmap,
+                    int bitmap_words, void* stream);
+
+/*
  * The selection for an attention that runs before (or beside) the step's admit: lkv_quest_topk in
  * LKV_ORDER_BLOCK, plus, for the j-th chosen block b of head h, hot[h * hot_ld + j] =
  * block_slot[h * cap + b] when that is a slot (>= 1), else -1, and a bitmap that marks only those

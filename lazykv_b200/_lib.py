@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lkv_quest_topk_admit": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_int,
                                      c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64,
                                      c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
+    "lkv_mark_blocks": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_int, c_void_p]),
 }
 
 

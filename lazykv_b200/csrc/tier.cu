@@ -455,3 +455,25 @@ extern "C" int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chose
   }
   return launched("lkv_tier_admit(fetch)");
 }
+
+// The bitmap of a given selection: one CTA per head clears the head's words, then sets the bit of
+// every listed id in [0, 32 * words); -1 entries (padding) and ids past the bitmap are skipped.
+__global__ void __launch_bounds__(256) mark_blocks_kernel(const int32_t* __restrict__ ids, int k, int64_t ld, uint32_t* __restrict__ bitmap,
+                                                          int words) {
+  const int j = blockIdx.x;
+  uint32_t* row = bitmap + (int64_t)j * words;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) row[w] = 0u;
+  __syncthreads();
+  const int32_t* r = ids + (int64_t)j * ld;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const int b = r[i];
+    if (b >= 0 && b < words * 32) atomicOr(row + (b >> 5), 1u << (b & 31));
+  }
+}
+
+extern "C" int lkv_mark_blocks(const int32_t* ids, int h, int k, int64_t ids_ld, uint32_t* bitmap, int bitmap_words, void* stream) {
+  if (h <= 0 || k < 0 || bitmap_words <= 0 || ids_ld < k) return fail(LKV_ERR_ARG, "lkv_mark_blocks: need h, bitmap_words > 0, k >= 0, ids_ld >= k");
+  if (bitmap == nullptr || (k > 0 && ids == nullptr)) return fail(LKV_ERR_PTR, "lkv_mark_blocks: null pointer");
+  mark_blocks_kernel<<<h, 256, 0, as_stream(stream)>>>(ids, k, ids_ld, bitmap, bitmap_words);
+  return launched("lkv_mark_blocks");
+}

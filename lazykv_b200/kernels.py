@@ -381,6 +381,18 @@ def tier_admit(chosen: torch.Tensor, block_slot: torch.Tensor, slot_block: torch
          ptr(slots_out), 0 if slots_out is None else slots_out.stride(0), ptr(miss_total), stream_handle(dev))
 
 
+def mark_blocks(ids: torch.Tensor, bitmap: torch.Tensor) -> torch.Tensor:
+    """Clear `bitmap` [h, words] and set the bit of every block id in `ids` [h, k] (int32; -1 is
+    skipped), as the selection marks its own choice (lkv_mark_blocks). Returns `bitmap`."""
+    dev = require_cuda(ids, bitmap)
+    if ids.dtype != torch.int32 or bitmap.dtype != torch.int32 or ids.stride(-1) != 1 or not bitmap.is_contiguous():
+        raise ValueError("mark_blocks needs int32 ids with unit column stride and a contiguous int32 bitmap")
+    if ids.shape[0] != bitmap.shape[0]:
+        raise ValueError(f"ids has {ids.shape[0]} heads, the bitmap {bitmap.shape[0]}")
+    call("lkv_mark_blocks", ptr(ids), ids.shape[0], ids.shape[1], ids.stride(0), ptr(bitmap), bitmap.shape[1], stream_handle(dev))
+    return bitmap
+
+
 def quest_topk_admit(query: torch.Tensor, kmin: torch.Tensor, kmax: torch.Tensor, first_block: int, n_cand: int, k: int, chosen: torch.Tensor,
                      bitmap: torch.Tensor | None, block_slot: torch.Tensor, slot_block: torch.Tensor, last_used: torch.Tensor,
                      evicted_at: torch.Tensor | None, step: int, store: torch.Tensor, pool: torch.Tensor, miss_blk: torch.Tensor,

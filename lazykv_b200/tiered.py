@@ -20,11 +20,17 @@ the device, asynchronously. The host only tracks lengths.
 Cold placement: the store the exact pass and the fetches read is the pinned host store through its
 device view (`cold_placement="host"`, zero-copy over the link), or a device copy kept alongside it
 (`"device"`).
+
+Record and replay (tiered.py:620-621, 715-724, 832-836): `record_selection=True` keeps a device
+copy of every selecting layer's chosen ids per step, read back by recorded_selection();
+`replay_selection` feeds such a map back in place of the selection (loaded, admitted and attended
+as the selection's own choice), which repeats the recorded run's fetches and outputs exactly.
 """
 
 from __future__ import annotations
 
 import time
+from collections.abc import Mapping
 from dataclasses import asdict, dataclass, field
 from typing import Any
 
@@ -370,10 +376,37 @@ class TieredLayer:
         K.tier_admit(self.chosen, self._block_slot, self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool,
                      self.miss_blk, self.miss_slot, self.n_miss, slots_out=self.hot_list[:, 1 : self.k + 1], miss_total=self.fetched_total)
 
+    def load_chosen(self, chosen: np.ndarray, bitmap: bool = False) -> None:
+        """A selection made elsewhere (a recorded one, replayed) into self.chosen, and into the
+        bitmap the cold pass skips when `bitmap`. The ids [h, K] must be distinct candidates
+        (1..n_full-1) per head. The upload goes through a pinned stage that is rewritten only after
+        the previous step's copy from it has completed, so the host may run steps ahead."""
+        arr = np.asarray(chosen)
+        n_full, _ = self.candidates()
+        if arr.shape != (self.h, self.k):
+            raise ValueError(f"a selection of this layer is [{self.h}, {self.k}] block ids, got {list(arr.shape)}")
+        if arr.size and (arr.min() < 1 or arr.max() >= n_full):
+            raise ValueError(f"selected block ids must lie in 1..{n_full - 1}")
+        if any(len(np.unique(row)) != self.k for row in arr):
+            raise ValueError("a head's selected block ids must be distinct")
+        stage, ev = getattr(self, "_stage", None), getattr(self, "_stage_done", None)
+        if stage is None:
+            stage = self._stage = torch.empty((self.h, self.k), dtype=torch.int32, pin_memory=True)
+        if ev is not None:
+            ev.synchronize()  # the last copy out of the stage has finished
+        stage.numpy()[:] = arr
+        self.chosen.copy_(stage, non_blocking=True)
+        ev = self._stage_done = torch.cuda.Event()
+        ev.record()
+        if bitmap:
+            K.mark_blocks(self.chosen, self.bitmap)
+
     def attend(self, query: torch.Tensor, scale: float, step: int, exact: bool, zerocopy: bool = False,
-               out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+               out_dtype: torch.dtype = torch.float32, chosen: np.ndarray | None = None) -> torch.Tensor:
         """One decode step of this layer on the device; returns out [hq, d] float32, or in `out_dtype`
-        (bf16 or float32) from the exact tier's fused call, which then writes that dtype directly."""
+        (bf16 or float32) from the exact tier's fused call, which then writes that dtype directly.
+        `chosen` [h, K] replaces the step's selection (a replayed one): it is loaded, admitted and
+        attended exactly as the device selection's own choice would be."""
         hq, d = query.shape[1], self.d
         if self.out is None or self.out.shape != (hq, d):
             self.out = torch.empty((hq, d), dtype=torch.float32, device=query.device)
@@ -384,19 +417,26 @@ class TieredLayer:
             self.out_q = torch.empty((hq, d), dtype=out_dtype, device=query.device)
         pool_strides = (self.h * 2 * self.bs * d, 2 * self.bs * d, d)
         if zerocopy:
+            if chosen is not None:
+                raise ValueError("the zero-copy fetch has no residency to replay")
             self.choose(query, bitmap=exact)
             return self._attend_zerocopy(query, scale, exact, pool_strides)
+        if chosen is not None:
+            self.load_chosen(chosen, bitmap=exact)
+            self.admit_device(step)
         if exact:  # choose_and_admit, then K.exact_attention into out_q: the two calls, argument lists cached
-            return self._exact_step(query, scale, step)
-        self.choose_and_admit(query, step, bitmap=exact)
+            return self._exact_step(query, scale, step, selected=chosen is not None)
+        if chosen is None:
+            self.choose_and_admit(query, step, bitmap=exact)
         K.hot_attention(query, self.pool, self.pool[:, :, 1], pool_strides, self.hot_list, self.fill, scale, self.bs, out=self.out, lse=self.lse)
         return self.out
 
-    def _exact_step(self, query: torch.Tensor, scale: float, step: int) -> torch.Tensor:
+    def _exact_step(self, query: torch.Tensor, scale: float, step: int, selected: bool = False) -> torch.Tensor:
         """choose_and_admit then the fused exact attention, as two library calls whose argument
         lists are built once per (query shape, dtype, sealed count) and only patched per step (the
         query's address, the step, the current block's fill, the stream): a decode step's host cost
-        is then little more than the two calls. Same launches and results as the wrappers."""
+        is then little more than the two calls. Same launches and results as the wrappers.
+        `selected`: the step's selection is already loaded and admitted; only the attention runs."""
         hq, d = query.shape[1], self.d
         dev = self.pool.device
         q = query.reshape(hq, d)
@@ -413,12 +453,13 @@ class TieredLayer:
             plan = self._plan = self._build_plan(key, q, n_cand, ws_sel, ws_att)
         stream = L.stream_handle(dev)
         sel, att, hot = plan["sel"], plan["att"], plan["hot"]
-        sel[0] = q.data_ptr()
-        sel[26] = step
-        sel[-1] = stream
-        rc = plan["sel_fn"](*sel)
-        if rc != 0:
-            raise L.LkvError(f"lkv_quest_topk_admit failed ({rc}): {L.last_error()}")
+        if not selected:
+            sel[0] = q.data_ptr()
+            sel[26] = step
+            sel[-1] = stream
+            rc = plan["sel_fn"](*sel)
+            if rc != 0:
+                raise L.LkvError(f"lkv_quest_topk_admit failed ({rc}): {L.last_error()}")
         hot.last_fill = self.fill
         att[0] = q.data_ptr()
         att[7] = scale
@@ -568,8 +609,12 @@ class TieredCache(Cache):
             n_slots = 0 if n_slots is None else n_slots
         if prefetch:
             raise ValueError("the layer-ahead prefetch is not built: residency is decided on the device, with no host round trip to hide")
-        if record_selection or replay_selection is not None:
-            raise ValueError("record/replay of selections is not built: the selection never reaches the host")
+        if replay_selection is not None and not isinstance(replay_selection, Mapping):
+            raise ValueError("replay_selection maps (layer, step) to the chosen block ids [h, K] of that step")
+        # (layer, step) -> chosen block ids [h, K]; recorded as device copies, read back on demand
+        # (tiered.py:620-621, 715-724). Scripts may assign both attributes directly, as the reference's do.
+        self._record: dict[tuple[int, int], Any] | None = {} if record_selection else None
+        self._replay: Mapping[tuple[int, int], np.ndarray] | None = replay_selection
         self.full, self.k_blocks, self.block_size, self.dense_layers = full, k_blocks, block_size, dense_layers
         self.thrash_window, self.instrument, self.quant, self.fetch = thrash_window, instrument, quant, fetch
         self.prefetch = False
@@ -658,7 +703,10 @@ class TieredCache(Cache):
         t0 = time.perf_counter()
         scale = scaling if scaling is not None else tier.d**-0.5
         out_dtype = query.dtype if self.exact_pass and self.fetch != "zerocopy" else torch.float32
-        out = tier.attend(query, scale, self._step, self.exact_pass, zerocopy=self.fetch == "zerocopy", out_dtype=out_dtype)
+        replay = None if self._replay is None else self._replay[(layer_idx, self._step)]
+        out = tier.attend(query, scale, self._step, self.exact_pass, zerocopy=self.fetch == "zerocopy", out_dtype=out_dtype, chosen=replay)
+        if self._record is not None:
+            self._record[(layer_idx, self._step)] = tier.chosen.clone()  # a device copy: no host sync per step
         c = self.counters
         c.selections += 1
         c.selected_pairs += tier.h * tier.k
@@ -674,13 +722,31 @@ class TieredCache(Cache):
             return None
         if self.fetch == "zerocopy":
             raise ValueError("the zero-copy tier attends in place; use decode()")
-        chosen = tier.rank(query, bitmap=self.exact_pass)
-        tier.chosen.copy_(torch.from_numpy(chosen).to(torch.int32))
+        if self._replay is None:
+            chosen = tier.rank(query, bitmap=self.exact_pass)
+            tier.chosen.copy_(torch.from_numpy(chosen).to(torch.int32))
+        else:
+            chosen = np.asarray(self._replay[(layer_idx, self._step)])
+            tier.load_chosen(chosen, bitmap=self.exact_pass)
+        if self._record is not None:
+            self._record[(layer_idx, self._step)] = chosen
         tier.admit_device(self._step)
         self._last_chosen = tier.chosen.clone()
         self.counters.selections += 1
         self.counters.selected_pairs += chosen.size
         return tier.gather(chosen, self._step, query, self._mask_cache)
+
+    def recorded_selection(self) -> dict[tuple[int, int], np.ndarray]:
+        """The (layer, step) -> chosen-blocks [h, K] map a `record_selection=True` run captured
+        (tiered.py:832-836). Device records are read back here (one sync), as int64 block ids:
+        ascending ids from decode() (the order the device selection hands its admit), rank order
+        from select(). Replaying the map through `replay_selection` repeats the run exactly."""
+        if self._record is None:
+            raise RuntimeError("this cache was not built with record_selection=True")
+        for key, v in self._record.items():
+            if isinstance(v, torch.Tensor):
+                self._record[key] = v.cpu().numpy().astype(np.int64)
+        return self._record
 
     # -- accounting --------------------------------------------------------------------------------------
 

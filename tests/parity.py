@@ -63,3 +63,30 @@ def index_parity(ours: np.ndarray, ref: np.ndarray, bound: np.ndarray, tie_tol: 
             else:
                 bad += 1
     return {"exact": exact, "tie": tie, "bad": bad}
+
+
+def lru_admit(chosen: np.ndarray, block_slot: np.ndarray, slot_block: np.ndarray, last_used: np.ndarray, evicted_at: np.ndarray,
+              step: int) -> list[np.ndarray]:
+    """The reference's admit rule (lazykv/tiered.py:389-463) per head on the host, updating the
+    tables in place: chosen blocks not in a slot miss; victims are the slots not holding a chosen
+    block, by (last_used, slot); misses take them in chosen order; every chosen slot is used at this
+    step. -1 entries are padding. Returns each head's misses in chosen order."""
+    misses = []
+    for j in range(chosen.shape[0]):
+        ch = chosen[j][chosen[j] >= 0]
+        cur = block_slot[j, ch]
+        kept = set((cur[cur >= 1] - 1).tolist())
+        free = sorted((s for s in range(slot_block.shape[1]) if s not in kept), key=lambda s: (last_used[j, s], s))
+        miss = [int(b) for b, c in zip(ch, cur) if c < 1]
+        for i, b in enumerate(miss):
+            v = free[i]
+            old = slot_block[j, v]
+            if old >= 0:
+                block_slot[j, old] = -1
+                evicted_at[j, old] = step
+            slot_block[j, v] = b
+            block_slot[j, b] = v + 1
+        for b in ch:
+            last_used[j, block_slot[j, b] - 1] = step
+        misses.append(np.array(miss, dtype=np.int64))
+    return misses

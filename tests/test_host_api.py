@@ -64,7 +64,9 @@ def test_tier_configurations_are_refused_before_any_device_work() -> None:
         TieredCache(full, 3, 8, 64, quant="int8")
     with pytest.raises(ValueError, match="zero-copy"):
         TieredCache(full, 3, 8, 64, fetch="zerocopy", record_selection=True)
-    with pytest.raises(ValueError, match="record/replay"):
+    with pytest.raises(ValueError, match="zero-copy"):
+        TieredCache(full, 3, 8, 64, fetch="zerocopy", replay_selection={})
+    with pytest.raises(ValueError, match="maps \\(layer, step\\)"):
         TieredCache(full, 3, 8, 64, replay_selection=[])
     with pytest.raises(ValueError, match="prefetch"):
         ExactTieredCache(full, 3, 8, 64, model=object(), prefetch=True)

@@ -12,6 +12,8 @@ from __future__ import annotations
 import pytest
 import torch
 
+from tests.parity import lru_admit
+
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 NEVER = -(2**40)
@@ -121,33 +123,6 @@ def test_resident_split_attends_as_the_admit_first_order(d: int) -> None:
     assert K.device_status() == 0
 
 
-def _ref_admit(chosen, block_slot, slot_block, last_used, evicted_at, step: int) -> list:  # noqa: ANN001
-    """The reference's admit rule (lazykv/tiered.py:389-463) per head on the host: chosen blocks not
-    in a slot miss; victims are the slots not holding a chosen block, by (last_used, slot); misses
-    take them in chosen order; every chosen slot is used at this step. -1 entries are padding."""
-    import numpy as np
-
-    misses = []
-    for j in range(chosen.shape[0]):
-        ch = chosen[j][chosen[j] >= 0]
-        cur = block_slot[j, ch]
-        kept = set((cur[cur >= 1] - 1).tolist())
-        free = sorted((s for s in range(slot_block.shape[1]) if s not in kept), key=lambda s: (last_used[j, s], s))
-        miss = [int(b) for b, c in zip(ch, cur) if c < 1]
-        for i, b in enumerate(miss):
-            v = free[i]
-            old = slot_block[j, v]
-            if old >= 0:
-                block_slot[j, old] = -1
-                evicted_at[j, old] = step
-            slot_block[j, v] = b
-            block_slot[j, b] = v + 1
-        for b in ch:
-            last_used[j, block_slot[j, b] - 1] = step
-        misses.append(np.array(miss, dtype=np.int64))
-    return misses
-
-
 def test_large_pool_admit_follows_the_lru_rule() -> None:
     """A pool of 16,384 slots per head with about a quarter of them chosen per step (the global
     selection's ranks at N = 4): the admit that selects only as many victims as there are misses
@@ -178,7 +153,7 @@ def test_large_pool_admit_follows_the_lru_rule() -> None:
             ch[j, : len(pick)] = np.sort(pick)
         chosen = torch.from_numpy(ch).int().to(DEV)
         K.tier_admit(chosen, dev["block_slot"], dev["slot_block"], dev["last_used"], dev["evicted_at"], step, rec, pool, miss_blk, miss_slot, n_miss)
-        misses = _ref_admit(ch, host["block_slot"], host["slot_block"], host["last_used"], host["evicted_at"], step)
+        misses = lru_admit(ch, host["block_slot"], host["slot_block"], host["last_used"], host["evicted_at"], step)
         torch.cuda.synchronize()
         for name in ("block_slot", "slot_block", "last_used", "evicted_at"):
             assert np.array_equal(dev[name].cpu().numpy(), host[name]), (step, name)

@@ -166,7 +166,7 @@ def test_budget_that_covers_every_block_is_refused(tiny) -> None:  # noqa: ANN00
 
 
 def test_refusals(tiny) -> None:  # noqa: ANN001
-    """The reference's layer-ahead prefetch and record/replay are refused loudly; so is zero-copy with them."""
+    """The reference's layer-ahead prefetch is refused loudly; so is zero-copy with it or with record/replay."""
     from lazykv_b200.tiered import TieredCache
 
     cfg, model = tiny
@@ -177,8 +177,8 @@ def test_refusals(tiny) -> None:  # noqa: ANN001
         TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="zerocopy", record_selection=True)
     with pytest.raises(ValueError, match="prefetch"):
         TieredCache(full, K, BS, capacity_tokens=CAP, model=model, dense_layers=1, prefetch=True)
-    with pytest.raises(ValueError, match="record/replay"):
-        TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, record_selection=True)
+    with pytest.raises(ValueError, match="zero-copy"):
+        TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="zerocopy", replay_selection={})
 
 
 def test_device_cold_placement_is_bit_identical(tiny) -> None:  # noqa: ANN001
