@@ -319,6 +319,26 @@ int lkv_ragged_exact_attention(const void* q, int rows, int g, int d, int bs, in
                                float* lse, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The cold tier of ragged rows in pinned host memory (lazykv/tiered.py:489-511 over
+ * lazykv/pinned.py:73-92, the zero-copy read of the cold store): before the attention, the records
+ * it will read are read over the link with mapped loads and staged in HBM. records [n_records,
+ * heads, width] is the host store's device address (mapped, pinned); table [n][table_stride] the
+ * batch's block tables; work [n_work][2] and row_info [rows][4] as lkv_ragged_quest_topk and
+ * lkv_ragged_exact_attention take them; excluded (optional) the blocks the attention will skip,
+ * which are not read. Candidate c (block 1 + c) of sequence i goes to staged row stage_first[i] + c
+ * of stage [stage_rows, heads, width] (device memory), and stage_table [n][stage_stride] gets that
+ * row (or -1 where the block table names no store row): lkv_ragged_exact_attention with
+ * records = stage and table = stage_table then attends exactly what it would over a device store.
+ * One launch of n_work CTAs; width a multiple of 16.
+ */
+int lkv_ragged_stage_records(const uint8_t* records, int64_t n_records, int heads, int width,
+                             const int32_t* table, int64_t table_stride, const int32_t* work,
+                             int n_work, const int32_t* row_info, const uint32_t* excluded,
+                             int bitmap_words, uint8_t* stage, int64_t stage_rows,
+                             const int32_t* stage_first, int32_t* stage_table,
+                             int64_t stage_stride, void* stream);
+
+/*
  * Residency admit on the device, fused with the fetch of the misses. Replaces the host side of
  * lazykv/tiered.py:383-487 (rank's device-to-host copy, the numpy LRU of admit, the staged H2D and
  * index_copy_, and the gather's last_used update), with the same LRU rule: for KV head j, chosen

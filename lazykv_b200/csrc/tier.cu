@@ -477,3 +477,77 @@ extern "C" int lkv_mark_blocks(const int32_t* ids, int h, int k, int64_t ids_ld,
   mark_blocks_kernel<<<h, 256, 0, as_stream(stream)>>>(ids, k, ids_ld, bitmap, bitmap_words);
   return launched("lkv_mark_blocks");
 }
+
+// ---- Ragged rows, cold tier in pinned host memory: the records a step attends, staged ----
+//
+// One CTA per 256-candidate chunk of a (sequence, KV head) row (the score kernel's work list); a
+// warp per candidate block not in the row's excluded bitmap reads its record over the link with
+// 16-byte loads (five in flight per lane) and stores it at the block's staged row, so that the
+// attention that follows reads it from HBM. The rows of head 0 also write the staged table entry of
+// each candidate (its staged row, or -1 where the block table names no store row).
+constexpr int kStageWarps = 8;
+constexpr int kStageChunk = 256;
+constexpr int kStageInflight = 5;
+
+__global__ void __launch_bounds__(32 * kStageWarps) ragged_stage_kernel(const uint4* __restrict__ records, int64_t n_records, int heads, int width16,
+                                                                        const int32_t* __restrict__ table, int64_t table_stride,
+                                                                        const int2* __restrict__ work, const int4* __restrict__ row_info,
+                                                                        const uint32_t* __restrict__ excluded, int bitmap_words, uint4* __restrict__ stage,
+                                                                        int64_t stage_rows, const int32_t* __restrict__ stage_first,
+                                                                        int32_t* __restrict__ stage_table, int64_t stage_stride) {
+  const int2 wk = work[blockIdx.x];
+  const int row = wk.x, first = wk.y;
+  const int seq = row / heads, head = row - seq * heads;
+  const int end = min(first + kStageChunk, row_info[row].z);
+  const int64_t sf = stage_first[seq];
+  const int32_t* tab = table + (int64_t)seq * table_stride;
+  if (head == 0) {
+    for (int c = first + (int)threadIdx.x; c < end; c += blockDim.x) {
+      const int src = tab[1 + c];
+      stage_table[(int64_t)seq * stage_stride + 1 + c] = (src >= 0 && src < n_records && sf + c < stage_rows) ? (int32_t)(sf + c) : -1;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t* ex = excluded != nullptr ? excluded + (int64_t)row * bitmap_words : nullptr;
+  for (int c = first + warp; c < end; c += kStageWarps) {
+    const int b = 1 + c;
+    if (ex != nullptr && ((ex[b >> 5] >> (b & 31)) & 1u)) continue;
+    const int src = tab[b];
+    if (src < 0 || src >= n_records || sf + c >= stage_rows) continue;
+    const uint4* s = records + ((int64_t)src * heads + head) * width16;
+    uint4* d = stage + ((sf + c) * heads + head) * width16;
+    for (int base = 0; base < width16; base += 32 * kStageInflight) {
+      uint4 v[kStageInflight];
+#pragma unroll
+      for (int u = 0; u < kStageInflight; ++u) {
+        const int i = base + 32 * u + lane;
+        if (i < width16) v[u] = __ldcs(s + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kStageInflight; ++u) {
+        const int i = base + 32 * u + lane;
+        if (i < width16) d[i] = v[u];
+      }
+    }
+  }
+}
+
+extern "C" int lkv_ragged_stage_records(const uint8_t* records, int64_t n_records, int heads, int width, const int32_t* table, int64_t table_stride,
+                                        const int32_t* work, int n_work, const int32_t* row_info, const uint32_t* excluded, int bitmap_words,
+                                        uint8_t* stage, int64_t stage_rows, const int32_t* stage_first, int32_t* stage_table, int64_t stage_stride,
+                                        void* stream) {
+  const char* who = "lkv_ragged_stage_records";
+  if (records == nullptr || table == nullptr || work == nullptr || row_info == nullptr || stage == nullptr || stage_first == nullptr ||
+      stage_table == nullptr)
+    return fail(LKV_ERR_PTR, "%s: null pointer", who);
+  if (heads <= 0 || width <= 0 || width % 16 || n_work < 0 || n_records <= 0 || stage_rows <= 0 || (excluded != nullptr && bitmap_words <= 0))
+    return fail(LKV_ERR_ARG, "%s: bad shape (heads %d, width %d, work %d)", who, heads, width, n_work);
+  if (!aligned(records, 16) || !aligned(stage, 16) || !aligned(work, 8) || !aligned(row_info, 16))
+    return fail(LKV_ERR_PTR, "%s: records and stage must be 16-byte aligned (work 8, row info 16)", who);
+  if (n_work == 0) return LKV_OK;
+  ragged_stage_kernel<<<n_work, 32 * kStageWarps, 0, as_stream(stream)>>>(
+      reinterpret_cast<const uint4*>(records), n_records, heads, width / 16, table, table_stride, reinterpret_cast<const int2*>(work),
+      reinterpret_cast<const int4*>(row_info), excluded, bitmap_words, reinterpret_cast<uint4*>(stage), stage_rows, stage_first, stage_table,
+      stage_stride);
+  return launched(who);
+}

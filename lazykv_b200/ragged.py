@@ -84,9 +84,11 @@ class RaggedTier:
     """
 
     def __init__(self, heads: int, group: int, head_dim: int, block_size: int, max_seqs: int, max_tokens: int, store_blocks: int,
-                 budget: float, device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16) -> None:
+                 budget: float, device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16, cold_placement: str = "device") -> None:
         if dtype != torch.bfloat16 or head_dim != 64 or block_size != 16 or group not in (1, 2, 4, 8):
             raise ValueError("ragged batching runs the bf16 tensor-core path: head_dim 64, block size 16, a query group of 1, 2, 4 or 8")
+        if cold_placement not in ("device", "host"):
+            raise ValueError(f"cold_placement is 'device' or 'host', got {cold_placement!r}")
         self.h, self.g, self.d, self.bs = heads, group, head_dim, block_size
         self.dev, self.dtype, self.budget = torch.device(device), dtype, budget
         self.max_seqs, self.max_tokens = max_seqs, max_tokens
@@ -96,7 +98,18 @@ class RaggedTier:
         self.k_max = blocks_for_budget(budget, max_tokens, block_size)
         self.per_seq = self.k_max + 2
         self.W = K.packed_pair_bytes(block_size, head_dim)
-        self.records = torch.zeros((store_blocks, heads, self.W), dtype=torch.uint8, device=self.dev)
+        self.cold_placement = cold_placement
+        if cold_placement == "host":
+            # The store in pinned host memory; kernels write and read it through its device view.
+            from lazykv_b200.pinned import device_view, pinned_empty
+
+            with torch.cuda.device(self.dev):
+                self.records_host = pinned_empty((store_blocks, heads, self.W), torch.uint8)
+                self.records = device_view(self.records_host)
+            self.stage: torch.Tensor | None = None  # the step's cold records, staged in HBM
+            self.stage_table = torch.full((max_seqs, self.max_blocks + 1), -1, dtype=torch.int32, device=self.dev)
+        else:
+            self.records = torch.zeros((store_blocks, heads, self.W), dtype=torch.uint8, device=self.dev)
         self.kmin = torch.zeros((heads, store_blocks, head_dim), dtype=dtype, device=self.dev)
         self.kmax = torch.zeros_like(self.kmin)
         self.pool = torch.zeros((max_seqs * self.per_seq, heads, 2, block_size, head_dim), dtype=dtype, device=self.dev)
@@ -210,12 +223,15 @@ class RaggedTier:
         n_ctas = sched.shape[0]
         row_sel = np.stack([n_cand, k], axis=1)
         row_info = np.stack([n_hot, fill, n_cand, np.zeros_like(k)], axis=1)
-        host = np.concatenate([row_sel.ravel(), work.ravel(), row_info.ravel(), sched.ravel()]).astype(np.int32)
+        seq_cand = n_cand[::h].astype(np.int64)
+        stage_first = np.cumsum(seq_cand) - seq_cand  # staged row of each sequence's first candidate (host cold tier)
+        host = np.concatenate([row_sel.ravel(), work.ravel(), row_info.ravel(), sched.ravel(), stage_first]).astype(np.int32)
         dmeta = torch.from_numpy(host).to(dev, non_blocking=False)
         o1 = row_sel.size
         o2 = o1 + work.size
         o3 = o2 + row_info.size
-        d_row_sel, d_work, d_row_info, d_sched = dmeta[:o1], dmeta[o1:o2], dmeta[o2:o3], dmeta[o3:]
+        o4 = o3 + sched.size
+        d_row_sel, d_work, d_row_info, d_sched, d_stage_first = dmeta[:o1], dmeta[o1:o2], dmeta[o2:o3], dmeta[o3:o4], dmeta[o4:]
         if o2 % 4 or o3 % 4:  # 16-byte alignment of row_info and sched
             d_row_info, d_sched = d_row_info.clone(), d_sched.clone()
         sid = torch.tensor(seq_ids, dtype=torch.long, device=dev)
@@ -257,7 +273,19 @@ class RaggedTier:
         hs = L.HotSet(ptr(self.pool), ptr(self.pool[:, :, 1]), dtype_code(self.dtype), s_row, s_head, s_tok, ptr(hot), hot.shape[1], None, 0, 0,
                       self.pool.shape[0])
         ws2 = K.workspace(dev, L.lib().lkv_ragged_attention_workspace(g, n_parts), slot=6)
-        call("lkv_ragged_exact_attention", ptr(query), rows, g, self.d, self.bs, h, ctypes.byref(hs), ptr(self.records), self.records.shape[0],
-             ptr(table), table.stride(0), ptr(excluded), self.words, ptr(d_row_info), ptr(d_sched), n_ctas, n_parts, float(scale), ptr(out),
+        records, att_table = self.records, table
+        if self.cold_placement == "host":
+            # 4. the records the attention reads (every candidate not in the hot set), read over the
+            # link with mapped loads and staged in HBM; the attention then reads them there.
+            n_stage = int(seq_cand.sum())
+            if self.stage is None or self.stage.shape[0] < n_stage:
+                self.stage = torch.empty((max(n_stage, 1), h, self.W), dtype=torch.uint8, device=dev)
+            att_table = self.stage_table[:n]
+            call("lkv_ragged_stage_records", ptr(self.records), self.records.shape[0], h, self.W, ptr(table), table.stride(0), ptr(d_work),
+                 work.shape[0], ptr(d_row_info), ptr(excluded), self.words, ptr(self.stage), self.stage.shape[0], ptr(d_stage_first),
+                 ptr(att_table), att_table.stride(0), stream_handle(dev))
+            records = self.stage
+        call("lkv_ragged_exact_attention", ptr(query), rows, g, self.d, self.bs, h, ctypes.byref(hs), ptr(records), records.shape[0],
+             ptr(att_table), att_table.stride(0), ptr(excluded), self.words, ptr(d_row_info), ptr(d_sched), n_ctas, n_parts, float(scale), ptr(out),
              L.LKV_F32, ptr(lse), ptr(ws2), ws2.numel(), stream_handle(dev))
         return out, lse, sel

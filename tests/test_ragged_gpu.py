@@ -48,13 +48,14 @@ def _check(tier, ids: list[int], kv: dict, gen: torch.Generator, fetch: bool) ->
         np.testing.assert_allclose(lse[b * H * G : (b + 1) * H * G].double().cpu().numpy().reshape(H, G), want["lse"], rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("placement", ["device", "host"])  # the int8 store in HBM, or pinned host memory read over the link
 @pytest.mark.parametrize("fetch", [False, True])  # kept blocks read in place from the store, or fetched into HBM slots
-def test_one_launch_matches_each_sequence_decoded_alone(fetch: bool) -> None:
+def test_one_launch_matches_each_sequence_decoded_alone(fetch: bool, placement: str) -> None:
     from lazykv_b200 import kernels
     from lazykv_b200.ragged import RaggedTier
 
     gen = torch.Generator(device="cuda").manual_seed(11)
-    tier = RaggedTier(H, G, D, BS, max_seqs=8, max_tokens=2048, store_blocks=1024, budget=0.25)
+    tier = RaggedTier(H, G, D, BS, max_seqs=8, max_tokens=2048, store_blocks=1024, budget=0.25, cold_placement=placement)
     lengths = [40, 47, 100, 333, 700, 1500]  # 2 sealed blocks (all kept), a partial tail, many blocks
     kv = {}
     ids = []
@@ -67,13 +68,14 @@ def test_one_launch_matches_each_sequence_decoded_alone(fetch: bool) -> None:
     assert kernels.device_status() == 0
 
 
+@pytest.mark.parametrize("placement", ["device", "host"])
 @pytest.mark.parametrize("fetch", [False, True])
-def test_sequences_grow_seal_finish_and_are_replaced(fetch: bool) -> None:
+def test_sequences_grow_seal_finish_and_are_replaced(fetch: bool, placement: str) -> None:
     from lazykv_b200 import kernels
     from lazykv_b200.ragged import RaggedTier
 
     gen = torch.Generator(device="cuda").manual_seed(12)
-    tier = RaggedTier(H, G, D, BS, max_seqs=6, max_tokens=1024, store_blocks=256, budget=0.25)
+    tier = RaggedTier(H, G, D, BS, max_seqs=6, max_tokens=1024, store_blocks=256, budget=0.25, cold_placement=placement)
     kv = {}
     for n in (63, 64, 200, 511):  # a block-boundary length: the current block starts empty
         keys, values = _kv(gen, n)
@@ -94,11 +96,45 @@ def test_sequences_grow_seal_finish_and_are_replaced(fetch: bool) -> None:
     assert kernels.device_status() == 0
 
 
+@pytest.mark.parametrize("fetch", [False, True])
+def test_host_cold_tier_is_bit_identical_to_the_device_store(fetch: bool) -> None:
+    """The store in pinned host memory (its records staged in HBM by mapped loads each step) gives
+    the outputs, log-sum-exps and selections of the store in HBM, bit for bit; the host store holds
+    the same records."""
+    from lazykv_b200.ragged import RaggedTier
+
+    tiers = [RaggedTier(H, G, D, BS, max_seqs=8, max_tokens=4096, store_blocks=2048, budget=0.0625, cold_placement=p) for p in ("device", "host")]
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    ids = []
+    for n in (33, 64, 777, 2049, 4000):
+        keys, values = _kv(gen, n)
+        slots = [t.add(keys, values) for t in tiers]
+        assert slots[0] == slots[1]
+        ids.append(slots[0])
+    for _ in range(3):
+        q = torch.randn((len(ids) * H * G, D), generator=gen, device="cuda").bfloat16()
+        (oa, la, sa), (ob, lb, sb) = (t.decode(ids, q, SCALE, fetch=fetch) for t in tiers)
+        assert torch.equal(oa, ob) and torch.equal(la, lb)
+        for i, s in enumerate(ids):  # selection entries past a row's K are unspecified
+            k = tiers[0].k_of(s)
+            assert torch.equal(sa[i * H : (i + 1) * H, :k], sb[i * H : (i + 1) * H, :k])
+        k1, v1 = _kv(gen, 1)
+        for t in tiers:
+            for s in ids:
+                t.append(s, k1[:, 0], v1[:, 0])
+    torch.cuda.synchronize()
+    used = torch.tensor(sorted(r for seq in tiers[0].seqs.values() for r in seq.rows))
+    assert used.numel() > 0
+    assert torch.equal(tiers[0].records.cpu()[used], tiers[1].records_host[used])
+
+
 def test_ragged_select_rejects_what_it_cannot_hold() -> None:
     from lazykv_b200.ragged import RaggedTier
 
     with pytest.raises(ValueError, match="tensor-core"):
         RaggedTier(H, G, 128, BS, 2, 1024, 64, 0.25)
+    with pytest.raises(ValueError, match="cold_placement"):
+        RaggedTier(H, G, D, BS, 2, 1024, 64, 0.25, cold_placement="disk")
     tier = RaggedTier(H, G, D, BS, max_seqs=1, max_tokens=256, store_blocks=8, budget=0.25)
     gen = torch.Generator(device="cuda").manual_seed(13)
     keys, values = _kv(gen, 100)
