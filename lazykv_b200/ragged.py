@@ -19,7 +19,11 @@ Layout (one selecting layer):
   - pool [max_seqs * (k_max + 2), h, 2, bs, d] in the model dtype: per sequence slot s, pool row
     s * (k_max + 2) holds the exact sink, the next k_max rows the blocks kept this step, the last
     the current (unsealed) block.
-The store lives in HBM, so by default the kept blocks are attended in place: their records are
+With `cold_placement="host"` the store is pinned host memory instead (written and read through
+its device view); each step the records the attention reads are read over the link with mapped
+loads into an HBM stage (lkv_ragged_stage_records, the zero-copy read of the cold tier of
+lazykv/tiered.py:489-511), and the attention reads the stage: the same values, bit for bit.
+Wherever the store lives, by default the kept blocks are attended in place: their records are
 dequantised in the attention kernel exactly as a fetch would dequantise them into a slot, so the
 step attends [sink, current] from the pool and every candidate block from the store (kept or not),
 which is the same set of values as the hot/cold split; the selection is still computed and returned
