@@ -47,6 +47,7 @@ from lazykv_b200.quant import packed_pair_bytes
 from lazykv_b200.selection import QUEST_DENSE_LAYERS, current_block_mask
 
 NEVER = -(2**40)  # "evicted at" of pairs never evicted (tiered.py:69)
+PREFETCH_WS_SLOT = 8  # selection workspace of the prefetch stream (the compute stream's selections use slot 1)
 BOUNDARY_CHUNK = 128  # blocks packed at once at the boundary (tiered.py:70)
 
 
@@ -69,6 +70,13 @@ class TierCounters:
     ingest_forwards: int = 0
     ingest_tokens: int = 0
     ingest_h2d_bytes: int = 0
+    # The layer-ahead prefetch (tiered.py:94-97): pairs its speculative admits fetched, its admits
+    # (one fetch launch each), their bytes, and how many of those pairs the real selection then chose.
+    host_prefetch_s: float = 0.0
+    prefetched_pairs: int = 0
+    prefetch_transfers: int = 0
+    prefetch_bytes: int = 0
+    prefetch_used_pairs: int = 0
     fetched_pairs_per_step: list[int] = field(default_factory=list)
 
 
@@ -371,6 +379,35 @@ class TieredLayer:
                            self.n_miss, slots_out=self.hot_list[:, 1 : self.k + 1], miss_total=self.fetched_total)
         return self.chosen
 
+    def prefetch_device(self, query: torch.Tensor, step: int, prefetched_total: torch.Tensor) -> None:
+        """The layer-ahead prefetch of this layer (tiered.py:749-798), on the current stream: the
+        selection a speculated query makes, admitted (misses fetched into slots) with the step's
+        LRU stamp, so that the real selection finds those blocks resident. Its own buffers and
+        selection workspace, as it runs on a side stream beside the previous layer."""
+        if getattr(self, "spec_chosen", None) is None:
+            dev = self.pool.device
+            self.spec_chosen = torch.zeros((self.h, self.k), dtype=torch.int32, device=dev)
+            self.spec_miss_blk = torch.zeros((self.h, self.k), dtype=torch.int32, device=dev)
+            self.spec_miss_slot = torch.zeros((self.h, self.k), dtype=torch.int32, device=dev)
+            self.spec_n_miss = torch.zeros((self.h,), dtype=torch.int32, device=dev)
+            self.spec_bitmap = torch.zeros((self.h, self.words), dtype=torch.int32, device=dev)
+            self.spec_lane = torch.arange(self.k, device=dev, dtype=torch.int32)
+        n_full, _ = self.candidates()
+        K.quest_topk(query, self.kmin[0], self.kmax[0], 1, n_full - 1, self.k, out_blocks=self.spec_chosen, by_block=True, ws_slot=PREFETCH_WS_SLOT)
+        K.tier_admit(self.spec_chosen, self._block_slot, self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool,
+                     self.spec_miss_blk, self.spec_miss_slot, self.spec_n_miss, miss_total=prefetched_total)
+        self.pending_prefetch = True
+
+    def count_prefetch_used(self, used_total: torch.Tensor) -> None:
+        """After the real selection (self.chosen): adds to `used_total` the pairs the pending
+        prefetch fetched that it chose (tiered.py:731-734), on the device."""
+        K.mark_blocks(self.chosen, self.spec_bitmap)
+        blk = self.spec_miss_blk
+        words = torch.gather(self.spec_bitmap, 1, (blk >> 5).long())
+        hit = ((words >> (blk & 31)) & 1).bool() & (self.spec_lane[None, :] < self.spec_n_miss[:, None])
+        used_total += hit.sum()
+        self.pending_prefetch = False
+
     def admit_device(self, step: int) -> None:
         """Device-side admit of self.chosen and the fetch of its misses; fills the hot list."""
         K.tier_admit(self.chosen, self._block_slot, self._slot_block, self._last_used, self._evicted_at, step, self.store, self.pool,
@@ -587,8 +624,11 @@ class TieredCache(Cache):
     """Decode-time cache: dense layers share the prefilled FullGPUCache, selecting layers are tiered.
 
     Constructor of lazykv/tiered.py:546-565 (plus `cold_placement`). The residency decision runs on
-    the device, which the reference's layer-ahead prefetch (rung 7) and its record/replay ablation
-    existed to work around; both are refused with a message rather than silently ignored.
+    the device. `prefetch=True` adds the reference's layer-ahead prefetch (rung 7): a pre-hook on
+    each decoder layer before a selecting one speculates the next layer's query and runs its
+    selection and admit on a side stream; the real selection then waits for it and finds those
+    blocks resident. Outputs do not change (the attention reads the same values wherever a block
+    sits); `close()` removes the hooks.
     """
 
     def __init__(self, full: FullGPUCache, k_blocks: int, block_size: int, capacity_tokens: int, model: PreTrainedModel | None = None,
@@ -607,8 +647,6 @@ class TieredCache(Cache):
             if prefetch or record_selection or replay_selection is not None:
                 raise ValueError("the zero-copy fetch has no residency to prefetch, record or replay")
             n_slots = 0 if n_slots is None else n_slots
-        if prefetch:
-            raise ValueError("the layer-ahead prefetch is not built: residency is decided on the device, with no host round trip to hide")
         if replay_selection is not None and not isinstance(replay_selection, Mapping):
             raise ValueError("replay_selection maps (layer, step) to the chosen block ids [h, K] of that step")
         # (layer, step) -> chosen block ids [h, K]; recorded as device copies, read back on demand
@@ -617,8 +655,8 @@ class TieredCache(Cache):
         self._replay: Mapping[tuple[int, int], np.ndarray] | None = replay_selection
         self.full, self.k_blocks, self.block_size, self.dense_layers = full, k_blocks, block_size, dense_layers
         self.thrash_window, self.instrument, self.quant, self.fetch = thrash_window, instrument, quant, fetch
-        self.prefetch = False
-        self.policy_name = "tiered_int8" if quant else ("tiered_zerocopy" if fetch == "zerocopy" else "tiered_sync")
+        self.prefetch = bool(prefetch)
+        self.policy_name = "tiered_int8" if quant else ("tiered_prefetch" if prefetch else ("tiered_zerocopy" if fetch == "zerocopy" else "tiered_sync"))
         self.counters = TierCounters()
         if tiers is None:
             tiers = {}
@@ -645,6 +683,22 @@ class TieredCache(Cache):
         for t in self.tiers.values():
             t.fetched_total = self._fetched
         self._last_chosen: torch.Tensor | None = None
+        # The layer-ahead prefetch (tiered.py:625-638): a pre-hook on decoder layer L speculates layer
+        # L + 1's query and runs that layer's selection and admit on a side stream while layer L computes.
+        self._hooks: list[Any] = []
+        self._copy_events: dict[int, torch.cuda.Event] = {}
+        self._window: dict[int, tuple[torch.cuda.Event, torch.cuda.Event, torch.cuda.Event]] = {}
+        self._timed: list[tuple[torch.cuda.Event, torch.cuda.Event, torch.cuda.Event, torch.cuda.Event]] = []
+        self.copy_stream: torch.cuda.Stream | None = None
+        if self.prefetch:
+            dev = next(iter(self.tiers.values())).pool.device
+            self._prefetched = torch.zeros((), dtype=torch.int64, device=dev)
+            self._prefetch_used = torch.zeros((), dtype=torch.int64, device=dev)
+            self.copy_stream = torch.cuda.Stream(device=dev)
+            decoder = model.model.layers  # type: ignore[union-attr]
+            for src in range(max(dense_layers - 1, 0), len(decoder) - 1):
+                if src + 1 in self.tiers:
+                    self._hooks.append(decoder[src].register_forward_pre_hook(self._make_hook(src + 1, decoder[src + 1]), with_kwargs=True))
 
     # -- transformers plumbing ------------------------------------------------------------------------
 
@@ -674,9 +728,81 @@ class TieredCache(Cache):
         return {"lazykv_selector": self}
 
     def close(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks.clear()
         if self._step > 0:
             self._flush_step()
             self._step = 0
+
+    def _make_hook(self, target: int, target_layer: torch.nn.Module):  # noqa: ANN202
+        """The pre-hook of the layer before `target` (tiered.py:749-798): layer target's query as it
+        would be if the layer in between changed nothing (the residual stream through target's own
+        norm, projection and rotary embedding), its selection and admit on the copy stream."""
+        attn, norm = target_layer.self_attn, target_layer.input_layernorm
+
+        def hook(module: torch.nn.Module, args: tuple[Any, ...], kwargs: dict[str, Any]) -> None:
+            hidden = args[0] if args else kwargs["hidden_states"]
+            if hidden.shape[1] != 1 or target not in self.tiers or kwargs.get("past_key_values", self) is not self:
+                return  # not a decode step, or a forward over another cache
+            t0 = time.perf_counter()
+            tier = self.tiers[target]
+            cos, sin = kwargs["position_embeddings"]
+            q = attn.q_proj(norm(hidden)).view(1, 1, -1, tier.d).transpose(1, 2)
+            half = tier.d // 2
+            q = q * cos.unsqueeze(1) + torch.cat((-q[..., half:], q[..., :half]), dim=-1) * sin.unsqueeze(1)
+            stream = self.copy_stream
+            assert stream is not None
+            ws = torch.cuda.Event(enable_timing=True) if self.instrument else None
+            if ws is not None:
+                ws.record()
+            stream.wait_stream(torch.cuda.current_stream(stream.device))
+            with torch.cuda.stream(stream):
+                start = torch.cuda.Event(enable_timing=self.instrument)
+                start.record()
+                tier.prefetch_device(q, self._step, self._prefetched)
+                done = torch.cuda.Event(enable_timing=self.instrument)
+                done.record()
+            q.record_stream(stream)
+            self._copy_events[target] = done
+            if ws is not None:
+                self._window[target] = (ws, start, done)
+            self.counters.prefetch_transfers += 1
+            self.counters.host_prefetch_s += time.perf_counter() - t0
+
+        return hook
+
+    def _await_prefetch(self, layer_idx: int) -> None:
+        """The selection below reads the tables and slots the layer's prefetch may still be writing."""
+        ev = self._copy_events.pop(layer_idx, None)
+        if ev is None:
+            return
+        win = self._window.pop(layer_idx, None)
+        if win is not None:
+            we = torch.cuda.Event(enable_timing=True)
+            we.record()  # the compute stream reaches the target layer
+            self._timed.append((win[0], win[1], win[2], we))
+        torch.cuda.current_stream().wait_event(ev)
+
+    def overlap(self) -> dict[str, Any]:
+        """Measured overlap of each prefetch with the compute it was launched beside (tiered.py:
+        802-830): per prefetch, its interval on the copy stream and the compute stream's interval
+        from the launch until the target layer began selecting; the overlap fraction is the share
+        of the prefetch inside that window, the stall how long the target layer waited for it.
+        Needs `instrument=True`; synchronises the device."""
+        if not self._timed:
+            return {"prefetches_timed": 0}
+        torch.cuda.synchronize()
+        fractions, copy_ms, stall_ms, window_ms = [], [], [], []
+        for ws, cs_ev, ce_ev, we_ev in self._timed:
+            cs, ce, we = ws.elapsed_time(cs_ev), ws.elapsed_time(ce_ev), ws.elapsed_time(we_ev)
+            dur = ce - cs
+            inside = max(0.0, min(ce, we) - max(cs, 0.0))
+            fractions.append(1.0 if dur <= 0 else inside / dur)
+            copy_ms.append(dur)
+            stall_ms.append(max(0.0, ce - we))
+            window_ms.append(we)
+        return {"prefetches_timed": len(self._timed), "overlap_fraction": fractions, "copy_ms": copy_ms, "stall_ms": stall_ms, "window_ms": window_ms}
 
     def _begin_step(self) -> None:
         # A bounded wait that ran out on the device during an earlier step poisoned that step's
@@ -704,7 +830,10 @@ class TieredCache(Cache):
         scale = scaling if scaling is not None else tier.d**-0.5
         out_dtype = query.dtype if self.exact_pass and self.fetch != "zerocopy" else torch.float32
         replay = None if self._replay is None else self._replay[(layer_idx, self._step)]
+        self._await_prefetch(layer_idx)
         out = tier.attend(query, scale, self._step, self.exact_pass, zerocopy=self.fetch == "zerocopy", out_dtype=out_dtype, chosen=replay)
+        if getattr(tier, "pending_prefetch", False):
+            tier.count_prefetch_used(self._prefetch_used)
         if self._record is not None:
             self._record[(layer_idx, self._step)] = tier.chosen.clone()  # a device copy: no host sync per step
         c = self.counters
@@ -722,6 +851,7 @@ class TieredCache(Cache):
             return None
         if self.fetch == "zerocopy":
             raise ValueError("the zero-copy tier attends in place; use decode()")
+        self._await_prefetch(layer_idx)
         if self._replay is None:
             chosen = tier.rank(query, bitmap=self.exact_pass)
             tier.chosen.copy_(torch.from_numpy(chosen).to(torch.int32))
@@ -731,6 +861,8 @@ class TieredCache(Cache):
         if self._record is not None:
             self._record[(layer_idx, self._step)] = chosen
         tier.admit_device(self._step)
+        if getattr(tier, "pending_prefetch", False):
+            tier.count_prefetch_used(self._prefetch_used)
         self._last_chosen = tier.chosen.clone()
         self.counters.selections += 1
         self.counters.selected_pairs += chosen.size
@@ -758,6 +890,10 @@ class TieredCache(Cache):
             self.counters.fetched_pairs = total
             self.counters.hit_pairs = self.counters.selected_pairs - total
             self.counters.fetch_bytes = total * next(iter(self.tiers.values())).pair_bytes
+        if self.prefetch:
+            self.counters.prefetched_pairs = int(self._prefetched.item())
+            self.counters.prefetch_bytes = self.counters.prefetched_pairs * next(iter(self.tiers.values())).pair_bytes
+            self.counters.prefetch_used_pairs = int(self._prefetch_used.item())
         return asdict(self.counters)
 
     def stats(self) -> CacheStats:

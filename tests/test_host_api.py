@@ -56,14 +56,14 @@ def test_tier_configurations_are_refused_before_any_device_work() -> None:
     full = FullGPUCache(4, 64)
     with pytest.raises(ValueError, match="needs the model"):
         TieredCache(full, 3, 8, 64, prefetch=True)
-    with pytest.raises(ValueError, match="not built"):
-        TieredCache(full, 3, 8, 64, model=object(), prefetch=True)  # type: ignore[arg-type]
     with pytest.raises(ValueError, match="unknown fetch"):
         TieredCache(full, 3, 8, 64, fetch="bulk")
     with pytest.raises(ValueError, match="needs fetch='gather'"):
         TieredCache(full, 3, 8, 64, quant="int8")
     with pytest.raises(ValueError, match="zero-copy"):
         TieredCache(full, 3, 8, 64, fetch="zerocopy", record_selection=True)
+    with pytest.raises(ValueError, match="zero-copy"):
+        TieredCache(full, 3, 8, 64, model=object(), fetch="zerocopy", prefetch=True)  # type: ignore[arg-type]
     with pytest.raises(ValueError, match="zero-copy"):
         TieredCache(full, 3, 8, 64, fetch="zerocopy", replay_selection={})
     with pytest.raises(ValueError, match="maps \\(layer, step\\)"):

@@ -18,9 +18,12 @@ def tiny():  # noqa: ANN201
     return make_tiny()
 
 
+@pytest.mark.parametrize("prefetch", [False, True])
 @pytest.mark.parametrize(("fetch", "spare"), [("runs", 0), ("gather", 0), ("gather", 2)])
-def test_tier_is_bit_identical_to_questview(tiny, fetch: str, spare: int) -> None:  # noqa: ANN001
-    """tests/test_tiered.py:58: residency moves blocks into slots; the attention reads the same bytes."""
+def test_tier_is_bit_identical_to_questview(tiny, fetch: str, spare: int, prefetch: bool) -> None:  # noqa: ANN001
+    """tests/test_tiered.py:58: residency moves blocks into slots; the attention reads the same bytes
+    (with the layer-ahead prefetch too: it changes where blocks sit and when they arrive, not what
+    is attended)."""
     from lazykv_b200.selection import QuestView
     from lazykv_b200.tiered import TieredCache
 
@@ -30,11 +33,15 @@ def test_tier_is_bit_identical_to_questview(tiny, fetch: str, spare: int) -> Non
     ref = forced(model, quest, pre, ids, 40)  # crosses several seals
     assert quest.counters.selections > 0
     full.truncate(PROMPT)
-    tier = TieredCache(full, K, BS, capacity_tokens=CAP, model=model, dense_layers=1, n_slots=K + spare, fetch=fetch)
+    tier = TieredCache(full, K, BS, capacity_tokens=CAP, model=model, dense_layers=1, n_slots=K + spare, fetch=fetch, prefetch=prefetch)
     got = forced(model, tier, pre, ids, 40)
     tier.close()
     assert torch.equal(got, ref)
     c = tier.counters_dict()
+    if prefetch:
+        assert c["prefetched_pairs"] > 0 and 0 <= c["prefetch_used_pairs"] <= c["prefetched_pairs"]
+        assert c["prefetch_transfers"] == c["selections"]  # every selecting layer step (layer 1's from the hook on layer 0)
+        assert tier.policy_name == "tiered_prefetch"
     assert c["selections"] == quest.counters.selections
     assert c["seals"] == ((PROMPT + 39) // BS - PROMPT // BS) * 3  # 3 tiered layers
     assert c["hit_pairs"] + c["fetched_pairs"] == c["selected_pairs"]
@@ -166,7 +173,7 @@ def test_budget_that_covers_every_block_is_refused(tiny) -> None:  # noqa: ANN00
 
 
 def test_refusals(tiny) -> None:  # noqa: ANN001
-    """The reference's layer-ahead prefetch is refused loudly; so is zero-copy with it or with record/replay."""
+    """Zero-copy has no residency to prefetch, record or replay: refused loudly."""
     from lazykv_b200.tiered import TieredCache
 
     cfg, model = tiny
@@ -175,8 +182,6 @@ def test_refusals(tiny) -> None:  # noqa: ANN001
         TieredCache(full, K, BS, capacity_tokens=CAP, model=model, dense_layers=1, fetch="zerocopy", prefetch=True)
     with pytest.raises(ValueError, match="zero-copy"):
         TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="zerocopy", record_selection=True)
-    with pytest.raises(ValueError, match="prefetch"):
-        TieredCache(full, K, BS, capacity_tokens=CAP, model=model, dense_layers=1, prefetch=True)
     with pytest.raises(ValueError, match="zero-copy"):
         TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="zerocopy", replay_selection={})
 
@@ -215,3 +220,44 @@ def test_select_protocol_matches_decode(tiny) -> None:  # noqa: ANN001
     proto.close()
     assert (a - b).abs().max().item() < 0.02
     check_residency(proto)
+
+
+def test_close_removes_prefetch_hooks(tiny) -> None:  # noqa: ANN001
+    """tests/test_tiered.py:141: one pre-hook per selecting layer after the first, removed by close()."""
+    from lazykv_b200.tiered import TieredCache
+
+    cfg, model = tiny
+    _, full, _ = prefilled(model, cfg)
+    before = [len(layer._forward_pre_hooks) for layer in model.model.layers]
+    cache = TieredCache(full, K, BS, capacity_tokens=CAP, model=model, prefetch=True, dense_layers=1)
+    assert sum(len(layer._forward_pre_hooks) for layer in model.model.layers) == sum(before) + 3
+    cache.close()
+    assert [len(layer._forward_pre_hooks) for layer in model.model.layers] == before
+
+
+@pytest.mark.parametrize("quant", [None, "int8"])
+def test_prefetch_leaves_the_decode_unchanged_and_measures_its_overlap(tiny, quant: str | None) -> None:  # noqa: ANN001
+    """The same log-probs with and without the prefetch (bf16 and int8 tiers, a pool of K + 3 slots
+    so that prefetched blocks can stay resident); with instrument=True, overlap() reports one timed
+    prefetch per prefetching layer step, each fraction in [0, 1]."""
+    from lazykv_b200.tiered import TieredCache
+
+    cfg, model = tiny
+    ids, full, pre = prefilled(model, cfg)
+    kw = {"fetch": "gather", "quant": quant, "n_slots": K + 3}
+    base = TieredCache(full, K, BS, capacity_tokens=CAP, model=model, dense_layers=1, **kw)
+    ref = forced(model, base, pre, ids, 30)
+    base.close()
+    full.truncate(PROMPT)
+    pf = TieredCache(full, K, BS, capacity_tokens=CAP, model=model, dense_layers=1, prefetch=True, instrument=True, **kw)
+    got = forced(model, pf, pre, ids, 30)
+    pf.close()
+    full.truncate(PROMPT)
+    assert torch.equal(got, ref)
+    c, b = pf.counters_dict(), base.counters_dict()
+    assert c["selected_pairs"] == b["selected_pairs"] and c["hit_pairs"] + c["fetched_pairs"] == c["selected_pairs"]
+    assert c["prefetched_pairs"] > 0 and c["prefetch_used_pairs"] > 0
+    ov = pf.overlap()
+    assert ov["prefetches_timed"] == 29 * 3  # every selecting layer, every decode step
+    assert all(0.0 <= f <= 1.0 for f in ov["overlap_fraction"]) and all(s >= 0.0 for s in ov["stall_ms"])
+    check_residency(pf)

@@ -29,14 +29,14 @@ def _reference(model, cfg, ids, chunk: int, cache_cls=None, **kw):  # noqa: ANN0
 
 
 @pytest.mark.parametrize("chunk", [32, 100, 128])
-@pytest.mark.parametrize("quant", [None, "int8"])
-def test_layer_major_prefill_matches_the_full_cache_path(tiny, chunk: int, quant: str | None) -> None:  # noqa: ANN001
+@pytest.mark.parametrize(("prefetch", "quant"), [(False, None), (True, None), (False, "int8")])
+def test_layer_major_prefill_matches_the_full_cache_path(tiny, chunk: int, prefetch: bool, quant: str | None) -> None:  # noqa: ANN001
     from lazykv_b200.generate import teacher_forced_decode
     from lazykv_b200.tiered_prefill import tiered_prefill
 
     cfg, model = tiny
     ids = ids_for(cfg)
-    kw = {"fetch": "gather", "quant": quant}
+    kw = {"prefetch": prefetch, "fetch": "gather", "quant": quant}
     ref_logits, ref = _reference(model, cfg, ids, chunk, **kw)
     got = tiered_prefill(model, ids[:, :PROMPT], chunk, K, BS, CAP, dense_layers=1, **kw)
     assert got.chunks == -(-PROMPT // chunk)
