@@ -557,6 +557,32 @@ class TieredLayer:
         K.lse_merge(torch.stack(parts_o), torch.stack(parts_l), torch.float32, out=self.out, lse_out=self.lse)
         return self.out
 
+    def gather_zerocopy(self, query: torch.Tensor, mask_cache: dict[str, Any], bitmap: bool = False) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Attention inputs read by the GPU straight from the pinned store (tiered.py:489-511): the
+        selection on the device in rank order (marking the bitmap when `bitmap`), the selected pairs
+        gathered through the store's device view (loads over the link), between the sink and the
+        current block from the pool. No slots, no host sync; the blocks and order of gather()."""
+        if self.quant is not None:
+            raise ValueError("the zero-copy fetch reads bf16 blocks in place; the int8 tier needs fetch='gather'")
+        n_full, _ = self.candidates()
+        top, _ = K.quest_topk(query, self.kmin[0], self.kmax[0], 1, n_full - 1, self.k, out_blocks=self.chosen,
+                              bitmap=self.bitmap if bitmap else None)
+        dev = self.pool.device
+        heads = torch.arange(self.h, device=dev)
+        rows = (top.long() * self.h + heads[:, None]).reshape(-1)
+        sel = self.host_dev.view(-1, 2, self.bs, self.d).index_select(0, rows).view(self.h, self.k, 2, self.bs, self.d)
+        ends = self.pool[[0, self.tail_slot]].permute(1, 0, 2, 3, 4)  # [h, 2 (sink, current), 2, bs, d]
+        blocks = torch.cat([ends[:, :1], sel, ends[:, 1:]], dim=1)  # [h, K + 2, 2, bs, d]
+        k2 = self.k + 2
+        shape = (1, self.h, k2 * self.bs, self.d)
+        k_sel = blocks[:, :, 0].reshape(shape)
+        v_sel = blocks[:, :, 1].reshape(shape)
+        fill = self.fill
+        if mask_cache.get("fill") != fill or mask_cache.get("total") != k2 * self.bs:
+            mask_cache["mask"] = current_block_mask(k2 * self.bs, self.bs, fill, query.dtype, query.device)
+            mask_cache["fill"], mask_cache["total"] = fill, k2 * self.bs
+        return k_sel, v_sel, mask_cache["mask"]
+
     # -- the reference's host-facing calls (synchronising) ------------------------------------------
 
     def rank(self, query: torch.Tensor, bitmap: bool = False) -> np.ndarray:
@@ -850,7 +876,12 @@ class TieredCache(Cache):
         if tier is None or query.shape[-2] != 1:
             return None
         if self.fetch == "zerocopy":
-            raise ValueError("the zero-copy tier attends in place; use decode()")
+            out = tier.gather_zerocopy(query, self._mask_cache, bitmap=self.exact_pass)
+            c = self.counters
+            c.selections += 1
+            c.selected_pairs += tier.h * tier.k
+            c.zerocopy_bytes += tier.h * tier.k * tier.pair_bytes
+            return out
         self._await_prefetch(layer_idx)
         if self._replay is None:
             chosen = tier.rank(query, bitmap=self.exact_pass)
@@ -907,6 +938,15 @@ class TieredCache(Cache):
 
     def host_pinned_bytes(self) -> int:
         return sum(t.host.numel() * t.host.element_size() for t in self.tiers.values())
+
+
+def allocate_stages(cap_pairs: int, heads: int, head_dim: int, block_size: int, dtype: torch.dtype = torch.bfloat16,
+                    quant: str | None = None) -> tuple[None, None]:
+    """The reference's gather-mode staging buffers (tiered.py:863-871), for drop-in calls: the
+    device admit fetches with loads from the store, with no host-side gather or staging copy, so
+    there is nothing to allocate; TieredCache accepts the returned pair as `stages` and ignores it."""
+    del cap_pairs, heads, head_dim, block_size, dtype, quant
+    return None, None
 
 
 def allocate_host_pools(n_layers: int, heads: int, head_dim: int, block_size: int, capacity_tokens: int, dtype: torch.dtype = torch.bfloat16,

@@ -116,5 +116,30 @@ def test_chunked_prefill_through_the_hook_matches_one_pass_on_cpu() -> None:
     pre = prefill(model, full, ids, chunk_size=16)
     assert pre.chunks == 3 and full.layers[0].get_seq_length() == 37
     assert torch.allclose(pre.last_logits, want, atol=1e-4)
-    toks = greedy_decode(model, full, pre.last_logits, 3)
-    assert len(toks) == 4 and full.layers[0].get_seq_length() == 40
+    res = greedy_decode(model, full, pre.last_logits, 3)
+    assert len(res.tokens) == 4 and len(res.wall_s) == len(res.event_s) == 3 and full.layers[0].get_seq_length() == 40
+    assert pre.wall_s > 0.0 and pre.event_s == 0.0  # a CPU model: no device events
+
+
+def test_teacher_forced_logprobs_are_the_decode_rows_on_cpu() -> None:
+    """teacher_forced_logprobs = prefill of the context, then one row per continuation position
+    from single-token steps; rows are log-probabilities."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from lazykv_b200.attention import IMPLEMENTATION_NAME, install
+    from lazykv_b200.generate import teacher_forced_decode, teacher_forced_logprobs, prefill
+
+    torch.manual_seed(1)
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2, head_dim=16,
+                      vocab_size=96, max_position_embeddings=256)
+    install()
+    model = LlamaForCausalLM(copy.deepcopy(cfg)).eval()
+    model.set_attn_implementation(IMPLEMENTATION_NAME)
+    ctx, cont = torch.randint(0, cfg.vocab_size, (1, 20)), torch.randint(0, cfg.vocab_size, (1, 5))
+    got = teacher_forced_logprobs(model, FullGPUCache(2, 64), ctx, cont, chunk_size=8)
+    full = FullGPUCache(2, 64)
+    pre = prefill(model, full, ctx, chunk_size=8)
+    want = torch.stack(list(teacher_forced_decode(model, full, pre.last_logits, cont)))
+    assert got.shape == (5, cfg.vocab_size) and got.device.type == "cpu"
+    assert torch.equal(got, want)
+    assert torch.allclose(got.exp().sum(-1), torch.ones(5), atol=1e-5)

@@ -261,3 +261,29 @@ def test_prefetch_leaves_the_decode_unchanged_and_measures_its_overlap(tiny, qua
     assert ov["prefetches_timed"] == 29 * 3  # every selecting layer, every decode step
     assert all(0.0 <= f <= 1.0 for f in ov["overlap_fraction"]) and all(s >= 0.0 for s in ov["stall_ms"])
     check_residency(pf)
+
+
+def test_zerocopy_select_gathers_what_the_slot_tier_gathers(tiny) -> None:  # noqa: ANN001
+    """tests/test_tiered.py:190 through select(): gather_zerocopy reads the selected pairs through
+    the pinned store's device view; the gathered keys and values (up to the current block's fill)
+    and the mask equal those of the slot tier's select(), which admits and gathers from slots."""
+    from lazykv_b200.tiered import TieredCache, allocate_stages
+
+    cfg, model = tiny
+    _, full, _ = prefilled(model, cfg)
+    zc = TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="zerocopy")
+    slots = TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="gather", stages=allocate_stages(64, 2, cfg.head_dim, BS))
+    h, hq, d = cfg.num_key_value_heads, cfg.num_attention_heads, cfg.head_dim
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    kv = torch.zeros((1, h, 1, d), dtype=torch.bfloat16, device="cuda")
+    for step in range(1, 4):
+        q = torch.randn((1, hq, 1, d), generator=gen, device="cuda").bfloat16()
+        for cache in (zc, slots):
+            cache._step = step
+        for layer in zc.tiers:
+            a, b = zc.select(layer, q, kv, kv), slots.select(layer, q, kv, kv)
+            valid = (K + 1) * BS + zc.tiers[layer].fill
+            assert torch.equal(a[0][:, :, :valid], b[0][:, :, :valid]) and torch.equal(a[1][:, :, :valid], b[1][:, :, :valid])
+            assert torch.equal(a[2], b[2])
+    c = zc.counters_dict()
+    assert c["zerocopy_bytes"] == c["selected_pairs"] * next(iter(zc.tiers.values())).pair_bytes > 0
