@@ -361,6 +361,16 @@ int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32
                    int32_t* slots_out, int64_t slots_ld, int64_t* miss_total, void* stream);
 
 /*
+ * Decode-time append (lazykv/tiered.py:306-334, the write of a new token into the block being
+ * filled): T tokens of keys k and values v (element (head, token, channel) at head * s_head + token *
+ * s_tok + channel, in elements of `dtype`) into slot [h, 2, bs, d] of the pool at token positions
+ * fill .. fill + T - 1 (fill + T <= bs). One launch for both halves.
+ */
+int lkv_append_tokens(const void* k, int64_t k_s_head, int64_t k_s_tok, const void* v,
+                      int64_t v_s_head, int64_t v_s_tok, int h, int t, int d, int dtype, void* slot,
+                      int bs, int fill, void* stream);
+
+/*
  * The bitmap of a selection made elsewhere (a recorded one replayed, lazykv/tiered.py:715-724):
  * for head j, bitmap [h, bitmap_words] row j is cleared, then the bit of every id in ids [h, k]
  * (row stride ids_ld) is set, as lkv_quest_topk sets it for its own selection; -1 entries and ids

@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                      c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64,
                                      c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "lkv_mark_blocks": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_int, c_void_p]),
+    "lkv_append_tokens": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p]),
     "lkv_ragged_stage_records": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
                                          c_int64, c_void_p, c_void_p, c_int64, c_void_p]),
 }

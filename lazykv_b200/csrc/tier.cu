@@ -551,3 +551,41 @@ extern "C" int lkv_ragged_stage_records(const uint8_t* records, int64_t n_record
       stage_stride);
   return launched(who);
 }
+
+// ---- Decode-time KV append into the pool's current block ----
+//
+// T tokens of keys and values (element (head, token, channel) at head * s_head + token * s_tok +
+// channel, in elements) into a pool slot [h, 2, bs, d] at token positions fill .. fill + T - 1: one
+// launch in place of a copy per half. Elements move as raw 2- or 4-byte words.
+template <typename W>
+__global__ void __launch_bounds__(256) append_tokens_kernel(const W* __restrict__ k, int64_t ksh, int64_t kst, const W* __restrict__ v, int64_t vsh,
+                                                            int64_t vst, W* __restrict__ slot, int h, int t, int d, int bs, int fill) {
+  const int64_t n = (int64_t)h * t * d;  // elements per half
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < 2 * n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int half = i >= n ? 1 : 0;
+    const int64_t r = i - half * n;
+    const int c = (int)(r % d);
+    const int64_t ht = r / d;
+    const int tok = (int)(ht % t), head = (int)(ht / t);
+    const W* src = half ? v + head * vsh + tok * vst : k + head * ksh + tok * kst;
+    slot[((int64_t)head * 2 + half) * bs * d + (int64_t)(fill + tok) * d + c] = src[c];
+  }
+}
+
+extern "C" int lkv_append_tokens(const void* k, int64_t k_s_head, int64_t k_s_tok, const void* v, int64_t v_s_head, int64_t v_s_tok, int h, int t,
+                                 int d, int dtype, void* slot, int bs, int fill, void* stream) {
+  if (!dtype_ok(dtype)) return fail(LKV_ERR_ARG, "lkv_append_tokens: bad dtype %d", dtype);
+  if (k == nullptr || v == nullptr || slot == nullptr) return fail(LKV_ERR_PTR, "lkv_append_tokens: null pointer");
+  if (h <= 0 || t <= 0 || d <= 0 || bs <= 0 || fill < 0 || fill + t > bs)
+    return fail(LKV_ERR_ARG, "lkv_append_tokens: %d tokens at fill %d do not fit a block of %d", t, fill, bs);
+  const int64_t total = 2ll * h * t * d;
+  const int blocks = (int)((total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024);
+  cudaStream_t st = as_stream(stream);
+  if (dtype == LKV_BF16)
+    append_tokens_kernel<uint16_t><<<blocks, 256, 0, st>>>(static_cast<const uint16_t*>(k), k_s_head, k_s_tok, static_cast<const uint16_t*>(v),
+                                                            v_s_head, v_s_tok, static_cast<uint16_t*>(slot), h, t, d, bs, fill);
+  else
+    append_tokens_kernel<uint32_t><<<blocks, 256, 0, st>>>(static_cast<const uint32_t*>(k), k_s_head, k_s_tok, static_cast<const uint32_t*>(v),
+                                                            v_s_head, v_s_tok, static_cast<uint32_t*>(slot), h, t, d, bs, fill);
+  return launched("lkv_append_tokens");
+}

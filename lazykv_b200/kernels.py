@@ -33,6 +33,12 @@ def workspace(device: torch.device, nbytes: int, slot: int = 0) -> torch.Tensor:
     return buf
 
 
+def current_workspace(device: torch.device, slot: int = 0) -> torch.Tensor | None:
+    """The buffer workspace() would hand out now for (device, slot), without growing it (None if
+    there is none yet): a caller holding an earlier buffer compares identities to see a regrowth."""
+    return _WS.get((device.index if device.index is not None else torch.cuda.current_device(), slot))
+
+
 def packed_pair_bytes(block_size: int, head_dim: int) -> int:
     return int(L.lib().lkv_packed_pair_bytes(block_size, head_dim))
 
@@ -379,6 +385,19 @@ def tier_admit(chosen: torch.Tensor, block_slot: torch.Tensor, slot_block: torch
     call("lkv_tier_admit", ptr(chosen), h, k, chosen.stride(0), ptr(block_slot), block_slot.shape[1], ptr(slot_block), ptr(last_used), n_slots,
          ptr(evicted_at), step, ptr(store), kind, ptr(pool), bs, d, dtype_code(pool.dtype), ptr(miss_blk), ptr(miss_slot), ptr(n_miss),
          ptr(slots_out), 0 if slots_out is None else slots_out.stride(0), ptr(miss_total), stream_handle(dev))
+
+
+def append_tokens(keys: torch.Tensor, values: torch.Tensor, slot: torch.Tensor, fill: int) -> None:
+    """keys / values [h, T, d] (unit channel stride) into pool slot [h, 2, bs, d] at token positions
+    fill .. fill + T - 1, in one launch (lkv_append_tokens)."""
+    dev = require_cuda(keys, values, slot)
+    h, t, d = keys.shape
+    if values.shape != keys.shape or keys.dtype != slot.dtype or values.dtype != slot.dtype or keys.stride(-1) != 1 or values.stride(-1) != 1:
+        raise ValueError("append_tokens needs keys and values [h, T, d] of the slot's dtype with unit channel stride")
+    if not slot.is_contiguous() or slot.shape[0] != h or slot.shape[1] != 2 or slot.shape[-1] != d:
+        raise ValueError(f"append_tokens needs a contiguous slot [{h}, 2, bs, {d}]")
+    call("lkv_append_tokens", ptr(keys), keys.stride(0), keys.stride(1), ptr(values), values.stride(0), values.stride(1), h, t, d,
+         dtype_code(slot.dtype), ptr(slot), slot.shape[2], fill, stream_handle(dev))
 
 
 def mark_blocks(ids: torch.Tensor, bitmap: torch.Tensor) -> torch.Tensor:

@@ -321,8 +321,33 @@ class TieredLayer:
             done += span
 
     def append(self, key: torch.Tensor, value: torch.Tensor, counters: TierCounters) -> None:
-        """One decode token's KV [1, h, 1, d]."""
-        self._write_tokens(key, value, counters)
+        """One decode token's KV [1, h, 1, d]: one launch writes both halves into the current block
+        (lkv_append_tokens); KV of another dtype goes through the converting copies."""
+        pool = self.pool
+        if key.dtype != pool.dtype or value.dtype != pool.dtype or key.stride(-1) != 1 or value.stride(-1) != 1 or key.device != pool.device:
+            self._write_tokens(key, value, counters)
+            return
+        if self.fill == self.bs:
+            self._seal(counters)
+        fast = self.__dict__.get("_append_args")
+        if fast is None:
+            fast = self._append_args = (L.lib().lkv_append_tokens, L.dtype_code(pool.dtype), pool[self.tail_slot].data_ptr())
+        fn, code, tail = fast
+        rc = fn(key.data_ptr(), key.stride(1), key.stride(2), value.data_ptr(), value.stride(1), value.stride(2), self.h, 1, self.d, code, tail,
+                self.bs, self.fill, L.stream_handle(pool.device))
+        if rc != 0:
+            raise L.LkvError(f"lkv_append_tokens failed ({rc}): {L.last_error()}")
+        self.fill += 1
+        self.length += 1
+
+    def tail_views(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """The current block's keys and values [1, h, bs, d] as views of the pool (what update()
+        returns for a decode token; the device attention never reads them)."""
+        views = self.__dict__.get("_tail_views")
+        if views is None:
+            t = self.tail_slot
+            views = self._tail_views = (self.pool[t : t + 1, :, 0], self.pool[t : t + 1, :, 1])
+        return views
 
     def extend(self, keys: torch.Tensor, values: torch.Tensor, counters: TierCounters) -> None:
         """A multi-token forward's KV [1, h, T, d], as T appends would write it."""
@@ -480,14 +505,17 @@ class TieredLayer:
         if not q.is_contiguous():
             q = q.contiguous()
         key = (hq, query.dtype, self.n_sealed, self.out_q.data_ptr())
-        plan = getattr(self, "_plan", None)
-        n_cand = self.n_sealed - 1
-        ws_sel = K.workspace(dev, self._ws_bytes(("sel", n_cand), lambda: int(L.lib().lkv_quest_topk_workspace(self.h, n_cand))), 1)
-        n_list = self.hot_list.shape[1]
-        ws_att = K.workspace(dev, self._ws_bytes(("att", hq, n_cand), lambda: int(L.lib().lkv_exact_attention_workspace(self.h, hq, d, n_list, n_cand))),
-                             0)
-        if plan is None or plan["key"] != key or plan["ws"] != (ws_sel.data_ptr(), ws_att.data_ptr()):
+        plan = self.__dict__.get("_plan")
+        # The plan holds the workspaces' addresses: it is rebuilt when the sealed count (and so the
+        # sizes) changes, or when another call grew and so replaced a workspace.
+        if plan is None or plan["key"] != key or K.current_workspace(dev, 1) is not plan["ws_t"][0] or K.current_workspace(dev, 0) is not plan["ws_t"][1]:
+            n_cand = self.n_sealed - 1
+            ws_sel = K.workspace(dev, self._ws_bytes(("sel", n_cand), lambda: int(L.lib().lkv_quest_topk_workspace(self.h, n_cand))), 1)
+            n_list = self.hot_list.shape[1]
+            ws_att = K.workspace(dev, self._ws_bytes(("att", hq, n_cand), lambda: int(L.lib().lkv_exact_attention_workspace(self.h, hq, d, n_list, n_cand))),
+                                 0)
             plan = self._plan = self._build_plan(key, q, n_cand, ws_sel, ws_att)
+            plan["ws_t"] = (ws_sel, ws_att)
         stream = L.stream_handle(dev)
         sel, att, hot = plan["sel"], plan["att"], plan["hot"]
         if not selected:
@@ -744,7 +772,7 @@ class TieredCache(Cache):
             c.ingest_h2d_bytes += moved
             return k, v
         tier.append(key_states, value_states, self.counters)
-        return tier.pool[tier.tail_slot : tier.tail_slot + 1, :, 0], tier.pool[tier.tail_slot : tier.tail_slot + 1, :, 1]
+        return tier.tail_views()
 
     def get_seq_length(self, layer_idx: int = 0) -> int:
         tier = self.tiers.get(layer_idx)

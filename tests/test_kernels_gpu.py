@@ -334,3 +334,25 @@ def test_bounds_and_selection_every_head_dim(d: int, dt: torch.dtype, order: str
     assert np.array_equal(np.sort(got, 1), np.sort(want, 1))
     if order == "bound":
         assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("t,fill", [(1, 0), (1, 15), (5, 3), (16, 0)])
+def test_append_tokens_writes_both_halves_at_the_fill(dtype: torch.dtype, t: int, fill: int) -> None:
+    """lkv_append_tokens: keys / values [h, T, d] (strided views) land at token positions fill ..
+    fill + T - 1 of the slot's two halves; nothing else in the pool changes."""
+    from lazykv_b200 import kernels as K
+    from lazykv_b200._lib import LkvError
+
+    h, bs, d = 8, 16, 64
+    gen = torch.Generator(device=DEV).manual_seed(t * 100 + fill)
+    pool = torch.randn((4, h, 2, bs, d), generator=gen, device=DEV).to(dtype)
+    kv = torch.randn((2, 1, h, t + 2, d), generator=gen, device=DEV).to(dtype)
+    keys, values = kv[0, 0, :, 1 : t + 1], kv[1, 0, :, 2 : t + 2]  # [h, T, d], token stride d, head stride (t + 2) d
+    want = pool.clone()
+    want[2, :, 0, fill : fill + t] = keys
+    want[2, :, 1, fill : fill + t] = values
+    K.append_tokens(keys, values, pool[2], fill)
+    assert torch.equal(pool, want)
+    with pytest.raises(LkvError):  # past the end of the block
+        K.append_tokens(keys, values, pool[2], bs - t + 1)
