@@ -39,7 +39,9 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // cuTensorMapEncodeTiled is a pure function of its arguments (the address, sizes, strides, box and
 // modes), so a map encoded once can be reused by every later launch over the same buffer: an eager
 // decode loop that calls the kernels with the same stores every step then pays the encoding once.
-// A fixed table of the most recent distinct argument sets, replaced round-robin, under a mutex.
+// A fixed table of distinct argument sets, looked up by a hash of the arguments (a short linear
+// probe from the hashed slot; a miss with every probed slot taken replaces the first of them),
+// under a mutex.
 
 namespace {
 
@@ -57,15 +59,23 @@ struct MapKey {
   CUtensorMapFloatOOBfill oob;
 };
 
-constexpr int kMapCacheSize = 512;
+constexpr int kMapCacheSize = 512;  // a power of two
+constexpr int kMapProbe = 8;
 struct MapEntry {
   bool used;
   MapKey key;
   CUtensorMap map;
 };
 MapEntry g_maps[kMapCacheSize];
-int g_map_next = 0;
 std::mutex g_map_mu;
+
+// FNV-1a over the key's bytes (padding zeroed by the caller).
+uint64_t map_hash(const MapKey& k) {
+  const unsigned char* p = reinterpret_cast<const unsigned char*>(&k);
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < sizeof(MapKey); ++i) h = (h ^ p[i]) * 1099511628211ull;
+  return h;
+}
 
 }  // namespace
 
@@ -89,16 +99,23 @@ CUresult encode_tiled(CUtensorMap* out, CUtensorMapDataType dt, cuuint32_t rank,
   key.sw = sw;
   key.l2 = l2;
   key.oob = oob;
+  const int home = (int)(map_hash(key) & (kMapCacheSize - 1));
   std::lock_guard<std::mutex> lock(g_map_mu);
-  for (int i = 0; i < kMapCacheSize; ++i)
-    if (g_maps[i].used && memcmp(&g_maps[i].key, &key, sizeof(key)) == 0) {
-      *out = g_maps[i].map;
+  int free_slot = -1;
+  for (int p = 0; p < kMapProbe; ++p) {
+    MapEntry& e = g_maps[(home + p) & (kMapCacheSize - 1)];
+    if (!e.used) {
+      if (free_slot < 0) free_slot = (home + p) & (kMapCacheSize - 1);
+      continue;
+    }
+    if (memcmp(&e.key, &key, sizeof(key)) == 0) {
+      *out = e.map;
       return CUDA_SUCCESS;
     }
+  }
   const CUresult r = enc(out, dt, rank, base, dims, strides, box, estr, il, sw, l2, oob);
   if (r == CUDA_SUCCESS) {
-    MapEntry& e = g_maps[g_map_next];
-    g_map_next = (g_map_next + 1) % kMapCacheSize;
+    MapEntry& e = g_maps[free_slot >= 0 ? free_slot : home];
     e.used = true;
     e.key = key;
     e.map = *out;

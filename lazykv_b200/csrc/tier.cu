@@ -13,6 +13,7 @@
 // The fetch kernel then copies each miss from the host store (pairs in the model dtype, or int8
 // records dequantised exactly as lazykv/quant.py:unpack) into its slot of the pool
 // [n_slots + 2, h, 2, bs, d].
+#include <atomic>
 #include "admit.cuh"
 #include "common.cuh"
 
@@ -405,7 +406,17 @@ extern "C" int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chose
     aa.slots_ld = slots_ld;
     aa.miss_total = miss_total;
     cudaError_t e = cudaSuccess;
-    if (staged > 48 * 1024) e = cudaFuncSetAttribute(admit_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged);
+    if (staged > 48 * 1024) {
+      // The attribute is raised once per device to the largest size a call has needed.
+      static std::atomic<int> set_bytes[64];
+      int dev = 0;
+      e = cudaGetDevice(&dev);
+      std::atomic<int>& cur = set_bytes[dev & 63];
+      if (e == cudaSuccess && cur.load() < (int)staged) {
+        e = cudaFuncSetAttribute(admit_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged);
+        if (e == cudaSuccess) cur.store((int)staged);
+      }
+    }
     if (e == cudaSuccess) e = launch_pdl(admit_staged_kernel, dim3(h), dim3(kAdmitCtaThreads), staged, st, 0, chosen, k, chosen_ld, aa);
     if (e != cudaSuccess) {
       cudaGetLastError();
