@@ -1295,7 +1295,8 @@ def run_e2e_api(args: argparse.Namespace, geo: dict, layers: list, dev, timed) -
         tiers[DENSE + i] = TieredLayer(keys, values, geo["k_total"], BS, cap, quant="int8", cold_placement="device")
         del keys, values
     full = FullGPUCache(DENSE + n_sel, cap)
-    cache = ExactTieredCache(full, geo["k_total"], BS, cap, dense_layers=DENSE, quant="int8", fetch="gather", tiers=tiers)
+    split = not args.admit_first  # the order of the device-timed step: the attention does not wait for the admit
+    cache = ExactTieredCache(full, geo["k_total"], BS, cap, dense_layers=DENSE, quant="int8", fetch="gather", tiers=tiers, resident_split=split)
     q_host = torch.stack([L.q_ring for L in layers], dim=1).cpu().pin_memory()  # [R, layers, HQ, D]
     kv_host = torch.randn((R, DENSE + n_sel, 2, 1, HKV, 1, D), generator=torch.Generator().manual_seed(7)).bfloat16().pin_memory()
     o_host = torch.empty((n_sel, HQ, D), dtype=torch.bfloat16).pin_memory()
@@ -1329,7 +1330,10 @@ def run_e2e_api(args: argparse.Namespace, geo: dict, layers: list, dev, timed) -
     return {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "path": "ExactTieredCache.update (every layer) + ExactTieredCache.decode (every selecting layer): the drop-in API a model's "
                     "attention hook calls, eager; each step one copy in of every layer's query and new KV from pinned host memory and one "
-                    "copy out of every layer's output; int8 tier with the cold store in HBM"}
+                    "copy out of every layer's output; int8 tier with the cold store in HBM; "
+                    + ("admit first (--admit-first)" if args.admit_first else
+                       "ExactTieredCache(resident_split=True): the attention before the admit, which runs beside it on a second stream, "
+                       "as in the device-timed step")}
 
 
 # ---------------------------------------------------------------------------------------------

@@ -87,11 +87,20 @@ class ExactTieredCache(TieredCache):
 
     Constructor of lazykv/exact.py:164 (`mirrors` and `threads` are accepted for drop-in calls and
     unused: there is no host mirror and no CPU pass). A prefetch is refused, as in the reference.
+
+    `resident_split=True` (an addition): each decode step selects with the resident slots listed
+    (lkv_quest_topk_resident), attends at once, the chosen blocks not resident yet from their cold
+    records, and runs the admit and the fetch of the misses beside the attention on a second stream.
+    The attention then no longer waits for the admit. Outputs equal the admit-first order's within
+    float32 rounding, but which blocks come from slots and which from records depends on residency,
+    so the last bits do too: a session restored from a snapshot (which reseeds residency) continues
+    bit for bit only with the default admit-first order.
     """
 
     exact_pass = True
 
-    def __init__(self, full: FullGPUCache, *args: Any, mirrors: Any = None, threads: int | None = 8, **kwargs: Any) -> None:
+    def __init__(self, full: FullGPUCache, *args: Any, mirrors: Any = None, threads: int | None = 8, resident_split: bool = False,
+                 **kwargs: Any) -> None:
         if kwargs.get("prefetch"):
             raise ValueError("rung 9 does not prefetch; the cold set is attended, not fetched")
         super().__init__(full, *args, **kwargs)
@@ -99,6 +108,11 @@ class ExactTieredCache(TieredCache):
         self.exact = ExactCounters()
         self.threads = threads
         self.mirrors: dict[int, Any] = {}
+        self.resident_split = bool(resident_split) and self.fetch != "zerocopy" and all(t.h <= 64 for t in self.tiers.values())
+        if self.resident_split:
+            stream = torch.cuda.Stream(device=next(iter(self.tiers.values())).pool.device)
+            for t in self.tiers.values():
+                t.admit_stream = stream
 
     def _count(self, layer_idx: int) -> None:
         tier = self.tiers[layer_idx]

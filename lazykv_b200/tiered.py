@@ -278,7 +278,48 @@ class TieredLayer:
     # -- residency tables, as numpy copies (synchronising) -----------------------------------------
 
     def _get(self, t: torch.Tensor) -> np.ndarray:
+        ev = self.__dict__.get("_admit_done")
+        if ev is not None:
+            ev.synchronize()  # an admit beside the attention may still be writing the tables
         return t.cpu().numpy()
+
+    # -- the admit beside the attention (exact tier, resident split) ---------------------------------
+
+    admit_stream: torch.cuda.Stream | None = None  # set by the cache: the exact pass attends before the admit
+
+    def join_admit(self) -> None:
+        """The current stream waits for this layer's last admit beside the attention (tables, slots
+        and the fetch counter it writes)."""
+        ev = self.__dict__.get("_admit_done")
+        if ev is not None:
+            torch.cuda.current_stream().wait_event(ev)
+
+    def _resident_listing(self) -> None:
+        """For a selection loaded into self.chosen: the hot list gets each chosen block's slot, or -1
+        where it is not resident, and the bitmap marks only the resident ones (what
+        lkv_quest_topk_resident writes for its own selection)."""
+        slots = torch.gather(self._block_slot, 1, self.chosen.long())
+        resident = slots >= 1
+        self.hot_list[:, 1 : self.k + 1] = torch.where(resident, slots, -1)
+        K.mark_blocks(torch.where(resident, self.chosen, -1), self.bitmap)
+
+    def _admit_beside(self, plan: dict, step: int) -> None:
+        """The admit of self.chosen and the fetch of its misses on the admit stream, after the
+        selection (`fork`, recorded before the attention was launched), with no slots_out: its victims
+        are never slots the hot list names. Launched after the attention, so that the attention's
+        CTAs are placed first."""
+        side = self.admit_stream
+        assert side is not None
+        fork, done = plan["events"]
+        side.wait_event(fork)
+        adm = plan["adm"]
+        adm[10] = step
+        adm[-1] = side.cuda_stream
+        rc = plan["adm_fn"](*adm)
+        if rc != 0:
+            raise L.LkvError(f"lkv_tier_admit failed ({rc}): {L.last_error()}")
+        done.record(side)
+        self._admit_done = done
 
     @property
     def slot_block(self) -> np.ndarray:
@@ -483,9 +524,13 @@ class TieredLayer:
                 raise ValueError("the zero-copy fetch has no residency to replay")
             self.choose(query, bitmap=exact)
             return self._attend_zerocopy(query, scale, exact, pool_strides)
+        split = exact and self.admit_stream is not None
         if chosen is not None:
-            self.load_chosen(chosen, bitmap=exact)
-            self.admit_device(step)
+            if split:
+                self.join_admit()  # the last admit beside the attention still reads self.chosen
+            self.load_chosen(chosen, bitmap=exact and not split)
+            if not split:
+                self.admit_device(step)
         if exact:  # choose_and_admit, then K.exact_attention into out_q: the two calls, argument lists cached
             return self._exact_step(query, scale, step, selected=chosen is not None)
         if chosen is None:
@@ -518,7 +563,22 @@ class TieredLayer:
             plan["ws_t"] = (ws_sel, ws_att)
         stream = L.stream_handle(dev)
         sel, att, hot = plan["sel"], plan["att"], plan["hot"]
-        if not selected:
+        split = self.admit_stream is not None
+        if split:
+            # Resident split: the selection lists the resident slots, the attention covers the misses
+            # from their records, and the admit runs beside it on the admit stream.
+            self.join_admit()
+            if not selected:
+                res = plan["res"]
+                res[0] = q.data_ptr()
+                res[-1] = stream
+                rc = plan["res_fn"](*res)
+                if rc != 0:
+                    raise L.LkvError(f"lkv_quest_topk_resident failed ({rc}): {L.last_error()}")
+            else:
+                self._resident_listing()
+            plan["events"][0].record()  # the selection is done: the admit may start after it
+        elif not selected:
             sel[0] = q.data_ptr()
             sel[26] = step
             sel[-1] = stream
@@ -532,6 +592,8 @@ class TieredLayer:
         rc = plan["att_fn"](*att)
         if rc != 0:
             raise L.LkvError(f"lkv_exact_attention failed ({rc}): {L.last_error()}")
+        if split:
+            self._admit_beside(plan, step)
         return self.out_q
 
     def _ws_bytes(self, key: tuple, size_of) -> int:  # noqa: ANN001
@@ -563,9 +625,19 @@ class TieredLayer:
         att = [q.data_ptr(), hq, h, d, self.bs, ctypes.byref(hot), ctypes.byref(cold), 1.0, self.out_q.data_ptr(), L.dtype_code(self.out_q.dtype),
                self.lse.data_ptr(), None, None,
                ws_att.data_ptr(), ws_att.numel(), 0]
+        # The resident selection (lkv_quest_topk_resident) and the admit without slots_out
+        # (lkv_tier_admit) of the resident split.
+        res = [q.data_ptr(), qd, hq, h, d, kmin.data_ptr(), kmax.data_ptr(), L.dtype_code(kmin.dtype), kmin.stride(-3), 1, n_cand, self.k, qd,
+               self.chosen.data_ptr(), self.chosen.stride(0), self._block_slot.data_ptr(), self._block_slot.shape[1], slots.data_ptr(),
+               slots.stride(0), self.bitmap.data_ptr(), self.bitmap.shape[-1], ws_sel.data_ptr(), ws_sel.numel(), 0]
+        adm = [self.chosen.data_ptr(), h, self.k, self.chosen.stride(0), self._block_slot.data_ptr(), self._block_slot.shape[1],
+               self._slot_block.data_ptr(), self._last_used.data_ptr(), self._slot_block.shape[1], self._evicted_at.data_ptr(), 0,
+               self.store.data_ptr(), kind, self.pool.data_ptr(), self.pool.shape[-2], self.d, L.dtype_code(self.pool.dtype), self.miss_blk.data_ptr(),
+               self.miss_slot.data_ptr(), self.n_miss.data_ptr(), None, 0, self.fetched_total.data_ptr(), 0]
         lib = L.lib()
         return {"key": key, "ws": (ws_sel.data_ptr(), ws_att.data_ptr()), "sel": sel, "att": att, "hot": hot, "cold": cold,
-                "sel_fn": lib.lkv_quest_topk_admit, "att_fn": lib.lkv_exact_attention}
+                "sel_fn": lib.lkv_quest_topk_admit, "att_fn": lib.lkv_exact_attention, "res": res, "res_fn": lib.lkv_quest_topk_resident,
+                "adm": adm, "adm_fn": lib.lkv_tier_admit, "events": (torch.cuda.Event(), torch.cuda.Event())}
 
     def _attend_zerocopy(self, query: torch.Tensor, scale: float, exact: bool, pool_strides: tuple[int, int, int]) -> torch.Tensor:
         """No slots: the selected blocks are read in place from the host store, the sink and the
@@ -866,9 +938,16 @@ class TieredCache(Cache):
             self._flush_step()
         self._step += 1
 
+    def _join_admits(self) -> None:
+        """The current stream waits for every admit still running beside an attention."""
+        for t in self.tiers.values():
+            if t.admit_stream is not None:
+                t.join_admit()
+
     def _flush_step(self) -> None:
         # The step's fetch total stays on the device until the counters are read: no host sync here.
         if self.fetch != "zerocopy":
+            self._join_admits()
             self._step_marks.append(self._fetched.clone())
 
     # -- decode ---------------------------------------------------------------------------------------------
@@ -942,6 +1021,7 @@ class TieredCache(Cache):
     # -- accounting --------------------------------------------------------------------------------------
 
     def counters_dict(self) -> dict[str, Any]:
+        self._join_admits()
         if self.fetch != "zerocopy":
             marks = [int(m.item()) for m in self._step_marks]
             self.counters.fetched_pairs_per_step = [b - a for a, b in zip([0] + marks[:-1], marks)]

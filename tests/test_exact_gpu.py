@@ -102,8 +102,9 @@ def _within_delta(want: torch.Tensor, got: torch.Tensor, bar: float) -> float:
 
 
 @pytest.mark.parametrize("budget_blocks", [2, K])
-@pytest.mark.parametrize("fetch", ["gather", "zerocopy"])
-def test_exact_tier_reproduces_the_full_cache(tiny, budget_blocks: int, fetch: str) -> None:  # noqa: ANN001
+@pytest.mark.parametrize(("fetch", "split"), [("gather", False), ("gather", True), ("zerocopy", False)])
+def test_exact_tier_reproduces_the_full_cache(tiny, budget_blocks: int, fetch: str, split: bool) -> None:  # noqa: ANN001
+    """split: the resident split (attention before the admit, the admit on a second stream)."""
     from lazykv_b200.exact import ExactTieredCache
 
     cfg, model = tiny
@@ -112,7 +113,8 @@ def test_exact_tier_reproduces_the_full_cache(tiny, budget_blocks: int, fetch: s
     want = forced(model, full, pre, ids, steps)
     full.truncate(PROMPT)
     n_slots = None if fetch == "zerocopy" else budget_blocks + 1
-    cache = ExactTieredCache(full, budget_blocks, BS, capacity_tokens=CAP, dense_layers=1, fetch=fetch, n_slots=n_slots)
+    cache = ExactTieredCache(full, budget_blocks, BS, capacity_tokens=CAP, dense_layers=1, fetch=fetch, n_slots=n_slots, resident_split=split)
+    assert cache.resident_split == split
     got = forced(model, cache, pre, ids, steps)
     cache.close()
     full.truncate(PROMPT)
@@ -168,11 +170,12 @@ def test_exact_tier_refuses_a_prefetch(tiny) -> None:  # noqa: ANN001
         ExactTieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="gather", model=model, prefetch=True)
 
 
-@pytest.mark.parametrize("placement", ["host", "device"])
-def test_int8_exact_step_matches_the_oracle(tiny, placement: str) -> None:  # noqa: ANN001
+@pytest.mark.parametrize(("placement", "split"), [("host", False), ("device", False), ("host", True), ("device", True)])
+def test_int8_exact_step_matches_the_oracle(tiny, placement: str, split: bool) -> None:  # noqa: ANN001
     """One exact int8 decode step of a tiered layer against the CPU restatement of the composition:
     sink and current block exact, every other sealed block as unpack(record) in bf16 (selected or
-    not), merged. Float32 output within 1e-5 of the float64 oracle."""
+    not), merged. Float32 output within 1e-5 of the float64 oracle. With the resident split the
+    chosen blocks not yet resident are attended from their records while the admit runs beside."""
     import oracle
     from lazykv_b200.exact import ExactTieredCache
     from tests.golden.inputs import to_np
@@ -180,7 +183,8 @@ def test_int8_exact_step_matches_the_oracle(tiny, placement: str) -> None:  # no
     cfg, model = tiny
     _, full, _ = prefilled(model, cfg)
     sealed_kv = {i: (full.layers[i].keys[0, :, :PROMPT].clone(), full.layers[i].values[0, :, :PROMPT].clone()) for i in range(1, 4)}
-    cache = ExactTieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="gather", quant="int8", cold_placement=placement)
+    cache = ExactTieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="gather", quant="int8", cold_placement=placement,
+                             resident_split=split)
     gen = torch.Generator(device="cuda").manual_seed(3)
     for i, tier in cache.tiers.items():
         q = torch.randn((1, cfg.num_attention_heads, 1, cfg.head_dim), generator=gen, device="cuda").to(torch.bfloat16)

@@ -31,10 +31,10 @@ def _cache(full, kind: str, **kw):  # noqa: ANN001, ANN202
         return TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="gather", **kw)
     if kind == "int8":
         return TieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="gather", quant="int8", **kw)
-    return ExactTieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="gather", quant="int8", **kw)
+    return ExactTieredCache(full, K, BS, capacity_tokens=CAP, dense_layers=1, fetch="gather", quant="int8", resident_split=kind == "exact_split", **kw)
 
 
-@pytest.mark.parametrize("kind", ["bf16", "int8", "exact"])
+@pytest.mark.parametrize("kind", ["bf16", "int8", "exact", "exact_split"])
 @pytest.mark.parametrize("stall", [False, True])
 def test_replaying_a_recorded_selection_reproduces_the_run_exactly(tiny, kind: str, stall: bool) -> None:  # noqa: ANN001
     cfg, model = tiny
