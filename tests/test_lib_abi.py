@@ -64,3 +64,27 @@ def test_invalid_arguments_return_a_status_and_a_message(lib) -> None:  # noqa: 
     assert lib.lkv_attention_workspace(8, 32, 64, 2048) > 0
     buf = ctypes.create_string_buffer(4)
     assert lib.lkv_last_error(buf, 4) > 3 and len(buf.value) == 3
+
+
+def test_the_append_mark_and_stage_entries_reject_bad_arguments(lib) -> None:  # noqa: ANN001
+    """lkv_append_tokens, lkv_mark_blocks and lkv_ragged_stage_records validate before any launch."""
+    from lazykv_b200 import _lib
+
+    fake = ctypes.c_void_p(16)  # never dereferenced: every call below fails its checks first
+    # 3 tokens at fill 14 overrun a block of 16
+    rc = lib.lkv_append_tokens(fake, 64, 64, fake, 64, 64, 8, 3, 64, _lib.LKV_BF16, fake, 16, 14, None)
+    assert rc == 1 and "do not fit" in _lib.last_error()
+    rc = lib.lkv_append_tokens(None, 64, 64, fake, 64, 64, 8, 1, 64, _lib.LKV_BF16, fake, 16, 0, None)
+    assert rc == 2 and "null" in _lib.last_error()
+    rc = lib.lkv_append_tokens(fake, 64, 64, fake, 64, 64, 8, 1, 64, 7, fake, 16, 0, None)
+    assert rc == 1 and "dtype" in _lib.last_error()
+    # a row stride below k; a null bitmap
+    rc = lib.lkv_mark_blocks(fake, 8, 10, 5, fake, 4, None)
+    assert rc == 1 and "ids_ld >= k" in _lib.last_error()
+    rc = lib.lkv_mark_blocks(fake, 8, 10, 10, None, 4, None)
+    assert rc == 2 and "null" in _lib.last_error()
+    # a record width that is not a multiple of 16; a misaligned stage
+    rc = lib.lkv_ragged_stage_records(fake, 10, 8, 2360, fake, 9, fake, 1, fake, None, 0, fake, 10, fake, fake, 9, None)
+    assert rc == 1 and "bad shape" in _lib.last_error()
+    rc = lib.lkv_ragged_stage_records(fake, 10, 8, 2368, fake, 9, fake, 1, fake, None, 0, ctypes.c_void_p(24), 10, fake, fake, 9, None)
+    assert rc == 2 and "16-byte aligned" in _lib.last_error()
