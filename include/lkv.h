@@ -361,6 +361,75 @@ int lkv_tier_admit(const int32_t* chosen, int h, int k, int64_t chosen_ld, int32
                    int32_t* slots_out, int64_t slots_ld, int64_t* miss_total, void* stream);
 
 /*
+ * One decode step of an exact int8/bf16 tier in the resident-split order, as a single call: for a
+ * host that issues every layer's step eagerly, the three calls and the stream hand-off below cost
+ * it less in one than in five (no reference counterpart: the reference's step is host-driven).
+ * In order, on `stream` unless said:
+ *   1. wait for the previous step's admit of the same events object (its tables, slots, chosen ids);
+ *   2. unless `selected` is set (a selection already in `chosen`, its hot list and bitmap written by
+ *      the caller), lkv_quest_topk_resident with the q / kmin / kmax / chosen / block_slot / hot /
+ *      bitmap fields and the selection workspace;
+ *   3. lkv_exact_attention over hot_set and cold_set into out / lse with the attention workspace;
+ *   4. on `admit_stream`, after step 2: lkv_tier_admit of `chosen` (no slots_out), the misses fetched
+ *      from `store` into `pool`, miss_total (optional) counting them; then the events object
+ *      records this admit's completion.
+ * The attention therefore runs while the admit does; its victims are never slots the hot list
+ * names. Field meanings, limits and errors are those of the three entry points; the first failure
+ * is returned (later parts are not issued). Events: lkv_split_events_create (two CUDA events,
+ * no device memory; make it with the tier's device current), lkv_split_events_destroy;
+ * lkv_split_join makes `stream` wait for the last admit, lkv_split_wait makes the host wait for it.
+ */
+typedef struct {
+  const void* q;
+  int q_dtype, hq, h, d;
+  const void* kmin;
+  const void* kmax;
+  int meta_dtype;
+  int64_t m_head;
+  int first_block, n_cand, k, bound_mode;
+  int32_t* chosen;
+  int chosen_ld;
+  int32_t* block_slot;
+  int cap;
+  int32_t* hot;
+  int64_t hot_ld;
+  uint32_t* bitmap;
+  int bitmap_words;
+  void* sel_workspace;
+  size_t sel_workspace_bytes;
+  int bs;
+  const lkv_hot_set* hot_set;
+  const lkv_cold_set* cold_set;
+  float scale;
+  void* out;
+  int out_dtype;
+  float* lse;
+  void* att_workspace;
+  size_t att_workspace_bytes;
+  int32_t* slot_block;
+  int64_t* last_used;
+  int n_slots;
+  int64_t* evicted_at;
+  int64_t step;
+  const void* store;
+  int store_kind;
+  void* pool;
+  int pool_dtype;
+  int32_t* miss_blk;
+  int32_t* miss_slot;
+  int32_t* n_miss;
+  int64_t* miss_total;
+  int selected;
+} lkv_split_step_args;
+
+typedef struct lkv_split_events lkv_split_events;
+int lkv_split_events_create(lkv_split_events** out);
+int lkv_split_events_destroy(lkv_split_events* ev);
+int lkv_split_step(const lkv_split_step_args* a, lkv_split_events* ev, void* stream, void* admit_stream);
+int lkv_split_join(lkv_split_events* ev, void* stream);
+int lkv_split_wait(lkv_split_events* ev);
+
+/*
  * Decode-time append (lazykv/tiered.py:306-334, the write of a new token into the block being
  * filled): T tokens of keys k and values v (element (head, token, channel) at head * s_head + token *
  * s_tok + channel, in elements of `dtype`) into slot [h, 2, bs, d] of the pool at token positions

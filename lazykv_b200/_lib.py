@@ -74,6 +74,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                      c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64,
                                      c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "lkv_mark_blocks": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_int, c_void_p]),
+    "lkv_split_events_create": (c_int, [c_void_p]),
+    "lkv_split_events_destroy": (c_int, [c_void_p]),
+    "lkv_split_step": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "lkv_split_join": (c_int, [c_void_p, c_void_p]),
+    "lkv_split_wait": (c_int, [c_void_p]),
     "lkv_append_tokens": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p]),
     "lkv_ragged_stage_records": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
                                          c_int64, c_void_p, c_void_p, c_int64, c_void_p]),
@@ -92,6 +97,20 @@ class ColdSet(ctypes.Structure):
     """lkv_cold_set of include/lkv.h."""
 
     _fields_ = [("store", c_void_p), ("kind", c_int), ("first_block", c_int), ("n_blocks", c_int), ("excluded", c_void_p), ("bitmap_words", c_int)]
+
+
+class SplitStepArgs(ctypes.Structure):
+    """lkv_split_step_args of include/lkv.h (same fields, same order)."""
+
+    _fields_ = [("q", c_void_p), ("q_dtype", c_int), ("hq", c_int), ("h", c_int), ("d", c_int), ("kmin", c_void_p), ("kmax", c_void_p),
+                ("meta_dtype", c_int), ("m_head", c_int64), ("first_block", c_int), ("n_cand", c_int), ("k", c_int), ("bound_mode", c_int),
+                ("chosen", c_void_p), ("chosen_ld", c_int), ("block_slot", c_void_p), ("cap", c_int), ("hot", c_void_p), ("hot_ld", c_int64),
+                ("bitmap", c_void_p), ("bitmap_words", c_int), ("sel_workspace", c_void_p), ("sel_workspace_bytes", c_size_t), ("bs", c_int),
+                ("hot_set", c_void_p), ("cold_set", c_void_p), ("scale", ctypes.c_float), ("out", c_void_p), ("out_dtype", c_int),
+                ("lse", c_void_p), ("att_workspace", c_void_p), ("att_workspace_bytes", c_size_t), ("slot_block", c_void_p),
+                ("last_used", c_void_p), ("n_slots", c_int), ("evicted_at", c_void_p), ("step", c_int64), ("store", c_void_p),
+                ("store_kind", c_int), ("pool", c_void_p), ("pool_dtype", c_int), ("miss_blk", c_void_p), ("miss_slot", c_void_p),
+                ("n_miss", c_void_p), ("miss_total", c_void_p), ("selected", c_int)]
 
 
 class LkvError(RuntimeError):

@@ -14,6 +14,7 @@
 // records dequantised exactly as lazykv/quant.py:unpack) into its slot of the pool
 // [n_slots + 2, h, 2, bs, d].
 #include <atomic>
+#include <new>
 #include "admit.cuh"
 #include "common.cuh"
 
@@ -599,4 +600,99 @@ extern "C" int lkv_append_tokens(const void* k, int64_t k_s_head, int64_t k_s_to
     append_tokens_kernel<uint32_t><<<blocks, 256, 0, st>>>(static_cast<const uint32_t*>(k), k_s_head, k_s_tok, static_cast<const uint32_t*>(v),
                                                             v_s_head, v_s_tok, static_cast<uint32_t*>(slot), h, t, d, bs, fill);
   return launched("lkv_append_tokens");
+}
+
+// ---- One resident-split decode step in one call (lkv_split_step) ----
+
+struct lkv_split_events {
+  cudaEvent_t fork;     // the selection is done: the admit may start
+  cudaEvent_t done;     // the admit is done
+  bool pending;         // done has been recorded at least once
+};
+
+extern "C" int lkv_split_events_create(lkv_split_events** out) {
+  if (out == nullptr) return fail(LKV_ERR_PTR, "lkv_split_events_create: null pointer");
+  auto* ev = new (std::nothrow) lkv_split_events{};
+  if (ev == nullptr) return fail(LKV_ERR_ARG, "lkv_split_events_create: out of host memory");
+  cudaError_t e = cudaEventCreateWithFlags(&ev->fork, cudaEventDisableTiming);
+  if (e == cudaSuccess) {
+    e = cudaEventCreateWithFlags(&ev->done, cudaEventDisableTiming);
+    if (e != cudaSuccess) cudaEventDestroy(ev->fork);
+  }
+  if (e != cudaSuccess) {
+    delete ev;
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_split_events_create: %s", cudaGetErrorString(e));
+  }
+  *out = ev;
+  return LKV_OK;
+}
+
+extern "C" int lkv_split_events_destroy(lkv_split_events* ev) {
+  if (ev == nullptr) return LKV_OK;
+  cudaEventDestroy(ev->fork);
+  cudaEventDestroy(ev->done);
+  cudaGetLastError();  // a context torn down at exit: nothing left to release
+  delete ev;
+  return LKV_OK;
+}
+
+extern "C" int lkv_split_join(lkv_split_events* ev, void* stream) {
+  if (ev == nullptr) return fail(LKV_ERR_PTR, "lkv_split_join: null events");
+  if (!ev->pending) return LKV_OK;
+  const cudaError_t e = cudaStreamWaitEvent(as_stream(stream), ev->done, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_split_join: %s", cudaGetErrorString(e));
+  }
+  return LKV_OK;
+}
+
+extern "C" int lkv_split_wait(lkv_split_events* ev) {
+  if (ev == nullptr) return fail(LKV_ERR_PTR, "lkv_split_wait: null events");
+  if (!ev->pending) return LKV_OK;
+  const cudaError_t e = cudaEventSynchronize(ev->done);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_split_wait: %s", cudaGetErrorString(e));
+  }
+  return LKV_OK;
+}
+
+extern "C" int lkv_split_step(const lkv_split_step_args* a, lkv_split_events* ev, void* stream, void* admit_stream) {
+  if (a == nullptr || ev == nullptr) return fail(LKV_ERR_PTR, "lkv_split_step: null arguments or events");
+  cudaStream_t st = as_stream(stream), side = as_stream(admit_stream);
+  if (st == side) return fail(LKV_ERR_ARG, "lkv_split_step: the admit needs a stream of its own");
+  if (int rc = lkv_split_join(ev, stream)) return rc;
+  if (!a->selected) {
+    if (int rc = lkv_quest_topk_resident(a->q, a->q_dtype, a->hq, a->h, a->d, a->kmin, a->kmax, a->meta_dtype, a->m_head, a->first_block, a->n_cand,
+                                         a->k, a->bound_mode, a->chosen, a->chosen_ld, a->block_slot, a->cap, a->hot, a->hot_ld, a->bitmap,
+                                         a->bitmap_words, a->sel_workspace, a->sel_workspace_bytes, stream))
+      return rc;
+  }
+  cudaError_t e = cudaEventRecord(ev->fork, st);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_split_step(fork): %s", cudaGetErrorString(e));
+  }
+  if (int rc = lkv_exact_attention(a->q, a->hq, a->h, a->d, a->bs, a->hot_set, a->cold_set, a->scale, a->out, a->out_dtype, a->lse, nullptr, nullptr,
+                                   a->att_workspace, a->att_workspace_bytes, stream))
+    return rc;
+  // Launched after the attention, so that the attention's CTAs are placed first.
+  e = cudaStreamWaitEvent(side, ev->fork, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_split_step(wait): %s", cudaGetErrorString(e));
+  }
+  if (int rc = lkv_tier_admit(a->chosen, a->h, a->k, a->chosen_ld, a->block_slot, a->cap, a->slot_block, a->last_used, a->n_slots, a->evicted_at,
+                              a->step, a->store, a->store_kind, a->pool, a->bs, a->d, a->pool_dtype, a->miss_blk, a->miss_slot, a->n_miss, nullptr, 0,
+                              a->miss_total, admit_stream))
+    return rc;
+  e = cudaEventRecord(ev->done, side);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LKV_ERR_CUDA, "lkv_split_step(done): %s", cudaGetErrorString(e));
+  }
+  ev->pending = true;
+  return LKV_OK;
 }

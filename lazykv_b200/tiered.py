@@ -29,7 +29,9 @@ as the selection's own choice), which repeats the recorded run's fetches and out
 
 from __future__ import annotations
 
+import ctypes
 import time
+import weakref
 from collections.abc import Mapping
 from dataclasses import asdict, dataclass, field
 from typing import Any
@@ -278,21 +280,37 @@ class TieredLayer:
     # -- residency tables, as numpy copies (synchronising) -----------------------------------------
 
     def _get(self, t: torch.Tensor) -> np.ndarray:
-        ev = self.__dict__.get("_admit_done")
+        ev = self.__dict__.get("_split_ev")
         if ev is not None:
-            ev.synchronize()  # an admit beside the attention may still be writing the tables
+            L.lib().lkv_split_wait(ev)  # an admit beside the attention may still be writing the tables
         return t.cpu().numpy()
 
     # -- the admit beside the attention (exact tier, resident split) ---------------------------------
 
     admit_stream: torch.cuda.Stream | None = None  # set by the cache: the exact pass attends before the admit
 
+    def _split_events(self) -> ctypes.c_void_p:
+        """The library-owned events (lkv_split_events) that order this layer's admits beside its
+        attentions; made on first use, with the tier's device current."""
+        ev = self.__dict__.get("_split_ev")
+        if ev is None:
+            ev = ctypes.c_void_p()
+            with torch.cuda.device(self.pool.device):
+                rc = L.lib().lkv_split_events_create(ctypes.byref(ev))
+            if rc != 0:
+                raise L.LkvError(f"lkv_split_events_create failed ({rc}): {L.last_error()}")
+            self._split_ev = ev
+            weakref.finalize(self, L.lib().lkv_split_events_destroy, ev.value)
+        return ev
+
     def join_admit(self) -> None:
         """The current stream waits for this layer's last admit beside the attention (tables, slots
         and the fetch counter it writes)."""
-        ev = self.__dict__.get("_admit_done")
+        ev = self.__dict__.get("_split_ev")
         if ev is not None:
-            torch.cuda.current_stream().wait_event(ev)
+            rc = L.lib().lkv_split_join(ev, L.stream_handle(self.pool.device))
+            if rc != 0:
+                raise L.LkvError(f"lkv_split_join failed ({rc}): {L.last_error()}")
 
     def _resident_listing(self) -> None:
         """For a selection loaded into self.chosen: the hot list gets each chosen block's slot, or -1
@@ -302,24 +320,6 @@ class TieredLayer:
         resident = slots >= 1
         self.hot_list[:, 1 : self.k + 1] = torch.where(resident, slots, -1)
         K.mark_blocks(torch.where(resident, self.chosen, -1), self.bitmap)
-
-    def _admit_beside(self, plan: dict, step: int) -> None:
-        """The admit of self.chosen and the fetch of its misses on the admit stream, after the
-        selection (`fork`, recorded before the attention was launched), with no slots_out: its victims
-        are never slots the hot list names. Launched after the attention, so that the attention's
-        CTAs are placed first."""
-        side = self.admit_stream
-        assert side is not None
-        fork, done = plan["events"]
-        side.wait_event(fork)
-        adm = plan["adm"]
-        adm[10] = step
-        adm[-1] = side.cuda_stream
-        rc = plan["adm_fn"](*adm)
-        if rc != 0:
-            raise L.LkvError(f"lkv_tier_admit failed ({rc}): {L.last_error()}")
-        done.record(side)
-        self._admit_done = done
 
     @property
     def slot_block(self) -> np.ndarray:
@@ -563,22 +563,23 @@ class TieredLayer:
             plan["ws_t"] = (ws_sel, ws_att)
         stream = L.stream_handle(dev)
         sel, att, hot = plan["sel"], plan["att"], plan["hot"]
-        split = self.admit_stream is not None
-        if split:
-            # Resident split: the selection lists the resident slots, the attention covers the misses
-            # from their records, and the admit runs beside it on the admit stream.
-            self.join_admit()
-            if not selected:
-                res = plan["res"]
-                res[0] = q.data_ptr()
-                res[-1] = stream
-                rc = plan["res_fn"](*res)
-                if rc != 0:
-                    raise L.LkvError(f"lkv_quest_topk_resident failed ({rc}): {L.last_error()}")
-            else:
+        if self.admit_stream is not None:
+            # Resident split, one library call: the selection lists the resident slots, the attention
+            # covers the misses from their records, and the admit runs beside it on the admit stream.
+            if selected:
+                self.join_admit()
                 self._resident_listing()
-            plan["events"][0].record()  # the selection is done: the admit may start after it
-        elif not selected:
+            args = plan["split"]
+            args.q = q.data_ptr()
+            args.scale = scale
+            args.step = step
+            args.selected = 1 if selected else 0
+            hot.last_fill = self.fill
+            rc = plan["split_fn"](plan["split_ref"], self._split_events(), stream, plan["side"])
+            if rc != 0:
+                raise L.LkvError(f"lkv_split_step failed ({rc}): {L.last_error()}")
+            return self.out_q
+        if not selected:
             sel[0] = q.data_ptr()
             sel[26] = step
             sel[-1] = stream
@@ -592,8 +593,6 @@ class TieredLayer:
         rc = plan["att_fn"](*att)
         if rc != 0:
             raise L.LkvError(f"lkv_exact_attention failed ({rc}): {L.last_error()}")
-        if split:
-            self._admit_beside(plan, step)
         return self.out_q
 
     def _ws_bytes(self, key: tuple, size_of) -> int:  # noqa: ANN001
@@ -604,8 +603,6 @@ class TieredLayer:
         return v
 
     def _build_plan(self, key: tuple, q: torch.Tensor, n_cand: int, ws_sel: torch.Tensor, ws_att: torch.Tensor) -> dict:
-        import ctypes
-
         hq, d, h = q.shape[0], self.d, self.h
         kind = L.LKV_COLD_INT8 if self.store.dtype == torch.uint8 else L.LKV_COLD_PAIRS
         kmin, kmax = self.kmin[0], self.kmax[0]
@@ -625,19 +622,26 @@ class TieredLayer:
         att = [q.data_ptr(), hq, h, d, self.bs, ctypes.byref(hot), ctypes.byref(cold), 1.0, self.out_q.data_ptr(), L.dtype_code(self.out_q.dtype),
                self.lse.data_ptr(), None, None,
                ws_att.data_ptr(), ws_att.numel(), 0]
-        # The resident selection (lkv_quest_topk_resident) and the admit without slots_out
-        # (lkv_tier_admit) of the resident split.
-        res = [q.data_ptr(), qd, hq, h, d, kmin.data_ptr(), kmax.data_ptr(), L.dtype_code(kmin.dtype), kmin.stride(-3), 1, n_cand, self.k, qd,
-               self.chosen.data_ptr(), self.chosen.stride(0), self._block_slot.data_ptr(), self._block_slot.shape[1], slots.data_ptr(),
-               slots.stride(0), self.bitmap.data_ptr(), self.bitmap.shape[-1], ws_sel.data_ptr(), ws_sel.numel(), 0]
-        adm = [self.chosen.data_ptr(), h, self.k, self.chosen.stride(0), self._block_slot.data_ptr(), self._block_slot.shape[1],
-               self._slot_block.data_ptr(), self._last_used.data_ptr(), self._slot_block.shape[1], self._evicted_at.data_ptr(), 0,
-               self.store.data_ptr(), kind, self.pool.data_ptr(), self.pool.shape[-2], self.d, L.dtype_code(self.pool.dtype), self.miss_blk.data_ptr(),
-               self.miss_slot.data_ptr(), self.n_miss.data_ptr(), None, 0, self.fetched_total.data_ptr(), 0]
         lib = L.lib()
-        return {"key": key, "ws": (ws_sel.data_ptr(), ws_att.data_ptr()), "sel": sel, "att": att, "hot": hot, "cold": cold,
-                "sel_fn": lib.lkv_quest_topk_admit, "att_fn": lib.lkv_exact_attention, "res": res, "res_fn": lib.lkv_quest_topk_resident,
-                "adm": adm, "adm_fn": lib.lkv_tier_admit, "events": (torch.cuda.Event(), torch.cuda.Event())}
+        plan = {"key": key, "ws": (ws_sel.data_ptr(), ws_att.data_ptr()), "sel": sel, "att": att, "hot": hot, "cold": cold,
+                "sel_fn": lib.lkv_quest_topk_admit, "att_fn": lib.lkv_exact_attention}
+        if self.admit_stream is not None:
+            # The resident split's one call (lkv_split_step): the resident selection, the attention and
+            # the admit without slots_out, their arguments in one struct patched per step.
+            a = L.SplitStepArgs(q=q.data_ptr(), q_dtype=qd, hq=hq, h=h, d=d, kmin=kmin.data_ptr(), kmax=kmax.data_ptr(),
+                                meta_dtype=L.dtype_code(kmin.dtype), m_head=kmin.stride(-3), first_block=1, n_cand=n_cand, k=self.k,
+                                bound_mode=qd, chosen=self.chosen.data_ptr(), chosen_ld=self.chosen.stride(0), block_slot=self._block_slot.data_ptr(),
+                                cap=self._block_slot.shape[1], hot=slots.data_ptr(), hot_ld=slots.stride(0), bitmap=self.bitmap.data_ptr(),
+                                bitmap_words=self.bitmap.shape[-1], sel_workspace=ws_sel.data_ptr(), sel_workspace_bytes=ws_sel.numel(),
+                                bs=self.bs, hot_set=ctypes.addressof(hot), cold_set=ctypes.addressof(cold), scale=1.0,
+                                out=self.out_q.data_ptr(), out_dtype=L.dtype_code(self.out_q.dtype), lse=self.lse.data_ptr(),
+                                att_workspace=ws_att.data_ptr(), att_workspace_bytes=ws_att.numel(), slot_block=self._slot_block.data_ptr(),
+                                last_used=self._last_used.data_ptr(), n_slots=self._slot_block.shape[1], evicted_at=self._evicted_at.data_ptr(),
+                                step=0, store=self.store.data_ptr(), store_kind=kind, pool=self.pool.data_ptr(), pool_dtype=L.dtype_code(self.pool.dtype),
+                                miss_blk=self.miss_blk.data_ptr(), miss_slot=self.miss_slot.data_ptr(), n_miss=self.n_miss.data_ptr(),
+                                miss_total=self.fetched_total.data_ptr(), selected=0)
+            plan.update(split=a, split_ref=ctypes.byref(a), split_fn=lib.lkv_split_step, side=self.admit_stream.cuda_stream)
+        return plan
 
     def _attend_zerocopy(self, query: torch.Tensor, scale: float, exact: bool, pool_strides: tuple[int, int, int]) -> torch.Tensor:
         """No slots: the selected blocks are read in place from the host store, the sink and the

@@ -88,3 +88,15 @@ def test_the_append_mark_and_stage_entries_reject_bad_arguments(lib) -> None:  #
     assert rc == 1 and "bad shape" in _lib.last_error()
     rc = lib.lkv_ragged_stage_records(fake, 10, 8, 2368, fake, 9, fake, 1, fake, None, 0, ctypes.c_void_p(24), 10, fake, fake, 9, None)
     assert rc == 2 and "16-byte aligned" in _lib.last_error()
+
+
+def test_the_split_step_entries_reject_missing_arguments(lib) -> None:  # noqa: ANN001
+    """lkv_split_step and its events API refuse null handles before touching a stream."""
+    from lazykv_b200 import _lib
+
+    assert lib.lkv_split_events_create(None) == 2 and "null" in _lib.last_error()
+    assert lib.lkv_split_step(None, None, None, None) == 2 and "null" in _lib.last_error()
+    assert lib.lkv_split_join(None, None) == 2 and "null" in _lib.last_error()
+    assert lib.lkv_split_wait(None) == 2 and "null" in _lib.last_error()
+    assert lib.lkv_split_events_destroy(None) == 0
+    assert ctypes.sizeof(_lib.SplitStepArgs) == 336  # the C struct's size on this ABI (x86-64)
